@@ -1,0 +1,171 @@
+"""Batched split-KV decode over paged latent pools (the ``asterq_latent_decode`` C ABI).
+
+``LatentPools`` holds the five device pools of one global-attention layer;
+``DeviceDecodePlan`` uploads a ``DecodePlan`` and owns the partial-record
+workspace, so that a decode step is one C call with no allocation (and can be
+captured in a CUDA graph by the caller).
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from .plan import DecodePlan
+
+LATENT_DIM = 512
+ROPE_DIM = 64
+GROUP_SIZE = 64
+
+
+@dataclass
+class LatentPools:
+    """Device pools (layout documented in include/asterq.h)."""
+
+    cold_codes: torch.Tensor  # uint8 [Pc, page, 256]
+    cold_scales: torch.Tensor  # fp16 [Pc, page, 8]
+    cold_rope: torch.Tensor  # bf16 [Pc, page, 64]
+    hot_latent: torch.Tensor  # bf16 [Ph, page, 512]
+    hot_rope: torch.Tensor  # bf16 [Ph, page, 64]
+
+    @property
+    def page_tokens(self) -> int:
+        return int(self.cold_codes.shape[1] if self.cold_codes.numel() else self.hot_latent.shape[1])
+
+    @staticmethod
+    def empty(n_cold_pages: int, n_hot_pages: int, page_tokens: int, device) -> "LatentPools":
+        return LatentPools(
+            cold_codes=torch.empty(n_cold_pages, page_tokens, LATENT_DIM // 2, dtype=torch.uint8, device=device),
+            cold_scales=torch.empty(n_cold_pages, page_tokens, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=device),
+            cold_rope=torch.empty(n_cold_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device),
+            hot_latent=torch.empty(n_hot_pages, page_tokens, LATENT_DIM, dtype=torch.bfloat16, device=device),
+            hot_rope=torch.empty(n_hot_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device),
+        )
+
+    @property
+    def num_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.cold_codes, self.cold_scales, self.cold_rope, self.hot_latent, self.hot_rope))
+
+
+class DeviceDecodePlan:
+    """A ``DecodePlan`` resident on the device plus its workspace."""
+
+    def __init__(self, plan: DecodePlan, device) -> None:
+        self.plan = plan
+        self.device = torch.device(device)
+
+        def up(a):
+            t = torch.from_numpy(a.copy()) if a.size else torch.zeros(1, 4, dtype=torch.int32)
+            return t.to(self.device)
+
+        self.tiles = up(plan.tiles)
+        self.items = up(plan.items)
+        self.combine = up(plan.combine)
+        ws_floats = max(1, plan.n_slots * 16 * (LATENT_DIM + 2))
+        self.workspace = torch.empty(ws_floats, dtype=torch.float32, device=self.device)
+
+    @property
+    def n_items(self) -> int:
+        return int(self.plan.items.shape[0])
+
+
+def make_params(
+    pools: LatentPools,
+    dplan: DeviceDecodePlan,
+    q_lat: torch.Tensor,
+    q_rope: torch.Tensor,
+    new_latent: torch.Tensor,
+    new_rope: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    n_heads: int,
+    softmax_scale: float,
+    logit_softcap: float | None = None,
+) -> _lib.DecodeParams:
+    plan = dplan.plan
+    p = _lib.DecodeParams()
+    p.n_heads = n_heads
+    p.latent_dim = LATENT_DIM
+    p.rope_dim = ROPE_DIM
+    p.group_size = GROUP_SIZE
+    p.page_tokens = int(pools.cold_codes.shape[1] if pools.cold_codes.dim() == 3 and pools.cold_codes.shape[0] else pools.hot_latent.shape[1])
+    p.out_dtype = _lib.DTYPE_F32 if out.dtype == torch.float32 else _lib.DTYPE_BF16
+    p.softmax_scale = float(softmax_scale)
+    p.logit_softcap = float(logit_softcap) if logit_softcap else 0.0
+    p.n_cold_pages = int(pools.cold_codes.shape[0])
+    p.n_hot_pages = int(pools.hot_latent.shape[0])
+    p.total_q = int(q_lat.shape[0])
+    p.n_tiles = int(plan.tiles.shape[0])
+    p.n_items = int(plan.items.shape[0])
+    p.n_combine = int(plan.combine.shape[0])
+    p.n_slots = int(plan.n_slots)
+    p.q_lat = q_lat.data_ptr()
+    p.q_rope = q_rope.data_ptr()
+    p.new_latent = new_latent.data_ptr()
+    p.new_rope = new_rope.data_ptr()
+    p.cold_codes = pools.cold_codes.data_ptr() if pools.cold_codes.numel() else None
+    p.cold_scales = pools.cold_scales.data_ptr() if pools.cold_scales.numel() else None
+    p.cold_rope = pools.cold_rope.data_ptr() if pools.cold_rope.numel() else None
+    p.hot_latent = pools.hot_latent.data_ptr() if pools.hot_latent.numel() else None
+    p.hot_rope = pools.hot_rope.data_ptr() if pools.hot_rope.numel() else None
+    p.tiles = dplan.tiles.data_ptr()
+    p.items = dplan.items.data_ptr()
+    p.combine = dplan.combine.data_ptr()
+    p.out = out.data_ptr()
+    p.workspace = dplan.workspace.data_ptr()
+    p.workspace_bytes = dplan.workspace.numel() * 4
+    return p
+
+
+def _check_inputs(q_lat, q_rope, new_latent, new_rope, n_heads):
+    for name, t in (("q_lat", q_lat), ("q_rope", q_rope), ("new_latent", new_latent), ("new_rope", new_rope)):
+        if not t.is_cuda:
+            raise RuntimeError(f"{name}: asterq kernels need CUDA tensors; there is no CPU path")
+        if t.dtype != torch.bfloat16:
+            raise ValueError(f"{name} must be bfloat16 (got {t.dtype})")
+        if not t.is_contiguous():
+            raise ValueError(f"{name} must be contiguous")
+    if q_lat.dim() != 3 or q_lat.shape[1:] != (n_heads, LATENT_DIM):
+        raise ValueError(f"q_lat must be [total_q, {n_heads}, {LATENT_DIM}] (got {tuple(q_lat.shape)})")
+    if q_rope.shape != (q_lat.shape[0], n_heads, ROPE_DIM):
+        raise ValueError(f"q_rope must be [total_q, {n_heads}, {ROPE_DIM}] (got {tuple(q_rope.shape)})")
+    if new_latent.shape != (q_lat.shape[0], LATENT_DIM) or new_rope.shape != (q_lat.shape[0], ROPE_DIM):
+        raise ValueError("new_latent / new_rope must be [total_q, 512] / [total_q, 64]")
+
+
+def latent_decode(
+    pools: LatentPools,
+    dplan: DeviceDecodePlan,
+    q_lat: torch.Tensor,
+    q_rope: torch.Tensor,
+    new_latent: torch.Tensor,
+    new_rope: torch.Tensor,
+    *,
+    softmax_scale: float | None = None,
+    logit_softcap: float | None = None,
+    out: torch.Tensor | None = None,
+    out_dtype: torch.dtype = torch.bfloat16,
+) -> torch.Tensor:
+    """Context latents [total_q, H, 512] for every query row of the batch.
+
+    ``softmax_scale`` defaults to 1/sqrt(512 + 64) (latent_attention.py:189 with
+    head_dim = latent_dim under absorption).
+    """
+    n_heads = dplan.plan.n_heads
+    _check_inputs(q_lat, q_rope, new_latent, new_rope, n_heads)
+    if q_lat.shape[0] < dplan.plan.total_q:
+        raise ValueError("q arrays are shorter than the plan's total_q")
+    if softmax_scale is None:
+        softmax_scale = 1.0 / math.sqrt(LATENT_DIM + ROPE_DIM)
+    if out is None:
+        out = torch.empty(q_lat.shape[0], n_heads, LATENT_DIM, dtype=out_dtype, device=q_lat.device)
+    elif out.dtype not in (torch.float32, torch.bfloat16) or out.shape != (q_lat.shape[0], n_heads, LATENT_DIM):
+        raise ValueError("out must be float32/bfloat16 [total_q, H, 512]")
+    p = make_params(pools, dplan, q_lat, q_rope, new_latent, new_rope, out, n_heads=n_heads,
+                    softmax_scale=softmax_scale, logit_softcap=logit_softcap)
+    lib = _lib.load()
+    _lib.check(lib.asterq_latent_decode(ctypes.byref(p), _lib.stream_handle(q_lat.device)))
+    return out

@@ -1,0 +1,164 @@
+"""Split-KV schedule for the ragged / paged decode batch.
+
+A batch is a list of sequences, each with its cold chunks (pages of INT4
+codes), its hot pages (BF16) and ``q_len`` new tokens.  The reference walks one
+sequence's chunks serially (cache.py:139-159, latent_attention.py:222-227);
+here every sequence's token list is cut into tiles (64 cold tokens or 16 hot /
+new tokens) and the tiles into work items, one CTA each, sized by the bytes
+they read so that a ragged batch fills all SMs.  Items that do not cover a
+whole sequence write partial (m, l, o) records merged by the combine step.
+
+Tables (int32, see include/asterq.h):
+  tiles   [n_tiles, 4]  {kind, page, offset, n_tokens}
+  items   [n_items, 8]  {seq, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
+  combine [n_combine, 4] {slot_begin, slot_end, out_row0, n_rows}
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import numpy as np
+
+from . import _lib
+
+COLD_TILE = 64
+HOT_TILE = 16
+ROWS_PER_BLOCK = 16
+MAX_Q_LEN = 16
+
+# bytes one tile streams from HBM (cost model for balancing)
+_COLD_TOKEN_BYTES = 256 + 16 + 128
+_HOT_TOKEN_BYTES = 1024 + 128
+_ITEM_OVERHEAD_BYTES = 48 * 1024  # query load + rotation + output/partial write
+
+
+@dataclass
+class SequenceLayout:
+    """Where one sequence's cache lives and where its new tokens sit.
+
+    ``cold``: (page, offset, n_tokens) chunks, oldest first.
+    ``hot``: (page, offset, n_tokens) runs of the hot window, oldest first.
+    ``q_start``: index of the first new token in the batch's q / new-token arrays.
+    """
+
+    cold: list[tuple[int, int, int]] = field(default_factory=list)
+    hot: list[tuple[int, int, int]] = field(default_factory=list)
+    q_start: int = 0
+    q_len: int = 1
+
+    @property
+    def cold_tokens(self) -> int:
+        return sum(n for _, _, n in self.cold)
+
+    @property
+    def hot_tokens(self) -> int:
+        return sum(n for _, _, n in self.hot)
+
+    @property
+    def cache_bytes(self) -> int:
+        return self.cold_tokens * _COLD_TOKEN_BYTES + (self.hot_tokens + self.q_len) * _HOT_TOKEN_BYTES
+
+
+@dataclass
+class DecodePlan:
+    tiles: np.ndarray
+    items: np.ndarray
+    combine: np.ndarray
+    n_slots: int
+    total_q: int
+    n_heads: int
+
+    @property
+    def workspace_bytes(self) -> int:
+        return self.n_slots * ROWS_PER_BLOCK * (512 + 2) * 4
+
+
+def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
+    out = []
+    for page, off, n in seq.cold:
+        for s in range(0, n, COLD_TILE):
+            out.append((_lib.TILE_COLD, page, off + s, min(COLD_TILE, n - s)))
+    for page, off, n in seq.hot:
+        for s in range(0, n, HOT_TILE):
+            out.append((_lib.TILE_HOT, page, off + s, min(HOT_TILE, n - s)))
+    if seq.q_len > 0:
+        out.append((_lib.TILE_NEW, seq.q_start, 0, seq.q_len))
+    return out
+
+
+def _tile_cost(kind: int, n: int) -> int:
+    return n * (_COLD_TOKEN_BYTES if kind == _lib.TILE_COLD else _HOT_TOKEN_BYTES)
+
+
+def build_plan(
+    seqs: list[SequenceLayout],
+    n_heads: int,
+    *,
+    n_sms: int = 148,
+    ctas_per_sm: int = 2,
+    waves: float = 2.0,
+    max_items_per_seq: int | None = None,
+) -> DecodePlan:
+    """Cut the batch into balanced work items (longest first)."""
+    if n_heads <= 0:
+        raise ValueError("n_heads must be positive")
+    tiles: list[tuple[int, int, int, int]] = []
+    seq_tile_ranges = []
+    total_q = 0
+    for seq in seqs:
+        if not (0 < seq.q_len <= MAX_Q_LEN):
+            raise ValueError(f"q_len must be in 1..{MAX_Q_LEN} (got {seq.q_len})")
+        for page, off, n in list(seq.cold) + list(seq.hot):
+            if n <= 0 or off < 0 or page < 0:
+                raise ValueError(f"bad chunk (page={page}, offset={off}, n={n})")
+        t0 = len(tiles)
+        tiles.extend(_tiles_of(seq))
+        seq_tile_ranges.append((t0, len(tiles)))
+        total_q = max(total_q, seq.q_start + seq.q_len)
+
+    tile_arr = np.asarray(tiles, dtype=np.int32).reshape(-1, 4)
+    costs = np.array([_tile_cost(k, n) for k, _, _, n in tiles], dtype=np.int64)
+    prefix = np.concatenate(([0], np.cumsum(costs)))
+
+    # work units: (seq, row_block)
+    units = []
+    total_cost = 0
+    for si, seq in enumerate(seqs):
+        rows = seq.q_len * n_heads
+        t0, t1 = seq_tile_ranges[si]
+        c = int(prefix[t1] - prefix[t0])
+        for rb in range((rows + ROWS_PER_BLOCK - 1) // ROWS_PER_BLOCK):
+            units.append((si, rb, t0, t1, c))
+            total_cost += c
+    slots_target = max(1, int(n_sms * ctas_per_sm * waves))
+    item_cost = max(total_cost / slots_target, 8 * COLD_TILE * _COLD_TOKEN_BYTES)
+
+    items = []
+    combine = []
+    n_slots = 0
+    for si, rb, t0, t1, c in units:
+        seq = seqs[si]
+        rows = seq.q_len * n_heads
+        out_row0 = seq.q_start * n_heads + rb * ROWS_PER_BLOCK
+        n_rows = min(ROWS_PER_BLOCK, rows - rb * ROWS_PER_BLOCK)
+        k = max(1, int(np.ceil((c + _ITEM_OVERHEAD_BYTES) / (item_cost + _ITEM_OVERHEAD_BYTES))))
+        k = min(k, t1 - t0)
+        if max_items_per_seq is not None:
+            k = min(k, max_items_per_seq)
+        if k <= 1:
+            items.append((si, rb, t0, t1, -1, out_row0, n_rows, seq.q_len, c))
+            continue
+        # contiguous ranges of ~equal cost
+        targets = prefix[t0] + (c * np.arange(1, k)) / k
+        cuts = np.searchsorted(prefix[t0 : t1 + 1], targets, side="left") + t0
+        bounds = [t0] + sorted(set(int(x) for x in cuts if t0 < x < t1)) + [t1]
+        s0 = n_slots
+        for a, b in zip(bounds[:-1], bounds[1:]):
+            items.append((si, rb, a, b, n_slots, out_row0, n_rows, seq.q_len, int(prefix[b] - prefix[a])))
+            n_slots += 1
+        combine.append((s0, n_slots, out_row0, n_rows))
+
+    items.sort(key=lambda it: -it[8])
+    item_arr = np.asarray([it[:8] for it in items], dtype=np.int32).reshape(-1, 8)
+    comb_arr = np.asarray(combine, dtype=np.int32).reshape(-1, 4)
+    return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads)

@@ -1,0 +1,161 @@
+// Shared device helpers for the asterq kernels (sm_100a only).
+//
+// Everything here is either a thin inline-PTX wrapper around one instruction
+// (mma.sync, ldmatrix, cp.async, packed f32x2 arithmetic) or plain integer /
+// IEEE arithmetic.  No CUDA math-library internals are restated.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "asterq kernels are written for sm_100a (B200) only"
+#endif
+
+#define ASTERQ_DEVICE __device__ __forceinline__
+
+namespace asterq {
+
+// ---------------------------------------------------------------------------
+// Packed float32x2 arithmetic (Blackwell add/sub/mul .f32x2).  Each lane of the
+// pair is an ordinary IEEE round-to-nearest float32 operation, so results are
+// bit-identical to two scalar operations.
+// ---------------------------------------------------------------------------
+ASTERQ_DEVICE unsigned long long f2_bits(float2 v) {
+  return (unsigned long long)__float_as_uint(v.x) | ((unsigned long long)__float_as_uint(v.y) << 32);
+}
+ASTERQ_DEVICE float2 bits_f2(unsigned long long b) {
+  return make_float2(__uint_as_float((unsigned)(b & 0xffffffffull)), __uint_as_float((unsigned)(b >> 32)));
+}
+ASTERQ_DEVICE float2 add2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+ASTERQ_DEVICE float2 sub2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+ASTERQ_DEVICE float2 mul2(float2 a, float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return bits_f2(d);
+}
+
+// ---------------------------------------------------------------------------
+// bf16 / fp16 bit helpers
+// ---------------------------------------------------------------------------
+ASTERQ_DEVICE float bf16lo_to_f32(uint32_t w) { return __uint_as_float(w << 16); }
+ASTERQ_DEVICE float bf16hi_to_f32(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+ASTERQ_DEVICE uint32_t pack_half2(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+ASTERQ_DEVICE uint32_t pack_bf162(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+ASTERQ_DEVICE float2 unpack_half2(uint32_t w) {
+  __half2 h = *reinterpret_cast<__half2*>(&w);
+  return __half22float2(h);
+}
+ASTERQ_DEVICE float2 unpack_bf162(uint32_t w) { return make_float2(bf16lo_to_f32(w), bf16hi_to_f32(w)); }
+
+// fp16x2 arithmetic on raw 32-bit registers
+ASTERQ_DEVICE uint32_t hsub2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+ASTERQ_DEVICE uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+ASTERQ_DEVICE uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+// (a & mask) | bits, one LOP3
+ASTERQ_DEVICE uint32_t and_or(uint32_t a, uint32_t mask, uint32_t bits) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(d) : "r"(a), "r"(mask), "r"(bits));
+  return d;
+}
+
+// ---------------------------------------------------------------------------
+// INT4 nibble -> fp16 conversion with the exponent-bias trick (published as the
+// "magic number" int->float conversion, e.g. Kim et al. 2022, "Who Says
+// Elephants Can't Run").  fp16 0x6400 is 1024.0 with an ulp of 1, so OR-ing a
+// nibble u into its low mantissa bits gives exactly 1024 + u; a nibble sitting in
+// mantissa bits 4..7 gives 1024 + 16u.  Codes are u - 8 in [-8, 7], exact in fp16.
+// ---------------------------------------------------------------------------
+constexpr uint32_t kF16Magic = 0x64006400u;   // (1024, 1024)
+constexpr uint32_t kF16Bias1032 = 0x64086408u; // (1032, 1032)
+constexpr uint32_t kF16Sixteenth = 0x2C002C00u; // (1/16, 1/16)
+constexpr uint32_t kF16Minus72 = 0xD480D480u;  // (-72, -72)
+
+// fp16x2 codes of the low nibbles at bit 0 and bit 16 of x
+ASTERQ_DEVICE uint32_t nib_lo_f16x2(uint32_t x) { return hsub2_u32(and_or(x, 0x000F000Fu, kF16Magic), kF16Bias1032); }
+// fp16x2 codes of the nibbles at bits 4..7 and 20..23 of x
+ASTERQ_DEVICE uint32_t nib_hi_f16x2(uint32_t x) {
+  return hfma2_u32(and_or(x, 0x00F000F0u, kF16Magic), kF16Sixteenth, kF16Minus72);
+}
+
+// ---------------------------------------------------------------------------
+// Warp-level tensor-core MMA (m16n8k16, fp32 accumulate)
+// ---------------------------------------------------------------------------
+ASTERQ_DEVICE void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+ASTERQ_DEVICE void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+ASTERQ_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+ASTERQ_DEVICE void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+ASTERQ_DEVICE void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// ---------------------------------------------------------------------------
+// Asynchronous global -> shared copies (16 bytes per thread, L2 only)
+// ---------------------------------------------------------------------------
+ASTERQ_DEVICE void cp_async16(uint32_t smem_addr, const void* gptr) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(smem_addr), "l"(gptr));
+}
+ASTERQ_DEVICE void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+ASTERQ_DEVICE void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+ASTERQ_DEVICE uint4 ldg_nc_v4(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+}  // namespace asterq

@@ -1,0 +1,163 @@
+/*
+ * asterq — B200 (sm_100a) kernels for AsterLM's Hadamard-INT4 latent-cache
+ * global-attention decode.  Plain C ABI: device pointers, sizes and a CUDA
+ * stream handle (passed as void*); no framework types.
+ *
+ * Reference interfaces each entry point replaces (AsterLM-Frontier, paths
+ * relative to its project root):
+ *   asterq_quantize        quantization/kv.py:76-118   quantize_tensor(x, scheme, group_size)
+ *   asterq_dequantize      quantization/kv.py:121-134  dequantize_tensor(q, dtype)
+ *   asterq_fwht            quantization/kv.py:13-32    normalized_fwht(x)
+ *   asterq_latent_decode   layers/latent_attention.py:177-231 _absorbed_decode (q_len = 1) and
+ *                          layers/latent_attention.py:116-175 _full_attention (q_len > 1, causal),
+ *                          iterating the cache like cache.py:139-159 iter_chunks
+ *   asterq_splitkv_combine layers/latent_attention.py:212-220 (the online-softmax merge rule)
+ *
+ * Every function returns ASTERQ_OK (0) or a negative status and never aborts;
+ * asterq_last_error() describes the last failure on the calling thread.  All
+ * work is enqueued on the given stream; nothing is allocated and nothing
+ * synchronizes the host.
+ */
+#ifndef ASTERQ_H_
+#define ASTERQ_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ASTERQ_VERSION 1
+
+/* status codes */
+#define ASTERQ_OK 0
+#define ASTERQ_ERR_INVALID_ARGUMENT -1 /* bad shape, size or pointer (reference: ValueError) */
+#define ASTERQ_ERR_UNSUPPORTED -2      /* valid request outside what the kernels implement */
+#define ASTERQ_ERR_MISALIGNED -3       /* pointer or stride not aligned as required */
+#define ASTERQ_ERR_WORKSPACE -4        /* workspace missing or too small */
+#define ASTERQ_ERR_CUDA -5             /* CUDA launch error */
+
+/* element types */
+#define ASTERQ_DTYPE_F32 0
+#define ASTERQ_DTYPE_BF16 1
+#define ASTERQ_DTYPE_F16 2
+
+/* storage schemes (kv.py:90 "int8", "int4", "hadamard_int4") */
+#define ASTERQ_SCHEME_HADAMARD_INT4 0
+#define ASTERQ_SCHEME_INT4 1
+#define ASTERQ_SCHEME_INT8 2
+
+/* tile kinds in the decode schedule */
+#define ASTERQ_TILE_COLD 0 /* tokens of a cold page: INT4 codes + fp16 scales + bf16 RoPE key */
+#define ASTERQ_TILE_HOT 1  /* tokens of a hot page: bf16 latent + bf16 RoPE key */
+#define ASTERQ_TILE_NEW 2  /* the step's own new tokens (causal among themselves) */
+
+int asterq_version(void);
+const char* asterq_last_error(void);
+
+/*
+ * Cache write path: rotate (hadamard_int4 only), groupwise absmax-quantize and
+ * pack n_tokens rows of `dim` values.  Replaces quantize_tensor
+ * (quantization/kv.py:76-118).  Output is bit-identical to the reference:
+ *   codes  uint8 [n_tokens, P/2] (int4; P = padded width) or int8 [n_tokens, P]
+ *   scales fp16  [n_tokens, P/group_size]
+ * where P = next power of two >= dim for hadamard_int4 and
+ * ceil(dim/group_size)*group_size otherwise.  x_dtype: ASTERQ_DTYPE_*.
+ * x_row_stride is in elements.  P <= 512, group_size in {16, 32, 64}.
+ */
+int asterq_quantize(const void* x, int x_dtype, int64_t n_tokens, int dim, int64_t x_row_stride, int scheme,
+                    int group_size, void* codes, void* scales, void* stream);
+
+/*
+ * Inverse of asterq_quantize (dequantize_tensor, quantization/kv.py:121-134):
+ * codes * float(scale), inverse normalized FWHT for hadamard_int4, cropped to
+ * `dim`, rounded to out_dtype.  Bit-identical to the reference.
+ */
+int asterq_dequantize(const void* codes, const void* scales, int64_t n_tokens, int dim, int scheme, int group_size,
+                      void* out, int out_dtype, int64_t out_row_stride, void* stream);
+
+/* Normalized Walsh-Hadamard transform of float32 rows (kv.py:13-32), bit-exact; n in 2..512. */
+int asterq_fwht(const float* x, float* y, int64_t rows, int n, void* stream);
+
+/*
+ * Decode attention over a paged hybrid latent cache.
+ *
+ * Layout in device memory (all row-major, token-major):
+ *   cold_codes  uint8 [n_cold_pages, page_tokens, latent_dim/2]   rotated INT4 codes (kv.py:41-48 packing)
+ *   cold_scales fp16  [n_cold_pages, page_tokens, latent_dim/64]
+ *   cold_rope   bf16  [n_cold_pages, page_tokens, rope_dim]
+ *   hot_latent  bf16  [n_hot_pages, page_tokens, latent_dim]
+ *   hot_rope    bf16  [n_hot_pages, page_tokens, rope_dim]
+ *   q_lat       bf16  [total_q, n_heads, latent_dim]   absorbed query q_content @ W_k
+ *   q_rope      bf16  [total_q, n_heads, rope_dim]     RoPE already applied
+ *   new_latent  bf16  [total_q, latent_dim]            the step's own tokens (attended causally)
+ *   new_rope    bf16  [total_q, rope_dim]
+ *   out         [total_q, n_heads, latent_dim] in out_dtype: the context latent
+ *               running_context / max(running_sum, 1e-20) (latent_attention.py:229)
+ *
+ * Schedule (built by the host, see the Python package's plan builder):
+ *   tiles [n_tiles][4] int32 = {kind, page (ASTERQ_TILE_NEW: first new-token row), token offset, n_tokens}
+ *          cold tiles hold <= 64 tokens, hot/new tiles <= 16 tokens.
+ *   items [n_items][8] int32 = {seq, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
+ *          one CTA per item; 16 query rows (t, h) per row block, rows flattened as t*n_heads + h.
+ *          slot < 0: the item covers the whole sequence and writes `out` directly;
+ *          slot >= 0: it writes an (m, l, o) partial to the workspace.
+ *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
+ * Geometry supported: latent_dim 512, rope_dim 64, scale groups of 64, page_tokens
+ * a multiple of 64, q_len <= 16.
+ */
+typedef struct asterq_decode_params {
+  int32_t n_heads;
+  int32_t latent_dim;
+  int32_t rope_dim;
+  int32_t group_size;
+  int32_t page_tokens;
+  int32_t out_dtype; /* ASTERQ_DTYPE_F32 or ASTERQ_DTYPE_BF16 */
+  float softmax_scale;
+  float logit_softcap; /* <= 0: off */
+  int64_t n_cold_pages;
+  int64_t n_hot_pages;
+  int64_t total_q;
+  int32_t n_tiles;
+  int32_t n_items;
+  int32_t n_combine;
+  int32_t n_slots;
+  const void* q_lat;
+  const void* q_rope;
+  const void* new_latent;
+  const void* new_rope;
+  const void* cold_codes;
+  const void* cold_scales;
+  const void* cold_rope;
+  const void* hot_latent;
+  const void* hot_rope;
+  const int32_t* tiles;
+  const int32_t* items;
+  const int32_t* combine;
+  void* out;
+  void* workspace;
+  int64_t workspace_bytes;
+} asterq_decode_params;
+
+/* Bytes of workspace asterq_latent_decode needs (n_slots partial records). */
+int64_t asterq_decode_workspace_bytes(const asterq_decode_params* p);
+
+/* Enqueue the split-KV decode (and, when n_combine > 0, the combine). */
+int asterq_latent_decode(const asterq_decode_params* p, void* stream);
+
+/*
+ * Merge split-KV partial records with the online-softmax rule of
+ * latent_attention.py:212-220 (used by the decode itself and by the
+ * context-parallel path after the partials of all ranks are gathered).
+ *   partials  float32 [n_slots, 16, 2 + latent_dim]  record = {m, l, o[latent_dim]}; o unnormalized
+ *   combine   int32   [n_combine][4] as in asterq_decode_params
+ *   out       [.., n_heads*?] rows of latent_dim in out_dtype, row index out_row0 + r
+ */
+int asterq_splitkv_combine(const float* partials, int32_t n_slots, const int32_t* combine, int32_t n_combine,
+                           int32_t latent_dim, void* out, int32_t out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ASTERQ_H_ */

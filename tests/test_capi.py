@@ -1,0 +1,104 @@
+"""The C-ABI library loads, exports every symbol include/asterq.h declares, and
+rejects bad arguments with a status (host-side validation, no GPU needed)."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from asterq import _lib
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def declared_functions() -> set[str]:
+    text = (REPO / "include" / "asterq.h").read_text()
+    return set(re.findall(r"^\s*(?:int|int64_t|const char\*)\s+(asterq_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_matches_binding():
+    assert declared_functions() == set(_lib.EXPORTED_SYMBOLS)
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.lib_path())], capture_output=True, text=True)
+    if out.returncode == 0:
+        for name in declared_functions():
+            assert re.search(rf"\bT {name}\b", out.stdout), name
+
+
+def test_version_and_error_string():
+    lib = _lib.load()
+    assert lib.asterq_version() == 1
+    assert isinstance(lib.asterq_last_error(), bytes)
+
+
+def test_struct_layout_matches_header():
+    # sizes of the C struct: 6 int32 + 2 float + 3 int64 + 4 int32 + 14 pointers + int64
+    assert ctypes.sizeof(_lib.DecodeParams) == 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8
+
+
+def test_quantize_rejects_bad_sizes_without_touching_the_gpu():
+    lib = _lib.load()
+    st = lib.asterq_quantize(None, _lib.DTYPE_BF16, -1, 512, 512, _lib.SCHEME_HADAMARD_INT4, 64, None, None, None)
+    assert st == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert b"bad sizes" in lib.asterq_last_error()
+    st = lib.asterq_quantize(None, _lib.DTYPE_BF16, 4, 512, 100, _lib.SCHEME_HADAMARD_INT4, 64, None, None, None)
+    assert st == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    # zero tokens is a valid no-op
+    assert lib.asterq_quantize(None, _lib.DTYPE_BF16, 0, 512, 512, 0, 64, None, None, None) == _lib.ASTERQ_OK
+    st = lib.asterq_fwht(None, None, 4, 48, None)
+    assert st == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+
+
+def _params(**kw) -> _lib.DecodeParams:
+    p = _lib.DecodeParams()
+    p.n_heads, p.latent_dim, p.rope_dim, p.group_size, p.page_tokens = 16, 512, 64, 64, 512
+    p.out_dtype = _lib.DTYPE_F32
+    p.softmax_scale = 1.0
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+@pytest.mark.parametrize(
+    "kw,status",
+    [
+        (dict(latent_dim=256), _lib.ASTERQ_ERR_UNSUPPORTED),
+        (dict(rope_dim=32), _lib.ASTERQ_ERR_UNSUPPORTED),
+        (dict(page_tokens=100), _lib.ASTERQ_ERR_UNSUPPORTED),
+        (dict(out_dtype=_lib.DTYPE_F16), _lib.ASTERQ_ERR_UNSUPPORTED),
+        (dict(n_heads=0), _lib.ASTERQ_ERR_INVALID_ARGUMENT),
+        (dict(n_items=3), _lib.ASTERQ_ERR_INVALID_ARGUMENT),  # null tables
+        (dict(n_slots=2, n_items=0), _lib.ASTERQ_ERR_WORKSPACE),
+        (dict(n_items=1, items=8, tiles=16, q_lat=16, q_rope=16, out=16), _lib.ASTERQ_ERR_MISALIGNED),
+    ],
+)
+def test_decode_validation(kw, status):
+    lib = _lib.load()
+    p = _params(**kw)
+    assert lib.asterq_latent_decode(ctypes.byref(p), None) == status
+    assert lib.asterq_last_error()
+
+
+def test_decode_noop_and_workspace_query():
+    lib = _lib.load()
+    p = _params()
+    assert lib.asterq_latent_decode(ctypes.byref(p), None) == _lib.ASTERQ_OK
+    p.n_slots = 3
+    assert lib.asterq_decode_workspace_bytes(ctypes.byref(p)) == 3 * 16 * 514 * 4
+
+
+def test_check_maps_status_to_exception_types():
+    lib = _lib.load()
+    lib.asterq_fwht(None, None, 1, 3, None)
+    with pytest.raises(ValueError):
+        _lib.check(_lib.ASTERQ_ERR_INVALID_ARGUMENT)
+    with pytest.raises(_lib.AsterqError):
+        _lib.check(_lib.ASTERQ_ERR_UNSUPPORTED)

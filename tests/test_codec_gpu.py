@@ -1,0 +1,166 @@
+"""Write path and dequantizer on the GPU: bit-exact against the reference/oracle."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hq4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _bf16_from_bits(bits: np.ndarray, device) -> torch.Tensor:
+    return torch.from_numpy(bits.astype(np.int16)).view(torch.bfloat16).to(device)
+
+
+def _codes_np(q) -> np.ndarray:
+    return q.data.cpu().numpy().view(np.uint8)
+
+
+def _scales_bits(q) -> np.ndarray:
+    return q.scale.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def test_encode_matches_reference_fixture(cuda, golden_encode):
+    from asterq.kv import quantize_tensor
+
+    x = _bf16_from_bits(golden_encode["enc_x_bits"], cuda)
+    q = quantize_tensor(x, "hadamard_int4", group_size=64)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(_codes_np(q), golden_encode["enc_codes"])
+    np.testing.assert_array_equal(_scales_bits(q).reshape(x.shape[0], -1), golden_encode["enc_scales"].view(np.uint16))
+    assert q.padded_dim == 512 and q.group_size == 64 and q.scheme == "hadamard_int4"
+    assert q.scale.shape == (x.shape[0], 8, 1) and q.data.shape == (x.shape[0], 256)
+
+
+@pytest.mark.parametrize("scheme", ["hadamard_int4", "int4", "int8"])
+def test_reference_test_case_48_dims_group16(cuda, golden_encode, scheme):
+    """tests/test_quantization.py:8-16 of the reference: [2, 7, 48] bf16, group 16."""
+    from asterq.kv import dequantize_tensor, quantize_tensor
+
+    x = _bf16_from_bits(golden_encode["small_x_bits"], cuda)
+    q = quantize_tensor(x, scheme, group_size=16)
+    np.testing.assert_array_equal(_codes_np(q), golden_encode[f"small_{scheme}_codes"].view(np.uint8))
+    np.testing.assert_array_equal(_scales_bits(q), golden_encode[f"small_{scheme}_scales"].view(np.uint16))
+    restored = dequantize_tensor(q, dtype=x.dtype)
+    assert restored.shape == x.shape
+    if scheme != "int8":
+        assert float((restored.float() - x.float()).square().mean().sqrt()) < 0.18
+    assert q.num_bytes < x.numel() * x.element_size()
+
+
+def test_round_half_even_ties(cuda, golden_encode):
+    from asterq.kv import quantize_tensor
+
+    x = _bf16_from_bits(golden_encode["tie_x_bits"], cuda)
+    q = quantize_tensor(x, "int4", group_size=16)
+    np.testing.assert_array_equal(_codes_np(q), golden_encode["tie_int4_codes"])
+
+
+@pytest.mark.parametrize("src_dtype", [torch.bfloat16, torch.float32, torch.float16])
+def test_encode_bit_exact_vs_oracle_random(cuda, src_dtype):
+    from asterq.kv import quantize_tensor
+    from asterq.synth import outlier_channels
+
+    g = torch.Generator(device=cuda).manual_seed(11)
+    x = torch.randn(20000, 512, generator=g, device=cuda)
+    x[:, outlier_channels(11).to(cuda)] *= 20
+    x = x.to(src_dtype)
+    q = quantize_tensor(x, "hadamard_int4", group_size=64)
+    ref = O.quantize(x.float().cpu().numpy(), "hadamard_int4", 64)
+    np.testing.assert_array_equal(_codes_np(q), ref.data)
+    np.testing.assert_array_equal(_scales_bits(q), ref.scale.view(np.uint16))
+
+
+@pytest.mark.parametrize("dim,group", [(512, 32), (512, 16), (256, 64), (128, 64), (96, 64), (64, 16)])
+def test_encode_other_geometries(cuda, dim, group):
+    """Production configs use latent 96 (padded to 128, kv.py:99-100)."""
+    from asterq.kv import quantize_tensor
+
+    g = torch.Generator(device=cuda).manual_seed(dim + group)
+    x = torch.randn(3000, dim, generator=g, device=cuda).to(torch.bfloat16)
+    q = quantize_tensor(x, "hadamard_int4", group_size=group)
+    ref = O.quantize(x.float().cpu().numpy(), "hadamard_int4", group)
+    np.testing.assert_array_equal(_codes_np(q), ref.data)
+    np.testing.assert_array_equal(_scales_bits(q), ref.scale.view(np.uint16))
+
+
+def test_encode_strided_rows_and_batch_dims(cuda):
+    """Row views of a wider tensor (e.g. a hot page slice) and [B, S, L] inputs."""
+    from asterq.kv import quantize_tensor
+
+    g = torch.Generator(device=cuda).manual_seed(5)
+    wide = torch.randn(3, 700, 640, generator=g, device=cuda).to(torch.bfloat16)
+    x = wide[..., :512]
+    q = quantize_tensor(x, "hadamard_int4", group_size=64)
+    ref = O.quantize(x.float().cpu().numpy(), "hadamard_int4", 64)
+    assert q.data.shape == (3, 700, 256) and q.scale.shape == (3, 700, 8, 1)
+    np.testing.assert_array_equal(_codes_np(q), ref.data)
+
+
+def test_encode_c2_full_size_properties(cuda):
+    """Config 2 at full size (64 x 4096 tokens): determinism, round-trip error,
+    and a bit-exact comparison of a strided sample of rows with the oracle."""
+    from asterq.kv import dequantize_tensor, quantize_tensor
+    from asterq.synth import outlier_channels
+
+    g = torch.Generator(device=cuda).manual_seed(2)
+    x = torch.randn(64, 4096, 512, generator=g, device=cuda)
+    x[..., outlier_channels(2).to(cuda)] *= 20
+    x = x.to(torch.bfloat16)
+    q1 = quantize_tensor(x, "hadamard_int4", group_size=64)
+    q2 = quantize_tensor(x, "hadamard_int4", group_size=64)
+    assert torch.equal(q1.data, q2.data) and torch.equal(q1.scale, q2.scale)
+    sample = x.reshape(-1, 512)[::97]
+    ref = O.quantize(sample.float().cpu().numpy(), "hadamard_int4", 64)
+    np.testing.assert_array_equal(q1.data.reshape(-1, 256)[::97].cpu().numpy(), ref.data)
+    restored = dequantize_tensor(q1, dtype=torch.float32)
+    err = (restored - x.float()).square().mean().sqrt() / x.float().square().mean().sqrt()
+    assert float(err) < 0.2
+
+
+@pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
+def test_dequantize_bit_exact(cuda, golden_encode, out_dtype):
+    from asterq.kv import QuantizedTensor, dequantize_tensor
+
+    codes = golden_encode["enc_codes"]
+    scales = golden_encode["enc_scales"].view(np.float16)
+    n = codes.shape[0]
+    q = QuantizedTensor(torch.from_numpy(codes).to(cuda), torch.from_numpy(scales.copy()).reshape(n, 8, 1).to(cuda),
+                        (n, 512), 512, 64, "hadamard_int4", torch.bfloat16)
+    out = dequantize_tensor(q, dtype=out_dtype).cpu()
+    ref = O.dequantize(O.Quantized(codes, scales.reshape(n, 8, 1), (n, 512), 512, 64, "hadamard_int4"))
+    ref_t = torch.from_numpy(ref).to(out_dtype)
+    # rows whose fp16 scale overflowed to inf hold NaN: compare NaN positions, not payload bits
+    nan = torch.isnan(ref_t)
+    assert torch.equal(torch.isnan(out), nan)
+    ibits = torch.int16 if out_dtype != torch.float32 else torch.int32
+    assert torch.equal(out.view(ibits)[~nan], ref_t.view(ibits)[~nan])
+
+
+@pytest.mark.parametrize("n", [2, 16, 64, 128, 512])
+def test_fwht_bit_exact(cuda, n):
+    from asterq.kv import normalized_fwht
+
+    g = torch.Generator(device=cuda).manual_seed(n)
+    x = torch.randn(777, n, generator=g, device=cuda) * 3
+    x[0] = 0.0
+    x[1] = 1e-38  # subnormal neighbourhood: exercises the IEEE-division fallback
+    y = normalized_fwht(x).cpu()
+    ref = torch.from_numpy(O.normalized_fwht(x.cpu().numpy()))
+    assert torch.equal(y.view(torch.int32), ref.view(torch.int32))
+
+
+def test_encode_rejects_cpu_tensors():
+    from asterq.kv import quantize_tensor
+
+    with pytest.raises(RuntimeError, match="CUDA"):
+        quantize_tensor(torch.zeros(4, 512), "hadamard_int4")
+
+
+def test_encode_empty_input(cuda):
+    from asterq.kv import quantize_tensor
+
+    q = quantize_tensor(torch.zeros(0, 512, dtype=torch.bfloat16, device=cuda), "hadamard_int4")
+    assert q.data.shape == (0, 256) and q.scale.shape == (0, 8, 1)

@@ -1,0 +1,69 @@
+"""Host-side schedule builder: tiles cover every token once, items are balanced."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from asterq import _lib
+from asterq.plan import COLD_TILE, HOT_TILE, SequenceLayout, build_plan
+
+
+def _layout(cold, hot, q_start=0, q_len=1):
+    return SequenceLayout(cold=cold, hot=hot, q_start=q_start, q_len=q_len)
+
+
+def test_tiles_cover_each_token_once():
+    seqs = [
+        _layout([(0, 0, 512), (1, 0, 300)], [(0, 0, 512), (1, 0, 7)], 0, 1),
+        _layout([], [(2, 10, 40)], 1, 3),
+        _layout([], [], 4, 2),
+    ]
+    plan = build_plan(seqs, 16, n_sms=4)
+    t = plan.tiles
+    cold = t[t[:, 0] == _lib.TILE_COLD]
+    hot = t[t[:, 0] == _lib.TILE_HOT]
+    new = t[t[:, 0] == _lib.TILE_NEW]
+    assert cold[:, 3].sum() == 812 and (cold[:, 3] <= COLD_TILE).all()
+    assert hot[:, 3].sum() == 512 + 7 + 40 and (hot[:, 3] <= HOT_TILE).all()
+    assert sorted(new[:, 1].tolist()) == [0, 1, 4] and sorted(new[:, 3].tolist()) == [1, 2, 3]
+    assert plan.total_q == 6
+
+
+def test_items_partition_tiles_per_row_block():
+    seqs = [_layout([(i, 0, 512) for i in range(40)], [(0, 0, 512)], 0, 3)]
+    plan = build_plan(seqs, 16, n_sms=8, ctas_per_sm=1, waves=1)
+    items = plan.items
+    # 3 q tokens x 16 heads = 48 rows = 3 row blocks, each split into several items
+    for rb in range(3):
+        mine = items[items[:, 1] == rb]
+        ranges = sorted((int(a), int(b)) for a, b in mine[:, 2:4])
+        assert ranges[0][0] == 0 and ranges[-1][1] == plan.tiles.shape[0]
+        assert all(r0[1] == r1[0] for r0, r1 in zip(ranges[:-1], ranges[1:]))
+        assert (mine[:, 4] >= 0).all()
+    assert plan.combine.shape[0] == 3
+    assert plan.n_slots == items.shape[0]
+    assert set(plan.combine[:, 2].tolist()) == {0, 16, 32}
+
+
+def test_single_item_sequences_write_output_directly():
+    seqs = [_layout([], [(0, 0, 100)], i, 1) for i in range(10)]
+    plan = build_plan(seqs, 16)
+    assert (plan.items[:, 4] == -1).all() and plan.n_slots == 0 and plan.combine.shape[0] == 0
+
+
+def test_items_sorted_longest_first():
+    seqs = [_layout([(i, 0, 512)] * (i + 1), [], i, 1) for i in range(6)]
+    plan = build_plan(seqs, 16, n_sms=1000)
+    sizes = plan.items[:, 3] - plan.items[:, 2]
+    assert (np.diff(sizes) <= 0).all()
+
+
+@pytest.mark.parametrize("bad", [dict(q_len=0), dict(q_len=17)])
+def test_rejects_bad_q_len(bad):
+    with pytest.raises(ValueError):
+        build_plan([_layout([], [], 0, **bad)], 16)
+
+
+def test_rejects_bad_chunks():
+    with pytest.raises(ValueError):
+        build_plan([_layout([(0, 0, 0)], [])], 16)
