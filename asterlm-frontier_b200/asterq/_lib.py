@@ -78,6 +78,7 @@ class DecodeParams(ctypes.Structure):
         ("out", ctypes.c_void_p),
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_int64),
+        ("device_status", ctypes.c_void_p),
     ]
 
 

@@ -3,7 +3,7 @@
 A batch is a list of sequences, each with its cold chunks (pages of INT4
 codes), its hot pages (BF16) and ``q_len`` new tokens.  The reference walks one
 sequence's chunks serially (cache.py:139-159, latent_attention.py:222-227);
-here every sequence's token list is cut into tiles (64 cold tokens or 16 hot /
+here every sequence's token list is cut into tiles (128 cold tokens or 32 hot /
 new tokens) and the tiles into work items, one CTA each, sized by the bytes
 they read so that a ragged batch fills all SMs.  Items that do not cover a
 whole sequence write partial (m, l, o) records merged by the combine step.
@@ -21,10 +21,10 @@ import numpy as np
 
 from . import _lib
 
-COLD_TILE = 64
-HOT_TILE = 16
+COLD_TILE = 128
+HOT_TILE = 32
 ROWS_PER_BLOCK = 16
-MAX_Q_LEN = 16
+MAX_Q_LEN = 16  # new tokens per sequence (one new-token tile of <= 32 tokens)
 
 # bytes one tile streams from HBM (cost model for balancing)
 _COLD_TOKEN_BYTES = 256 + 16 + 128
@@ -95,7 +95,7 @@ def build_plan(
     n_heads: int,
     *,
     n_sms: int = 148,
-    ctas_per_sm: int = 2,
+    ctas_per_sm: int = 1,
     waves: float = 2.0,
     max_items_per_seq: int | None = None,
 ) -> DecodePlan:
@@ -131,7 +131,7 @@ def build_plan(
             units.append((si, rb, t0, t1, c))
             total_cost += c
     slots_target = max(1, int(n_sms * ctas_per_sm * waves))
-    item_cost = max(total_cost / slots_target, 8 * COLD_TILE * _COLD_TOKEN_BYTES)
+    item_cost = max(total_cost / slots_target, 4 * COLD_TILE * _COLD_TOKEN_BYTES)
 
     items = []
     combine = []

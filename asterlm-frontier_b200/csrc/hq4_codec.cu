@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(256) encode_kernel(const void* __restrict__ x,
 // crop, cast.  Bit-exact for hadamard_int4 / int4 / int8.
 // ---------------------------------------------------------------------------
 template <int D, int G, bool ROT, int QMAX>
-__global__ void __launch_bounds__(256) decode_kernel(const uint8_t* __restrict__ codes, const __half* __restrict__ scales,
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ codes, const __half* __restrict__ scales,
                                                      int64_t n_tokens, int dim_code, int dim_out, void* __restrict__ out,
                                                      int out_dtype, int64_t out_stride) {
   constexpr int EPL = D < 128 ? D : 128;
@@ -466,7 +466,7 @@ int launch_decode_one(const uint8_t* codes, const __half* scales, int64_t n, int
                       int out_dtype, int64_t out_stride, cudaStream_t st) {
   constexpr int EPL = D < 128 ? D : 128;
   constexpr int TPB = 8 * (32 / (D / EPL));
-  decode_kernel<D, G, ROT, QMAX><<<grid_for(n, TPB), 256, 0, st>>>(codes, scales, n, dim_code, dim_out, out, out_dtype,
+  dequant_kernel<D, G, ROT, QMAX><<<grid_for(n, TPB), 256, 0, st>>>(codes, scales, n, dim_code, dim_out, out, out_dtype,
                                                                  out_stride);
   return check_launch("decode");
 }

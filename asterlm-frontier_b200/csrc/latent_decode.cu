@@ -7,28 +7,34 @@
 //   _full_attention  :116-175  q_len > 1, mask k <= past_len + i (:151-153)
 // and the cache walk of src/asterlm/cache.py:139-159 (cold chunks, then hot).
 //
-// What the kernel computes differently from the reference (same mathematics):
-//  * Cold chunks are never dequantized.  The normalized Hadamard H is symmetric
-//    and orthogonal, so q . (H c) = (H q) . c: the query is rotated once per work
-//    item and scored directly against the INT4 codes; the per-(token, group)
-//    fp16 scale multiplies the group's partial dot product.
+// Same mathematics, computed differently:
+//  * Cold chunks are never dequantized to memory.  The normalized Hadamard H is
+//    symmetric and orthogonal, so q . (H c) = (H q) . c: the query is rotated once
+//    per work item and scored directly against the INT4 codes; the per-(token,
+//    group) fp16 scale multiplies the group's partial dot product.
 //  * Values of cold tokens accumulate in the rotated basis, those of hot tokens in
-//    the plain basis.  One running (max, sum) covers both; the rotated accumulator
-//    is rotated back once (O = H O_rot + O_plain).
-//  * Tensor cores do all contractions (mma.sync m16n8k16).  Operand precision:
-//    cold QK fp16 codes (exact) x rotated query split hi+lo in fp16 (per-row
-//    power-of-two prescale); cold PV fp16 codes x fp16 (p * scale); hot QK bf16
-//    latent x bf16 query (exact); hot PV bf16 latent x p split hi+lo in bf16.
-//    Accumulation is fp32 throughout.
+//    the plain basis, under one running (max, sum); the rotated accumulator is
+//    rotated back once (O = H O_rot + O_plain).
+//  * Tensor-core operand precision: cold QK = fp16 codes (exact) x rotated query
+//    split hi + lo in fp16 after a per-row power-of-two prescale; cold PV = fp16
+//    codes x fp16 (p * scale); hot QK = bf16 latent x bf16 query (exact); hot PV =
+//    bf16 latent x p split hi + lo in bf16; fp32 accumulation everywhere.
 //
-// Work decomposition: one CTA per work item = (sequence, block of 16 query rows,
-// contiguous range of tiles).  Cold tiles hold 64 tokens, hot/new tiles 16.  An
-// item that covers a whole sequence writes the normalized output; otherwise it
-// writes an (m, l, o) partial record and combine_kernel merges the records.
-//
-// Warp roles (8 warps): for QK and PV warp w owns scale group w (latent dims
-// 64w..64w+63); warps 0-3 also own one 16-wide slice of the RoPE dims.  QK
-// partials of the 8 groups are reduced through shared memory.
+// CTA organisation (one CTA per work item, 12 warps):
+//  * TMA producer (lane 0 of warp 4): streams the item's tiles (128 cold tokens or
+//    32 hot/new tokens) into a 3-stage ring with cp.async.bulk.tensor (128-byte
+//    hardware swizzle) and mbarrier completion; tile i+3 is issued as soon as
+//    every warp has released tile i.
+//  * warps 0-3 ("score warps"): each owns a quarter of a tile's tokens and all 512
+//    latent dims, so every score row is complete inside one warp (no cross-warp
+//    reduction).  They finish the online softmax (one named barrier to combine the
+//    four warps' tile maxima) and hand p to the value warps through a
+//    double-buffered shared-memory tile.
+//  * warps 4-11 ("value warps"): each owns 64 latent dims (one scale group) of
+//    the 16 x 512 accumulator and accumulates p . V for every tile.
+// Every wait is bounded; a timeout sets a status flag instead of hanging.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "asterq_internal.h"
 
@@ -38,66 +44,111 @@ namespace dec {
 constexpr int kL = 512;
 constexpr int kRope = 64;
 constexpr int kRows = 16;
-constexpr int kCold = 64;
-constexpr int kHot = 16;
-constexpr int kThreads = 256;
+constexpr int kColdTile = 128;
+constexpr int kHotTile = 32;
+constexpr int kStages = 3;
+constexpr int kScoreWarps = 4;
+constexpr int kValueWarps = 8;
+constexpr int kProducerWarp = 4;  // lane 0 of the first value warp issues the TMA loads
+constexpr int kThreads = 32 * (kScoreWarps + kValueWarps);
 
-// one pipeline stage
-constexpr int kCodesOff = 0;                        // cold: [64][256 B] codes, 32-byte segments swizzled
-constexpr int kScaleOff = kCold * 256;              // cold: [64][8] fp16 scales
-constexpr int kCRopeOff = kScaleOff + kCold * 16;   // cold: [64][128 B] RoPE, 16-byte chunks swizzled
-constexpr int kHotLatOff = 0;                       // hot:  [16][1024 B] latent, 16-byte chunks swizzled per 128 B
-constexpr int kHotRopeOff = kHot * 1024;            // hot:  [16][128 B] RoPE
-constexpr int kStageBytes = kCRopeOff + kCold * 128;  // 25600 (>= 18432 for a hot tile)
+// one pipeline stage (offsets in bytes, swizzled regions 1024-aligned)
+constexpr int kCodesLo = 0;        // cold: [128][128 B] codes of dims 0..255, SW128
+constexpr int kCodesHi = 16384;    // cold: [128][128 B] codes of dims 256..511, SW128
+constexpr int kCRope = 32768;      // cold: [128][128 B] RoPE keys, SW128
+constexpr int kScales = 49152;     // cold: [128][16 B] fp16 scales, plain
+constexpr int kHotBlock = 4096;    // hot: latent scale-group g at g*4096: [32][128 B], SW128
+constexpr int kHRope = 32768;      // hot: [32][128 B] RoPE keys, SW128
+constexpr int kStageBytes = 51200;
 
-constexpr int kPartFloats = 8 * kCold * kRows;  // QK partials [warp][token][row]; also [16][512] scratch
-constexpr int kRedStride = kRows + 1;
-constexpr int kRedFloats = kCold * kRedStride;
-constexpr int kPfColdU2 = 8 * 4 * 2 * 32;  // [group][kstep][ntile][lane] uint2 (fp16x4)
-constexpr int kPfHotU2 = 2 * 2 * 32;       // [hi/lo][ntile][lane] uint2 (bf16x4)
+constexpr int kOffQc = kStages * kStageBytes;  // cold query B fragments [8][4][2][2][32] uint2
+constexpr int kOffQh = kOffQc + 32768;          // hot query B fragments  [8][4][2][32] uint2
+constexpr int kOffQr = kOffQh + 16384;          // rope query B fragments [4][2][32] uint2
+constexpr int kPStride = kColdTile + 4;         // p tile row stride (floats)
+constexpr int kPBytes = kRows * kPStride * 4;
+constexpr int kOffP = kOffQr + 2048;            // 2 x p tile [16][132] fp32
+constexpr int kOffMisc = kOffP + 2 * kPBytes;   // 256 floats of per-row scalars
+constexpr int kOffBar = kOffMisc + 1024;        // mbarriers
+constexpr int kSmemBytes = kOffBar + 128 + 1024;  // + alignment slack
 
-template <int NSTAGE>
-struct Smem {
-  static constexpr int kStages = 0;
-  static constexpr int kPart = NSTAGE * kStageBytes;
-  static constexpr int kRed = kPart + kPartFloats * 4;
-  static constexpr int kPfCold = kRed + kRedFloats * 4;
-  static constexpr int kPfHot = kPfCold + kPfColdU2 * 8;
-  static constexpr int kRowF = kPfHot + kPfHotU2 * 8;  // 6 x [16] floats
-  static constexpr int kTotal = kRowF + 6 * 16 * 4;
-};
+// misc (float index)
+constexpr int kMAlpha = 0;     // [2][16]
+constexpr int kMWmax = 32;     // [2][4][16]; after the tile loop [16] = final running max
+constexpr int kMLw = 160;      // [4][16]
+constexpr int kMQscale = 224;  // [16]
+constexpr int kMQinv = 240;    // [16]  (score multiplier 2^-e * softmax_scale)
 
-// XOR swizzle of the 32-byte segments of a 256-byte code row: rows 4 apart and
-// consecutive rows land in different bank octets for both access patterns.
-ASTERQ_DEVICE int code_swz(int row) { return (row + (row >> 2)) & 3; }
-
-ASTERQ_DEVICE uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-ASTERQ_DEVICE uint2 lds64(const uint8_t* p) { return *reinterpret_cast<const uint2*>(p); }
+// mbarrier slots (8 bytes each)
+constexpr int kBarFull = 0;    // [3] TMA landed
+constexpr int kBarEmpty = 3;   // [3] score + value warps done with a stage
+constexpr int kBarPFull = 6;   // [2] p tile written
+constexpr int kBarPEmpty = 8;  // [2] p tile consumed
+constexpr int kBarAbort = 10;  // int flag (shares the slot area)
 
 constexpr float kLog2e = 1.4426950408889634f;
 
-// Normalized FWHT of 16 rows x 512 float32 held in shared memory (not on the
-// bit-exact path: used to rotate the query and the cold accumulator).
-ASTERQ_DEVICE void block_fwht16(float* buf) {
-  const int tid = threadIdx.x;
-#pragma unroll 1
-  for (int lh = 0; lh < 9; ++lh) {
-    const int h = 1 << lh;
-#pragma unroll 4
-    for (int b = tid; b < kRows * (kL / 2); b += kThreads) {
-      const int r = b >> 8, k = b & 255;
-      const int j = ((k >> lh) << (lh + 1)) | (k & (h - 1));
-      float* p = buf + r * kL + j;
-      const float a = p[0], c = p[h];
-      p[0] = a + c;
-      p[h] = a - c;
-    }
-    __syncthreads();
-  }
-  const float inv = 0.04419417382415922f;  // 1/sqrt(512)
-  for (int i = tid; i < kRows * kL; i += kThreads) buf[i] *= inv;
-  __syncthreads();
+struct TensorMaps {
+  CUtensorMap codes;  // cold codes  [tokens][256 B], box [128 B][128 rows]
+  CUtensorMap crope;  // cold rope   [tokens][128 B], box [128 B][128 rows]
+  CUtensorMap hlat;   // hot latent  [tokens][1024 B], box [128 B][32 rows]
+  CUtensorMap hrope;  // hot rope    [tokens][128 B], box [128 B][32 rows]
+  CUtensorMap nlat;   // new latent  [total_q][1024 B], box [128 B][32 rows]
+  CUtensorMap nrope;  // new rope    [total_q][128 B], box [128 B][32 rows]
+};
+
+// ---------------------------------------------------------------------------
+// mbarrier / TMA helpers
+// ---------------------------------------------------------------------------
+ASTERQ_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
+ASTERQ_DEVICE void mbar_expect_tx(uint32_t bar, uint32_t tx) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(tx) : "memory");
+}
+ASTERQ_DEVICE void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+ASTERQ_DEVICE uint32_t mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok;
+}
+// Bounded wait (about 2 s of SM clock): on timeout raise the CTA abort flag so
+// every other wait returns at once and the kernel drains instead of hanging.
+ASTERQ_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (clock64() - t0 > 4000000000LL) {
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+ASTERQ_DEVICE void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+ASTERQ_DEVICE void bulk_1d(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+ASTERQ_DEVICE void named_sync(int id, int count) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory"); }
+ASTERQ_DEVICE void fence_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+// byte offset of (row, 16-byte chunk) in a [rows][128 B] region written with the
+// 128-byte TMA swizzle: chunk index XOR (row mod 8)
+ASTERQ_DEVICE int swz(int row, int chunk) { return row * 128 + ((chunk ^ (row & 7)) << 4); }
 
 struct Tile {
   int kind, page, off, n;
@@ -106,14 +157,15 @@ struct Tile {
 ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) {
   const int4 t = *reinterpret_cast<const int4*>(p.tiles + 4 * (int64_t)idx);
   Tile tile{t.x, t.y, t.z, t.w};
-  // Defensive clamp: a malformed entry reads nothing instead of faulting.
+  // a malformed entry reads nothing instead of faulting
   bool ok = tile.n > 0 && tile.off >= 0;
   if (tile.kind == ASTERQ_TILE_COLD) {
-    ok = ok && tile.page >= 0 && tile.page < p.n_cold_pages && tile.n <= kCold && tile.off + tile.n <= p.page_tokens;
+    ok = ok && tile.page >= 0 && tile.page < p.n_cold_pages && tile.n <= kColdTile &&
+         tile.off + tile.n <= p.page_tokens;
   } else if (tile.kind == ASTERQ_TILE_HOT) {
-    ok = ok && tile.page >= 0 && tile.page < p.n_hot_pages && tile.n <= kHot && tile.off + tile.n <= p.page_tokens;
+    ok = ok && tile.page >= 0 && tile.page < p.n_hot_pages && tile.n <= kHotTile && tile.off + tile.n <= p.page_tokens;
   } else if (tile.kind == ASTERQ_TILE_NEW) {
-    ok = ok && tile.page >= 0 && tile.n <= kHot && (int64_t)tile.page + tile.off + tile.n <= p.total_q;
+    ok = ok && tile.page >= 0 && tile.n <= kHotTile && (int64_t)tile.page + tile.off + tile.n <= p.total_q;
   } else {
     ok = false;
   }
@@ -121,527 +173,672 @@ ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) {
   return tile;
 }
 
-// Issue the cp.async copies of one tile into a stage buffer.
-ASTERQ_DEVICE void issue_tile(const asterq_decode_params& p, const Tile& t, uint8_t* stage) {
-  const int tid = threadIdx.x;
-  const uint32_t sb = smem_u32(stage);
-  if (t.kind == ASTERQ_TILE_COLD) {
-    const int64_t tok0 = (int64_t)t.page * p.page_tokens + t.off;
-    const uint8_t* gc = reinterpret_cast<const uint8_t*>(p.cold_codes) + tok0 * 256;
-    const uint8_t* gs = reinterpret_cast<const uint8_t*>(p.cold_scales) + tok0 * 16;
-    const uint8_t* gr = reinterpret_cast<const uint8_t*>(p.cold_rope) + tok0 * 128;
-    for (int c = tid; c < kCold * 16 + kCold + kCold * 8; c += kThreads) {
-      if (c < kCold * 16) {
-        const int row = c >> 4, ch = c & 15;
-        if (row < t.n)
-          cp_async16(sb + kCodesOff + row * 256 + (((ch >> 1) ^ code_swz(row)) << 5) + ((ch & 1) << 4),
-                     gc + row * 256 + ch * 16);
-      } else if (c < kCold * 17) {
-        const int row = c - kCold * 16;
-        if (row < t.n) cp_async16(sb + kScaleOff + row * 16, gs + row * 16);
-      } else {
-        const int cc = c - kCold * 17;
-        const int row = cc >> 3, ch = cc & 7;
-        if (row < t.n) cp_async16(sb + kCRopeOff + row * 128 + ((ch ^ (row & 7)) << 4), gr + row * 128 + ch * 16);
-      }
+// Normalized FWHT of rows [r0, r0 + nrows) of a [16][512] fp32 buffer, one warp:
+// lane l holds elements 16l..16l+15; stages h < 16 are lane-local, h >= 16 pair
+// lane l with l ^ (h / 16).  Not on the bit-exact path.
+ASTERQ_DEVICE void warp_fwht_rows(float* buf, int r0, int nrows, int lane) {
+  for (int r = r0; r < r0 + nrows; ++r) {
+    float v[16];
+    float4* src = reinterpret_cast<float4*>(buf + r * kL + 16 * lane);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float4 x = src[k];
+      v[4 * k] = x.x;
+      v[4 * k + 1] = x.y;
+      v[4 * k + 2] = x.z;
+      v[4 * k + 3] = x.w;
     }
-  } else {
-    const uint8_t* gl;
-    const uint8_t* gr;
-    if (t.kind == ASTERQ_TILE_HOT) {
-      const int64_t tok0 = (int64_t)t.page * p.page_tokens + t.off;
-      gl = reinterpret_cast<const uint8_t*>(p.hot_latent) + tok0 * 1024;
-      gr = reinterpret_cast<const uint8_t*>(p.hot_rope) + tok0 * 128;
-    } else {
-      const int64_t tok0 = (int64_t)t.page + t.off;
-      gl = reinterpret_cast<const uint8_t*>(p.new_latent) + tok0 * 1024;
-      gr = reinterpret_cast<const uint8_t*>(p.new_rope) + tok0 * 128;
-    }
-    for (int c = tid; c < kHot * 64 + kHot * 8; c += kThreads) {
-      if (c < kHot * 64) {
-        const int row = c >> 6, ch = c & 63;
-        const int dst = kHotLatOff + row * 1024 + ((ch >> 3) << 7) + (((ch & 7) ^ (row & 7)) << 4);
-        if (row < t.n) {
-          cp_async16(sb + dst, gl + row * 1024 + ch * 16);
-        } else {
-          // masked value rows must be finite: P = 0 times NaN would poison the MMA
-          *reinterpret_cast<uint4*>(stage + dst) = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int h = 1; h < 16; h <<= 1)
+#pragma unroll
+      for (int j = 0; j < 16; ++j)
+        if (!(j & h)) {
+          const float a = v[j], b = v[j + h];
+          v[j] = a + b;
+          v[j + h] = a - b;
         }
-      } else {
-        const int cc = c - kHot * 64;
-        const int row = cc >> 3, ch = cc & 7;
-        if (row < t.n) cp_async16(sb + kHotRopeOff + row * 128 + ((ch ^ (row & 7)) << 4), gr + row * 128 + ch * 16);
+#pragma unroll
+    for (int m = 1; m < 32; m <<= 1) {
+      const bool upper = (lane & m) != 0;
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        const float o = __shfl_xor_sync(0xffffffffu, v[j], m);
+        v[j] = upper ? (o - v[j]) : (v[j] + o);
       }
     }
+    const float inv = 0.04419417382415922f;  // 1/sqrt(512)
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+      src[k] = make_float4(v[4 * k] * inv, v[4 * k + 1] * inv, v[4 * k + 2] * inv, v[4 * k + 3] * inv);
   }
 }
 
-template <int NSTAGE>
-__global__ void __launch_bounds__(kThreads, 2) decode_kernel(const asterq_decode_params p) {
-  using S = Smem<NSTAGE>;
-  extern __shared__ __align__(128) uint8_t smem[];
-  float* spart = reinterpret_cast<float*>(smem + S::kPart);
-  float* sred = reinterpret_cast<float*>(smem + S::kRed);
-  uint2* pfc = reinterpret_cast<uint2*>(smem + S::kPfCold);
-  uint2* pfh = reinterpret_cast<uint2*>(smem + S::kPfHot);
-  float* alpha = reinterpret_cast<float*>(smem + S::kRowF);
-  float* qscale = alpha + 16;
-  float* qinv = alpha + 32;
-  float* mrow = alpha + 48;
-  float* lrow = alpha + 64;
-  float* rowmax = alpha + 80;
+// Tile row (token) held at m-tile row r (0..15) of score-warp m-tile m.  Rows are
+// permuted so that the 8-byte code loads of one instruction fall in distinct
+// banks under the 128-byte swizzle: lanes gid 0..3 read rows 0,2,4,6 and gid 4..7
+// read rows 1,3,5,7 of each 8-row group.
+ASTERQ_DEVICE int qk_token(int warp, int m, int r) {
+  const int g = r & 7;
+  return 32 * warp + 16 * m + (((g & 3) << 1) | (g >> 2)) + (r & 8);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    decode_kernel(const asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  float* misc = reinterpret_cast<float*>(smem + kOffMisc);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + kBarAbort);
+  auto bar = [&](int i) { return smem_u32(bars + i); };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tq = lane & 3;
   const int* itm = p.items + 8 * (int64_t)blockIdx.x;
   const int rb = itm[1];
-  // Defensive clamps: a malformed item never reads or writes out of bounds.
   const int tile_begin = max(itm[2], 0);
   const int tile_end = max(min(itm[3], p.n_tiles), tile_begin);
   const int slot = (itm[4] < p.n_slots) ? itm[4] : -2;  // -2: out-of-range slot, write nothing
   const int64_t out_row0 = itm[5];
   const int n_rows = min(itm[6], kRows);
   const int H = p.n_heads;
+  const int n_t = tile_end - tile_begin;
+
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar(kBarFull + s), 1);
+      mbar_init(bar(kBarEmpty + s), kThreads);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(kBarPFull + b), 32 * kScoreWarps);
+      mbar_init(bar(kBarPEmpty + b), 32 * kValueWarps);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+
+  // ---------------- producer: issue one tile into its stage ----------------
+  auto issue = [&](int j) {
+    const int s = j % kStages;
+    const Tile t = load_tile(p, tile_begin + j);
+    const uint32_t full = bar(kBarFull + s);
+    const uint32_t st = sbase + s * kStageBytes;
+    if (t.n == 0) {
+      mbar_arrive(full);
+      return;
+    }
+    if (t.kind == ASTERQ_TILE_COLD) {
+      const int y = t.page * p.page_tokens + t.off;
+      mbar_expect_tx(full, 3 * 16384 + 16 * t.n);
+      tma_2d(st + kCodesLo, &maps.codes, 0, y, full);
+      tma_2d(st + kCodesHi, &maps.codes, 128, y, full);
+      tma_2d(st + kCRope, &maps.crope, 0, y, full);
+      bulk_1d(st + kScales, reinterpret_cast<const uint8_t*>(p.cold_scales) + (int64_t)y * 16, 16 * t.n, full);
+    } else {
+      const bool hot = t.kind == ASTERQ_TILE_HOT;
+      const int y = hot ? t.page * p.page_tokens + t.off : t.page + t.off;
+      const CUtensorMap* lat = hot ? &maps.hlat : &maps.nlat;
+      mbar_expect_tx(full, 9 * 4096);
+#pragma unroll 1
+      for (int g = 0; g < 8; ++g) tma_2d(st + g * kHotBlock, lat, 128 * g, y, full);
+      tma_2d(st + kHRope, hot ? &maps.hrope : &maps.nrope, 0, y, full);
+    }
+  };
+  if (warp == kProducerWarp) {
+    if (lane == 0)
+      for (int j = 0; j < min(n_t, kStages - 1); ++j) issue(j);
+    __syncwarp();
+  }
 
   // ---------------- prologue: rotated, prescaled query fragments ----------------
-  {
-    const uint16_t* ql = reinterpret_cast<const uint16_t*>(p.q_lat);
-    for (int i = tid; i < kRows * kL / 8; i += kThreads) {
-      const int r = i >> 6, c8 = i & 63;
-      uint4 w = make_uint4(0u, 0u, 0u, 0u);
-      if (r < n_rows) w = *reinterpret_cast<const uint4*>(ql + (out_row0 + r) * kL + 8 * c8);
-      float* d = spart + r * kL + 8 * c8;
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        d[2 * k] = bf16lo_to_f32(ws[k]);
-        d[2 * k + 1] = bf16hi_to_f32(ws[k]);
-      }
-    }
-    __syncthreads();
-    block_fwht16(spart);
-    {
-      const int r = tid >> 4, part = tid & 15;
-      float mx = 0.0f;
-      for (int k = 0; k < 32; ++k) mx = fmaxf(mx, fabsf(spart[r * kL + 32 * part + k]));
-#pragma unroll
-      for (int off = 1; off < 16; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      if (part == 0) rowmax[r] = mx;
-    }
-    __syncthreads();
-    if (tid < kRows) {
-      const float mx = rowmax[tid];
-      int e = 0;
-      if (mx > 0.0f) {
-        int ex;
-        frexpf(mx, &ex);
-        e = min(max(14 - ex, -100), 100);
-      }
-      qscale[tid] = ldexpf(1.0f, e);
-      qinv[tid] = ldexpf(1.0f, -e) * p.softmax_scale;
-    }
-    __syncthreads();
-  }
-
-  uint32_t qc[4][2][2][2];  // cold: [kstep][ntile][hi/lo][b0/b1] fp16, K-permuted to match the code layout
-  uint32_t qh[4][2][2];     // hot:  [kstep][ntile][b0/b1] bf16
-  uint32_t qr[2][2];        // rope: [ntile][b0/b1] bf16 (warps 0-3)
-  {
+  // scratch: the last stage (its first tile is issued after the prologue)
+  float* scratch = reinterpret_cast<float*>(smem + (kStages - 1) * kStageBytes);  // [16][512] fp32
+  // raw bf16 query rows [16][512] and RoPE-query rows [16][64] behind it
+  uint16_t* qraw = reinterpret_cast<uint16_t*>(smem + (kStages - 1) * kStageBytes + 32768);
+  uint16_t* rraw = reinterpret_cast<uint16_t*>(smem + (kStages - 1) * kStageBytes + 49152);
+  if (warp < 8) {
     const uint16_t* ql = reinterpret_cast<const uint16_t*>(p.q_lat);
     const uint16_t* qrp = reinterpret_cast<const uint16_t*>(p.q_rope);
+    for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
+      float* dst = scratch + r * kL + 16 * lane;
+      uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a, c = a;
+      if (r < n_rows) {
+        a = *reinterpret_cast<const uint4*>(ql + (out_row0 + r) * kL + 16 * lane);
+        b = *reinterpret_cast<const uint4*>(ql + (out_row0 + r) * kL + 16 * lane + 8);
+        if (lane < 8) c = *reinterpret_cast<const uint4*>(qrp + (out_row0 + r) * kRope + 8 * lane);
+      }
+      *reinterpret_cast<uint4*>(qraw + r * kL + 16 * lane) = a;
+      *reinterpret_cast<uint4*>(qraw + r * kL + 16 * lane + 8) = b;
+      if (lane < 8) *reinterpret_cast<uint4*>(rraw + r * kRope + 8 * lane) = c;
+      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int row = 8 * nt + gid;
-      const float sc = qscale[row];
-      const bool rv = row < n_rows;
+      for (int k = 0; k < 8; ++k) {
+        dst[2 * k] = bf16lo_to_f32(w[k]);
+        dst[2 * k + 1] = bf16hi_to_f32(w[k]);
+      }
+    }
+    __syncwarp();
+    warp_fwht_rows(scratch, 2 * warp, 2, lane);
+    __syncwarp();
+    for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
+      float mx = 0.0f;
 #pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        // K permutation: see the code-fragment extraction in the cold QK loop
-        const int base = 64 * warp + 16 * tq + 8 * (s >> 1) + 2 * (s & 1);
+      for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(scratch[r * kL + 16 * lane + k]));
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      if (lane == 0) {
+        int e = 0;
+        if (mx > 0.0f) {
+          int ex;
+          frexpf(mx, &ex);
+          e = min(max(14 - ex, -100), 100);
+        }
+        misc[kMQscale + r] = ldexpf(1.0f, e);
+        misc[kMQinv + r] = ldexpf(1.0f, -e) * p.softmax_scale;
+      }
+    }
+  }
+  __syncthreads();
+  // B fragments, stored in the order each consumer lane loads them
+  {
+    {
+      uint2* qc = reinterpret_cast<uint2*>(smem + kOffQc);
+      for (int e = tid; e < 8 * 4 * 2 * 2 * 32; e += kThreads) {
+        const int ln = e & 31, hl = (e >> 5) & 1, nt = (e >> 6) & 1, ks = (e >> 7) & 3, g = e >> 9;
+        const int row = 8 * nt + (ln >> 2);
+        // K permutation matching the cold code extraction in the score loop
+        const int base = 64 * g + 16 * (ln & 3) + 8 * (ks >> 1) + 2 * (ks & 1);
         const int dims[4] = {base, base + 4, base + 1, base + 5};
-        float x[4];
-        __half hi[4], lo[4];
+        const float sc = misc[kMQscale + row];
+        uint16_t h[4];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
-          x[k] = spart[row * kL + dims[k]] * sc;
-          hi[k] = __float2half_rn(x[k]);
-          lo[k] = __float2half_rn(x[k] - __half2float(hi[k]));
+          const float x = scratch[row * kL + dims[k]] * sc;
+          const __half hi = __float2half_rn(x);
+          h[k] = hl ? __half_as_ushort(__float2half_rn(x - __half2float(hi))) : __half_as_ushort(hi);
         }
-        qc[s][nt][0][0] = (uint32_t)__half_as_ushort(hi[0]) | ((uint32_t)__half_as_ushort(hi[1]) << 16);
-        qc[s][nt][0][1] = (uint32_t)__half_as_ushort(hi[2]) | ((uint32_t)__half_as_ushort(hi[3]) << 16);
-        qc[s][nt][1][0] = (uint32_t)__half_as_ushort(lo[0]) | ((uint32_t)__half_as_ushort(lo[1]) << 16);
-        qc[s][nt][1][1] = (uint32_t)__half_as_ushort(lo[2]) | ((uint32_t)__half_as_ushort(lo[3]) << 16);
-        // hot query: plain basis, bf16 (exact after the power-of-two prescale)
-        const int e0 = 64 * warp + 16 * s + 2 * tq;
-        uint32_t w0 = 0u, w1 = 0u;
-        if (rv) {
-          w0 = *reinterpret_cast<const uint32_t*>(ql + (out_row0 + row) * kL + e0);
-          w1 = *reinterpret_cast<const uint32_t*>(ql + (out_row0 + row) * kL + e0 + 8);
-        }
+        qc[e] = make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+      }
+      uint2* qh = reinterpret_cast<uint2*>(smem + kOffQh);
+      for (int e = tid; e < 8 * 4 * 2 * 32; e += kThreads) {
+        const int ln = e & 31, nt = (e >> 5) & 1, ks = (e >> 6) & 3, g = e >> 8;
+        const int row = 8 * nt + (ln >> 2);
+        const int e0 = 64 * g + 16 * ks + 2 * (ln & 3);
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(qraw + row * kL + e0);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(qraw + row * kL + e0 + 8);
+        const float sc = misc[kMQscale + row];
         const float2 f0 = unpack_bf162(w0), f1 = unpack_bf162(w1);
-        qh[s][nt][0] = pack_bf162(f0.x * sc, f0.y * sc);
-        qh[s][nt][1] = pack_bf162(f1.x * sc, f1.y * sc);
+        qh[e] = make_uint2(pack_bf162(f0.x * sc, f0.y * sc), pack_bf162(f1.x * sc, f1.y * sc));
       }
-      uint32_t r0 = 0u, r1 = 0u;
-      if (rv && warp < 4) {
-        const int e0 = 16 * warp + 2 * tq;
-        r0 = *reinterpret_cast<const uint32_t*>(qrp + (out_row0 + row) * kRope + e0);
-        r1 = *reinterpret_cast<const uint32_t*>(qrp + (out_row0 + row) * kRope + e0 + 8);
+      uint2* qr = reinterpret_cast<uint2*>(smem + kOffQr);
+      for (int e = tid; e < 4 * 2 * 32; e += kThreads) {
+        const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
+        const int row = 8 * nt + (ln >> 2);
+        const int e0 = 16 * ks + 2 * (ln & 3);
+        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rraw + row * kRope + e0);
+        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rraw + row * kRope + e0 + 8);
+        const float sc = misc[kMQscale + row];
+        const float2 f0 = unpack_bf162(w0), f1 = unpack_bf162(w1);
+        qr[e] = make_uint2(pack_bf162(f0.x * sc, f0.y * sc), pack_bf162(f1.x * sc, f1.y * sc));
       }
-      const float2 g0 = unpack_bf162(r0), g1 = unpack_bf162(r1);
-      qr[nt][0] = pack_bf162(g0.x * sc, g0.y * sc);
-      qr[nt][1] = pack_bf162(g1.x * sc, g1.y * sc);
     }
   }
-  __syncthreads();  // spart is reused below
-
-  // ---------------- main loop over tiles ----------------
-  float o[4][2][4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-      for (int k = 0; k < 4; ++k) o[i][j][k] = 0.0f;
-
-  const int n_t = tile_end - tile_begin;
-  // order 0: accumulator holds cold tokens, rotated basis, code-derived row order
-  // order 1: plain basis, natural row order
-  int order = 0;
-  if (n_t > 0) {
-    const int k0 = p.tiles[4 * (int64_t)tile_begin];  // tile_begin < tile_end <= n_tiles
-    order = (k0 == ASTERQ_TILE_COLD) ? 0 : 1;
-  }
-  float m_run = -INFINITY, l_run = 0.0f;  // softmax state of row tid>>4 (replicated over 16 threads)
-  const int srow = tid >> 4, sj = tid & 15;
-
-#pragma unroll 1
-  for (int i = 0; i < NSTAGE - 1; ++i) {
-    if (i < n_t) issue_tile(p, load_tile(p, tile_begin + i), smem + i * kStageBytes);
-    cp_async_commit();
+  __syncthreads();  // fragments ready; the scratch stage is free
+  if (warp == kProducerWarp) {
+    if (lane == 0 && n_t > kStages - 1) issue(kStages - 1);
+    __syncwarp();
   }
 
-#pragma unroll 1
-  for (int ti = 0; ti < n_t; ++ti) {
-    {
-      const int nxt = ti + NSTAGE - 1;
-      if (nxt < n_t) issue_tile(p, load_tile(p, tile_begin + nxt), smem + (nxt % NSTAGE) * kStageBytes);
-      cp_async_commit();
+  if (warp < kScoreWarps) {
+    // =====================================================================
+    // score warps
+    // =====================================================================
+    const uint2* qc = reinterpret_cast<const uint2*>(smem + kOffQc);
+    const uint2* qh = reinterpret_cast<const uint2*>(smem + kOffQh);
+    const uint2* qr = reinterpret_cast<const uint2*>(smem + kOffQr);
+    float qinv[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      qinv[nt][0] = misc[kMQinv + 8 * nt + 2 * tq];
+      qinv[nt][1] = misc[kMQinv + 8 * nt + 2 * tq + 1];
     }
-    const Tile t = load_tile(p, tile_begin + ti);
-    const uint8_t* st = smem + (ti % NSTAGE) * kStageBytes;
-    cp_async_wait<NSTAGE - 1>();
-    __syncthreads();
-
-    const bool cold = (t.kind == ASTERQ_TILE_COLD);
-    // ---------------- QK: per-warp partial scores ----------------
-    if (cold) {
-#pragma unroll 1
-      for (int m = 0; m < 4; ++m) {
-        float acc[2][4];
-#pragma unroll
-        for (int j = 0; j < 2; ++j)
-#pragma unroll
-          for (int k = 0; k < 4; ++k) acc[j][k] = 0.0f;
-        const int r0 = 16 * m + gid, r1 = r0 + 8;
-        const uint2 v0 = lds64(st + kCodesOff + r0 * 256 + ((warp ^ code_swz(r0)) << 5) + 8 * tq);
-        const uint2 v1 = lds64(st + kCodesOff + r1 * 256 + ((warp ^ code_swz(r1)) << 5) + 8 * tq);
-#pragma unroll
-        for (int s = 0; s < 4; ++s) {
-          // word w covers dims 16tq + 8w + j (nibble j); k-step s uses word s>>1,
-          // nibble pairs (0,4),(1,5) for even s and (2,6),(3,7) for odd s.
-          uint32_t x0 = (s < 2) ? v0.x : v0.y;
-          uint32_t x1 = (s < 2) ? v1.x : v1.y;
-          if (s & 1) {
-            x0 >>= 8;
-            x1 >>= 8;
-          }
-          uint32_t a[4];
-          a[0] = nib_lo_f16x2(x0);
-          a[1] = nib_lo_f16x2(x1);
-          a[2] = nib_hi_f16x2(x0);
-          a[3] = nib_hi_f16x2(x1);
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            mma_f16(acc[nt], a, qc[s][nt][0][0], qc[s][nt][0][1]);
-            mma_f16(acc[nt], a, qc[s][nt][1][0], qc[s][nt][1][1]);
-          }
-        }
-        const __half* scl = reinterpret_cast<const __half*>(st + kScaleOff);
-        const float s0 = __half2float(scl[r0 * 8 + warp]);
-        const float s1 = __half2float(scl[r1 * 8 + warp]);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          acc[nt][0] *= s0;
-          acc[nt][1] *= s0;
-          acc[nt][2] *= s1;
-          acc[nt][3] *= s1;
-        }
-        if (warp < 4) {
-          const int row = 16 * m + (lane & 7) + 8 * ((lane >> 3) & 1);
-          const int ch = 2 * warp + (lane >> 4);
-          uint32_t ra[4];
-          ldmatrix_x4(ra, smem_u32(st + kCRopeOff + row * 128 + ((ch ^ (row & 7)) << 4)));
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) mma_bf16(acc[nt], ra, qr[nt][0], qr[nt][1]);
-        }
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          *reinterpret_cast<float2*>(spart + (warp * kCold + r0) * kRows + 8 * nt + 2 * tq) =
-              make_float2(acc[nt][0], acc[nt][1]);
-          *reinterpret_cast<float2*>(spart + (warp * kCold + r1) * kRows + 8 * nt + 2 * tq) =
-              make_float2(acc[nt][2], acc[nt][3]);
-        }
-      }
-    } else {
-      float acc[2][4];
-#pragma unroll
-      for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int k = 0; k < 4; ++k) acc[j][k] = 0.0f;
-#pragma unroll
-      for (int s = 0; s < 4; ++s) {
-        const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
-        const int ch = 2 * s + (lane >> 4);
-        uint32_t a[4];
-        ldmatrix_x4(a, smem_u32(st + kHotLatOff + row * 1024 + (warp << 7) + ((ch ^ (row & 7)) << 4)));
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) mma_bf16(acc[nt], a, qh[s][nt][0], qh[s][nt][1]);
-      }
-      if (warp < 4) {
-        const int row = (lane & 7) + 8 * ((lane >> 3) & 1);
-        const int ch = 2 * warp + (lane >> 4);
-        uint32_t ra[4];
-        ldmatrix_x4(ra, smem_u32(st + kHotRopeOff + row * 128 + ((ch ^ (row & 7)) << 4)));
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) mma_bf16(acc[nt], ra, qr[nt][0], qr[nt][1]);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        *reinterpret_cast<float2*>(spart + (warp * kCold + gid) * kRows + 8 * nt + 2 * tq) =
-            make_float2(acc[nt][0], acc[nt][1]);
-        *reinterpret_cast<float2*>(spart + (warp * kCold + gid + 8) * kRows + 8 * nt + 2 * tq) =
-            make_float2(acc[nt][2], acc[nt][3]);
-      }
-    }
-    __syncthreads();
-
-    // ---------------- reduce the 8 group partials, scale, mask ----------------
-    const int ntok = cold ? kCold : kHot;
-    {
-      const int tok = tid >> 2, rq = tid & 3;
-      if (tok < ntok) {
-        float4 acc = *reinterpret_cast<const float4*>(spart + tok * kRows + 4 * rq);
-#pragma unroll
-        for (int w = 1; w < 8; ++w) {
-          const float4 v = *reinterpret_cast<const float4*>(spart + (w * kCold + tok) * kRows + 4 * rq);
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
-        }
-        const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int r = 4 * rq + c;
-          float sv = vals[c] * qinv[r];
-          if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
-          bool valid = tok < t.n;
-          if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tok) <= (rb * kRows + r) / H;
-          sred[tok * kRedStride + r] = valid ? sv : -INFINITY;
-        }
-      }
-    }
-    __syncthreads();
-
-    // ---------------- online softmax (latent_attention.py:203-220) ----------------
-    {
-      float sv[4];
-      float tmax = -INFINITY;
-      if (cold) {
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          sv[i] = sred[(4 * sj + i) * kRedStride + srow];
-          tmax = fmaxf(tmax, sv[i]);
-        }
-      } else {
-        sv[0] = sred[sj * kRedStride + srow];
-        sv[1] = sv[2] = sv[3] = -INFINITY;
-        tmax = sv[0];
-      }
-#pragma unroll
-      for (int off = 1; off < 16; off <<= 1) tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, off));
-      const float m_new = fmaxf(m_run, tmax);
-      float a_r, msub;
-      if (m_new == -INFINITY) {
-        a_r = 1.0f;
-        msub = 0.0f;
-      } else {
-        a_r = exp2f((m_run - m_new) * kLog2e);
-        msub = m_new;
-      }
-      float pv[4];
-      float psum = 0.0f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        pv[i] = exp2f((sv[i] - msub) * kLog2e);
-        psum += pv[i];
-      }
-#pragma unroll
-      for (int off = 1; off < 16; off <<= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
-      l_run = l_run * a_r + psum;
-      m_run = m_new;
-      if (sj == 0) alpha[srow] = a_r;
-      if (cold) {
-        const uint8_t* scl = st + kScaleOff;
-        uint4 sc[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sc[i] = *reinterpret_cast<const uint4*>(scl + (4 * sj + i) * 16);
-        const int kt = sj >> 2, nt = srow >> 3;
-        const int ln = (srow & 7) * 4 + (sj & 3);
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          float f[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const uint32_t wd = (&sc[i].x)[g >> 1];
-            const float s = (g & 1) ? unpack_half2(wd).y : unpack_half2(wd).x;
-            f[i] = (4 * sj + i < t.n) ? pv[i] * s : 0.0f;
-          }
-          pfc[((g * 4 + kt) * 2 + nt) * 32 + ln] = make_uint2(pack_half2(f[0], f[1]), pack_half2(f[2], f[3]));
-        }
-      } else {
-        const float pp = pv[0];
-        const __nv_bfloat16 hi = __float2bfloat16_rn(pp);
-        const __nv_bfloat16 lo = __float2bfloat16_rn(pp - __bfloat162float(hi));
-        const int nt = srow >> 3;
-        const int ln = (srow & 7) * 4 + ((sj & 7) >> 1);
-        uint16_t* ph = reinterpret_cast<uint16_t*>(pfh);
-        const int idx = (sj >> 3) * 2 + (sj & 1);
-        ph[((0 * 2 + nt) * 32 + ln) * 4 + idx] = __bfloat16_as_ushort(hi);
-        ph[((1 * 2 + nt) * 32 + ln) * 4 + idx] = __bfloat16_as_ushort(lo);
-      }
-    }
-    __syncthreads();
-
-    // ---------------- basis change before the first hot tile ----------------
-    if (!cold && order == 0) {
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int dim = 64 * warp + 2 * (4 * gid + mi) + (c >> 1);
-            const int row = 8 * nt + 2 * tq + (c & 1);
-            spart[row * kL + dim] = o[mi][nt][c];
-          }
-      __syncthreads();
-      block_fwht16(spart);
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int dim = 64 * warp + 16 * mi + gid + 8 * (c >> 1);
-            const int row = 8 * nt + 2 * tq + (c & 1);
-            o[mi][nt][c] = spart[row * kL + dim];
-          }
-      order = 1;
-      __syncthreads();
-    }
-
-    // ---------------- PV ----------------
-    {
-      float al[2][2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        al[nt][0] = alpha[8 * nt + 2 * tq];
-        al[nt][1] = alpha[8 * nt + 2 * tq + 1];
-      }
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          o[mi][nt][0] *= al[nt][0];
-          o[mi][nt][1] *= al[nt][1];
-          o[mi][nt][2] *= al[nt][0];
-          o[mi][nt][3] *= al[nt][1];
-        }
-    }
-    if (cold) {
-#pragma unroll 1
-      for (int kt = 0; kt < 4; ++kt) {
-        uint32_t x[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row = 16 * kt + 4 * tq + i;
-          x[i] = lds32(st + kCodesOff + row * 256 + ((warp ^ code_swz(row)) << 5) + 4 * gid);
-        }
-        uint2 pb[2];
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) pb[nt] = pfc[((warp * 4 + kt) * 2 + nt) * 32 + lane];
-#pragma unroll
-        for (int mi = 0; mi < 4; ++mi) {
-          // rows gid / gid+8 of m-tile mi are dims 2(4gid+mi) / 2(4gid+mi)+1 (the two
-          // nibbles of byte 4gid+mi); columns k are tokens 4tq+{0,1} / 4tq+{2,3}
-          const uint32_t sel = (uint32_t)mi | ((uint32_t)mi << 4) | ((uint32_t)(4 + mi) << 8) | ((uint32_t)(4 + mi) << 12);
-          const uint32_t z01 = prmt(x[0], x[1], sel);
-          const uint32_t z23 = prmt(x[2], x[3], sel);
-          uint32_t a[4];
-          a[0] = nib_lo_f16x2(z01);
-          a[1] = nib_hi_f16x2(z01);
-          a[2] = nib_lo_f16x2(z23);
-          a[3] = nib_hi_f16x2(z23);
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt].x, pb[nt].y);
-        }
-      }
-    } else {
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi) {
-        const int row = (lane & 7) + 8 * (lane >> 4);
-        const int ch = 2 * mi + ((lane >> 3) & 1);
-        uint32_t a[4];
-        ldmatrix_x4_trans(a, smem_u32(st + kHotLatOff + row * 1024 + (warp << 7) + ((ch ^ (row & 7)) << 4)));
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-#pragma unroll
-          for (int hl = 0; hl < 2; ++hl) {
-            const uint2 b = pfh[(hl * 2 + nt) * 32 + lane];
-            mma_bf16(o[mi][nt], a, b.x, b.y);
-          }
-        }
-      }
-    }
-    __syncthreads();
-  }
-  cp_async_wait<0>();
-
-  // ---------------- epilogue ----------------
-  if (sj == 0) {
-    mrow[srow] = m_run;
-    lrow[srow] = l_run;
-  }
-#pragma unroll
-  for (int mi = 0; mi < 4; ++mi)
+    // softmax state of rows 8nt + 2tq + cc, replicated across the 8 gid lanes
+    float m_run[2][2], l_w[2][2];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const int dim = (order == 0) ? 64 * warp + 2 * (4 * gid + mi) + (c >> 1) : 64 * warp + 16 * mi + gid + 8 * (c >> 1);
-        const int row = 8 * nt + 2 * tq + (c & 1);
-        spart[row * kL + dim] = o[mi][nt][c];
+      for (int cc = 0; cc < 2; ++cc) {
+        m_run[nt][cc] = -INFINITY;
+        l_w[nt][cc] = 0.0f;
       }
-  __syncthreads();
-  if (order == 0) block_fwht16(spart);
 
+#pragma unroll 1
+    for (int i = 0; i < n_t; ++i) {
+      const int s = i % kStages, b = i & 1;
+      const Tile t = load_tile(p, tile_begin + i);
+      mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);
+      const uint8_t* st = smem + s * kStageBytes;
+      const uint32_t sst = sbase + s * kStageBytes;
+      const bool cold = t.kind == ASTERQ_TILE_COLD;
+      float S[2][2][4];
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) S[m][nt][c] = 0.0f;
+
+      if (cold) {
+        int tok[2][2];
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(warp, m, gid + 8 * h);
+        const __half* scl = reinterpret_cast<const __half*>(st + kScales);
+#pragma unroll 1
+        for (int g = 0; g < 8; ++g) {
+          const int region = (g < 4) ? kCodesLo : kCodesHi;
+          const int chunk = 2 * (g & 3) + (tq >> 1);
+          uint2 v[2][2];
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              v[m][h] = *reinterpret_cast<const uint2*>(st + region + swz(tok[m][h], chunk) + 8 * (tq & 1));
+          float acc[2][2][4];
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) acc[m][nt][c] = 0.0f;
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            uint2 bq[2][2];
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int hl = 0; hl < 2; ++hl) bq[nt][hl] = qc[(((g * 4 + ks) * 2 + nt) * 2 + hl) * 32 + lane];
+            uint32_t a[2][4];
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              // word (ks>>1) holds dims 16tq + 8(ks>>1) + j (nibble j); k-step ks uses
+              // nibble pairs (0,4),(1,5) for even ks and (2,6),(3,7) for odd ks
+              uint32_t x0 = (ks < 2) ? v[m][0].x : v[m][0].y;
+              uint32_t x1 = (ks < 2) ? v[m][1].x : v[m][1].y;
+              if (ks & 1) {
+                x0 >>= 8;
+                x1 >>= 8;
+              }
+              a[m][0] = nib_lo_f16x2(x0);
+              a[m][1] = nib_lo_f16x2(x1);
+              a[m][2] = nib_hi_f16x2(x0);
+              a[m][3] = nib_hi_f16x2(x1);
+            }
+            // the hi and lo products of one accumulator are four MMAs apart
+#pragma unroll
+            for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+              for (int m = 0; m < 2; ++m)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) mma_f16(acc[m][nt], a[m], bq[nt][hl].x, bq[nt][hl].y);
+          }
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const float s0 = __half2float(scl[8 * tok[m][0] + g]);
+            const float s1 = __half2float(scl[8 * tok[m][1] + g]);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              S[m][nt][0] = fmaf(acc[m][nt][0], s0, S[m][nt][0]);
+              S[m][nt][1] = fmaf(acc[m][nt][1], s0, S[m][nt][1]);
+              S[m][nt][2] = fmaf(acc[m][nt][2], s1, S[m][nt][2]);
+              S[m][nt][3] = fmaf(acc[m][nt][3], s1, S[m][nt][3]);
+            }
+          }
+        }
+        // RoPE channel (bf16, exact products, not multiplied by the code scales)
+#pragma unroll
+        for (int m = 0; m < 2; ++m) {
+          const int row = qk_token(warp, m, (lane & 7) + 8 * ((lane >> 3) & 1));
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            uint32_t a[4];
+            ldmatrix_x4(a, sst + kCRope + swz(row, 2 * ks + (lane >> 4)));
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
+              mma_bf16(S[m][nt], a, bq.x, bq.y);
+            }
+          }
+        }
+      } else {
+        // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
+        // S[1] is a second partial accumulator (odd groups) folded in below
+        const int row = 8 * warp + (lane & 7);
+#pragma unroll 1
+        for (int g = 0; g < 8; g += 2) {
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            uint32_t a[2][4];
+            ldmatrix_x4(a[0], sst + g * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+            ldmatrix_x4(a[1], sst + (g + 1) * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) {
+                const uint2 bq = qh[(((g + h2) * 4 + ks) * 2 + nt) * 32 + lane];
+                mma_bf16(S[h2][nt], a[h2], bq.x, bq.y);
+              }
+          }
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            S[0][nt][c] += S[1][nt][c];
+            S[1][nt][c] = 0.0f;
+          }
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks) {
+          uint32_t a[4];
+          ldmatrix_x4(a, sst + kHRope + swz(row, 2 * ks + (lane >> 4)));
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
+            mma_bf16(S[0][nt], a, bq.x, bq.y);
+          }
+        }
+      }
+
+      // ---- finalize scores, mask, tile max ----
+      const int n_m = cold ? 2 : 1;
+      float tmax[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) tmax[nt][cc] = -INFINITY;
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int h = c >> 1, cc = c & 1;
+            const int r = 8 * nt + 2 * tq + cc;
+            const int tk = cold ? qk_token(warp, m, gid + 8 * h) : 8 * warp + gid;
+            bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
+            if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
+            float sv = S[m][nt][c] * qinv[nt][cc];
+            if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
+            sv = valid ? sv : -INFINITY;
+            S[m][nt][c] = sv;
+            tmax[nt][cc] = fmaxf(tmax[nt][cc], sv);
+          }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1)
+            tmax[nt][cc] = fmaxf(tmax[nt][cc], __shfl_xor_sync(0xffffffffu, tmax[nt][cc], off));
+      float* wmax = misc + kMWmax + (i & 1) * 64;
+      if (gid == 0) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) wmax[warp * 16 + 8 * nt + 2 * tq + cc] = tmax[nt][cc];
+      }
+      named_sync(1, 128);
+      float alpha_r[2][2], msub[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          const int r = 8 * nt + 2 * tq + cc;
+          const float mt = fmaxf(fmaxf(wmax[r], wmax[16 + r]), fmaxf(wmax[32 + r], wmax[48 + r]));
+          const float m_new = fmaxf(m_run[nt][cc], mt);
+          if (m_new == -INFINITY) {
+            alpha_r[nt][cc] = 1.0f;
+            msub[nt][cc] = 0.0f;
+          } else {
+            alpha_r[nt][cc] = exp2f((m_run[nt][cc] - m_new) * kLog2e);
+            msub[nt][cc] = m_new;
+          }
+          m_run[nt][cc] = m_new;
+        }
+      // ---- p = exp(s - m), handed to the value warps ----
+      if (i >= 2) mbar_wait(bar(kBarPEmpty + b), ((i >> 1) - 1) & 1, abort_flag);
+      float* P = reinterpret_cast<float*>(smem + kOffP + b * kPBytes);
+      float psum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+#pragma unroll
+      for (int m = 0; m < 2; ++m)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int h = c >> 1, cc = c & 1;
+            const int r = 8 * nt + 2 * tq + cc;
+            const float pv = exp2f((S[m][nt][c] - msub[nt][cc]) * kLog2e);
+            if (cold) {
+              if (m < n_m) {
+                P[r * kPStride + qk_token(warp, m, gid + 8 * h)] = pv;
+                psum[nt][cc] += pv;
+              }
+            } else if (m == 0 && h == 0) {
+              P[r * kPStride + 8 * warp + gid] = pv;
+              psum[nt][cc] += pv;
+            }
+          }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+#pragma unroll
+          for (int off = 4; off < 32; off <<= 1) psum[nt][cc] += __shfl_xor_sync(0xffffffffu, psum[nt][cc], off);
+          l_w[nt][cc] = l_w[nt][cc] * alpha_r[nt][cc] + psum[nt][cc];
+        }
+      if (warp == 0 && gid == 0) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) misc[kMAlpha + b * 16 + 8 * nt + 2 * tq + cc] = alpha_r[nt][cc];
+      }
+      mbar_arrive(bar(kBarPFull + b));
+      mbar_arrive(bar(kBarEmpty + s));
+    }
+    // final per-warp sums and the running max
+    named_sync(1, 128);
+    if (gid == 0) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          misc[kMLw + warp * 16 + 8 * nt + 2 * tq + cc] = l_w[nt][cc];
+          if (warp == 0) misc[kMWmax + 8 * nt + 2 * tq + cc] = m_run[nt][cc];
+        }
+    }
+  } else {
+    // =====================================================================
+    // value warps: scale group g = warp - 4, latent dims [64g, 64g + 64)
+    // =====================================================================
+    const int g = warp - kScoreWarps;
+    float o[4][2][4];
+#pragma unroll
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int d = 0; d < 4; ++d) o[a][c][d] = 0.0f;
+    // order 0: accumulator holds cold tokens, rotated basis, code-derived row order
+    // order 1: plain basis, natural row order
+    int order = 1;
+    if (n_t > 0) order = (load_tile(p, tile_begin).kind == ASTERQ_TILE_COLD) ? 0 : 1;
+    // [16][512] scratch, usable once the cold query fragments are no longer read
+    float* scratch_o = reinterpret_cast<float*>(smem + kOffQc);
+    const int region = (g < 4) ? kCodesLo : kCodesHi;
+    const int cchunk = 2 * (g & 3) + (gid >> 2);
+
+    auto store_o = [&]() {
+#pragma unroll
+      for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            const int dim = (order == 0) ? 64 * g + 2 * (4 * gid + mi) + (c >> 1) : 64 * g + 16 * mi + gid + 8 * (c >> 1);
+            scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + dim] = o[mi][nt][c];
+          }
+    };
+
+#pragma unroll 1
+    for (int i = 0; i < n_t; ++i) {
+      const int s = i % kStages, b = i & 1;
+      const Tile t = load_tile(p, tile_begin + i);
+      mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
+      mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);  // TMA data visible to this warp
+      const uint8_t* st = smem + s * kStageBytes;
+      const uint32_t sst = sbase + s * kStageBytes;
+      const float* P = reinterpret_cast<const float*>(smem + kOffP + b * kPBytes);
+      const bool cold = t.kind == ASTERQ_TILE_COLD;
+
+      if (!cold && order == 0) {
+        // first hot tile after cold ones: rotate the accumulator back (O = H O_rot)
+        store_o();
+        named_sync(2, 32 * kValueWarps);
+        warp_fwht_rows(scratch_o, 2 * g, 2, lane);
+        named_sync(2, 32 * kValueWarps);
+        order = 1;
+#pragma unroll
+        for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c)
+              o[mi][nt][c] = scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + 64 * g + 16 * mi + gid + 8 * (c >> 1)];
+      }
+      {
+        float al[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          al[nt][0] = misc[kMAlpha + b * 16 + 8 * nt + 2 * tq];
+          al[nt][1] = misc[kMAlpha + b * 16 + 8 * nt + 2 * tq + 1];
+        }
+#pragma unroll
+        for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            o[mi][nt][0] *= al[nt][0];
+            o[mi][nt][1] *= al[nt][1];
+            o[mi][nt][2] *= al[nt][0];
+            o[mi][nt][3] *= al[nt][1];
+          }
+      }
+      if (cold) {
+        const __half* scl = reinterpret_cast<const __half*>(st + kScales);
+#pragma unroll 2
+        for (int kt = 0; kt < kColdTile / 16; ++kt) {
+          // tokens 16kt + {2tq, 2tq+1, 2tq+8, 2tq+9} are this lane's k indices
+          const int t0 = 16 * kt + 2 * tq;
+          const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
+          float f[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) f[j] = (tk[j] < t.n) ? __half2float(scl[8 * tk[j] + g]) : 0.0f;
+          uint32_t pb[2][2];  // [ntile][b0/b1]: (p * scale) in fp16
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const float2 p01 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + t0);
+            const float2 p89 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + t0 + 8);
+            pb[nt][0] = pack_half2(p01.x * f[0], p01.y * f[1]);
+            pb[nt][1] = pack_half2(p89.x * f[2], p89.y * f[3]);
+          }
+          uint32_t x[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            x[j] = *reinterpret_cast<const uint32_t*>(st + region + swz(tk[j], cchunk) + 4 * (gid & 3));
+#pragma unroll
+          for (int mi = 0; mi < 4; ++mi) {
+            // rows gid / gid+8 of m-tile mi are dims 2(4gid+mi) / 2(4gid+mi)+1 of group g
+            const uint32_t sel =
+                (uint32_t)mi | ((uint32_t)mi << 4) | ((uint32_t)(4 + mi) << 8) | ((uint32_t)(4 + mi) << 12);
+            const uint32_t z01 = prmt(x[0], x[1], sel);
+            const uint32_t z23 = prmt(x[2], x[3], sel);
+            uint32_t a[4];
+            a[0] = nib_lo_f16x2(z01);
+            a[1] = nib_hi_f16x2(z01);
+            a[2] = nib_lo_f16x2(z23);
+            a[3] = nib_hi_f16x2(z23);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt][0], pb[nt][1]);
+          }
+        }
+      } else {
+        // rows beyond n hold stale data: zero this warp's latent block there
+        // (p is 0 for them, but 0 x NaN would poison the accumulator)
+        if (t.n < kHotTile) {
+          for (int e = lane; e < (kHotTile - t.n) * 8; e += 32)
+            *reinterpret_cast<uint4*>(smem + s * kStageBytes + g * kHotBlock + (t.n + e / 8) * 128 + (e % 8) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          __syncwarp();
+        }
+#pragma unroll 1
+        for (int kt = 0; kt < kHotTile / 16; ++kt) {
+          uint32_t pb[2][2][2];  // [ntile][hi/lo][b0/b1]
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const float2 p01 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + 16 * kt + 2 * tq);
+            const float2 p89 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + 16 * kt + 2 * tq + 8);
+            const uint32_t h0 = pack_bf162(p01.x, p01.y), h1 = pack_bf162(p89.x, p89.y);
+            const float2 r0 = unpack_bf162(h0), r1 = unpack_bf162(h1);
+            pb[nt][0][0] = h0;
+            pb[nt][0][1] = h1;
+            pb[nt][1][0] = pack_bf162(p01.x - r0.x, p01.y - r0.y);
+            pb[nt][1][1] = pack_bf162(p89.x - r1.x, p89.y - r1.y);
+          }
+          uint32_t a[4][4];
+#pragma unroll
+          for (int mi = 0; mi < 4; ++mi) {
+            const int row = 16 * kt + (lane & 7) + 8 * (lane >> 4);
+            ldmatrix_x4_trans(a[mi], sst + g * kHotBlock + swz(row, 2 * mi + ((lane >> 3) & 1)));
+          }
+#pragma unroll
+          for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+            for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) mma_bf16(o[mi][nt], a[mi], pb[nt][hl][0], pb[nt][hl][1]);
+        }
+        fence_async_shared();  // the zero fill precedes the next TMA write of this stage
+      }
+      mbar_arrive(bar(kBarPEmpty + b));
+      mbar_arrive(bar(kBarEmpty + s));
+      if (warp == kProducerWarp) {
+        // refill this stage with tile i + 3 once every warp has released tile i
+        if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag))
+          issue(i + kStages);
+        __syncwarp();
+      }
+    }
+    // accumulator -> scratch in natural order, rotated back if it is still rotated
+    store_o();
+    named_sync(2, 32 * kValueWarps);
+    if (order == 0) {
+      warp_fwht_rows(scratch_o, 2 * g, 2, lane);
+      named_sync(2, 32 * kValueWarps);
+    }
+  }
+  __syncthreads();
+
+  // ---------------- epilogue: normalize or write the partial record ----------------
+  const float* O = reinterpret_cast<const float*>(smem + kOffQc);
+  const float* lw = misc + kMLw;
+  const float* mrow = misc + kMWmax;
   if (slot == -1) {
-    for (int i = tid; i < kRows * kL / 4; i += kThreads) {
-      const int r = i >> 7, c4 = i & 127;
+    for (int e = tid; e < kRows * kL / 4; e += kThreads) {
+      const int r = e >> 7, c4 = e & 127;
       if (r >= n_rows) continue;
-      const float inv = 1.0f / fmaxf(lrow[r], 1e-20f);
-      const float4 v = *reinterpret_cast<const float4*>(spart + r * kL + 4 * c4);
+      const float l = lw[r] + lw[16 + r] + lw[32 + r] + lw[48 + r];
+      const float inv = 1.0f / fmaxf(l, 1e-20f);
+      const float4 v = *reinterpret_cast<const float4*>(O + r * kL + 4 * c4);
       const int64_t off = (out_row0 + r) * kL + 4 * c4;
       if (p.out_dtype == ASTERQ_DTYPE_F32) {
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) =
@@ -655,16 +852,17 @@ __global__ void __launch_bounds__(kThreads, 2) decode_kernel(const asterq_decode
     float* wo = reinterpret_cast<float*>(p.workspace);
     float* wm = wo + (int64_t)p.n_slots * kRows * kL;
     float* wl = wm + (int64_t)p.n_slots * kRows;
-    for (int i = tid; i < kRows * kL / 4; i += kThreads) {
-      const int r = i >> 7, c4 = i & 127;
+    for (int e = tid; e < kRows * kL / 4; e += kThreads) {
+      const int r = e >> 7, c4 = e & 127;
       *reinterpret_cast<float4*>(wo + ((int64_t)slot * kRows + r) * kL + 4 * c4) =
-          *reinterpret_cast<const float4*>(spart + r * kL + 4 * c4);
+          *reinterpret_cast<const float4*>(O + r * kL + 4 * c4);
     }
     if (tid < kRows) {
       wm[(int64_t)slot * kRows + tid] = mrow[tid];
-      wl[(int64_t)slot * kRows + tid] = lrow[tid];
+      wl[(int64_t)slot * kRows + tid] = lw[tid] + lw[16 + tid] + lw[32 + tid] + lw[48 + tid];
     }
   }
+  if (tid == 0 && *abort_flag && p.device_status) atomicExch(p.device_status, 1);
 }
 
 // Merge partial records (latent_attention.py:212-220 applied across splits).
@@ -700,17 +898,18 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   }
 }
 
-constexpr int kNStage = 2;
-
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
 int validate(const asterq_decode_params* p) {
   if (!p) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null params");
   if (p->latent_dim != kL || p->rope_dim != kRope || p->group_size != 64)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: geometry latent=%d rope=%d group=%d unsupported (512/64/64)",
                      p->latent_dim, p->rope_dim, p->group_size);
   if (p->n_heads <= 0) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: n_heads must be positive");
-  if (p->page_tokens <= 0 || p->page_tokens % kCold)
-    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: page_tokens %d must be a positive multiple of %d",
-                     p->page_tokens, kCold);
+  if (p->page_tokens <= 0 || p->page_tokens % 16)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: page_tokens %d must be a positive multiple of 16",
+                     p->page_tokens);
   if (p->out_dtype != ASTERQ_DTYPE_F32 && p->out_dtype != ASTERQ_DTYPE_BF16)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: out_dtype must be f32 or bf16");
   if (p->n_items < 0 || p->n_tiles < 0 || p->n_combine < 0 || p->n_slots < 0)
@@ -721,15 +920,57 @@ int validate(const asterq_decode_params* p) {
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null cold pool");
   if (p->n_hot_pages > 0 && (!p->hot_latent || !p->hot_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null hot pool");
+  if (p->n_items > 0 && p->total_q > 0 && (!p->new_latent || !p->new_rope))
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null new-token arrays");
   const void* aligned[] = {p->q_lat, p->q_rope, p->new_latent, p->new_rope, p->cold_codes, p->cold_scales,
                            p->cold_rope, p->hot_latent, p->hot_rope, p->tiles, p->items, p->combine, p->out,
                            p->workspace};
   for (const void* ptr : aligned)
-    if (reinterpret_cast<uintptr_t>(ptr) & 15) return set_error(ASTERQ_ERR_MISALIGNED, "decode: pointers must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(ptr) & 15)
+      return set_error(ASTERQ_ERR_MISALIGNED, "decode: pointers must be 16-byte aligned");
   const int64_t need = (int64_t)p->n_slots * kRows * (kL + 2) * 4;
   if (p->n_slots > 0 && (!p->workspace || p->workspace_bytes < need))
     return set_error(ASTERQ_ERR_WORKSPACE, "decode: workspace of %lld bytes < %lld needed",
                      (long long)p->workspace_bytes, (long long)need);
+  return ASTERQ_OK;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// 2-D byte tensor [rows][row_bytes] read in boxes of [box_rows][128 B] with the
+// 128-byte swizzle.  An empty pool gets a map of one row of a valid buffer; the
+// kernel never references it (tiles of that kind fail validation).
+int make_map(CUtensorMap* map, const void* base, int64_t rows, int row_bytes, int box_rows, const void* dummy,
+             int dummy_row_bytes) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn) return set_error(ASTERQ_ERR_CUDA, "decode: cuTensorMapEncodeTiled unavailable");
+  if (!base || rows <= 0) {
+    base = dummy;
+    rows = 1;
+    row_bytes = dummy_row_bytes;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(ASTERQ_ERR_CUDA, "decode: tensor map encoding failed (%d)", (int)r);
   return ASTERQ_OK;
 }
 
@@ -748,18 +989,29 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
   int st = dec::validate(p);
   if (st != ASTERQ_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  using S = dec::Smem<dec::kNStage>;
   if (p->n_items > 0) {
     int dev = 0;
     cudaGetDevice(&dev);
     static unsigned long long configured = 0;  // one bit per device ordinal
     if (dev >= 64 || !(configured & (1ull << dev))) {
-      cudaError_t e = cudaFuncSetAttribute(dec::decode_kernel<dec::kNStage>,
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, S::kTotal);
+      cudaError_t e =
+          cudaFuncSetAttribute(dec::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
       if (dev < 64) configured |= (1ull << dev);
     }
-    dec::decode_kernel<dec::kNStage><<<p->n_items, dec::kThreads, S::kTotal, s>>>(*p);
+    dec::TensorMaps maps;
+    // q_lat rows are 1024 bytes (16 heads x 512 bf16 at least): a valid stand-in
+    // base for the map of an empty pool
+    const void* dummy = p->q_lat;
+    const int64_t cold_rows = p->n_cold_pages * p->page_tokens, hot_rows = p->n_hot_pages * p->page_tokens;
+    if ((st = dec::make_map(&maps.codes, p->cold_codes, cold_rows, 256, dec::kColdTile, dummy, 1024)) ||
+        (st = dec::make_map(&maps.crope, p->cold_rope, cold_rows, 128, dec::kColdTile, dummy, 1024)) ||
+        (st = dec::make_map(&maps.hlat, p->hot_latent, hot_rows, 1024, dec::kHotTile, dummy, 1024)) ||
+        (st = dec::make_map(&maps.hrope, p->hot_rope, hot_rows, 128, dec::kHotTile, dummy, 1024)) ||
+        (st = dec::make_map(&maps.nlat, p->new_latent, p->total_q, 1024, dec::kHotTile, dummy, 1024)) ||
+        (st = dec::make_map(&maps.nrope, p->new_rope, p->total_q, 128, dec::kHotTile, dummy, 1024)))
+      return st;
+    dec::decode_kernel<<<p->n_items, dec::kThreads, dec::kSmemBytes, s>>>(*p, maps);
     st = check_launch("latent_decode");
     if (st != ASTERQ_OK) return st;
   }
@@ -767,8 +1019,8 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     const float* wo = reinterpret_cast<const float*>(p->workspace);
     const float* wm = wo + (int64_t)p->n_slots * dec::kRows * dec::kL;
     const float* wl = wm + (int64_t)p->n_slots * dec::kRows;
-    dec::combine_kernel<<<dim3(p->n_combine, dec::kL / dec::kCombDims), 256, 0, s>>>(wo, wm, wl, p->combine, p->n_slots, dec::kL, p->out,
-                                                     p->out_dtype);
+    dec::combine_kernel<<<dim3(p->n_combine, dec::kL / dec::kCombDims), 256, 0, s>>>(
+        wo, wm, wl, p->combine, p->n_slots, dec::kL, p->out, p->out_dtype);
     st = check_launch("splitkv_combine");
   }
   return st;
@@ -784,11 +1036,12 @@ extern "C" int asterq_splitkv_combine(const float* partials, int32_t n_slots, co
   if (!partials || !combine || !out) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "combine: null pointer");
   if (out_dtype != ASTERQ_DTYPE_F32 && out_dtype != ASTERQ_DTYPE_BF16)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "combine: out_dtype must be f32 or bf16");
-  if ((reinterpret_cast<uintptr_t>(partials) | reinterpret_cast<uintptr_t>(combine) | reinterpret_cast<uintptr_t>(out)) & 15)
+  if ((reinterpret_cast<uintptr_t>(partials) | reinterpret_cast<uintptr_t>(combine) | reinterpret_cast<uintptr_t>(out)) &
+      15)
     return set_error(ASTERQ_ERR_MISALIGNED, "combine: pointers must be 16-byte aligned");
   const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
   const float* wl = wm + (int64_t)n_slots * dec::kRows;
-  dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(partials, wm, wl, combine, n_slots,
-                                                                                     latent_dim, out, out_dtype);
+  dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      partials, wm, wl, combine, n_slots, latent_dim, out, out_dtype);
   return check_launch("splitkv_combine");
 }

@@ -1,0 +1,465 @@
+"""Decode-attention benchmark (one JSON line on rank 0).
+
+Workload (per GPU): BASELINE config 3, ragged continuous-batching decode --
+64 sequences with seeded context lengths U[1024, 32768], the newest
+min(len, 2048) tokens hot BF16, the rest INT4 chunks of 512, 16 heads, latent
+512 + RoPE 64, q_len 1.  Sequences are sharded across GPUs: every rank owns its
+own 64-sequence batch (weak scaling, no collective in the timed step).
+
+  value  device-timed whole-job seq-steps/s (CUDA events, max over ranks),
+         inputs resident in HBM (0.53 GB per GPU, larger than the 126 MB L2)
+  e2e    the same metric through the public API (asterq.decode.latent_decode)
+         with the step's query/new-token inputs copied from pinned host memory
+         and the context latents copied back, every step
+  roofline  achieved HBM GB/s of the decode kernel = algorithmic bytes per
+         launch / its CUDA-event duration, against MEASURED_PEAKS.json
+  cpu_baseline  the CPU oracle port on the host cores (bounded sample)
+
+  python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for p in (ROOT, ROOT / "asterlm-frontier_b200"):
+    if str(p) not in sys.path:
+        sys.path.insert(0, str(p))
+
+METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"] if (ROOT / "BASELINE.json").exists() else \
+    "decode-attn seq-steps/s per GPU and % of HBM peak, 1/2/4/8 B200 vs host CPU"
+UNIT = "seq-steps/s"
+SOFTMAX_SCALE = 1.0 / math.sqrt(512 + 64)
+WORKLOAD = ("C3 ragged continuous-batching decode: 64 seqs/GPU, ctx U[1024,32768] (seed 0), hot min(len,2048) "
+            "BF16 + INT4 chunks of 512, 16 heads, latent 512 + RoPE 64, q_len 1")
+
+
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def measured_peaks() -> tuple[float, str]:
+    f = ROOT / "MEASURED_PEAKS.json"
+    if f.exists():
+        return float(json.loads(f.read_text())["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic() -> float | None:
+    """dram bytes per decode launch from the committed ncu summary, if any."""
+    f = ROOT / "profiles" / "decode_kernel_c3.md"
+    if not f.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch\s*=\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except (OSError, ValueError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self._t.join(timeout=2)
+
+    def summary(self) -> dict:
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {
+            "sm_mhz": statistics.median(sms) if sms else None,
+            "sm_max_mhz": max(maxes) if maxes else None,
+            "reasons": sorted(reasons),
+            "samples": len(sms),
+        }
+
+
+def build_workload(device, rank: int, n_seqs: int = 64, keep_host=None):
+    from asterq.synth import c3_lengths, make_workload
+
+    lens = c3_lengths(0, n_seqs)
+    return make_workload("C3", lens, [min(n, 2048) for n in lens], q_len=1, seed=1000 + rank, device=device,
+                         keep_host=keep_host)
+
+
+def cpu_oracle_rate(host_seqs: dict, lengths, hot, budget_s: float = 12.0, threads: int | None = None):
+    """Oracle decode (numpy port of the reference path) on host cores; seq-steps/s."""
+    import numpy as np
+
+    from oracle import hq4_oracle as O
+
+    caches = []
+    for i, h in sorted(host_seqs.items()):
+        lat = h["latent"].float().numpy()
+        rope = h["rope"].float().numpy()
+        n = lengths[i]
+        caches.append((O.build_cache_split(lat[:n], rope[:n], hot[i], 512), h, lat[n:], rope[n:]))
+    done, t0 = 0, time.perf_counter()
+    tokens = 0
+    while True:
+        for cache, h, nl, nr in caches:
+            O.absorbed_decode(h["q_lat"].float().numpy(), h["q_rope"].float().numpy(), nl, nr, cache, SOFTMAX_SCALE)
+            done += 1
+            tokens += cache.length
+            if time.perf_counter() - t0 > budget_s:
+                break
+        if time.perf_counter() - t0 > budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return done / dt, done, tokens, dt
+
+
+def run_reference_arm(args) -> None:
+    """--impl reference: the CPU oracle port of the reference path, all host threads."""
+    import torch
+
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from asterq.synth import c3_lengths
+
+    lens = c3_lengths(0, 64)
+    hot = [min(n, 2048) for n in lens]
+    # the sample: 8 sequences of the config-3 batch, generated on the CPU
+    pick = list(range(0, 64, 8))
+    host = {}
+    g = torch.Generator().manual_seed(7)
+    from asterq.synth import outlier_channels
+
+    oc = outlier_channels(7)
+    for i in pick:
+        n = lens[i]
+        lat = torch.randn(n + 1, 512, generator=g)
+        lat[:, oc] *= 20
+        host[i] = {"latent": lat.to(torch.bfloat16), "rope": torch.randn(n + 1, 64, generator=g).to(torch.bfloat16),
+                   "q_lat": torch.randn(1, 16, 512, generator=g).to(torch.bfloat16),
+                   "q_rope": torch.randn(1, 16, 64, generator=g).to(torch.bfloat16)}
+    cores = host_cores()
+    for _ in range(max(0, args.warmup)):
+        cpu_oracle_rate(host, lens, hot, budget_s=0.5)
+    rates = []
+    t0 = time.perf_counter()
+    for _ in range(max(1, args.steps)):
+        r, _, _, _ = cpu_oracle_rate(host, lens, hot, budget_s=2.0)
+        rates.append(r)
+    elapsed = time.perf_counter() - t0
+    value = statistics.median(rates)
+    sample = f"{len(pick)} config-3 sequences (every 8th), each step = 2 s of oracle decodes"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": elapsed / max(1, args.steps) * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": sample},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="asterq", choices=["asterq", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from asterq import _lib
+    from asterq.decode import DeviceDecodePlan, latent_decode, make_params
+    from asterq.plan import build_plan
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    args.warmup = max(args.warmup, 3)
+
+    keep = set(range(0, 64, 16)) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    wl = build_workload(dev, rank, keep_host=keep)
+    plan = build_plan(wl.layouts, wl.n_heads)
+    dplan = DeviceDecodePlan(plan, dev)
+    out = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(dev)
+    sh = stream.cuda_stream
+
+    # decode-only and combine-only parameter blocks (same kernels as latent_decode)
+    p_dec = make_params(wl.pools, dplan, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out,
+                        n_heads=wl.n_heads, softmax_scale=SOFTMAX_SCALE)
+    n_combine = p_dec.n_combine
+    p_dec.n_combine = 0
+    ws = dplan.workspace
+
+    def step_device():
+        _lib.check(lib.asterq_latent_decode(ctypes.byref(p_dec), sh))
+        if n_combine:
+            _lib.check(lib.asterq_splitkv_combine(ws.data_ptr(), plan.n_slots, dplan.combine.data_ptr(), n_combine,
+                                                  512, out.data_ptr(), _lib.DTYPE_BF16, sh))
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x: float) -> float:
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize()
+
+    # ---- device-timed steps ----
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(stream)
+        for e0, e1, e2 in ev:
+            e0.record(stream)
+            _lib.check(lib.asterq_latent_decode(ctypes.byref(p_dec), sh))
+            e1.record(stream)
+            if n_combine:
+                _lib.check(lib.asterq_splitkv_combine(ws.data_ptr(), plan.n_slots, dplan.combine.data_ptr(),
+                                                      n_combine, 512, out.data_ptr(), _lib.DTYPE_BF16, sh))
+            e2.record(stream)
+        t_end.record(stream)
+        torch.cuda.synchronize()
+    barrier()
+    total_ms = max_over_ranks(t_start.elapsed_time(t_end))
+    dec_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1, _ in ev)
+    comb_ms = statistics.mean(e1.elapsed_time(e2) for _, e1, e2 in ev)
+    ms_per_step = total_ms / args.steps
+    n_seqs = len(wl.lengths)
+    value = world * n_seqs / (ms_per_step / 1e3)
+
+    # ---- end-to-end through the public API with host buffers ----
+    host_in = [t.cpu().pin_memory() for t in (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)]
+    dev_in = [torch.empty_like(t) for t in (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)]
+    host_out = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def step_e2e():
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        latent_decode(wl.pools, dplan, *dev_in, softmax_scale=SOFTMAX_SCALE, out=out)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(args.warmup):
+        step_e2e()
+    torch.cuda.synchronize()
+    barrier()
+    e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_s.record(stream)
+    for _ in range(args.steps):
+        step_e2e()
+    e_e.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e_s.elapsed_time(e_e)) / args.steps
+    e2e_value = world * n_seqs / (e2e_ms / 1e3)
+
+    peak, peak_kind = measured_peaks()
+    alg_bytes = wl.algorithmic_bytes()
+    achieved = alg_bytes / (dec_ms / 1e3) / 1e9
+    traffic = profiled_traffic()
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "int4 codes + bf16/fp16 tensor-core operands, fp32 accumulate",
+        "data": "synthetic",
+        "config": {
+            "workload": WORKLOAD,
+            "seqs_per_gpu": n_seqs,
+            "cached_tokens_per_gpu": int(sum(wl.lengths)),
+            "q_len": 1,
+            "n_heads": wl.n_heads,
+            "parallelism": f"sequence sharding x{world} (independent batches, no collective)",
+            "l2": f"no flush: {alg_bytes / 1e9:.2f} GB read per step per GPU > 126 MB L2",
+            "work_items": int(plan.items.shape[0]),
+        },
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_kind": peak_kind,
+            "traffic": traffic,
+            "kernel": "asterq::dec::decode_kernel",
+            "algorithmic_bytes_per_launch": alg_bytes,
+            "kernel_ms": dec_ms,
+            "combine_ms": comb_ms,
+        },
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms},
+        "gpu_launches": args.steps * (2 if n_combine else 1),
+        "clocks": clocks.summary(),
+    }
+
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["extras"] = extras(dev, args)
+
+    if keep:
+        rate, done, toks, dt = cpu_oracle_rate(wl.host, wl.lengths, wl.hot)
+        line["cpu_baseline"] = {
+            "value": rate, "unit": UNIT, "cores": host_cores(), "kind": "port",
+            "sample": f"{len(keep)} of the 64 sequences, {done} oracle decodes ({toks} cached tokens) in {dt:.1f} s",
+        }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def extras(dev, args) -> dict:
+    """Secondary single-GPU measurements: the write path (config 2) and configs 1, 4, 5."""
+    import torch
+
+    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.kv import quantize_tensor
+    from asterq.plan import build_plan
+    from asterq.synth import c1_inputs, c4_workload, c5_workload, PoolBuilder, outlier_channels
+
+    peak, _ = measured_peaks()
+    res = {}
+
+    def timed(fn, iters):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / iters
+
+    g = torch.Generator(device=dev).manual_seed(2)
+    x = torch.randn(64 * 4096, 512, generator=g, device=dev)
+    x[:, outlier_channels(2).to(dev)] *= 20
+    x = x.to(torch.bfloat16)
+    ms = timed(lambda: quantize_tensor(x, "hadamard_int4", group_size=64), 20)
+    b = 64 * 4096 * (1024 + 256 + 16)
+    res["c2_write_path"] = {"tokens": 64 * 4096, "ms": ms, "tokens_per_s": 64 * 4096 / ms * 1e3,
+                            "GB/s": b / ms / 1e6, "frac_hbm": b / ms / 1e6 / peak}
+    del x
+
+    def decode_rate(wl, name, iters):
+        plan = build_plan(wl.layouts, wl.n_heads)
+        dp = DeviceDecodePlan(plan, dev)
+        out = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
+        ms = timed(lambda: latent_decode(wl.pools, dp, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope,
+                                         softmax_scale=SOFTMAX_SCALE, out=out), iters)
+        b = wl.algorithmic_bytes()
+        res[name] = {"seqs": len(wl.lengths), "q_len": wl.q_len, "ms": ms, "seq_steps_per_s": len(wl.lengths) / ms * 1e3,
+                     "GB/s": b / ms / 1e6, "frac_hbm": b / ms / 1e6 / peak, "TFLOP/s": wl.flops() / ms / 1e9}
+
+    inp = c1_inputs(seed=0)
+    b1 = PoolBuilder([8192], [1024], q_len=1, n_heads=16, device=dev)
+    b1.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    decode_rate(b1.finish("C1"), "c1_single_sequence", 50)
+    wl = c4_workload(dev)
+    decode_rate(wl, "c4_long_context_1gpu", 30)
+    del wl
+    wl = c5_workload(dev)
+    decode_rate(wl, "c5_mtp_verification_1gpu", 10)
+    del wl
+    torch.cuda.empty_cache()
+    return res
+
+
+if __name__ == "__main__":
+    main()

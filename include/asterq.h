@@ -97,14 +97,14 @@ int asterq_fwht(const float* x, float* y, int64_t rows, int n, void* stream);
  *
  * Schedule (built by the host, see the Python package's plan builder):
  *   tiles [n_tiles][4] int32 = {kind, page (ASTERQ_TILE_NEW: first new-token row), token offset, n_tokens}
- *          cold tiles hold <= 64 tokens, hot/new tiles <= 16 tokens.
+ *          cold tiles hold <= 128 tokens, hot/new tiles <= 32 tokens; a tile never crosses a page.
  *   items [n_items][8] int32 = {seq, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
  *          one CTA per item; 16 query rows (t, h) per row block, rows flattened as t*n_heads + h.
  *          slot < 0: the item covers the whole sequence and writes `out` directly;
  *          slot >= 0: it writes an (m, l, o) partial to the workspace.
  *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
  * Geometry supported: latent_dim 512, rope_dim 64, scale groups of 64, page_tokens
- * a multiple of 64, q_len <= 16.
+ * a multiple of 128, q_len <= 16.  cold tiles hold <= 128 tokens, hot/new tiles <= 32.
  */
 typedef struct asterq_decode_params {
   int32_t n_heads;
@@ -137,6 +137,7 @@ typedef struct asterq_decode_params {
   void* out;
   void* workspace;
   int64_t workspace_bytes;
+  int32_t* device_status; /* optional int32 on the device: set nonzero if a pipeline wait timed out */
 } asterq_decode_params;
 
 /* Bytes of workspace asterq_latent_decode needs (n_slots partial records). */
@@ -149,9 +150,9 @@ int asterq_latent_decode(const asterq_decode_params* p, void* stream);
  * Merge split-KV partial records with the online-softmax rule of
  * latent_attention.py:212-220 (used by the decode itself and by the
  * context-parallel path after the partials of all ranks are gathered).
- *   partials  float32 [n_slots, 16, 2 + latent_dim]  record = {m, l, o[latent_dim]}; o unnormalized
+ *   partials  float32: o [n_slots][16][latent_dim] (unnormalized), then m [n_slots][16], then l [n_slots][16]
  *   combine   int32   [n_combine][4] as in asterq_decode_params
- *   out       [.., n_heads*?] rows of latent_dim in out_dtype, row index out_row0 + r
+ *   out       rows of latent_dim in out_dtype (float32 or bfloat16); job row r goes to row out_row0 + r
  */
 int asterq_splitkv_combine(const float* partials, int32_t n_slots, const int32_t* combine, int32_t n_combine,
                            int32_t latent_dim, void* out, int32_t out_dtype, void* stream);

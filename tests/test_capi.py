@@ -40,8 +40,8 @@ def test_version_and_error_string():
 
 
 def test_struct_layout_matches_header():
-    # sizes of the C struct: 6 int32 + 2 float + 3 int64 + 4 int32 + 14 pointers + int64
-    assert ctypes.sizeof(_lib.DecodeParams) == 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8
+    # sizes of the C struct: 6 int32 + 2 float + 3 int64 + 4 int32 + 14 pointers + int64 + pointer
+    assert ctypes.sizeof(_lib.DecodeParams) == 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8 + 8
 
 
 def test_quantize_rejects_bad_sizes_without_touching_the_gpu():
@@ -73,6 +73,7 @@ def _params(**kw) -> _lib.DecodeParams:
         (dict(latent_dim=256), _lib.ASTERQ_ERR_UNSUPPORTED),
         (dict(rope_dim=32), _lib.ASTERQ_ERR_UNSUPPORTED),
         (dict(page_tokens=100), _lib.ASTERQ_ERR_UNSUPPORTED),
+        (dict(page_tokens=0), _lib.ASTERQ_ERR_UNSUPPORTED),
         (dict(out_dtype=_lib.DTYPE_F16), _lib.ASTERQ_ERR_UNSUPPORTED),
         (dict(n_heads=0), _lib.ASTERQ_ERR_INVALID_ARGUMENT),
         (dict(n_items=3), _lib.ASTERQ_ERR_INVALID_ARGUMENT),  # null tables
