@@ -40,6 +40,7 @@ EXPORTED_SYMBOLS = (
     "asterq_fwht",
     "asterq_decode_workspace_bytes",
     "asterq_latent_decode",
+    "asterq_latent_decode_noalloc",
     "asterq_splitkv_combine",
 )
 
@@ -124,6 +125,8 @@ def load() -> ctypes.CDLL:
     lib.asterq_decode_workspace_bytes.argtypes = [ctypes.POINTER(DecodeParams)]
     lib.asterq_latent_decode.restype = ctypes.c_int
     lib.asterq_latent_decode.argtypes = [ctypes.POINTER(DecodeParams), vp]
+    lib.asterq_latent_decode_noalloc.restype = ctypes.c_int
+    lib.asterq_latent_decode_noalloc.argtypes = [ctypes.POINTER(DecodeParams), vp]
     lib.asterq_splitkv_combine.restype = ctypes.c_int
     lib.asterq_splitkv_combine.argtypes = [vp, i32, vp, i32, i32, vp, i32, vp]
     _lib = lib

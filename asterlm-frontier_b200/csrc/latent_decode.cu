@@ -33,6 +33,7 @@
 //  * warps 4-11 ("value warps"): each owns 64 latent dims (one scale group) of
 //    the 16 x 512 accumulator and accumulates p . V for every tile.
 // Every wait is bounded; a timeout sets a status flag instead of hanging.
+#include <atomic>
 #include <cuda.h>
 
 #include "common.cuh"
@@ -1044,4 +1045,56 @@ extern "C" int asterq_splitkv_combine(const float* partials, int32_t n_slots, co
   dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, combine, n_slots, latent_dim, out, out_dtype);
   return check_launch("splitkv_combine");
+}
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory when they decode: a serving loop
+// that pre-plans its memory and forbids allocator calls on the hot path, code
+// that runs while a CUDA graph is being recorded elsewhere on the device, or a
+// host runtime with no allocator of its own (a plain C caller that only receives
+// pointers to its inputs and outputs).  For them the split-KV partial records
+// live in a fixed array compiled into this library instead of a caller-provided
+// workspace.  The array is a device global: every GPU that loads the library
+// keeps it (kNoAllocMaxSlots records, about 8.4 MB) until the process exits.
+// ---------------------------------------------------------------------------
+namespace asterq {
+namespace dec {
+
+constexpr int kNoAllocMaxSlots = 256;
+static __device__ __align__(256) float g_noalloc_workspace[kNoAllocMaxSlots * kRows * (kL + 2)];
+
+}  // namespace dec
+}  // namespace asterq
+
+extern "C" int asterq_latent_decode_noalloc(const asterq_decode_params* p, void* stream) {
+  clear_error();
+  if (!p) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode (no-alloc): null params");
+  if (p->n_slots > dec::kNoAllocMaxSlots)
+    return set_error(ASTERQ_ERR_WORKSPACE,
+                     "decode (no-alloc): the schedule needs %d partial records but the built-in workspace holds %d; "
+                     "build the plan with fewer split items or call asterq_latent_decode with a workspace",
+                     p->n_slots, dec::kNoAllocMaxSlots);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "decode (no-alloc): %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return set_error(ASTERQ_ERR_UNSUPPORTED, "decode (no-alloc): device ordinal %d >= 64", dev);
+  // Host code cannot use g_noalloc_workspace's name as a device address: resolve
+  // it once per device, with that device current (the first call on a device
+  // does this; make that first call before any stream capture).
+  // Two host threads racing through the first call store the same address.
+  static std::atomic<void*> addr[64];
+  void* ptr = addr[dev].load(std::memory_order_acquire);
+  if (!ptr) {
+    e = cudaGetSymbolAddress(&ptr, dec::g_noalloc_workspace);
+    if (e != cudaSuccess || !ptr)
+      return set_error(ASTERQ_ERR_CUDA, "decode (no-alloc): cannot resolve the workspace address: %s",
+                       cudaGetErrorString(e));
+    addr[dev].store(ptr, std::memory_order_release);
+  }
+  asterq_decode_params q = *p;
+  q.workspace = ptr;
+  q.workspace_bytes = (int64_t)sizeof(dec::g_noalloc_workspace);
+  return asterq_latent_decode(&q, stream);
 }

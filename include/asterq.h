@@ -147,6 +147,23 @@ int64_t asterq_decode_workspace_bytes(const asterq_decode_params* p);
 int asterq_latent_decode(const asterq_decode_params* p, void* stream);
 
 /*
+ * Same as asterq_latent_decode, but allocates nothing and ignores
+ * p->workspace / p->workspace_bytes: the split-KV partial records go to a
+ * fixed array inside this library (room for 256 records, about 8.4 MB on every
+ * GPU that loads the library, kept until the process exits).  No counterpart in
+ * the reference; it exists for callers that cannot allocate device memory at
+ * decode time (pre-planned serving loops, plain C hosts that only hold pointers
+ * to their inputs and outputs).
+ *   - Schedules needing more than 256 partial records are rejected with
+ *     ASTERQ_ERR_WORKSPACE (build the plan with fewer split items).
+ *   - The first call on a device resolves the array's address; make that first
+ *     call before any stream capture.
+ *   - All calls share the one array: calls that overlap on the GPU (for
+ *     example on two streams) race and corrupt each other's results.
+ */
+int asterq_latent_decode_noalloc(const asterq_decode_params* p, void* stream);
+
+/*
  * Merge split-KV partial records with the online-softmax rule of
  * latent_attention.py:212-220 (used by the decode itself and by the
  * context-parallel path after the partials of all ranks are gathered).
