@@ -71,6 +71,11 @@ ASTERQ_DEVICE uint32_t hsub2_u32(uint32_t a, uint32_t b) {
   asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
   return d;
 }
+ASTERQ_DEVICE uint32_t hmul2_u32(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
 ASTERQ_DEVICE uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
   uint32_t d;
   asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
@@ -126,6 +131,31 @@ ASTERQ_DEVICE void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, 
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+
+// int8 tensor path (m16n8k32, int32 accumulate).  mma_s8 accumulates in place;
+// mma_s8_from starts every accumulator element at `c`.
+ASTERQ_DEVICE void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+ASTERQ_DEVICE void mma_s8_from(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c) {
+  asm(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c));
+}
+
+// INT4 nibbles u = code + 8 -> signed bytes 16 * code: a nibble placed in the high half
+// of a byte is 16u, and flipping bit 7 subtracts 128 = 16 * 8.  The four high nibbles
+// (odd values of a packed word) need one logic op, the four low nibbles a shift first.
+ASTERQ_DEVICE uint32_t s8_hi_nibbles(uint32_t x) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(x), "r"(0xF0F0F0F0u), "r"(0x80808080u));  // (a & b) ^ c
+  return d;
+}
+ASTERQ_DEVICE uint32_t s8_lo_nibbles(uint32_t x) { return s8_hi_nibbles(x << 4); }
 
 ASTERQ_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 

@@ -15,10 +15,15 @@
 //  * Values of cold tokens accumulate in the rotated basis, those of hot tokens in
 //    the plain basis, under one running (max, sum); the rotated accumulator is
 //    rotated back once (O = H O_rot + O_plain).
-//  * Tensor-core operand precision: cold QK = fp16 codes (exact) x rotated query
-//    split hi + lo in fp16 after a per-row power-of-two prescale; cold PV = fp16
-//    codes x fp16 (p * scale); hot QK = bf16 latent x bf16 query (exact); hot PV =
-//    bf16 latent x p split hi + lo in bf16; fp32 accumulation everywhere.
+//  * Tensor-core operands: cold QK runs on the int8 tensor path (m16n8k32): the
+//    codes expand to exact signed bytes (16 x code, two logic ops per four
+//    values) and the rotated query is a per-row 16-bit fixed-point number split
+//    into two int8 limbs; each scale group's integer dot products start from a
+//    float-exponent bias so that the int32 accumulator reads as an exact fp32
+//    value, then scale x (256 hi + lo) is accumulated in fp32.  Cold PV = fp16
+//    codes x fp16 p times the fp16 code scale; hot QK = bf16 latent x bf16
+//    query (exact); hot PV = bf16 latent x p split hi + lo in bf16; RoPE = bf16
+//    x bf16; fp32 accumulation everywhere.
 //
 // CTA organisation (one CTA per work item, 12 warps):
 //  * TMA producer (lane 0 of warp 4): streams the item's tiles (128 cold tokens or
@@ -28,8 +33,9 @@
 //  * warps 0-3 ("score warps"): each owns a quarter of a tile's tokens and all 512
 //    latent dims, so every score row is complete inside one warp (no cross-warp
 //    reduction).  They finish the online softmax (one named barrier to combine the
-//    four warps' tile maxima) and hand p to the value warps through a
-//    double-buffered shared-memory tile.
+//    four warps' tile maxima) and hand p to the value warps through
+//    double-buffered shared memory (cold tiles: fp16 [token][row] plus the
+//    tokens' code scales by group; hot tiles: fp32 [row][token]).
 //  * warps 4-11 ("value warps"): each owns 64 latent dims (one scale group) of
 //    the 16 x 512 accumulator and accumulates p . V for every tile.
 // Every wait is bounded; a timeout sets a status flag instead of hanging.
@@ -62,14 +68,16 @@ constexpr int kHotBlock = 4096;    // hot: latent scale-group g at g*4096: [32][
 constexpr int kHRope = 32768;      // hot: [32][128 B] RoPE keys, SW128
 constexpr int kStageBytes = 51200;
 
-constexpr int kOffQc = kStages * kStageBytes;  // cold query B fragments [8][4][2][2][32] uint2
-constexpr int kOffQh = kOffQc + 32768;          // hot query B fragments  [8][4][2][32] uint2
+constexpr int kOffQi = kStages * kStageBytes;  // cold query int8 limb fragments [16 k-steps][2][32] uint4
+                                               // (32 KB region: the [16][512] fp32 scratch after the tiles)
+constexpr int kOffQh = kOffQi + 32768;          // hot query B fragments  [8][4][2][32] uint2
 constexpr int kOffQr = kOffQh + 16384;          // rope query B fragments [4][2][32] uint2
 constexpr int kPStride = kColdTile + 4;         // p tile row stride (floats)
 constexpr int kPBytes = kRows * kPStride * 4;
 constexpr int kOffP = kOffQr + 2048;            // 2 x p tile [16][132] fp32
-constexpr int kOffMisc = kOffP + 2 * kPBytes;   // 256 floats of per-row scalars
-constexpr int kOffBar = kOffMisc + 1024;        // mbarriers
+constexpr int kOffST = kOffP + 2 * kPBytes;     // 2 x cold code scales [8 groups][128 tokens] fp16
+constexpr int kOffMisc = kOffST + 2 * 2048;     // 512 floats of per-row scalars
+constexpr int kOffBar = kOffMisc + 2048;        // mbarriers
 constexpr int kSmemBytes = kOffBar + 128 + 1024;  // + alignment slack
 
 // misc (float index)
@@ -78,6 +86,9 @@ constexpr int kMWmax = 32;     // [2][4][16]; after the tile loop [16] = final r
 constexpr int kMLw = 160;      // [4][16]
 constexpr int kMQscale = 224;  // [16]
 constexpr int kMQinv = 240;    // [16]  (score multiplier 2^-e * softmax_scale)
+constexpr int kMQint = 256;    // [16]  fixed-point query scale (32511 / max |rotated row|)
+constexpr int kMQinvI = 272;   // [16]  cold integer-score multiplier softmax_scale / (16 * kMQint)
+constexpr int kMRopeR = 288;   // [16]  RoPE score -> integer-score units (kMQinv / kMQinvI)
 
 // mbarrier slots (8 bytes each)
 constexpr int kBarFull = 0;    // [3] TMA landed
@@ -87,6 +98,10 @@ constexpr int kBarPEmpty = 8;  // [2] p tile consumed
 constexpr int kBarAbort = 10;  // int flag (shares the slot area)
 
 constexpr float kLog2e = 1.4426950408889634f;
+// 0x4B400000 read as fp32 is 1.5 * 2^23 = 12582912: an int32 accumulator started at this
+// bias and moved by |x| < 2^22 reads as the exact float 12582912 + x
+constexpr int kAccBias = 0x4B400000;
+constexpr float kAccBiasF = 12582912.0f;
 
 struct TensorMaps {
   CUtensorMap codes;  // cold codes  [tokens][256 B], box [128 B][128 rows]
@@ -336,6 +351,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         misc[kMQscale + r] = ldexpf(1.0f, e);
         misc[kMQinv + r] = ldexpf(1.0f, -e) * p.softmax_scale;
+        const float qs = (mx > 0.0f) ? 32511.0f / mx : 1.0f;
+        misc[kMQint + r] = qs;
+        misc[kMQinvI + r] = p.softmax_scale / (16.0f * qs);
+        misc[kMRopeR + r] = ldexpf(1.0f, -e) * (16.0f * qs);
       }
     }
   }
@@ -343,22 +362,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   // B fragments, stored in the order each consumer lane loads them
   {
     {
-      uint2* qc = reinterpret_cast<uint2*>(smem + kOffQc);
-      for (int e = tid; e < 8 * 4 * 2 * 2 * 32; e += kThreads) {
-        const int ln = e & 31, hl = (e >> 5) & 1, nt = (e >> 6) & 1, ks = (e >> 7) & 3, g = e >> 9;
-        const int row = 8 * nt + (ln >> 2);
-        // K permutation matching the cold code extraction in the score loop
-        const int base = 64 * g + 16 * (ln & 3) + 8 * (ks >> 1) + 2 * (ks & 1);
-        const int dims[4] = {base, base + 4, base + 1, base + 5};
-        const float sc = misc[kMQscale + row];
-        uint16_t h[4];
+      // cold QK B fragments: k-step ks = 2 * group + j; lane (gid, tq) holds query row 8nt + gid at
+      // k = 4tq + i (b0) and 16 + 4tq + i (b1), which the code expansion maps to dims 8W + 2i and
+      // 8W + 2i + 1 of code word W = 8 * group + 2tq + j.  Two int8 limbs: q = 256 hi + lo.
+      uint4* qi = reinterpret_cast<uint4*>(smem + kOffQi);
+      for (int e = tid; e < 16 * 2 * 32; e += kThreads) {
+        const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
+        const int row = 8 * nt + (ln >> 2), W = 8 * (ks >> 1) + 2 * (ln & 3) + (ks & 1);
+        const float qs = misc[kMQint + row];
+        uint32_t hb[2] = {0u, 0u}, lb[2] = {0u, 0u};
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const float x = scratch[row * kL + dims[k]] * sc;
-          const __half hi = __float2half_rn(x);
-          h[k] = hl ? __half_as_ushort(__float2half_rn(x - __half2float(hi))) : __half_as_ushort(hi);
-        }
-        qc[e] = make_uint2((uint32_t)h[0] | ((uint32_t)h[1] << 16), (uint32_t)h[2] | ((uint32_t)h[3] << 16));
+        for (int half = 0; half < 2; ++half)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int qv = min(max(__float2int_rn(scratch[row * kL + 8 * W + 2 * i + half] * qs), -32511), 32511);
+            const int q1 = (qv + 128) >> 8;  // floor((q + 128) / 256): q1 in [-127, 127], q - 256 q1 in [-128, 127]
+            const int q2 = qv - 256 * q1;
+            hb[half] |= (uint32_t)(q1 & 0xff) << (8 * i);
+            lb[half] |= (uint32_t)(q2 & 0xff) << (8 * i);
+          }
+        qi[e] = make_uint4(hb[0], hb[1], lb[0], lb[1]);
       }
       uint2* qh = reinterpret_cast<uint2*>(smem + kOffQh);
       for (int e = tid; e < 8 * 4 * 2 * 32; e += kThreads) {
@@ -394,15 +417,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =====================================================================
     // score warps
     // =====================================================================
-    const uint2* qc = reinterpret_cast<const uint2*>(smem + kOffQc);
     const uint2* qh = reinterpret_cast<const uint2*>(smem + kOffQh);
     const uint2* qr = reinterpret_cast<const uint2*>(smem + kOffQr);
-    float qinv[2][2];
+    float qinv[2][2], qinvi[2][2], rratio[2][2];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      qinv[nt][0] = misc[kMQinv + 8 * nt + 2 * tq];
-      qinv[nt][1] = misc[kMQinv + 8 * nt + 2 * tq + 1];
-    }
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int cc = 0; cc < 2; ++cc) {
+        qinv[nt][cc] = misc[kMQinv + 8 * nt + 2 * tq + cc];
+        qinvi[nt][cc] = misc[kMQinvI + 8 * nt + 2 * tq + cc];
+        rratio[nt][cc] = misc[kMRopeR + 8 * nt + 2 * tq + cc];
+      }
     // softmax state of rows 8nt + 2tq + cc, replicated across the 8 gid lanes
     float m_run[2][2], l_w[2][2];
 #pragma unroll
@@ -436,68 +461,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(warp, m, gid + 8 * h);
         const __half* scl = reinterpret_cast<const __half*>(st + kScales);
-#pragma unroll 1
-        for (int g = 0; g < 8; ++g) {
-          const int region = (g < 4) ? kCodesLo : kCodesHi;
-          const int chunk = 2 * (g & 3) + (tq >> 1);
-          uint2 v[2][2];
-#pragma unroll
-          for (int m = 0; m < 2; ++m)
-#pragma unroll
-            for (int h = 0; h < 2; ++h)
-              v[m][h] = *reinterpret_cast<const uint2*>(st + region + swz(tok[m][h], chunk) + 8 * (tq & 1));
-          float acc[2][2][4];
-#pragma unroll
-          for (int m = 0; m < 2; ++m)
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-              for (int c = 0; c < 4; ++c) acc[m][nt][c] = 0.0f;
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            uint2 bq[2][2];
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-              for (int hl = 0; hl < 2; ++hl) bq[nt][hl] = qc[(((g * 4 + ks) * 2 + nt) * 2 + hl) * 32 + lane];
-            uint32_t a[2][4];
-#pragma unroll
-            for (int m = 0; m < 2; ++m) {
-              // word (ks>>1) holds dims 16tq + 8(ks>>1) + j (nibble j); k-step ks uses
-              // nibble pairs (0,4),(1,5) for even ks and (2,6),(3,7) for odd ks
-              uint32_t x0 = (ks < 2) ? v[m][0].x : v[m][0].y;
-              uint32_t x1 = (ks < 2) ? v[m][1].x : v[m][1].y;
-              if (ks & 1) {
-                x0 >>= 8;
-                x1 >>= 8;
-              }
-              a[m][0] = nib_lo_f16x2(x0);
-              a[m][1] = nib_lo_f16x2(x1);
-              a[m][2] = nib_hi_f16x2(x0);
-              a[m][3] = nib_hi_f16x2(x1);
-            }
-            // the hi and lo products of one accumulator are four MMAs apart
-#pragma unroll
-            for (int hl = 0; hl < 2; ++hl)
-#pragma unroll
-              for (int m = 0; m < 2; ++m)
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) mma_f16(acc[m][nt], a[m], bq[nt][hl].x, bq[nt][hl].y);
-          }
-#pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const float s0 = __half2float(scl[8 * tok[m][0] + g]);
-            const float s1 = __half2float(scl[8 * tok[m][1] + g]);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              S[m][nt][0] = fmaf(acc[m][nt][0], s0, S[m][nt][0]);
-              S[m][nt][1] = fmaf(acc[m][nt][1], s0, S[m][nt][1]);
-              S[m][nt][2] = fmaf(acc[m][nt][2], s1, S[m][nt][2]);
-              S[m][nt][3] = fmaf(acc[m][nt][3], s1, S[m][nt][3]);
-            }
-          }
-        }
-        // RoPE channel (bf16, exact products, not multiplied by the code scales)
+        // RoPE channel first (bf16, exact products), moved into the integer-score units
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
           const int row = qk_token(warp, m, (lane & 7) + 8 * ((lane >> 3) & 1));
@@ -510,6 +474,58 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
               mma_bf16(S[m][nt], a, bq.x, bq.y);
             }
+          }
+        }
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
+        const uint4* qi = reinterpret_cast<const uint4*>(smem + kOffQi);
+#pragma unroll 1
+        for (int g = 0; g < 8; ++g) {
+          // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens
+          const int region = (g < 4) ? kCodesLo : kCodesHi;
+          const int chunk = 2 * (g & 3) + (tq >> 1);
+          uint2 v[2][2];
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int h = 0; h < 2; ++h)
+              v[m][h] = *reinterpret_cast<const uint2*>(st + region + swz(tok[m][h], chunk) + 8 * (tq & 1));
+          int acc[2][2][2][4];  // [limb][m][nt][c]
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              const uint32_t x0 = j ? v[m][0].y : v[m][0].x, x1 = j ? v[m][1].y : v[m][1].x;
+              const uint32_t a[4] = {s8_lo_nibbles(x0), s8_lo_nibbles(x1), s8_hi_nibbles(x0), s8_hi_nibbles(x1)};
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) {
+                if (j == 0) {
+                  mma_s8_from(acc[0][m][nt], a, bq[nt].x, bq[nt].y, kAccBias);
+                  mma_s8_from(acc[1][m][nt], a, bq[nt].z, bq[nt].w, kAccBias);
+                } else {
+                  mma_s8(acc[0][m][nt], a, bq[nt].x, bq[nt].y);
+                  mma_s8(acc[1][m][nt], a, bq[nt].z, bq[nt].w);
+                }
+              }
+            }
+          }
+#pragma unroll
+          for (int m = 0; m < 2; ++m) {
+            const float s0 = __half2float(scl[8 * tok[m][0] + g]);
+            const float s1 = __half2float(scl[8 * tok[m][1] + g]);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                const float fh = __int_as_float(acc[0][m][nt][c]) - kAccBiasF;
+                const float fl = __int_as_float(acc[1][m][nt][c]) - kAccBiasF;
+                S[m][nt][c] = fmaf(fmaf(fh, 256.0f, fl), (c < 2) ? s0 : s1, S[m][nt][c]);
+              }
           }
         }
       } else {
@@ -569,7 +585,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tk = cold ? qk_token(warp, m, gid + 8 * h) : 8 * warp + gid;
             bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
             if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
-            float sv = S[m][nt][c] * qinv[nt][cc];
+            float sv = S[m][nt][c] * (cold ? qinvi[nt][cc] : qinv[nt][cc]);
             if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
             sv = valid ? sv : -INFINITY;
             S[m][nt][c] = sv;
@@ -609,27 +625,45 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       // ---- p = exp(s - m), handed to the value warps ----
       if (i >= 2) mbar_wait(bar(kBarPEmpty + b), ((i >> 1) - 1) & 1, abort_flag);
-      float* P = reinterpret_cast<float*>(smem + kOffP + b * kPBytes);
       float psum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+      if (cold) {
+        // p as fp16 [token][16 rows]; the two 16-byte halves of a token's row swap on every
+        // other group of 4 tokens so that ldmatrix reads of 8 consecutive tokens hit 32 banks
+        uint8_t* Pc = smem + kOffP + b * kPBytes;
+        uint16_t* sT = reinterpret_cast<uint16_t*>(smem + kOffST + b * 2048);
+        const uint16_t* scl = reinterpret_cast<const uint16_t*>(smem + s * kStageBytes + kScales);
 #pragma unroll
-      for (int m = 0; m < 2; ++m)
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int tk = qk_token(warp, m, gid + 8 * h);
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              const float p0 = exp2f((S[m][nt][2 * h] - msub[nt][0]) * kLog2e);
+              const float p1 = exp2f((S[m][nt][2 * h + 1] - msub[nt][1]) * kLog2e);
+              psum[nt][0] += p0;
+              psum[nt][1] += p1;
+              *reinterpret_cast<uint32_t*>(Pc + tk * 32 + ((nt ^ ((tk >> 2) & 1)) << 4) + 4 * tq) = pack_half2(p0, p1);
+            }
+            // lane tq publishes groups 2tq and 2tq + 1 of this token's code scales (0 outside the tile)
+            const bool ok = tk < t.n;
+#pragma unroll
+            for (int u = 0; u < 2; ++u) {
+              const int g = 2 * tq + u;
+              sT[g * kColdTile + tk] = ok ? scl[8 * tk + g] : (uint16_t)0;
+            }
+          }
+      } else {
+        float* P = reinterpret_cast<float*>(smem + kOffP + b * kPBytes);
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int h = c >> 1, cc = c & 1;
-            const int r = 8 * nt + 2 * tq + cc;
-            const float pv = exp2f((S[m][nt][c] - msub[nt][cc]) * kLog2e);
-            if (cold) {
-              if (m < n_m) {
-                P[r * kPStride + qk_token(warp, m, gid + 8 * h)] = pv;
-                psum[nt][cc] += pv;
-              }
-            } else if (m == 0 && h == 0) {
-              P[r * kPStride + 8 * warp + gid] = pv;
-              psum[nt][cc] += pv;
-            }
+          for (int c = 0; c < 2; ++c) {
+            const float pv = exp2f((S[0][nt][c] - msub[nt][c]) * kLog2e);
+            P[(8 * nt + 2 * tq + c) * kPStride + 8 * warp + gid] = pv;
+            psum[nt][c] += pv;
           }
+      }
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -675,7 +709,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     int order = 1;
     if (n_t > 0) order = (load_tile(p, tile_begin).kind == ASTERQ_TILE_COLD) ? 0 : 1;
     // [16][512] scratch, usable once the cold query fragments are no longer read
-    float* scratch_o = reinterpret_cast<float*>(smem + kOffQc);
+    float* scratch_o = reinterpret_cast<float*>(smem + kOffQi);
     const int region = (g < 4) ? kCodesLo : kCodesHi;
     const int cchunk = 2 * (g & 3) + (gid >> 2);
 
@@ -735,23 +769,27 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
       }
       if (cold) {
-        const __half* scl = reinterpret_cast<const __half*>(st + kScales);
+        const uint32_t pbase = sbase + kOffP + b * kPBytes;
+        const uint16_t* sT = reinterpret_cast<const uint16_t*>(smem + kOffST + b * 2048) + g * kColdTile;
+        const int lt = (lane & 7) + 8 * ((lane >> 3) & 1), lhalf = lane >> 4;
 #pragma unroll 2
         for (int kt = 0; kt < kColdTile / 16; ++kt) {
           // tokens 16kt + {2tq, 2tq+1, 2tq+8, 2tq+9} are this lane's k indices
           const int t0 = 16 * kt + 2 * tq;
           const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
-          float f[4];
-#pragma unroll
-          for (int j = 0; j < 4; ++j) f[j] = (tk[j] < t.n) ? __half2float(scl[8 * tk[j] + g]) : 0.0f;
-          uint32_t pb[2][2];  // [ntile][b0/b1]: (p * scale) in fp16
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const float2 p01 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + t0);
-            const float2 p89 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + t0 + 8);
-            pb[nt][0] = pack_half2(p01.x * f[0], p01.y * f[1]);
-            pb[nt][1] = pack_half2(p89.x * f[2], p89.y * f[3]);
+          // p B fragments (fp16) of rows 0-7 / 8-15, times the tokens' group-g code scales
+          uint32_t pr[4];
+          {
+            const int tok = 16 * kt + lt;
+            ldmatrix_x4_trans(pr, pbase + tok * 32 + ((lhalf ^ ((tok >> 2) & 1)) << 4));
           }
+          const uint32_t s01 = *reinterpret_cast<const uint32_t*>(sT + t0);
+          const uint32_t s89 = *reinterpret_cast<const uint32_t*>(sT + t0 + 8);
+          uint32_t pb[2][2];
+          pb[0][0] = hmul2_u32(pr[0], s01);
+          pb[0][1] = hmul2_u32(pr[1], s89);
+          pb[1][0] = hmul2_u32(pr[2], s01);
+          pb[1][1] = hmul2_u32(pr[3], s89);
           uint32_t x[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j)
@@ -830,7 +868,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   // ---------------- epilogue: normalize or write the partial record ----------------
-  const float* O = reinterpret_cast<const float*>(smem + kOffQc);
+  const float* O = reinterpret_cast<const float*>(smem + kOffQi);
   const float* lw = misc + kMLw;
   const float* mrow = misc + kMWmax;
   if (slot == -1) {

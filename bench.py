@@ -69,18 +69,71 @@ def profiled_traffic() -> float | None:
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+    """SM clocks and throttle reasons sampled during the timed region.
+
+    NVML is polled from a thread every ~2 ms (read-only queries), so even a
+    timed region of a few tens of milliseconds yields samples.  Falls back to
+    ``nvidia-smi -lms 100`` when NVML cannot be opened.
+    """
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown", 0x8),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown", 0x40),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown", 0x20),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap", 0x4),
+               ("hw_power_brake_slowdown", "nvmlClocksEventReasonHwPowerBrakeSlowdown", 0x80))
 
-    def __init__(self, gpu_index: int):
+    def __init__(self, gpu_index: int, torch_device=None):
         self.gpu = gpu_index
+        self.torch_device = torch_device
         self.proc = None
         self.lines: list[str] = []
+        self.samples: list[tuple[float, float, int]] = []  # (sm MHz, max sm MHz, reason bits)
+        self._stop = threading.Event()
+        self._t = None
+        self._nvml = None
+
+    def _nvml_handle(self):
+        import pynvml
+
+        pynvml.nvmlInit()
+        self._nvml = pynvml
+        if self.torch_device is not None:
+            try:
+                import torch
+
+                uuid = str(torch.cuda.get_device_properties(self.torch_device).uuid)
+                return pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+            except Exception:
+                pass
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        idx = self.gpu
+        if vis and all(x.strip().isdigit() for x in vis.split(",")):
+            idx = int(vis.split(",")[self.gpu])
+        return pynvml.nvmlDeviceGetHandleByIndex(idx)
+
+    def _poll_nvml(self, h):
+        nv = self._nvml
+        mx = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+        while not self._stop.is_set():
+            try:
+                sm = float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM))
+                bits = int(nv.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.samples.append((sm, mx, bits))
+            except Exception:
+                break
+            time.sleep(0.002)
 
     def __enter__(self):
+        try:
+            h = self._nvml_handle()
+            self._t = threading.Thread(target=self._poll_nvml, args=(h,), daemon=True)
+            self._t.start()
+            return self
+        except Exception:
+            self._nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -96,34 +149,52 @@ class ClockSampler:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        self._stop.set()
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+        if self._t is not None:
             self._t.join(timeout=2)
+        if self._nvml is not None:
+            try:
+                self._nvml.nvmlShutdown()
+            except Exception:
+                pass
 
     def summary(self) -> dict:
         sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sms.append(float(parts[1]))
-                maxes.append(float(parts[2]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
+        if self.samples:
+            for sm, mx, bits in self.samples:
+                sms.append(sm)
+                maxes.append(mx)
+                for name, attr, default in self.REASONS:
+                    if bits & int(getattr(self._nvml, attr, default) if self._nvml else default):
+                        reasons.add(name)
+            source = "nvml"
+        else:
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for ln in self.lines:
+                parts = [x.strip() for x in ln.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    sms.append(float(parts[1]))
+                    maxes.append(float(parts[2]))
+                except ValueError:
+                    continue
+                for name, val in zip(names, parts[5:9]):
+                    if val.lower() == "active":
+                        reasons.add(name)
+            source = "nvidia-smi"
         return {
             "sm_mhz": statistics.median(sms) if sms else None,
             "sm_max_mhz": max(maxes) if maxes else None,
             "reasons": sorted(reasons),
             "samples": len(sms),
+            "source": source,
         }
 
 
@@ -192,12 +263,14 @@ def run_reference_arm(args) -> None:
         cpu_oracle_rate(host, lens, hot, budget_s=0.5)
     rates = []
     t0 = time.perf_counter()
+    # each step is a bounded sample; the whole timed run stays near one minute
+    step_budget = min(2.0, 60.0 / max(1, args.steps))
     for _ in range(max(1, args.steps)):
-        r, _, _, _ = cpu_oracle_rate(host, lens, hot, budget_s=2.0)
+        r, _, _, _ = cpu_oracle_rate(host, lens, hot, budget_s=step_budget)
         rates.append(r)
     elapsed = time.perf_counter() - t0
     value = statistics.median(rates)
-    sample = f"{len(pick)} config-3 sequences (every 8th), each step = 2 s of oracle decodes"
+    sample = f"{len(pick)} config-3 sequences (every 8th), each step = {step_budget:.2f} s of oracle decodes"
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -222,7 +295,7 @@ def run_reference_arm(args) -> None:
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="asterq", choices=["asterq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -292,7 +365,7 @@ def main() -> None:
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local, dev) as clocks:
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
