@@ -42,6 +42,7 @@ EXPORTED_SYMBOLS = (
     "asterq_latent_decode",
     "asterq_latent_decode_noalloc",
     "asterq_splitkv_combine",
+    "asterq_splitkv_merge",
 )
 
 
@@ -129,6 +130,8 @@ def load() -> ctypes.CDLL:
     lib.asterq_latent_decode_noalloc.argtypes = [ctypes.POINTER(DecodeParams), vp]
     lib.asterq_splitkv_combine.restype = ctypes.c_int
     lib.asterq_splitkv_combine.argtypes = [vp, i32, vp, i32, i32, vp, i32, vp]
+    lib.asterq_splitkv_merge.restype = ctypes.c_int
+    lib.asterq_splitkv_merge.argtypes = [vp, i32, vp, i32, i32, vp, vp]
     _lib = lib
     return lib
 

@@ -1,0 +1,377 @@
+"""Drop-in for AsterLM's latent cache (src/asterlm/cache.py) on paged device pools.
+
+``LatentLayerCache`` keeps the reference's fields, properties and methods
+(cache.py:52-221): ``length``, ``cold_length``, ``num_bytes``, ``append``,
+``iter_chunks``, ``materialize_latent`` / ``materialize_rope`` and the
+``latent`` / ``rope_key`` / ``cold_latent`` / ``cold_rope`` pieces.  Storage is
+different: every batch row's tokens live in fixed-size pages of two pools
+(``chunk_tokens`` tokens per page),
+
+* hot pages: bf16 latent [page, 512] + bf16 RoPE key [page, 64],
+* cold pages: INT4 codes [page, 256] + fp16 scales [page, 8] + bf16 RoPE key,
+
+so that appending writes the new token in place (no re-concatenation of the
+hot window, cache.py:195-200) and a flush (cache.py:167-177) encodes the oldest
+full hot page of every row straight into a cold page with the write-path kernel
+and releases the hot page.  The decode kernel reads the pools through
+``decode_layouts``; nothing is materialized on the decode path.
+
+The hot window holds at most ``recent_tokens + chunk_tokens`` tokens, exactly as
+in the reference: after every append, whole chunks move from the front of the
+hot window to the cold pool while the hot length exceeds that threshold.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+
+from . import _lib
+from .decode import GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools
+from .kv import QuantizedTensor, dequantize_tensor
+from .plan import SequenceLayout
+
+_KERNEL_SCHEMES = ("hadamard_int4", "bfloat16")
+
+
+class _Pool:
+    """Growable set of equally sized pages with a free list (one tensor per field)."""
+
+    def __init__(self, fields: dict[str, tuple[tuple[int, ...], torch.dtype]], page_tokens: int, device) -> None:
+        self.fields = fields
+        self.page_tokens = page_tokens
+        self.device = torch.device(device)
+        self.capacity = 0
+        self.tensors = {name: torch.empty((0, page_tokens, *shape), dtype=dt, device=self.device)
+                        for name, (shape, dt) in fields.items()}
+        self.free: list[int] = []
+
+    def alloc(self, n: int) -> list[int]:
+        while len(self.free) < n:
+            self._grow(max(n - len(self.free), self.capacity))
+        out, self.free = self.free[:n], self.free[n:]
+        return out
+
+    def release(self, pages: list[int]) -> None:
+        self.free.extend(pages)
+        self.free.sort()
+
+    def _grow(self, extra: int) -> None:
+        extra = max(extra, 4)
+        for name, (shape, dt) in self.fields.items():
+            new = torch.empty((self.capacity + extra, self.page_tokens, *shape), dtype=dt, device=self.device)
+            if self.capacity:
+                new[: self.capacity].copy_(self.tensors[name])
+            self.tensors[name] = new
+        self.free.extend(range(self.capacity, self.capacity + extra))
+        self.capacity += extra
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        return self.tensors[name]
+
+
+@dataclass
+class LatentLayerCache:
+    """Hot/cold latent cache for one global-attention layer (cache.py:52).
+
+    Same constructor fields and defaults as the reference.  The decode kernels
+    serve ``cache_dtype`` "hadamard_int4" (cold chunks) and "bfloat16" (never
+    flushes, cache.py:169); ``group_size`` must be 64 and ``quantize_rope``
+    False for the kernel path, as in every BASELINE configuration.
+    """
+
+    cache_dtype: str = "bfloat16"
+    group_size: int = 64
+    recent_tokens: int = 512
+    chunk_tokens: int = 1024
+    quantize_rope: bool = False
+    _batch: int = field(default=0, repr=False)
+    _hot_len: int = field(default=0, repr=False)
+    _hot_pages: list[list[int]] = field(default_factory=list, repr=False)
+    _cold_pages: list[list[int]] = field(default_factory=list, repr=False)
+    _hot: _Pool | None = field(default=None, repr=False)
+    _cold: _Pool | None = field(default=None, repr=False)
+    _dtype: torch.dtype = field(default=torch.bfloat16, repr=False)
+
+    def __post_init__(self) -> None:
+        if self.cache_dtype not in _KERNEL_SCHEMES:
+            raise NotImplementedError(
+                f"cache_dtype {self.cache_dtype!r}: the asterq pools serve 'hadamard_int4' and 'bfloat16'")
+        if self.cache_dtype == "hadamard_int4" and self.group_size != GROUP_SIZE:
+            raise NotImplementedError(f"group_size {self.group_size}: the decode kernels use groups of {GROUP_SIZE}")
+        if self.quantize_rope:
+            raise NotImplementedError("quantize_rope=True: the decode kernels read bf16 RoPE keys")
+        if self.chunk_tokens <= 0 or self.chunk_tokens % 16:
+            raise ValueError("chunk_tokens must be a positive multiple of 16 (one chunk per page)")
+        if self.recent_tokens < 0:
+            raise ValueError("recent_tokens must be non-negative")
+
+    # ------------------------------------------------------------------ sizes
+    @property
+    def page_tokens(self) -> int:
+        return self.chunk_tokens
+
+    @property
+    def batch_size(self) -> int:
+        return self._batch
+
+    @property
+    def cold_chunks(self) -> int:
+        return len(self._cold_pages[0]) if self._cold_pages else 0
+
+    @property
+    def cold_length(self) -> int:
+        return self.cold_chunks * self.chunk_tokens
+
+    @property
+    def hot_length(self) -> int:
+        return self._hot_len
+
+    @property
+    def length(self) -> int:
+        return self.cold_length + self._hot_len
+
+    @property
+    def num_bytes(self) -> int:
+        """Bytes the reference would account (cache.py:79-87): codes + scales + cold RoPE + hot tensors."""
+        b, cold = self._batch, self.cold_length
+        total = b * cold * (LATENT_DIM // 2 + (LATENT_DIM // GROUP_SIZE) * 2 + ROPE_DIM * 2)
+        total += b * self._hot_len * (LATENT_DIM + ROPE_DIM) * 2
+        return int(total)
+
+    # ------------------------------------------------------------------ pools
+    def _ensure_pools(self, batch: int, device: torch.device, dtype: torch.dtype) -> None:
+        if self._hot is None:
+            self._batch = batch
+            self._dtype = dtype
+            self._hot = _Pool({"latent": ((LATENT_DIM,), torch.bfloat16), "rope": ((ROPE_DIM,), torch.bfloat16)},
+                              self.page_tokens, device)
+            self._cold = _Pool({"codes": ((LATENT_DIM // 2,), torch.uint8),
+                                "scales": ((LATENT_DIM // GROUP_SIZE,), torch.float16),
+                                "rope": ((ROPE_DIM,), torch.bfloat16)}, self.page_tokens, device)
+            self._hot_pages = [[] for _ in range(batch)]
+            self._cold_pages = [[] for _ in range(batch)]
+        elif batch != self._batch:
+            raise ValueError(f"batch size changed from {self._batch} to {batch}")
+
+    def pools(self) -> LatentPools:
+        """The five device pools in the layout the decode C ABI reads."""
+        if self._hot is None:
+            raise RuntimeError("empty cache")
+        return LatentPools(cold_codes=self._cold["codes"], cold_scales=self._cold["scales"],
+                           cold_rope=self._cold["rope"], hot_latent=self._hot["latent"], hot_rope=self._hot["rope"])
+
+    def decode_layouts(self, q_len: int) -> list[SequenceLayout]:
+        """One SequenceLayout per batch row; row b's new tokens are rows b*q_len.. of the step's arrays."""
+        P = self.page_tokens
+        out = []
+        for b in range(self._batch):
+            cold = [(pg, 0, P) for pg in self._cold_pages[b]]
+            hot = []
+            left = self._hot_len
+            for pg in self._hot_pages[b]:
+                n = min(P, left)
+                if n > 0:
+                    hot.append((pg, 0, n))
+                left -= n
+            out.append(SequenceLayout(cold=cold, hot=hot, q_start=b * q_len, q_len=q_len))
+        return out
+
+    # ------------------------------------------------------------------ writes
+    def append(self, latent: torch.Tensor, rope_key: torch.Tensor, window_size: int | None = None,
+               sink_tokens: int = 0) -> None:
+        """Append [B, T, 512] latents and [B, T, 64] RoPE keys (cache.py:185-221)."""
+        latent = latent.detach()
+        rope_key = rope_key.detach()
+        if latent.dim() != 3 or latent.shape[-1] != LATENT_DIM or rope_key.shape != (*latent.shape[:2], ROPE_DIM):
+            raise ValueError("latent must be [B, T, 512] and rope_key [B, T, 64]")
+        if not latent.is_cuda:
+            raise RuntimeError("asterq caches live on the GPU; there is no CPU path")
+        bsz, t = latent.shape[:2]
+        self._ensure_pools(bsz, latent.device, latent.dtype)
+        if t:
+            self._write_hot(latent, rope_key)
+        self._flush_cold_chunks()
+        trim_slack = self.chunk_tokens if window_size is not None and window_size > 2 * self.chunk_tokens else 0
+        if window_size is not None and self.length > window_size + trim_slack:
+            self._trim(window_size, sink_tokens, latent.dtype, latent.device)
+
+    def _write_hot(self, latent: torch.Tensor, rope_key: torch.Tensor) -> None:
+        P, (bsz, t) = self.page_tokens, latent.shape[:2]
+        end = self._hot_len + t
+        need = (end + P - 1) // P
+        for b in range(bsz):
+            missing = need - len(self._hot_pages[b])
+            if missing > 0:
+                self._hot_pages[b].extend(self._hot.alloc(missing))
+        pos = torch.arange(self._hot_len, end, device=latent.device)
+        pages = torch.tensor(self._hot_pages, dtype=torch.int64, device=latent.device)  # [B, n_pages]
+        slot = pages[:, pos // P] * P + (pos % P)  # [B, T]
+        flat = slot.reshape(-1)
+        self._hot["latent"].view(-1, LATENT_DIM).index_copy_(0, flat, latent.reshape(-1, LATENT_DIM).to(torch.bfloat16))
+        self._hot["rope"].view(-1, ROPE_DIM).index_copy_(0, flat, rope_key.reshape(-1, ROPE_DIM).to(torch.bfloat16))
+        self._hot_len = end
+
+    def _flush_cold_chunks(self) -> None:
+        """cache.py:167-177: while hot > recent + chunk, encode the oldest chunk of every row."""
+        if self.cache_dtype == "bfloat16" or self._hot is None:
+            return
+        threshold = self.recent_tokens + self.chunk_tokens
+        while self._hot_len > threshold:
+            self._flush_one()
+
+    def _flush_one(self) -> None:
+        P, bsz = self.page_tokens, self._batch
+        dev = self._hot.device
+        src = torch.tensor([self._hot_pages[b][0] for b in range(bsz)], dtype=torch.int64, device=dev)
+        dst_pages = self._cold.alloc(bsz)
+        dst = torch.tensor(dst_pages, dtype=torch.int64, device=dev)
+        x = self._hot["latent"].index_select(0, src).reshape(bsz * P, LATENT_DIM)
+        codes = torch.empty(bsz * P, LATENT_DIM // 2, dtype=torch.uint8, device=dev)
+        scales = torch.empty(bsz * P, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=dev)
+        lib = _lib.load()
+        _lib.check(lib.asterq_quantize(x.data_ptr(), _lib.DTYPE_BF16, bsz * P, LATENT_DIM, LATENT_DIM,
+                                       _lib.SCHEME_HADAMARD_INT4, GROUP_SIZE, codes.data_ptr(), scales.data_ptr(),
+                                       _lib.stream_handle(dev)))
+        self._cold["codes"].index_copy_(0, dst, codes.view(bsz, P, -1))
+        self._cold["scales"].index_copy_(0, dst, scales.view(bsz, P, -1))
+        self._cold["rope"].index_copy_(0, dst, self._hot["rope"].index_select(0, src))
+        freed = []
+        for b in range(bsz):
+            self._cold_pages[b].append(dst_pages[b])
+            freed.append(self._hot_pages[b].pop(0))
+        self._hot.release(freed)
+        self._hot_len -= P
+
+    def _trim(self, window_size: int, sink_tokens: int, dtype: torch.dtype, device: torch.device) -> None:
+        """cache.py:203-221: keep sink + recent tokens and re-encode them (double quantization, as the reference)."""
+        all_latent = self.materialize_latent(dtype=dtype, device=device)
+        all_rope = self.materialize_rope(dtype=dtype, device=device)
+        sink = min(sink_tokens, window_size)
+        recent = window_size - sink
+        if sink and recent:
+            all_latent = torch.cat((all_latent[:, :sink], all_latent[:, -recent:]), dim=1)
+            all_rope = torch.cat((all_rope[:, :sink], all_rope[:, -recent:]), dim=1)
+        elif recent:
+            all_latent, all_rope = all_latent[:, -recent:], all_rope[:, -recent:]
+        else:
+            all_latent, all_rope = all_latent[:, :sink], all_rope[:, :sink]
+        self._release_all()
+        self._write_hot(all_latent.contiguous(), all_rope.contiguous())
+        self._flush_cold_chunks()
+
+    def _release_all(self) -> None:
+        for b in range(self._batch):
+            self._hot.release(self._hot_pages[b])
+            self._cold.release(self._cold_pages[b])
+            self._hot_pages[b] = []
+            self._cold_pages[b] = []
+        self._hot_len = 0
+
+    # ------------------------------------------------------------------ reads (API parity, not the decode path)
+    @property
+    def latent(self) -> torch.Tensor | None:
+        """Hot window [B, S_hot, 512] (a gathered copy of the hot pages)."""
+        return self._gather_hot("latent")
+
+    @property
+    def rope_key(self) -> torch.Tensor | None:
+        return self._gather_hot("rope")
+
+    def _gather_hot(self, name: str) -> torch.Tensor | None:
+        if self._hot is None:
+            return None
+        pool = self._hot[name]
+        rows = [torch.cat([pool[pg] for pg in self._hot_pages[b]], dim=0)[: self._hot_len] if self._hot_pages[b]
+                else pool.new_empty(0, pool.shape[-1]) for b in range(self._batch)]
+        return torch.stack(rows).to(self._dtype)
+
+    @property
+    def cold_latent(self) -> list[QuantizedTensor]:
+        """One reference-format QuantizedTensor per cold chunk (kv.py:58-73): data [B, chunk, 256], scale [B, chunk, 8, 1]."""
+        out = []
+        for c in range(self.cold_chunks):
+            pages = [self._cold_pages[b][c] for b in range(self._batch)]
+            data = torch.stack([self._cold["codes"][pg] for pg in pages])
+            scale = torch.stack([self._cold["scales"][pg] for pg in pages]).unsqueeze(-1)
+            out.append(QuantizedTensor(data=data, scale=scale, original_shape=(self._batch, self.chunk_tokens, LATENT_DIM),
+                                       padded_dim=LATENT_DIM, group_size=GROUP_SIZE, scheme="hadamard_int4",
+                                       source_dtype=self._dtype))
+        return out
+
+    @property
+    def cold_rope(self) -> list[torch.Tensor]:
+        return [torch.stack([self._cold["rope"][self._cold_pages[b][c]] for b in range(self._batch)])
+                for c in range(self.cold_chunks)]
+
+    def iter_chunks(self, *, dtype: torch.dtype, device: torch.device):
+        """cache.py:139-159: dequantized (latent, rope) per cold chunk, then the hot window."""
+        for q, rope in zip(self.cold_latent, self.cold_rope, strict=True):
+            yield dequantize_tensor(q, dtype=dtype).to(device), rope.to(device=device, dtype=dtype)
+        if self._hot_len:
+            yield self.latent.to(device=device, dtype=dtype), self.rope_key.to(device=device, dtype=dtype)
+
+    def materialize_latent(self, *, dtype: torch.dtype | None = None, device: torch.device | None = None):
+        """cache.py:89-116."""
+        if self._hot is None or self.length == 0:
+            return None
+        dtype = self._dtype if dtype is None else dtype
+        device = self._hot.device if device is None else device
+        parts = [dequantize_tensor(q, dtype=dtype).to(device) for q in self.cold_latent]
+        if self._hot_len:
+            parts.append(self.latent.to(device=device, dtype=dtype))
+        return torch.cat(parts, dim=1)
+
+    def materialize_rope(self, *, dtype: torch.dtype | None = None, device: torch.device | None = None):
+        """cache.py:118-137."""
+        if self._hot is None or self.length == 0:
+            return None
+        dtype = self._dtype if dtype is None else dtype
+        device = self._hot.device if device is None else device
+        parts = [r.to(device=device, dtype=dtype) for r in self.cold_rope]
+        if self._hot_len:
+            parts.append(self.rope_key.to(device=device, dtype=dtype))
+        return torch.cat(parts, dim=1)
+
+
+@dataclass
+class AsterCache:
+    """Latent-layer part of the reference's mixed cache (cache.py:224-292)."""
+
+    seen_tokens: int = 0
+    latent: dict[int, LatentLayerCache] = field(default_factory=dict)
+    kda_states: dict[int, torch.Tensor] = field(default_factory=dict)
+    cache_dtype: str = "bfloat16"
+    cache_group_size: int = 64
+    cache_recent_tokens: int = 512
+    cache_chunk_tokens: int = 1024
+    cache_quantize_rope: bool = False
+
+    @classmethod
+    def create(cls, config: Any | None = None) -> "AsterCache":
+        kwargs: dict[str, Any] = {}
+        if config is not None:
+            kwargs = {"cache_dtype": config.cache_dtype, "cache_group_size": config.cache_group_size,
+                      "cache_recent_tokens": config.cache_recent_tokens, "cache_chunk_tokens": config.cache_chunk_tokens,
+                      "cache_quantize_rope": config.cache_quantize_rope}
+        return cls(**kwargs)
+
+    def latent_layer(self, layer_idx: int) -> LatentLayerCache:
+        if layer_idx not in self.latent:
+            self.latent[layer_idx] = LatentLayerCache(cache_dtype=self.cache_dtype, group_size=self.cache_group_size,
+                                                      recent_tokens=self.cache_recent_tokens,
+                                                      chunk_tokens=self.cache_chunk_tokens,
+                                                      quantize_rope=self.cache_quantize_rope)
+        return self.latent[layer_idx]
+
+    @property
+    def num_bytes(self) -> int:
+        total = sum(layer.num_bytes for layer in self.latent.values())
+        total += sum(s.numel() * s.element_size() for s in self.kda_states.values())
+        return int(total)
+
+    def reset(self) -> None:
+        self.seen_tokens = 0
+        self.latent.clear()
+        self.kda_states.clear()

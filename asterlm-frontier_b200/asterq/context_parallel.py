@@ -1,0 +1,128 @@
+"""Context-parallel decode of long sequences (config C4) across ranks.
+
+The cold chunks of a sequence are split into contiguous ranges, one per rank,
+balanced by the bytes a decode step streams (the last rank also holds the hot
+window and the step's new tokens, so it takes fewer chunks).  Each rank:
+
+1. runs the split-KV decode over its own pages, every work item writing an
+   (m, l, o) partial record (``build_plan(..., force_partial=True)``);
+2. merges its records into one record per 16-row block with
+   ``asterq_splitkv_merge`` (about 33 KB per row block);
+3. exchanges the merged records with one ``all_gather`` over the process group
+   (NCCL on GPUs; the records are fp32 in the workspace layout);
+4. combines the gathered records with ``asterq_splitkv_combine`` into the
+   context latents, identically on every rank.
+
+The merge rule is the reference's online softmax (latent_attention.py:212-220)
+applied across ranks instead of across chunks.  No TMA or library kernel reads
+another GPU's memory: the records arrive by NCCL into local buffers.
+"""
+from __future__ import annotations
+
+import ctypes
+from dataclasses import replace
+
+import torch
+
+from . import _lib
+from .decode import LATENT_DIM, DeviceDecodePlan, LatentPools, make_params
+from .plan import ROWS_PER_BLOCK, SequenceLayout, build_plan
+from .sharding import COLD_TOKEN_BYTES, HOT_TOKEN_BYTES
+
+RECORD_FLOATS = ROWS_PER_BLOCK * (LATENT_DIM + 2)
+
+
+def split_chunks(chunk_tokens: list[int], hot_tokens: int, world: int, q_len: int = 1) -> list[tuple[int, int]]:
+    """Contiguous [begin, end) ranges of cold chunks per rank; the hot window and new tokens go to the last rank.
+
+    Ranges are cut at equal shares of the step's total bytes, counting the last
+    rank's hot window and new tokens as part of its share.
+    """
+    if world <= 0:
+        raise ValueError("world must be positive")
+    n = len(chunk_tokens)
+    costs = [t * COLD_TOKEN_BYTES for t in chunk_tokens]
+    total = sum(costs) + (hot_tokens + q_len) * HOT_TOKEN_BYTES
+    share = total / world
+    bounds = [0]
+    acc = 0.0
+    i = 0
+    for r in range(world - 1):
+        target = share * (r + 1)
+        while i < n and acc + costs[i] / 2 <= target:
+            acc += costs[i]
+            i += 1
+        bounds.append(i)
+    bounds.append(n)
+    return [(bounds[r], bounds[r + 1]) for r in range(world)]
+
+
+def rank_layout(layout: SequenceLayout, rank: int, world: int) -> SequenceLayout:
+    """The part of one sequence's layout that `rank` reads."""
+    ranges = split_chunks([c[2] for c in layout.cold], layout.hot_tokens, world, layout.q_len)
+    a, b = ranges[rank]
+    last = rank == world - 1
+    return replace(layout, cold=list(layout.cold[a:b]), hot=list(layout.hot) if last else [], attend_new=last)
+
+
+class ContextParallelDecoder:
+    """One rank's share of a context-parallel decode step for one sequence (B = 1)."""
+
+    def __init__(self, pools: LatentPools, layout: SequenceLayout, n_heads: int, rank: int, world: int,
+                 device, **plan_kw) -> None:
+        self.pools, self.rank, self.world, self.n_heads = pools, rank, world, n_heads
+        self.device = torch.device(device)
+        self.local = rank_layout(replace(layout, q_start=0), rank, world)
+        self.plan = build_plan([self.local], n_heads, force_partial=True, **plan_kw)
+        self.dplan = DeviceDecodePlan(self.plan, self.device)
+        self.n_rb = int(self.plan.combine.shape[0])
+        self.q_len = layout.q_len
+        self.merged = torch.empty(self.n_rb * RECORD_FLOATS, dtype=torch.float32, device=self.device)
+        self.gathered = torch.empty(world * self.n_rb * RECORD_FLOATS, dtype=torch.float32, device=self.device)
+        self.slot_major = torch.empty_like(self.gathered)
+        jobs = [(rb * world, (rb + 1) * world, int(self.plan.combine[rb, 2]), int(self.plan.combine[rb, 3]))
+                for rb in range(self.n_rb)]
+        self.final_jobs = torch.tensor(jobs, dtype=torch.int32, device=self.device).reshape(-1, 4)
+
+    def partial(self, q_lat, q_rope, new_latent, new_rope, *, softmax_scale: float,
+                logit_softcap: float | None = None) -> torch.Tensor:
+        """Steps 1-2: this rank's merged (m, l, o) records, [n_rb * 16 * 514] fp32."""
+        out = torch.empty(q_lat.shape[0], self.n_heads, LATENT_DIM, dtype=torch.float32, device=self.device)
+        p = make_params(self.pools, self.dplan, q_lat, q_rope, new_latent, new_rope, out, n_heads=self.n_heads,
+                        softmax_scale=softmax_scale, logit_softcap=logit_softcap)
+        p.n_combine = 0  # the records are merged below, not combined
+        lib = _lib.load()
+        stream = _lib.stream_handle(self.device)
+        _lib.check(lib.asterq_latent_decode(ctypes.byref(p), stream))
+        _lib.check(lib.asterq_splitkv_merge(self.dplan.workspace.data_ptr(), self.plan.n_slots,
+                                            self.dplan.combine.data_ptr(), self.n_rb, LATENT_DIM,
+                                            self.merged.data_ptr(), stream))
+        return self.merged
+
+    def finish(self, gathered: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+        """Step 4: combine the records of all ranks (rank-major as all_gather leaves them) into `out`."""
+        w, n = self.world, self.n_rb
+        o_part = gathered.view(w, n * RECORD_FLOATS)
+        src_o = o_part[:, : n * ROWS_PER_BLOCK * LATENT_DIM].reshape(w, n, ROWS_PER_BLOCK * LATENT_DIM)
+        src_m = o_part[:, n * ROWS_PER_BLOCK * LATENT_DIM: n * ROWS_PER_BLOCK * (LATENT_DIM + 1)].reshape(w, n, ROWS_PER_BLOCK)
+        src_l = o_part[:, n * ROWS_PER_BLOCK * (LATENT_DIM + 1):].reshape(w, n, ROWS_PER_BLOCK)
+        dst = self.slot_major
+        no = w * n * ROWS_PER_BLOCK * LATENT_DIM
+        dst[:no].view(n, w, -1).copy_(src_o.transpose(0, 1))
+        dst[no: no + w * n * ROWS_PER_BLOCK].view(n, w, -1).copy_(src_m.transpose(0, 1))
+        dst[no + w * n * ROWS_PER_BLOCK:].view(n, w, -1).copy_(src_l.transpose(0, 1))
+        dtype = _lib.DTYPE_F32 if out.dtype == torch.float32 else _lib.DTYPE_BF16
+        lib = _lib.load()
+        _lib.check(lib.asterq_splitkv_combine(dst.data_ptr(), w * n, self.final_jobs.data_ptr(), n, LATENT_DIM,
+                                              out.data_ptr(), dtype, _lib.stream_handle(self.device)))
+        return out
+
+    def step(self, q_lat, q_rope, new_latent, new_rope, out, *, group=None, softmax_scale: float,
+             logit_softcap: float | None = None) -> torch.Tensor:
+        """Steps 1-4 with ``torch.distributed.all_gather_into_tensor`` over `group`."""
+        import torch.distributed as dist
+
+        rec = self.partial(q_lat, q_rope, new_latent, new_rope, softmax_scale=softmax_scale,
+                           logit_softcap=logit_softcap)
+        dist.all_gather_into_tensor(self.gathered, rec, group=group)
+        return self.finish(self.gathered, out)

@@ -45,6 +45,7 @@ class SequenceLayout:
     hot: list[tuple[int, int, int]] = field(default_factory=list)
     q_start: int = 0
     q_len: int = 1
+    attend_new: bool = True  # False: the query rows attend to the cache only (a context-parallel rank without them)
 
     @property
     def cold_tokens(self) -> int:
@@ -56,7 +57,7 @@ class SequenceLayout:
 
     @property
     def cache_bytes(self) -> int:
-        return self.cold_tokens * _COLD_TOKEN_BYTES + (self.hot_tokens + self.q_len) * _HOT_TOKEN_BYTES
+        return self.cold_tokens * _COLD_TOKEN_BYTES + (self.hot_tokens + self.q_len * self.attend_new) * _HOT_TOKEN_BYTES
 
 
 @dataclass
@@ -81,7 +82,7 @@ def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
     for page, off, n in seq.hot:
         for s in range(0, n, HOT_TILE):
             out.append((_lib.TILE_HOT, page, off + s, min(HOT_TILE, n - s)))
-    if seq.q_len > 0:
+    if seq.q_len > 0 and seq.attend_new:
         out.append((_lib.TILE_NEW, seq.q_start, 0, seq.q_len))
     return out
 
@@ -98,8 +99,14 @@ def build_plan(
     ctas_per_sm: int = 1,
     waves: float = 2.0,
     max_items_per_seq: int | None = None,
+    force_partial: bool = False,
 ) -> DecodePlan:
-    """Cut the batch into balanced work items (longest first)."""
+    """Cut the batch into balanced work items (longest first).
+
+    ``force_partial``: every (sequence, row block) writes partial records and gets
+    a combine job, even when one item covers it (context-parallel decode merges
+    these records across ranks).
+    """
     if n_heads <= 0:
         raise ValueError("n_heads must be positive")
     tiles: list[tuple[int, int, int, int]] = []
@@ -145,9 +152,10 @@ def build_plan(
         k = min(k, t1 - t0)
         if max_items_per_seq is not None:
             k = min(k, max_items_per_seq)
-        if k <= 1:
+        if k <= 1 and not force_partial:
             items.append((si, rb, t0, t1, -1, out_row0, n_rows, seq.q_len, c))
             continue
+        k = max(k, 1)
         # contiguous ranges of ~equal cost
         targets = prefix[t0] + (c * np.arange(1, k)) / k
         cuts = np.searchsorted(prefix[t0 : t1 + 1], targets, side="left") + t0

@@ -937,6 +937,39 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
   }
 }
 
+// Merge partial records into fewer partial records (same rule, no normalisation):
+// job j turns slots [slot_begin, slot_end) into record j of `merged`, laid out like
+// the workspace (o [n_jobs][16][latent_dim], then m [n_jobs][16], then l [n_jobs][16]).
+// Context-parallel decode merges each rank's split-KV records this way before
+// the records of all ranks are gathered.
+__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
+                                                    const float* __restrict__ wl, const int32_t* __restrict__ jobs,
+                                                    int n_slots, int n_jobs, int latent_dim, float* __restrict__ merged) {
+  const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
+  const int slot_begin = max(job.x, 0), slot_end = min(job.y, n_slots);
+  const int r = threadIdx.x >> 4, d = blockIdx.y * kCombDims + 2 * (threadIdx.x & 15);
+  if (d >= latent_dim) return;
+  float mmax = -INFINITY;
+  for (int s = slot_begin; s < slot_end; ++s) mmax = fmaxf(mmax, wm[(int64_t)s * kRows + r]);
+  const float msub = (mmax == -INFINITY) ? 0.0f : mmax;
+  float l = 0.0f, a0 = 0.0f, a1 = 0.0f;
+  for (int s = slot_begin; s < slot_end; ++s) {
+    const float w = exp2f((wm[(int64_t)s * kRows + r] - msub) * kLog2e);
+    l += w * wl[(int64_t)s * kRows + r];
+    const float2 v = *reinterpret_cast<const float2*>(wo + ((int64_t)s * kRows + r) * latent_dim + d);
+    a0 += w * v.x;
+    a1 += w * v.y;
+  }
+  float* mo = merged;
+  float* mm = mo + (int64_t)n_jobs * kRows * latent_dim;
+  float* ml = mm + (int64_t)n_jobs * kRows;
+  *reinterpret_cast<float2*>(mo + ((int64_t)blockIdx.x * kRows + r) * latent_dim + d) = make_float2(a0, a1);
+  if (blockIdx.y == 0 && (threadIdx.x & 15) == 0) {
+    mm[(int64_t)blockIdx.x * kRows + r] = mmax;
+    ml[(int64_t)blockIdx.x * kRows + r] = l;
+  }
+}
+
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
@@ -1083,6 +1116,23 @@ extern "C" int asterq_splitkv_combine(const float* partials, int32_t n_slots, co
   dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, combine, n_slots, latent_dim, out, out_dtype);
   return check_launch("splitkv_combine");
+}
+
+extern "C" int asterq_splitkv_merge(const float* partials, int32_t n_slots, const int32_t* jobs, int32_t n_jobs,
+                                    int32_t latent_dim, float* merged, void* stream) {
+  clear_error();
+  if (latent_dim != dec::kL) return set_error(ASTERQ_ERR_UNSUPPORTED, "merge: latent_dim must be 512");
+  if (n_slots < 0 || n_jobs < 0) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "merge: negative sizes");
+  if (n_jobs == 0) return ASTERQ_OK;
+  if (!partials || !jobs || !merged) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "merge: null pointer");
+  if ((reinterpret_cast<uintptr_t>(partials) | reinterpret_cast<uintptr_t>(jobs) | reinterpret_cast<uintptr_t>(merged)) &
+      15)
+    return set_error(ASTERQ_ERR_MISALIGNED, "merge: pointers must be 16-byte aligned");
+  const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
+  const float* wl = wm + (int64_t)n_slots * dec::kRows;
+  dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      partials, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged);
+  return check_launch("splitkv_merge");
 }
 
 // ---------------------------------------------------------------------------

@@ -12,6 +12,7 @@
  *                          layers/latent_attention.py:116-175 _full_attention (q_len > 1, causal),
  *                          iterating the cache like cache.py:139-159 iter_chunks
  *   asterq_splitkv_combine layers/latent_attention.py:212-220 (the online-softmax merge rule)
+ *   asterq_splitkv_merge   the same rule, leaving merged (m, l, o) records for a later combine
  *
  * Every function returns ASTERQ_OK (0) or a negative status and never aborts;
  * asterq_last_error() describes the last failure on the calling thread.  All
@@ -173,6 +174,18 @@ int asterq_latent_decode_noalloc(const asterq_decode_params* p, void* stream);
  */
 int asterq_splitkv_combine(const float* partials, int32_t n_slots, const int32_t* combine, int32_t n_combine,
                            int32_t latent_dim, void* out, int32_t out_dtype, void* stream);
+
+/*
+ * Merge split-KV partial records into fewer partial records with the same rule,
+ * without normalising: job j (combine table layout; out_row0 / n_rows unused)
+ * turns slots [slot_begin, slot_end) into record j of `merged`, which has the
+ * workspace layout (o [n_jobs][16][latent_dim], m [n_jobs][16], l [n_jobs][16]).
+ * Used by context-parallel decode before the ranks' records are gathered;
+ * replaces the per-chunk merge step of latent_attention.py:212-220 applied
+ * across ranks.
+ */
+int asterq_splitkv_merge(const float* partials, int32_t n_slots, const int32_t* jobs, int32_t n_jobs,
+                         int32_t latent_dim, float* merged, void* stream);
 
 #ifdef __cplusplus
 }

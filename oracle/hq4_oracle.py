@@ -354,6 +354,45 @@ def decode(q_lat, q_rope, new_latent, new_rope, cache, softmax_scale, logit_soft
     return causal_attention(q_lat, q_rope, new_latent, new_rope, cache, softmax_scale, logit_softcap)
 
 
+def partial_attention(
+    q_lat: np.ndarray,
+    q_rope: np.ndarray,
+    chunks: list[tuple[np.ndarray, np.ndarray]],
+    softmax_scale: float,
+) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Unnormalised softmax state over a subset of one sequence's keys.
+
+    Returns (m [T, H], l [T, H], o [T, H, L]) with m the score maximum, l the sum
+    of exp(s - m) and o the exp(s - m)-weighted sum of latents: the running
+    state of latent_attention.py:203-220 after consuming only `chunks`
+    (latent [n, L], rope [n, R] pairs).  An empty subset gives (-inf, 0, 0).
+    """
+    q_lat = np.asarray(q_lat, np.float32)
+    q_rope = np.asarray(q_rope, np.float32)
+    t, h, dim = q_lat.shape
+    if not chunks:
+        return (np.full((t, h), -np.inf, np.float32), np.zeros((t, h), np.float32), np.zeros((t, h, dim), np.float32))
+    lat = np.concatenate([c[0] for c in chunks]).astype(np.float32)
+    rope = np.concatenate([c[1] for c in chunks]).astype(np.float32)
+    s = (np.einsum("thl,sl->ths", q_lat, lat) + np.einsum("thr,sr->ths", q_rope, rope)) * np.float32(softmax_scale)
+    m = s.max(axis=-1)
+    p = np.exp(s - m[..., None])
+    return m, p.sum(axis=-1), np.einsum("ths,sl->thl", p, lat)
+
+
+def merge_partials(parts: list[tuple[np.ndarray, np.ndarray, np.ndarray]]) -> np.ndarray:
+    """Combine partial states with the online-softmax rule (latent_attention.py:212-220); returns o / max(l, 1e-20)."""
+    m = np.max(np.stack([p[0] for p in parts]), axis=0)
+    msub = np.where(np.isneginf(m), 0.0, m)
+    l = np.zeros_like(parts[0][1])
+    o = np.zeros_like(parts[0][2])
+    for pm, pl, po in parts:
+        w = np.exp(pm - msub)
+        l += w * pl
+        o += w[..., None] * po
+    return (o / np.maximum(l, np.float32(1e-20))[..., None]).astype(np.float32)
+
+
 def build_cache_from_tokens(
     latent: np.ndarray,
     rope: np.ndarray,

@@ -1,0 +1,49 @@
+"""Host-side behaviour of the drop-in cache that needs no GPU: argument checks and error types."""
+from __future__ import annotations
+
+import pytest
+import torch
+
+
+def test_unsupported_configurations_raise():
+    from asterq.cache import LatentLayerCache
+
+    with pytest.raises(NotImplementedError):
+        LatentLayerCache("int8")
+    with pytest.raises(NotImplementedError):
+        LatentLayerCache("hadamard_int4", group_size=32)
+    with pytest.raises(NotImplementedError):
+        LatentLayerCache("hadamard_int4", quantize_rope=True)
+    with pytest.raises(ValueError):
+        LatentLayerCache("hadamard_int4", chunk_tokens=100)
+
+
+def test_empty_cache_reports_nothing():
+    from asterq.cache import LatentLayerCache
+
+    c = LatentLayerCache("hadamard_int4", chunk_tokens=512)
+    assert c.length == 0 and c.cold_length == 0 and c.num_bytes == 0
+    assert c.latent is None and c.materialize_latent() is None
+    assert list(c.iter_chunks(dtype=torch.float32, device=torch.device("cpu"))) == []
+
+
+def test_cpu_tensors_are_rejected():
+    from asterq.cache import LatentLayerCache
+
+    c = LatentLayerCache("hadamard_int4", chunk_tokens=512)
+    with pytest.raises(RuntimeError):
+        c.append(torch.zeros(1, 4, 512), torch.zeros(1, 4, 64), None, 0)
+    with pytest.raises(ValueError):
+        c.append(torch.zeros(1, 4, 256), torch.zeros(1, 4, 64), None, 0)
+
+
+def test_aster_cache_builds_layers_from_its_settings():
+    from asterq.cache import AsterCache
+
+    cache = AsterCache(cache_dtype="hadamard_int4", cache_recent_tokens=256, cache_chunk_tokens=512)
+    layer = cache.latent_layer(3)
+    assert layer is cache.latent_layer(3)
+    assert (layer.cache_dtype, layer.recent_tokens, layer.chunk_tokens) == ("hadamard_int4", 256, 512)
+    assert cache.num_bytes == 0
+    cache.reset()
+    assert not cache.latent

@@ -1,0 +1,175 @@
+"""The paged drop-in cache and attention mirror against the oracle's replay of the reference.
+
+* cold chunks: codes and scales bit-identical to ``quantize_tensor`` on the same
+  tokens, flushed at the reference's threshold (cache.py:167-177), whether the
+  history arrives at once or token by token;
+* lengths and ``num_bytes`` as the reference accounts them (cache.py:72-87);
+* ``materialize_*`` / ``iter_chunks`` equal the oracle's dequantized view bit for bit;
+* ``latent_attention`` / ``LatentAttentionKernels`` within the decode tolerance
+  (rel-L2 <= 1e-3, max-abs <= 2e-2 on fp32 outputs).
+"""
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import hq4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+SCALE = 1.0 / math.sqrt(512 + 64)
+
+
+def _inputs(seed, n, q_len=1):
+    from asterq.synth import c1_inputs
+
+    return c1_inputs(seed=seed, ctx=n, q_len=q_len)
+
+
+def _bf16_np(t):
+    return t.float().cpu().numpy()
+
+
+def test_bulk_append_matches_reference_flush(cuda):
+    from asterq.cache import LatentLayerCache
+
+    inp = _inputs(1, 3000)
+    lat, rope = inp["latent"][:3000], inp["rope"][:3000]
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=512, chunk_tokens=512)
+    cache.append(lat[None].to(cuda), rope[None].to(cuda), None, 0)
+    ref = O.build_cache_from_tokens(_bf16_np(lat), _bf16_np(rope), 512, 512)
+    assert cache.cold_chunks == len(ref.cold) and cache.length == ref.length == 3000
+    assert cache.hot_length == ref.hot_latent.shape[0]
+    for q, r, c in zip(cache.cold_latent, cache.cold_rope, ref.cold):
+        np.testing.assert_array_equal(q.data[0].cpu().numpy(), c.codes)
+        np.testing.assert_array_equal(q.scale[0, :, :, 0].cpu().numpy(), c.scales)
+        np.testing.assert_array_equal(_bf16_np(r[0]), c.rope)
+    np.testing.assert_array_equal(_bf16_np(cache.latent[0]), ref.hot_latent)
+    np.testing.assert_array_equal(_bf16_np(cache.rope_key[0]), ref.hot_rope)
+    assert cache.num_bytes == ref.cold_length * 400 + ref.hot_latent.shape[0] * 1152
+
+
+def test_token_by_token_append_equals_bulk(cuda):
+    from asterq.cache import LatentLayerCache
+
+    inp = _inputs(2, 1700)
+    lat, rope = inp["latent"][:1700].to(cuda), inp["rope"][:1700].to(cuda)
+    bulk = LatentLayerCache("hadamard_int4", 64, recent_tokens=256, chunk_tokens=512)
+    bulk.append(lat[None], rope[None], None, 0)
+    step = LatentLayerCache("hadamard_int4", 64, recent_tokens=256, chunk_tokens=512)
+    step.append(lat[None, :900], rope[None, :900], None, 0)
+    for i in range(900, 1700, 40):
+        step.append(lat[None, i:i + 40], rope[None, i:i + 40], None, 0)
+        assert step.hot_length <= 256 + 512
+    assert step.cold_chunks == bulk.cold_chunks and step.length == bulk.length
+    for a, b in zip(step.cold_latent, bulk.cold_latent):
+        assert torch.equal(a.data, b.data) and torch.equal(a.scale, b.scale)
+    assert torch.equal(step.latent, bulk.latent)
+
+
+def test_batch_rows_are_independent(cuda):
+    from asterq.cache import LatentLayerCache
+
+    a, b = _inputs(3, 1400), _inputs(4, 1400)
+    lat = torch.stack([a["latent"][:1400], b["latent"][:1400]]).to(cuda)
+    rope = torch.stack([a["rope"][:1400], b["rope"][:1400]]).to(cuda)
+    both = LatentLayerCache("hadamard_int4", 64, recent_tokens=128, chunk_tokens=256)
+    both.append(lat, rope, None, 0)
+    for row in range(2):
+        one = LatentLayerCache("hadamard_int4", 64, recent_tokens=128, chunk_tokens=256)
+        one.append(lat[row:row + 1], rope[row:row + 1], None, 0)
+        for x, y in zip(both.cold_latent, one.cold_latent):
+            assert torch.equal(x.data[row], y.data[0]) and torch.equal(x.scale[row], y.scale[0])
+        assert torch.equal(both.latent[row], one.latent[0])
+
+
+def test_materialize_and_iter_chunks_match_oracle(cuda):
+    from asterq.cache import LatentLayerCache
+
+    inp = _inputs(5, 2100)
+    lat, rope = inp["latent"][:2100], inp["rope"][:2100]
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=512, chunk_tokens=512)
+    cache.append(lat[None].to(cuda), rope[None].to(cuda), None, 0)
+    ref = O.build_cache_from_tokens(_bf16_np(lat), _bf16_np(rope), 512, 512)
+    want_lat, want_rope = ref.materialize()
+    got_lat = cache.materialize_latent(dtype=torch.float32)[0].cpu().numpy()
+    got_rope = cache.materialize_rope(dtype=torch.float32)[0].cpu().numpy()
+    np.testing.assert_array_equal(got_lat, want_lat)
+    np.testing.assert_array_equal(got_rope, want_rope)
+    chunks = list(cache.iter_chunks(dtype=torch.float32, device=cuda))
+    assert len(chunks) == len(ref.cold) + 1
+    np.testing.assert_array_equal(torch.cat([c[0] for c in chunks], dim=1)[0].cpu().numpy(), want_lat)
+
+
+@pytest.mark.parametrize("q_len", [1, 3])
+def test_latent_attention_over_the_cache(cuda, q_len):
+    from asterq.attention import latent_attention
+    from asterq.cache import LatentLayerCache
+
+    n = 4000
+    inp = _inputs(6 + q_len, n, q_len)
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=512, chunk_tokens=512)
+    cache.append(inp["latent"][None, :n].to(cuda), inp["rope"][None, :n].to(cuda), None, 0)
+    out = latent_attention(inp["q_lat"][None].to(cuda), inp["q_rope"][None].to(cuda),
+                           inp["latent"][None, n:].to(cuda), inp["rope"][None, n:].to(cuda), cache,
+                           softmax_scale=SCALE)
+    lat, rope = _bf16_np(inp["latent"]), _bf16_np(inp["rope"])
+    ref_cache = O.build_cache_from_tokens(lat[:n], rope[:n], 512, 512)
+    ref = O.decode(_bf16_np(inp["q_lat"]), _bf16_np(inp["q_rope"]), lat[n:], rope[n:], ref_cache, SCALE)
+    got = out[0].cpu().numpy()
+    assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2
+
+
+def test_empty_cache_prefill_is_causal(cuda):
+    from asterq.attention import latent_attention
+
+    inp = _inputs(9, 0, 4)
+    out = latent_attention(inp["q_lat"][None].to(cuda), inp["q_rope"][None].to(cuda),
+                           inp["latent"][None].to(cuda), inp["rope"][None].to(cuda), None, softmax_scale=SCALE)
+    ref = O.decode(_bf16_np(inp["q_lat"]), _bf16_np(inp["q_rope"]), _bf16_np(inp["latent"]), _bf16_np(inp["rope"]),
+                   O.LatentCacheView(cold=[], hot_latent=np.zeros((0, 512), np.float32),
+                                     hot_rope=np.zeros((0, 64), np.float32)), SCALE)
+    got = out[0].cpu().numpy()
+    assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2
+
+
+def test_kernel_module_absorbs_weights(cuda):
+    from asterq.attention import LatentAttentionKernels
+    from asterq.cache import LatentLayerCache
+
+    n, heads, hd = 2500, 16, 64
+    inp = _inputs(10, n)
+    g = torch.Generator().manual_seed(11)
+    wk = (torch.randn(heads * hd, 512, generator=g) / 24).to(cuda)
+    wv = (torch.randn(heads * hd, 512, generator=g) / 24).to(cuda)
+    mod = LatentAttentionKernels(wk, wv, heads, hd)
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=512, chunk_tokens=512)
+    cache.append(inp["latent"][None, :n].to(cuda), inp["rope"][None, :n].to(cuda), None, 0)
+    q_content = torch.randn(1, 1, heads, hd, generator=g).to(cuda)
+    q_rope = inp["q_rope"][None].float().to(cuda)
+    out = mod._absorbed_decode(q_content, q_rope, inp["latent"][None, n:].float().to(cuda),
+                               inp["rope"][None, n:].float().to(cuda), cache)
+    # oracle: same absorbed query, oracle attention, same value projection
+    q_lat = torch.einsum("bthd,hdl->bthl", q_content, wk.view(heads, hd, 512))
+    q_lat_bf = q_lat.to(torch.bfloat16).float()[0].cpu().numpy()
+    lat, rope = _bf16_np(inp["latent"]), _bf16_np(inp["rope"])
+    ctx = O.decode(q_lat_bf, _bf16_np(inp["q_rope"]), lat[n:], rope[n:], O.build_cache_from_tokens(lat[:n], rope[:n], 512, 512),
+                   1.0 / math.sqrt(hd + 64))
+    want = torch.einsum("thl,hdl->thd", torch.from_numpy(ctx), wv.view(heads, hd, 512).cpu()).numpy()
+    got = out[0].cpu().numpy()
+    assert O.rel_l2(got, want) <= 1e-3
+
+
+def test_window_trim_keeps_sink_and_recent(cuda):
+    from asterq.cache import LatentLayerCache
+
+    inp = _inputs(12, 3000)
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=256, chunk_tokens=256)
+    lat, rope = inp["latent"][None, :3000].to(cuda), inp["rope"][None, :3000].to(cuda)
+    cache.append(lat[:, :2000], rope[:, :2000], 1000, 4)
+    assert cache.length == 1000
+    cache.append(lat[:, 2000:2100], rope[:, 2000:2100], 1000, 4)
+    assert cache.length <= 1000 + 256 and cache.hot_length <= 512
