@@ -81,6 +81,9 @@ class DecodeParams(ctypes.Structure):
         ("workspace", ctypes.c_void_p),
         ("workspace_bytes", ctypes.c_int64),
         ("device_status", ctypes.c_void_p),
+        ("units", ctypes.c_void_p),
+        ("n_units", ctypes.c_int32),
+        ("_pad", ctypes.c_int32),
     ]
 
 

@@ -64,8 +64,8 @@ class DeviceDecodePlan:
         self.tiles = up(plan.tiles)
         self.items = up(plan.items)
         self.combine = up(plan.combine)
-        ws_floats = max(1, plan.n_slots * 16 * (LATENT_DIM + 2))
-        self.workspace = torch.empty(ws_floats, dtype=torch.float32, device=self.device)
+        self.units = up(plan.units)
+        self.workspace = torch.empty(max(4, plan.workspace_bytes // 4), dtype=torch.float32, device=self.device)
 
     @property
     def n_items(self) -> int:
@@ -117,6 +117,8 @@ def make_params(
     p.out = out.data_ptr()
     p.workspace = dplan.workspace.data_ptr()
     p.workspace_bytes = dplan.workspace.numel() * 4
+    p.units = dplan.units.data_ptr()
+    p.n_units = int(plan.n_units)
     return p
 
 

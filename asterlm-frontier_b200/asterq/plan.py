@@ -60,6 +60,9 @@ class SequenceLayout:
         return self.cold_tokens * _COLD_TOKEN_BYTES + (self.hot_tokens + self.q_len * self.attend_new) * _HOT_TOKEN_BYTES
 
 
+QPREP_BYTES = 35328  # prepared query operands of one 16-row block (int8 limbs, bf16 fragments, scalars)
+
+
 @dataclass
 class DecodePlan:
     tiles: np.ndarray
@@ -68,10 +71,15 @@ class DecodePlan:
     n_slots: int
     total_q: int
     n_heads: int
+    units: np.ndarray = field(default_factory=lambda: np.zeros((0, 2), np.int32))  # [n_units][2] {out_row0, n_rows}
+
+    @property
+    def n_units(self) -> int:
+        return int(self.units.shape[0])
 
     @property
     def workspace_bytes(self) -> int:
-        return self.n_slots * ROWS_PER_BLOCK * (512 + 2) * 4
+        return self.n_slots * ROWS_PER_BLOCK * (512 + 2) * 4 + self.n_units * QPREP_BYTES
 
 
 def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
@@ -97,7 +105,7 @@ def build_plan(
     *,
     n_sms: int = 148,
     ctas_per_sm: int = 1,
-    waves: float = 2.0,
+    waves: float = 3.0,
     max_items_per_seq: int | None = None,
     force_partial: bool = False,
 ) -> DecodePlan:
@@ -142,18 +150,20 @@ def build_plan(
 
     items = []
     combine = []
+    unit_rows = []
     n_slots = 0
-    for si, rb, t0, t1, c in units:
+    for ui, (si, rb, t0, t1, c) in enumerate(units):
         seq = seqs[si]
         rows = seq.q_len * n_heads
         out_row0 = seq.q_start * n_heads + rb * ROWS_PER_BLOCK
         n_rows = min(ROWS_PER_BLOCK, rows - rb * ROWS_PER_BLOCK)
+        unit_rows.append((out_row0, n_rows))
         k = max(1, int(np.ceil((c + _ITEM_OVERHEAD_BYTES) / (item_cost + _ITEM_OVERHEAD_BYTES))))
         k = min(k, t1 - t0)
         if max_items_per_seq is not None:
             k = min(k, max_items_per_seq)
         if k <= 1 and not force_partial:
-            items.append((si, rb, t0, t1, -1, out_row0, n_rows, seq.q_len, c))
+            items.append((ui, rb, t0, t1, -1, out_row0, n_rows, seq.q_len, c))
             continue
         k = max(k, 1)
         # contiguous ranges of ~equal cost
@@ -162,11 +172,12 @@ def build_plan(
         bounds = [t0] + sorted(set(int(x) for x in cuts if t0 < x < t1)) + [t1]
         s0 = n_slots
         for a, b in zip(bounds[:-1], bounds[1:]):
-            items.append((si, rb, a, b, n_slots, out_row0, n_rows, seq.q_len, int(prefix[b] - prefix[a])))
+            items.append((ui, rb, a, b, n_slots, out_row0, n_rows, seq.q_len, int(prefix[b] - prefix[a])))
             n_slots += 1
         combine.append((s0, n_slots, out_row0, n_rows))
 
     items.sort(key=lambda it: -it[8])
     item_arr = np.asarray([it[:8] for it in items], dtype=np.int32).reshape(-1, 8)
     comb_arr = np.asarray(combine, dtype=np.int32).reshape(-1, 4)
-    return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads)
+    unit_arr = np.asarray(unit_rows, dtype=np.int32).reshape(-1, 2)
+    return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr)

@@ -89,6 +89,12 @@ constexpr int kMQinv = 240;    // [16]  (score multiplier 2^-e * softmax_scale)
 constexpr int kMQint = 256;    // [16]  fixed-point query scale (32511 / max |rotated row|)
 constexpr int kMQinvI = 272;   // [16]  cold integer-score multiplier softmax_scale / (16 * kMQint)
 constexpr int kMRopeR = 288;   // [16]  RoPE score -> integer-score units (kMQinv / kMQinvI)
+constexpr int kQScalars = 80;  // kMQscale .. kMRopeR: the per-row scalars of a prepared query block
+
+// workspace: n_slots partial records, then n_units prepared query blocks
+constexpr int kRecordBytes = kRows * (kL + 2) * 4;                    // 32,896
+constexpr int kQPrepBytes = 16384 + 16384 + 2048 + 512;               // 35,328: qi | qh | qr | scalars
+constexpr uint32_t kQPrepCopyBytes = 16384 + 16384 + 2048 + 4 * kQScalars;
 
 // mbarrier slots (8 bytes each)
 constexpr int kBarFull = 0;    // [3] TMA landed
@@ -96,6 +102,7 @@ constexpr int kBarEmpty = 3;   // [3] score + value warps done with a stage
 constexpr int kBarPFull = 6;   // [2] p tile written
 constexpr int kBarPEmpty = 8;  // [2] p tile consumed
 constexpr int kBarAbort = 10;  // int flag (shares the slot area)
+constexpr int kBarQ = 11;      // prepared query operands landed
 
 constexpr float kLog2e = 1.4426950408889634f;
 // 0x4B400000 read as fp32 is 1.5 * 2^23 = 12582912: an int32 accumulator started at this
@@ -238,6 +245,125 @@ ASTERQ_DEVICE int qk_token(int warp, int m, int r) {
   return 32 * warp + 16 * m + (((g & 3) << 1) | (g >> 2)) + (r & 8);
 }
 
+// ---------------------------------------------------------------------------
+// Query preparation: one CTA per 16-row block (unit) writes the block's query
+// operands to the workspace, in the layout of their shared-memory regions, so
+// that every work item of the block starts with a 35 KB bulk copy instead of
+// rotating and re-encoding the query itself.
+//   qi      [16 k-steps][2 row tiles][32 lanes] uint4: rotated query as a per-row
+//           16-bit fixed-point number split in two int8 limbs (cold QK B operand)
+//   qh      [8 groups][4 k-steps][2][32] uint2: bf16 query x 2^e (hot QK B operand)
+//   qr      [4][2][32] uint2: bf16 RoPE query x 2^e
+//   scalars 2^e, 2^-e * scale, fixed-point scale, the two score multipliers
+// ---------------------------------------------------------------------------
+constexpr int kPrepThreads = 256;
+constexpr int kPrepSmem = 16 * kL * 4 + 16 * kL * 2 + 16 * kRope * 2 + 4 * kQScalars;
+
+__global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const asterq_decode_params p) {
+  extern __shared__ __align__(16) uint8_t prep_smem[];
+  float* scratch = reinterpret_cast<float*>(prep_smem);                            // [16][512] fp32
+  uint16_t* qraw = reinterpret_cast<uint16_t*>(prep_smem + 16 * kL * 4);           // [16][512] bf16
+  uint16_t* rraw = reinterpret_cast<uint16_t*>(prep_smem + 16 * kL * 6);           // [16][64] bf16
+  float* sc = reinterpret_cast<float*>(prep_smem + 16 * kL * 6 + 16 * kRope * 2);  // kQScalars, from kMQscale
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int unit = blockIdx.x;
+  const int64_t out_row0 = p.units[2 * unit];
+  const int n_rows = min(max(p.units[2 * unit + 1], 0), kRows);
+  uint8_t* dst = reinterpret_cast<uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes + (int64_t)unit * kQPrepBytes;
+
+  const uint16_t* ql = reinterpret_cast<const uint16_t*>(p.q_lat);
+  const uint16_t* qrp = reinterpret_cast<const uint16_t*>(p.q_rope);
+  for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
+    float* d = scratch + r * kL + 16 * lane;
+    uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a, c = a;
+    if (r < n_rows) {
+      a = *reinterpret_cast<const uint4*>(ql + (out_row0 + r) * kL + 16 * lane);
+      b = *reinterpret_cast<const uint4*>(ql + (out_row0 + r) * kL + 16 * lane + 8);
+      if (lane < 8) c = *reinterpret_cast<const uint4*>(qrp + (out_row0 + r) * kRope + 8 * lane);
+    }
+    *reinterpret_cast<uint4*>(qraw + r * kL + 16 * lane) = a;
+    *reinterpret_cast<uint4*>(qraw + r * kL + 16 * lane + 8) = b;
+    if (lane < 8) *reinterpret_cast<uint4*>(rraw + r * kRope + 8 * lane) = c;
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      d[2 * k] = bf16lo_to_f32(w[k]);
+      d[2 * k + 1] = bf16hi_to_f32(w[k]);
+    }
+  }
+  __syncwarp();
+  warp_fwht_rows(scratch, 2 * warp, 2, lane);
+  __syncwarp();
+  for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
+    float mx = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(scratch[r * kL + 16 * lane + k]));
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    if (lane == 0) {
+      int e = 0;
+      if (mx > 0.0f) {
+        int ex;
+        frexpf(mx, &ex);
+        e = min(max(14 - ex, -100), 100);
+      }
+      const float qs = (mx > 0.0f) ? 32511.0f / mx : 1.0f;
+      sc[r] = ldexpf(1.0f, e);
+      sc[kMQinv - kMQscale + r] = ldexpf(1.0f, -e) * p.softmax_scale;
+      sc[kMQint - kMQscale + r] = qs;
+      sc[kMQinvI - kMQscale + r] = p.softmax_scale / (16.0f * qs);
+      sc[kMRopeR - kMQscale + r] = ldexpf(1.0f, -e) * (16.0f * qs);
+    }
+  }
+  __syncthreads();
+  // cold QK B fragments: k-step ks = 2 * group + j; lane (gid, tq) holds query row 8nt + gid at
+  // k = 4tq + i (b0) and 16 + 4tq + i (b1), which the code expansion maps to dims 8W + 2i and
+  // 8W + 2i + 1 of code word W = 8 * group + 2tq + j.  Two int8 limbs: q = 256 hi + lo.
+  uint4* qi = reinterpret_cast<uint4*>(dst);
+  for (int e = tid; e < 16 * 2 * 32; e += kPrepThreads) {
+    const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
+    const int row = 8 * nt + (ln >> 2), W = 8 * (ks >> 1) + 2 * (ln & 3) + (ks & 1);
+    const float qs = sc[kMQint - kMQscale + row];
+    uint32_t hb[2] = {0u, 0u}, lb[2] = {0u, 0u};
+#pragma unroll
+    for (int half = 0; half < 2; ++half)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int qv = min(max(__float2int_rn(scratch[row * kL + 8 * W + 2 * i + half] * qs), -32511), 32511);
+        const int q1 = (qv + 128) >> 8;  // floor((q + 128) / 256): q1 in [-127, 127], q - 256 q1 in [-128, 127]
+        const int q2 = qv - 256 * q1;
+        hb[half] |= (uint32_t)(q1 & 0xff) << (8 * i);
+        lb[half] |= (uint32_t)(q2 & 0xff) << (8 * i);
+      }
+    qi[e] = make_uint4(hb[0], hb[1], lb[0], lb[1]);
+  }
+  // hot-tile and RoPE bf16 fragments, in the order each consumer lane loads them
+  uint2* qh = reinterpret_cast<uint2*>(dst + 16384);
+  for (int e = tid; e < 8 * 4 * 2 * 32; e += kPrepThreads) {
+    const int ln = e & 31, nt = (e >> 5) & 1, ks = (e >> 6) & 3, g = e >> 8;
+    const int row = 8 * nt + (ln >> 2);
+    const int e0 = 64 * g + 16 * ks + 2 * (ln & 3);
+    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(qraw + row * kL + e0);
+    const uint32_t w1 = *reinterpret_cast<const uint32_t*>(qraw + row * kL + e0 + 8);
+    const float s2 = sc[row];
+    const float2 f0 = unpack_bf162(w0), f1 = unpack_bf162(w1);
+    qh[e] = make_uint2(pack_bf162(f0.x * s2, f0.y * s2), pack_bf162(f1.x * s2, f1.y * s2));
+  }
+  uint2* qr = reinterpret_cast<uint2*>(dst + 32768);
+  for (int e = tid; e < 4 * 2 * 32; e += kPrepThreads) {
+    const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
+    const int row = 8 * nt + (ln >> 2);
+    const int e0 = 16 * ks + 2 * (ln & 3);
+    const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rraw + row * kRope + e0);
+    const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rraw + row * kRope + e0 + 8);
+    const float s2 = sc[row];
+    const float2 f0 = unpack_bf162(w0), f1 = unpack_bf162(w1);
+    qr[e] = make_uint2(pack_bf162(f0.x * s2, f0.y * s2), pack_bf162(f1.x * s2, f1.y * s2));
+  }
+  float* scalars = reinterpret_cast<float*>(dst + 34816);
+  for (int e = tid; e < kQScalars; e += kPrepThreads) scalars[e] = sc[e];
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
   extern __shared__ uint8_t smem_raw[];
@@ -268,6 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(kBarPFull + b), 32 * kScoreWarps);
       mbar_init(bar(kBarPEmpty + b), 32 * kValueWarps);
     }
+    mbar_init(bar(kBarQ), 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -306,110 +433,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   }
 
-  // ---------------- prologue: rotated, prescaled query fragments ----------------
-  // scratch: the last stage (its first tile is issued after the prologue)
-  float* scratch = reinterpret_cast<float*>(smem + (kStages - 1) * kStageBytes);  // [16][512] fp32
-  // raw bf16 query rows [16][512] and RoPE-query rows [16][64] behind it
-  uint16_t* qraw = reinterpret_cast<uint16_t*>(smem + (kStages - 1) * kStageBytes + 32768);
-  uint16_t* rraw = reinterpret_cast<uint16_t*>(smem + (kStages - 1) * kStageBytes + 49152);
-  if (warp < 8) {
-    const uint16_t* ql = reinterpret_cast<const uint16_t*>(p.q_lat);
-    const uint16_t* qrp = reinterpret_cast<const uint16_t*>(p.q_rope);
-    for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
-      float* dst = scratch + r * kL + 16 * lane;
-      uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a, c = a;
-      if (r < n_rows) {
-        a = *reinterpret_cast<const uint4*>(ql + (out_row0 + r) * kL + 16 * lane);
-        b = *reinterpret_cast<const uint4*>(ql + (out_row0 + r) * kL + 16 * lane + 8);
-        if (lane < 8) c = *reinterpret_cast<const uint4*>(qrp + (out_row0 + r) * kRope + 8 * lane);
-      }
-      *reinterpret_cast<uint4*>(qraw + r * kL + 16 * lane) = a;
-      *reinterpret_cast<uint4*>(qraw + r * kL + 16 * lane + 8) = b;
-      if (lane < 8) *reinterpret_cast<uint4*>(rraw + r * kRope + 8 * lane) = c;
-      const uint32_t w[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-      for (int k = 0; k < 8; ++k) {
-        dst[2 * k] = bf16lo_to_f32(w[k]);
-        dst[2 * k + 1] = bf16hi_to_f32(w[k]);
-      }
-    }
-    __syncwarp();
-    warp_fwht_rows(scratch, 2 * warp, 2, lane);
-    __syncwarp();
-    for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
-      float mx = 0.0f;
-#pragma unroll
-      for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(scratch[r * kL + 16 * lane + k]));
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
-      if (lane == 0) {
-        int e = 0;
-        if (mx > 0.0f) {
-          int ex;
-          frexpf(mx, &ex);
-          e = min(max(14 - ex, -100), 100);
-        }
-        misc[kMQscale + r] = ldexpf(1.0f, e);
-        misc[kMQinv + r] = ldexpf(1.0f, -e) * p.softmax_scale;
-        const float qs = (mx > 0.0f) ? 32511.0f / mx : 1.0f;
-        misc[kMQint + r] = qs;
-        misc[kMQinvI + r] = p.softmax_scale / (16.0f * qs);
-        misc[kMRopeR + r] = ldexpf(1.0f, -e) * (16.0f * qs);
-      }
-    }
-  }
-  __syncthreads();
-  // B fragments, stored in the order each consumer lane loads them
-  {
-    {
-      // cold QK B fragments: k-step ks = 2 * group + j; lane (gid, tq) holds query row 8nt + gid at
-      // k = 4tq + i (b0) and 16 + 4tq + i (b1), which the code expansion maps to dims 8W + 2i and
-      // 8W + 2i + 1 of code word W = 8 * group + 2tq + j.  Two int8 limbs: q = 256 hi + lo.
-      uint4* qi = reinterpret_cast<uint4*>(smem + kOffQi);
-      for (int e = tid; e < 16 * 2 * 32; e += kThreads) {
-        const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
-        const int row = 8 * nt + (ln >> 2), W = 8 * (ks >> 1) + 2 * (ln & 3) + (ks & 1);
-        const float qs = misc[kMQint + row];
-        uint32_t hb[2] = {0u, 0u}, lb[2] = {0u, 0u};
-#pragma unroll
-        for (int half = 0; half < 2; ++half)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int qv = min(max(__float2int_rn(scratch[row * kL + 8 * W + 2 * i + half] * qs), -32511), 32511);
-            const int q1 = (qv + 128) >> 8;  // floor((q + 128) / 256): q1 in [-127, 127], q - 256 q1 in [-128, 127]
-            const int q2 = qv - 256 * q1;
-            hb[half] |= (uint32_t)(q1 & 0xff) << (8 * i);
-            lb[half] |= (uint32_t)(q2 & 0xff) << (8 * i);
-          }
-        qi[e] = make_uint4(hb[0], hb[1], lb[0], lb[1]);
-      }
-      uint2* qh = reinterpret_cast<uint2*>(smem + kOffQh);
-      for (int e = tid; e < 8 * 4 * 2 * 32; e += kThreads) {
-        const int ln = e & 31, nt = (e >> 5) & 1, ks = (e >> 6) & 3, g = e >> 8;
-        const int row = 8 * nt + (ln >> 2);
-        const int e0 = 64 * g + 16 * ks + 2 * (ln & 3);
-        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(qraw + row * kL + e0);
-        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(qraw + row * kL + e0 + 8);
-        const float sc = misc[kMQscale + row];
-        const float2 f0 = unpack_bf162(w0), f1 = unpack_bf162(w1);
-        qh[e] = make_uint2(pack_bf162(f0.x * sc, f0.y * sc), pack_bf162(f1.x * sc, f1.y * sc));
-      }
-      uint2* qr = reinterpret_cast<uint2*>(smem + kOffQr);
-      for (int e = tid; e < 4 * 2 * 32; e += kThreads) {
-        const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
-        const int row = 8 * nt + (ln >> 2);
-        const int e0 = 16 * ks + 2 * (ln & 3);
-        const uint32_t w0 = *reinterpret_cast<const uint32_t*>(rraw + row * kRope + e0);
-        const uint32_t w1 = *reinterpret_cast<const uint32_t*>(rraw + row * kRope + e0 + 8);
-        const float sc = misc[kMQscale + row];
-        const float2 f0 = unpack_bf162(w0), f1 = unpack_bf162(w1);
-        qr[e] = make_uint2(pack_bf162(f0.x * sc, f0.y * sc), pack_bf162(f1.x * sc, f1.y * sc));
-      }
-    }
-  }
-  __syncthreads();  // fragments ready; the scratch stage is free
+  // ---------------- prologue: this row block's prepared query operands ----------------
+  // (qprep_kernel wrote them to the workspace: int8 limb fragments, hot and RoPE bf16
+  // fragments, per-row scalars, laid out like their shared-memory regions)
   if (warp == kProducerWarp) {
-    if (lane == 0 && n_t > kStages - 1) issue(kStages - 1);
+    if (lane == 0) {
+      const uint8_t* src = reinterpret_cast<const uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes +
+                           (int64_t)max(itm[0], 0) * kQPrepBytes;
+      const uint32_t qb = bar(kBarQ);
+      mbar_expect_tx(qb, kQPrepCopyBytes);
+      bulk_1d(sbase + kOffQi, src, 16384, qb);
+      bulk_1d(sbase + kOffQh, src + 16384, 16384, qb);
+      bulk_1d(sbase + kOffQr, src + 32768, 2048, qb);
+      bulk_1d(sbase + kOffMisc + 4 * kMQscale, src + 34816, 4 * kQScalars, qb);
+      if (n_t > kStages - 1) issue(kStages - 1);
+    }
     __syncwarp();
   }
 
@@ -417,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =====================================================================
     // score warps
     // =====================================================================
+    mbar_wait(bar(kBarQ), 0, abort_flag);
     const uint2* qh = reinterpret_cast<const uint2*>(smem + kOffQh);
     const uint2* qr = reinterpret_cast<const uint2*>(smem + kOffQr);
     float qinv[2][2], qinvi[2][2], rratio[2][2];
@@ -438,10 +477,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         l_w[nt][cc] = 0.0f;
       }
 
+    Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
 #pragma unroll 1
     for (int i = 0; i < n_t; ++i) {
       const int s = i % kStages, b = i & 1;
-      const Tile t = load_tile(p, tile_begin + i);
+      const Tile t = t_next;
+      // the next tile's descriptor is fetched while this one is processed
+      if (i + 1 < n_t) t_next = load_tile(p, tile_begin + i + 1);
       mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);
       const uint8_t* st = smem + s * kStageBytes;
       const uint32_t sst = sbase + s * kStageBytes;
@@ -483,8 +525,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
         const uint4* qi = reinterpret_cast<const uint4*>(smem + kOffQi);
-#pragma unroll 1
-        for (int g = 0; g < 8; ++g) {
+        // Group g's integer dot products (two int8 limbs of the query, both k-steps):
+        // loads, code expansion and 16 MMAs into acc.
+        auto qk_issue = [&](int g, int (&acc)[2][2][2][4]) {
           // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens
           const int region = (g < 4) ? kCodesLo : kCodesHi;
           const int chunk = 2 * (g & 3) + (tq >> 1);
@@ -494,7 +537,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int h = 0; h < 2; ++h)
               v[m][h] = *reinterpret_cast<const uint2*>(st + region + swz(tok[m][h], chunk) + 8 * (tq & 1));
-          int acc[2][2][2][4];  // [limb][m][nt][c]
 #pragma unroll
           for (int j = 0; j < 2; ++j) {
             const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
@@ -514,6 +556,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           }
+        };
+        // S += scale_g x (256 hi + lo), the biased accumulators read as exact floats
+        // (packed f32x2 arithmetic: two accumulator elements per instruction; elements
+        // c = 0,1 belong to token row gid, c = 2,3 to row gid + 8)
+        auto qk_finish = [&](int g, const int (&acc)[2][2][2][4]) {
+          const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
 #pragma unroll
           for (int m = 0; m < 2; ++m) {
             const float s0 = __half2float(scl[8 * tok[m][0] + g]);
@@ -521,12 +569,27 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-              for (int c = 0; c < 4; ++c) {
-                const float fh = __int_as_float(acc[0][m][nt][c]) - kAccBiasF;
-                const float fl = __int_as_float(acc[1][m][nt][c]) - kAccBiasF;
-                S[m][nt][c] = fmaf(fmaf(fh, 256.0f, fl), (c < 2) ? s0 : s1, S[m][nt][c]);
+              for (int h = 0; h < 2; ++h) {
+                const float2 fh = add2(make_float2(__int_as_float(acc[0][m][nt][2 * h]), __int_as_float(acc[0][m][nt][2 * h + 1])), bias2);
+                const float2 fl = add2(make_float2(__int_as_float(acc[1][m][nt][2 * h]), __int_as_float(acc[1][m][nt][2 * h + 1])), bias2);
+                const float sc = h ? s1 : s0;
+                const float2 r = fma2(fma2(fh, k256, fl), make_float2(sc, sc),
+                                      make_float2(S[m][nt][2 * h], S[m][nt][2 * h + 1]));
+                S[m][nt][2 * h] = r.x;
+                S[m][nt][2 * h + 1] = r.y;
               }
           }
+        };
+        // two groups in flight: group g + 1's MMAs run on the tensor pipe while
+        // group g's accumulators are scaled into S
+        int accA[2][2][2][4], accB[2][2][2][4];
+        qk_issue(0, accA);
+#pragma unroll 1
+        for (int g = 0; g < 8; g += 2) {
+          qk_issue(g + 1, accB);
+          qk_finish(g, accA);
+          if (g + 2 < 8) qk_issue(g + 2, accA);
+          qk_finish(g + 1, accB);
         }
       } else {
         // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
@@ -725,10 +788,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
     };
 
+    Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
 #pragma unroll 1
     for (int i = 0; i < n_t; ++i) {
       const int s = i % kStages, b = i & 1;
-      const Tile t = load_tile(p, tile_begin + i);
+      const Tile t = t_next;
+      if (i + 1 < n_t) t_next = load_tile(p, tile_begin + i + 1);
       mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
       mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);  // TMA data visible to this warp
       const uint8_t* st = smem + s * kStageBytes;
@@ -1000,8 +1065,13 @@ int validate(const asterq_decode_params* p) {
   for (const void* ptr : aligned)
     if (reinterpret_cast<uintptr_t>(ptr) & 15)
       return set_error(ASTERQ_ERR_MISALIGNED, "decode: pointers must be 16-byte aligned");
-  const int64_t need = (int64_t)p->n_slots * kRows * (kL + 2) * 4;
-  if (p->n_slots > 0 && (!p->workspace || p->workspace_bytes < need))
+  if (p->n_units < 0) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: negative unit count");
+  if (p->n_items > 0 && (p->n_units == 0 || !p->units))
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: work items need a units table");
+  if (reinterpret_cast<uintptr_t>(p->units) & 7)
+    return set_error(ASTERQ_ERR_MISALIGNED, "decode: the units table must be 8-byte aligned");
+  const int64_t need = (int64_t)p->n_slots * kRecordBytes + (p->n_items > 0 ? (int64_t)p->n_units * kQPrepBytes : 0);
+  if (need > 0 && (!p->workspace || p->workspace_bytes < need))
     return set_error(ASTERQ_ERR_WORKSPACE, "decode: workspace of %lld bytes < %lld needed",
                      (long long)p->workspace_bytes, (long long)need);
   return ASTERQ_OK;
@@ -1052,8 +1122,8 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int row_bytes, in
 using namespace asterq;
 
 extern "C" int64_t asterq_decode_workspace_bytes(const asterq_decode_params* p) {
-  if (!p || p->n_slots <= 0) return 0;
-  return (int64_t)p->n_slots * dec::kRows * (dec::kL + 2) * 4;
+  if (!p) return 0;
+  return (int64_t)max(p->n_slots, 0) * dec::kRecordBytes + (int64_t)max(p->n_units, 0) * dec::kQPrepBytes;
 }
 
 extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream) {
@@ -1068,6 +1138,8 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     if (dev >= 64 || !(configured & (1ull << dev))) {
       cudaError_t e =
           cudaFuncSetAttribute(dec::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(dec::qprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kPrepSmem);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
       if (dev < 64) configured |= (1ull << dev);
     }
@@ -1083,6 +1155,9 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
         (st = dec::make_map(&maps.nlat, p->new_latent, p->total_q, 1024, dec::kHotTile, dummy, 1024)) ||
         (st = dec::make_map(&maps.nrope, p->new_rope, p->total_q, 128, dec::kHotTile, dummy, 1024)))
       return st;
+    dec::qprep_kernel<<<p->n_units, dec::kPrepThreads, dec::kPrepSmem, s>>>(*p);
+    st = check_launch("latent_decode (query preparation)");
+    if (st != ASTERQ_OK) return st;
     dec::decode_kernel<<<p->n_items, dec::kThreads, dec::kSmemBytes, s>>>(*p, maps);
     st = check_launch("latent_decode");
     if (st != ASTERQ_OK) return st;
@@ -1145,13 +1220,16 @@ extern "C" int asterq_splitkv_merge(const float* partials, int32_t n_slots, cons
 // pointers to its inputs and outputs).  For them the split-KV partial records
 // live in a fixed array compiled into this library instead of a caller-provided
 // workspace.  The array is a device global: every GPU that loads the library
-// keeps it (kNoAllocMaxSlots records, about 8.4 MB) until the process exits.
+// keeps it (room for kNoAllocMaxSlots partial records and kNoAllocMaxUnits
+// prepared query blocks, about 17.5 MB) until the process exits.
 // ---------------------------------------------------------------------------
 namespace asterq {
 namespace dec {
 
 constexpr int kNoAllocMaxSlots = 256;
-static __device__ __align__(256) float g_noalloc_workspace[kNoAllocMaxSlots * kRows * (kL + 2)];
+constexpr int kNoAllocMaxUnits = 256;
+static __device__ __align__(256) float
+    g_noalloc_workspace[(kNoAllocMaxSlots * kRecordBytes + kNoAllocMaxUnits * kQPrepBytes) / 4];
 
 }  // namespace dec
 }  // namespace asterq
@@ -1159,11 +1237,12 @@ static __device__ __align__(256) float g_noalloc_workspace[kNoAllocMaxSlots * kR
 extern "C" int asterq_latent_decode_noalloc(const asterq_decode_params* p, void* stream) {
   clear_error();
   if (!p) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode (no-alloc): null params");
-  if (p->n_slots > dec::kNoAllocMaxSlots)
+  if (p->n_slots > dec::kNoAllocMaxSlots || p->n_units > dec::kNoAllocMaxUnits)
     return set_error(ASTERQ_ERR_WORKSPACE,
-                     "decode (no-alloc): the schedule needs %d partial records but the built-in workspace holds %d; "
-                     "build the plan with fewer split items or call asterq_latent_decode with a workspace",
-                     p->n_slots, dec::kNoAllocMaxSlots);
+                     "decode (no-alloc): the schedule needs %d partial records and %d query blocks but the built-in "
+                     "workspace holds %d and %d; build the plan with fewer split items or smaller batches, or call "
+                     "asterq_latent_decode with a workspace",
+                     p->n_slots, p->n_units, dec::kNoAllocMaxSlots, dec::kNoAllocMaxUnits);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "decode (no-alloc): %s", cudaGetErrorString(e));

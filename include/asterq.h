@@ -99,7 +99,9 @@ int asterq_fwht(const float* x, float* y, int64_t rows, int n, void* stream);
  * Schedule (built by the host, see the Python package's plan builder):
  *   tiles [n_tiles][4] int32 = {kind, page (ASTERQ_TILE_NEW: first new-token row), token offset, n_tokens}
  *          cold tiles hold <= 128 tokens, hot/new tiles <= 32 tokens; a tile never crosses a page.
- *   items [n_items][8] int32 = {seq, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
+ *   units [n_units][2] int32 = {out_row0, n_rows}: one per 16-row query block; its query operands
+ *          (rotated, fixed-point, fragment-ordered) are prepared once per call into the workspace.
+ *   items [n_items][8] int32 = {unit, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
  *          one CTA per item; 16 query rows (t, h) per row block, rows flattened as t*n_heads + h.
  *          slot < 0: the item covers the whole sequence and writes `out` directly;
  *          slot >= 0: it writes an (m, l, o) partial to the workspace.
@@ -139,9 +141,13 @@ typedef struct asterq_decode_params {
   void* workspace;
   int64_t workspace_bytes;
   int32_t* device_status; /* optional int32 on the device: set nonzero if a pipeline wait timed out */
+  const int32_t* units;   /* [n_units][2] {out_row0, n_rows}: the 16-row query blocks, prepared once per step */
+  int32_t n_units;
+  int32_t reserved;
 } asterq_decode_params;
 
-/* Bytes of workspace asterq_latent_decode needs (n_slots partial records). */
+/* Bytes of workspace asterq_latent_decode needs: n_slots partial records of 32,896 B
+ * (16 x 514 fp32) followed by n_units prepared query blocks of 35,328 B. */
 int64_t asterq_decode_workspace_bytes(const asterq_decode_params* p);
 
 /* Enqueue the split-KV decode (and, when n_combine > 0, the combine). */
@@ -149,14 +155,15 @@ int asterq_latent_decode(const asterq_decode_params* p, void* stream);
 
 /*
  * Same as asterq_latent_decode, but allocates nothing and ignores
- * p->workspace / p->workspace_bytes: the split-KV partial records go to a
- * fixed array inside this library (room for 256 records, about 8.4 MB on every
- * GPU that loads the library, kept until the process exits).  No counterpart in
+ * p->workspace / p->workspace_bytes: the split-KV partial records and the
+ * prepared query blocks go to a fixed array inside this library (room for 256
+ * records and 256 query blocks, about 17.5 MB on every GPU that loads the
+ * library, kept until the process exits).  No counterpart in
  * the reference; it exists for callers that cannot allocate device memory at
  * decode time (pre-planned serving loops, plain C hosts that only hold pointers
  * to their inputs and outputs).
- *   - Schedules needing more than 256 partial records are rejected with
- *     ASTERQ_ERR_WORKSPACE (build the plan with fewer split items).
+ *   - Schedules needing more than 256 partial records or 256 query blocks
+ *     (16 query rows each) are rejected with ASTERQ_ERR_WORKSPACE.
  *   - The first call on a device resolves the array's address; make that first
  *     call before any stream capture.
  *   - All calls share the one array: calls that overlap on the GPU (for
