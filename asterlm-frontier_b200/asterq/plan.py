@@ -159,7 +159,8 @@ def build_plan(
         n_rows = min(ROWS_PER_BLOCK, rows - rb * ROWS_PER_BLOCK)
         unit_rows.append((out_row0, n_rows))
         k = max(1, int(np.ceil((c + _ITEM_OVERHEAD_BYTES) / (item_cost + _ITEM_OVERHEAD_BYTES))))
-        k = min(k, t1 - t0)
+        # one row block never needs more items than can run at once
+        k = min(k, t1 - t0, max(1, int(n_sms * ctas_per_sm)))
         if max_items_per_seq is not None:
             k = min(k, max_items_per_seq)
         if k <= 1 and not force_partial:

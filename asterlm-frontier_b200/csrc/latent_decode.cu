@@ -970,17 +970,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Merge partial records (latent_attention.py:212-220 applied across splits).
-// Grid: (combine job, 32-dim slice of the latent); 256 threads = 16 rows x 16
-// pairs of dims, so a long sequence's many records are read by many CTAs.
-constexpr int kCombDims = 32;
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
+// Grid: (combine job, 8-dim slice of the latent); 64 threads = 16 rows x 4 pairs
+// of dims, so a long sequence's many records are read by 64 CTAs per job.
+constexpr int kCombDims = 8;
+constexpr int kCombThreads = kRows * kCombDims / 2;
+__global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                       const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                       int n_slots, int latent_dim, void* __restrict__ out,
                                                       int out_dtype) {
   const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
   const int slot_begin = max(job.x, 0), slot_end = min(job.y, n_slots), n_rows = min(job.w, kRows);
   const int64_t out_row0 = job.z;
-  const int r = threadIdx.x >> 4, d = blockIdx.y * kCombDims + 2 * (threadIdx.x & 15);
+  const int r = threadIdx.x / (kCombDims / 2), d = blockIdx.y * kCombDims + 2 * (threadIdx.x % (kCombDims / 2));
   if (r >= n_rows || slot_end <= slot_begin || d >= latent_dim) return;
   float mmax = -INFINITY;
   for (int s = slot_begin; s < slot_end; ++s) mmax = fmaxf(mmax, wm[(int64_t)s * kRows + r]);
@@ -1007,12 +1008,12 @@ __global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ 
 // the workspace (o [n_jobs][16][latent_dim], then m [n_jobs][16], then l [n_jobs][16]).
 // Context-parallel decode merges each rank's split-KV records this way before
 // the records of all ranks are gathered.
-__global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
+__global__ void __launch_bounds__(kCombThreads) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                     const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                     int n_slots, int n_jobs, int latent_dim, float* __restrict__ merged) {
   const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
   const int slot_begin = max(job.x, 0), slot_end = min(job.y, n_slots);
-  const int r = threadIdx.x >> 4, d = blockIdx.y * kCombDims + 2 * (threadIdx.x & 15);
+  const int r = threadIdx.x / (kCombDims / 2), d = blockIdx.y * kCombDims + 2 * (threadIdx.x % (kCombDims / 2));
   if (d >= latent_dim) return;
   float mmax = -INFINITY;
   for (int s = slot_begin; s < slot_end; ++s) mmax = fmaxf(mmax, wm[(int64_t)s * kRows + r]);
@@ -1029,7 +1030,7 @@ __global__ void __launch_bounds__(256) merge_kernel(const float* __restrict__ wo
   float* mm = mo + (int64_t)n_jobs * kRows * latent_dim;
   float* ml = mm + (int64_t)n_jobs * kRows;
   *reinterpret_cast<float2*>(mo + ((int64_t)blockIdx.x * kRows + r) * latent_dim + d) = make_float2(a0, a1);
-  if (blockIdx.y == 0 && (threadIdx.x & 15) == 0) {
+  if (blockIdx.y == 0 && threadIdx.x % (kCombDims / 2) == 0) {
     mm[(int64_t)blockIdx.x * kRows + r] = mmax;
     ml[(int64_t)blockIdx.x * kRows + r] = l;
   }
@@ -1166,7 +1167,7 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     const float* wo = reinterpret_cast<const float*>(p->workspace);
     const float* wm = wo + (int64_t)p->n_slots * dec::kRows * dec::kL;
     const float* wl = wm + (int64_t)p->n_slots * dec::kRows;
-    dec::combine_kernel<<<dim3(p->n_combine, dec::kL / dec::kCombDims), 256, 0, s>>>(
+    dec::combine_kernel<<<dim3(p->n_combine, dec::kL / dec::kCombDims), dec::kCombThreads, 0, s>>>(
         wo, wm, wl, p->combine, p->n_slots, dec::kL, p->out, p->out_dtype);
     st = check_launch("splitkv_combine");
   }
@@ -1188,7 +1189,7 @@ extern "C" int asterq_splitkv_combine(const float* partials, int32_t n_slots, co
     return set_error(ASTERQ_ERR_MISALIGNED, "combine: pointers must be 16-byte aligned");
   const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
   const float* wl = wm + (int64_t)n_slots * dec::kRows;
-  dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), dec::kCombThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, combine, n_slots, latent_dim, out, out_dtype);
   return check_launch("splitkv_combine");
 }
@@ -1205,7 +1206,7 @@ extern "C" int asterq_splitkv_merge(const float* partials, int32_t n_slots, cons
     return set_error(ASTERQ_ERR_MISALIGNED, "merge: pointers must be 16-byte aligned");
   const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
   const float* wl = wm + (int64_t)n_slots * dec::kRows;
-  dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), dec::kCombThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged);
   return check_launch("splitkv_merge");
 }

@@ -449,19 +449,24 @@ def main() -> None:
             "frac": achieved / peak,
             "peak_kind": peak_kind,
             "traffic": traffic,
-            "kernel": "asterq::dec::decode_kernel",
+            "kernel": "asterq::dec::decode_kernel (timed with its query-preparation launch)",
             "algorithmic_bytes_per_launch": alg_bytes,
             "kernel_ms": dec_ms,
             "combine_ms": comb_ms,
         },
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "ms_per_step": e2e_ms},
-        "gpu_launches": args.steps * (2 if n_combine else 1),
+        # per step: query preparation + decode_kernel, then combine_kernel when items were split
+        "gpu_launches": args.steps * (3 if n_combine else 2),
         "clocks": clocks.summary(),
     }
 
     if rank == 0 and world == 1 and not args.no_extras:
         line["extras"] = extras(dev, args)
+    if world > 1 and not args.no_extras:
+        cp = context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier)
+        if rank == 0:
+            line["extras"] = {"c4_context_parallel": cp}
 
     if keep:
         rate, done, toks, dt = cpu_oracle_rate(wl.host, wl.lengths, wl.hot)
@@ -474,6 +479,38 @@ def main() -> None:
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier) -> dict:
+    """C4 (one 131,072-token sequence) split by cold chunk over the ranks, partials gathered over NCCL."""
+    import torch
+
+    from asterq.context_parallel import ContextParallelDecoder
+    from asterq.synth import c4_workload
+
+    wl = c4_workload(dev, seed=4)
+    dec = ContextParallelDecoder(wl.pools, wl.layouts[0], wl.n_heads, rank, world, dev)
+    out = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
+
+    def step():
+        dec.step(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SOFTMAX_SCALE)
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    iters = 20
+    s.record()
+    for _ in range(iters):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = max_over_ranks(s.elapsed_time(e) / iters)
+    alg = wl.algorithmic_bytes()
+    return {"seqs": 1, "cached_tokens": int(wl.lengths[0]), "ranks": world, "ms": ms,
+            "seq_steps_per_s": 1e3 / ms, "GB/s_total": alg / (ms / 1e3) / 1e9,
+            "collective": "one all_gather_into_tensor of 32,896 B per rank per step (NCCL)"}
 
 
 def extras(dev, args) -> dict:
