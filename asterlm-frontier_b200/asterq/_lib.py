@@ -38,6 +38,7 @@ EXPORTED_SYMBOLS = (
     "asterq_quantize",
     "asterq_dequantize",
     "asterq_fwht",
+    "asterq_codec_status",
     "asterq_decode_workspace_bytes",
     "asterq_latent_decode",
     "asterq_latent_decode_noalloc",
@@ -125,6 +126,8 @@ def load() -> ctypes.CDLL:
     lib.asterq_dequantize.argtypes = [vp, vp, i64, ctypes.c_int, ctypes.c_int, ctypes.c_int, vp, ctypes.c_int, i64, vp]
     lib.asterq_fwht.restype = ctypes.c_int
     lib.asterq_fwht.argtypes = [vp, vp, i64, ctypes.c_int, vp]
+    lib.asterq_codec_status.restype = ctypes.c_int
+    lib.asterq_codec_status.argtypes = [ctypes.POINTER(ctypes.c_int32)]
     lib.asterq_decode_workspace_bytes.restype = i64
     lib.asterq_decode_workspace_bytes.argtypes = [ctypes.POINTER(DecodeParams)]
     lib.asterq_latent_decode.restype = ctypes.c_int

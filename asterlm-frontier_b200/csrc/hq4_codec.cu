@@ -265,6 +265,353 @@ __global__ void __launch_bounds__(256) encode_kernel(const void* __restrict__ x,
 }
 
 // ---------------------------------------------------------------------------
+// K1b: encode in the latent cache's own layout -- 512 bf16 values per token,
+// hadamard_int4, groups of 16/32/64, 16-byte aligned rows.
+//
+// Each warp streams tiles of 4 tokens through a private 3-stage shared-memory
+// ring filled by cp.async.bulk (one 1 KB copy per token row, completion on an
+// mbarrier), so two further tiles are in flight while one is transformed; 16
+// warps per SM.  Eight lanes own a token.  Lane l starts with elements
+// 64 l + [0, 64) as eight blocks of 8; block k sits at register position
+// p = k ^ l.  With that placement every butterfly partner is at a register
+// position that does not depend on the lane:
+//   bits 0-2  inside a block;
+//   bits 3-5  positions p and p ^ 1 (p ^ 2, p ^ 4); the lane's bit says which of
+//             the two holds the lower element, applied as a +-1 factor of an
+//             FMA, which rounds exactly like the reference's add or subtract;
+//   exchange  position p moves to lane l ^ p (seven xor shuffles, no selects);
+//   bits 6-8  as bits 3-5, on the exchanged blocks.
+// Afterwards lane l holds elements 64 b + 8 l + [0, 8) at position b ^ l.  A
+// group's absmax is reduced by recursive halving (7 shuffles for groups of 64),
+// which leaves each lane owning whole groups; the owner computes the scale once
+// and the other lanes fetch it.  The XOR placement also spreads the shared-memory
+// reads of a warp over all banks.
+//
+// Divisions.  RN(y / c) for c = float32(sqrt(512)) is RN(y*ch + RN(y*cl)) with
+// ch = RN(1/c), cl = RN(1/c - ch) (Brisebarre and Muller, "Correctly rounded
+// multiplication by arbitrary precision constants", IEEE Trans. Computers 57(2),
+// 2008); tests/div_check.c checks it over every significand.  Division by the
+// group scale (and of the absmax by 7) keeps Markstein's correction step.  Both
+// are exact for 2^-98 <= |y| <= 2^120; below that range the code is 0 either way,
+// and a tile holding a group whose absmax is above 2^119 (or not finite) takes
+// IEEE divisions throughout.
+// ---------------------------------------------------------------------------
+namespace lat512 {
+constexpr int kWarps = 16;
+constexpr int kThreads = kWarps * 32;
+constexpr int kStages = 3;
+constexpr int kTok = 4;                        // tokens per warp tile
+constexpr int kRowBytes = 1024;                // one bf16 token row
+constexpr int kPitch = 1040;                   // shared row pitch (16-byte multiple)
+constexpr int kStageBytes = kTok * kPitch;     // 4,160
+constexpr int kWarpBytes = kStages * kStageBytes;
+constexpr int kBarOff = kWarps * kWarpBytes;   // 199,680
+constexpr int kSmem = kBarOff + kWarps * kStages * 8 + 16;
+constexpr float kC = 0x1.6a09e6p+4f;           // float32(sqrt(512))
+constexpr float kCh = 0x1.6a09e6p-5f;          // RN(1 / kC)
+constexpr float kCl = 0x1.9fcef4p-30f;         // RN(1 / kC - kCh)
+constexpr float kR7 = 0x1.24924ap-3f;          // RN(1 / 7)
+}  // namespace lat512
+
+__device__ int g_codec_timeouts;  // encode waits that gave up (read by asterq_codec_status)
+
+ASTERQ_DEVICE uint4 lds128(uint32_t addr) {
+  uint4 r;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];" : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w) : "r"(addr) : "memory");
+  return r;
+}
+
+// (a, b) -> (a + b, a - b) for two neighbouring pairs at once
+ASTERQ_DEVICE void bfly_pair(float& a0, float& a1, float& b0, float& b1) {
+  const float2 A = make_float2(a0, a1), B = make_float2(b0, b1);
+  const float2 s = add2(A, B), d = sub2(A, B);
+  a0 = s.x; a1 = s.y; b0 = d.x; b1 = d.y;
+}
+
+// Butterflies on element-index bit log2(H) (H = 2, 4), inside every block of 8.
+template <int H>
+ASTERQ_DEVICE void block_stage(float (&x)[64]) {
+#pragma unroll
+  for (int base = 0; base < 64; base += 2 * H) {
+#pragma unroll
+    for (int j = 0; j < H; j += 2) bfly_pair(x[base + j], x[base + j + 1], x[base + j + H], x[base + j + H + 1]);
+  }
+}
+
+// Butterflies between register positions p and p ^ M (blocks of 8).  sg = +1 when
+// the position with bit M clear holds the lower element of every pair, -1 when it
+// holds the upper one: A' = sg*A + B and B' = A - sg*B are then lower + upper at
+// the lower element's position and lower - upper at the upper one's, one rounding each.
+template <int M>
+ASTERQ_DEVICE void pos_stage(float (&x)[64], float sg) {
+  const float2 s2 = make_float2(sg, sg), n2 = make_float2(-sg, -sg);
+#pragma unroll
+  for (int p = 0; p < 8; ++p) {
+    if (p & M) continue;
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+      float& a0 = x[p * 8 + i];
+      float& a1 = x[p * 8 + i + 1];
+      float& b0 = x[(p ^ M) * 8 + i];
+      float& b1 = x[(p ^ M) * 8 + i + 1];
+      const float2 A = make_float2(a0, a1), B = make_float2(b0, b1);
+      const float2 nA = fma2(s2, A, B), nB = fma2(n2, B, A);
+      a0 = nA.x; a1 = nA.y; b0 = nB.x; b1 = nB.y;
+    }
+  }
+}
+
+constexpr float kMagic = 12582920.0f;  // 1.5 * 2^23 + 8: rounds to an integer, ties to even, plus the int4 offset
+constexpr float kTieGuard = 0.5f - 0x1p-16f;
+
+// One byte from the low nibbles of t0 (even element) and t1 (odd element):
+// t0 + 16 * t1, whose low byte is u0 | u1 << 4 (kv.py:47-48) as both low bytes
+// hold q + 8 in [1, 15].
+ASTERQ_DEVICE uint32_t pack_pair(float t0, float t1) {
+  uint32_t r;
+  asm("mad.lo.u32 %0, %1, 16, %2;" : "=r"(r) : "r"(__float_as_uint(t1)), "r"(__float_as_uint(t0)));
+  return r;
+}
+ASTERQ_DEVICE uint32_t pack_word(const uint32_t (&by)[4]) {
+  return prmt(prmt(by[0], by[1], 0x0040u), prmt(by[2], by[3], 0x0040u), 0x5410u);
+}
+
+// Codes of one block of 8 elements exactly as the reference rounds them,
+// rint(RN(RN(y / c) / sc)), packed into one word.  rs = RN(1 / sc).
+template <bool IEEE>
+ASTERQ_DEVICE uint32_t quantize8(const float* y, float sc, float rs) {
+  uint32_t by[4];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    float t0, t1;
+    if (IEEE) {
+      t0 = __fadd_rn(__fdiv_rn(__fdiv_rn(y[i], lat512::kC), sc), kMagic);
+      t1 = __fadd_rn(__fdiv_rn(__fdiv_rn(y[i + 1], lat512::kC), sc), kMagic);
+    } else {
+      const float2 Y = make_float2(y[i], y[i + 1]);
+      const float2 vq = fma2(Y, make_float2(lat512::kCh, lat512::kCh), mul2(Y, make_float2(lat512::kCl, lat512::kCl)));
+      const float2 r2 = make_float2(rs, rs);
+      const float2 q0 = mul2(vq, r2);
+      const float2 e = fma2(q0, make_float2(-sc, -sc), vq);
+      const float2 q1 = fma2(e, r2, q0);
+      const float2 t = add2(q1, make_float2(kMagic, kMagic));
+      t0 = t.x;
+      t1 = t.y;
+    }
+    by[i / 2] = pack_pair(t0, t1);
+  }
+  return pack_word(by);
+}
+
+// Candidate codes rint(y * k) for k = RN(1 / RN(c * sc)), packed into one word,
+// with max |y*k - rint(y*k)| folded into dmax.  The exact product y*k is within
+// a relative 2^-22 of the reference's RN(RN(y / c) / sc) (|value| <= 7), so where
+// it lies farther than 2^-16 from every half-integer (dmax < kTieGuard) both
+// round to the same integer; otherwise the caller recomputes with quantize8.
+ASTERQ_DEVICE uint32_t quantize8_fast(const float* y, float k, float& dmax) {
+  const float2 k2 = make_float2(k, k), m2 = make_float2(kMagic, kMagic);
+  uint32_t by[4];
+#pragma unroll
+  for (int i = 0; i < 8; i += 2) {
+    const float2 Y = make_float2(y[i], y[i + 1]);
+    const float2 t = fma2(Y, k2, m2);   // kMagic + rint(y*k), one rounding of the exact y*k + kMagic
+    const float2 nq = sub2(m2, t);      // -rint(y*k), exact
+    const float2 d = fma2(Y, k2, nq);   // y*k - rint(y*k)
+    dmax = fmaxf(dmax, fmaxf(fabsf(d.x), fabsf(d.y)));
+    by[i / 2] = pack_pair(t.x, t.y);
+  }
+  return pack_word(by);
+}
+
+// Scale of one group from the absmax of its (unnormalized) transform outputs:
+// RN(max(RN(amax / c), 1e-8) / 7) (kv.py:104-106).
+template <bool IEEE>
+ASTERQ_DEVICE float group_scale(float amax) {
+  if (IEEE) return __fdiv_rn(fmaxf(__fdiv_rn(amax, lat512::kC), 1e-8f), 7.0f);
+  const float av = fmaf(amax, lat512::kCh, __fmul_rn(amax, lat512::kCl));
+  const float m = fmaxf(av, 1e-8f);
+  const float q0 = __fmul_rn(m, lat512::kR7);
+  return fmaf(fmaf(-q0, 7.0f, m), lat512::kR7, q0);
+}
+
+ASTERQ_DEVICE void mbar_drain(uint32_t bar, uint32_t parity) {
+  const long long t0 = clock64();
+  while (!mbar_try(bar, parity) && clock64() - t0 < 4000000000LL) {
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(lat512::kThreads, 1)
+    encode_lat512_kernel(const uint16_t* __restrict__ x, int64_t n_tokens, int64_t x_stride,
+                         uint8_t* __restrict__ codes, __half* __restrict__ scales) {
+  using namespace lat512;
+  constexpr int LPG = G / 8;       // lanes sharing a group
+  constexpr int OWN = 8 / LPG;     // groups owned per lane after the reduction
+  constexpr int GPT = 512 / G;     // groups per token
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = lane >> 3, l = lane & 7;
+  const uint32_t ring = smem_u32(smem) + warp * kWarpBytes;
+  const uint32_t bar0 = smem_u32(smem + kBarOff) + warp * kStages * 8;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + kBarOff + kWarps * kStages * 8);
+  if (lane == 0) {
+#pragma unroll
+    for (int s = 0; s < kStages; ++s) mbar_init(bar0 + 8 * s, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (threadIdx.x == 0) *abort_flag = 0;
+  __syncthreads();
+
+  const int64_t n_tiles = (n_tokens + kTok - 1) / kTok;
+  const int64_t first = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t step = (int64_t)gridDim.x * kWarps;
+  auto issue = [&](int64_t tile, int s) {
+    const int64_t tok0 = tile * kTok;
+    const int nv = (int)((n_tokens - tok0) < kTok ? (n_tokens - tok0) : kTok);
+    if (lane == 0) mbar_expect_tx(bar0 + 8 * s, (uint32_t)(nv * kRowBytes));
+    __syncwarp();
+    if (lane < nv) bulk_1d(ring + s * kStageBytes + lane * kPitch, x + (tok0 + lane) * x_stride, kRowBytes, bar0 + 8 * s);
+  };
+#pragma unroll
+  for (int s = 0; s < kStages; ++s)
+    if (first + s * step < n_tiles) issue(first + s * step, s);
+
+  // Long launches: start the four warps of each scheduler a microsecond apart so
+  // their FMA-heavy and ALU-heavy phases overlap instead of coinciding.
+  if (n_tiles >= 8 * step) __nanosleep(1000u * (unsigned)(warp >> 2));
+  const float sg0 = (l & 1) ? -1.0f : 1.0f;
+  const float sg1 = (l & 2) ? -1.0f : 1.0f;
+  const float sg2 = (l & 4) ? -1.0f : 1.0f;
+  int64_t it = 0;
+  for (;; ++it) {
+    const int64_t tile = first + it * step;
+    if (tile >= n_tiles) break;
+    const int s = (int)(it % kStages);
+    const uint32_t parity = (uint32_t)((it / kStages) & 1);
+    if (!mbar_wait(bar0 + 8 * s, parity, abort_flag)) break;
+    const int64_t tok = tile * kTok + t;
+    const bool valid = tok < n_tokens;
+
+    // load with butterfly stage h = 1 (element pairs 2m, 2m + 1 are one bf16x2 word)
+    float v[64];
+    {
+      const uint32_t row = ring + s * kStageBytes + t * kPitch + 128 * l;
+      uint4 w[8];
+#pragma unroll
+      for (int p = 0; p < 8; ++p) w[p] = lds128(row + 16 * (p ^ l));
+#pragma unroll
+      for (int p = 0; p < 8; ++p) {
+        const uint32_t ws[4] = {w[p].x, w[p].y, w[p].z, w[p].w};
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          // lo + hi and lo - hi with lo read as bf16 straight from the word's low half
+          // (bf16 -> f32 is exact, so each is the reference's single f32 rounding)
+          const float hi = bf16hi_to_f32(ws[m]);
+          const unsigned short lo = (unsigned short)(ws[m] & 0xffffu);
+          float s0, s1;
+          asm("add.rn.f32.bf16 %0, %1, %2;" : "=f"(s0) : "h"(lo), "f"(hi));
+          asm("sub.rn.f32.bf16 %0, %1, %2;" : "=f"(s1) : "h"(lo), "f"(hi));
+          v[p * 8 + 2 * m] = s0;
+          v[p * 8 + 2 * m + 1] = s1;
+        }
+      }
+    }
+    // every lane's copy of the stage is in registers: refill it with the tile kStages ahead
+    __syncwarp();
+    fence_async_shared();
+    if (tile + kStages * step < n_tiles) issue(tile + kStages * step, s);
+
+    block_stage<2>(v);
+    block_stage<4>(v);
+    pos_stage<1>(v, sg0);
+    pos_stage<2>(v, sg1);
+    pos_stage<4>(v, sg2);
+#pragma unroll
+    for (int p = 1; p < 8; ++p) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[p * 8 + i] = __shfl_xor_sync(0xffffffffu, v[p * 8 + i], p);
+    }
+    pos_stage<1>(v, sg0);
+    pos_stage<2>(v, sg1);
+    pos_stage<4>(v, sg2);
+
+    // absmax of each block, then recursive halving over the LPG lanes of a group:
+    // lane l ^ m keeps the same block at position q ^ m, so after the round for m
+    // the positions with bit m clear hold the maximum over both lanes
+    float am[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      float a = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a = fmaxf(a, fabsf(v[q * 8 + i]));
+      am[q] = a;
+    }
+#pragma unroll
+    for (int m = LPG / 2; m >= 1; m /= 2) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        if ((q & (LPG - 1)) >= m) continue;  // still active and bit m clear
+        am[q] = fmaxf(am[q], __shfl_xor_sync(0xffffffffu, am[q ^ m], m));
+      }
+    }
+    // this lane owns the groups at positions q with q & (LPG - 1) == 0
+    bool big = false;
+#pragma unroll
+    for (int o = 0; o < OWN; ++o) big |= !(am[o * LPG] <= 0x1p119f);
+    big = big && valid;
+    const bool ieee = __any_sync(0xffffffffu, big);
+    float osc[OWN];
+#pragma unroll
+    for (int o = 0; o < OWN; ++o) osc[o] = ieee ? group_scale<true>(am[o * LPG]) : group_scale<false>(am[o * LPG]);
+    // position q's group is owned by lane l ^ (q & (LPG - 1)) at its position q & ~(LPG - 1)
+    auto fetch = [&](const float (&own)[OWN], int q) {
+      const int m = q & (LPG - 1);
+      return m ? __shfl_xor_sync(0xffffffffu, own[q / LPG], m) : own[q / LPG];
+    };
+    uint32_t cw[8];
+    if (!ieee) {
+      float ok[OWN];
+#pragma unroll
+      for (int o = 0; o < OWN; ++o) ok[o] = __frcp_rn(__fmul_rn(kC, osc[o]));
+      float dmax = 0.0f;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cw[q] = quantize8_fast(v + q * 8, fetch(ok, q), dmax);
+      if (__any_sync(0xffffffffu, valid && !(dmax < kTieGuard))) {
+        // a value within 2^-16 of a half-integer somewhere in the tile: redo the tile exactly
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const float sc = fetch(osc, q);
+          cw[q] = quantize8<false>(v + q * 8, sc, __frcp_rn(sc));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cw[q] = quantize8<true>(v + q * 8, fetch(osc, q), 0.0f);
+    }
+    if (valid) {
+      // block b = q ^ l holds elements 64 b + 8 l + [0, 8): code bytes 32 b + 4 l
+      uint8_t* crow = codes + tok * 256 + 4 * l;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) *reinterpret_cast<uint32_t*>(crow + 32 * (q ^ l)) = cw[q];
+#pragma unroll
+      for (int o = 0; o < OWN; ++o) {
+        const int g = (64 * ((o * LPG) ^ l) + 8 * l) / G;
+        scales[tok * GPT + g] = __float2half_rn(osc[o]);
+      }
+    }
+  }
+  if (*abort_flag) {
+    // a copy never completed: record it and wait (bounded) for this warp's copies still in flight
+    if (lane == 0) atomicAdd(&g_codec_timeouts, 1);
+    for (int64_t k = it; k < it + kStages; ++k) {
+      const int64_t tile = first + k * step;
+      if (tile >= n_tiles) break;
+      mbar_drain(bar0 + 8 * (int)(k % kStages), (uint32_t)((k / kStages) & 1));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Dequantize (kv.py:121-134): restored = codes * float(scale), inverse FWHT,
 // crop, cast.  Bit-exact for hadamard_int4 / int4 / int8.
 // ---------------------------------------------------------------------------
@@ -461,6 +808,26 @@ int launch_encode_d(int D, int G, const void* x, int x_dtype, int64_t n, int dim
   }
 }
 
+template <int G>
+int launch_encode_lat512(const void* x, int64_t n, int64_t stride, uint8_t* codes, __half* scales, cudaStream_t st) {
+  static int attr_set[64];  // per device: the kernel's dynamic shared memory limit is raised once
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  if (dev >= 64 || !attr_set[dev]) {
+    const cudaError_t e = cudaFuncSetAttribute(encode_lat512_kernel<G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               lat512::kSmem);
+    if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "encode: %s", cudaGetErrorString(e));
+    if (dev < 64) attr_set[dev] = 1;
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t tiles = (n + lat512::kTok - 1) / lat512::kTok;
+  int64_t blocks = (tiles + lat512::kWarps - 1) / lat512::kWarps;
+  if (blocks > sms) blocks = sms;
+  encode_lat512_kernel<G><<<(int)blocks, lat512::kThreads, lat512::kSmem, st>>>(
+      reinterpret_cast<const uint16_t*>(x), n, stride, codes, scales);
+  return check_launch("encode");
+}
+
 template <int D, int G, bool ROT, int QMAX>
 int launch_decode_one(const uint8_t* codes, const __half* scales, int64_t n, int dim_code, int dim_out, void* out,
                       int out_dtype, int64_t out_stride, cudaStream_t st) {
@@ -542,6 +909,15 @@ extern "C" int asterq_quantize(const void* x, int x_dtype, int64_t n_tokens, int
     if (padded % group_size) return set_error(ASTERQ_ERR_UNSUPPORTED, "quantize: group %d does not divide %d", group_size, padded);
     if ((reinterpret_cast<uintptr_t>(codes) & 15) || (reinterpret_cast<uintptr_t>(scales) & 1))
       return set_error(ASTERQ_ERR_MISALIGNED, "quantize: codes must be 16-byte aligned");
+    // the cache's own rows (512 bf16 values, 16-byte aligned) take the TMA-fed kernel
+    if (dim == 512 && x_dtype == ASTERQ_DTYPE_BF16 && !(reinterpret_cast<uintptr_t>(x) & 15) && x_row_stride % 8 == 0 &&
+        !(reinterpret_cast<uintptr_t>(scales) & 15)) {
+      uint8_t* c8 = reinterpret_cast<uint8_t*>(codes);
+      __half* sh = reinterpret_cast<__half*>(scales);
+      if (group_size == 64) return launch_encode_lat512<64>(x, n_tokens, x_row_stride, c8, sh, st);
+      if (group_size == 32) return launch_encode_lat512<32>(x, n_tokens, x_row_stride, c8, sh, st);
+      if (group_size == 16) return launch_encode_lat512<16>(x, n_tokens, x_row_stride, c8, sh, st);
+    }
     return launch_encode_d<true, 7>(padded, group_size, x, x_dtype, n_tokens, dim, x_row_stride, padded,
                                     reinterpret_cast<uint8_t*>(codes), reinterpret_cast<__half*>(scales), st);
   }
@@ -621,4 +997,14 @@ extern "C" int asterq_fwht(const float* x, float* y, int64_t rows, int n, void* 
     default:
       return set_error(ASTERQ_ERR_UNSUPPORTED, "fwht: length %d unsupported (2..512)", n);
   }
+}
+
+extern "C" int asterq_codec_status(int32_t* timeouts) {
+  clear_error();
+  if (!timeouts) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "codec_status: null pointer");
+  int v = 0;
+  const cudaError_t e = cudaMemcpyFromSymbol(&v, g_codec_timeouts, sizeof(int));
+  if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "codec_status: %s", cudaGetErrorString(e));
+  *timeouts = v;
+  return ASTERQ_OK;
 }

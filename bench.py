@@ -300,9 +300,18 @@ def main() -> None:
     ap.add_argument("--impl", default="asterq", choices=["asterq", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--write-path-only", action="store_true",
+                    help="time only the config-2 encode (3 + --steps launches per entry point) and print it")
     args = ap.parse_args()
     if args.impl == "reference":
         run_reference_arm(args)
+        return
+    if args.write_path_only:
+        import torch
+
+        torch.cuda.set_device(0)
+        print(json.dumps({"c2_write_path": write_path_rate(torch.device("cuda", 0), measured_peaks()[0],
+                                                            iters=args.steps)}), flush=True)
         return
 
     import torch
@@ -513,39 +522,62 @@ def context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier) -> d
             "collective": "one all_gather_into_tensor of 32,896 B per rank per step (NCCL)"}
 
 
-def extras(dev, args) -> dict:
-    """Secondary single-GPU measurements: the write path (config 2) and configs 1, 4, 5."""
+def timed_ms(fn, iters: int) -> float:
+    """Average device time of `fn` over `iters` calls after 3 warm-up calls (CUDA events, current stream)."""
     import torch
 
-    from asterq.decode import DeviceDecodePlan, latent_decode
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def write_path_rate(dev, peak: float, iters: int = 20) -> dict:
+    """Config 2: encode 64 x 4096 bf16 latent rows (hadamard_int4, groups of 64)."""
+    import torch
+
+    from asterq import _lib
     from asterq.kv import quantize_tensor
-    from asterq.plan import build_plan
-    from asterq.synth import c1_inputs, c4_workload, c5_workload, PoolBuilder, outlier_channels
-
-    peak, _ = measured_peaks()
-    res = {}
-
-    def timed(fn, iters):
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        s.record()
-        for _ in range(iters):
-            fn()
-        e.record()
-        torch.cuda.synchronize()
-        return s.elapsed_time(e) / iters
+    from asterq.synth import outlier_channels
 
     g = torch.Generator(device=dev).manual_seed(2)
     x = torch.randn(64 * 4096, 512, generator=g, device=dev)
     x[:, outlier_channels(2).to(dev)] *= 20
     x = x.to(torch.bfloat16)
-    ms = timed(lambda: quantize_tensor(x, "hadamard_int4", group_size=64), 20)
+    ms_api = timed_ms(lambda: quantize_tensor(x, "hadamard_int4", group_size=64), iters)
+    # the kernel alone: the C entry point into preallocated codes and scales
+    lib = _lib.load()
+    codes = torch.empty(64 * 4096, 256, dtype=torch.uint8, device=dev)
+    scales = torch.empty(64 * 4096, 8, dtype=torch.float16, device=dev)
+    stream = _lib.stream_handle(dev)
+    ms = timed_ms(lambda: lib.asterq_quantize(x.data_ptr(), _lib.DTYPE_BF16, 64 * 4096, 512, 512,
+                                              _lib.SCHEME_HADAMARD_INT4, 64, codes.data_ptr(), scales.data_ptr(),
+                                              stream), iters)
     b = 64 * 4096 * (1024 + 256 + 16)
-    res["c2_write_path"] = {"tokens": 64 * 4096, "ms": ms, "tokens_per_s": 64 * 4096 / ms * 1e3,
-                            "GB/s": b / ms / 1e6, "frac_hbm": b / ms / 1e6 / peak}
-    del x
+    res = {"tokens": 64 * 4096, "ms": ms, "ms_quantize_tensor": ms_api, "tokens_per_s": 64 * 4096 / ms * 1e3,
+           "GB/s": b / ms / 1e6, "frac_hbm": b / ms / 1e6 / peak}
+    del codes, scales, x
+    return res
+
+
+def extras(dev, args) -> dict:
+    """Secondary single-GPU measurements: the write path (config 2) and configs 1, 4, 5."""
+    import torch
+
+    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.plan import build_plan
+    from asterq.synth import c1_inputs, c4_workload, c5_workload, PoolBuilder
+
+    peak, _ = measured_peaks()
+    res = {}
+    timed = timed_ms
+    res["c2_write_path"] = write_path_rate(dev, peak)
 
     def decode_rate(wl, name, iters):
         plan = build_plan(wl.layouts, wl.n_heads)

@@ -81,6 +81,14 @@ int asterq_dequantize(const void* codes, const void* scales, int64_t n_tokens, i
 int asterq_fwht(const float* x, float* y, int64_t rows, int n, void* stream);
 
 /*
+ * Health of the write path: *timeouts = how many encode warps gave up waiting
+ * for a bulk copy of their input rows (each such wait is bounded at about two
+ * seconds, after which the warp stops, so its rows' codes are not written).
+ * Synchronizes the current device.  0 in normal operation.
+ */
+int asterq_codec_status(int32_t* timeouts);
+
+/*
  * Decode attention over a paged hybrid latent cache.
  *
  * Layout in device memory (all row-major, token-major):

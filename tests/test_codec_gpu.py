@@ -99,6 +99,82 @@ def test_encode_strided_rows_and_batch_dims(cuda):
     np.testing.assert_array_equal(_codes_np(q), ref.data)
 
 
+@pytest.mark.parametrize("n", [1, 7, 9, 63, 65, 8 * 8 * 3 + 5])
+def test_encode_extreme_magnitudes_and_ragged_tiles(cuda, n):
+    """512-value rows in every magnitude regime of the division shortcuts, in
+    tiles of 8 tokens with a ragged last tile: zero rows, absmax far below 2^-98
+    (codes 0 whatever the quotient), rows whose transform absmax exceeds 2^119
+    (the tile switches to IEEE divisions), half-zero rows and constant rows."""
+    from asterq.kv import quantize_tensor
+
+    g = torch.Generator(device=cuda).manual_seed(17 + n)
+    x = torch.randn(max(n, 12), 512, generator=g, device=cuda)
+    x[0] = 0.0
+    x[1] *= 1e-30
+    x[2] *= 1e-36
+    x[3] *= 1e35
+    x[4, :64] *= 1e34
+    x[5, ::2] = 0.0
+    x[6] = 1.0
+    x[7] = -3.0
+    x[8, 7] = 2.0**60
+    x = x[:n].to(torch.bfloat16)
+    for group in (64, 32, 16):
+        q = quantize_tensor(x, "hadamard_int4", group_size=group)
+        ref = O.quantize(x.float().cpu().numpy(), "hadamard_int4", group)
+        np.testing.assert_array_equal(_codes_np(q), ref.data)
+        np.testing.assert_array_equal(_scales_bits(q), ref.scale.view(np.uint16))
+
+
+def test_encode_near_ties_take_the_exact_path(cuda):
+    """Rows whose normalized transform holds values at (or within rounding of)
+    k + 1/2 scale steps: x = a e_0 + b e_1 transforms to (a + b) / c and
+    (a - b) / c, and (a - b) / (a + b) = (2k + 1) / 14 puts the smaller one at
+    code k + 1/2.  The candidate-and-check rounding must hand these tiles to the
+    exact double division."""
+    from asterq.kv import quantize_tensor
+
+    g = torch.Generator(device=cuda).manual_seed(29)
+    x = torch.randn(37, 512, generator=g, device=cuda)
+    for k in range(7):
+        a, b = (14 + 2 * k + 1) / 2, (14 - 2 * k - 1) / 2
+        for r, sign in ((2 * k, 1.0), (2 * k + 1, -1.0)):
+            x[r] = 0.0
+            x[r, 0], x[r, 1] = sign * a, b
+    x = x.to(torch.bfloat16)
+    for group in (64, 32, 16):
+        q = quantize_tensor(x, "hadamard_int4", group_size=group)
+        ref = O.quantize(x.float().cpu().numpy(), "hadamard_int4", group)
+        np.testing.assert_array_equal(_codes_np(q), ref.data)
+        np.testing.assert_array_equal(_scales_bits(q), ref.scale.view(np.uint16))
+
+
+def test_encode_unaligned_rows_take_the_generic_kernel(cuda):
+    """A row base that is not 16-byte aligned cannot feed the bulk copies; the
+    generic kernel handles it with the same codes."""
+    from asterq.kv import quantize_tensor
+
+    g = torch.Generator(device=cuda).manual_seed(23)
+    flat = torch.randn(300 * 512 + 1, generator=g, device=cuda).to(torch.bfloat16)
+    x = flat[1:].view(300, 512)
+    q = quantize_tensor(x, "hadamard_int4", group_size=64)
+    ref = O.quantize(x.float().cpu().numpy(), "hadamard_int4", 64)
+    np.testing.assert_array_equal(_codes_np(q), ref.data)
+    np.testing.assert_array_equal(_scales_bits(q), ref.scale.view(np.uint16))
+
+
+def test_codec_status_reports_no_timeouts(cuda):
+    import ctypes
+
+    from asterq import _lib
+    from asterq.kv import quantize_tensor
+
+    quantize_tensor(torch.ones(100, 512, dtype=torch.bfloat16, device=cuda), "hadamard_int4")
+    v = ctypes.c_int32(-1)
+    assert _lib.load().asterq_codec_status(ctypes.byref(v)) == 0
+    assert v.value == 0
+
+
 def test_encode_c2_full_size_properties(cuda):
     """Config 2 at full size (64 x 4096 tokens): determinism, round-trip error,
     and a bit-exact comparison of a strided sample of rows with the oracle."""
