@@ -276,16 +276,16 @@ __global__ void __launch_bounds__(256) encode_kernel(const void* __restrict__ x,
 // p = k ^ l.  With that placement every butterfly partner is at a register
 // position that does not depend on the lane:
 //   bits 0-2  inside a block;
-//   bits 3-5  positions p and p ^ 1 (p ^ 2, p ^ 4); the lane's bit says which of
-//             the two holds the lower element, applied as a +-1 factor of an
-//             FMA, which rounds exactly like the reference's add or subtract;
+//   bits 3-5  positions p and p ^ 1 (p ^ 2, p ^ 4); which of the two holds the
+//             lower element depends on the lane, absorbed by a per-position
+//             storage sign (pos_stage);
 //   exchange  position p moves to lane l ^ p (seven xor shuffles, no selects);
 //   bits 6-8  as bits 3-5, on the exchanged blocks.
 // Afterwards lane l holds elements 64 b + 8 l + [0, 8) at position b ^ l.  A
 // group's absmax is reduced by recursive halving (7 shuffles for groups of 64),
 // which leaves each lane owning whole groups; the owner computes the scale once
-// and the other lanes fetch it.  The XOR placement also spreads the shared-memory
-// reads of a warp over all banks.
+// and the other lanes fetch it.  The XOR placement also spreads each 16-byte
+// shared-memory read of a warp evenly over the banks (4 wavefronts per 512 bytes).
 //
 // Divisions.  RN(y / c) for c = float32(sqrt(512)) is RN(y*ch + RN(y*cl)) with
 // ch = RN(1/c), cl = RN(1/c - ch) (Brisebarre and Muller, "Correctly rounded
@@ -302,10 +302,9 @@ constexpr int kThreads = kWarps * 32;
 constexpr int kStages = 3;
 constexpr int kTok = 4;                        // tokens per warp tile
 constexpr int kRowBytes = 1024;                // one bf16 token row
-constexpr int kPitch = 1040;                   // shared row pitch (16-byte multiple)
-constexpr int kStageBytes = kTok * kPitch;     // 4,160
+constexpr int kStageBytes = kTok * kRowBytes;  // 4 KB: rows back to back
 constexpr int kWarpBytes = kStages * kStageBytes;
-constexpr int kBarOff = kWarps * kWarpBytes;   // 199,680
+constexpr int kBarOff = kWarps * kWarpBytes;   // 196,608
 constexpr int kSmem = kBarOff + kWarps * kStages * 8 + 16;
 constexpr float kC = 0x1.6a09e6p+4f;           // float32(sqrt(512))
 constexpr float kCh = 0x1.6a09e6p-5f;          // RN(1 / kC)
@@ -338,25 +337,25 @@ ASTERQ_DEVICE void block_stage(float (&x)[64]) {
   }
 }
 
-// Butterflies between register positions p and p ^ M (blocks of 8).  sg = +1 when
-// the position with bit M clear holds the lower element of every pair, -1 when it
-// holds the upper one: A' = sg*A + B and B' = A - sg*B are then lower + upper at
-// the lower element's position and lower - upper at the upper one's, one rounding each.
+// Butterflies between register positions p and p ^ M (blocks of 8), the same
+// add and subtract in every lane.  Which of the two positions holds the lower
+// element depends on the lane; that is absorbed by storing position p negated
+// when parity(p & l) is odd.  With A = s a and B = s b (p holds the lower a),
+// A + B = s (a + b) and A - B = s (a - b); with A = -s b and B = s a (p holds the
+// upper b), A + B = s (a - b) and A - B = -s (a + b): each output is the
+// reference's single rounding, up to a sign.  The upper case flips every sign of
+// the lane at once, which keeps the parity pattern; the exchange between phases
+// preserves it too (received position q carries parity(q & ~l) + popcount(l ^ q),
+// which equals parity(q & l) + popcount(l) mod 2), so after all six stages
+// position q holds (-1)^parity(q & l) times the true outputs.
 template <int M>
-ASTERQ_DEVICE void pos_stage(float (&x)[64], float sg) {
-  const float2 s2 = make_float2(sg, sg), n2 = make_float2(-sg, -sg);
+ASTERQ_DEVICE void pos_stage(float (&x)[64]) {
 #pragma unroll
   for (int p = 0; p < 8; ++p) {
     if (p & M) continue;
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
-      float& a0 = x[p * 8 + i];
-      float& a1 = x[p * 8 + i + 1];
-      float& b0 = x[(p ^ M) * 8 + i];
-      float& b1 = x[(p ^ M) * 8 + i + 1];
-      const float2 A = make_float2(a0, a1), B = make_float2(b0, b1);
-      const float2 nA = fma2(s2, A, B), nB = fma2(n2, B, A);
-      a0 = nA.x; a1 = nA.y; b0 = nB.x; b1 = nB.y;
+      bfly_pair(x[p * 8 + i], x[p * 8 + i + 1], x[(p ^ M) * 8 + i], x[(p ^ M) * 8 + i + 1]);
     }
   }
 }
@@ -434,6 +433,10 @@ ASTERQ_DEVICE float group_scale(float amax) {
   return fmaf(fmaf(-q0, 7.0f, m), lat512::kR7, q0);
 }
 
+// f negated where the position's storage sign is negative.  A negated divisor (or
+// factor) undoes the stored negation exactly: RN(-a / -s) = RN(a / s).
+ASTERQ_DEVICE float signed_by(float f, uint32_t negmask) { return __uint_as_float(__float_as_uint(f) ^ (negmask << 16)); }
+
 ASTERQ_DEVICE void mbar_drain(uint32_t bar, uint32_t parity) {
   const long long t0 = clock64();
   while (!mbar_try(bar, parity) && clock64() - t0 < 4000000000LL) {
@@ -470,7 +473,11 @@ __global__ void __launch_bounds__(lat512::kThreads, 1)
     const int nv = (int)((n_tokens - tok0) < kTok ? (n_tokens - tok0) : kTok);
     if (lane == 0) mbar_expect_tx(bar0 + 8 * s, (uint32_t)(nv * kRowBytes));
     __syncwarp();
-    if (lane < nv) bulk_1d(ring + s * kStageBytes + lane * kPitch, x + (tok0 + lane) * x_stride, kRowBytes, bar0 + 8 * s);
+    if (x_stride == 512) {  // contiguous rows: one copy for the tile
+      if (lane == 0) bulk_1d(ring + s * kStageBytes, x + tok0 * 512, (uint32_t)(nv * kRowBytes), bar0 + 8 * s);
+    } else if (lane < nv) {
+      bulk_1d(ring + s * kStageBytes + lane * kRowBytes, x + (tok0 + lane) * x_stride, kRowBytes, bar0 + 8 * s);
+    }
   };
 #pragma unroll
   for (int s = 0; s < kStages; ++s)
@@ -479,9 +486,9 @@ __global__ void __launch_bounds__(lat512::kThreads, 1)
   // Long launches: start the four warps of each scheduler a microsecond apart so
   // their FMA-heavy and ALU-heavy phases overlap instead of coinciding.
   if (n_tiles >= 8 * step) __nanosleep(1000u * (unsigned)(warp >> 2));
-  const float sg0 = (l & 1) ? -1.0f : 1.0f;
-  const float sg1 = (l & 2) ? -1.0f : 1.0f;
-  const float sg2 = (l & 4) ? -1.0f : 1.0f;
+  uint32_t negm[8];  // 0x80008000 where parity(p & l) is odd: position p is stored negated
+#pragma unroll
+  for (int p = 0; p < 8; ++p) negm[p] = (__popc(p & l) & 1) ? 0x80008000u : 0u;
   int64_t it = 0;
   for (;; ++it) {
     const int64_t tile = first + it * step;
@@ -495,7 +502,7 @@ __global__ void __launch_bounds__(lat512::kThreads, 1)
     // load with butterfly stage h = 1 (element pairs 2m, 2m + 1 are one bf16x2 word)
     float v[64];
     {
-      const uint32_t row = ring + s * kStageBytes + t * kPitch + 128 * l;
+      const uint32_t row = ring + s * kStageBytes + t * kRowBytes + 128 * l;
       uint4 w[8];
 #pragma unroll
       for (int p = 0; p < 8; ++p) w[p] = lds128(row + 16 * (p ^ l));
@@ -504,13 +511,14 @@ __global__ void __launch_bounds__(lat512::kThreads, 1)
         const uint32_t ws[4] = {w[p].x, w[p].y, w[p].z, w[p].w};
 #pragma unroll
         for (int m = 0; m < 4; ++m) {
-          // lo + hi and lo - hi with lo read as bf16 straight from the word's low half
-          // (bf16 -> f32 is exact, so each is the reference's single f32 rounding)
-          const float hi = bf16hi_to_f32(ws[m]);
-          const unsigned short lo = (unsigned short)(ws[m] & 0xffffu);
+          // lo + hi and lo - hi (negated for the position's storage sign) with lo read
+          // as bf16 straight from the word's low half: bf16 -> f32 is exact, so each
+          // is the reference's single f32 rounding
+          const uint32_t w2 = ws[m] ^ negm[p];
           float s0, s1;
-          asm("add.rn.f32.bf16 %0, %1, %2;" : "=f"(s0) : "h"(lo), "f"(hi));
-          asm("sub.rn.f32.bf16 %0, %1, %2;" : "=f"(s1) : "h"(lo), "f"(hi));
+          asm("{\n .reg .b16 lo, hi;\n mov.b32 {lo, hi}, %2;\n add.rn.f32.bf16 %0, lo, %3;\n sub.rn.f32.bf16 %1, lo, %3;\n}"
+              : "=f"(s0), "=f"(s1)
+              : "r"(w2), "f"(bf16hi_to_f32(w2)));
           v[p * 8 + 2 * m] = s0;
           v[p * 8 + 2 * m + 1] = s1;
         }
@@ -523,17 +531,17 @@ __global__ void __launch_bounds__(lat512::kThreads, 1)
 
     block_stage<2>(v);
     block_stage<4>(v);
-    pos_stage<1>(v, sg0);
-    pos_stage<2>(v, sg1);
-    pos_stage<4>(v, sg2);
+    pos_stage<1>(v);
+    pos_stage<2>(v);
+    pos_stage<4>(v);
 #pragma unroll
     for (int p = 1; p < 8; ++p) {
 #pragma unroll
       for (int i = 0; i < 8; ++i) v[p * 8 + i] = __shfl_xor_sync(0xffffffffu, v[p * 8 + i], p);
     }
-    pos_stage<1>(v, sg0);
-    pos_stage<2>(v, sg1);
-    pos_stage<4>(v, sg2);
+    pos_stage<1>(v);
+    pos_stage<2>(v);
+    pos_stage<4>(v);
 
     // absmax of each block, then recursive halving over the LPG lanes of a group:
     // lane l ^ m keeps the same block at position q ^ m, so after the round for m
@@ -575,18 +583,18 @@ __global__ void __launch_bounds__(lat512::kThreads, 1)
       for (int o = 0; o < OWN; ++o) ok[o] = __frcp_rn(__fmul_rn(kC, osc[o]));
       float dmax = 0.0f;
 #pragma unroll
-      for (int q = 0; q < 8; ++q) cw[q] = quantize8_fast(v + q * 8, fetch(ok, q), dmax);
+      for (int q = 0; q < 8; ++q) cw[q] = quantize8_fast(v + q * 8, signed_by(fetch(ok, q), negm[q]), dmax);
       if (__any_sync(0xffffffffu, valid && !(dmax < kTieGuard))) {
         // a value within 2^-16 of a half-integer somewhere in the tile: redo the tile exactly
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
-          const float sc = fetch(osc, q);
+          const float sc = signed_by(fetch(osc, q), negm[q]);
           cw[q] = quantize8<false>(v + q * 8, sc, __frcp_rn(sc));
         }
       }
     } else {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) cw[q] = quantize8<true>(v + q * 8, fetch(osc, q), 0.0f);
+      for (int q = 0; q < 8; ++q) cw[q] = quantize8<true>(v + q * 8, signed_by(fetch(osc, q), negm[q]), 0.0f);
     }
     if (valid) {
       // block b = q ^ l holds elements 64 b + 8 l + [0, 8): code bytes 32 b + 4 l
