@@ -210,14 +210,32 @@ ASTERQ_DEVICE uint32_t mbar_try(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok;
 }
+// try_wait that lets the hardware suspend the thread for up to `hint_ns`
+// nanoseconds until the phase completes (it wakes as soon as it does), so a
+// waiting warp takes almost no issue slots from the warps doing the work.
+ASTERQ_DEVICE uint32_t mbar_try_sleep(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok;
+}
+ASTERQ_DEVICE int ld_shared_volatile(const volatile int* p) {
+  int v;
+  asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"((uint32_t)__cvta_generic_to_shared((const void*)p)) : "memory");
+  return v;
+}
 // Bounded wait (about 2 s of SM clock): on timeout raise the CTA abort flag so
 // every other wait returns at once and the kernel drains instead of hanging.
+// `abort_flag` points to shared memory.
 ASTERQ_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
-    if (mbar_try(bar, parity)) return true;
-    if (*abort_flag) return false;
+    if (mbar_try_sleep(bar, parity, 20000u)) return true;
+    if (ld_shared_volatile(abort_flag)) return false;
     if (clock64() - t0 > 4000000000LL) {
       *abort_flag = 1;
       return false;

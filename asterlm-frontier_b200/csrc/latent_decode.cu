@@ -327,7 +327,9 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const asterq_decode
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte aligned base, derived by indexing the __shared__ array so that the
+  // compiler keeps every access through `smem` in the shared state space
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const uint32_t sbase = smem_u32(smem);
   float* misc = reinterpret_cast<float*>(smem + kOffMisc);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kOffBar);
