@@ -204,7 +204,7 @@ ASTERQ_DEVICE void mbar_arrive(uint32_t bar) {
 ASTERQ_DEVICE uint32_t mbar_try(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");

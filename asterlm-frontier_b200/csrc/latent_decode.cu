@@ -137,8 +137,13 @@ struct Tile {
   int kind, page, off, n;
 };
 
-ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) {
-  const int4 t = *reinterpret_cast<const int4*>(p.tiles + 4 * (int64_t)idx);
+ASTERQ_DEVICE int4 fetch_tile(const asterq_decode_params& p, int idx) {
+  return *reinterpret_cast<const int4*>(p.tiles + 4 * (int64_t)idx);
+}
+
+// Descriptor checks, applied when the tile is used: the main loops fetch the raw
+// entry two tiles ahead and check it one tile ahead, so no warp waits on the load.
+ASTERQ_DEVICE Tile check_tile(const asterq_decode_params& p, int4 t) {
   Tile tile{t.x, t.y, t.z, t.w};
   // a malformed entry reads nothing instead of faulting
   bool ok = tile.n > 0 && tile.off >= 0;
@@ -155,6 +160,8 @@ ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) {
   if (!ok) tile.n = 0;
   return tile;
 }
+
+ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) { return check_tile(p, fetch_tile(p, idx)); }
 
 // Normalized FWHT of rows [r0, r0 + nrows) of a [16][512] fp32 buffer, one warp:
 // lane l holds elements 16l..16l+15; stages h < 16 are lane-local, h >= 16 pair
@@ -219,7 +226,7 @@ ASTERQ_DEVICE int qk_token(int warp, int m, int r) {
 constexpr int kPrepThreads = 256;
 constexpr int kPrepSmem = 16 * kL * 4 + 16 * kL * 2 + 16 * kRope * 2 + 4 * kQScalars;
 
-__global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const asterq_decode_params p) {
+__global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_constant__ asterq_decode_params p) {
   extern __shared__ __align__(16) uint8_t prep_smem[];
   float* scratch = reinterpret_cast<float*>(prep_smem);                            // [16][512] fp32
   uint16_t* qraw = reinterpret_cast<uint16_t*>(prep_smem + 16 * kL * 4);           // [16][512] bf16
@@ -325,7 +332,7 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const asterq_decode
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
-    decode_kernel(const asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
+    decode_kernel(const __grid_constant__ asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base, derived by indexing the __shared__ array so that the
   // compiler keeps every access through `smem` in the shared state space
@@ -440,12 +447,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
 
     Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
+    int4 raw_next = (n_t > 1) ? fetch_tile(p, tile_begin + 1) : make_int4(0, 0, 0, 0);
 #pragma unroll 1
     for (int i = 0; i < n_t; ++i) {
       const int s = i % kStages, b = i & 1;
       const Tile t = t_next;
-      // the next tile's descriptor is fetched while this one is processed
-      if (i + 1 < n_t) t_next = load_tile(p, tile_begin + i + 1);
+      // descriptors: tile i + 1 checked (fetched an iteration ago), tile i + 2 fetched
+      if (i + 1 < n_t) t_next = check_tile(p, raw_next);
+      if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
       mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);
       const uint8_t* st = smem + s * kStageBytes;
       const uint32_t sst = sbase + s * kStageBytes;
@@ -751,11 +760,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
 
     Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
+    int4 raw_next = (n_t > 1) ? fetch_tile(p, tile_begin + 1) : make_int4(0, 0, 0, 0);
 #pragma unroll 1
     for (int i = 0; i < n_t; ++i) {
       const int s = i % kStages, b = i & 1;
       const Tile t = t_next;
-      if (i + 1 < n_t) t_next = load_tile(p, tile_begin + i + 1);
+      if (i + 1 < n_t) t_next = check_tile(p, raw_next);
+      if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
       mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
       mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);  // TMA data visible to this warp
       const uint8_t* st = smem + s * kStageBytes;
