@@ -54,10 +54,18 @@ constexpr int kRows = 16;
 constexpr int kColdTile = 128;
 constexpr int kHotTile = 32;
 constexpr int kStages = 3;
-constexpr int kScoreWarps = 4;
+constexpr int kTeamWarps = 4;                  // score warps of one team (one tile at a time)
+constexpr int kScoreWarps = 2 * kTeamWarps;    // two teams take alternate tiles
 constexpr int kValueWarps = 8;
-constexpr int kProducerWarp = 4;  // lane 0 of the first value warp issues the TMA loads
+constexpr int kProducerWarp = kScoreWarps;     // lane 0 of the first value warp issues the TMA loads
 constexpr int kThreads = 32 * (kScoreWarps + kValueWarps);
+// Register split (setmaxnreg; the launch gives every thread 128): score warps hold two
+// groups of int8 accumulators in flight, value warps one 16 x 64 fp32 accumulator.
+constexpr int kScoreRegs = 160;
+constexpr int kValueRegs = 96;
+constexpr int kLaunchRegs = 128;
+static_assert(32 * (kScoreWarps * kScoreRegs + kValueWarps * kValueRegs) <= kThreads * kLaunchRegs,
+              "setmaxnreg split exceeds the launch's register allocation");
 
 // one pipeline stage (offsets in bytes, swizzled regions 1024-aligned)
 constexpr int kCodesLo = 0;        // cold: [128][128 B] codes of dims 0..255, SW128
@@ -76,20 +84,23 @@ constexpr int kPStride = kColdTile + 4;         // p tile row stride (floats)
 constexpr int kPBytes = kRows * kPStride * 4;
 constexpr int kOffP = kOffQr + 2048;            // 2 x p tile [16][132] fp32
 constexpr int kOffST = kOffP + 2 * kPBytes;     // 2 x cold code scales [8 groups][128 tokens] fp16
-constexpr int kOffMisc = kOffST + 2 * 2048;     // 512 floats of per-row scalars
-constexpr int kOffBar = kOffMisc + 2048;        // mbarriers
+constexpr int kOffMisc = kOffST + 2 * 2048;     // 1024 floats of per-row scalars
+constexpr int kOffBar = kOffMisc + 4096;        // mbarriers
 constexpr int kSmemBytes = kOffBar + 128 + 1024;  // + alignment slack
+static_assert(kSmemBytes <= 232448, "dynamic shared memory per block");
 
 // misc (float index)
 constexpr int kMAlpha = 0;     // [2][16]
-constexpr int kMWmax = 32;     // [2][4][16]; after the tile loop [16] = final running max
-constexpr int kMLw = 160;      // [4][16]
-constexpr int kMQscale = 224;  // [16]
-constexpr int kMQinv = 240;    // [16]  (score multiplier 2^-e * softmax_scale)
-constexpr int kMQint = 256;    // [16]  fixed-point query scale (32511 / max |rotated row|)
-constexpr int kMQinvI = 272;   // [16]  cold integer-score multiplier softmax_scale / (16 * kMQint)
-constexpr int kMRopeR = 288;   // [16]  RoPE score -> integer-score units (kMQinv / kMQinvI)
+constexpr int kMQscale = 32;   // [16]
+constexpr int kMQinv = 48;     // [16]  (score multiplier 2^-e * softmax_scale)
+constexpr int kMQint = 64;     // [16]  fixed-point query scale (32511 / max |rotated row|)
+constexpr int kMQinvI = 80;    // [16]  cold integer-score multiplier softmax_scale / (16 * kMQint)
+constexpr int kMRopeR = 96;    // [16]  RoPE score -> integer-score units (kMQinv / kMQinvI)
 constexpr int kQScalars = 80;  // kMQscale .. kMRopeR: the per-row scalars of a prepared query block
+constexpr int kMWmax = 112;    // [2 teams][2][4][16] tile maxima (a team's tiles alternate buffers);
+                               // after the tile loop [16] = final running max
+constexpr int kMLw = 368;      // [8 score warps][16]
+constexpr int kMMrun = 496;    // [2][16] running max after tile i, in slot i & 1 (team hand-off)
 
 // workspace: n_slots partial records, then n_units prepared query blocks
 constexpr int kRecordBytes = kRows * (kL + 2) * 4;                    // 32,896
@@ -97,12 +108,18 @@ constexpr int kQPrepBytes = 16384 + 16384 + 2048 + 512;               // 35,328:
 constexpr uint32_t kQPrepCopyBytes = 16384 + 16384 + 2048 + 4 * kQScalars;
 
 // mbarrier slots (8 bytes each)
-constexpr int kBarFull = 0;    // [3] TMA landed
-constexpr int kBarEmpty = 3;   // [3] score + value warps done with a stage
-constexpr int kBarPFull = 6;   // [2] p tile written
-constexpr int kBarPEmpty = 8;  // [2] p tile consumed
-constexpr int kBarAbort = 10;  // int flag (shares the slot area)
-constexpr int kBarQ = 11;      // prepared query operands landed
+// Tile i lands in stage i % 3 and completes barrier kBarFull + i % 6: each of those six
+// barriers serves one team's tiles only (i and i + 6 have the same parity), so a team's
+// parity wait on it is never one phase behind or ahead of the tile it wants.
+constexpr int kFullBars = 2 * kStages;
+constexpr int kBarFull = 0;    // [6] TMA landed
+constexpr int kBarEmpty = 6;   // [3] the tile's team + value warps done with a stage
+constexpr int kBarPFull = 9;   // [2] p tile written
+constexpr int kBarPEmpty = 11; // [2] p tile consumed
+constexpr int kBarAbort = 13;  // int flag (shares the slot area)
+constexpr int kBarQ = 14;      // prepared query operands landed
+constexpr int kBarM = 15;      // running max after tile i published and the one before it read (phase i)
+static_assert(kBarM * 8 + 8 <= 128, "mbarrier area holds 16 slots");
 
 constexpr float kLog2e = 1.4426950408889634f;
 // 0x4B400000 read as fp32 is 1.5 * 2^23 = 12582912: an int32 accumulator started at this
@@ -162,6 +179,15 @@ ASTERQ_DEVICE Tile check_tile(const asterq_decode_params& p, int4 t) {
 }
 
 ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) { return check_tile(p, fetch_tile(p, idx)); }
+
+// tanh(x) = sign(x) (1 - e) / (1 + e) with e = exp(-2|x|), from the definition: absolute
+// error a few 1e-8, far below the score tolerance.  Used for the optional logit softcap
+// (latent_attention.py:200-201) in place of the library tanhf, whose code does not run
+// correctly inside the score warps' setmaxnreg register region.
+ASTERQ_DEVICE float softcap_tanh(float x) {
+  const float e = exp2f(-2.0f * kLog2e * fabsf(x));
+  return copysignf(__fdividef(1.0f - e, 1.0f + e), x);
+}
 
 // Normalized FWHT of rows [r0, r0 + nrows) of a [16][512] fp32 buffer, one warp:
 // lane l holds elements 16l..16l+15; stages h < 16 are lane-local, h >= 16 pair
@@ -356,14 +382,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(bar(kBarFull + s), 1);
-      mbar_init(bar(kBarEmpty + s), kThreads);
+      mbar_init(bar(kBarEmpty + s), 32 * (kTeamWarps + kValueWarps));
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(kBarPFull + b), 32 * kScoreWarps);
+      mbar_init(bar(kBarPFull + b), 32 * kTeamWarps);
       mbar_init(bar(kBarPEmpty + b), 32 * kValueWarps);
     }
+    for (int f = 0; f < kFullBars; ++f) mbar_init(bar(kBarFull + f), 1);
     mbar_init(bar(kBarQ), 1);
+    mbar_init(bar(kBarM), 32 * kTeamWarps);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -373,7 +400,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto issue = [&](int j) {
     const int s = j % kStages;
     const Tile t = load_tile(p, tile_begin + j);
-    const uint32_t full = bar(kBarFull + s);
+    const uint32_t full = bar(kBarFull + j % kFullBars);
     const uint32_t st = sbase + s * kStageBytes;
     if (t.n == 0) {
       mbar_arrive(full);
@@ -424,6 +451,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =====================================================================
     // score warps
     // =====================================================================
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kScoreRegs));
+    // team `team` takes tiles team, team + 2, ...; tw is the warp's index in its team
+    const int team = warp / kTeamWarps, tw = warp % kTeamWarps;
     mbar_wait(bar(kBarQ), 0, abort_flag);
     const uint2* qh = reinterpret_cast<const uint2*>(smem + kOffQh);
     const uint2* qr = reinterpret_cast<const uint2*>(smem + kOffQr);
@@ -436,26 +466,31 @@ __global__ void __launch_bounds__(kThreads, 1)
         qinvi[nt][cc] = misc[kMQinvI + 8 * nt + 2 * tq + cc];
         rratio[nt][cc] = misc[kMRopeR + 8 * nt + 2 * tq + cc];
       }
-    // softmax state of rows 8nt + 2tq + cc, replicated across the 8 gid lanes
-    float m_run[2][2], l_w[2][2];
+    // Softmax state of rows 8nt + 2tq + cc, replicated across the 8 gid lanes.  The running
+    // max is one chain over all tiles: the team of tile i reads the max after tile i - 1
+    // from the other team (kBarM phase i - 1) and publishes its own (phase i), so one team's
+    // QK of its next tile overlaps the other team's softmax.  Each team sums its own tiles'
+    // p relative to the max after its latest tile (m_team); both sums are brought to the
+    // final max at the end.
+    float m_team[2][2], l_w[2][2];
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
-        m_run[nt][cc] = -INFINITY;
+        m_team[nt][cc] = -INFINITY;
         l_w[nt][cc] = 0.0f;
       }
 
-    Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
-    int4 raw_next = (n_t > 1) ? fetch_tile(p, tile_begin + 1) : make_int4(0, 0, 0, 0);
+    Tile t_next = (team < n_t) ? load_tile(p, tile_begin + team) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
+    int4 raw_next = (team + 2 < n_t) ? fetch_tile(p, tile_begin + team + 2) : make_int4(0, 0, 0, 0);
 #pragma unroll 1
-    for (int i = 0; i < n_t; ++i) {
+    for (int i = team; i < n_t; i += 2) {
       const int s = i % kStages, b = i & 1;
       const Tile t = t_next;
-      // descriptors: tile i + 1 checked (fetched an iteration ago), tile i + 2 fetched
-      if (i + 1 < n_t) t_next = check_tile(p, raw_next);
-      if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
-      mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);
+      // descriptors: this team's next tile checked (fetched a tile ago), the one after fetched
+      if (i + 2 < n_t) t_next = check_tile(p, raw_next);
+      if (i + 4 < n_t) raw_next = fetch_tile(p, tile_begin + i + 4);
+      mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);
       const uint8_t* st = smem + s * kStageBytes;
       const uint32_t sst = sbase + s * kStageBytes;
       const bool cold = t.kind == ASTERQ_TILE_COLD;
@@ -472,12 +507,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int m = 0; m < 2; ++m)
 #pragma unroll
-          for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(warp, m, gid + 8 * h);
+          for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(tw, m, gid + 8 * h);
         const __half* scl = reinterpret_cast<const __half*>(st + kScales);
         // RoPE channel first (bf16, exact products), moved into the integer-score units
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
-          const int row = qk_token(warp, m, (lane & 7) + 8 * ((lane >> 3) & 1));
+          const int row = qk_token(tw, m, (lane & 7) + 8 * ((lane >> 3) & 1));
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
             uint32_t a[4];
@@ -565,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       } else {
         // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
         // S[1] is a second partial accumulator (odd groups) folded in below
-        const int row = 8 * warp + (lane & 7);
+        const int row = 8 * tw + (lane & 7);
 #pragma unroll 1
         for (int g = 0; g < 8; g += 2) {
 #pragma unroll
@@ -616,11 +651,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int c = 0; c < 4; ++c) {
             const int h = c >> 1, cc = c & 1;
             const int r = 8 * nt + 2 * tq + cc;
-            const int tk = cold ? qk_token(warp, m, gid + 8 * h) : 8 * warp + gid;
+            const int tk = cold ? qk_token(tw, m, gid + 8 * h) : 8 * tw + gid;
             bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
             if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
             float sv = S[m][nt][c] * (cold ? qinvi[nt][cc] : qinv[nt][cc]);
-            if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
+            if (p.logit_softcap > 0.0f) sv = p.logit_softcap * softcap_tanh(sv / p.logit_softcap);
             sv = valid ? sv : -INFINITY;
             S[m][nt][c] = sv;
             tmax[nt][cc] = fmaxf(tmax[nt][cc], sv);
@@ -632,31 +667,47 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int off = 4; off < 32; off <<= 1)
             tmax[nt][cc] = fmaxf(tmax[nt][cc], __shfl_xor_sync(0xffffffffu, tmax[nt][cc], off));
-      float* wmax = misc + kMWmax + (i & 1) * 64;
+      float* wmax = misc + kMWmax + team * 128 + ((i >> 1) & 1) * 64;
       if (gid == 0) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) wmax[warp * 16 + 8 * nt + 2 * tq + cc] = tmax[nt][cc];
+          for (int cc = 0; cc < 2; ++cc) wmax[tw * 16 + 8 * nt + 2 * tq + cc] = tmax[nt][cc];
       }
-      named_sync(1, 128);
-      float alpha_r[2][2], msub[2][2];
+      named_sync(1 + team, 32 * kTeamWarps);
+      // the running max before this tile, published by the other team
+      if (i > 0) mbar_wait(bar(kBarM), (i - 1) & 1, abort_flag);
+      const float* m_in = misc + kMMrun + ((i - 1) & 1) * 16;
+      float alpha_r[2][2], msub[2][2], lfac[2][2];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
           const int r = 8 * nt + 2 * tq + cc;
           const float mt = fmaxf(fmaxf(wmax[r], wmax[16 + r]), fmaxf(wmax[32 + r], wmax[48 + r]));
-          const float m_new = fmaxf(m_run[nt][cc], mt);
+          const float m_prev = (i > 0) ? m_in[r] : -INFINITY;
+          const float m_new = fmaxf(m_prev, mt);
           if (m_new == -INFINITY) {
             alpha_r[nt][cc] = 1.0f;
             msub[nt][cc] = 0.0f;
           } else {
-            alpha_r[nt][cc] = exp2f((m_run[nt][cc] - m_new) * kLog2e);
+            alpha_r[nt][cc] = exp2f((m_prev - m_new) * kLog2e);
             msub[nt][cc] = m_new;
           }
-          m_run[nt][cc] = m_new;
+          lfac[nt][cc] = (m_team[nt][cc] == -INFINITY) ? 0.0f : exp2f((m_team[nt][cc] - m_new) * kLog2e);
+          m_team[nt][cc] = m_new;
         }
+      // publish the running max after tile i (lanes gid 0 of the team's first warp hold all
+      // 16 rows).  Every thread of the team arrives once it has read the max before this
+      // tile: the phase completes only then, so the other team cannot overwrite that slot
+      // (with the max after tile i + 1) while a slow warp of this team still reads it.
+      if (tw == 0 && gid == 0) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) misc[kMMrun + (i & 1) * 16 + 8 * nt + 2 * tq + cc] = m_team[nt][cc];
+      }
+      mbar_arrive(bar(kBarM));
       // ---- p = exp(s - m), handed to the value warps ----
       if (i >= 2) mbar_wait(bar(kBarPEmpty + b), ((i >> 1) - 1) & 1, abort_flag);
       float psum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
@@ -670,7 +721,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int m = 0; m < 2; ++m)
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int tk = qk_token(warp, m, gid + 8 * h);
+            const int tk = qk_token(tw, m, gid + 8 * h);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
               const float p0 = exp2f((S[m][nt][2 * h] - msub[nt][0]) * kLog2e);
@@ -694,7 +745,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const float pv = exp2f((S[0][nt][c] - msub[nt][c]) * kLog2e);
-            P[(8 * nt + 2 * tq + c) * kPStride + 8 * warp + gid] = pv;
+            P[(8 * nt + 2 * tq + c) * kPStride + 8 * tw + gid] = pv;
             psum[nt][c] += pv;
           }
       }
@@ -704,9 +755,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
           for (int off = 4; off < 32; off <<= 1) psum[nt][cc] += __shfl_xor_sync(0xffffffffu, psum[nt][cc], off);
-          l_w[nt][cc] = l_w[nt][cc] * alpha_r[nt][cc] + psum[nt][cc];
+          l_w[nt][cc] = l_w[nt][cc] * lfac[nt][cc] + psum[nt][cc];
         }
-      if (warp == 0 && gid == 0) {
+      if (tw == 0 && gid == 0) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -715,21 +766,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(bar(kBarPFull + b));
       mbar_arrive(bar(kBarEmpty + s));
     }
-    // final per-warp sums and the running max
-    named_sync(1, 128);
+    // final per-warp sums, brought to the final running max, and the running max itself
+    // (the team that did not take the last tile reads it from the other team: phase n_t - 1)
+    const int last = n_t - 1;
+    if (n_t > 0 && (last & 1) != team) mbar_wait(bar(kBarM), last & 1, abort_flag);
+    named_sync(1 + team, 32 * kTeamWarps);
     if (gid == 0) {
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int cc = 0; cc < 2; ++cc) {
-          misc[kMLw + warp * 16 + 8 * nt + 2 * tq + cc] = l_w[nt][cc];
-          if (warp == 0) misc[kMWmax + 8 * nt + 2 * tq + cc] = m_run[nt][cc];
+          const int r = 8 * nt + 2 * tq + cc;
+          const float m_fin = (n_t > 0) ? misc[kMMrun + (last & 1) * 16 + r] : -INFINITY;
+          const float f = (m_team[nt][cc] == -INFINITY) ? 0.0f : exp2f((m_team[nt][cc] - m_fin) * kLog2e);
+          misc[kMLw + warp * 16 + r] = l_w[nt][cc] * f;
+          if (warp == 0) misc[kMWmax + r] = m_fin;
         }
     }
   } else {
     // =====================================================================
     // value warps: scale group g = warp - 4, latent dims [64g, 64g + 64)
     // =====================================================================
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kValueRegs));
     const int g = warp - kScoreWarps;
     float o[4][2][4];
 #pragma unroll
@@ -768,7 +826,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (i + 1 < n_t) t_next = check_tile(p, raw_next);
       if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
       mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
-      mbar_wait(bar(kBarFull + s), (i / kStages) & 1, abort_flag);  // TMA data visible to this warp
+      mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);  // TMA data visible to this warp
       const uint8_t* st = smem + s * kStageBytes;
       const uint32_t sst = sbase + s * kStageBytes;
       const float* P = reinterpret_cast<const float*>(smem + kOffP + b * kPBytes);
@@ -777,9 +835,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!cold && order == 0) {
         // first hot tile after cold ones: rotate the accumulator back (O = H O_rot)
         store_o();
-        named_sync(2, 32 * kValueWarps);
+        named_sync(3, 32 * kValueWarps);
         warp_fwht_rows(scratch_o, 2 * g, 2, lane);
-        named_sync(2, 32 * kValueWarps);
+        named_sync(3, 32 * kValueWarps);
         order = 1;
 #pragma unroll
         for (int mi = 0; mi < 4; ++mi)
@@ -897,10 +955,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // accumulator -> scratch in natural order, rotated back if it is still rotated
     store_o();
-    named_sync(2, 32 * kValueWarps);
+    named_sync(3, 32 * kValueWarps);
     if (order == 0) {
       warp_fwht_rows(scratch_o, 2 * g, 2, lane);
-      named_sync(2, 32 * kValueWarps);
+      named_sync(3, 32 * kValueWarps);
     }
   }
   __syncthreads();
@@ -913,7 +971,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int e = tid; e < kRows * kL / 4; e += kThreads) {
       const int r = e >> 7, c4 = e & 127;
       if (r >= n_rows) continue;
-      const float l = lw[r] + lw[16 + r] + lw[32 + r] + lw[48 + r];
+      float l = 0.0f;
+#pragma unroll
+      for (int w2 = 0; w2 < kScoreWarps; ++w2) l += lw[16 * w2 + r];
       const float inv = 1.0f / fmaxf(l, 1e-20f);
       const float4 v = *reinterpret_cast<const float4*>(O + r * kL + 4 * c4);
       const int64_t off = (out_row0 + r) * kL + 4 * c4;
@@ -936,7 +996,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (tid < kRows) {
       wm[(int64_t)slot * kRows + tid] = mrow[tid];
-      wl[(int64_t)slot * kRows + tid] = lw[tid] + lw[16 + tid] + lw[32 + tid] + lw[48 + tid];
+      float l = 0.0f;
+#pragma unroll
+      for (int w2 = 0; w2 < kScoreWarps; ++w2) l += lw[16 * w2 + tid];
+      wl[(int64_t)slot * kRows + tid] = l;
     }
   }
   if (tid == 0 && *abort_flag && p.device_status) atomicExch(p.device_status, 1);
@@ -1115,6 +1178,14 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(dec::qprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kPrepSmem);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
+      // the score/value register split (setmaxnreg) assumes exactly kLaunchRegs per thread at launch:
+      // refuse to launch a build that allocates fewer (an increase could then never be granted)
+      cudaFuncAttributes fa;
+      e = cudaFuncGetAttributes(&fa, dec::decode_kernel);
+      if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
+      if (fa.numRegs != dec::kLaunchRegs)
+        return set_error(ASTERQ_ERR_CUDA, "latent_decode: kernel built with %d registers per thread, the register split needs %d",
+                         fa.numRegs, dec::kLaunchRegs);
       if (dev < 64) configured |= (1ull << dev);
     }
     dec::TensorMaps maps;
