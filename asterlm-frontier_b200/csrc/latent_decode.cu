@@ -180,15 +180,6 @@ ASTERQ_DEVICE Tile check_tile(const asterq_decode_params& p, int4 t) {
 
 ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) { return check_tile(p, fetch_tile(p, idx)); }
 
-// tanh(x) = sign(x) (1 - e) / (1 + e) with e = exp(-2|x|), from the definition: absolute
-// error a few 1e-8, far below the score tolerance.  Used for the optional logit softcap
-// (latent_attention.py:200-201) in place of the library tanhf, whose code does not run
-// correctly inside the score warps' setmaxnreg register region.
-ASTERQ_DEVICE float softcap_tanh(float x) {
-  const float e = exp2f(-2.0f * kLog2e * fabsf(x));
-  return copysignf(__fdividef(1.0f - e, 1.0f + e), x);
-}
-
 // Normalized FWHT of rows [r0, r0 + nrows) of a [16][512] fp32 buffer, one warp:
 // lane l holds elements 16l..16l+15; stages h < 16 are lane-local, h >= 16 pair
 // lane l with l ^ (h / 16).  Not on the bit-exact path.
@@ -397,9 +388,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
 
   // ---------------- producer: issue one tile into its stage ----------------
-  auto issue = [&](int j) {
+  auto issue_tile = [&](int j, const Tile t) {
     const int s = j % kStages;
-    const Tile t = load_tile(p, tile_begin + j);
     const uint32_t full = bar(kBarFull + j % kFullBars);
     const uint32_t st = sbase + s * kStageBytes;
     if (t.n == 0) {
@@ -423,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_2d(st + kHRope, hot ? &maps.hrope : &maps.nrope, 0, y, full);
     }
   };
+  auto issue = [&](int j) { issue_tile(j, load_tile(p, tile_begin + j)); };
   if (warp == kProducerWarp) {
     if (lane == 0)
       for (int j = 0; j < min(n_t, kStages - 1); ++j) issue(j);
@@ -655,7 +646,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
             if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
             float sv = S[m][nt][c] * (cold ? qinvi[nt][cc] : qinv[nt][cc]);
-            if (p.logit_softcap > 0.0f) sv = p.logit_softcap * softcap_tanh(sv / p.logit_softcap);
+            if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
             sv = valid ? sv : -INFINITY;
             S[m][nt][c] = sv;
             tmax[nt][cc] = fmaxf(tmax[nt][cc], sv);
@@ -819,6 +810,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
     int4 raw_next = (n_t > 1) ? fetch_tile(p, tile_begin + 1) : make_int4(0, 0, 0, 0);
+    // producer lane: raw descriptor of the next tile it will issue
+    int4 praw = (warp == kProducerWarp && lane == 0 && kStages < n_t) ? fetch_tile(p, tile_begin + kStages)
+                                                                         : make_int4(0, 0, 0, 0);
 #pragma unroll 1
     for (int i = 0; i < n_t; ++i) {
       const int s = i % kStages, b = i & 1;
@@ -947,9 +941,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(bar(kBarPEmpty + b));
       mbar_arrive(bar(kBarEmpty + s));
       if (warp == kProducerWarp) {
-        // refill this stage with tile i + 3 once every warp has released tile i
+        // refill this stage with tile i + 3 once every warp has released tile i; its
+        // descriptor was fetched a tile ago, so the issue does not wait on global memory
         if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag))
-          issue(i + kStages);
+          issue_tile(i + kStages, check_tile(p, praw));
+        if (lane == 0 && i + kStages + 1 < n_t) praw = fetch_tile(p, tile_begin + i + kStages + 1);
         __syncwarp();
       }
     }
