@@ -25,19 +25,22 @@
 //    query (exact); hot PV = bf16 latent x p split hi + lo in bf16; RoPE = bf16
 //    x bf16; fp32 accumulation everywhere.
 //
-// CTA organisation (one CTA per work item, 12 warps):
-//  * TMA producer (lane 0 of warp 4): streams the item's tiles (128 cold tokens or
+// CTA organisation (one CTA per work item, 16 warps):
+//  * TMA producer (lane 0 of warp 8): streams the item's tiles (128 cold tokens or
 //    32 hot/new tokens) into a 3-stage ring with cp.async.bulk.tensor (128-byte
 //    hardware swizzle) and mbarrier completion; tile i+3 is issued as soon as
-//    every warp has released tile i.
-//  * warps 0-3 ("score warps"): each owns a quarter of a tile's tokens and all 512
-//    latent dims, so every score row is complete inside one warp (no cross-warp
-//    reduction).  They finish the online softmax (one named barrier to combine the
-//    four warps' tile maxima) and hand p to the value warps through
-//    double-buffered shared memory (cold tiles: fp16 [token][row] plus the
-//    tokens' code scales by group; hot tiles: fp32 [row][token]).
-//  * warps 4-11 ("value warps"): each owns 64 latent dims (one scale group) of
-//    the 16 x 512 accumulator and accumulates p . V for every tile.
+//    tile i's team and the value warps have released it.
+//  * warps 0-7 ("score warps"): two teams of 4 that take alternate tiles, so one
+//    team's softmax overlaps the other's QK.  In a team each warp owns a quarter of
+//    the tile's tokens and all 512 latent dims, so every score row is complete
+//    inside one warp.  The team finishes the online softmax (one named barrier per
+//    team for the tile maxima; the running max passes between the teams) and hands
+//    p to the value warps through shared memory, one buffer per team (cold tiles:
+//    fp16 [token][row] plus the tokens' code scales by group; hot tiles: fp32
+//    [row][token]).
+//  * warps 8-15 ("value warps"): each owns 64 latent dims (one scale group) of
+//    the 16 x 512 accumulator and accumulates p . V for every tile, in order.
+// setmaxnreg gives the score warpgroups 160 registers and the value warpgroups 96.
 // Every wait is bounded; a timeout sets a status flag instead of hanging.
 #include <atomic>
 #include <cuda.h>
@@ -776,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // =====================================================================
-    // value warps: scale group g = warp - 4, latent dims [64g, 64g + 64)
+    // value warps: scale group g = warp - 8, latent dims [64g, 64g + 64)
     // =====================================================================
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kValueRegs));
     const int g = warp - kScoreWarps;
