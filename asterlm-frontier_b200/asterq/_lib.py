@@ -84,7 +84,7 @@ class DecodeParams(ctypes.Structure):
         ("device_status", ctypes.c_void_p),
         ("units", ctypes.c_void_p),
         ("n_units", ctypes.c_int32),
-        ("_pad", ctypes.c_int32),
+        ("cold_scheme", ctypes.c_int32),
     ]
 
 

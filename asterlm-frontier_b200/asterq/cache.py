@@ -32,7 +32,8 @@ from .decode import GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools
 from .kv import QuantizedTensor, dequantize_tensor
 from .plan import SequenceLayout
 
-_KERNEL_SCHEMES = ("hadamard_int4", "bfloat16")
+_KERNEL_SCHEMES = ("hadamard_int4", "int4", "bfloat16")
+_SCHEME_IDS = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4}
 
 
 class _Pool:
@@ -76,7 +77,7 @@ class LatentLayerCache:
     """Hot/cold latent cache for one global-attention layer (cache.py:52).
 
     Same constructor fields and defaults as the reference.  The decode kernels
-    serve ``cache_dtype`` "hadamard_int4" (cold chunks) and "bfloat16" (never
+    serve ``cache_dtype`` "hadamard_int4" and "int4" (cold chunks) and "bfloat16" (never
     flushes, cache.py:169); ``group_size`` must be 64 and ``quantize_rope``
     False for the kernel path, as in every BASELINE configuration.
     """
@@ -97,8 +98,8 @@ class LatentLayerCache:
     def __post_init__(self) -> None:
         if self.cache_dtype not in _KERNEL_SCHEMES:
             raise NotImplementedError(
-                f"cache_dtype {self.cache_dtype!r}: the asterq pools serve 'hadamard_int4' and 'bfloat16'")
-        if self.cache_dtype == "hadamard_int4" and self.group_size != GROUP_SIZE:
+                f"cache_dtype {self.cache_dtype!r}: the asterq pools serve 'hadamard_int4', 'int4' and 'bfloat16'")
+        if self.cache_dtype in _SCHEME_IDS and self.group_size != GROUP_SIZE:
             raise NotImplementedError(f"group_size {self.group_size}: the decode kernels use groups of {GROUP_SIZE}")
         if self.quantize_rope:
             raise NotImplementedError("quantize_rope=True: the decode kernels read bf16 RoPE keys")
@@ -160,7 +161,8 @@ class LatentLayerCache:
         if self._hot is None:
             raise RuntimeError("empty cache")
         return LatentPools(cold_codes=self._cold["codes"], cold_scales=self._cold["scales"],
-                           cold_rope=self._cold["rope"], hot_latent=self._hot["latent"], hot_rope=self._hot["rope"])
+                           cold_rope=self._cold["rope"], hot_latent=self._hot["latent"], hot_rope=self._hot["rope"],
+                           cold_scheme=self.cache_dtype if self.cache_dtype in _SCHEME_IDS else "hadamard_int4")
 
     def decode_layouts(self, q_len: int) -> list[SequenceLayout]:
         """One SequenceLayout per batch row; row b's new tokens are rows b*q_len.. of the step's arrays."""
@@ -232,7 +234,7 @@ class LatentLayerCache:
         scales = torch.empty(bsz * P, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=dev)
         lib = _lib.load()
         _lib.check(lib.asterq_quantize(x.data_ptr(), _lib.DTYPE_BF16, bsz * P, LATENT_DIM, LATENT_DIM,
-                                       _lib.SCHEME_HADAMARD_INT4, GROUP_SIZE, codes.data_ptr(), scales.data_ptr(),
+                                       _SCHEME_IDS[self.cache_dtype], GROUP_SIZE, codes.data_ptr(), scales.data_ptr(),
                                        _lib.stream_handle(dev)))
         self._cold["codes"].index_copy_(0, dst, codes.view(bsz, P, -1))
         self._cold["scales"].index_copy_(0, dst, scales.view(bsz, P, -1))
@@ -296,7 +298,7 @@ class LatentLayerCache:
             data = torch.stack([self._cold["codes"][pg] for pg in pages])
             scale = torch.stack([self._cold["scales"][pg] for pg in pages]).unsqueeze(-1)
             out.append(QuantizedTensor(data=data, scale=scale, original_shape=(self._batch, self.chunk_tokens, LATENT_DIM),
-                                       padded_dim=LATENT_DIM, group_size=GROUP_SIZE, scheme="hadamard_int4",
+                                       padded_dim=LATENT_DIM, group_size=GROUP_SIZE, scheme=self.cache_dtype,
                                        source_dtype=self._dtype))
         return out
 

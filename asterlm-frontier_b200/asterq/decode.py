@@ -19,6 +19,7 @@ from .plan import DecodePlan
 LATENT_DIM = 512
 ROPE_DIM = 64
 GROUP_SIZE = 64
+COLD_SCHEMES = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4}
 
 
 @dataclass
@@ -30,6 +31,7 @@ class LatentPools:
     cold_rope: torch.Tensor  # bf16 [Pc, page, 64]
     hot_latent: torch.Tensor  # bf16 [Ph, page, 512]
     hot_rope: torch.Tensor  # bf16 [Ph, page, 64]
+    cold_scheme: str = "hadamard_int4"  # or "int4": plain groupwise codes, same layout
 
     @property
     def page_tokens(self) -> int:
@@ -119,6 +121,9 @@ def make_params(
     p.workspace_bytes = dplan.workspace.numel() * 4
     p.units = dplan.units.data_ptr()
     p.n_units = int(plan.n_units)
+    if pools.cold_scheme not in COLD_SCHEMES:
+        raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
+    p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]
     return p
 
 

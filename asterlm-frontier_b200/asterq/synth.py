@@ -96,7 +96,7 @@ class PoolBuilder:
     chunks (the newest possibly partial) and encoded with the write-path kernel.
     """
 
-    def __init__(self, lengths, hot, *, q_len, n_heads, page_tokens=512, device="cuda"):
+    def __init__(self, lengths, hot, *, q_len, n_heads, page_tokens=512, device="cuda", scheme="hadamard_int4"):
         from . import _lib
 
         self._lib = _lib
@@ -107,6 +107,8 @@ class PoolBuilder:
         n_cold_pages = sum(math.ceil(max(0, n - h) / page_tokens) for n, h in zip(lengths, hot))
         n_hot_pages = sum(math.ceil(h / page_tokens) for h in hot)
         self.pools = LatentPools.empty(n_cold_pages, n_hot_pages, page_tokens, self.device)
+        self.pools.cold_scheme = scheme
+        self._scheme_id = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4}[scheme]
         total_q = len(self.lengths) * q_len
         dev = self.device
         self.q_lat = torch.zeros(total_q, n_heads, LATENT_DIM, dtype=torch.bfloat16, device=dev)
@@ -136,7 +138,7 @@ class PoolBuilder:
             self._lib.check(
                 self.lib.asterq_quantize(
                     lat.data_ptr(), self._lib.DTYPE_BF16, cold, LATENT_DIM, LATENT_DIM,
-                    self._lib.SCHEME_HADAMARD_INT4, GROUP_SIZE, codes[r0].data_ptr(), scales[r0].data_ptr(),
+                    self._scheme_id, GROUP_SIZE, codes[r0].data_ptr(), scales[r0].data_ptr(),
                     self._lib.stream_handle(self.device),
                 )
             )

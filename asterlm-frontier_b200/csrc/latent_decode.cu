@@ -279,7 +279,8 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
     }
   }
   __syncwarp();
-  warp_fwht_rows(scratch, 2 * warp, 2, lane);
+  // hadamard_int4 scores the codes in the rotated basis (H q); plain int4 in the natural one
+  if (p.cold_scheme == ASTERQ_SCHEME_HADAMARD_INT4) warp_fwht_rows(scratch, 2 * warp, 2, lane);
   __syncwarp();
   for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
     float mx = 0.0f;
@@ -783,6 +784,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =====================================================================
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kValueRegs));
     const int g = warp - kScoreWarps;
+    const bool rotated = p.cold_scheme == ASTERQ_SCHEME_HADAMARD_INT4;  // else plain int4: no rotation back
     float o[4][2][4];
 #pragma unroll
     for (int a = 0; a < 4; ++a)
@@ -833,8 +835,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // first hot tile after cold ones: rotate the accumulator back (O = H O_rot)
         store_o();
         named_sync(3, 32 * kValueWarps);
-        warp_fwht_rows(scratch_o, 2 * g, 2, lane);
-        named_sync(3, 32 * kValueWarps);
+        if (rotated) {
+          warp_fwht_rows(scratch_o, 2 * g, 2, lane);
+          named_sync(3, 32 * kValueWarps);
+        }
         order = 1;
 #pragma unroll
         for (int mi = 0; mi < 4; ++mi)
@@ -955,7 +959,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // accumulator -> scratch in natural order, rotated back if it is still rotated
     store_o();
     named_sync(3, 32 * kValueWarps);
-    if (order == 0) {
+    if (order == 0 && rotated) {
       warp_fwht_rows(scratch_o, 2 * g, 2, lane);
       named_sync(3, 32 * kValueWarps);
     }
@@ -1085,6 +1089,8 @@ int validate(const asterq_decode_params* p) {
                      p->page_tokens);
   if (p->out_dtype != ASTERQ_DTYPE_F32 && p->out_dtype != ASTERQ_DTYPE_BF16)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: out_dtype must be f32 or bf16");
+  if (p->cold_scheme != ASTERQ_SCHEME_HADAMARD_INT4 && p->cold_scheme != ASTERQ_SCHEME_INT4)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: cold scheme %d unsupported (hadamard_int4 or int4)", p->cold_scheme);
   if (p->n_items < 0 || p->n_tiles < 0 || p->n_combine < 0 || p->n_slots < 0)
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: negative table size");
   if (p->n_items > 0 && (!p->items || !p->tiles || !p->q_lat || !p->q_rope || !p->out))

@@ -114,6 +114,7 @@ int asterq_codec_status(int32_t* timeouts);
  *          slot < 0: the item covers the whole sequence and writes `out` directly;
  *          slot >= 0: it writes an (m, l, o) partial to the workspace.
  *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
+ * Cold schemes: hadamard_int4 and int4 (params.cold_scheme).
  * Geometry supported: latent_dim 512, rope_dim 64, scale groups of 64, page_tokens
  * a multiple of 128, q_len <= 16.  cold tiles hold <= 128 tokens, hot/new tiles <= 32.
  */
@@ -151,7 +152,9 @@ typedef struct asterq_decode_params {
   int32_t* device_status; /* optional int32 on the device: set nonzero if a pipeline wait timed out */
   const int32_t* units;   /* [n_units][2] {out_row0, n_rows}: the 16-row query blocks, prepared once per step */
   int32_t n_units;
-  int32_t reserved;
+  int32_t cold_scheme;    /* ASTERQ_SCHEME_HADAMARD_INT4 (0): cold codes rotated by the normalized Hadamard
+                             transform (kv.py scheme "hadamard_int4"); ASTERQ_SCHEME_INT4: plain groupwise
+                             int4 codes (scheme "int4"), same packing and scale layout */
 } asterq_decode_params;
 
 /* Bytes of workspace asterq_latent_decode needs: n_slots partial records of 32,896 B

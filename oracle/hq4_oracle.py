@@ -202,6 +202,7 @@ class ColdChunk:
     rope: np.ndarray
     latent_dim: int
     group_size: int = 64
+    scheme: str = "hadamard_int4"
 
     @property
     def length(self) -> int:
@@ -209,14 +210,14 @@ class ColdChunk:
 
     def dequantized_latent(self) -> np.ndarray:
         """Dequantize like ``iter_chunks`` (cache.py:143-148 -> kv.py:121-134)."""
-        padded = next_power_of_two(self.latent_dim)
+        padded = next_power_of_two(self.latent_dim) if self.scheme == "hadamard_int4" else self.latent_dim
         q = Quantized(
             data=self.codes,
             scale=self.scales.reshape(self.length, -1, 1),
             original_shape=(self.length, self.latent_dim),
             padded_dim=padded,
             group_size=self.group_size,
-            scheme="hadamard_int4",
+            scheme=self.scheme,
         )
         return dequantize(q)
 
@@ -399,6 +400,7 @@ def build_cache_from_tokens(
     recent_tokens: int,
     chunk_tokens: int,
     group_size: int = 64,
+    scheme: str = "hadamard_int4",
 ) -> LatentCacheView:
     """Replay ``LatentLayerCache.append`` + ``_flush_cold_chunks`` (cache.py:167-201).
 
@@ -414,7 +416,7 @@ def build_cache_from_tokens(
     start = 0
     while latent.shape[0] - start > threshold:
         piece = latent[start : start + chunk_tokens]
-        q = quantize(piece, "hadamard_int4", group_size)
+        q = quantize(piece, scheme, group_size)
         cold.append(
             ColdChunk(
                 codes=q.data,
@@ -422,6 +424,7 @@ def build_cache_from_tokens(
                 rope=rope[start : start + chunk_tokens].copy(),
                 latent_dim=latent.shape[-1],
                 group_size=group_size,
+                scheme=scheme,
             )
         )
         start += chunk_tokens
@@ -434,6 +437,7 @@ def build_cache_split(
     hot_tokens: int,
     chunk_tokens: int,
     group_size: int = 64,
+    scheme: str = "hadamard_int4",
 ) -> LatentCacheView:
     """Cold/hot split used by the ragged workloads: the newest ``hot_tokens``
     stay hot, the rest is cut oldest-first into ``chunk_tokens`` chunks whose
@@ -446,7 +450,7 @@ def build_cache_split(
     cold = []
     for start in range(0, n_cold, chunk_tokens):
         end = min(start + chunk_tokens, n_cold)
-        q = quantize(latent[start:end], "hadamard_int4", group_size)
+        q = quantize(latent[start:end], scheme, group_size)
         cold.append(
             ColdChunk(
                 codes=q.data,
@@ -454,6 +458,7 @@ def build_cache_split(
                 rope=rope[start:end].copy(),
                 latent_dim=latent.shape[-1],
                 group_size=group_size,
+                scheme=scheme,
             )
         )
     return LatentCacheView(cold=cold, hot_latent=latent[n_cold:].copy(), hot_rope=rope[n_cold:].copy())

@@ -86,14 +86,15 @@ def test_batch_rows_are_independent(cuda):
         assert torch.equal(both.latent[row], one.latent[0])
 
 
-def test_materialize_and_iter_chunks_match_oracle(cuda):
+@pytest.mark.parametrize("scheme", ["hadamard_int4", "int4"])
+def test_materialize_and_iter_chunks_match_oracle(cuda, scheme):
     from asterq.cache import LatentLayerCache
 
     inp = _inputs(5, 2100)
     lat, rope = inp["latent"][:2100], inp["rope"][:2100]
-    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=512, chunk_tokens=512)
+    cache = LatentLayerCache(scheme, 64, recent_tokens=512, chunk_tokens=512)
     cache.append(lat[None].to(cuda), rope[None].to(cuda), None, 0)
-    ref = O.build_cache_from_tokens(_bf16_np(lat), _bf16_np(rope), 512, 512)
+    ref = O.build_cache_from_tokens(_bf16_np(lat), _bf16_np(rope), 512, 512, scheme=scheme)
     want_lat, want_rope = ref.materialize()
     got_lat = cache.materialize_latent(dtype=torch.float32)[0].cpu().numpy()
     got_rope = cache.materialize_rope(dtype=torch.float32)[0].cpu().numpy()
@@ -104,20 +105,22 @@ def test_materialize_and_iter_chunks_match_oracle(cuda):
     np.testing.assert_array_equal(torch.cat([c[0] for c in chunks], dim=1)[0].cpu().numpy(), want_lat)
 
 
-@pytest.mark.parametrize("q_len", [1, 3])
-def test_latent_attention_over_the_cache(cuda, q_len):
+@pytest.mark.parametrize("q_len,scheme", [(1, "hadamard_int4"), (3, "hadamard_int4"), (1, "int4"), (3, "int4")])
+def test_latent_attention_over_the_cache(cuda, q_len, scheme):
+    """Both cold schemes the kernels read: hadamard_int4 (scores in the rotated basis)
+    and plain int4 (kv.py scheme "int4", no rotation)."""
     from asterq.attention import latent_attention
     from asterq.cache import LatentLayerCache
 
     n = 4000
     inp = _inputs(6 + q_len, n, q_len)
-    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=512, chunk_tokens=512)
+    cache = LatentLayerCache(scheme, 64, recent_tokens=512, chunk_tokens=512)
     cache.append(inp["latent"][None, :n].to(cuda), inp["rope"][None, :n].to(cuda), None, 0)
     out = latent_attention(inp["q_lat"][None].to(cuda), inp["q_rope"][None].to(cuda),
                            inp["latent"][None, n:].to(cuda), inp["rope"][None, n:].to(cuda), cache,
                            softmax_scale=SCALE)
     lat, rope = _bf16_np(inp["latent"]), _bf16_np(inp["rope"])
-    ref_cache = O.build_cache_from_tokens(lat[:n], rope[:n], 512, 512)
+    ref_cache = O.build_cache_from_tokens(lat[:n], rope[:n], 512, 512, scheme=scheme)
     ref = O.decode(_bf16_np(inp["q_lat"]), _bf16_np(inp["q_rope"]), lat[n:], rope[n:], ref_cache, SCALE)
     got = out[0].cpu().numpy()
     assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2

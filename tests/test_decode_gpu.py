@@ -58,18 +58,18 @@ def run_decode(wl, *, out_dtype=torch.float32, softcap=None, **plan_kw):
     return out, plan
 
 
-def single_sequence_workload(inp, ctx, hot, q_len, device):
+def single_sequence_workload(inp, ctx, hot, q_len, device, scheme="hadamard_int4"):
     from asterq.synth import PoolBuilder
 
-    b = PoolBuilder([ctx], [hot], q_len=q_len, n_heads=inp["q_lat"].shape[1], device=device)
+    b = PoolBuilder([ctx], [hot], q_len=q_len, n_heads=inp["q_lat"].shape[1], device=device, scheme=scheme)
     b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
     return b.finish("single")
 
 
-def oracle_for(inp, ctx, hot, q_len, softcap=None, chunk=512):
+def oracle_for(inp, ctx, hot, q_len, softcap=None, chunk=512, scheme="hadamard_int4"):
     lat = inp["latent"].float().numpy()
     rope = inp["rope"].float().numpy()
-    cache = O.build_cache_split(lat[:ctx], rope[:ctx], hot, chunk)
+    cache = O.build_cache_split(lat[:ctx], rope[:ctx], hot, chunk, scheme=scheme)
     return O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[ctx:], rope[ctx:], cache,
                     SCALE, softcap)
 
@@ -130,6 +130,23 @@ def test_softcap(cuda):
     wl = single_sequence_workload(inp, 2500, 600, 1, cuda)
     out, _ = run_decode(wl, softcap=2.0)
     assert_close(out.cpu().numpy(), oracle_for(inp, 2500, 600, 1, softcap=2.0), "softcap")
+
+
+@pytest.mark.parametrize("q_len", [1, 3])
+def test_plain_int4_cold_scheme(cuda, q_len):
+    """Cold chunks in kv.py's scheme "int4" (no Hadamard rotation): the query is not
+    rotated and the cold accumulator is not rotated back; split items and the
+    combine kernel included."""
+    from asterq.synth import c1_inputs
+
+    inp = c1_inputs(seed=31 + q_len, ctx=6000, q_len=q_len)
+    wl = single_sequence_workload(inp, 6000, 900, q_len, cuda, scheme="int4")
+    ref = oracle_for(inp, 6000, 900, q_len, scheme="int4")
+    one, _ = run_decode(wl, max_items_per_seq=1)
+    many, plan = run_decode(wl, n_sms=32, ctas_per_sm=2, waves=4)
+    assert plan.n_slots > 2
+    assert_close(one.cpu().numpy(), ref, f"int4 q_len {q_len}")
+    assert_close(many.cpu().numpy(), ref, f"int4 q_len {q_len} split")
 
 
 def test_n_heads_not_multiple_of_16(cuda):
