@@ -115,5 +115,5 @@ class LatentAttentionKernels:
         return self._context(q_content, q_rope, latent, k_rope, previous)
 
     def _full_attention(self, q_content, q_rope, latent, k_rope, previous: LatentLayerCache | None) -> torch.Tensor:
-        """latent_attention.py:116-175 for T <= 16 new tokens (MTP verification, short prefill steps)."""
+        """latent_attention.py:116-175 for T <= 2048 new tokens (MTP verification, prefill chunks)."""
         return self._context(q_content, q_rope, latent, k_rope, previous)

@@ -24,7 +24,7 @@ from . import _lib
 COLD_TILE = 128
 HOT_TILE = 32
 ROWS_PER_BLOCK = 16
-MAX_Q_LEN = 16  # new tokens per sequence (one new-token tile of <= 32 tokens)
+MAX_Q_LEN = 2048  # new tokens per sequence and step (the reference prefills in chunks of 2048)
 
 # bytes one tile streams from HBM (cost model for balancing)
 _COLD_TOKEN_BYTES = 256 + 16 + 128
@@ -91,8 +91,20 @@ def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
         for s in range(0, n, HOT_TILE):
             out.append((_lib.TILE_HOT, page, off + s, min(HOT_TILE, n - s)))
     if seq.q_len > 0 and seq.attend_new:
-        out.append((_lib.TILE_NEW, seq.q_start, 0, seq.q_len))
+        for s in range(0, seq.q_len, HOT_TILE):
+            out.append((_lib.TILE_NEW, seq.q_start, s, min(HOT_TILE, seq.q_len - s)))
     return out
+
+
+def _visible_tiles(seq: SequenceLayout, t0: int, t1: int, rb: int, n_heads: int) -> int:
+    """End of the tiles row block `rb` can see: new-token tiles wholly after its last
+    token are fully masked (k <= past_len + i, latent_attention.py:151-153) and dropped."""
+    if not (seq.q_len > 0 and seq.attend_new):
+        return t1
+    n_new = (seq.q_len + HOT_TILE - 1) // HOT_TILE
+    last_row = min(seq.q_len * n_heads, (rb + 1) * ROWS_PER_BLOCK) - 1
+    last_token = last_row // n_heads
+    return t1 - n_new + last_token // HOT_TILE + 1
 
 
 def _tile_cost(kind: int, n: int) -> int:
@@ -140,9 +152,10 @@ def build_plan(
     total_cost = 0
     for si, seq in enumerate(seqs):
         rows = seq.q_len * n_heads
-        t0, t1 = seq_tile_ranges[si]
-        c = int(prefix[t1] - prefix[t0])
+        t0, t1s = seq_tile_ranges[si]
         for rb in range((rows + ROWS_PER_BLOCK - 1) // ROWS_PER_BLOCK):
+            t1 = _visible_tiles(seq, t0, t1s, rb, n_heads)
+            c = int(prefix[t1] - prefix[t0])
             units.append((si, rb, t0, t1, c))
             total_cost += c
     slots_target = max(1, int(n_sms * ctas_per_sm * waves))

@@ -116,7 +116,7 @@ int asterq_codec_status(int32_t* timeouts);
  *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
  * Cold schemes: hadamard_int4 and int4 (params.cold_scheme).
  * Geometry supported: latent_dim 512, rope_dim 64, scale groups of 64, page_tokens
- * a multiple of 128, q_len <= 16.  cold tiles hold <= 128 tokens, hot/new tiles <= 32.
+ * a multiple of 128, q_len <= 2048.  cold tiles hold <= 128 tokens, hot/new tiles <= 32.
  */
 typedef struct asterq_decode_params {
   int32_t n_heads;

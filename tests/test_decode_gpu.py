@@ -112,6 +112,19 @@ def test_q_len_causal(cuda, q_len):
     assert_close(out.cpu().numpy(), oracle_for(inp, 3000, 700, q_len), f"q_len {q_len}")
 
 
+@pytest.mark.parametrize("q_len,n_heads", [(40, 16), (100, 16), (37, 6)])
+def test_prefill_chunk_over_the_cache(cuda, q_len, n_heads):
+    """Chunked prefill (q_len > 32, several new-token tiles) over the quantized cache:
+    new token i sees the cache and new tokens 0..i (latent_attention.py:151-153)."""
+    from asterq.synth import c1_inputs
+
+    inp = c1_inputs(seed=40 + q_len, ctx=2500, q_len=q_len, n_heads=n_heads)
+    wl = single_sequence_workload(inp, 2500, 700, q_len, cuda)
+    out, plan = run_decode(wl)
+    assert int((plan.tiles[:, 0] == 2).sum()) == (q_len + 31) // 32
+    assert_close(out.cpu().numpy(), oracle_for(inp, 2500, 700, q_len), f"prefill q_len {q_len}")
+
+
 @pytest.mark.parametrize("ctx,hot", [(0, 0), (5, 5), (513, 0), (640, 100), (1000, 1000), (4097, 2049)])
 def test_edge_layouts(cuda, ctx, hot):
     """Empty cache (new tokens only), tiny caches, cold-only, partial chunks/tiles."""

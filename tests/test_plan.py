@@ -58,10 +58,26 @@ def test_items_sorted_longest_first():
     assert (np.diff(sizes) <= 0).all()
 
 
-@pytest.mark.parametrize("bad", [dict(q_len=0), dict(q_len=17)])
+@pytest.mark.parametrize("bad", [dict(q_len=0), dict(q_len=2049)])
 def test_rejects_bad_q_len(bad):
     with pytest.raises(ValueError):
         build_plan([_layout([], [], 0, **bad)], 16)
+
+
+def test_prefill_chunk_row_blocks_see_only_their_causal_prefix():
+    """q_len 100 new tokens, 16 heads: 32-token new tiles; row block rb (token rb)
+    keeps the cache plus the new tiles up to its own token."""
+    from asterq.plan import HOT_TILE
+
+    lay = _layout([(0, 0, 512)], [(1, 0, 64)], 0, q_len=100)
+    plan = build_plan([lay], 16, max_items_per_seq=1)
+    new = plan.tiles[plan.tiles[:, 0] == 2]
+    assert [int(n) for n in new[:, 3]] == [32, 32, 32, 4]
+    assert [int(o) for o in new[:, 2]] == [0, 32, 64, 96]
+    n_cache = 512 // 128 + 64 // HOT_TILE
+    for it in plan.items:
+        rb, t0, t1 = int(it[1]), int(it[2]), int(it[3])
+        assert t1 - t0 == n_cache + rb // HOT_TILE + 1
 
 
 def test_rejects_bad_chunks():
