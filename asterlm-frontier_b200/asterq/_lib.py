@@ -85,6 +85,9 @@ class DecodeParams(ctypes.Structure):
         ("units", ctypes.c_void_p),
         ("n_units", ctypes.c_int32),
         ("cold_scheme", ctypes.c_int32),
+        ("workers", ctypes.c_void_p),
+        ("n_workers", ctypes.c_int32),
+        ("reserved0", ctypes.c_int32),
     ]
 
 

@@ -67,6 +67,7 @@ class DeviceDecodePlan:
         self.items = up(plan.items)
         self.combine = up(plan.combine)
         self.units = up(plan.units)
+        self.workers = None if plan.workers is None else torch.from_numpy(plan.workers.copy()).to(self.device)
         self.workspace = torch.empty(max(4, plan.workspace_bytes // 4), dtype=torch.float32, device=self.device)
 
     @property
@@ -121,6 +122,9 @@ def make_params(
     p.workspace_bytes = dplan.workspace.numel() * 4
     p.units = dplan.units.data_ptr()
     p.n_units = int(plan.n_units)
+    if dplan.workers is not None and plan.n_workers > 0:
+        p.workers = dplan.workers.data_ptr()
+        p.n_workers = plan.n_workers
     if pools.cold_scheme not in COLD_SCHEMES:
         raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
     p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]

@@ -4,17 +4,23 @@ A batch is a list of sequences, each with its cold chunks (pages of INT4
 codes), its hot pages (BF16) and ``q_len`` new tokens.  The reference walks one
 sequence's chunks serially (cache.py:139-159, latent_attention.py:222-227);
 here every sequence's token list is cut into tiles (128 cold tokens or 32 hot /
-new tokens) and the tiles into work items, one CTA each, sized by the bytes
-they read so that a ragged batch fills all SMs.  Items that do not cover a
-whole sequence write partial (m, l, o) records merged by the combine step.
+new tokens).  The default (persistent) schedule gives every SM one worker CTA
+and cuts the concatenated tile lists of all 16-row query blocks into one
+contiguous share per worker of equal estimated time (measured per-tile costs
+plus a fixed cost per item); a worker runs its items one after another, so a
+ragged batch ends on all SMs at about the same time.  Items that do not cover
+a whole query block write partial (m, l, o) records merged by the combine step.
 
 Tables (int32, see include/asterq.h):
   tiles   [n_tiles, 4]  {kind, page, offset, n_tokens}
-  items   [n_items, 8]  {seq, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
+  items   [n_items, 8]  {unit, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
   combine [n_combine, 4] {slot_begin, slot_end, out_row0, n_rows}
+  workers [n_workers + 1] item offsets: worker w runs items workers[w] .. workers[w + 1] - 1
 """
 from __future__ import annotations
 
+import bisect
+import heapq
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -30,6 +36,14 @@ MAX_Q_LEN = 2048  # new tokens per sequence and step (the reference prefills in 
 _COLD_TOKEN_BYTES = 256 + 16 + 128
 _HOT_TOKEN_BYTES = 1024 + 128
 _ITEM_OVERHEAD_BYTES = 48 * 1024  # query load + rotation + output/partial write
+
+# time model of the persistent schedule (ns, one B200 SM; item timelines of the C3 batch):
+# a full cold tile 3.0 us, a full hot tile 1.9 us, an item's fixed cost (query copy,
+# first tile in flight, rotation back and output or partial write) 7.5 us
+_COLD_TILE_NS = (1200, 1830)  # fixed + per full tile
+_HOT_TILE_NS = (800, 1130)
+_ITEM_NS = 7500
+_MIN_PIECE_NS = 4 * sum(_COLD_TILE_NS)  # a worker does not start a piece of a block below this
 
 
 @dataclass
@@ -72,6 +86,11 @@ class DecodePlan:
     total_q: int
     n_heads: int
     units: np.ndarray = field(default_factory=lambda: np.zeros((0, 2), np.int32))  # [n_units][2] {out_row0, n_rows}
+    workers: np.ndarray | None = None  # [n_workers + 1] item offsets, or None: one CTA per item
+
+    @property
+    def n_workers(self) -> int:
+        return 0 if self.workers is None else int(self.workers.shape[0]) - 1
 
     @property
     def n_units(self) -> int:
@@ -111,6 +130,69 @@ def _tile_cost(kind: int, n: int) -> int:
     return n * (_COLD_TOKEN_BYTES if kind == _lib.TILE_COLD else _HOT_TOKEN_BYTES)
 
 
+def _tile_ns(kind: int, n: int) -> int:
+    if kind == _lib.TILE_COLD:
+        return _COLD_TILE_NS[0] + (_COLD_TILE_NS[1] * n) // COLD_TILE
+    return _HOT_TILE_NS[0] + (_HOT_TILE_NS[1] * n) // HOT_TILE
+
+
+def _greedy_cut(units, P, T: int, limit: int):
+    """Fill workers in order with contiguous pieces of the units' tile ranges, each
+    worker up to T ns (an item costs _ITEM_NS on top of its tiles).  A unit is cut
+    only into pieces of at least _MIN_PIECE_NS.  Returns the pieces
+    [(unit, a, b, worker)] or None when more than `limit` workers are needed."""
+    pieces = []
+    w, load = 0, 0
+
+    def next_worker():
+        nonlocal w, load
+        w, load = w + 1, 0
+        return w < limit
+
+    for ui, t0, t1 in units:
+        a = t0
+        while a < t1:
+            rest = P[t1] - P[a]
+            room = T - load - _ITEM_NS
+            if rest <= room or (rest < 2 * _MIN_PIECE_NS and load == 0):
+                pieces.append((ui, a, t1, w))  # the rest fits, or cannot be cut and the worker is empty
+                load += _ITEM_NS + rest
+                break
+            if rest < 2 * _MIN_PIECE_NS or room < _MIN_PIECE_NS:
+                if load > 0:
+                    if not next_worker():
+                        return None
+                    continue
+                room = _MIN_PIECE_NS
+            b = bisect.bisect_right(P, P[a] + room, a + 1, t1 + 1) - 1
+            if P[t1] - P[b] < _MIN_PIECE_NS:  # leave the next worker a piece of useful size
+                b = bisect.bisect_right(P, P[t1] - _MIN_PIECE_NS, a + 1, t1 + 1) - 1
+            b = min(max(b, a + 1), t1)
+            pieces.append((ui, a, b, w))
+            load += _ITEM_NS + P[b] - P[a]
+            a = b
+            if a < t1 and not next_worker():
+                return None
+    return pieces
+
+
+def _balanced_cut(units, P, n_workers: int):
+    """Smallest per-worker time T (binary search) for which the greedy cut fits."""
+    total = int(sum(P[t1] - P[t0] for _, t0, t1 in units)) + _ITEM_NS * len(units)
+    longest_tile = int(np.diff(np.asarray(P)).max()) if len(P) > 1 else 0
+    lo = max(total // n_workers, _ITEM_NS + longest_tile) - 1
+    hi = total + _ITEM_NS * (n_workers + len(units)) + int(P[-1])
+    best = _greedy_cut(units, P, hi, n_workers)
+    while hi - lo > 1000:  # 1 us resolution
+        mid = (lo + hi) // 2
+        got = _greedy_cut(units, P, mid, n_workers)
+        if got is None:
+            lo = mid
+        else:
+            hi, best = mid, got
+    return best
+
+
 def build_plan(
     seqs: list[SequenceLayout],
     n_heads: int,
@@ -120,9 +202,15 @@ def build_plan(
     waves: float = 3.0,
     max_items_per_seq: int | None = None,
     force_partial: bool = False,
+    persistent: bool = True,
 ) -> DecodePlan:
-    """Cut the batch into balanced work items (longest first).
+    """Cut the batch into balanced work items.
 
+    ``persistent`` (default): ``n_sms * ctas_per_sm`` workers, each a contiguous share
+    of the query blocks' tiles of equal estimated time (``waves`` is not used); with
+    ``max_items_per_seq`` the blocks are first cut as below and the items dealt to the
+    workers longest first.  ``persistent=False``: one CTA per item, about
+    ``waves`` items per SM, longest first.
     ``force_partial``: every (sequence, row block) writes partial records and gets
     a combine job, even when one item covers it (context-parallel decode merges
     these records across ranks).
@@ -158,19 +246,53 @@ def build_plan(
             c = int(prefix[t1] - prefix[t0])
             units.append((si, rb, t0, t1, c))
             total_cost += c
+    n_workers = max(1, int(n_sms * ctas_per_sm))
+    unit_rows = []
+    for si, rb, t0, t1, c in units:
+        seq = seqs[si]
+        rows = seq.q_len * n_heads
+        unit_rows.append((seq.q_start * n_heads + rb * ROWS_PER_BLOCK, min(ROWS_PER_BLOCK, rows - rb * ROWS_PER_BLOCK)))
+    unit_arr = np.asarray(unit_rows, dtype=np.int32).reshape(-1, 2)
+
+    if persistent and max_items_per_seq is None:
+        tns = np.array([_tile_ns(k, n) for k, _, _, n in tiles], dtype=np.int64)
+        P = np.concatenate(([0], np.cumsum(tns))).tolist()
+        work = [(ui, t0, t1) for ui, (_, _, t0, t1, _) in enumerate(units) if t1 > t0]
+        pieces = _balanced_cut(work, P, n_workers) if work else []
+        by_unit: dict[int, list] = {}
+        for ui, a, b, w in pieces:
+            by_unit.setdefault(ui, []).append((a, b, w))
+        items, combine, n_slots = [], [], 0
+        for ui, (si, rb, t0, t1, c) in enumerate(units):
+            out_row0, n_rows = unit_rows[ui]
+            q_len = seqs[si].q_len
+            segs = by_unit.get(ui, [(t0, t1, 0)])  # a block with no visible tile: one empty item
+            if len(segs) == 1 and not force_partial:
+                a, b, w = segs[0]
+                items.append((w, a, (ui, rb, a, b, -1, out_row0, n_rows, q_len)))
+                continue
+            s0 = n_slots
+            for a, b, w in segs:
+                items.append((w, a, (ui, rb, a, b, n_slots, out_row0, n_rows, q_len)))
+                n_slots += 1
+            combine.append((s0, n_slots, out_row0, n_rows))
+        items.sort(key=lambda x: (x[0], x[1]))
+        item_arr = np.asarray([it[2] for it in items], dtype=np.int32).reshape(-1, 8)
+        used = max((it[0] for it in items), default=-1) + 1
+        counts = np.bincount(np.asarray([it[0] for it in items], dtype=np.int64), minlength=used)
+        workers = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
+        comb_arr = np.asarray(combine, dtype=np.int32).reshape(-1, 4)
+        return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, workers)
+
     slots_target = max(1, int(n_sms * ctas_per_sm * waves))
     item_cost = max(total_cost / slots_target, 4 * COLD_TILE * _COLD_TOKEN_BYTES)
 
     items = []
     combine = []
-    unit_rows = []
     n_slots = 0
     for ui, (si, rb, t0, t1, c) in enumerate(units):
         seq = seqs[si]
-        rows = seq.q_len * n_heads
-        out_row0 = seq.q_start * n_heads + rb * ROWS_PER_BLOCK
-        n_rows = min(ROWS_PER_BLOCK, rows - rb * ROWS_PER_BLOCK)
-        unit_rows.append((out_row0, n_rows))
+        out_row0, n_rows = unit_rows[ui]
         k = max(1, int(np.ceil((c + _ITEM_OVERHEAD_BYTES) / (item_cost + _ITEM_OVERHEAD_BYTES))))
         # one row block never needs more items than can run at once
         k = min(k, t1 - t0, max(1, int(n_sms * ctas_per_sm)))
@@ -193,5 +315,19 @@ def build_plan(
     items.sort(key=lambda it: -it[8])
     item_arr = np.asarray([it[:8] for it in items], dtype=np.int32).reshape(-1, 8)
     comb_arr = np.asarray(combine, dtype=np.int32).reshape(-1, 4)
-    unit_arr = np.asarray(unit_rows, dtype=np.int32).reshape(-1, 2)
-    return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr)
+    if not persistent or not items:
+        return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr)
+    # deal the items (longest first) to the least loaded of the workers
+    tns = np.array([_tile_ns(k, n) for k, _, _, n in tiles], dtype=np.int64)
+    P = np.concatenate(([0], np.cumsum(tns)))
+    heap = [(0, w) for w in range(min(n_workers, len(items)))]
+    owner = []
+    for it in item_arr:
+        load, w = heapq.heappop(heap)
+        owner.append(w)
+        heapq.heappush(heap, (load + _ITEM_NS + int(P[it[3]] - P[it[2]]), w))
+    order = np.argsort(np.asarray(owner), kind="stable")
+    item_arr = item_arr[order]
+    counts = np.bincount(np.asarray(owner), minlength=len(heap))
+    workers = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
+    return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, workers)

@@ -195,6 +195,10 @@ ASTERQ_DEVICE void cp_async_wait() {
 ASTERQ_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
 }
+// an initialized mbarrier is invalidated before its slot is initialized again
+ASTERQ_DEVICE void mbar_inval(uint32_t bar) {
+  asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
 ASTERQ_DEVICE void mbar_expect_tx(uint32_t bar, uint32_t tx) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(tx) : "memory");
 }

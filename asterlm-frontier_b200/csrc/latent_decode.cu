@@ -365,17 +365,37 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar = [&](int i) { return smem_u32(bars + i); };
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, gid = lane >> 2, tq = lane & 3;
-  const int* itm = p.items + 8 * (int64_t)blockIdx.x;
-  const int rb = itm[1];
-  const int tile_begin = max(itm[2], 0);
-  const int tile_end = max(min(itm[3], p.n_tiles), tile_begin);
-  const int slot = (itm[4] < p.n_slots) ? itm[4] : -2;  // -2: out-of-range slot, write nothing
-  const int64_t out_row0 = itm[5];
-  const int n_rows = min(itm[6], kRows);
   const int H = p.n_heads;
-  const int n_t = tile_end - tile_begin;
+  // This CTA's work items: one (item blockIdx.x) without a worker table, else the
+  // contiguous range workers[blockIdx.x] .. workers[blockIdx.x + 1], run one after another.
+  int it_begin = blockIdx.x, it_end = blockIdx.x + 1;
+  if (p.workers != nullptr) {
+    it_begin = max(p.workers[blockIdx.x], 0);
+    it_end = min(p.workers[blockIdx.x + 1], p.n_items);
+  }
+  // fields of the current item (begin_item)
+  const int* itm = p.items;
+  int rb = 0, tile_begin = 0, slot = -2, n_rows = 0, n_t = 0;
+  int64_t out_row0 = 0;
+  auto begin_item = [&](int it) {
+    itm = p.items + 8 * (int64_t)it;
+    rb = itm[1];
+    tile_begin = max(itm[2], 0);
+    const int tile_end = max(min(itm[3], p.n_tiles), tile_begin);
+    slot = (itm[4] < p.n_slots) ? itm[4] : -2;  // -2: out-of-range slot, write nothing
+    out_row0 = itm[5];
+    n_rows = min(itm[6], kRows);
+    n_t = tile_end - tile_begin;
+  };
 
-  if (tid == 0) {
+  // every item starts from freshly initialized barriers (the previous item's are
+  // quiescent: each of its copies was waited for before the CTA-wide barrier)
+  auto init_barriers = [&](bool again) {
+    if (again) {
+#pragma unroll 1
+      for (int k = 0; k <= kBarM; ++k)
+        if (k != kBarAbort) mbar_inval(bar(k));
+    }
     for (int s = 0; s < kStages; ++s) {
       mbar_init(bar(kBarEmpty + s), 32 * (kTeamWarps + kValueWarps));
     }
@@ -388,8 +408,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(bar(kBarM), 32 * kTeamWarps);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
+  };
+  if (tid == 0) init_barriers(false);
   __syncthreads();
+  // between two items: the previous epilogue is done everywhere, then thread 0 resets the barriers
+  auto next_item_sync = [&]() {
+    named_sync(0, kThreads);
+    if (tid == 0) init_barriers(true);
+    named_sync(0, kThreads);
+  };
 
   // ---------------- producer: issue one tile into its stage ----------------
   auto issue_tile = [&](int j, const Tile t) {
@@ -418,29 +445,68 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   };
   auto issue = [&](int j) { issue_tile(j, load_tile(p, tile_begin + j)); };
-  if (warp == kProducerWarp) {
-    if (lane == 0)
-      for (int j = 0; j < min(n_t, kStages - 1); ++j) issue(j);
-    __syncwarp();
-  }
+  // ---------------- prologue (producer lane): first tiles and the prepared query ----------------
+  // (qprep_kernel wrote the query operands to the workspace: int8 limb fragments, hot and
+  // RoPE bf16 fragments, per-row scalars, laid out like their shared-memory regions)
+  auto prologue = [&]() {
+    for (int j = 0; j < min(n_t, kStages - 1); ++j) issue(j);
+    const uint8_t* src = reinterpret_cast<const uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes +
+                         (int64_t)max(itm[0], 0) * kQPrepBytes;
+    const uint32_t qb = bar(kBarQ);
+    mbar_expect_tx(qb, kQPrepCopyBytes);
+    bulk_1d(sbase + kOffQi, src, 16384, qb);
+    bulk_1d(sbase + kOffQh, src + 16384, 16384, qb);
+    bulk_1d(sbase + kOffQr, src + 32768, 2048, qb);
+    bulk_1d(sbase + kOffMisc + 4 * kMQscale, src + 34816, 4 * kQScalars, qb);
+    if (n_t > kStages - 1) issue(kStages - 1);
+  };
 
-  // ---------------- prologue: this row block's prepared query operands ----------------
-  // (qprep_kernel wrote them to the workspace: int8 limb fragments, hot and RoPE bf16
-  // fragments, per-row scalars, laid out like their shared-memory regions)
-  if (warp == kProducerWarp) {
-    if (lane == 0) {
-      const uint8_t* src = reinterpret_cast<const uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes +
-                           (int64_t)max(itm[0], 0) * kQPrepBytes;
-      const uint32_t qb = bar(kBarQ);
-      mbar_expect_tx(qb, kQPrepCopyBytes);
-      bulk_1d(sbase + kOffQi, src, 16384, qb);
-      bulk_1d(sbase + kOffQh, src + 16384, 16384, qb);
-      bulk_1d(sbase + kOffQr, src + 32768, 2048, qb);
-      bulk_1d(sbase + kOffMisc + 4 * kMQscale, src + 34816, 4 * kQScalars, qb);
-      if (n_t > kStages - 1) issue(kStages - 1);
+  // ---------------- epilogue: normalize or write the partial record ----------------
+  // (after a CTA-wide barrier; returns true when a wait of this item timed out: the CTA
+  // then records the failure and stops)
+  auto epilogue = [&]() -> bool {
+    const float* O = reinterpret_cast<const float*>(smem + kOffQi);
+    const float* lw = misc + kMLw;
+    const float* mrow = misc + kMWmax;
+    if (slot == -1) {
+      for (int e = tid; e < kRows * kL / 4; e += kThreads) {
+        const int r = e >> 7, c4 = e & 127;
+        if (r >= n_rows) continue;
+        float l = 0.0f;
+#pragma unroll
+        for (int w2 = 0; w2 < kScoreWarps; ++w2) l += lw[16 * w2 + r];
+        const float inv = 1.0f / fmaxf(l, 1e-20f);
+        const float4 v = *reinterpret_cast<const float4*>(O + r * kL + 4 * c4);
+        const int64_t off = (out_row0 + r) * kL + 4 * c4;
+        if (p.out_dtype == ASTERQ_DTYPE_F32) {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) =
+              make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
+        } else {
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + off) =
+              make_uint2(pack_bf162(v.x * inv, v.y * inv), pack_bf162(v.z * inv, v.w * inv));
+        }
+      }
+    } else if (slot >= 0) {
+      float* wo = reinterpret_cast<float*>(p.workspace);
+      float* wm = wo + (int64_t)p.n_slots * kRows * kL;
+      float* wl = wm + (int64_t)p.n_slots * kRows;
+      for (int e = tid; e < kRows * kL / 4; e += kThreads) {
+        const int r = e >> 7, c4 = e & 127;
+        *reinterpret_cast<float4*>(wo + ((int64_t)slot * kRows + r) * kL + 4 * c4) =
+            *reinterpret_cast<const float4*>(O + r * kL + 4 * c4);
+      }
+      if (tid < kRows) {
+        wm[(int64_t)slot * kRows + tid] = mrow[tid];
+        float l = 0.0f;
+#pragma unroll
+        for (int w2 = 0; w2 < kScoreWarps; ++w2) l += lw[16 * w2 + tid];
+        wl[(int64_t)slot * kRows + tid] = l;
+      }
     }
-    __syncwarp();
-  }
+    const bool stop = *abort_flag != 0;
+    if (tid == 0 && stop && p.device_status) atomicExch(p.device_status, 1);
+    return stop;
+  };
 
   if (warp < kScoreWarps) {
     // =====================================================================
@@ -449,334 +515,341 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kScoreRegs));
     // team `team` takes tiles team, team + 2, ...; tw is the warp's index in its team
     const int team = warp / kTeamWarps, tw = warp % kTeamWarps;
-    mbar_wait(bar(kBarQ), 0, abort_flag);
-    const uint2* qh = reinterpret_cast<const uint2*>(smem + kOffQh);
-    const uint2* qr = reinterpret_cast<const uint2*>(smem + kOffQr);
-    float qinv[2][2], qinvi[2][2], rratio[2][2];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        qinv[nt][cc] = misc[kMQinv + 8 * nt + 2 * tq + cc];
-        qinvi[nt][cc] = misc[kMQinvI + 8 * nt + 2 * tq + cc];
-        rratio[nt][cc] = misc[kMRopeR + 8 * nt + 2 * tq + cc];
-      }
-    // Softmax state of rows 8nt + 2tq + cc, replicated across the 8 gid lanes.  The running
-    // max is one chain over all tiles: the team of tile i reads the max after tile i - 1
-    // from the other team (kBarM phase i - 1) and publishes its own (phase i), so one team's
-    // QK of its next tile overlaps the other team's softmax.  Each team sums its own tiles'
-    // p relative to the max after its latest tile (m_team); both sums are brought to the
-    // final max at the end.
-    float m_team[2][2], l_w[2][2];
-#pragma unroll
-    for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        m_team[nt][cc] = -INFINITY;
-        l_w[nt][cc] = 0.0f;
-      }
-
-    Tile t_next = (team < n_t) ? load_tile(p, tile_begin + team) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
-    int4 raw_next = (team + 2 < n_t) ? fetch_tile(p, tile_begin + team + 2) : make_int4(0, 0, 0, 0);
 #pragma unroll 1
-    for (int i = team; i < n_t; i += 2) {
-      const int s = i % kStages, b = i & 1;
-      const Tile t = t_next;
-      // descriptors: this team's next tile checked (fetched a tile ago), the one after fetched
-      if (i + 2 < n_t) t_next = check_tile(p, raw_next);
-      if (i + 4 < n_t) raw_next = fetch_tile(p, tile_begin + i + 4);
-      mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);
-      const uint8_t* st = smem + s * kStageBytes;
-      const uint32_t sst = sbase + s * kStageBytes;
-      const bool cold = t.kind == ASTERQ_TILE_COLD;
-      float S[2][2][4];
+    for (int it = it_begin; it < it_end; ++it) {
+      begin_item(it);
+      if (it > it_begin) next_item_sync();
+      mbar_wait(bar(kBarQ), 0, abort_flag);
+      const uint2* qh = reinterpret_cast<const uint2*>(smem + kOffQh);
+      const uint2* qr = reinterpret_cast<const uint2*>(smem + kOffQr);
+      float qinv[2][2], qinvi[2][2], rratio[2][2];
 #pragma unroll
-      for (int m = 0; m < 2; ++m)
+      for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) S[m][nt][c] = 0.0f;
-
-      if (cold) {
-        int tok[2][2];
-#pragma unroll
-        for (int m = 0; m < 2; ++m)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(tw, m, gid + 8 * h);
-        const __half* scl = reinterpret_cast<const __half*>(st + kScales);
-        // RoPE channel first (bf16, exact products), moved into the integer-score units
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-          const int row = qk_token(tw, m, (lane & 7) + 8 * ((lane >> 3) & 1));
-#pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            uint32_t a[4];
-            ldmatrix_x4(a, sst + kCRope + swz(row, 2 * ks + (lane >> 4)));
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
-              mma_bf16(S[m][nt], a, bq.x, bq.y);
-            }
-          }
+        for (int cc = 0; cc < 2; ++cc) {
+          qinv[nt][cc] = misc[kMQinv + 8 * nt + 2 * tq + cc];
+          qinvi[nt][cc] = misc[kMQinvI + 8 * nt + 2 * tq + cc];
+          rratio[nt][cc] = misc[kMRopeR + 8 * nt + 2 * tq + cc];
         }
+      // Softmax state of rows 8nt + 2tq + cc, replicated across the 8 gid lanes.  The running
+      // max is one chain over all tiles: the team of tile i reads the max after tile i - 1
+      // from the other team (kBarM phase i - 1) and publishes its own (phase i), so one team's
+      // QK of its next tile overlaps the other team's softmax.  Each team sums its own tiles'
+      // p relative to the max after its latest tile (m_team); both sums are brought to the
+      // final max at the end.
+      float m_team[2][2], l_w[2][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          m_team[nt][cc] = -INFINITY;
+          l_w[nt][cc] = 0.0f;
+        }
+
+      Tile t_next = (team < n_t) ? load_tile(p, tile_begin + team) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
+      int4 raw_next = (team + 2 < n_t) ? fetch_tile(p, tile_begin + team + 2) : make_int4(0, 0, 0, 0);
+#pragma unroll 1
+      for (int i = team; i < n_t; i += 2) {
+        const int s = i % kStages, b = i & 1;
+        const Tile t = t_next;
+        // descriptors: this team's next tile checked (fetched a tile ago), the one after fetched
+        if (i + 2 < n_t) t_next = check_tile(p, raw_next);
+        if (i + 4 < n_t) raw_next = fetch_tile(p, tile_begin + i + 4);
+        mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);
+        const uint8_t* st = smem + s * kStageBytes;
+        const uint32_t sst = sbase + s * kStageBytes;
+        const bool cold = t.kind == ASTERQ_TILE_COLD;
+        float S[2][2][4];
 #pragma unroll
         for (int m = 0; m < 2; ++m)
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
-        const uint4* qi = reinterpret_cast<const uint4*>(smem + kOffQi);
-        // Group g's integer dot products (two int8 limbs of the query, both k-steps):
-        // loads, code expansion and 16 MMAs into acc.
-        auto qk_issue = [&](int g, int (&acc)[2][2][2][4]) {
-          // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens
-          const int region = (g < 4) ? kCodesLo : kCodesHi;
-          const int chunk = 2 * (g & 3) + (tq >> 1);
-          uint2 v[2][2];
+            for (int c = 0; c < 4; ++c) S[m][nt][c] = 0.0f;
+
+        if (cold) {
+          int tok[2][2];
 #pragma unroll
           for (int m = 0; m < 2; ++m)
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
-              v[m][h] = *reinterpret_cast<const uint2*>(st + region + swz(tok[m][h], chunk) + 8 * (tq & 1));
+            for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(tw, m, gid + 8 * h);
+          const __half* scl = reinterpret_cast<const __half*>(st + kScales);
+          // RoPE channel first (bf16, exact products), moved into the integer-score units
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
+          for (int m = 0; m < 2; ++m) {
+            const int row = qk_token(tw, m, (lane & 7) + 8 * ((lane >> 3) & 1));
 #pragma unroll
-            for (int m = 0; m < 2; ++m) {
-              const uint32_t x0 = j ? v[m][0].y : v[m][0].x, x1 = j ? v[m][1].y : v[m][1].x;
-              const uint32_t a[4] = {s8_lo_nibbles(x0), s8_lo_nibbles(x1), s8_hi_nibbles(x0), s8_hi_nibbles(x1)};
+            for (int ks = 0; ks < 4; ++ks) {
+              uint32_t a[4];
+              ldmatrix_x4(a, sst + kCRope + swz(row, 2 * ks + (lane >> 4)));
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) {
-                if (j == 0) {
-                  mma_s8_from(acc[0][m][nt], a, bq[nt].x, bq[nt].y, kAccBias);
-                  mma_s8_from(acc[1][m][nt], a, bq[nt].z, bq[nt].w, kAccBias);
-                } else {
-                  mma_s8(acc[0][m][nt], a, bq[nt].x, bq[nt].y);
-                  mma_s8(acc[1][m][nt], a, bq[nt].z, bq[nt].w);
-                }
+                const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
+                mma_bf16(S[m][nt], a, bq.x, bq.y);
               }
             }
           }
-        };
-        // S += scale_g x (256 hi + lo), the biased accumulators read as exact floats
-        // (packed f32x2 arithmetic: two accumulator elements per instruction; elements
-        // c = 0,1 belong to token row gid, c = 2,3 to row gid + 8)
-        auto qk_finish = [&](int g, const int (&acc)[2][2][2][4]) {
-          const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
 #pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const float s0 = __half2float(scl[8 * tok[m][0] + g]);
-            const float s1 = __half2float(scl[8 * tok[m][1] + g]);
+          for (int m = 0; m < 2; ++m)
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float2 fh = add2(make_float2(__int_as_float(acc[0][m][nt][2 * h]), __int_as_float(acc[0][m][nt][2 * h + 1])), bias2);
-                const float2 fl = add2(make_float2(__int_as_float(acc[1][m][nt][2 * h]), __int_as_float(acc[1][m][nt][2 * h + 1])), bias2);
-                const float sc = h ? s1 : s0;
-                const float2 r = fma2(fma2(fh, k256, fl), make_float2(sc, sc),
-                                      make_float2(S[m][nt][2 * h], S[m][nt][2 * h + 1]));
-                S[m][nt][2 * h] = r.x;
-                S[m][nt][2 * h + 1] = r.y;
+              for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
+          const uint4* qi = reinterpret_cast<const uint4*>(smem + kOffQi);
+          // Group g's integer dot products (two int8 limbs of the query, both k-steps):
+          // loads, code expansion and 16 MMAs into acc.
+          auto qk_issue = [&](int g, int (&acc)[2][2][2][4]) {
+            // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens
+            const int region = (g < 4) ? kCodesLo : kCodesHi;
+            const int chunk = 2 * (g & 3) + (tq >> 1);
+            uint2 v[2][2];
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                v[m][h] = *reinterpret_cast<const uint2*>(st + region + swz(tok[m][h], chunk) + 8 * (tq & 1));
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
+#pragma unroll
+              for (int m = 0; m < 2; ++m) {
+                const uint32_t x0 = j ? v[m][0].y : v[m][0].x, x1 = j ? v[m][1].y : v[m][1].x;
+                const uint32_t a[4] = {s8_lo_nibbles(x0), s8_lo_nibbles(x1), s8_hi_nibbles(x0), s8_hi_nibbles(x1)};
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                  if (j == 0) {
+                    mma_s8_from(acc[0][m][nt], a, bq[nt].x, bq[nt].y, kAccBias);
+                    mma_s8_from(acc[1][m][nt], a, bq[nt].z, bq[nt].w, kAccBias);
+                  } else {
+                    mma_s8(acc[0][m][nt], a, bq[nt].x, bq[nt].y);
+                    mma_s8(acc[1][m][nt], a, bq[nt].z, bq[nt].w);
+                  }
+                }
               }
+            }
+          };
+          // S += scale_g x (256 hi + lo), the biased accumulators read as exact floats
+          // (packed f32x2 arithmetic: two accumulator elements per instruction; elements
+          // c = 0,1 belong to token row gid, c = 2,3 to row gid + 8)
+          auto qk_finish = [&](int g, const int (&acc)[2][2][2][4]) {
+            const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+              const float s0 = __half2float(scl[8 * tok[m][0] + g]);
+              const float s1 = __half2float(scl[8 * tok[m][1] + g]);
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float2 fh = add2(make_float2(__int_as_float(acc[0][m][nt][2 * h]), __int_as_float(acc[0][m][nt][2 * h + 1])), bias2);
+                  const float2 fl = add2(make_float2(__int_as_float(acc[1][m][nt][2 * h]), __int_as_float(acc[1][m][nt][2 * h + 1])), bias2);
+                  const float sc = h ? s1 : s0;
+                  const float2 r = fma2(fma2(fh, k256, fl), make_float2(sc, sc),
+                                        make_float2(S[m][nt][2 * h], S[m][nt][2 * h + 1]));
+                  S[m][nt][2 * h] = r.x;
+                  S[m][nt][2 * h + 1] = r.y;
+                }
+            }
+          };
+          // two groups in flight: group g + 1's MMAs run on the tensor pipe while
+          // group g's accumulators are scaled into S
+          int accA[2][2][2][4], accB[2][2][2][4];
+          qk_issue(0, accA);
+#pragma unroll 1
+          for (int g = 0; g < 8; g += 2) {
+            qk_issue(g + 1, accB);
+            qk_finish(g, accA);
+            if (g + 2 < 8) qk_issue(g + 2, accA);
+            qk_finish(g + 1, accB);
           }
-        };
-        // two groups in flight: group g + 1's MMAs run on the tensor pipe while
-        // group g's accumulators are scaled into S
-        int accA[2][2][2][4], accB[2][2][2][4];
-        qk_issue(0, accA);
+        } else {
+          // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
+          // S[1] is a second partial accumulator (odd groups) folded in below
+          const int row = 8 * tw + (lane & 7);
 #pragma unroll 1
-        for (int g = 0; g < 8; g += 2) {
-          qk_issue(g + 1, accB);
-          qk_finish(g, accA);
-          if (g + 2 < 8) qk_issue(g + 2, accA);
-          qk_finish(g + 1, accB);
-        }
-      } else {
-        // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
-        // S[1] is a second partial accumulator (odd groups) folded in below
-        const int row = 8 * tw + (lane & 7);
-#pragma unroll 1
-        for (int g = 0; g < 8; g += 2) {
+          for (int g = 0; g < 8; g += 2) {
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              uint32_t a[2][4];
+              ldmatrix_x4(a[0], sst + g * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+              ldmatrix_x4(a[1], sst + (g + 1) * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                  const uint2 bq = qh[(((g + h2) * 4 + ks) * 2 + nt) * 32 + lane];
+                  mma_bf16(S[h2][nt], a[h2], bq.x, bq.y);
+                }
+            }
+          }
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              S[0][nt][c] += S[1][nt][c];
+              S[1][nt][c] = 0.0f;
+            }
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
-            uint32_t a[2][4];
-            ldmatrix_x4(a[0], sst + g * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
-            ldmatrix_x4(a[1], sst + (g + 1) * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+            uint32_t a[4];
+            ldmatrix_x4(a, sst + kHRope + swz(row, 2 * ks + (lane >> 4)));
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2)
+            for (int nt = 0; nt < 2; ++nt) {
+              const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
+              mma_bf16(S[0][nt], a, bq.x, bq.y);
+            }
+          }
+        }
+
+        // ---- finalize scores, mask, tile max ----
+        const int n_m = cold ? 2 : 1;
+        float tmax[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) tmax[nt][cc] = -INFINITY;
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int h = c >> 1, cc = c & 1;
+              const int r = 8 * nt + 2 * tq + cc;
+              const int tk = cold ? qk_token(tw, m, gid + 8 * h) : 8 * tw + gid;
+              bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
+              if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
+              float sv = S[m][nt][c] * (cold ? qinvi[nt][cc] : qinv[nt][cc]);
+              if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
+              sv = valid ? sv : -INFINITY;
+              S[m][nt][c] = sv;
+              tmax[nt][cc] = fmaxf(tmax[nt][cc], sv);
+            }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc)
+#pragma unroll
+            for (int off = 4; off < 32; off <<= 1)
+              tmax[nt][cc] = fmaxf(tmax[nt][cc], __shfl_xor_sync(0xffffffffu, tmax[nt][cc], off));
+        float* wmax = misc + kMWmax + team * 128 + ((i >> 1) & 1) * 64;
+        if (gid == 0) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) wmax[tw * 16 + 8 * nt + 2 * tq + cc] = tmax[nt][cc];
+        }
+        named_sync(1 + team, 32 * kTeamWarps);
+        // the running max before this tile, published by the other team
+        if (i > 0) mbar_wait(bar(kBarM), (i - 1) & 1, abort_flag);
+        const float* m_in = misc + kMMrun + ((i - 1) & 1) * 16;
+        float alpha_r[2][2], msub[2][2], lfac[2][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int cc = 0; cc < 2; ++cc) {
+            const int r = 8 * nt + 2 * tq + cc;
+            const float mt = fmaxf(fmaxf(wmax[r], wmax[16 + r]), fmaxf(wmax[32 + r], wmax[48 + r]));
+            const float m_prev = (i > 0) ? m_in[r] : -INFINITY;
+            const float m_new = fmaxf(m_prev, mt);
+            if (m_new == -INFINITY) {
+              alpha_r[nt][cc] = 1.0f;
+              msub[nt][cc] = 0.0f;
+            } else {
+              alpha_r[nt][cc] = exp2f((m_prev - m_new) * kLog2e);
+              msub[nt][cc] = m_new;
+            }
+            lfac[nt][cc] = (m_team[nt][cc] == -INFINITY) ? 0.0f : exp2f((m_team[nt][cc] - m_new) * kLog2e);
+            m_team[nt][cc] = m_new;
+          }
+        // publish the running max after tile i (lanes gid 0 of the team's first warp hold all
+        // 16 rows).  Every thread of the team arrives once it has read the max before this
+        // tile: the phase completes only then, so the other team cannot overwrite that slot
+        // (with the max after tile i + 1) while a slow warp of this team still reads it.
+        if (tw == 0 && gid == 0) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) misc[kMMrun + (i & 1) * 16 + 8 * nt + 2 * tq + cc] = m_team[nt][cc];
+        }
+        mbar_arrive(bar(kBarM));
+        // ---- p = exp(s - m), handed to the value warps ----
+        if (i >= 2) mbar_wait(bar(kBarPEmpty + b), ((i >> 1) - 1) & 1, abort_flag);
+        float psum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+        if (cold) {
+          // p as fp16 [token][16 rows]; the two 16-byte halves of a token's row swap on every
+          // other group of 4 tokens so that ldmatrix reads of 8 consecutive tokens hit 32 banks
+          uint8_t* Pc = smem + kOffP + b * kPBytes;
+          uint16_t* sT = reinterpret_cast<uint16_t*>(smem + kOffST + b * 2048);
+          const uint16_t* scl = reinterpret_cast<const uint16_t*>(smem + s * kStageBytes + kScales);
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int tk = qk_token(tw, m, gid + 8 * h);
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) {
-                const uint2 bq = qh[(((g + h2) * 4 + ks) * 2 + nt) * 32 + lane];
-                mma_bf16(S[h2][nt], a[h2], bq.x, bq.y);
+                const float p0 = exp2f((S[m][nt][2 * h] - msub[nt][0]) * kLog2e);
+                const float p1 = exp2f((S[m][nt][2 * h + 1] - msub[nt][1]) * kLog2e);
+                psum[nt][0] += p0;
+                psum[nt][1] += p1;
+                *reinterpret_cast<uint32_t*>(Pc + tk * 32 + ((nt ^ ((tk >> 2) & 1)) << 4) + 4 * tq) = pack_half2(p0, p1);
               }
-          }
+              // lane tq publishes groups 2tq and 2tq + 1 of this token's code scales (0 outside the tile)
+              const bool ok = tk < t.n;
+#pragma unroll
+              for (int u = 0; u < 2; ++u) {
+                const int g = 2 * tq + u;
+                sT[g * kColdTile + tk] = ok ? scl[8 * tk + g] : (uint16_t)0;
+              }
+            }
+        } else {
+          float* P = reinterpret_cast<float*>(smem + kOffP + b * kPBytes);
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const float pv = exp2f((S[0][nt][c] - msub[nt][c]) * kLog2e);
+              P[(8 * nt + 2 * tq + c) * kPStride + 8 * tw + gid] = pv;
+              psum[nt][c] += pv;
+            }
         }
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            S[0][nt][c] += S[1][nt][c];
-            S[1][nt][c] = 0.0f;
-          }
+          for (int cc = 0; cc < 2; ++cc) {
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks) {
-          uint32_t a[4];
-          ldmatrix_x4(a, sst + kHRope + swz(row, 2 * ks + (lane >> 4)));
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
-            mma_bf16(S[0][nt], a, bq.x, bq.y);
+            for (int off = 4; off < 32; off <<= 1) psum[nt][cc] += __shfl_xor_sync(0xffffffffu, psum[nt][cc], off);
+            l_w[nt][cc] = l_w[nt][cc] * lfac[nt][cc] + psum[nt][cc];
           }
+        if (tw == 0 && gid == 0) {
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int cc = 0; cc < 2; ++cc) misc[kMAlpha + b * 16 + 8 * nt + 2 * tq + cc] = alpha_r[nt][cc];
         }
+        mbar_arrive(bar(kBarPFull + b));
+        mbar_arrive(bar(kBarEmpty + s));
       }
-
-      // ---- finalize scores, mask, tile max ----
-      const int n_m = cold ? 2 : 1;
-      float tmax[2][2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) tmax[nt][cc] = -INFINITY;
-#pragma unroll
-      for (int m = 0; m < 2; ++m)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int h = c >> 1, cc = c & 1;
-            const int r = 8 * nt + 2 * tq + cc;
-            const int tk = cold ? qk_token(tw, m, gid + 8 * h) : 8 * tw + gid;
-            bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
-            if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
-            float sv = S[m][nt][c] * (cold ? qinvi[nt][cc] : qinv[nt][cc]);
-            if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
-            sv = valid ? sv : -INFINITY;
-            S[m][nt][c] = sv;
-            tmax[nt][cc] = fmaxf(tmax[nt][cc], sv);
-          }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc)
-#pragma unroll
-          for (int off = 4; off < 32; off <<= 1)
-            tmax[nt][cc] = fmaxf(tmax[nt][cc], __shfl_xor_sync(0xffffffffu, tmax[nt][cc], off));
-      float* wmax = misc + kMWmax + team * 128 + ((i >> 1) & 1) * 64;
+      // final per-warp sums, brought to the final running max, and the running max itself
+      // (the team that did not take the last tile reads it from the other team: phase n_t - 1)
+      const int last = n_t - 1;
+      if (n_t > 0 && (last & 1) != team) mbar_wait(bar(kBarM), last & 1, abort_flag);
+      named_sync(1 + team, 32 * kTeamWarps);
       if (gid == 0) {
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int cc = 0; cc < 2; ++cc) wmax[tw * 16 + 8 * nt + 2 * tq + cc] = tmax[nt][cc];
-      }
-      named_sync(1 + team, 32 * kTeamWarps);
-      // the running max before this tile, published by the other team
-      if (i > 0) mbar_wait(bar(kBarM), (i - 1) & 1, abort_flag);
-      const float* m_in = misc + kMMrun + ((i - 1) & 1) * 16;
-      float alpha_r[2][2], msub[2][2], lfac[2][2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int r = 8 * nt + 2 * tq + cc;
-          const float mt = fmaxf(fmaxf(wmax[r], wmax[16 + r]), fmaxf(wmax[32 + r], wmax[48 + r]));
-          const float m_prev = (i > 0) ? m_in[r] : -INFINITY;
-          const float m_new = fmaxf(m_prev, mt);
-          if (m_new == -INFINITY) {
-            alpha_r[nt][cc] = 1.0f;
-            msub[nt][cc] = 0.0f;
-          } else {
-            alpha_r[nt][cc] = exp2f((m_prev - m_new) * kLog2e);
-            msub[nt][cc] = m_new;
-          }
-          lfac[nt][cc] = (m_team[nt][cc] == -INFINITY) ? 0.0f : exp2f((m_team[nt][cc] - m_new) * kLog2e);
-          m_team[nt][cc] = m_new;
-        }
-      // publish the running max after tile i (lanes gid 0 of the team's first warp hold all
-      // 16 rows).  Every thread of the team arrives once it has read the max before this
-      // tile: the phase completes only then, so the other team cannot overwrite that slot
-      // (with the max after tile i + 1) while a slow warp of this team still reads it.
-      if (tw == 0 && gid == 0) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc) misc[kMMrun + (i & 1) * 16 + 8 * nt + 2 * tq + cc] = m_team[nt][cc];
-      }
-      mbar_arrive(bar(kBarM));
-      // ---- p = exp(s - m), handed to the value warps ----
-      if (i >= 2) mbar_wait(bar(kBarPEmpty + b), ((i >> 1) - 1) & 1, abort_flag);
-      float psum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
-      if (cold) {
-        // p as fp16 [token][16 rows]; the two 16-byte halves of a token's row swap on every
-        // other group of 4 tokens so that ldmatrix reads of 8 consecutive tokens hit 32 banks
-        uint8_t* Pc = smem + kOffP + b * kPBytes;
-        uint16_t* sT = reinterpret_cast<uint16_t*>(smem + kOffST + b * 2048);
-        const uint16_t* scl = reinterpret_cast<const uint16_t*>(smem + s * kStageBytes + kScales);
-#pragma unroll
-        for (int m = 0; m < 2; ++m)
-#pragma unroll
-          for (int h = 0; h < 2; ++h) {
-            const int tk = qk_token(tw, m, gid + 8 * h);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) {
-              const float p0 = exp2f((S[m][nt][2 * h] - msub[nt][0]) * kLog2e);
-              const float p1 = exp2f((S[m][nt][2 * h + 1] - msub[nt][1]) * kLog2e);
-              psum[nt][0] += p0;
-              psum[nt][1] += p1;
-              *reinterpret_cast<uint32_t*>(Pc + tk * 32 + ((nt ^ ((tk >> 2) & 1)) << 4) + 4 * tq) = pack_half2(p0, p1);
-            }
-            // lane tq publishes groups 2tq and 2tq + 1 of this token's code scales (0 outside the tile)
-            const bool ok = tk < t.n;
-#pragma unroll
-            for (int u = 0; u < 2; ++u) {
-              const int g = 2 * tq + u;
-              sT[g * kColdTile + tk] = ok ? scl[8 * tk + g] : (uint16_t)0;
-            }
-          }
-      } else {
-        float* P = reinterpret_cast<float*>(smem + kOffP + b * kPBytes);
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            const float pv = exp2f((S[0][nt][c] - msub[nt][c]) * kLog2e);
-            P[(8 * nt + 2 * tq + c) * kPStride + 8 * tw + gid] = pv;
-            psum[nt][c] += pv;
+          for (int cc = 0; cc < 2; ++cc) {
+            const int r = 8 * nt + 2 * tq + cc;
+            const float m_fin = (n_t > 0) ? misc[kMMrun + (last & 1) * 16 + r] : -INFINITY;
+            const float f = (m_team[nt][cc] == -INFINITY) ? 0.0f : exp2f((m_team[nt][cc] - m_fin) * kLog2e);
+            misc[kMLw + warp * 16 + r] = l_w[nt][cc] * f;
+            if (warp == 0) misc[kMWmax + r] = m_fin;
           }
       }
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-#pragma unroll
-          for (int off = 4; off < 32; off <<= 1) psum[nt][cc] += __shfl_xor_sync(0xffffffffu, psum[nt][cc], off);
-          l_w[nt][cc] = l_w[nt][cc] * lfac[nt][cc] + psum[nt][cc];
-        }
-      if (tw == 0 && gid == 0) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int cc = 0; cc < 2; ++cc) misc[kMAlpha + b * 16 + 8 * nt + 2 * tq + cc] = alpha_r[nt][cc];
-      }
-      mbar_arrive(bar(kBarPFull + b));
-      mbar_arrive(bar(kBarEmpty + s));
-    }
-    // final per-warp sums, brought to the final running max, and the running max itself
-    // (the team that did not take the last tile reads it from the other team: phase n_t - 1)
-    const int last = n_t - 1;
-    if (n_t > 0 && (last & 1) != team) mbar_wait(bar(kBarM), last & 1, abort_flag);
-    named_sync(1 + team, 32 * kTeamWarps);
-    if (gid == 0) {
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int cc = 0; cc < 2; ++cc) {
-          const int r = 8 * nt + 2 * tq + cc;
-          const float m_fin = (n_t > 0) ? misc[kMMrun + (last & 1) * 16 + r] : -INFINITY;
-          const float f = (m_team[nt][cc] == -INFINITY) ? 0.0f : exp2f((m_team[nt][cc] - m_fin) * kLog2e);
-          misc[kMLw + warp * 16 + r] = l_w[nt][cc] * f;
-          if (warp == 0) misc[kMWmax + r] = m_fin;
-        }
+      named_sync(0, kThreads);
+      if (epilogue()) break;
     }
   } else {
     // =====================================================================
@@ -785,227 +858,196 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kValueRegs));
     const int g = warp - kScoreWarps;
     const bool rotated = p.cold_scheme == ASTERQ_SCHEME_HADAMARD_INT4;  // else plain int4: no rotation back
-    float o[4][2][4];
-#pragma unroll
-    for (int a = 0; a < 4; ++a)
-#pragma unroll
-      for (int c = 0; c < 2; ++c)
-#pragma unroll
-        for (int d = 0; d < 4; ++d) o[a][c][d] = 0.0f;
-    // order 0: accumulator holds cold tokens, rotated basis, code-derived row order
-    // order 1: plain basis, natural row order
-    int order = 1;
-    if (n_t > 0) order = (load_tile(p, tile_begin).kind == ASTERQ_TILE_COLD) ? 0 : 1;
-    // [16][512] scratch, usable once the cold query fragments are no longer read
-    float* scratch_o = reinterpret_cast<float*>(smem + kOffQi);
-    const int region = (g < 4) ? kCodesLo : kCodesHi;
-    const int cchunk = 2 * (g & 3) + (gid >> 2);
-
-    auto store_o = [&]() {
-#pragma unroll
-      for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            const int dim = (order == 0) ? 64 * g + 2 * (4 * gid + mi) + (c >> 1) : 64 * g + 16 * mi + gid + 8 * (c >> 1);
-            scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + dim] = o[mi][nt][c];
-          }
-    };
-
-    Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
-    int4 raw_next = (n_t > 1) ? fetch_tile(p, tile_begin + 1) : make_int4(0, 0, 0, 0);
-    // producer lane: raw descriptor of the next tile it will issue
-    int4 praw = (warp == kProducerWarp && lane == 0 && kStages < n_t) ? fetch_tile(p, tile_begin + kStages)
-                                                                         : make_int4(0, 0, 0, 0);
 #pragma unroll 1
-    for (int i = 0; i < n_t; ++i) {
-      const int s = i % kStages, b = i & 1;
-      const Tile t = t_next;
-      if (i + 1 < n_t) t_next = check_tile(p, raw_next);
-      if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
-      mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
-      mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);  // TMA data visible to this warp
-      const uint8_t* st = smem + s * kStageBytes;
-      const uint32_t sst = sbase + s * kStageBytes;
-      const float* P = reinterpret_cast<const float*>(smem + kOffP + b * kPBytes);
-      const bool cold = t.kind == ASTERQ_TILE_COLD;
+    for (int it = it_begin; it < it_end; ++it) {
+      begin_item(it);
+      if (it > it_begin) next_item_sync();
+      if (warp == kProducerWarp) {
+        if (lane == 0) prologue();
+        __syncwarp();
+      }
+      float o[4][2][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+#pragma unroll
+          for (int d = 0; d < 4; ++d) o[a][c][d] = 0.0f;
+      // order 0: accumulator holds cold tokens, rotated basis, code-derived row order
+      // order 1: plain basis, natural row order
+      int order = 1;
+      if (n_t > 0) order = (load_tile(p, tile_begin).kind == ASTERQ_TILE_COLD) ? 0 : 1;
+      // [16][512] scratch, usable once the cold query fragments are no longer read
+      float* scratch_o = reinterpret_cast<float*>(smem + kOffQi);
+      const int region = (g < 4) ? kCodesLo : kCodesHi;
+      const int cchunk = 2 * (g & 3) + (gid >> 2);
 
-      if (!cold && order == 0) {
-        // first hot tile after cold ones: rotate the accumulator back (O = H O_rot)
-        store_o();
-        named_sync(3, 32 * kValueWarps);
-        if (rotated) {
-          warp_fwht_rows(scratch_o, 2 * g, 2, lane);
-          named_sync(3, 32 * kValueWarps);
-        }
-        order = 1;
+      auto store_o = [&]() {
 #pragma unroll
         for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-            for (int c = 0; c < 4; ++c)
-              o[mi][nt][c] = scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + 64 * g + 16 * mi + gid + 8 * (c >> 1)];
-      }
-      {
-        float al[2][2];
+            for (int c = 0; c < 4; ++c) {
+              const int dim = (order == 0) ? 64 * g + 2 * (4 * gid + mi) + (c >> 1) : 64 * g + 16 * mi + gid + 8 * (c >> 1);
+              scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + dim] = o[mi][nt][c];
+            }
+      };
+
+      Tile t_next = (n_t > 0) ? load_tile(p, tile_begin) : Tile{ASTERQ_TILE_HOT, 0, 0, 0};
+      int4 raw_next = (n_t > 1) ? fetch_tile(p, tile_begin + 1) : make_int4(0, 0, 0, 0);
+      // producer lane: raw descriptor of the next tile it will issue
+      int4 praw = (warp == kProducerWarp && lane == 0 && kStages < n_t) ? fetch_tile(p, tile_begin + kStages)
+                                                                           : make_int4(0, 0, 0, 0);
+#pragma unroll 1
+      for (int i = 0; i < n_t; ++i) {
+        const int s = i % kStages, b = i & 1;
+        const Tile t = t_next;
+        if (i + 1 < n_t) t_next = check_tile(p, raw_next);
+        if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
+        mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
+        mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);  // TMA data visible to this warp
+        const uint8_t* st = smem + s * kStageBytes;
+        const uint32_t sst = sbase + s * kStageBytes;
+        const float* P = reinterpret_cast<const float*>(smem + kOffP + b * kPBytes);
+        const bool cold = t.kind == ASTERQ_TILE_COLD;
+
+        if (!cold && order == 0) {
+          // first hot tile after cold ones: rotate the accumulator back (O = H O_rot)
+          store_o();
+          named_sync(3, 32 * kValueWarps);
+          if (rotated) {
+            warp_fwht_rows(scratch_o, 2 * g, 2, lane);
+            named_sync(3, 32 * kValueWarps);
+          }
+          order = 1;
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          al[nt][0] = misc[kMAlpha + b * 16 + 8 * nt + 2 * tq];
-          al[nt][1] = misc[kMAlpha + b * 16 + 8 * nt + 2 * tq + 1];
+          for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int c = 0; c < 4; ++c)
+                o[mi][nt][c] = scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + 64 * g + 16 * mi + gid + 8 * (c >> 1)];
         }
-#pragma unroll
-        for (int mi = 0; mi < 4; ++mi)
+        {
+          float al[2][2];
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
-            o[mi][nt][0] *= al[nt][0];
-            o[mi][nt][1] *= al[nt][1];
-            o[mi][nt][2] *= al[nt][0];
-            o[mi][nt][3] *= al[nt][1];
+            al[nt][0] = misc[kMAlpha + b * 16 + 8 * nt + 2 * tq];
+            al[nt][1] = misc[kMAlpha + b * 16 + 8 * nt + 2 * tq + 1];
           }
-      }
-      if (cold) {
-        const uint32_t pbase = sbase + kOffP + b * kPBytes;
-        const uint16_t* sT = reinterpret_cast<const uint16_t*>(smem + kOffST + b * 2048) + g * kColdTile;
-        const int lt = (lane & 7) + 8 * ((lane >> 3) & 1), lhalf = lane >> 4;
-#pragma unroll 2
-        for (int kt = 0; kt < kColdTile / 16; ++kt) {
-          // tokens 16kt + {2tq, 2tq+1, 2tq+8, 2tq+9} are this lane's k indices
-          const int t0 = 16 * kt + 2 * tq;
-          const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
-          // p B fragments (fp16) of rows 0-7 / 8-15, times the tokens' group-g code scales
-          uint32_t pr[4];
-          {
-            const int tok = 16 * kt + lt;
-            ldmatrix_x4_trans(pr, pbase + tok * 32 + ((lhalf ^ ((tok >> 2) & 1)) << 4));
-          }
-          const uint32_t s01 = *reinterpret_cast<const uint32_t*>(sT + t0);
-          const uint32_t s89 = *reinterpret_cast<const uint32_t*>(sT + t0 + 8);
-          uint32_t pb[2][2];
-          pb[0][0] = hmul2_u32(pr[0], s01);
-          pb[0][1] = hmul2_u32(pr[1], s89);
-          pb[1][0] = hmul2_u32(pr[2], s01);
-          pb[1][1] = hmul2_u32(pr[3], s89);
-          uint32_t x[4];
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            x[j] = *reinterpret_cast<const uint32_t*>(st + region + swz(tk[j], cchunk) + 4 * (gid & 3));
+          for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-          for (int mi = 0; mi < 4; ++mi) {
-            // rows gid / gid+8 of m-tile mi are dims 2(4gid+mi) / 2(4gid+mi)+1 of group g
-            const uint32_t sel =
-                (uint32_t)mi | ((uint32_t)mi << 4) | ((uint32_t)(4 + mi) << 8) | ((uint32_t)(4 + mi) << 12);
-            const uint32_t z01 = prmt(x[0], x[1], sel);
-            const uint32_t z23 = prmt(x[2], x[3], sel);
-            uint32_t a[4];
-            a[0] = nib_lo_f16x2(z01);
-            a[1] = nib_hi_f16x2(z01);
-            a[2] = nib_lo_f16x2(z23);
-            a[3] = nib_hi_f16x2(z23);
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt][0], pb[nt][1]);
-          }
+            for (int nt = 0; nt < 2; ++nt) {
+              o[mi][nt][0] *= al[nt][0];
+              o[mi][nt][1] *= al[nt][1];
+              o[mi][nt][2] *= al[nt][0];
+              o[mi][nt][3] *= al[nt][1];
+            }
         }
-      } else {
-        // rows beyond n hold stale data: zero this warp's latent block there
-        // (p is 0 for them, but 0 x NaN would poison the accumulator)
-        if (t.n < kHotTile) {
-          for (int e = lane; e < (kHotTile - t.n) * 8; e += 32)
-            *reinterpret_cast<uint4*>(smem + s * kStageBytes + g * kHotBlock + (t.n + e / 8) * 128 + (e % 8) * 16) =
-                make_uint4(0u, 0u, 0u, 0u);
+        if (cold) {
+          const uint32_t pbase = sbase + kOffP + b * kPBytes;
+          const uint16_t* sT = reinterpret_cast<const uint16_t*>(smem + kOffST + b * 2048) + g * kColdTile;
+          const int lt = (lane & 7) + 8 * ((lane >> 3) & 1), lhalf = lane >> 4;
+#pragma unroll 2
+          for (int kt = 0; kt < kColdTile / 16; ++kt) {
+            // tokens 16kt + {2tq, 2tq+1, 2tq+8, 2tq+9} are this lane's k indices
+            const int t0 = 16 * kt + 2 * tq;
+            const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
+            // p B fragments (fp16) of rows 0-7 / 8-15, times the tokens' group-g code scales
+            uint32_t pr[4];
+            {
+              const int tok = 16 * kt + lt;
+              ldmatrix_x4_trans(pr, pbase + tok * 32 + ((lhalf ^ ((tok >> 2) & 1)) << 4));
+            }
+            const uint32_t s01 = *reinterpret_cast<const uint32_t*>(sT + t0);
+            const uint32_t s89 = *reinterpret_cast<const uint32_t*>(sT + t0 + 8);
+            uint32_t pb[2][2];
+            pb[0][0] = hmul2_u32(pr[0], s01);
+            pb[0][1] = hmul2_u32(pr[1], s89);
+            pb[1][0] = hmul2_u32(pr[2], s01);
+            pb[1][1] = hmul2_u32(pr[3], s89);
+            uint32_t x[4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              x[j] = *reinterpret_cast<const uint32_t*>(st + region + swz(tk[j], cchunk) + 4 * (gid & 3));
+#pragma unroll
+            for (int mi = 0; mi < 4; ++mi) {
+              // rows gid / gid+8 of m-tile mi are dims 2(4gid+mi) / 2(4gid+mi)+1 of group g
+              const uint32_t sel =
+                  (uint32_t)mi | ((uint32_t)mi << 4) | ((uint32_t)(4 + mi) << 8) | ((uint32_t)(4 + mi) << 12);
+              const uint32_t z01 = prmt(x[0], x[1], sel);
+              const uint32_t z23 = prmt(x[2], x[3], sel);
+              uint32_t a[4];
+              a[0] = nib_lo_f16x2(z01);
+              a[1] = nib_hi_f16x2(z01);
+              a[2] = nib_lo_f16x2(z23);
+              a[3] = nib_hi_f16x2(z23);
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt][0], pb[nt][1]);
+            }
+          }
+        } else {
+          // rows beyond n hold stale data: zero this warp's latent block there
+          // (p is 0 for them, but 0 x NaN would poison the accumulator)
+          if (t.n < kHotTile) {
+            for (int e = lane; e < (kHotTile - t.n) * 8; e += 32)
+              *reinterpret_cast<uint4*>(smem + s * kStageBytes + g * kHotBlock + (t.n + e / 8) * 128 + (e % 8) * 16) =
+                  make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+          }
+#pragma unroll 1
+          for (int kt = 0; kt < kHotTile / 16; ++kt) {
+            uint32_t pb[2][2][2];  // [ntile][hi/lo][b0/b1]
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt) {
+              const float2 p01 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + 16 * kt + 2 * tq);
+              const float2 p89 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + 16 * kt + 2 * tq + 8);
+              const uint32_t h0 = pack_bf162(p01.x, p01.y), h1 = pack_bf162(p89.x, p89.y);
+              const float2 r0 = unpack_bf162(h0), r1 = unpack_bf162(h1);
+              pb[nt][0][0] = h0;
+              pb[nt][0][1] = h1;
+              pb[nt][1][0] = pack_bf162(p01.x - r0.x, p01.y - r0.y);
+              pb[nt][1][1] = pack_bf162(p89.x - r1.x, p89.y - r1.y);
+            }
+            uint32_t a[4][4];
+#pragma unroll
+            for (int mi = 0; mi < 4; ++mi) {
+              const int row = 16 * kt + (lane & 7) + 8 * (lane >> 4);
+              ldmatrix_x4_trans(a[mi], sst + g * kHotBlock + swz(row, 2 * mi + ((lane >> 3) & 1)));
+            }
+#pragma unroll
+            for (int hl = 0; hl < 2; ++hl)
+#pragma unroll
+              for (int mi = 0; mi < 4; ++mi)
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) mma_bf16(o[mi][nt], a[mi], pb[nt][hl][0], pb[nt][hl][1]);
+          }
+          fence_async_shared();  // the zero fill precedes the next TMA write of this stage
+        }
+        mbar_arrive(bar(kBarPEmpty + b));
+        mbar_arrive(bar(kBarEmpty + s));
+        if (warp == kProducerWarp) {
+          // refill this stage with tile i + 3 once every warp has released tile i; its
+          // descriptor was fetched a tile ago, so the issue does not wait on global memory
+          if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag))
+            issue_tile(i + kStages, check_tile(p, praw));
+          if (lane == 0 && i + kStages + 1 < n_t) praw = fetch_tile(p, tile_begin + i + kStages + 1);
           __syncwarp();
         }
-#pragma unroll 1
-        for (int kt = 0; kt < kHotTile / 16; ++kt) {
-          uint32_t pb[2][2][2];  // [ntile][hi/lo][b0/b1]
-#pragma unroll
-          for (int nt = 0; nt < 2; ++nt) {
-            const float2 p01 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + 16 * kt + 2 * tq);
-            const float2 p89 = *reinterpret_cast<const float2*>(P + (8 * nt + gid) * kPStride + 16 * kt + 2 * tq + 8);
-            const uint32_t h0 = pack_bf162(p01.x, p01.y), h1 = pack_bf162(p89.x, p89.y);
-            const float2 r0 = unpack_bf162(h0), r1 = unpack_bf162(h1);
-            pb[nt][0][0] = h0;
-            pb[nt][0][1] = h1;
-            pb[nt][1][0] = pack_bf162(p01.x - r0.x, p01.y - r0.y);
-            pb[nt][1][1] = pack_bf162(p89.x - r1.x, p89.y - r1.y);
-          }
-          uint32_t a[4][4];
-#pragma unroll
-          for (int mi = 0; mi < 4; ++mi) {
-            const int row = 16 * kt + (lane & 7) + 8 * (lane >> 4);
-            ldmatrix_x4_trans(a[mi], sst + g * kHotBlock + swz(row, 2 * mi + ((lane >> 3) & 1)));
-          }
-#pragma unroll
-          for (int hl = 0; hl < 2; ++hl)
-#pragma unroll
-            for (int mi = 0; mi < 4; ++mi)
-#pragma unroll
-              for (int nt = 0; nt < 2; ++nt) mma_bf16(o[mi][nt], a[mi], pb[nt][hl][0], pb[nt][hl][1]);
-        }
-        fence_async_shared();  // the zero fill precedes the next TMA write of this stage
       }
-      mbar_arrive(bar(kBarPEmpty + b));
-      mbar_arrive(bar(kBarEmpty + s));
-      if (warp == kProducerWarp) {
-        // refill this stage with tile i + 3 once every warp has released tile i; its
-        // descriptor was fetched a tile ago, so the issue does not wait on global memory
-        if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag))
-          issue_tile(i + kStages, check_tile(p, praw));
-        if (lane == 0 && i + kStages + 1 < n_t) praw = fetch_tile(p, tile_begin + i + kStages + 1);
-        __syncwarp();
-      }
-    }
-    // accumulator -> scratch in natural order, rotated back if it is still rotated
-    store_o();
-    named_sync(3, 32 * kValueWarps);
-    if (order == 0 && rotated) {
-      warp_fwht_rows(scratch_o, 2 * g, 2, lane);
+      // accumulator -> scratch in natural order, rotated back if it is still rotated
+      store_o();
       named_sync(3, 32 * kValueWarps);
-    }
-  }
-  __syncthreads();
-
-  // ---------------- epilogue: normalize or write the partial record ----------------
-  const float* O = reinterpret_cast<const float*>(smem + kOffQi);
-  const float* lw = misc + kMLw;
-  const float* mrow = misc + kMWmax;
-  if (slot == -1) {
-    for (int e = tid; e < kRows * kL / 4; e += kThreads) {
-      const int r = e >> 7, c4 = e & 127;
-      if (r >= n_rows) continue;
-      float l = 0.0f;
-#pragma unroll
-      for (int w2 = 0; w2 < kScoreWarps; ++w2) l += lw[16 * w2 + r];
-      const float inv = 1.0f / fmaxf(l, 1e-20f);
-      const float4 v = *reinterpret_cast<const float4*>(O + r * kL + 4 * c4);
-      const int64_t off = (out_row0 + r) * kL + 4 * c4;
-      if (p.out_dtype == ASTERQ_DTYPE_F32) {
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) =
-            make_float4(v.x * inv, v.y * inv, v.z * inv, v.w * inv);
-      } else {
-        *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + off) =
-            make_uint2(pack_bf162(v.x * inv, v.y * inv), pack_bf162(v.z * inv, v.w * inv));
+      if (order == 0 && rotated) {
+        warp_fwht_rows(scratch_o, 2 * g, 2, lane);
+        named_sync(3, 32 * kValueWarps);
       }
-    }
-  } else if (slot >= 0) {
-    float* wo = reinterpret_cast<float*>(p.workspace);
-    float* wm = wo + (int64_t)p.n_slots * kRows * kL;
-    float* wl = wm + (int64_t)p.n_slots * kRows;
-    for (int e = tid; e < kRows * kL / 4; e += kThreads) {
-      const int r = e >> 7, c4 = e & 127;
-      *reinterpret_cast<float4*>(wo + ((int64_t)slot * kRows + r) * kL + 4 * c4) =
-          *reinterpret_cast<const float4*>(O + r * kL + 4 * c4);
-    }
-    if (tid < kRows) {
-      wm[(int64_t)slot * kRows + tid] = mrow[tid];
-      float l = 0.0f;
-#pragma unroll
-      for (int w2 = 0; w2 < kScoreWarps; ++w2) l += lw[16 * w2 + tid];
-      wl[(int64_t)slot * kRows + tid] = l;
+      named_sync(0, kThreads);
+      if (epilogue()) break;
     }
   }
-  if (tid == 0 && *abort_flag && p.device_status) atomicExch(p.device_status, 1);
 }
 
 // Merge partial records (latent_attention.py:212-220 applied across splits).
@@ -1108,6 +1150,10 @@ int validate(const asterq_decode_params* p) {
     if (reinterpret_cast<uintptr_t>(ptr) & 15)
       return set_error(ASTERQ_ERR_MISALIGNED, "decode: pointers must be 16-byte aligned");
   if (p->n_units < 0) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: negative unit count");
+  if (p->n_workers < 0 || (p->n_workers > 0 && !p->workers))
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: a worker count needs a workers table");
+  if (reinterpret_cast<uintptr_t>(p->workers) & 3)
+    return set_error(ASTERQ_ERR_MISALIGNED, "decode: the workers table must be 4-byte aligned");
   if (p->n_items > 0 && (p->n_units == 0 || !p->units))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: work items need a units table");
   if (reinterpret_cast<uintptr_t>(p->units) & 7)
@@ -1208,7 +1254,11 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     dec::qprep_kernel<<<p->n_units, dec::kPrepThreads, dec::kPrepSmem, s>>>(*p);
     st = check_launch("latent_decode (query preparation)");
     if (st != ASTERQ_OK) return st;
-    dec::decode_kernel<<<p->n_items, dec::kThreads, dec::kSmemBytes, s>>>(*p, maps);
+    // with a workers table, one CTA per worker (the table is read only when n_workers > 0)
+    asterq_decode_params kp = *p;
+    if (kp.n_workers == 0) kp.workers = nullptr;
+    const int grid = (kp.n_workers > 0) ? kp.n_workers : kp.n_items;
+    if (grid > 0) dec::decode_kernel<<<grid, dec::kThreads, dec::kSmemBytes, s>>>(kp, maps);
     st = check_launch("latent_decode");
     if (st != ASTERQ_OK) return st;
   }

@@ -110,7 +110,8 @@ int asterq_codec_status(int32_t* timeouts);
  *   units [n_units][2] int32 = {out_row0, n_rows}: one per 16-row query block; its query operands
  *          (rotated, fixed-point, fragment-ordered) are prepared once per call into the workspace.
  *   items [n_items][8] int32 = {unit, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
- *          one CTA per item; 16 query rows (t, h) per row block, rows flattened as t*n_heads + h.
+ *          16 query rows (t, h) per row block, rows flattened as t*n_heads + h; one CTA per item, or
+          with a workers table one CTA per worker running its items in order.
  *          slot < 0: the item covers the whole sequence and writes `out` directly;
  *          slot >= 0: it writes an (m, l, o) partial to the workspace.
  *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
@@ -155,6 +156,10 @@ typedef struct asterq_decode_params {
   int32_t cold_scheme;    /* ASTERQ_SCHEME_HADAMARD_INT4 (0): cold codes rotated by the normalized Hadamard
                              transform (kv.py scheme "hadamard_int4"); ASTERQ_SCHEME_INT4: plain groupwise
                              int4 codes (scheme "int4"), same packing and scale layout */
+  const int32_t* workers; /* optional [n_workers + 1] int32: CTA w runs items workers[w] .. workers[w + 1] - 1
+                             in order (a balanced, persistent schedule); NULL: one CTA per item */
+  int32_t n_workers;
+  int32_t reserved0;
 } asterq_decode_params;
 
 /* Bytes of workspace asterq_latent_decode needs: n_slots partial records of 32,896 B

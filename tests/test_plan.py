@@ -53,9 +53,77 @@ def test_single_item_sequences_write_output_directly():
 
 def test_items_sorted_longest_first():
     seqs = [_layout([(i, 0, 512)] * (i + 1), [], i, 1) for i in range(6)]
-    plan = build_plan(seqs, 16, n_sms=1000)
+    plan = build_plan(seqs, 16, n_sms=1000, persistent=False)
     sizes = plan.items[:, 3] - plan.items[:, 2]
     assert (np.diff(sizes) <= 0).all()
+    assert plan.workers is None
+
+
+def _ragged_batch(n=64, seed=0):
+    """C3-like: lengths U[1024, 32768], hot window 2048, cold chunks of 512, q_len 1."""
+    rng = np.random.default_rng(seed)
+    seqs, cp, hp = [], 0, 0
+    for i, length in enumerate(rng.integers(1024, 32769, n)):
+        hot = min(int(length), 2048)
+        cold = int(length) - hot
+        chunks = [(cp + k, 0, min(512, cold - s)) for k, s in enumerate(range(0, cold, 512))]
+        cp += len(chunks)
+        hots = [(hp + k, 0, min(512, hot - s)) for k, s in enumerate(range(0, hot, 512))]
+        hp += len(hots)
+        seqs.append(_layout(chunks, hots, i, 1))
+    return seqs
+
+
+def _item_ns(plan):
+    from asterq.plan import _ITEM_NS, _tile_ns
+
+    tns = np.array([_tile_ns(k, n) for k, _, _, n in plan.tiles])
+    P = np.concatenate(([0], np.cumsum(tns)))
+    return P[plan.items[:, 3]] - P[plan.items[:, 2]] + _ITEM_NS
+
+
+@pytest.mark.parametrize("n_sms", [148, 37, 8])
+def test_persistent_workers_cover_every_tile_once_and_balance(n_sms):
+    from asterq.plan import _MIN_PIECE_NS
+
+    seqs = _ragged_batch()
+    plan = build_plan(seqs, 16, n_sms=n_sms)
+    w = plan.workers
+    assert w is not None and w[0] == 0 and w[-1] == plan.items.shape[0] and (np.diff(w) >= 1).all()
+    assert plan.n_workers <= n_sms
+    # every unit's items tile its visible range exactly once, in order
+    for unit in range(plan.n_units):
+        mine = plan.items[plan.items[:, 0] == unit]
+        ranges = sorted((int(a), int(b)) for a, b in mine[:, 2:4])
+        assert all(r0[1] == r1[0] for r0, r1 in zip(ranges[:-1], ranges[1:]))
+        assert ranges[-1][1] - ranges[0][0] == sum(b - a for a, b in ranges)
+        if len(mine) == 1:
+            assert mine[0, 4] == -1
+        else:
+            assert (mine[:, 4] >= 0).all()
+    assert sorted(plan.items[plan.items[:, 4] >= 0, 4].tolist()) == list(range(plan.n_slots))
+    # workers' estimated times within a few tiles of each other; pieces never tiny
+    cost = _item_ns(plan)
+    loads = np.array([cost[w[k]:w[k + 1]].sum() for k in range(plan.n_workers)])
+    assert loads.max() <= loads.mean() + 2 * _MIN_PIECE_NS
+    split = plan.items[:, 4] >= 0
+    assert (cost[split] - 7500 >= 0.5 * _MIN_PIECE_NS).all()
+
+
+def test_persistent_schedule_does_not_split_small_blocks():
+    seqs = [_layout([], [(i, 0, 100)], i, 1) for i in range(10)]
+    plan = build_plan(seqs, 16)
+    assert plan.items.shape[0] == 10 and plan.n_slots == 0 and plan.n_workers == 10
+
+
+def test_max_items_per_seq_deals_whole_blocks_to_workers():
+    seqs = _ragged_batch(n=20, seed=1)
+    plan = build_plan(seqs, 16, n_sms=8, max_items_per_seq=1)
+    assert plan.items.shape[0] == 20 and plan.n_slots == 0 and plan.n_workers == 8
+    cost = _item_ns(plan)
+    w = plan.workers
+    loads = np.array([cost[w[k]:w[k + 1]].sum() for k in range(8)])
+    assert loads.max() - loads.min() <= cost.max()
 
 
 @pytest.mark.parametrize("bad", [dict(q_len=0), dict(q_len=2049)])
