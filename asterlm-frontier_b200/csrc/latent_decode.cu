@@ -701,6 +701,22 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
 
+        // The team's last read of this stage: the code scales the value warps need (groups
+        // 2tq, 2tq + 1 of this lane's four tokens) move to registers, and the stage is
+        // released to the producer before the softmax.
+        uint32_t kept_scl[2][2] = {{0u, 0u}, {0u, 0u}};
+        if (cold) {
+          const uint16_t* scl = reinterpret_cast<const uint16_t*>(st + kScales);
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int tk = qk_token(tw, m, gid + 8 * h);
+              kept_scl[m][h] = (tk < t.n) ? *reinterpret_cast<const uint32_t*>(scl + 8 * tk + 2 * tq) : 0u;
+            }
+        }
+        mbar_arrive(bar(kBarEmpty + s));
+
         // ---- finalize scores, mask, tile max ----
         const int n_m = cold ? 2 : 1;
         float tmax[2][2];
@@ -781,7 +797,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           // other group of 4 tokens so that ldmatrix reads of 8 consecutive tokens hit 32 banks
           uint8_t* Pc = smem + kOffP + b * kPBytes;
           uint16_t* sT = reinterpret_cast<uint16_t*>(smem + kOffST + b * 2048);
-          const uint16_t* scl = reinterpret_cast<const uint16_t*>(smem + s * kStageBytes + kScales);
 #pragma unroll
           for (int m = 0; m < 2; ++m)
 #pragma unroll
@@ -796,12 +811,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 *reinterpret_cast<uint32_t*>(Pc + tk * 32 + ((nt ^ ((tk >> 2) & 1)) << 4) + 4 * tq) = pack_half2(p0, p1);
               }
               // lane tq publishes groups 2tq and 2tq + 1 of this token's code scales (0 outside the tile)
-              const bool ok = tk < t.n;
-#pragma unroll
-              for (int u = 0; u < 2; ++u) {
-                const int g = 2 * tq + u;
-                sT[g * kColdTile + tk] = ok ? scl[8 * tk + g] : (uint16_t)0;
-              }
+              sT[(2 * tq) * kColdTile + tk] = (uint16_t)(kept_scl[m][h] & 0xffffu);
+              sT[(2 * tq + 1) * kColdTile + tk] = (uint16_t)(kept_scl[m][h] >> 16);
             }
         } else {
           float* P = reinterpret_cast<float*>(smem + kOffP + b * kPBytes);
@@ -829,7 +840,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int cc = 0; cc < 2; ++cc) misc[kMAlpha + b * 16 + 8 * nt + 2 * tq + cc] = alpha_r[nt][cc];
         }
         mbar_arrive(bar(kBarPFull + b));
-        mbar_arrive(bar(kBarEmpty + s));
       }
       // final per-warp sums, brought to the final running max, and the running max itself
       // (the team that did not take the last tile reads it from the other team: phase n_t - 1)
@@ -905,12 +915,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Tile t = t_next;
         if (i + 1 < n_t) t_next = check_tile(p, raw_next);
         if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
-        mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
         mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);  // TMA data visible to this warp
         const uint8_t* st = smem + s * kStageBytes;
         const uint32_t sst = sbase + s * kStageBytes;
         const float* P = reinterpret_cast<const float*>(smem + kOffP + b * kPBytes);
         const bool cold = t.kind == ASTERQ_TILE_COLD;
+
+        // This warp's whole share of the stage goes to registers first (cold: its code words
+        // of all 128 tokens; hot: its bf16 A fragments of all 32 tokens), so the stage is
+        // released, and refilled with tile i + 3, before this tile's p is even ready.
+        uint32_t xs[8][4];
+        if (cold) {
+#pragma unroll
+          for (int kt = 0; kt < kColdTile / 16; ++kt) {
+            const int t0 = 16 * kt + 2 * tq;
+            const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};  // this lane's k indices
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              xs[kt][j] = *reinterpret_cast<const uint32_t*>(st + region + swz(tk[j], cchunk) + 4 * (gid & 3));
+          }
+        } else {
+          // rows beyond n hold stale data: zero this warp's latent block there
+          // (p is 0 for them, but 0 x NaN would poison the accumulator)
+          if (t.n < kHotTile) {
+            for (int e = lane; e < (kHotTile - t.n) * 8; e += 32)
+              *reinterpret_cast<uint4*>(smem + s * kStageBytes + g * kHotBlock + (t.n + e / 8) * 128 + (e % 8) * 16) =
+                  make_uint4(0u, 0u, 0u, 0u);
+            __syncwarp();
+          }
+#pragma unroll
+          for (int kt = 0; kt < kHotTile / 16; ++kt)
+#pragma unroll
+            for (int mi = 0; mi < 4; ++mi) {
+              const int row = 16 * kt + (lane & 7) + 8 * (lane >> 4);
+              ldmatrix_x4_trans(xs[4 * kt + mi], sst + g * kHotBlock + swz(row, 2 * mi + ((lane >> 3) & 1)));
+            }
+          fence_async_shared();  // the zero fill precedes the next TMA write of this stage
+        }
+        mbar_arrive(bar(kBarEmpty + s));
+        if (warp == kProducerWarp) {
+          // refill this stage with tile i + 3 once the tile's team and every value warp have
+          // released it; its descriptor was fetched a tile ago, so the issue does not wait
+          // on global memory
+          if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag))
+            issue_tile(i + kStages, check_tile(p, praw));
+          if (lane == 0 && i + kStages + 1 < n_t) praw = fetch_tile(p, tile_begin + i + kStages + 1);
+          __syncwarp();
+        }
+        mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
 
         if (!cold && order == 0) {
           // first hot tile after cold ones: rotate the accumulator back (O = H O_rot)
@@ -950,11 +1002,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t pbase = sbase + kOffP + b * kPBytes;
           const uint16_t* sT = reinterpret_cast<const uint16_t*>(smem + kOffST + b * 2048) + g * kColdTile;
           const int lt = (lane & 7) + 8 * ((lane >> 3) & 1), lhalf = lane >> 4;
-#pragma unroll 2
+#pragma unroll
           for (int kt = 0; kt < kColdTile / 16; ++kt) {
             // tokens 16kt + {2tq, 2tq+1, 2tq+8, 2tq+9} are this lane's k indices
             const int t0 = 16 * kt + 2 * tq;
-            const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
             // p B fragments (fp16) of rows 0-7 / 8-15, times the tokens' group-g code scales
             uint32_t pr[4];
             {
@@ -968,17 +1019,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             pb[0][1] = hmul2_u32(pr[1], s89);
             pb[1][0] = hmul2_u32(pr[2], s01);
             pb[1][1] = hmul2_u32(pr[3], s89);
-            uint32_t x[4];
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              x[j] = *reinterpret_cast<const uint32_t*>(st + region + swz(tk[j], cchunk) + 4 * (gid & 3));
 #pragma unroll
             for (int mi = 0; mi < 4; ++mi) {
               // rows gid / gid+8 of m-tile mi are dims 2(4gid+mi) / 2(4gid+mi)+1 of group g
               const uint32_t sel =
                   (uint32_t)mi | ((uint32_t)mi << 4) | ((uint32_t)(4 + mi) << 8) | ((uint32_t)(4 + mi) << 12);
-              const uint32_t z01 = prmt(x[0], x[1], sel);
-              const uint32_t z23 = prmt(x[2], x[3], sel);
+              const uint32_t z01 = prmt(xs[kt][0], xs[kt][1], sel);
+              const uint32_t z23 = prmt(xs[kt][2], xs[kt][3], sel);
               uint32_t a[4];
               a[0] = nib_lo_f16x2(z01);
               a[1] = nib_hi_f16x2(z01);
@@ -989,15 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         } else {
-          // rows beyond n hold stale data: zero this warp's latent block there
-          // (p is 0 for them, but 0 x NaN would poison the accumulator)
-          if (t.n < kHotTile) {
-            for (int e = lane; e < (kHotTile - t.n) * 8; e += 32)
-              *reinterpret_cast<uint4*>(smem + s * kStageBytes + g * kHotBlock + (t.n + e / 8) * 128 + (e % 8) * 16) =
-                  make_uint4(0u, 0u, 0u, 0u);
-            __syncwarp();
-          }
-#pragma unroll 1
+#pragma unroll
           for (int kt = 0; kt < kHotTile / 16; ++kt) {
             uint32_t pb[2][2][2];  // [ntile][hi/lo][b0/b1]
 #pragma unroll
@@ -1011,31 +1050,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               pb[nt][1][0] = pack_bf162(p01.x - r0.x, p01.y - r0.y);
               pb[nt][1][1] = pack_bf162(p89.x - r1.x, p89.y - r1.y);
             }
-            uint32_t a[4][4];
-#pragma unroll
-            for (int mi = 0; mi < 4; ++mi) {
-              const int row = 16 * kt + (lane & 7) + 8 * (lane >> 4);
-              ldmatrix_x4_trans(a[mi], sst + g * kHotBlock + swz(row, 2 * mi + ((lane >> 3) & 1)));
-            }
 #pragma unroll
             for (int hl = 0; hl < 2; ++hl)
 #pragma unroll
               for (int mi = 0; mi < 4; ++mi)
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) mma_bf16(o[mi][nt], a[mi], pb[nt][hl][0], pb[nt][hl][1]);
+                for (int nt = 0; nt < 2; ++nt) mma_bf16(o[mi][nt], xs[4 * kt + mi], pb[nt][hl][0], pb[nt][hl][1]);
           }
-          fence_async_shared();  // the zero fill precedes the next TMA write of this stage
         }
         mbar_arrive(bar(kBarPEmpty + b));
-        mbar_arrive(bar(kBarEmpty + s));
-        if (warp == kProducerWarp) {
-          // refill this stage with tile i + 3 once every warp has released tile i; its
-          // descriptor was fetched a tile ago, so the issue does not wait on global memory
-          if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag))
-            issue_tile(i + kStages, check_tile(p, praw));
-          if (lane == 0 && i + kStages + 1 < n_t) praw = fetch_tile(p, tile_begin + i + kStages + 1);
-          __syncwarp();
-        }
       }
       // accumulator -> scratch in natural order, rotated back if it is still rotated
       store_o();
