@@ -37,12 +37,13 @@ _COLD_TOKEN_BYTES = 256 + 16 + 128
 _HOT_TOKEN_BYTES = 1024 + 128
 _ITEM_OVERHEAD_BYTES = 48 * 1024  # query load + rotation + output/partial write
 
-# time model of the persistent schedule (ns, one B200 SM; item timelines of the C3 batch):
-# a full cold tile 3.0 us, a full hot tile 1.9 us, an item's fixed cost (query copy,
-# first tile in flight, rotation back and output or partial write) 7.5 us
-_COLD_TILE_NS = (1200, 1830)  # fixed + per full tile
-_HOT_TILE_NS = (800, 1130)
-_ITEM_NS = 7500
+# time model of the persistent schedule (ns, one B200 SM; least-squares fit to the item
+# timelines of the C3 and C5 batches): a full cold tile 3.1 us, a full hot tile 2.1 us, an
+# item's fixed cost (query copy, first tile in flight, rotation back and output or partial
+# write, barrier reset) 5 us
+_COLD_TILE_NS = (1200, 1890)  # fixed + per full tile
+_HOT_TILE_NS = (800, 1285)
+_ITEM_NS = 5000
 _MIN_PIECE_NS = 4 * sum(_COLD_TILE_NS)  # a worker does not start a piece of a block below this
 
 

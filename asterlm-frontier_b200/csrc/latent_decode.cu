@@ -448,8 +448,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------- prologue (producer lane): first tiles and the prepared query ----------------
   // (qprep_kernel wrote the query operands to the workspace: int8 limb fragments, hot and
   // RoPE bf16 fragments, per-row scalars, laid out like their shared-memory regions)
+  // (the query block first: it comes from L2 and gates every tile, the tiles come from HBM)
   auto prologue = [&]() {
-    for (int j = 0; j < min(n_t, kStages - 1); ++j) issue(j);
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes +
                          (int64_t)max(itm[0], 0) * kQPrepBytes;
     const uint32_t qb = bar(kBarQ);
@@ -458,7 +458,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bulk_1d(sbase + kOffQh, src + 16384, 16384, qb);
     bulk_1d(sbase + kOffQr, src + 32768, 2048, qb);
     bulk_1d(sbase + kOffMisc + 4 * kMQscale, src + 34816, 4 * kQScalars, qb);
-    if (n_t > kStages - 1) issue(kStages - 1);
+    for (int j = 0; j < min(n_t, kStages); ++j) issue(j);
   };
 
   // ---------------- epilogue: normalize or write the partial record ----------------

@@ -84,7 +84,7 @@ def _item_ns(plan):
 
 @pytest.mark.parametrize("n_sms", [148, 37, 8])
 def test_persistent_workers_cover_every_tile_once_and_balance(n_sms):
-    from asterq.plan import _MIN_PIECE_NS
+    from asterq.plan import _ITEM_NS, _MIN_PIECE_NS
 
     seqs = _ragged_batch()
     plan = build_plan(seqs, 16, n_sms=n_sms)
@@ -107,7 +107,7 @@ def test_persistent_workers_cover_every_tile_once_and_balance(n_sms):
     loads = np.array([cost[w[k]:w[k + 1]].sum() for k in range(plan.n_workers)])
     assert loads.max() <= loads.mean() + 2 * _MIN_PIECE_NS
     split = plan.items[:, 4] >= 0
-    assert (cost[split] - 7500 >= 0.5 * _MIN_PIECE_NS).all()
+    assert (cost[split] - _ITEM_NS >= 0.5 * _MIN_PIECE_NS).all()
 
 
 def test_persistent_schedule_does_not_split_small_blocks():
