@@ -87,7 +87,8 @@ class DecodeParams(ctypes.Structure):
         ("cold_scheme", ctypes.c_int32),
         ("workers", ctypes.c_void_p),
         ("n_workers", ctypes.c_int32),
-        ("reserved0", ctypes.c_int32),
+        ("n_combine_total", ctypes.c_int32),
+        ("unit_jobs", ctypes.c_void_p),
     ]
 
 

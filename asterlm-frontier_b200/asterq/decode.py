@@ -68,6 +68,7 @@ class DeviceDecodePlan:
         self.combine = up(plan.combine)
         self.units = up(plan.units)
         self.workers = None if plan.workers is None else torch.from_numpy(plan.workers.copy()).to(self.device)
+        self.unit_jobs = None if plan.unit_jobs is None else torch.from_numpy(plan.unit_jobs.copy()).to(self.device)
         self.workspace = torch.empty(max(4, plan.workspace_bytes // 4), dtype=torch.float32, device=self.device)
 
     @property
@@ -103,7 +104,8 @@ def make_params(
     p.total_q = int(q_lat.shape[0])
     p.n_tiles = int(plan.tiles.shape[0])
     p.n_items = int(plan.items.shape[0])
-    p.n_combine = int(plan.combine.shape[0])
+    p.n_combine = plan.n_separate  # jobs for the combine launch; the rest run inside the decode kernel
+    p.n_combine_total = int(plan.combine.shape[0])
     p.n_slots = int(plan.n_slots)
     p.q_lat = q_lat.data_ptr()
     p.q_rope = q_rope.data_ptr()
@@ -125,6 +127,8 @@ def make_params(
     if dplan.workers is not None and plan.n_workers > 0:
         p.workers = dplan.workers.data_ptr()
         p.n_workers = plan.n_workers
+    if dplan.unit_jobs is not None:
+        p.unit_jobs = dplan.unit_jobs.data_ptr()
     if pools.cold_scheme not in COLD_SCHEMES:
         raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
     p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]

@@ -45,6 +45,9 @@ _COLD_TILE_NS = (1200, 1890)  # fixed + per full tile
 _HOT_TILE_NS = (800, 1285)
 _ITEM_NS = 5000
 _MIN_PIECE_NS = 4 * sum(_COLD_TILE_NS)  # a worker does not start a piece of a block below this
+# a block cut into at most this many pieces is merged by the decode kernel itself (the CTA
+# that writes the last piece reads them all back from L2); more pieces go to the combine launch
+FUSED_COMBINE_MAX_PARTS = 8
 
 
 @dataclass
@@ -88,6 +91,10 @@ class DecodePlan:
     n_heads: int
     units: np.ndarray = field(default_factory=lambda: np.zeros((0, 2), np.int32))  # [n_units][2] {out_row0, n_rows}
     workers: np.ndarray | None = None  # [n_workers + 1] item offsets, or None: one CTA per item
+    # combine jobs [0, n_separate_combine) run in the combine launch; the others are run by
+    # the decode kernel itself (unit_jobs[u] = the unit's job, or -1)
+    n_separate_combine: int | None = None
+    unit_jobs: np.ndarray | None = None
 
     @property
     def n_workers(self) -> int:
@@ -98,8 +105,13 @@ class DecodePlan:
         return int(self.units.shape[0])
 
     @property
+    def n_separate(self) -> int:
+        return int(self.combine.shape[0]) if self.n_separate_combine is None else self.n_separate_combine
+
+    @property
     def workspace_bytes(self) -> int:
-        return self.n_slots * ROWS_PER_BLOCK * (512 + 2) * 4 + self.n_units * QPREP_BYTES
+        counters = (self.n_units * 4 + 15) // 16 * 16  # one int32 per unit (fused combine jobs)
+        return self.n_slots * ROWS_PER_BLOCK * (512 + 2) * 4 + self.n_units * QPREP_BYTES + counters
 
 
 def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
@@ -263,7 +275,7 @@ def build_plan(
         by_unit: dict[int, list] = {}
         for ui, a, b, w in pieces:
             by_unit.setdefault(ui, []).append((a, b, w))
-        items, combine, n_slots = [], [], 0
+        items, separate, fused, n_slots = [], [], [], 0
         for ui, (si, rb, t0, t1, c) in enumerate(units):
             out_row0, n_rows = unit_rows[ui]
             q_len = seqs[si].q_len
@@ -276,14 +288,25 @@ def build_plan(
             for a, b, w in segs:
                 items.append((w, a, (ui, rb, a, b, n_slots, out_row0, n_rows, q_len)))
                 n_slots += 1
-            combine.append((s0, n_slots, out_row0, n_rows))
-        items.sort(key=lambda x: (x[0], x[1]))
+            job = (s0, n_slots, out_row0, n_rows)
+            if not force_partial and len(segs) <= FUSED_COMBINE_MAX_PARTS:
+                fused.append((ui, job))
+            else:
+                separate.append(job)
+        combine = separate + [job for _, job in fused]
+        unit_jobs = np.full(len(units), -1, dtype=np.int32)
+        for k, (ui, _) in enumerate(fused):
+            unit_jobs[ui] = len(separate) + k
+        # a worker runs its pieces of cut blocks before its whole blocks, so that the last
+        # piece of a block (whose CTA then merges the block) rarely ends with the kernel
+        items.sort(key=lambda x: (x[0], x[2][4] < 0, x[1]))
         item_arr = np.asarray([it[2] for it in items], dtype=np.int32).reshape(-1, 8)
         used = max((it[0] for it in items), default=-1) + 1
         counts = np.bincount(np.asarray([it[0] for it in items], dtype=np.int64), minlength=used)
         workers = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
         comb_arr = np.asarray(combine, dtype=np.int32).reshape(-1, 4)
-        return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, workers)
+        return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, workers,
+                          n_separate_combine=len(separate), unit_jobs=unit_jobs if fused else None)
 
     slots_target = max(1, int(n_sms * ctas_per_sm * waves))
     item_cost = max(total_cost / slots_target, 4 * COLD_TILE * _COLD_TOKEN_BYTES)

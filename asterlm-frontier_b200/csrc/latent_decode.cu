@@ -104,10 +104,16 @@ constexpr int kMWmax = 112;    // [2 teams][2][4][16] tile maxima (a team's tile
                                // after the tile loop [16] = final running max
 constexpr int kMLw = 368;      // [8 score warps][16]
 constexpr int kMMrun = 496;    // [2][16] running max after tile i, in slot i & 1 (team hand-off)
+constexpr int kMComb = 528;    // fused combine: [2][16] per-row max and 1 / sum, then [8][16] part weights
 
 // workspace: n_slots partial records, then n_units prepared query blocks
 constexpr int kRecordBytes = kRows * (kL + 2) * 4;                    // 32,896
 constexpr int kQPrepBytes = 16384 + 16384 + 2048 + 512;               // 35,328: qi | qh | qr | scalars
+// then one int32 per unit: partial records written so far (fused combine jobs)
+__host__ __device__ inline int64_t counters_offset(int n_slots, int n_units) {
+  return (int64_t)n_slots * kRecordBytes + (int64_t)n_units * kQPrepBytes;
+}
+inline int64_t counter_bytes(int n_units) { return ((int64_t)n_units * 4 + 15) / 16 * 16; }
 constexpr uint32_t kQPrepCopyBytes = 16384 + 16384 + 2048 + 4 * kQScalars;
 
 // mbarrier slots (8 bytes each)
@@ -257,6 +263,9 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   const int64_t out_row0 = p.units[2 * unit];
   const int n_rows = min(max(p.units[2 * unit + 1], 0), kRows);
   uint8_t* dst = reinterpret_cast<uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes + (int64_t)unit * kQPrepBytes;
+  // this call's fused-combine count of the unit starts at zero (the decode kernel runs after this kernel)
+  if (tid == 0)
+    reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(p.workspace) + counters_offset(p.n_slots, p.n_units))[unit] = 0;
 
   const uint16_t* ql = reinterpret_cast<const uint16_t*>(p.q_lat);
   const uint16_t* qrp = reinterpret_cast<const uint16_t*>(p.q_rope);
@@ -501,6 +510,82 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int w2 = 0; w2 < kScoreWarps; ++w2) l += lw[16 * w2 + tid];
         wl[(int64_t)slot * kRows + tid] = l;
+      }
+      // Fused combine job of this unit: every CTA that writes one of its partial records
+      // counts it; the one that writes the last merges them all (latent_attention.py:212-220
+      // applied across splits, as combine_kernel does), so no separate launch is needed.
+      const int unit = itm[0];
+      const int job = (p.unit_jobs != nullptr && unit >= 0 && unit < p.n_units) ? p.unit_jobs[unit] : -1;
+      if (job >= p.n_combine && job < p.n_combine_total) {
+        const int4 jb = *reinterpret_cast<const int4*>(p.combine + 4 * (int64_t)job);
+        const int s0 = max(jb.x, 0), s1 = min(jb.y, p.n_slots), rows = min(jb.w, kRows);
+        __threadfence();  // this CTA's record is visible device-wide before the count moves
+        named_sync(0, kThreads);
+        volatile int* last = reinterpret_cast<volatile int*>(misc + kMAlpha);
+        if (tid == 0) {
+          int* ctr = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(p.workspace) + counters_offset(p.n_slots, p.n_units));
+          *last = atomicAdd(ctr + unit, 1) == s1 - s0 - 1;
+        }
+        named_sync(0, kThreads);
+        if (*last) {
+          __threadfence();
+          const int n_parts = s1 - s0;
+          if (tid < kRows) {
+            float mmax = -INFINITY;
+            for (int q = s0; q < s1; ++q) mmax = fmaxf(mmax, __ldcg(wm + (int64_t)q * kRows + tid));
+            const float msub = (mmax == -INFINITY) ? 0.0f : mmax;
+            float l = 0.0f;
+            for (int q = s0; q < s1; ++q)
+              l += exp2f((__ldcg(wm + (int64_t)q * kRows + tid) - msub) * kLog2e) * __ldcg(wl + (int64_t)q * kRows + tid);
+            misc[kMComb + tid] = msub;
+            misc[kMComb + kRows + tid] = 1.0f / fmaxf(l, 1e-20f);
+          }
+          // this thread's four outputs (rows r0 + 4j, 4 dims at c4), accumulated over the parts
+          // eight at a time: weights w_q / l of the eight parts in shared memory, then the
+          // eight records' loads issued together
+          const int r0 = tid >> 7, c4 = tid & 127;
+          float4 acc[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[j] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+          float* wq = misc + kMComb + 2 * kRows;  // [8 parts][16 rows]
+          for (int c = 0; c < n_parts; c += 8) {
+            named_sync(0, kThreads);  // row scalars written / previous weights consumed
+            if (tid < 8 * kRows) {
+              const int q = c + (tid >> 4), r = tid & 15;
+              wq[tid] = (q < n_parts) ? exp2f((__ldcg(wm + (int64_t)(s0 + q) * kRows + r) - misc[kMComb + r]) * kLog2e) *
+                                            misc[kMComb + kRows + r]
+                                      : 0.0f;
+            }
+            named_sync(0, kThreads);
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              if (c + q >= n_parts) break;
+              const float* rec = wo + (int64_t)(s0 + c + q) * kRows * kL;
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int r = r0 + 4 * j;
+                const float w = wq[q * kRows + r];
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(rec + r * kL + 4 * c4));
+                acc[j].x += w * v.x;
+                acc[j].y += w * v.y;
+                acc[j].z += w * v.z;
+                acc[j].w += w * v.w;
+              }
+            }
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int r = r0 + 4 * j;
+            if (r >= rows) continue;
+            const int64_t off = ((int64_t)jb.z + r) * kL + 4 * c4;
+            if (p.out_dtype == ASTERQ_DTYPE_F32) {
+              *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + off) = acc[j];
+            } else {
+              *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + off) =
+                  make_uint2(pack_bf162(acc[j].x, acc[j].y), pack_bf162(acc[j].z, acc[j].w));
+            }
+          }
+        }
       }
     }
     const bool stop = *abort_flag != 0;
@@ -1181,7 +1266,11 @@ int validate(const asterq_decode_params* p) {
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: work items need a units table");
   if (reinterpret_cast<uintptr_t>(p->units) & 7)
     return set_error(ASTERQ_ERR_MISALIGNED, "decode: the units table must be 8-byte aligned");
-  const int64_t need = (int64_t)p->n_slots * kRecordBytes + (p->n_items > 0 ? (int64_t)p->n_units * kQPrepBytes : 0);
+  if (p->unit_jobs && (reinterpret_cast<uintptr_t>(p->unit_jobs) & 3))
+    return set_error(ASTERQ_ERR_MISALIGNED, "decode: the unit_jobs table must be 4-byte aligned");
+  if (p->n_combine_total < 0) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: negative combine job count");
+  const int64_t need = (int64_t)p->n_slots * kRecordBytes +
+                       (p->n_items > 0 ? (int64_t)p->n_units * kQPrepBytes + counter_bytes(p->n_units) : 0);
   if (need > 0 && (!p->workspace || p->workspace_bytes < need))
     return set_error(ASTERQ_ERR_WORKSPACE, "decode: workspace of %lld bytes < %lld needed",
                      (long long)p->workspace_bytes, (long long)need);
@@ -1234,7 +1323,8 @@ using namespace asterq;
 
 extern "C" int64_t asterq_decode_workspace_bytes(const asterq_decode_params* p) {
   if (!p) return 0;
-  return (int64_t)max(p->n_slots, 0) * dec::kRecordBytes + (int64_t)max(p->n_units, 0) * dec::kQPrepBytes;
+  return (int64_t)max(p->n_slots, 0) * dec::kRecordBytes + (int64_t)max(p->n_units, 0) * dec::kQPrepBytes +
+         dec::counter_bytes(max(p->n_units, 0));
 }
 
 extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream) {
@@ -1352,7 +1442,7 @@ namespace dec {
 constexpr int kNoAllocMaxSlots = 256;
 constexpr int kNoAllocMaxUnits = 256;
 static __device__ __align__(256) float
-    g_noalloc_workspace[(kNoAllocMaxSlots * kRecordBytes + kNoAllocMaxUnits * kQPrepBytes) / 4];
+    g_noalloc_workspace[(kNoAllocMaxSlots * kRecordBytes + kNoAllocMaxUnits * kQPrepBytes + 4 * kNoAllocMaxUnits) / 4];
 
 }  // namespace dec
 }  // namespace asterq

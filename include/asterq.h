@@ -159,11 +159,16 @@ typedef struct asterq_decode_params {
   const int32_t* workers; /* optional [n_workers + 1] int32: CTA w runs items workers[w] .. workers[w + 1] - 1
                              in order (a balanced, persistent schedule); NULL: one CTA per item */
   int32_t n_workers;
-  int32_t reserved0;
+  int32_t n_combine_total;  /* jobs in `combine`: [0, n_combine) run by the combine launch,
+                               [n_combine, n_combine_total) by the decode kernel itself (unit_jobs) */
+  const int32_t* unit_jobs; /* optional [n_units] int32: the combine job (index in [n_combine,
+                               n_combine_total)) that the decode kernel runs itself, in the CTA that
+                               writes the unit's last partial record, or -1.  NULL: none. */
 } asterq_decode_params;
 
 /* Bytes of workspace asterq_latent_decode needs: n_slots partial records of 32,896 B
- * (16 x 514 fp32) followed by n_units prepared query blocks of 35,328 B. */
+ * (16 x 514 fp32), n_units prepared query blocks of 35,328 B, then one int32 counter per
+ * unit (rounded up to 16 bytes) for the fused combine jobs. */
 int64_t asterq_decode_workspace_bytes(const asterq_decode_params* p);
 
 /* Enqueue the split-KV decode (and, when n_combine > 0, the combine). */

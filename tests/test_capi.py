@@ -41,9 +41,9 @@ def test_version_and_error_string():
 
 def test_struct_layout_matches_header():
     # sizes of the C struct: 6 int32 + 2 float + 3 int64 + 4 int32 + 14 pointers + int64 + 2 pointers + 2 int32
-    # + the workers pointer + 2 int32
-    assert ctypes.sizeof(_lib.DecodeParams) == 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8 + 8 + 8 + 2 * 4 + 8 + 2 * 4
-    assert _lib.DecodeParams.workers.offset == ctypes.sizeof(_lib.DecodeParams) - 16
+    # + the workers pointer + 2 int32 + the unit_jobs pointer
+    assert ctypes.sizeof(_lib.DecodeParams) == 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8 + 8 + 8 + 2 * 4 + 8 + 2 * 4 + 8
+    assert _lib.DecodeParams.workers.offset == ctypes.sizeof(_lib.DecodeParams) - 24
 
 
 def test_quantize_rejects_bad_sizes_without_touching_the_gpu():
