@@ -249,7 +249,8 @@ ASTERQ_DEVICE int qk_token(int warp, int m, int r) {
 //   qr      [4][2][32] uint2: bf16 RoPE query x 2^e
 //   scalars 2^e, 2^-e * scale, fixed-point scale, the two score multipliers
 // ---------------------------------------------------------------------------
-constexpr int kPrepThreads = 256;
+constexpr int kPrepThreads = 512;
+constexpr int kPrepRowsPerWarp = kRows / (kPrepThreads / 32);  // one query row per warp
 constexpr int kPrepSmem = 16 * kL * 4 + 16 * kL * 2 + 16 * kRope * 2 + 4 * kQScalars;
 
 __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_constant__ asterq_decode_params p) {
@@ -260,6 +261,8 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   float* sc = reinterpret_cast<float*>(prep_smem + 16 * kL * 6 + 16 * kRope * 2);  // kQScalars, from kMQscale
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int unit = blockIdx.x;
+  // the decode grid may launch now; it waits for this grid's results before reading them
+  asm volatile("griddepcontrol.launch_dependents;");
   const int64_t out_row0 = p.units[2 * unit];
   const int n_rows = min(max(p.units[2 * unit + 1], 0), kRows);
   uint8_t* dst = reinterpret_cast<uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes + (int64_t)unit * kQPrepBytes;
@@ -269,7 +272,7 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
 
   const uint16_t* ql = reinterpret_cast<const uint16_t*>(p.q_lat);
   const uint16_t* qrp = reinterpret_cast<const uint16_t*>(p.q_rope);
-  for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
+  for (int r = kPrepRowsPerWarp * warp; r < kPrepRowsPerWarp * (warp + 1); ++r) {
     float* d = scratch + r * kL + 16 * lane;
     uint4 a = make_uint4(0u, 0u, 0u, 0u), b = a, c = a;
     if (r < n_rows) {
@@ -289,9 +292,9 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   }
   __syncwarp();
   // hadamard_int4 scores the codes in the rotated basis (H q); plain int4 in the natural one
-  if (p.cold_scheme == ASTERQ_SCHEME_HADAMARD_INT4) warp_fwht_rows(scratch, 2 * warp, 2, lane);
+  if (p.cold_scheme == ASTERQ_SCHEME_HADAMARD_INT4) warp_fwht_rows(scratch, kPrepRowsPerWarp * warp, kPrepRowsPerWarp, lane);
   __syncwarp();
-  for (int r = 2 * warp; r < 2 * warp + 2; ++r) {
+  for (int r = kPrepRowsPerWarp * warp; r < kPrepRowsPerWarp * (warp + 1); ++r) {
     float mx = 0.0f;
 #pragma unroll
     for (int k = 0; k < 16; ++k) mx = fmaxf(mx, fabsf(scratch[r * kL + 16 * lane + k]));
@@ -457,8 +460,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ---------------- prologue (producer lane): first tiles and the prepared query ----------------
   // (qprep_kernel wrote the query operands to the workspace: int8 limb fragments, hot and
   // RoPE bf16 fragments, per-row scalars, laid out like their shared-memory regions)
-  // (the query block first: it comes from L2 and gates every tile, the tiles come from HBM)
-  auto prologue = [&]() {
+  // (the query block first: it comes from L2 and gates every tile, the tiles come from HBM;
+  // the CTA's first item has its tiles in flight already, see below)
+  auto prologue = [&](bool tiles_issued) {
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes +
                          (int64_t)max(itm[0], 0) * kQPrepBytes;
     const uint32_t qb = bar(kBarQ);
@@ -467,8 +471,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     bulk_1d(sbase + kOffQh, src + 16384, 16384, qb);
     bulk_1d(sbase + kOffQr, src + 32768, 2048, qb);
     bulk_1d(sbase + kOffMisc + 4 * kMQscale, src + 34816, 4 * kQScalars, qb);
-    for (int j = 0; j < min(n_t, kStages); ++j) issue(j);
+    if (!tiles_issued)
+      for (int j = 0; j < min(n_t, kStages); ++j) issue(j);
   };
+  // This grid may start while qprep_kernel still runs (programmatic dependent launch): the
+  // first item's tiles read only the cache, so they are requested before every thread
+  // waits for qprep_kernel's results (the query blocks and the unit counters).
+  if (warp == kProducerWarp && lane == 0 && it_begin < it_end) {
+    begin_item(it_begin);
+    for (int j = 0; j < min(n_t, kStages); ++j) issue(j);
+  }
+  asm volatile("griddepcontrol.wait;" ::: "memory");
 
   // ---------------- epilogue: normalize or write the partial record ----------------
   // (after a CTA-wide barrier; returns true when a wait of this item timed out: the CTA
@@ -958,7 +971,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       begin_item(it);
       if (it > it_begin) next_item_sync();
       if (warp == kProducerWarp) {
-        if (lane == 0) prologue();
+        if (lane == 0) prologue(it == it_begin);
         __syncwarp();
       }
       float o[4][2][4];
@@ -1371,7 +1384,21 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     asterq_decode_params kp = *p;
     if (kp.n_workers == 0) kp.workers = nullptr;
     const int grid = (kp.n_workers > 0) ? kp.n_workers : kp.n_items;
-    if (grid > 0) dec::decode_kernel<<<grid, dec::kThreads, dec::kSmemBytes, s>>>(kp, maps);
+    if (grid > 0) {
+      // programmatic dependent launch: the decode grid starts while qprep_kernel finishes
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(grid);
+      cfg.blockDim = dim3(dec::kThreads);
+      cfg.dynamicSmemBytes = dec::kSmemBytes;
+      cfg.stream = s;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[0].val.programmaticStreamSerializationAllowed = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cudaError_t e = cudaLaunchKernelEx(&cfg, dec::decode_kernel, kp, maps);
+      if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: launch failed: %s", cudaGetErrorString(e));
+    }
     st = check_launch("latent_decode");
     if (st != ASTERQ_OK) return st;
   }

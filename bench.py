@@ -388,16 +388,16 @@ def main() -> None:
             e0.record(stream)
             _lib.check(lib.asterq_latent_decode(ctypes.byref(p_dec), sh))
             e1.record(stream)
-            if n_combine:
+            if n_combine:  # blocks cut into more pieces than the decode kernel merges itself
                 _lib.check(lib.asterq_splitkv_combine(ws.data_ptr(), plan.n_slots, dplan.combine.data_ptr(),
                                                       n_combine, 512, out.data_ptr(), _lib.DTYPE_BF16, sh))
-            e2.record(stream)
+                e2.record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
     barrier()
     total_ms = max_over_ranks(t_start.elapsed_time(t_end))
     dec_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1, _ in ev)
-    comb_ms = statistics.mean(e1.elapsed_time(e2) for _, e1, e2 in ev)
+    comb_ms = statistics.mean(e1.elapsed_time(e2) for _, e1, e2 in ev) if n_combine else 0.0
     ms_per_step = total_ms / args.steps
     n_seqs = len(wl.lengths)
     value = world * n_seqs / (ms_per_step / 1e3)

@@ -81,6 +81,11 @@ def _params(**kw) -> _lib.DecodeParams:
         (dict(n_items=3), _lib.ASTERQ_ERR_INVALID_ARGUMENT),  # null tables
         (dict(n_slots=2, n_items=0), _lib.ASTERQ_ERR_WORKSPACE),
         (dict(n_items=1, items=8, tiles=16, q_lat=16, q_rope=16, out=16), _lib.ASTERQ_ERR_MISALIGNED),
+        (dict(n_workers=4), _lib.ASTERQ_ERR_INVALID_ARGUMENT),  # a worker count without a workers table
+        (dict(n_workers=-1), _lib.ASTERQ_ERR_INVALID_ARGUMENT),
+        (dict(n_workers=1, workers=18), _lib.ASTERQ_ERR_MISALIGNED),
+        (dict(unit_jobs=6), _lib.ASTERQ_ERR_MISALIGNED),
+        (dict(n_combine_total=-1), _lib.ASTERQ_ERR_INVALID_ARGUMENT),
     ],
 )
 def test_decode_validation(kw, status):
@@ -96,6 +101,21 @@ def test_decode_noop_and_workspace_query():
     assert lib.asterq_latent_decode(ctypes.byref(p), None) == _lib.ASTERQ_OK
     p.n_slots = 3
     assert lib.asterq_decode_workspace_bytes(ctypes.byref(p)) == 3 * 16 * 514 * 4
+    # + the prepared query blocks and one counter per unit (fused combine), rounded to 16 bytes
+    p.n_units = 5
+    assert lib.asterq_decode_workspace_bytes(ctypes.byref(p)) == 3 * 16 * 514 * 4 + 5 * 35328 + 32
+
+
+def test_plan_workspace_matches_the_library():
+    from asterq.plan import SequenceLayout, build_plan
+
+    lib = _lib.load()
+    seqs = [SequenceLayout(cold=[(i, 0, 512)] * (4 * i + 1), hot=[(i, 0, 200)], q_start=i, q_len=1 + (i % 3))
+            for i in range(9)]
+    for kw in (dict(), dict(n_sms=8), dict(persistent=False)):
+        plan = build_plan(seqs, 16, **kw)
+        p = _params(n_slots=plan.n_slots, n_units=plan.n_units)
+        assert lib.asterq_decode_workspace_bytes(ctypes.byref(p)) == plan.workspace_bytes
 
 
 def test_check_maps_status_to_exception_types():

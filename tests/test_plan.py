@@ -151,3 +151,37 @@ def test_prefill_chunk_row_blocks_see_only_their_causal_prefix():
 def test_rejects_bad_chunks():
     with pytest.raises(ValueError):
         build_plan([_layout([(0, 0, 0)], [])], 16)
+
+
+@pytest.mark.parametrize("n_sms", [148, 16, 3])
+def test_fused_combine_jobs(n_sms):
+    """Blocks cut into at most FUSED_COMBINE_MAX_PARTS pieces are merged by the decode kernel:
+    their jobs follow the separate ones and unit_jobs points at them."""
+    from asterq.plan import FUSED_COMBINE_MAX_PARTS
+
+    seqs = _ragged_batch(n=24, seed=2)
+    seqs.append(_layout([(9000 + k, 0, 512) for k in range(400)], [], 24, 1))  # one very long block
+    plan = build_plan(seqs, 16, n_sms=n_sms)
+    n_sep = plan.n_separate
+    parts = plan.combine[:, 1] - plan.combine[:, 0]
+    assert (parts[:n_sep] > FUSED_COMBINE_MAX_PARTS).all()
+    assert (parts[n_sep:] <= FUSED_COMBINE_MAX_PARTS).all() and (parts[n_sep:] >= 2).all()
+    jobs = plan.unit_jobs if plan.unit_jobs is not None else np.full(plan.n_units, -1)
+    assert sorted(j for j in jobs.tolist() if j >= 0) == list(range(n_sep, plan.combine.shape[0]))
+    for unit, job in enumerate(jobs.tolist()):
+        mine = plan.items[plan.items[:, 0] == unit]
+        if job >= 0:  # the job covers exactly this unit's slots
+            a, b = plan.combine[job, :2]
+            assert sorted(mine[:, 4].tolist()) == list(range(a, b))
+    # a worker runs its pieces of cut blocks first
+    w = plan.workers
+    for k in range(plan.n_workers):
+        whole = plan.items[w[k]:w[k + 1], 4] < 0
+        assert not (whole[:-1] & ~whole[1:]).any()
+
+
+def test_force_partial_fuses_nothing():
+    seqs = _ragged_batch(n=8, seed=3)
+    plan = build_plan(seqs, 16, n_sms=8, force_partial=True)
+    assert plan.unit_jobs is None and plan.n_separate == plan.combine.shape[0] == plan.n_units
+    assert (plan.items[:, 4] >= 0).all()
