@@ -1460,8 +1460,11 @@ extern "C" int asterq_splitkv_merge(const float* partials, int32_t n_slots, cons
 // pointers to its inputs and outputs).  For them the split-KV partial records
 // live in a fixed array compiled into this library instead of a caller-provided
 // workspace.  The array is a device global: every GPU that loads the library
-// keeps it (room for kNoAllocMaxSlots partial records and kNoAllocMaxUnits
-// prepared query blocks, about 17.5 MB) until the process exits.
+// keeps it (room for kNoAllocMaxSlots partial records, kNoAllocMaxUnits
+// prepared query blocks and one fused-combine counter per block, about 17.5 MB)
+// until the process exits.  The array keeps the previous call's contents; the
+// only part that must start at zero, the counters, is zeroed by the query
+// preparation at the start of every call.
 // ---------------------------------------------------------------------------
 namespace asterq {
 namespace dec {
