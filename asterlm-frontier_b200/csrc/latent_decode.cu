@@ -1172,36 +1172,93 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Merge partial records (latent_attention.py:212-220 applied across splits).
-// Grid: (combine job, 8-dim slice of the latent); 64 threads = 16 rows x 4 pairs
-// of dims, so a long sequence's many records are read by 64 CTAs per job.
+// Grid: (combine job, 8-dim slice of the latent), so a long sequence's many records are
+// read by 64 CTAs per job.  256 threads: first the per-row max and sum over all of the
+// job's records (16 threads per row), then each (row, 4 dims) output is accumulated by 8
+// lanes that take every 8th record, four records' loads in flight per lane, and summed
+// with shuffles.  The records' weights w / l are staged in shared memory 256 records at a
+// time.
 constexpr int kCombDims = 8;
-constexpr int kCombThreads = kRows * kCombDims / 2;
+constexpr int kCombThreads = 256;     // 16 rows x 2 float4 x 8 record lanes
+constexpr int kCombWindow = 256;      // records whose weights are staged at a time
+constexpr int kCombMergeThreads = kRows * kCombDims / 2;  // merge_kernel: 16 rows x 4 pairs
 __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                       const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                       int n_slots, int latent_dim, void* __restrict__ out,
                                                       int out_dtype) {
+  __shared__ float w_s[kCombWindow * kRows];
+  __shared__ float row_s[2 * kRows];  // per-row max, 1 / sum
   const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
   const int slot_begin = max(job.x, 0), slot_end = min(job.y, n_slots), n_rows = min(job.w, kRows);
   const int64_t out_row0 = job.z;
-  const int r = threadIdx.x / (kCombDims / 2), d = blockIdx.y * kCombDims + 2 * (threadIdx.x % (kCombDims / 2));
-  if (r >= n_rows || slot_end <= slot_begin || d >= latent_dim) return;
-  float mmax = -INFINITY;
-  for (int s = slot_begin; s < slot_end; ++s) mmax = fmaxf(mmax, wm[(int64_t)s * kRows + r]);
-  const float msub = (mmax == -INFINITY) ? 0.0f : mmax;
-  float l = 0.0f, a0 = 0.0f, a1 = 0.0f;
-  for (int s = slot_begin; s < slot_end; ++s) {
-    const float w = exp2f((wm[(int64_t)s * kRows + r] - msub) * kLog2e);
-    l += w * wl[(int64_t)s * kRows + r];
-    const float2 v = *reinterpret_cast<const float2*>(wo + ((int64_t)s * kRows + r) * latent_dim + d);
-    a0 += w * v.x;
-    a1 += w * v.y;
+  const int tid = threadIdx.x;
+  if (slot_end <= slot_begin) return;
+  {
+    const int r = tid >> 4, j = tid & 15;
+    float mmax = -INFINITY;
+    for (int q = slot_begin + j; q < slot_end; q += 16) mmax = fmaxf(mmax, wm[(int64_t)q * kRows + r]);
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, off));
+    const float msub = (mmax == -INFINITY) ? 0.0f : mmax;
+    float l = 0.0f;
+    for (int q = slot_begin + j; q < slot_end; q += 16)
+      l += exp2f((wm[(int64_t)q * kRows + r] - msub) * kLog2e) * wl[(int64_t)q * kRows + r];
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
+    if (j == 0) {
+      row_s[r] = msub;
+      row_s[kRows + r] = 1.0f / fmaxf(l, 1e-20f);
+    }
   }
-  const float inv = 1.0f / fmaxf(l, 1e-20f);
+  const int lq = tid & 7, f = (tid >> 3) & 1, r = tid >> 4;
+  const int d = blockIdx.y * kCombDims + 4 * f;
+  float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  for (int w0 = slot_begin; w0 < slot_end; w0 += kCombWindow) {
+    const int nw = min(kCombWindow, slot_end - w0);
+    __syncthreads();  // row scalars written / previous window consumed
+    for (int e = tid; e < nw * kRows; e += kCombThreads) {
+      const int q = e >> 4, rr = e & 15;
+      w_s[e] = exp2f((wm[(int64_t)(w0 + q) * kRows + rr] - row_s[rr]) * kLog2e) * row_s[kRows + rr];
+    }
+    __syncthreads();
+    int q = lq;
+    for (; q + 24 < nw; q += 32) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        v[u] = *reinterpret_cast<const float4*>(wo + ((int64_t)(w0 + q + 8 * u) * kRows + r) * latent_dim + d);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const float w = w_s[(q + 8 * u) * kRows + r];
+        acc.x += w * v[u].x;
+        acc.y += w * v[u].y;
+        acc.z += w * v[u].z;
+        acc.w += w * v[u].w;
+      }
+    }
+    for (; q < nw; q += 8) {
+      const float4 v = *reinterpret_cast<const float4*>(wo + ((int64_t)(w0 + q) * kRows + r) * latent_dim + d);
+      const float w = w_s[q * kRows + r];
+      acc.x += w * v.x;
+      acc.y += w * v.y;
+      acc.z += w * v.z;
+      acc.w += w * v.w;
+    }
+  }
+#pragma unroll
+  for (int off = 1; off < 8; off <<= 1) {
+    acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
+    acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
+    acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
+    acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
+  }
+  if (lq != 0 || r >= n_rows || d >= latent_dim) return;
   const int64_t off = (out_row0 + r) * latent_dim + d;
   if (out_dtype == ASTERQ_DTYPE_F32) {
-    *reinterpret_cast<float2*>(reinterpret_cast<float*>(out) + off) = make_float2(a0 * inv, a1 * inv);
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + off) = acc;
   } else {
-    *reinterpret_cast<uint32_t*>(reinterpret_cast<__nv_bfloat16*>(out) + off) = pack_bf162(a0 * inv, a1 * inv);
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + off) =
+        make_uint2(pack_bf162(acc.x, acc.y), pack_bf162(acc.z, acc.w));
   }
 }
 
@@ -1210,7 +1267,7 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
 // the workspace (o [n_jobs][16][latent_dim], then m [n_jobs][16], then l [n_jobs][16]).
 // Context-parallel decode merges each rank's split-KV records this way before
 // the records of all ranks are gathered.
-__global__ void __launch_bounds__(kCombThreads) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
+__global__ void __launch_bounds__(kCombMergeThreads) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                     const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                     int n_slots, int n_jobs, int latent_dim, float* __restrict__ merged) {
   const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
@@ -1445,7 +1502,7 @@ extern "C" int asterq_splitkv_merge(const float* partials, int32_t n_slots, cons
     return set_error(ASTERQ_ERR_MISALIGNED, "merge: pointers must be 16-byte aligned");
   const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
   const float* wl = wm + (int64_t)n_slots * dec::kRows;
-  dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), dec::kCombThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), dec::kCombMergeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged);
   return check_launch("splitkv_merge");
 }
