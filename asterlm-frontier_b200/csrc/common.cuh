@@ -164,6 +164,15 @@ ASTERQ_DEVICE uint32_t s8_lo_nibbles(uint32_t x) { return s8_hi_nibbles(x << 4);
 
 ASTERQ_DEVICE uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
+// 2^x by the hardware approximation with subnormal results flushed to zero (PTX
+// ex2.approx.ftz.f32): softmax weights exp(s - max) <= 1, where a weight below 2^-126 is
+// as good as zero
+ASTERQ_DEVICE float ex2_ftz(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 ASTERQ_DEVICE void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])

@@ -870,10 +870,10 @@ __global__ void __launch_bounds__(kThreads, 1)
               alpha_r[nt][cc] = 1.0f;
               msub[nt][cc] = 0.0f;
             } else {
-              alpha_r[nt][cc] = exp2f((m_prev - m_new) * kLog2e);
+              alpha_r[nt][cc] = ex2_ftz((m_prev - m_new) * kLog2e);
               msub[nt][cc] = m_new;
             }
-            lfac[nt][cc] = (m_team[nt][cc] == -INFINITY) ? 0.0f : exp2f((m_team[nt][cc] - m_new) * kLog2e);
+            lfac[nt][cc] = (m_team[nt][cc] == -INFINITY) ? 0.0f : ex2_ftz((m_team[nt][cc] - m_new) * kLog2e);
             m_team[nt][cc] = m_new;
           }
         // publish the running max after tile i (lanes gid 0 of the team's first warp hold all
@@ -902,8 +902,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int tk = qk_token(tw, m, gid + 8 * h);
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) {
-                const float p0 = exp2f((S[m][nt][2 * h] - msub[nt][0]) * kLog2e);
-                const float p1 = exp2f((S[m][nt][2 * h + 1] - msub[nt][1]) * kLog2e);
+                const float p0 = ex2_ftz((S[m][nt][2 * h] - msub[nt][0]) * kLog2e);
+                const float p1 = ex2_ftz((S[m][nt][2 * h + 1] - msub[nt][1]) * kLog2e);
                 psum[nt][0] += p0;
                 psum[nt][1] += p1;
                 *reinterpret_cast<uint32_t*>(Pc + tk * 32 + ((nt ^ ((tk >> 2) & 1)) << 4) + 4 * tq) = pack_half2(p0, p1);
@@ -918,7 +918,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-              const float pv = exp2f((S[0][nt][c] - msub[nt][c]) * kLog2e);
+              const float pv = ex2_ftz((S[0][nt][c] - msub[nt][c]) * kLog2e);
               P[(8 * nt + 2 * tq + c) * kPStride + 8 * tw + gid] = pv;
               psum[nt][c] += pv;
             }
