@@ -137,11 +137,11 @@ constexpr int kAccBias = 0x4B400000;
 constexpr float kAccBiasF = 12582912.0f;
 
 struct TensorMaps {
-  CUtensorMap codes;  // cold codes  [tokens][256 B], box [128 B][128 rows]
+  CUtensorMap codes;  // cold codes  [tokens][2 x 128 B], box [2 blocks][128 rows][128 B]
   CUtensorMap crope;  // cold rope   [tokens][128 B], box [128 B][128 rows]
-  CUtensorMap hlat;   // hot latent  [tokens][1024 B], box [128 B][32 rows]
+  CUtensorMap hlat;   // hot latent  [tokens][8 x 128 B], box [8 blocks][32 rows][128 B]
   CUtensorMap hrope;  // hot rope    [tokens][128 B], box [128 B][32 rows]
-  CUtensorMap nlat;   // new latent  [total_q][1024 B], box [128 B][32 rows]
+  CUtensorMap nlat;   // new latent  [total_q][8 x 128 B], box [8 blocks][32 rows][128 B]
   CUtensorMap nrope;  // new rope    [total_q][128 B], box [128 B][32 rows]
 };
 
@@ -153,6 +153,15 @@ ASTERQ_DEVICE void tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y, ui
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
           dst),
       "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+// a [blocks][rows][128 B] box of a map whose third dimension steps through the 128-byte
+// blocks of each row: one instruction for a tile's whole rows
+ASTERQ_DEVICE void tma_3d(uint32_t dst, const CUtensorMap* map, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(map), "r"(0), "r"(y), "r"(0), "r"(bar)
       : "memory");
 }
 // byte offset of (row, 16-byte chunk) in a [rows][128 B] region written with the
@@ -442,8 +451,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (t.kind == ASTERQ_TILE_COLD) {
       const int y = t.page * p.page_tokens + t.off;
       mbar_expect_tx(full, 3 * 16384 + 16 * t.n);
-      tma_2d(st + kCodesLo, &maps.codes, 0, y, full);
-      tma_2d(st + kCodesHi, &maps.codes, 128, y, full);
+      tma_3d(st + kCodesLo, &maps.codes, y, full);  // both halves: kCodesHi = kCodesLo + 128 rows x 128 B
       tma_2d(st + kCRope, &maps.crope, 0, y, full);
       bulk_1d(st + kScales, reinterpret_cast<const uint8_t*>(p.cold_scales) + (int64_t)y * 16, 16 * t.n, full);
     } else {
@@ -451,8 +459,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int y = hot ? t.page * p.page_tokens + t.off : t.page + t.off;
       const CUtensorMap* lat = hot ? &maps.hlat : &maps.nlat;
       mbar_expect_tx(full, 9 * 4096);
-#pragma unroll 1
-      for (int g = 0; g < 8; ++g) tma_2d(st + g * kHotBlock, lat, 128 * g, y, full);
+      tma_3d(st, lat, y, full);  // block g lands at g * kHotBlock
       tma_2d(st + kHRope, hot ? &maps.hrope : &maps.nrope, 0, y, full);
     }
   };
@@ -1364,10 +1371,13 @@ EncodeTiledFn encode_fn() {
 }
 
 // 2-D byte tensor [rows][row_bytes] read in boxes of [box_rows][128 B] with the
-// 128-byte swizzle.  An empty pool gets a map of one row of a valid buffer; the
-// kernel never references it (tiles of that kind fail validation).
+// 128-byte swizzle.  With blocks > 1 the rows are blocks x 128 B and the map is 3-D
+// (128 B, rows, blocks): one box [blocks][box_rows][128 B] lands block-major, the layout
+// the kernel reads (each block a [box_rows][128 B] region), in one instruction.  An empty
+// pool gets a map of one row of a valid buffer; the kernel never references it (tiles of
+// that kind fail validation).
 int make_map(CUtensorMap* map, const void* base, int64_t rows, int row_bytes, int box_rows, const void* dummy,
-             int dummy_row_bytes) {
+             int dummy_row_bytes, int blocks = 1) {
   EncodeTiledFn fn = encode_fn();
   if (!fn) return set_error(ASTERQ_ERR_CUDA, "decode: cuTensorMapEncodeTiled unavailable");
   if (!base || rows <= 0) {
@@ -1375,13 +1385,25 @@ int make_map(CUtensorMap* map, const void* base, int64_t rows, int row_bytes, in
     rows = 1;
     row_bytes = dummy_row_bytes;
   }
-  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
-  cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r;
+  if (blocks == 1) {
+    cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+    cuuint32_t box[2] = {128u, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1u, 1u};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  } else {
+    if (row_bytes < 128 * blocks) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: row of %d bytes < %d blocks", row_bytes, blocks);
+    cuuint64_t dims[3] = {128u, (cuuint64_t)rows, (cuuint64_t)blocks};
+    cuuint64_t strides[2] = {(cuuint64_t)row_bytes, 128u};
+    cuuint32_t box[3] = {128u, (cuuint32_t)box_rows, (cuuint32_t)blocks};
+    cuuint32_t estr[3] = {1u, 1u, 1u};
+    r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, estr,
+           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  }
   if (r != CUDA_SUCCESS) return set_error(ASTERQ_ERR_CUDA, "decode: tensor map encoding failed (%d)", (int)r);
   return ASTERQ_OK;
 }
@@ -1427,11 +1449,11 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     // base for the map of an empty pool
     const void* dummy = p->q_lat;
     const int64_t cold_rows = p->n_cold_pages * p->page_tokens, hot_rows = p->n_hot_pages * p->page_tokens;
-    if ((st = dec::make_map(&maps.codes, p->cold_codes, cold_rows, 256, dec::kColdTile, dummy, 1024)) ||
+    if ((st = dec::make_map(&maps.codes, p->cold_codes, cold_rows, 256, dec::kColdTile, dummy, 1024, 2)) ||
         (st = dec::make_map(&maps.crope, p->cold_rope, cold_rows, 128, dec::kColdTile, dummy, 1024)) ||
-        (st = dec::make_map(&maps.hlat, p->hot_latent, hot_rows, 1024, dec::kHotTile, dummy, 1024)) ||
+        (st = dec::make_map(&maps.hlat, p->hot_latent, hot_rows, 1024, dec::kHotTile, dummy, 1024, 8)) ||
         (st = dec::make_map(&maps.hrope, p->hot_rope, hot_rows, 128, dec::kHotTile, dummy, 1024)) ||
-        (st = dec::make_map(&maps.nlat, p->new_latent, p->total_q, 1024, dec::kHotTile, dummy, 1024)) ||
+        (st = dec::make_map(&maps.nlat, p->new_latent, p->total_q, 1024, dec::kHotTile, dummy, 1024, 8)) ||
         (st = dec::make_map(&maps.nrope, p->new_rope, p->total_q, 128, dec::kHotTile, dummy, 1024)))
       return st;
     dec::qprep_kernel<<<p->n_units, dec::kPrepThreads, dec::kPrepSmem, s>>>(*p);
