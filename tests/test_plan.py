@@ -46,7 +46,7 @@ def test_items_partition_tiles_per_row_block():
 
 
 def test_single_item_sequences_write_output_directly():
-    seqs = [_layout([], [(0, 0, 100)], i, 1) for i in range(10)]
+    seqs = [_layout([], [(0, 0, 40)], i, 1) for i in range(10)]
     plan = build_plan(seqs, 16)
     assert (plan.items[:, 4] == -1).all() and plan.n_slots == 0 and plan.combine.shape[0] == 0
 
@@ -111,9 +111,27 @@ def test_persistent_workers_cover_every_tile_once_and_balance(n_sms):
 
 
 def test_persistent_schedule_does_not_split_small_blocks():
-    seqs = [_layout([], [(i, 0, 100)], i, 1) for i in range(10)]
+    # blocks under two full cold tiles of work are never cut
+    seqs = [_layout([], [(i, 0, 40)], i, 1) for i in range(10)]
     plan = build_plan(seqs, 16)
     assert plan.items.shape[0] == 10 and plan.n_slots == 0 and plan.n_workers == 10
+
+
+def test_small_batch_cuts_finer_but_not_below_one_cold_tile():
+    from asterq.plan import _COLD_TILE_NS, _ITEM_NS
+
+    seqs = [_layout([(i, 0, 512) for i in range(14)], [(0, 0, 512), (1, 0, 512)], 0, 1)]  # one 8k sequence
+    plan = build_plan(seqs, 16)
+    assert plan.items.shape[0] > 40  # far more pieces than the 4-cold-tile minimum of a full batch allows
+    cost = _item_ns(plan) - _ITEM_NS
+    single_tile = (plan.items[:, 3] - plan.items[:, 2]) == 1
+    assert ((cost >= sum(_COLD_TILE_NS) - 1) | single_tile).all()
+    # a full batch keeps the larger minimum piece
+    big = build_plan(_ragged_batch(), 16)
+    from asterq.plan import _MIN_PIECE_NS
+
+    split = big.items[:, 4] >= 0
+    assert ((_item_ns(big) - _ITEM_NS)[split] >= 0.5 * _MIN_PIECE_NS).all()
 
 
 def test_max_items_per_seq_deals_whole_blocks_to_workers():
