@@ -129,6 +129,51 @@ def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
     return out
 
 
+def _tile_table(seqs: list[SequenceLayout]) -> tuple[np.ndarray, np.ndarray]:
+    """All sequences' tiles at once (numpy, no per-tile Python): [n_tiles, 4] int32 in the
+    order of _tiles_of per sequence, and [n_seqs + 1] offsets of each sequence's tiles."""
+    rows, seg_kind, seg_len, per_seq = [], [], [], []
+    cold_k, hot_k, new_k = _lib.TILE_COLD, _lib.TILE_HOT, _lib.TILE_NEW
+    for seq in seqs:
+        r0 = len(rows)
+        rows.extend(seq.cold)
+        rows.extend(seq.hot)
+        seg_kind += [cold_k, hot_k]
+        seg_len += [len(seq.cold), len(seq.hot)]
+        if seq.q_len > 0 and seq.attend_new:  # the new tokens: "page" = first row in the batch
+            rows.append((seq.q_start, 0, seq.q_len))
+            seg_kind.append(new_k)
+            seg_len.append(1)
+        per_seq.append(len(rows) - r0)
+    A = np.asarray(rows, dtype=np.int64).reshape(-1, 3)
+    K = np.repeat(np.asarray(seg_kind, dtype=np.int64), np.asarray(seg_len, dtype=np.int64))
+    Pg, Of, N = A[:, 0], A[:, 1], A[:, 2]
+    bad = (N <= 0) | (Of < 0) | (Pg < 0)
+    if bad.any():
+        i = int(np.argmax(bad))
+        raise ValueError(f"bad chunk (page={int(Pg[i])}, offset={int(Of[i])}, n={int(N[i])})")
+    T = np.where(K == cold_k, COLD_TILE, HOT_TILE)
+    cnt = (N + T - 1) // T
+    rep = np.repeat(np.arange(K.shape[0]), cnt)
+    first = np.cumsum(cnt) - cnt
+    j = np.arange(int(cnt.sum())) - first[rep]
+    Tr = T[rep]
+    tiles = np.stack([K[rep], Pg[rep], Of[rep] + j * Tr, np.minimum(Tr, N[rep] - j * Tr)], axis=1).astype(np.int32)
+    chunk_off = np.concatenate(([0], np.cumsum(per_seq)))
+    tile_off = np.concatenate(([0], np.cumsum(cnt)))[chunk_off]
+    return tiles.reshape(-1, 4), tile_off
+
+
+def _tile_costs(tiles: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Per-tile bytes (cost model of the one-CTA-per-item schedule) and estimated ns."""
+    cold = tiles[:, 0] == _lib.TILE_COLD
+    n = tiles[:, 3].astype(np.int64)
+    nbytes = n * np.where(cold, _COLD_TOKEN_BYTES, _HOT_TOKEN_BYTES)
+    ns = np.where(cold, _COLD_TILE_NS[0] + (_COLD_TILE_NS[1] * n) // COLD_TILE,
+                  _HOT_TILE_NS[0] + (_HOT_TILE_NS[1] * n) // HOT_TILE)
+    return nbytes.astype(np.int64), ns.astype(np.int64)
+
+
 def _visible_tiles(seq: SequenceLayout, t0: int, t1: int, rb: int, n_heads: int) -> int:
     """End of the tiles row block `rb` can see: new-token tiles wholly after its last
     token are fully masked (k <= past_len + i, latent_attention.py:151-153) and dropped."""
@@ -234,22 +279,14 @@ def build_plan(
     """
     if n_heads <= 0:
         raise ValueError("n_heads must be positive")
-    tiles: list[tuple[int, int, int, int]] = []
-    seq_tile_ranges = []
     total_q = 0
     for seq in seqs:
         if not (0 < seq.q_len <= MAX_Q_LEN):
             raise ValueError(f"q_len must be in 1..{MAX_Q_LEN} (got {seq.q_len})")
-        for page, off, n in list(seq.cold) + list(seq.hot):
-            if n <= 0 or off < 0 or page < 0:
-                raise ValueError(f"bad chunk (page={page}, offset={off}, n={n})")
-        t0 = len(tiles)
-        tiles.extend(_tiles_of(seq))
-        seq_tile_ranges.append((t0, len(tiles)))
         total_q = max(total_q, seq.q_start + seq.q_len)
-
-    tile_arr = np.asarray(tiles, dtype=np.int32).reshape(-1, 4)
-    costs = np.array([_tile_cost(k, n) for k, _, _, n in tiles], dtype=np.int64)
+    tile_arr, tile_off = _tile_table(seqs)
+    seq_tile_ranges = [(int(a), int(b)) for a, b in zip(tile_off[:-1], tile_off[1:])]
+    costs, tile_ns = _tile_costs(tile_arr)
     prefix = np.concatenate(([0], np.cumsum(costs)))
 
     # work units: (seq, row_block)
@@ -272,8 +309,7 @@ def build_plan(
     unit_arr = np.asarray(unit_rows, dtype=np.int32).reshape(-1, 2)
 
     if persistent and max_items_per_seq is None:
-        tns = np.array([_tile_ns(k, n) for k, _, _, n in tiles], dtype=np.int64)
-        P = np.concatenate(([0], np.cumsum(tns))).tolist()
+        P = np.concatenate(([0], np.cumsum(tile_ns))).tolist()
         work = [(ui, t0, t1) for ui, (_, _, t0, t1, _) in enumerate(units) if t1 > t0]
         pieces = _balanced_cut(work, P, n_workers) if work else []
         by_unit: dict[int, list] = {}
@@ -346,8 +382,7 @@ def build_plan(
     if not persistent or not items:
         return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr)
     # deal the items (longest first) to the least loaded of the workers
-    tns = np.array([_tile_ns(k, n) for k, _, _, n in tiles], dtype=np.int64)
-    P = np.concatenate(([0], np.cumsum(tns)))
+    P = np.concatenate(([0], np.cumsum(tile_ns)))
     heap = [(0, w) for w in range(min(n_workers, len(items)))]
     owner = []
     for it in item_arr:

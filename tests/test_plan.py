@@ -203,3 +203,22 @@ def test_force_partial_fuses_nothing():
     plan = build_plan(seqs, 16, n_sms=8, force_partial=True)
     assert plan.unit_jobs is None and plan.n_separate == plan.combine.shape[0] == plan.n_units
     assert (plan.items[:, 4] >= 0).all()
+
+
+def test_vectorized_tile_table_matches_the_per_sequence_walk():
+    from asterq.plan import _tile_table, _tiles_of
+
+    rng = np.random.default_rng(5)
+    seqs = []
+    for i in range(40):
+        cold = [(int(rng.integers(0, 99)), int(rng.integers(0, 64)), int(rng.integers(1, 513))) for _ in range(rng.integers(0, 5))]
+        hot = [(int(rng.integers(0, 99)), int(rng.integers(0, 64)), int(rng.integers(1, 600))) for _ in range(rng.integers(0, 4))]
+        seqs.append(SequenceLayout(cold=cold, hot=hot, q_start=3 * i, q_len=int(rng.integers(1, 70)),
+                                   attend_new=bool(rng.integers(0, 4))))
+    tiles, off = _tile_table(seqs)
+    want = []
+    for k, seq in enumerate(seqs):
+        mine = _tiles_of(seq)
+        assert off[k + 1] - off[k] == len(mine)
+        want.extend(mine)
+    assert np.array_equal(tiles, np.asarray(want, dtype=np.int32).reshape(-1, 4))
