@@ -1188,18 +1188,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 constexpr int kCombDims = 8;
 constexpr int kCombThreads = 256;     // 16 rows x 2 float4 x 8 record lanes
 constexpr int kCombWindow = 256;      // records whose weights are staged at a time
-constexpr int kCombMergeThreads = kRows * kCombDims / 2;  // merge_kernel: 16 rows x 4 pairs
-__global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
-                                                      const float* __restrict__ wl, const int32_t* __restrict__ jobs,
-                                                      int n_slots, int latent_dim, void* __restrict__ out,
-                                                      int out_dtype) {
+// kMerge: write the merged record unnormalized (o, m, l) to record blockIdx.x of `out`
+// (laid out like the workspace: o [n_jobs][16][latent_dim], m [n_jobs][16], l [n_jobs][16])
+// instead of the normalized output rows.
+template <bool kMerge>
+__device__ __forceinline__ void combine_job(const float* __restrict__ wo, const float* __restrict__ wm,
+                                            const float* __restrict__ wl, const int32_t* __restrict__ jobs, int n_slots,
+                                            int n_jobs, int latent_dim, void* __restrict__ out, int out_dtype) {
   __shared__ float w_s[kCombWindow * kRows];
   __shared__ float row_s[2 * kRows];  // per-row max, 1 / sum
   const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
   const int slot_begin = max(job.x, 0), slot_end = min(job.y, n_slots), n_rows = min(job.w, kRows);
   const int64_t out_row0 = job.z;
   const int tid = threadIdx.x;
-  if (slot_end <= slot_begin) return;
+  if (!kMerge && slot_end <= slot_begin) return;  // (a merge still writes an empty record)
   {
     const int r = tid >> 4, j = tid & 15;
     float mmax = -INFINITY;
@@ -1214,7 +1216,12 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
     for (int off = 1; off < 16; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
     if (j == 0) {
       row_s[r] = msub;
-      row_s[kRows + r] = 1.0f / fmaxf(l, 1e-20f);
+      row_s[kRows + r] = kMerge ? 1.0f : 1.0f / fmaxf(l, 1e-20f);
+      if (kMerge && blockIdx.y == 0) {
+        float* mm = reinterpret_cast<float*>(out) + (int64_t)n_jobs * kRows * latent_dim;
+        mm[(int64_t)blockIdx.x * kRows + r] = mmax;
+        mm[(int64_t)n_jobs * kRows + (int64_t)blockIdx.x * kRows + r] = l;
+      }
     }
   }
   const int lq = tid & 7, f = (tid >> 3) & 1, r = tid >> 4;
@@ -1259,7 +1266,12 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
     acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
     acc.w += __shfl_xor_sync(0xffffffffu, acc.w, off);
   }
-  if (lq != 0 || r >= n_rows || d >= latent_dim) return;
+  if (lq != 0 || d >= latent_dim) return;
+  if (kMerge) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + ((int64_t)blockIdx.x * kRows + r) * latent_dim + d) = acc;
+    return;
+  }
+  if (r >= n_rows) return;
   const int64_t off = (out_row0 + r) * latent_dim + d;
   if (out_dtype == ASTERQ_DTYPE_F32) {
     *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + off) = acc;
@@ -1269,37 +1281,22 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
   }
 }
 
+__global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
+                                                      const float* __restrict__ wl, const int32_t* __restrict__ jobs,
+                                                      int n_slots, int latent_dim, void* __restrict__ out,
+                                                      int out_dtype) {
+  combine_job<false>(wo, wm, wl, jobs, n_slots, 0, latent_dim, out, out_dtype);
+}
+
 // Merge partial records into fewer partial records (same rule, no normalisation):
 // job j turns slots [slot_begin, slot_end) into record j of `merged`, laid out like
 // the workspace (o [n_jobs][16][latent_dim], then m [n_jobs][16], then l [n_jobs][16]).
 // Context-parallel decode merges each rank's split-KV records this way before
 // the records of all ranks are gathered.
-__global__ void __launch_bounds__(kCombMergeThreads) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
+__global__ void __launch_bounds__(kCombThreads) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                     const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                     int n_slots, int n_jobs, int latent_dim, float* __restrict__ merged) {
-  const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
-  const int slot_begin = max(job.x, 0), slot_end = min(job.y, n_slots);
-  const int r = threadIdx.x / (kCombDims / 2), d = blockIdx.y * kCombDims + 2 * (threadIdx.x % (kCombDims / 2));
-  if (d >= latent_dim) return;
-  float mmax = -INFINITY;
-  for (int s = slot_begin; s < slot_end; ++s) mmax = fmaxf(mmax, wm[(int64_t)s * kRows + r]);
-  const float msub = (mmax == -INFINITY) ? 0.0f : mmax;
-  float l = 0.0f, a0 = 0.0f, a1 = 0.0f;
-  for (int s = slot_begin; s < slot_end; ++s) {
-    const float w = exp2f((wm[(int64_t)s * kRows + r] - msub) * kLog2e);
-    l += w * wl[(int64_t)s * kRows + r];
-    const float2 v = *reinterpret_cast<const float2*>(wo + ((int64_t)s * kRows + r) * latent_dim + d);
-    a0 += w * v.x;
-    a1 += w * v.y;
-  }
-  float* mo = merged;
-  float* mm = mo + (int64_t)n_jobs * kRows * latent_dim;
-  float* ml = mm + (int64_t)n_jobs * kRows;
-  *reinterpret_cast<float2*>(mo + ((int64_t)blockIdx.x * kRows + r) * latent_dim + d) = make_float2(a0, a1);
-  if (blockIdx.y == 0 && threadIdx.x % (kCombDims / 2) == 0) {
-    mm[(int64_t)blockIdx.x * kRows + r] = mmax;
-    ml[(int64_t)blockIdx.x * kRows + r] = l;
-  }
+  combine_job<true>(wo, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged, ASTERQ_DTYPE_F32);
 }
 
 // ---------------------------------------------------------------------------
@@ -1524,7 +1521,7 @@ extern "C" int asterq_splitkv_merge(const float* partials, int32_t n_slots, cons
     return set_error(ASTERQ_ERR_MISALIGNED, "merge: pointers must be 16-byte aligned");
   const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
   const float* wl = wm + (int64_t)n_slots * dec::kRows;
-  dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), dec::kCombMergeThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+  dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), dec::kCombThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged);
   return check_launch("splitkv_merge");
 }
