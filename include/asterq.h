@@ -111,7 +111,7 @@ int asterq_codec_status(int32_t* timeouts);
  *          (rotated, fixed-point, fragment-ordered) are prepared once per call into the workspace.
  *   items [n_items][8] int32 = {unit, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
  *          16 query rows (t, h) per row block, rows flattened as t*n_heads + h; one CTA per item, or
-          with a workers table one CTA per worker running its items in order.
+ *          with a workers table one CTA per worker running its items in order.
  *          slot < 0: the item covers the whole sequence and writes `out` directly;
  *          slot >= 0: it writes an (m, l, o) partial to the workspace.
  *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
