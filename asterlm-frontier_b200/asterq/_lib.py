@@ -44,6 +44,7 @@ EXPORTED_SYMBOLS = (
     "asterq_latent_decode_noalloc",
     "asterq_splitkv_combine",
     "asterq_splitkv_merge",
+    "asterq_splitkv_combine_ranks",
 )
 
 
@@ -142,6 +143,8 @@ def load() -> ctypes.CDLL:
     lib.asterq_splitkv_combine.argtypes = [vp, i32, vp, i32, i32, vp, i32, vp]
     lib.asterq_splitkv_merge.restype = ctypes.c_int
     lib.asterq_splitkv_merge.argtypes = [vp, i32, vp, i32, i32, vp, vp]
+    lib.asterq_splitkv_combine_ranks.restype = ctypes.c_int
+    lib.asterq_splitkv_combine_ranks.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp]
     _lib = lib
     return lib
 

@@ -10,8 +10,11 @@ window and the step's new tokens, so it takes fewer chunks).  Each rank:
    ``asterq_splitkv_merge`` (about 33 KB per row block);
 3. exchanges the merged records with one ``all_gather`` over the process group
    (NCCL on GPUs; the records are fp32 in the workspace layout);
-4. combines the gathered records with ``asterq_splitkv_combine`` into the
-   context latents, identically on every rank.
+4. combines the gathered records where they landed with
+   ``asterq_splitkv_combine_ranks`` into the context latents, identically on
+   every rank.
+
+``capture`` records the four steps as one CUDA graph per rank.
 
 The merge rule is the reference's online softmax (latent_attention.py:212-220)
 applied across ranks instead of across chunks.  No TMA or library kernel reads
@@ -25,7 +28,7 @@ from dataclasses import replace
 import torch
 
 from . import _lib
-from .decode import LATENT_DIM, DeviceDecodePlan, LatentPools, make_params
+from .decode import LATENT_DIM, DeviceDecodePlan, LatentPools, capture_step, make_params
 from .plan import ROWS_PER_BLOCK, SequenceLayout, build_plan
 from .sharding import COLD_TOKEN_BYTES, HOT_TOKEN_BYTES
 
@@ -79,15 +82,18 @@ class ContextParallelDecoder:
         self.q_len = layout.q_len
         self.merged = torch.empty(self.n_rb * RECORD_FLOATS, dtype=torch.float32, device=self.device)
         self.gathered = torch.empty(world * self.n_rb * RECORD_FLOATS, dtype=torch.float32, device=self.device)
-        self.slot_major = torch.empty_like(self.gathered)
-        jobs = [(rb * world, (rb + 1) * world, int(self.plan.combine[rb, 2]), int(self.plan.combine[rb, 3]))
-                for rb in range(self.n_rb)]
+        # job rb merges record rb of every rank (asterq_splitkv_combine_ranks)
+        jobs = [(0, world, int(self.plan.combine[rb, 2]), int(self.plan.combine[rb, 3])) for rb in range(self.n_rb)]
         self.final_jobs = torch.tensor(jobs, dtype=torch.int32, device=self.device).reshape(-1, 4)
+        # the decode's own output rows stay unwritten (every item writes partial records)
+        self._unused_out = torch.empty(layout.q_len, n_heads, LATENT_DIM, dtype=torch.float32, device=self.device)
 
     def partial(self, q_lat, q_rope, new_latent, new_rope, *, softmax_scale: float,
                 logit_softcap: float | None = None) -> torch.Tensor:
         """Steps 1-2: this rank's merged (m, l, o) records, [n_rb * 16 * 514] fp32."""
-        out = torch.empty(q_lat.shape[0], self.n_heads, LATENT_DIM, dtype=torch.float32, device=self.device)
+        out = self._unused_out
+        if out.shape[0] != q_lat.shape[0]:
+            out = torch.empty(q_lat.shape[0], self.n_heads, LATENT_DIM, dtype=torch.float32, device=self.device)
         p = make_params(self.pools, self.dplan, q_lat, q_rope, new_latent, new_rope, out, n_heads=self.n_heads,
                         softmax_scale=softmax_scale, logit_softcap=logit_softcap)
         p.n_combine = 0  # the records are merged below, not combined
@@ -100,21 +106,15 @@ class ContextParallelDecoder:
         return self.merged
 
     def finish(self, gathered: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
-        """Step 4: combine the records of all ranks (rank-major as all_gather leaves them) into `out`."""
-        w, n = self.world, self.n_rb
-        o_part = gathered.view(w, n * RECORD_FLOATS)
-        src_o = o_part[:, : n * ROWS_PER_BLOCK * LATENT_DIM].reshape(w, n, ROWS_PER_BLOCK * LATENT_DIM)
-        src_m = o_part[:, n * ROWS_PER_BLOCK * LATENT_DIM: n * ROWS_PER_BLOCK * (LATENT_DIM + 1)].reshape(w, n, ROWS_PER_BLOCK)
-        src_l = o_part[:, n * ROWS_PER_BLOCK * (LATENT_DIM + 1):].reshape(w, n, ROWS_PER_BLOCK)
-        dst = self.slot_major
-        no = w * n * ROWS_PER_BLOCK * LATENT_DIM
-        dst[:no].view(n, w, -1).copy_(src_o.transpose(0, 1))
-        dst[no: no + w * n * ROWS_PER_BLOCK].view(n, w, -1).copy_(src_m.transpose(0, 1))
-        dst[no + w * n * ROWS_PER_BLOCK:].view(n, w, -1).copy_(src_l.transpose(0, 1))
+        """Step 4: combine the records of all ranks (rank-major as all_gather leaves them) into `out`.
+
+        ``asterq_splitkv_combine_ranks`` reads the gathered records in place.
+        """
         dtype = _lib.DTYPE_F32 if out.dtype == torch.float32 else _lib.DTYPE_BF16
         lib = _lib.load()
-        _lib.check(lib.asterq_splitkv_combine(dst.data_ptr(), w * n, self.final_jobs.data_ptr(), n, LATENT_DIM,
-                                              out.data_ptr(), dtype, _lib.stream_handle(self.device)))
+        _lib.check(lib.asterq_splitkv_combine_ranks(gathered.data_ptr(), self.world, self.n_rb,
+                                                    self.final_jobs.data_ptr(), LATENT_DIM, out.data_ptr(), dtype,
+                                                    _lib.stream_handle(self.device)))
         return out
 
     def step(self, q_lat, q_rope, new_latent, new_rope, out, *, group=None, softmax_scale: float,
@@ -126,3 +126,16 @@ class ContextParallelDecoder:
                            logit_softcap=logit_softcap)
         dist.all_gather_into_tensor(self.gathered, rec, group=group)
         return self.finish(self.gathered, out)
+
+    def capture(self, q_lat, q_rope, new_latent, new_rope, out, *, group=None, softmax_scale: float,
+                logit_softcap: float | None = None) -> torch.cuda.CUDAGraph:
+        """``step`` recorded as one CUDA graph (decode, merge, all-gather, combine) on these buffers.
+
+        Each ``replay()`` is one context-parallel step with no Python between the
+        launches; every rank must capture and replay in the same order.  Refill the
+        inputs in place between replays, and release the graph before the process
+        group is destroyed (it holds an NCCL collective).
+        """
+        return capture_step(lambda: self.step(q_lat, q_rope, new_latent, new_rope, out, group=group,
+                                              softmax_scale=softmax_scale, logit_softcap=logit_softcap),
+                            self.device)

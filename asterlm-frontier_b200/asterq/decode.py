@@ -151,6 +151,28 @@ def _check_inputs(q_lat, q_rope, new_latent, new_rope, n_heads):
         raise ValueError("new_latent / new_rope must be [total_q, 512] / [total_q, 64]")
 
 
+def capture_step(fn, device, warmup: int = 3) -> "torch.cuda.CUDAGraph":
+    """Record `fn` (a decode step on fixed buffers) as a CUDA graph; replay it with ``.replay()``.
+
+    `fn` runs `warmup` times eagerly on a side stream first (NCCL collectives
+    need that before capture).  Every tensor `fn` reads or writes must stay
+    allocated while the graph lives; refill inputs in place between replays.
+    A graph holding an NCCL collective must be released before the process
+    group is destroyed.
+    """
+    dev = torch.device(device)
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        for _ in range(warmup):
+            fn()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    return graph
+
+
 def latent_decode(
     pools: LatentPools,
     dplan: DeviceDecodePlan,

@@ -1191,12 +1191,24 @@ constexpr int kCombWindow = 256;      // records whose weights are staged at a t
 // kMerge: write the merged record unnormalized (o, m, l) to record blockIdx.x of `out`
 // (laid out like the workspace: o [n_jobs][16][latent_dim], m [n_jobs][16], l [n_jobs][16])
 // instead of the normalized output rows.
+// Where slot q of job j lives (floats): o rows at wo + j * o_job + q * o_slot + row * latent_dim,
+// m at wm + j * ml_job + q * ml_slot + row (l likewise).  The workspace layout is
+// {16 * latent_dim, 16, 0, 0}; records gathered rank-major from `world` ranks of `n`
+// merged records each are {n * record, n * record, 16 * latent_dim, 16}, record = 16 * (latent_dim + 2).
+struct SlotLayout {
+  int64_t o_slot, ml_slot, o_job, ml_job;
+};
+
 template <bool kMerge>
 __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const float* __restrict__ wm,
                                             const float* __restrict__ wl, const int32_t* __restrict__ jobs, int n_slots,
-                                            int n_jobs, int latent_dim, void* __restrict__ out, int out_dtype) {
+                                            int n_jobs, int latent_dim, void* __restrict__ out, int out_dtype,
+                                            const SlotLayout lay) {
   __shared__ float w_s[kCombWindow * kRows];
   __shared__ float row_s[2 * kRows];  // per-row max, 1 / sum
+  wo += blockIdx.x * lay.o_job;
+  wm += blockIdx.x * lay.ml_job;
+  wl += blockIdx.x * lay.ml_job;
   const int4 job = *reinterpret_cast<const int4*>(jobs + 4 * (int64_t)blockIdx.x);
   const int slot_begin = max(job.x, 0), slot_end = min(job.y, n_slots), n_rows = min(job.w, kRows);
   const int64_t out_row0 = job.z;
@@ -1205,13 +1217,13 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
   {
     const int r = tid >> 4, j = tid & 15;
     float mmax = -INFINITY;
-    for (int q = slot_begin + j; q < slot_end; q += 16) mmax = fmaxf(mmax, wm[(int64_t)q * kRows + r]);
+    for (int q = slot_begin + j; q < slot_end; q += 16) mmax = fmaxf(mmax, wm[q * lay.ml_slot + r]);
 #pragma unroll
     for (int off = 1; off < 16; off <<= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, off));
     const float msub = (mmax == -INFINITY) ? 0.0f : mmax;
     float l = 0.0f;
     for (int q = slot_begin + j; q < slot_end; q += 16)
-      l += exp2f((wm[(int64_t)q * kRows + r] - msub) * kLog2e) * wl[(int64_t)q * kRows + r];
+      l += exp2f((wm[q * lay.ml_slot + r] - msub) * kLog2e) * wl[q * lay.ml_slot + r];
 #pragma unroll
     for (int off = 1; off < 16; off <<= 1) l += __shfl_xor_sync(0xffffffffu, l, off);
     if (j == 0) {
@@ -1232,7 +1244,7 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
     __syncthreads();  // row scalars written / previous window consumed
     for (int e = tid; e < nw * kRows; e += kCombThreads) {
       const int q = e >> 4, rr = e & 15;
-      w_s[e] = exp2f((wm[(int64_t)(w0 + q) * kRows + rr] - row_s[rr]) * kLog2e) * row_s[kRows + rr];
+      w_s[e] = exp2f((wm[(w0 + q) * lay.ml_slot + rr] - row_s[rr]) * kLog2e) * row_s[kRows + rr];
     }
     __syncthreads();
     int q = lq;
@@ -1240,7 +1252,7 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
       float4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        v[u] = *reinterpret_cast<const float4*>(wo + ((int64_t)(w0 + q + 8 * u) * kRows + r) * latent_dim + d);
+        v[u] = *reinterpret_cast<const float4*>(wo + (w0 + q + 8 * u) * lay.o_slot + r * latent_dim + d);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const float w = w_s[(q + 8 * u) * kRows + r];
@@ -1251,7 +1263,7 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
       }
     }
     for (; q < nw; q += 8) {
-      const float4 v = *reinterpret_cast<const float4*>(wo + ((int64_t)(w0 + q) * kRows + r) * latent_dim + d);
+      const float4 v = *reinterpret_cast<const float4*>(wo + (w0 + q) * lay.o_slot + r * latent_dim + d);
       const float w = w_s[q * kRows + r];
       acc.x += w * v.x;
       acc.y += w * v.y;
@@ -1284,8 +1296,8 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
 __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                       const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                       int n_slots, int latent_dim, void* __restrict__ out,
-                                                      int out_dtype) {
-  combine_job<false>(wo, wm, wl, jobs, n_slots, 0, latent_dim, out, out_dtype);
+                                                      int out_dtype, const SlotLayout lay) {
+  combine_job<false>(wo, wm, wl, jobs, n_slots, 0, latent_dim, out, out_dtype, lay);
 }
 
 // Merge partial records into fewer partial records (same rule, no normalisation):
@@ -1296,7 +1308,8 @@ __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __re
 __global__ void __launch_bounds__(kCombThreads) merge_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                     const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                     int n_slots, int n_jobs, int latent_dim, float* __restrict__ merged) {
-  combine_job<true>(wo, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged, ASTERQ_DTYPE_F32);
+  combine_job<true>(wo, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged, ASTERQ_DTYPE_F32,
+                    SlotLayout{(int64_t)kRows * latent_dim, kRows, 0, 0});
 }
 
 // ---------------------------------------------------------------------------
@@ -1483,7 +1496,8 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     const float* wm = wo + (int64_t)p->n_slots * dec::kRows * dec::kL;
     const float* wl = wm + (int64_t)p->n_slots * dec::kRows;
     dec::combine_kernel<<<dim3(p->n_combine, dec::kL / dec::kCombDims), dec::kCombThreads, 0, s>>>(
-        wo, wm, wl, p->combine, p->n_slots, dec::kL, p->out, p->out_dtype);
+        wo, wm, wl, p->combine, p->n_slots, dec::kL, p->out, p->out_dtype,
+        dec::SlotLayout{(int64_t)dec::kRows * dec::kL, dec::kRows, 0, 0});
     st = check_launch("splitkv_combine");
   }
   return st;
@@ -1505,7 +1519,8 @@ extern "C" int asterq_splitkv_combine(const float* partials, int32_t n_slots, co
   const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
   const float* wl = wm + (int64_t)n_slots * dec::kRows;
   dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), dec::kCombThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
-      partials, wm, wl, combine, n_slots, latent_dim, out, out_dtype);
+      partials, wm, wl, combine, n_slots, latent_dim, out, out_dtype,
+      dec::SlotLayout{(int64_t)dec::kRows * latent_dim, dec::kRows, 0, 0});
   return check_launch("splitkv_combine");
 }
 
@@ -1524,6 +1539,30 @@ extern "C" int asterq_splitkv_merge(const float* partials, int32_t n_slots, cons
   dec::merge_kernel<<<dim3(n_jobs, dec::kL / dec::kCombDims), dec::kCombThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, jobs, n_slots, n_jobs, latent_dim, merged);
   return check_launch("splitkv_merge");
+}
+
+extern "C" int asterq_splitkv_combine_ranks(const float* gathered, int32_t world, int32_t n_blocks,
+                                            const int32_t* jobs, int32_t latent_dim, void* out, int32_t out_dtype,
+                                            void* stream) {
+  clear_error();
+  if (latent_dim != dec::kL) return set_error(ASTERQ_ERR_UNSUPPORTED, "combine_ranks: latent_dim must be 512");
+  if (world <= 0 || n_blocks < 0) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "combine_ranks: bad sizes");
+  if (n_blocks == 0) return ASTERQ_OK;
+  if (!gathered || !jobs || !out) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "combine_ranks: null pointer");
+  if (out_dtype != ASTERQ_DTYPE_F32 && out_dtype != ASTERQ_DTYPE_BF16)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "combine_ranks: out_dtype must be f32 or bf16");
+  if ((reinterpret_cast<uintptr_t>(gathered) | reinterpret_cast<uintptr_t>(jobs) | reinterpret_cast<uintptr_t>(out)) &
+      15)
+    return set_error(ASTERQ_ERR_MISALIGNED, "combine_ranks: pointers must be 16-byte aligned");
+  // rank r's part: o [n_blocks][16][512], m [n_blocks][16], l [n_blocks][16]
+  const int64_t part = (int64_t)n_blocks * dec::kRows * (latent_dim + 2);
+  const float* wm = gathered + (int64_t)n_blocks * dec::kRows * latent_dim;
+  const float* wl = wm + (int64_t)n_blocks * dec::kRows;
+  dec::combine_kernel<<<dim3(n_blocks, dec::kL / dec::kCombDims), dec::kCombThreads, 0,
+                        reinterpret_cast<cudaStream_t>(stream)>>>(
+      gathered, wm, wl, jobs, world, latent_dim, out, out_dtype,
+      dec::SlotLayout{part, part, (int64_t)dec::kRows * latent_dim, dec::kRows});
+  return check_launch("splitkv_combine_ranks");
 }
 
 // ---------------------------------------------------------------------------

@@ -533,21 +533,29 @@ def context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier) -> d
     def step():
         dec.step(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SOFTMAX_SCALE)
 
-    for _ in range(max(3, args.warmup)):
-        step()
+    def timed(fn, iters=20):
+        for _ in range(max(3, args.warmup)):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(s.elapsed_time(e) / iters)
+
+    ms_eager = timed(step)
+    # the same step as one CUDA graph per rank (decode, merge, NCCL all-gather, combine)
+    graph = dec.capture(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SOFTMAX_SCALE)
+    ms = timed(graph.replay)
     torch.cuda.synchronize()
-    barrier()
-    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    iters = 20
-    s.record()
-    for _ in range(iters):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = max_over_ranks(s.elapsed_time(e) / iters)
+    del graph  # released before the process group is destroyed
     alg = wl.algorithmic_bytes()
-    return {"seqs": 1, "cached_tokens": int(wl.lengths[0]), "ranks": world, "ms": ms,
+    return {"seqs": 1, "cached_tokens": int(wl.lengths[0]), "ranks": world, "ms": ms, "ms_eager": ms_eager,
             "seq_steps_per_s": 1e3 / ms, "GB/s_total": alg / (ms / 1e3) / 1e9,
+            "launch": "CUDA graph replay per step (ms_eager: the same step launched from Python)",
             "collective": "one all_gather_into_tensor of 32,896 B per rank per step (NCCL)"}
 
 
@@ -599,7 +607,7 @@ def extras(dev, args) -> dict:
     """Secondary single-GPU measurements: the write path (config 2) and configs 1, 4, 5."""
     import torch
 
-    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.decode import DeviceDecodePlan, capture_step, latent_decode
     from asterq.plan import build_plan
     from asterq.synth import c1_inputs, c4_workload, c5_workload, PoolBuilder
 
@@ -612,11 +620,16 @@ def extras(dev, args) -> dict:
         plan = build_plan(wl.layouts, wl.n_heads)
         dp = DeviceDecodePlan(plan, dev)
         out = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
-        ms = timed(lambda: latent_decode(wl.pools, dp, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope,
-                                         softmax_scale=SOFTMAX_SCALE, out=out), iters)
+        fn = lambda: latent_decode(wl.pools, dp, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope,  # noqa: E731
+                                   softmax_scale=SOFTMAX_SCALE, out=out)
+        ms = timed(fn, iters)
+        graph = capture_step(fn, dev)
+        ms_graph = timed(graph.replay, iters)
+        del graph
         b = wl.algorithmic_bytes()
         res[name] = {"seqs": len(wl.lengths), "q_len": wl.q_len, "ms": ms, "seq_steps_per_s": len(wl.lengths) / ms * 1e3,
-                     "GB/s": b / ms / 1e6, "frac_hbm": b / ms / 1e6 / peak, "TFLOP/s": wl.flops() / ms / 1e9}
+                     "GB/s": b / ms / 1e6, "frac_hbm": b / ms / 1e6 / peak, "TFLOP/s": wl.flops() / ms / 1e9,
+                     "ms_graph": ms_graph, "seq_steps_per_s_graph": len(wl.lengths) / ms_graph * 1e3}
 
     inp = c1_inputs(seed=0)
     b1 = PoolBuilder([8192], [1024], q_len=1, n_heads=16, device=dev)

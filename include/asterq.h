@@ -13,6 +13,8 @@
  *                          iterating the cache like cache.py:139-159 iter_chunks
  *   asterq_splitkv_combine layers/latent_attention.py:212-220 (the online-softmax merge rule)
  *   asterq_splitkv_merge   the same rule, leaving merged (m, l, o) records for a later combine
+ *   asterq_splitkv_combine_ranks  the same rule over the merged records of all ranks, read where
+ *                          a rank-major all-gather left them
  *
  * Every function returns ASTERQ_OK (0) or a negative status and never aborts;
  * asterq_last_error() describes the last failure on the calling thread.  All
@@ -214,6 +216,19 @@ int asterq_splitkv_combine(const float* partials, int32_t n_slots, const int32_t
  */
 int asterq_splitkv_merge(const float* partials, int32_t n_slots, const int32_t* jobs, int32_t n_jobs,
                          int32_t latent_dim, float* merged, void* stream);
+
+/*
+ * Combine the merged records of `world` ranks as a rank-major all-gather leaves
+ * them: rank r's part, at gathered + r * n_blocks * 16 * (latent_dim + 2), is the
+ * asterq_splitkv_merge output for n_blocks jobs (o [n_blocks][16][latent_dim],
+ * m [n_blocks][16], l [n_blocks][16]).  jobs int32 [n_blocks][4]: job b merges
+ * record b of ranks [slot_begin, slot_end) (normally 0 and world) into rows
+ * out_row0 .. out_row0 + n_rows - 1 of `out`.  Same rule as
+ * asterq_splitkv_combine (latent_attention.py:212-220 applied across ranks),
+ * with no reordering copy of the gathered records first.
+ */
+int asterq_splitkv_combine_ranks(const float* gathered, int32_t world, int32_t n_blocks, const int32_t* jobs,
+                                 int32_t latent_dim, void* out, int32_t out_dtype, void* stream);
 
 #ifdef __cplusplus
 }

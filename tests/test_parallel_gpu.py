@@ -2,8 +2,11 @@
 
 Each emulated rank decodes its chunk range into partial records, merges them
 with ``asterq_splitkv_merge``, and the records are concatenated rank-major as
-``all_gather_into_tensor`` would leave them; ``finish`` must reproduce the
-single-GPU oracle decode (rel-L2 <= 1e-3, max-abs <= 2e-2, fp32 output).
+``all_gather_into_tensor`` would leave them; ``finish`` (which combines them in
+place with ``asterq_splitkv_combine_ranks``) must reproduce the single-GPU
+oracle decode (rel-L2 <= 1e-3, max-abs <= 2e-2, fp32 output), with one or
+several 16-row blocks per rank (q_len 1 to 3).  Decode and context-parallel
+steps recorded as CUDA graphs must replay to the eager result.
 """
 from __future__ import annotations
 
@@ -20,19 +23,19 @@ pytestmark = pytest.mark.gpu
 SCALE = 1.0 / math.sqrt(512 + 64)
 
 
-@pytest.mark.parametrize("world", [1, 2, 3, 8])
-def test_emulated_ranks_match_oracle(cuda, world):
+@pytest.mark.parametrize("world,q_len", [(1, 1), (2, 1), (3, 1), (8, 1), (3, 2), (2, 3)])
+def test_emulated_ranks_match_oracle(cuda, world, q_len):
     from asterq.context_parallel import ContextParallelDecoder
     from asterq.synth import PoolBuilder, c1_inputs
 
     ctx, hot = 20 * 512 + 300, 700
-    inp = c1_inputs(seed=40 + world, ctx=ctx, q_len=1)
-    b = PoolBuilder([ctx], [hot], q_len=1, n_heads=16, device=cuda)
+    inp = c1_inputs(seed=40 + world, ctx=ctx, q_len=q_len)
+    b = PoolBuilder([ctx], [hot], q_len=q_len, n_heads=16, device=cuda)
     b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
     wl = b.finish("cp")
     decs = [ContextParallelDecoder(wl.pools, wl.layouts[0], 16, r, world, cuda) for r in range(world)]
     recs = [d.partial(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE).clone() for d in decs]
-    out = torch.empty(1, 16, 512, dtype=torch.float32, device=cuda)
+    out = torch.empty(q_len, 16, 512, dtype=torch.float32, device=cuda)
     decs[0].finish(torch.cat(recs), out)
     torch.cuda.synchronize()
     lat, rope = inp["latent"].float().numpy(), inp["rope"].float().numpy()
@@ -72,3 +75,67 @@ def test_merge_then_combine_equals_direct_combine(cuda):
                                           _lib.DTYPE_F32, _lib.stream_handle(cuda)))
     torch.cuda.synchronize()
     assert O.rel_l2(out.cpu().numpy(), direct.cpu().numpy()) < 1e-6
+
+
+def test_decode_step_replays_as_cuda_graph(cuda):
+    """A decode step recorded by ``capture_step`` replays to the eager step's exact output."""
+    from asterq.decode import DeviceDecodePlan, capture_step, latent_decode
+    from asterq.plan import build_plan
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    ctx = 6 * 512 + 200
+    inp = c1_inputs(seed=91, ctx=ctx, q_len=1)
+    b = PoolBuilder([ctx], [700], q_len=1, n_heads=16, device=cuda)
+    b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    wl = b.finish("g")
+    dp = DeviceDecodePlan(build_plan(wl.layouts, 16), cuda)
+    out = torch.empty(1, 16, 512, dtype=torch.float32, device=cuda)
+
+    def step():
+        latent_decode(wl.pools, dp, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE, out=out)
+
+    step()
+    eager = out.clone()
+    graph = capture_step(step, cuda)
+    out.zero_()
+    for _ in range(2):
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(out, eager)
+    del graph
+
+
+def test_context_parallel_step_replays_as_cuda_graph(cuda):
+    """The context-parallel step (decode, merge, NCCL all-gather, combine) captured at world size 1."""
+    import torch.distributed as dist
+
+    from asterq.context_parallel import ContextParallelDecoder
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    if dist.is_initialized():
+        pytest.skip("a process group is already initialised in this process")
+    ctx, hot = 12 * 512 + 100, 600
+    inp = c1_inputs(seed=92, ctx=ctx, q_len=1)
+    b = PoolBuilder([ctx], [hot], q_len=1, n_heads=16, device=cuda)
+    b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    wl = b.finish("cpg")
+    dist.init_process_group("nccl", store=dist.HashStore(), rank=0, world_size=1, device_id=cuda)
+    try:
+        dec = ContextParallelDecoder(wl.pools, wl.layouts[0], 16, 0, 1, cuda)
+        out = torch.empty(1, 16, 512, dtype=torch.float32, device=cuda)
+        dec.step(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SCALE)
+        eager = out.clone()
+        graph = dec.capture(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SCALE)
+        out.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(out, eager)
+        del graph
+        torch.cuda.synchronize()
+    finally:
+        dist.destroy_process_group()
+    lat, rope = inp["latent"].float().numpy(), inp["rope"].float().numpy()
+    cache = O.build_cache_split(lat[:ctx], rope[:ctx], hot, 512)
+    ref = O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[ctx:], rope[ctx:], cache, SCALE)
+    got = eager.cpu().numpy()
+    assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2
