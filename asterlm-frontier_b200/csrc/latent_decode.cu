@@ -1179,14 +1179,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // Merge partial records (latent_attention.py:212-220 applied across splits).
-// Grid: (combine job, 8-dim slice of the latent), so a long sequence's many records are
-// read by 64 CTAs per job.  256 threads: first the per-row max and sum over all of the
-// job's records (16 threads per row), then each (row, 4 dims) output is accumulated by 8
-// lanes that take every 8th record, four records' loads in flight per lane, and summed
-// with shuffles.  The records' weights w / l are staged in shared memory 256 records at a
-// time.
-constexpr int kCombDims = 8;
-constexpr int kCombThreads = 256;     // 16 rows x 2 float4 x 8 record lanes
+// Grid: (combine job, 4-dim slice of the latent), so a long sequence's many records are
+// read by 128 CTAs per job.  256 threads: first the per-row max and sum over all of the
+// job's records (16 threads per row, four records' loads in flight), then each (row,
+// 4 dims) output is accumulated by 16 lanes that take every 16th record, four records'
+// loads in flight per lane, and summed with shuffles.  The records' weights w / l are
+// staged in shared memory 256 records at a time.  The loop is a chain of dependent L2
+// round trips, so it is cut short by spreading records over lanes and CTAs.
+constexpr int kCombDims = 4;
+constexpr int kCombLanes = 16;        // record lanes per output
+constexpr int kCombThreads = 256;     // 16 rows x 16 record lanes (one float4 of output each)
 constexpr int kCombWindow = 256;      // records whose weights are staged at a time
 // kMerge: write the merged record unnormalized (o, m, l) to record blockIdx.x of `out`
 // (laid out like the workspace: o [n_jobs][16][latent_dim], m [n_jobs][16], l [n_jobs][16])
@@ -1217,11 +1219,13 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
   {
     const int r = tid >> 4, j = tid & 15;
     float mmax = -INFINITY;
+#pragma unroll 4
     for (int q = slot_begin + j; q < slot_end; q += 16) mmax = fmaxf(mmax, wm[q * lay.ml_slot + r]);
 #pragma unroll
     for (int off = 1; off < 16; off <<= 1) mmax = fmaxf(mmax, __shfl_xor_sync(0xffffffffu, mmax, off));
     const float msub = (mmax == -INFINITY) ? 0.0f : mmax;
     float l = 0.0f;
+#pragma unroll 4
     for (int q = slot_begin + j; q < slot_end; q += 16)
       l += exp2f((wm[q * lay.ml_slot + r] - msub) * kLog2e) * wl[q * lay.ml_slot + r];
 #pragma unroll
@@ -1236,8 +1240,8 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
       }
     }
   }
-  const int lq = tid & 7, f = (tid >> 3) & 1, r = tid >> 4;
-  const int d = blockIdx.y * kCombDims + 4 * f;
+  const int lq = tid & (kCombLanes - 1), r = tid >> 4;
+  const int d = blockIdx.y * kCombDims;
   float4 acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   for (int w0 = slot_begin; w0 < slot_end; w0 += kCombWindow) {
     const int nw = min(kCombWindow, slot_end - w0);
@@ -1248,21 +1252,21 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
     }
     __syncthreads();
     int q = lq;
-    for (; q + 24 < nw; q += 32) {
+    for (; q + 3 * kCombLanes < nw; q += 4 * kCombLanes) {
       float4 v[4];
 #pragma unroll
       for (int u = 0; u < 4; ++u)
-        v[u] = *reinterpret_cast<const float4*>(wo + (w0 + q + 8 * u) * lay.o_slot + r * latent_dim + d);
+        v[u] = *reinterpret_cast<const float4*>(wo + (w0 + q + kCombLanes * u) * lay.o_slot + r * latent_dim + d);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        const float w = w_s[(q + 8 * u) * kRows + r];
+        const float w = w_s[(q + kCombLanes * u) * kRows + r];
         acc.x += w * v[u].x;
         acc.y += w * v[u].y;
         acc.z += w * v[u].z;
         acc.w += w * v[u].w;
       }
     }
-    for (; q < nw; q += 8) {
+    for (; q < nw; q += kCombLanes) {
       const float4 v = *reinterpret_cast<const float4*>(wo + (w0 + q) * lay.o_slot + r * latent_dim + d);
       const float w = w_s[q * kRows + r];
       acc.x += w * v.x;
@@ -1272,7 +1276,7 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
     }
   }
 #pragma unroll
-  for (int off = 1; off < 8; off <<= 1) {
+  for (int off = 1; off < kCombLanes; off <<= 1) {
     acc.x += __shfl_xor_sync(0xffffffffu, acc.x, off);
     acc.y += __shfl_xor_sync(0xffffffffu, acc.y, off);
     acc.z += __shfl_xor_sync(0xffffffffu, acc.z, off);
