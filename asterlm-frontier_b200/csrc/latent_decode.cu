@@ -1165,7 +1165,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive(bar(kBarPEmpty + b));
       }
-      // accumulator -> scratch in natural order, rotated back if it is still rotated
+      // accumulator -> scratch in natural order, rotated back if it is still rotated.  The
+      // scratch is the query-fragment region: an item with no tiles (a context-parallel
+      // rank that holds none of a block's pages) waits for its query copy to land first,
+      // or the copy could overwrite the zero record after it is stored.
+      if (n_t == 0) mbar_wait(bar(kBarQ), 0, abort_flag);
       store_o();
       named_sync(3, 32 * kValueWarps);
       if (order == 0 && rotated) {

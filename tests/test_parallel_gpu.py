@@ -23,12 +23,14 @@ pytestmark = pytest.mark.gpu
 SCALE = 1.0 / math.sqrt(512 + 64)
 
 
-@pytest.mark.parametrize("world,q_len", [(1, 1), (2, 1), (3, 1), (8, 1), (3, 2), (2, 3)])
-def test_emulated_ranks_match_oracle(cuda, world, q_len):
+@pytest.mark.parametrize("world,q_len,n_chunks",
+                         [(1, 1, 20), (2, 1, 20), (3, 1, 20), (8, 1, 20), (3, 2, 20), (2, 3, 20), (8, 2, 3)])
+def test_emulated_ranks_match_oracle(cuda, world, q_len, n_chunks):
+    """(8, 2, 3): more ranks than cold chunks, so some ranks read nothing and send empty records."""
     from asterq.context_parallel import ContextParallelDecoder
     from asterq.synth import PoolBuilder, c1_inputs
 
-    ctx, hot = 20 * 512 + 300, 700
+    ctx, hot = n_chunks * 512 + 300, 700
     inp = c1_inputs(seed=40 + world, ctx=ctx, q_len=q_len)
     b = PoolBuilder([ctx], [hot], q_len=q_len, n_heads=16, device=cuda)
     b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
