@@ -59,6 +59,20 @@ def test_quantize_rejects_bad_sizes_without_touching_the_gpu():
     assert st == _lib.ASTERQ_ERR_INVALID_ARGUMENT
 
 
+def test_combine_ranks_rejects_bad_arguments_without_touching_the_gpu():
+    lib = _lib.load()
+    f32 = _lib.DTYPE_F32
+    assert lib.asterq_splitkv_combine_ranks(None, 2, 1, None, 256, None, f32, None) == _lib.ASTERQ_ERR_UNSUPPORTED
+    assert lib.asterq_splitkv_combine_ranks(None, 0, 1, None, 512, None, f32, None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert lib.asterq_splitkv_combine_ranks(None, 2, -1, None, 512, None, f32, None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert lib.asterq_splitkv_combine_ranks(None, 2, 1, None, 512, None, f32, None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert b"null pointer" in lib.asterq_last_error()
+    assert lib.asterq_splitkv_combine_ranks(16, 2, 1, 16, 512, 16, 7, None) == _lib.ASTERQ_ERR_UNSUPPORTED
+    assert lib.asterq_splitkv_combine_ranks(8, 2, 1, 16, 512, 16, f32, None) == _lib.ASTERQ_ERR_MISALIGNED
+    # no row blocks is a valid no-op
+    assert lib.asterq_splitkv_combine_ranks(None, 2, 0, None, 512, None, f32, None) == _lib.ASTERQ_OK
+
+
 def _params(**kw) -> _lib.DecodeParams:
     p = _lib.DecodeParams()
     p.n_heads, p.latent_dim, p.rope_dim, p.group_size, p.page_tokens = 16, 512, 64, 64, 512
