@@ -30,6 +30,7 @@ SCHEME_INT8 = 2
 TILE_COLD = 0
 TILE_HOT = 1
 TILE_NEW = 2
+TILE_HOLD = 3  # failure-detection test hook (see include/asterq.h)
 
 # entry points declared in include/asterq.h
 EXPORTED_SYMBOLS = (
@@ -45,6 +46,9 @@ EXPORTED_SYMBOLS = (
     "asterq_splitkv_combine",
     "asterq_splitkv_merge",
     "asterq_splitkv_combine_ranks",
+    "asterq_plan_scratch_bytes",
+    "asterq_plan_batch",
+    "asterq_batch_append",
 )
 
 
@@ -90,6 +94,46 @@ class DecodeParams(ctypes.Structure):
         ("n_workers", ctypes.c_int32),
         ("n_combine_total", ctypes.c_int32),
         ("unit_jobs", ctypes.c_void_p),
+        ("wait_limit_cycles", ctypes.c_int64),
+        ("plan_counts", ctypes.c_void_p),
+    ]
+
+
+class BatchDesc(ctypes.Structure):
+    """Mirror of ``asterq_batch_desc`` (device page tables and lengths of a ragged batch)."""
+
+    _fields_ = [
+        ("n_seqs", ctypes.c_int32),
+        ("n_heads", ctypes.c_int32),
+        ("page_tokens", ctypes.c_int32),
+        ("max_cold_pages", ctypes.c_int32),
+        ("max_hot_pages", ctypes.c_int32),
+        ("n_workers", ctypes.c_int32),
+        ("n_cold_pages", ctypes.c_void_p),
+        ("cold_pages", ctypes.c_void_p),
+        ("cold_page_tokens", ctypes.c_void_p),
+        ("hot_tokens", ctypes.c_void_p),
+        ("hot_pages", ctypes.c_void_p),
+        ("q_len", ctypes.c_void_p),
+        ("q_start", ctypes.c_void_p),
+    ]
+
+
+class PlanBuffers(ctypes.Structure):
+    """Mirror of ``asterq_plan_buffers`` (the tables ``asterq_plan_batch`` writes)."""
+
+    _fields_ = [
+        ("cap_tiles", ctypes.c_int32),
+        ("cap_units", ctypes.c_int32),
+        ("cap_items", ctypes.c_int32),
+        ("tiles", ctypes.c_void_p),
+        ("units", ctypes.c_void_p),
+        ("items", ctypes.c_void_p),
+        ("combine", ctypes.c_void_p),
+        ("unit_jobs", ctypes.c_void_p),
+        ("workers", ctypes.c_void_p),
+        ("counts", ctypes.c_void_p),
+        ("scratch", ctypes.c_void_p),
     ]
 
 
@@ -145,6 +189,12 @@ def load() -> ctypes.CDLL:
     lib.asterq_splitkv_merge.argtypes = [vp, i32, vp, i32, i32, vp, vp]
     lib.asterq_splitkv_combine_ranks.restype = ctypes.c_int
     lib.asterq_splitkv_combine_ranks.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp]
+    lib.asterq_plan_scratch_bytes.restype = i64
+    lib.asterq_plan_scratch_bytes.argtypes = [ctypes.POINTER(BatchDesc), i32, i32, i32]
+    lib.asterq_plan_batch.restype = ctypes.c_int
+    lib.asterq_plan_batch.argtypes = [ctypes.POINTER(BatchDesc), ctypes.POINTER(PlanBuffers), vp]
+    lib.asterq_batch_append.restype = ctypes.c_int
+    lib.asterq_batch_append.argtypes = [ctypes.POINTER(BatchDesc), vp, vp, vp, i64, vp, vp, i64, vp, vp]
     _lib = lib
     return lib
 

@@ -70,10 +70,19 @@ class DeviceDecodePlan:
         self.workers = None if plan.workers is None else torch.from_numpy(plan.workers.copy()).to(self.device)
         self.unit_jobs = None if plan.unit_jobs is None else torch.from_numpy(plan.unit_jobs.copy()).to(self.device)
         self.workspace = torch.empty(max(4, plan.workspace_bytes // 4), dtype=torch.float32, device=self.device)
+        # set nonzero by the kernel when one of its bounded pipeline waits ran out
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
 
     @property
     def n_items(self) -> int:
         return int(self.plan.items.shape[0])
+
+    def raise_if_failed(self) -> None:
+        """Synchronize and raise ``RuntimeError`` if a decode on this plan timed out in a pipeline
+        wait (the kernel stopped instead of hanging; its output is not valid).  Clears the status."""
+        if int(self.status.item()) != 0:
+            self.status.zero_()
+            raise RuntimeError("asterq decode: a pipeline wait timed out on the device (output not valid)")
 
 
 def make_params(
@@ -88,6 +97,7 @@ def make_params(
     n_heads: int,
     softmax_scale: float,
     logit_softcap: float | None = None,
+    wait_limit_cycles: int = 0,
 ) -> _lib.DecodeParams:
     plan = dplan.plan
     p = _lib.DecodeParams()
@@ -129,6 +139,8 @@ def make_params(
         p.n_workers = plan.n_workers
     if dplan.unit_jobs is not None:
         p.unit_jobs = dplan.unit_jobs.data_ptr()
+    p.device_status = dplan.status.data_ptr()
+    p.wait_limit_cycles = int(wait_limit_cycles)
     if pools.cold_scheme not in COLD_SCHEMES:
         raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
     p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]
@@ -185,11 +197,14 @@ def latent_decode(
     logit_softcap: float | None = None,
     out: torch.Tensor | None = None,
     out_dtype: torch.dtype = torch.bfloat16,
+    wait_limit_cycles: int = 0,
 ) -> torch.Tensor:
     """Context latents [total_q, H, 512] for every query row of the batch.
 
     ``softmax_scale`` defaults to 1/sqrt(512 + 64) (latent_attention.py:189 with
-    head_dim = latent_dim under absorption).
+    head_dim = latent_dim under absorption).  Nothing synchronizes the host: a decode whose
+    pipeline wait ran out (after ``wait_limit_cycles`` SM cycles, 0: about 2 s) leaves the
+    plan's status set, which ``dplan.raise_if_failed()`` turns into ``RuntimeError``.
     """
     n_heads = dplan.plan.n_heads
     _check_inputs(q_lat, q_rope, new_latent, new_rope, n_heads)
@@ -202,7 +217,7 @@ def latent_decode(
     elif out.dtype not in (torch.float32, torch.bfloat16) or out.shape != (q_lat.shape[0], n_heads, LATENT_DIM):
         raise ValueError("out must be float32/bfloat16 [total_q, H, 512]")
     p = make_params(pools, dplan, q_lat, q_rope, new_latent, new_rope, out, n_heads=n_heads,
-                    softmax_scale=softmax_scale, logit_softcap=logit_softcap)
+                    softmax_scale=softmax_scale, logit_softcap=logit_softcap, wait_limit_cycles=wait_limit_cycles)
     lib = _lib.load()
     _lib.check(lib.asterq_latent_decode(ctypes.byref(p), _lib.stream_handle(q_lat.device)))
     return out

@@ -240,16 +240,18 @@ ASTERQ_DEVICE int ld_shared_volatile(const volatile int* p) {
   asm volatile("ld.volatile.shared.u32 %0, [%1];" : "=r"(v) : "r"((uint32_t)__cvta_generic_to_shared((const void*)p)) : "memory");
   return v;
 }
-// Bounded wait (about 2 s of SM clock): on timeout raise the CTA abort flag so
-// every other wait returns at once and the kernel drains instead of hanging.
-// `abort_flag` points to shared memory.
-ASTERQ_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+// Bounded wait (`limit` SM clock cycles, by default 4e9: about 2 s): on timeout raise
+// the CTA abort flag so every other wait returns at once and the kernel drains
+// instead of hanging.  `abort_flag` points to shared memory.
+constexpr long long kDefaultWaitLimit = 4000000000LL;
+ASTERQ_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                             long long limit = kDefaultWaitLimit) {
   if (mbar_try(bar, parity)) return true;
   const long long t0 = clock64();
   while (true) {
     if (mbar_try_sleep(bar, parity, 20000u)) return true;
     if (ld_shared_volatile(abort_flag)) return false;
-    if (clock64() - t0 > 4000000000LL) {
+    if (clock64() - t0 > limit) {
       *abort_flag = 1;
       return false;
     }

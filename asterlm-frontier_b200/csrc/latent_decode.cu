@@ -43,6 +43,7 @@
 // setmaxnreg gives the score warpgroups 160 registers and the value warpgroups 96.
 // Every wait is bounded; a timeout sets a status flag instead of hanging.
 #include <atomic>
+#include <mutex>
 #include <cuda.h>
 
 #include "common.cuh"
@@ -89,7 +90,7 @@ constexpr int kOffP = kOffQr + 2048;            // 2 x p tile [16][132] fp32
 constexpr int kOffST = kOffP + 2 * kPBytes;     // 2 x cold code scales [8 groups][128 tokens] fp16
 constexpr int kOffMisc = kOffST + 2 * 2048;     // 1024 floats of per-row scalars
 constexpr int kOffBar = kOffMisc + 4096;        // mbarriers
-constexpr int kSmemBytes = kOffBar + 128 + 1024;  // + alignment slack
+constexpr int kSmemBytes = kOffBar + 192 + 1024;  // + alignment slack
 static_assert(kSmemBytes <= 232448, "dynamic shared memory per block");
 
 // misc (float index)
@@ -128,7 +129,8 @@ constexpr int kBarPEmpty = 11; // [2] p tile consumed
 constexpr int kBarAbort = 13;  // int flag (shares the slot area)
 constexpr int kBarQ = 14;      // prepared query operands landed
 constexpr int kBarM = 15;      // running max after tile i published and the one before it read (phase i)
-static_assert(kBarM * 8 + 8 <= 128, "mbarrier area holds 16 slots");
+constexpr int kSlotIssued = 16;  // int: producer's issued-tile mark (shares the slot area)
+static_assert(kSlotIssued * 8 + 8 <= 192, "mbarrier area holds 24 slots");
 
 constexpr float kLog2e = 1.4426950408889634f;
 // 0x4B400000 read as fp32 is 1.5 * 2^23 = 12582912: an int32 accumulator started at this
@@ -197,6 +199,11 @@ ASTERQ_DEVICE Tile check_tile(const asterq_decode_params& p, int4 t) {
 }
 
 ASTERQ_DEVICE Tile load_tile(const asterq_decode_params& p, int idx) { return check_tile(p, fetch_tile(p, idx)); }
+
+// bound of every pipeline wait (asterq_decode_params.wait_limit_cycles; 0: the default)
+ASTERQ_DEVICE long long wait_limit(const asterq_decode_params& p) {
+  return (p.wait_limit_cycles > 0) ? p.wait_limit_cycles : kDefaultWaitLimit;
+}
 
 // Normalized FWHT of rows [r0, r0 + nrows) of a [16][512] fp32 buffer, one warp:
 // lane l holds elements 16l..16l+15; stages h < 16 are lane-local, h >= 16 pair
@@ -272,6 +279,7 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   const int unit = blockIdx.x;
   // the decode grid may launch now; it waits for this grid's results before reading them
   asm volatile("griddepcontrol.launch_dependents;");
+  if (p.plan_counts != nullptr && unit >= __ldg(p.plan_counts + 1)) return;  // beyond a device-built schedule
   const int64_t out_row0 = p.units[2 * unit];
   const int n_rows = min(max(p.units[2 * unit + 1], 0), kRows);
   uint8_t* dst = reinterpret_cast<uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes + (int64_t)unit * kQPrepBytes;
@@ -398,6 +406,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int* itm = p.items;
   int rb = 0, tile_begin = 0, slot = -2, n_rows = 0, n_t = 0;
   int64_t out_row0 = 0;
+  // producer lane: one past the last tile of the current item it has requested (shared memory)
+  volatile int* issued_hi = reinterpret_cast<volatile int*>(bars + kSlotIssued);
   auto begin_item = [&](int it) {
     itm = p.items + 8 * (int64_t)it;
     rb = itm[1];
@@ -444,6 +454,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int s = j % kStages;
     const uint32_t full = bar(kBarFull + j % kFullBars);
     const uint32_t st = sbase + s * kStageBytes;
+    if (t.kind == ASTERQ_TILE_HOLD) return;  // test hook: never arrives (the waits for it time out)
+    *issued_hi = j + 1;
     if (t.n == 0) {
       mbar_arrive(full);
       return;
@@ -470,6 +482,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // (the query block first: it comes from L2 and gates every tile, the tiles come from HBM;
   // the CTA's first item has its tiles in flight already, see below)
   auto prologue = [&](bool tiles_issued) {
+    if (!tiles_issued) *issued_hi = 0;
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes +
                          (int64_t)max(itm[0], 0) * kQPrepBytes;
     const uint32_t qb = bar(kBarQ);
@@ -485,6 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first item's tiles read only the cache, so they are requested before every thread
   // waits for qprep_kernel's results (the query blocks and the unit counters).
   if (warp == kProducerWarp && lane == 0 && it_begin < it_end) {
+    *issued_hi = 0;
     begin_item(it_begin);
     for (int j = 0; j < min(n_t, kStages); ++j) issue(j);
   }
@@ -536,7 +550,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // applied across splits, as combine_kernel does), so no separate launch is needed.
       const int unit = itm[0];
       const int job = (p.unit_jobs != nullptr && unit >= 0 && unit < p.n_units) ? p.unit_jobs[unit] : -1;
-      if (job >= p.n_combine && job < p.n_combine_total) {
+      const int first_fused = (p.plan_counts != nullptr) ? __ldg(p.plan_counts + 6) : p.n_combine;
+      if (job >= first_fused && job < p.n_combine_total) {
         const int4 jb = *reinterpret_cast<const int4*>(p.combine + 4 * (int64_t)job);
         const int s0 = max(jb.x, 0), s1 = min(jb.y, p.n_slots), rows = min(jb.w, kRows);
         __threadfence();  // this CTA's record is visible device-wide before the count moves
@@ -624,7 +639,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int it = it_begin; it < it_end; ++it) {
       begin_item(it);
       if (it > it_begin) next_item_sync();
-      mbar_wait(bar(kBarQ), 0, abort_flag);
+      mbar_wait(bar(kBarQ), 0, abort_flag, wait_limit(p));
       const uint2* qh = reinterpret_cast<const uint2*>(smem + kOffQh);
       const uint2* qr = reinterpret_cast<const uint2*>(smem + kOffQr);
       float qinv[2][2], qinvi[2][2], rratio[2][2];
@@ -660,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // descriptors: this team's next tile checked (fetched a tile ago), the one after fetched
         if (i + 2 < n_t) t_next = check_tile(p, raw_next);
         if (i + 4 < n_t) raw_next = fetch_tile(p, tile_begin + i + 4);
-        mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);
+        mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag, wait_limit(p));
         const uint8_t* st = smem + s * kStageBytes;
         const uint32_t sst = sbase + s * kStageBytes;
         const bool cold = t.kind == ASTERQ_TILE_COLD;
@@ -862,7 +877,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         named_sync(1 + team, 32 * kTeamWarps);
         // the running max before this tile, published by the other team
-        if (i > 0) mbar_wait(bar(kBarM), (i - 1) & 1, abort_flag);
+        if (i > 0) mbar_wait(bar(kBarM), (i - 1) & 1, abort_flag, wait_limit(p));
         const float* m_in = misc + kMMrun + ((i - 1) & 1) * 16;
         float alpha_r[2][2], msub[2][2], lfac[2][2];
 #pragma unroll
@@ -895,7 +910,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         mbar_arrive(bar(kBarM));
         // ---- p = exp(s - m), handed to the value warps ----
-        if (i >= 2) mbar_wait(bar(kBarPEmpty + b), ((i >> 1) - 1) & 1, abort_flag);
+        if (i >= 2) mbar_wait(bar(kBarPEmpty + b), ((i >> 1) - 1) & 1, abort_flag, wait_limit(p));
         float psum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
         if (cold) {
           // p as fp16 [token][16 rows]; the two 16-byte halves of a token's row swap on every
@@ -949,7 +964,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // final per-warp sums, brought to the final running max, and the running max itself
       // (the team that did not take the last tile reads it from the other team: phase n_t - 1)
       const int last = n_t - 1;
-      if (n_t > 0 && (last & 1) != team) mbar_wait(bar(kBarM), last & 1, abort_flag);
+      if (n_t > 0 && (last & 1) != team) mbar_wait(bar(kBarM), last & 1, abort_flag, wait_limit(p));
       named_sync(1 + team, 32 * kTeamWarps);
       if (gid == 0) {
 #pragma unroll
@@ -1020,7 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Tile t = t_next;
         if (i + 1 < n_t) t_next = check_tile(p, raw_next);
         if (i + 2 < n_t) raw_next = fetch_tile(p, tile_begin + i + 2);
-        mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag);  // TMA data visible to this warp
+        mbar_wait(bar(kBarFull + i % kFullBars), (i / kFullBars) & 1, abort_flag, wait_limit(p));  // TMA data visible to this warp
         const uint8_t* st = smem + s * kStageBytes;
         const uint32_t sst = sbase + s * kStageBytes;
         const float* P = reinterpret_cast<const float*>(smem + kOffP + b * kPBytes);
@@ -1062,12 +1077,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           // refill this stage with tile i + 3 once the tile's team and every value warp have
           // released it; its descriptor was fetched a tile ago, so the issue does not wait
           // on global memory
-          if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag))
+          if (lane == 0 && i + kStages < n_t && mbar_wait(bar(kBarEmpty + s), (i / kStages) & 1, abort_flag, wait_limit(p)))
             issue_tile(i + kStages, check_tile(p, praw));
           if (lane == 0 && i + kStages + 1 < n_t) praw = fetch_tile(p, tile_begin + i + kStages + 1);
           __syncwarp();
         }
-        mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag);
+        mbar_wait(bar(kBarPFull + b), (i >> 1) & 1, abort_flag, wait_limit(p));
 
         if (!cold && order == 0) {
           // first hot tile after cold ones: rotate the accumulator back (O = H O_rot)
@@ -1169,7 +1184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // scratch is the query-fragment region: an item with no tiles (a context-parallel
       // rank that holds none of a block's pages) waits for its query copy to land first,
       // or the copy could overwrite the zero record after it is stored.
-      if (n_t == 0) mbar_wait(bar(kBarQ), 0, abort_flag);
+      if (n_t == 0) mbar_wait(bar(kBarQ), 0, abort_flag, wait_limit(p));
       store_o();
       named_sync(3, 32 * kValueWarps);
       if (order == 0 && rotated) {
@@ -1178,6 +1193,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       named_sync(0, kThreads);
       if (epilogue()) break;
+    }
+    // After a timed-out wait: the copies this CTA requested and nobody waited for land before
+    // the CTA exits (bounded), so no copy writes into the shared memory of a later CTA.
+    if (warp == kProducerWarp && lane == 0 && *abort_flag) {
+      const int hi = *issued_hi;
+      for (int j = max(0, hi - kStages); j < hi; ++j)
+        for (int k = 0; k < (1 << 20) && !mbar_try(bar(kBarFull + j % kFullBars), (j / kFullBars) & 1); ++k) {
+        }
     }
   }
 }
@@ -1304,7 +1327,9 @@ __device__ __forceinline__ void combine_job(const float* __restrict__ wo, const 
 __global__ void __launch_bounds__(kCombThreads) combine_kernel(const float* __restrict__ wo, const float* __restrict__ wm,
                                                       const float* __restrict__ wl, const int32_t* __restrict__ jobs,
                                                       int n_slots, int latent_dim, void* __restrict__ out,
-                                                      int out_dtype, const SlotLayout lay) {
+                                                      int out_dtype, const SlotLayout lay,
+                                                      const int32_t* __restrict__ n_live) {
+  if (n_live != nullptr && (int)blockIdx.x >= __ldg(n_live)) return;  // beyond a device-built schedule's jobs
   combine_job<false>(wo, wm, wl, jobs, n_slots, 0, latent_dim, out, out_dtype, lay);
 }
 
@@ -1505,7 +1530,8 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     const float* wl = wm + (int64_t)p->n_slots * dec::kRows;
     dec::combine_kernel<<<dim3(p->n_combine, dec::kL / dec::kCombDims), dec::kCombThreads, 0, s>>>(
         wo, wm, wl, p->combine, p->n_slots, dec::kL, p->out, p->out_dtype,
-        dec::SlotLayout{(int64_t)dec::kRows * dec::kL, dec::kRows, 0, 0});
+        dec::SlotLayout{(int64_t)dec::kRows * dec::kL, dec::kRows, 0, 0},
+        p->plan_counts != nullptr ? p->plan_counts + 6 : nullptr);
     st = check_launch("splitkv_combine");
   }
   return st;
@@ -1528,7 +1554,7 @@ extern "C" int asterq_splitkv_combine(const float* partials, int32_t n_slots, co
   const float* wl = wm + (int64_t)n_slots * dec::kRows;
   dec::combine_kernel<<<dim3(n_combine, dec::kL / dec::kCombDims), dec::kCombThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       partials, wm, wl, combine, n_slots, latent_dim, out, out_dtype,
-      dec::SlotLayout{(int64_t)dec::kRows * latent_dim, dec::kRows, 0, 0});
+      dec::SlotLayout{(int64_t)dec::kRows * latent_dim, dec::kRows, 0, 0}, nullptr);
   return check_launch("splitkv_combine");
 }
 
@@ -1569,7 +1595,7 @@ extern "C" int asterq_splitkv_combine_ranks(const float* gathered, int32_t world
   dec::combine_kernel<<<dim3(n_blocks, dec::kL / dec::kCombDims), dec::kCombThreads, 0,
                         reinterpret_cast<cudaStream_t>(stream)>>>(
       gathered, wm, wl, jobs, world, latent_dim, out, out_dtype,
-      dec::SlotLayout{part, part, (int64_t)dec::kRows * latent_dim, dec::kRows});
+      dec::SlotLayout{part, part, (int64_t)dec::kRows * latent_dim, dec::kRows}, nullptr);
   return check_launch("splitkv_combine_ranks");
 }
 
@@ -1597,6 +1623,22 @@ constexpr int kNoAllocMaxUnits = 256;
 static __device__ __align__(256) float
     g_noalloc_workspace[(kNoAllocMaxSlots * kRecordBytes + kNoAllocMaxUnits * kQPrepBytes + 4 * kNoAllocMaxUnits) / 4];
 
+// the calling thread's current CUDA context (driver API, looked up through the runtime), or null
+void* current_context() {
+  using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+  static CtxGetCurrentFn fn = []() -> CtxGetCurrentFn {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      return reinterpret_cast<CtxGetCurrentFn>(f);
+    return nullptr;
+  }();
+  CUcontext c = nullptr;
+  if (fn && fn(&c) == CUDA_SUCCESS) return reinterpret_cast<void*>(c);
+  return nullptr;
+}
+
 }  // namespace dec
 }  // namespace asterq
 
@@ -1613,18 +1655,29 @@ extern "C" int asterq_latent_decode_noalloc(const asterq_decode_params* p, void*
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "decode (no-alloc): %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= 64) return set_error(ASTERQ_ERR_UNSUPPORTED, "decode (no-alloc): device ordinal %d >= 64", dev);
-  // Host code cannot use g_noalloc_workspace's name as a device address: resolve
-  // it once per device, with that device current (the first call on a device
-  // does this; make that first call before any stream capture).
-  // Two host threads racing through the first call store the same address.
-  static std::atomic<void*> addr[64];
-  void* ptr = addr[dev].load(std::memory_order_acquire);
-  if (!ptr) {
-    e = cudaGetSymbolAddress(&ptr, dec::g_noalloc_workspace);
-    if (e != cudaSuccess || !ptr)
-      return set_error(ASTERQ_ERR_CUDA, "decode (no-alloc): cannot resolve the workspace address: %s",
-                       cudaGetErrorString(e));
-    addr[dev].store(ptr, std::memory_order_release);
+  // Host code cannot use g_noalloc_workspace's name as a device address: resolve it
+  // with the device current, once per device and CUDA context (the first call on a
+  // device does this, and the first call after the device's context changes, e.g.
+  // after cudaDeviceReset reloaded the module; make those calls before any stream
+  // capture).  The resolved address is remembered together with the context it
+  // belongs to, under a lock.
+  static std::mutex lock;
+  static void* ctx_of[64] = {};
+  static void* addr[64] = {};
+  void* ctx = dec::current_context();
+  void* ptr = nullptr;
+  {
+    std::lock_guard<std::mutex> guard(lock);
+    if (!addr[dev] || ctx_of[dev] != ctx) {
+      void* resolved = nullptr;
+      e = cudaGetSymbolAddress(&resolved, dec::g_noalloc_workspace);
+      if (e != cudaSuccess || !resolved)
+        return set_error(ASTERQ_ERR_CUDA, "decode (no-alloc): cannot resolve the workspace address: %s",
+                         cudaGetErrorString(e));
+      addr[dev] = resolved;
+      ctx_of[dev] = ctx;
+    }
+    ptr = addr[dev];
   }
   asterq_decode_params q = *p;
   q.workspace = ptr;

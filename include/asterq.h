@@ -54,6 +54,9 @@ extern "C" {
 #define ASTERQ_TILE_COLD 0 /* tokens of a cold page: INT4 codes + fp16 scales + bf16 RoPE key */
 #define ASTERQ_TILE_HOT 1  /* tokens of a hot page: bf16 latent + bf16 RoPE key */
 #define ASTERQ_TILE_NEW 2  /* the step's own new tokens (causal among themselves) */
+#define ASTERQ_TILE_HOLD 3 /* failure-detection test hook: nothing is loaded for this tile and its
+                              arrival is never signalled, so the waits for it run into the bounded-wait
+                              limit; the call then ends with *device_status = 1 and no output */
 
 int asterq_version(void);
 const char* asterq_last_error(void);
@@ -166,7 +169,86 @@ typedef struct asterq_decode_params {
   const int32_t* unit_jobs; /* optional [n_units] int32: the combine job (index in [n_combine,
                                n_combine_total)) that the decode kernel runs itself, in the CTA that
                                writes the unit's last partial record, or -1.  NULL: none. */
+  int64_t wait_limit_cycles; /* bound of every pipeline wait inside the kernel, in SM clock cycles;
+                                0: the default (4e9, about 2 s).  A wait that runs out sets
+                                *device_status (when given) and the kernel stops without hanging. */
+  const int32_t* plan_counts; /* optional, device: the counts a device-built schedule wrote
+                                 (asterq_plan_batch); the table sizes above are then its capacities:
+                                 query blocks beyond counts[1] are not prepared, jobs [0, counts[6])
+                                 run in the combine launch (n_combine is its grid), the others in
+                                 the decode kernel.  NULL: the sizes above are exact. */
 } asterq_decode_params;
+
+/*
+ * Device-side schedule for a ragged, paged batch (continuous batching): the same tables the
+ * host planner builds (tiles, units, items, workers, combine jobs), built on the GPU from page
+ * tables and lengths that live on the GPU, so a decode loop that appends tokens to every
+ * sequence each step replans without a host round trip (and can be recorded in a CUDA graph).
+ * Replaces the host-side walk of the cache (cache.py:139-159 iter_chunks) by one small kernel.
+ *
+ * Sequence s: cold pages cold_pages[s][0 .. n_cold_pages[s]) oldest first, page j holding
+ * cold_page_tokens[s][j] tokens from offset 0; a hot window of hot_tokens[s] tokens in pages
+ * hot_pages[s][0 ..] (every page full except the last); q_len[s] new tokens at rows
+ * q_start[s] .. of the step's arrays (q_len[s] <= 0: an empty slot, planned as nothing).
+ * Tiles of a sequence: cold (<= 128 tokens, never across a page), hot (<= 32), new (<= 32);
+ * every 16-row query block is a unit; the units' tile ranges are cut into one contiguous share
+ * per worker of equal estimated time.
+ */
+typedef struct asterq_batch_desc {
+  int32_t n_seqs;
+  int32_t n_heads;
+  int32_t page_tokens;      /* a multiple of 16 */
+  int32_t max_cold_pages;   /* row stride of cold_pages and cold_page_tokens */
+  int32_t max_hot_pages;    /* row stride of hot_pages */
+  int32_t n_workers;        /* worker CTAs (the decode grid), typically the SM count */
+  const int32_t* n_cold_pages;      /* [n_seqs] */
+  const int32_t* cold_pages;        /* [n_seqs][max_cold_pages] */
+  const int32_t* cold_page_tokens;  /* [n_seqs][max_cold_pages] */
+  const int32_t* hot_tokens;        /* [n_seqs] */
+  const int32_t* hot_pages;         /* [n_seqs][max_hot_pages] */
+  const int32_t* q_len;             /* [n_seqs], <= 2048 */
+  const int32_t* q_start;           /* [n_seqs] */
+} asterq_batch_desc;
+
+/* Device tables asterq_plan_batch writes, sized by capacities chosen by the caller. */
+typedef struct asterq_plan_buffers {
+  int32_t cap_tiles;
+  int32_t cap_units;
+  int32_t cap_items;   /* also the partial-record slots; cap_units + n_workers always suffices */
+  int32_t* tiles;      /* [cap_tiles][4] */
+  int32_t* units;      /* [cap_units][2] */
+  int32_t* items;      /* [cap_items][8] */
+  int32_t* combine;    /* [cap_units][4]: jobs [0, counts[6]) for the combine launch, then the fused ones */
+  int32_t* unit_jobs;  /* [cap_units] */
+  int32_t* workers;    /* [n_workers + 1] */
+  int32_t* counts;     /* [8]: n_tiles, n_units, n_items, n_slots, n_jobs, status (1: a capacity was
+                          exceeded, nothing is planned), n_separate (jobs for the combine launch), 0 */
+  void* scratch;       /* asterq_plan_scratch_bytes(...) bytes */
+} asterq_plan_buffers;
+
+/* Scratch bytes asterq_plan_batch needs for this descriptor's n_seqs, max_cold_pages and
+ * n_workers and these capacities (0 on bad arguments). */
+int64_t asterq_plan_scratch_bytes(const asterq_batch_desc* d, int32_t cap_tiles, int32_t cap_units,
+                                  int32_t cap_items);
+
+/* Enqueue the planner (one CTA).  Decode with the tables it wrote: asterq_latent_decode with
+ * tiles/units/items/combine/unit_jobs/workers, n_tiles/n_units/n_items = the capacities,
+ * n_slots = cap_items, n_combine = (n_workers + 15) / 16 (a unit goes to the combine launch
+ * only when cut into more than 16 pieces, and every cut is a distinct worker boundary),
+ * n_combine_total = cap_units, n_workers, plan_counts = counts. */
+int asterq_plan_batch(const asterq_batch_desc* d, const asterq_plan_buffers* b, void* stream);
+
+/* Append a step's new tokens to the hot windows in place (cache.py:195-200 without the
+ * re-concatenation): for every s with q_len[s] > 0, rows q_start[s] .. q_start[s] + q_len[s] - 1
+ * of new_latent (bf16 [total_q, 512]) and new_rope (bf16 [total_q, 64]) go to hot positions
+ * hot_tokens[s] .. of the sequence's hot pages, then hot_tokens[s] += q_len[s].  `hot_tokens` is
+ * the writable array (d->hot_tokens is not read).  A sequence whose positions reach a page that
+ * is not in hot_pages (beyond max_hot_pages, or an id outside [0, n_hot_pool_pages)), or whose
+ * rows pass total_q, is left unchanged and sets *status = 1 (status may be NULL).  One CTA per
+ * sequence. */
+int asterq_batch_append(const asterq_batch_desc* d, int32_t* hot_tokens, const void* new_latent,
+                        const void* new_rope, int64_t total_q, void* hot_latent, void* hot_rope,
+                        int64_t n_hot_pool_pages, int32_t* status, void* stream);
 
 /* Bytes of workspace asterq_latent_decode needs: n_slots partial records of 32,896 B
  * (16 x 514 fp32), n_units prepared query blocks of 35,328 B, then one int32 counter per

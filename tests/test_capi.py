@@ -41,9 +41,15 @@ def test_version_and_error_string():
 
 def test_struct_layout_matches_header():
     # sizes of the C struct: 6 int32 + 2 float + 3 int64 + 4 int32 + 14 pointers + int64 + 2 pointers + 2 int32
-    # + the workers pointer + 2 int32 + the unit_jobs pointer
-    assert ctypes.sizeof(_lib.DecodeParams) == 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8 + 8 + 8 + 2 * 4 + 8 + 2 * 4 + 8
-    assert _lib.DecodeParams.workers.offset == ctypes.sizeof(_lib.DecodeParams) - 24
+    # + the workers pointer + 2 int32 + the unit_jobs pointer + the int64 wait limit + the plan_counts pointer
+    size = 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8 + 8 + 8 + 2 * 4 + 8 + 2 * 4 + 8 + 8 + 8
+    assert ctypes.sizeof(_lib.DecodeParams) == size
+    assert _lib.DecodeParams.workers.offset == size - 40
+    assert _lib.DecodeParams.wait_limit_cycles.offset == size - 16
+    assert _lib.DecodeParams.plan_counts.offset == size - 8
+    # asterq_batch_desc: 6 int32 + 7 pointers; asterq_plan_buffers: 3 int32 (+ padding) + 8 pointers
+    assert ctypes.sizeof(_lib.BatchDesc) == 6 * 4 + 7 * 8
+    assert ctypes.sizeof(_lib.PlanBuffers) == 16 + 8 * 8 and _lib.PlanBuffers.tiles.offset == 16
 
 
 def test_quantize_rejects_bad_sizes_without_touching_the_gpu():
@@ -139,3 +145,42 @@ def test_check_maps_status_to_exception_types():
         _lib.check(_lib.ASTERQ_ERR_INVALID_ARGUMENT)
     with pytest.raises(_lib.AsterqError):
         _lib.check(_lib.ASTERQ_ERR_UNSUPPORTED)
+
+
+def test_plan_and_append_reject_bad_arguments_without_touching_the_gpu():
+    lib = _lib.load()
+    d = _lib.BatchDesc()
+    d.n_seqs, d.n_heads, d.page_tokens, d.n_workers = 2, 16, 512, 148
+    b = _lib.PlanBuffers()
+    assert lib.asterq_plan_batch(None, ctypes.byref(b), None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert lib.asterq_plan_batch(ctypes.byref(d), ctypes.byref(b), None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert b"null sequence table" in lib.asterq_last_error()
+    for name in ("n_cold_pages", "cold_pages", "cold_page_tokens", "hot_tokens", "hot_pages", "q_len", "q_start"):
+        setattr(d, name, 16)
+    d.max_cold_pages, d.max_hot_pages = 4, 4
+    assert lib.asterq_plan_batch(ctypes.byref(d), ctypes.byref(b), None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert b"null plan buffer" in lib.asterq_last_error()
+    for name in ("tiles", "units", "items", "combine", "unit_jobs", "workers", "counts", "scratch"):
+        setattr(b, name, 32)
+    b.items = 40
+    assert lib.asterq_plan_batch(ctypes.byref(d), ctypes.byref(b), None) == _lib.ASTERQ_ERR_MISALIGNED
+    d.page_tokens = 100
+    assert lib.asterq_plan_batch(ctypes.byref(d), ctypes.byref(b), None) == _lib.ASTERQ_ERR_UNSUPPORTED
+    assert lib.asterq_plan_scratch_bytes(ctypes.byref(d), -1, 4, 4) == 0
+    d.page_tokens = 512
+    d.n_workers = 0
+    assert lib.asterq_plan_batch(ctypes.byref(d), ctypes.byref(b), None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert lib.asterq_plan_scratch_bytes(ctypes.byref(d), 4, 4, 4) == 0
+    d.n_workers = 148
+    # scratch: tile costs, segment and per-unit prefix arrays (int64), per-boundary and per-item int32
+    n_segs = 2 * (4 + 2)
+    want = 8 * (10 + 1 + n_segs + 1 + 2 + 1 + 6 * (3 + 1) + 148 + 1) + 4 * (3 * 148 + 5)
+    assert lib.asterq_plan_scratch_bytes(ctypes.byref(d), 10, 3, 5) == want
+    # append: null and misaligned arrays
+    assert lib.asterq_batch_append(ctypes.byref(d), None, 16, 16, 2, 16, 16, 8, None, None) == \
+        _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert lib.asterq_batch_append(ctypes.byref(d), 16, 16, 16, -1, 16, 16, 8, None, None) == \
+        _lib.ASTERQ_ERR_INVALID_ARGUMENT
+    assert lib.asterq_batch_append(ctypes.byref(d), 16, 16, 24, 2, 16, 16, 8, None, None) == _lib.ASTERQ_ERR_MISALIGNED
+    d.n_seqs = 0  # nothing to append is a valid no-op
+    assert lib.asterq_batch_append(ctypes.byref(d), None, None, None, 0, None, None, 0, None, None) == _lib.ASTERQ_OK

@@ -224,3 +224,31 @@ def test_rejects_bad_inputs(cuda):
         latent_decode(wl.pools, dplan, wl.q_lat.float(), wl.q_rope, wl.new_latent, wl.new_rope)
     with pytest.raises(ValueError):
         latent_decode(wl.pools, dplan, wl.q_lat[:, :8], wl.q_rope, wl.new_latent, wl.new_rope)
+
+
+def test_timed_out_wait_is_reported_and_the_context_survives(cuda):
+    """Failure detection without a fault: a tile whose arrival is never signalled (the
+    ASTERQ_TILE_HOLD test hook) makes the pipeline waits run out after a short host-set limit;
+    the kernel stops, the status word is set and the host raises.  A normal decode on the same
+    context afterwards still matches the oracle."""
+    from asterq import _lib
+    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.plan import build_plan
+    from asterq.synth import c1_inputs
+
+    inp = c1_inputs(seed=31, ctx=3000)
+    wl = single_sequence_workload(inp, 3000, 700, 1, cuda)
+    dplan = DeviceDecodePlan(build_plan(wl.layouts, 16, n_sms=8), cuda)
+    kept = int(dplan.tiles[3, 0].item())
+    dplan.tiles[3, 0] = _lib.TILE_HOLD
+    latent_decode(wl.pools, dplan, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE,
+                  out_dtype=torch.float32, wait_limit_cycles=2_000_000)
+    torch.cuda.synchronize()
+    assert int(dplan.status.item()) == 1
+    with pytest.raises(RuntimeError, match="timed out"):
+        dplan.raise_if_failed()
+    dplan.tiles[3, 0] = kept
+    out = latent_decode(wl.pools, dplan, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE,
+                        out_dtype=torch.float32)
+    dplan.raise_if_failed()
+    assert_close(out.cpu().numpy(), oracle_for(inp, 3000, 700, 1), "after a timed-out call")

@@ -49,7 +49,8 @@ def _params(wl, plan_kw, out_dtype):
 
 
 def _decode_both(wl, plan_kw, out_dtype=torch.float32):
-    """(ordinary entry point's output, no-alloc entry point's output, n_slots)."""
+    """(ordinary entry point's output, no-alloc entry point's output, n_slots, combine jobs the decode
+    kernel runs itself with the counters that live in the built-in array)."""
     from asterq import _lib
 
     lib = _lib.load()
@@ -62,7 +63,8 @@ def _decode_both(wl, plan_kw, out_dtype=torch.float32):
     p.workspace_bytes = 0
     _lib.check(lib.asterq_latent_decode_noalloc(ctypes.byref(p), stream))
     torch.cuda.synchronize()
-    return out_ref.float().cpu().numpy(), out_na.float().cpu().numpy(), int(p.n_slots)
+    return (out_ref.float().cpu().numpy(), out_na.float().cpu().numpy(), int(p.n_slots),
+            int(p.n_combine_total) - int(p.n_combine))
 
 
 def _assert_same(got, want, what):
@@ -77,11 +79,16 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cuda):
     split = dict(n_sms=32, ctas_per_sm=2, waves=4)
     calls = [(wl_a, split, torch.float32), (wl_a, split, torch.float32), (wl_b, split, torch.bfloat16),
              (wl_a, dict(max_items_per_seq=1), torch.float32)]
+    fused_calls = 0
     for i, (wl, kw, dt) in enumerate(calls):
-        ref, got, n_slots = _decode_both(wl, kw, dt)
+        ref, got, n_slots, n_fused = _decode_both(wl, kw, dt)
         if kw is split:
             assert 0 < n_slots <= MAX_SLOTS, n_slots
+        fused_calls += n_fused > 0
         _assert_same(got, ref, f"call {i} ({wl.lengths}, {dt})")
+    # the in-kernel merge (whose per-block counters sit in the built-in array, zeroed every call)
+    # ran on consecutive calls
+    assert fused_calls >= 2
 
 
 def test_noalloc_rejects_schedules_beyond_its_array(cuda):
@@ -91,5 +98,9 @@ def test_noalloc_rejects_schedules_beyond_its_array(cuda):
     wl = _workload(13, [700], cuda)
     p, _, _ = _params(wl, dict(max_items_per_seq=1), torch.float32)
     p.n_slots = MAX_SLOTS + 1
+    assert lib.asterq_latent_decode_noalloc(ctypes.byref(p), _lib.stream_handle(cuda)) == _lib.ASTERQ_ERR_WORKSPACE
+    assert b"no-alloc" in lib.asterq_last_error()
+    p.n_slots = 0
+    p.n_units = MAX_SLOTS + 1  # the array also holds one prepared query block and one counter per 16-row block
     assert lib.asterq_latent_decode_noalloc(ctypes.byref(p), _lib.stream_handle(cuda)) == _lib.ASTERQ_ERR_WORKSPACE
     assert b"no-alloc" in lib.asterq_last_error()
