@@ -186,9 +186,21 @@ def make_workload(
     device = torch.device(device)
     keep_host = keep_host or set()
     b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=n_heads, page_tokens=page_tokens, device=device)
+    host: dict[int, dict[str, torch.Tensor]] = {}
+    for i, lat, rope, ql, qr in generate_sequences(lengths, q_len=q_len, n_heads=n_heads, seed=seed, device=device):
+        b.add(lat, rope, ql, qr)
+        if i in keep_host:
+            host[i] = {"latent": lat.cpu(), "rope": rope.cpu(), "q_lat": ql.cpu(), "q_rope": qr.cpu()}
+    return b.finish(name, host)
+
+
+def generate_sequences(lengths, *, q_len: int = 1, n_heads: int = 16, seed: int = 0, device="cuda"):
+    """The seeded tensors of a batch, sequence by sequence, in the order every workload draws them:
+    yields (index, latent [n + q_len, 512], rope [n + q_len, 64], q_lat [q_len, H, 512],
+    q_rope [q_len, H, 64]), bfloat16 on `device`; the last q_len tokens are the step's new tokens."""
+    device = torch.device(device)
     out_ch = outlier_channels(seed).to(device)
     gen = torch.Generator(device=device).manual_seed(seed)
-    host: dict[int, dict[str, torch.Tensor]] = {}
     for i, n in enumerate(lengths):
         lat = torch.randn(n + q_len, LATENT_DIM, generator=gen, device=device)
         lat[:, out_ch] *= OUTLIER_SCALE
@@ -196,9 +208,54 @@ def make_workload(
         rope = torch.randn(n + q_len, ROPE_DIM, generator=gen, device=device).to(torch.bfloat16)
         ql = torch.randn(q_len, n_heads, LATENT_DIM, generator=gen, device=device).to(torch.bfloat16)
         qr = torch.randn(q_len, n_heads, ROPE_DIM, generator=gen, device=device).to(torch.bfloat16)
-        b.add(lat, rope, ql, qr)
+        yield i, lat, rope, ql, qr
+
+
+def host_sequences(lengths, indices, *, q_len: int = 1, n_heads: int = 16, seed: int = 0, device="cuda"):
+    """CPU copies of the sequences `indices` of a seeded batch, without building any pool
+    (no asterq kernel runs): the inputs of a CPU baseline on exactly the tensors the GPU times."""
+    want = set(indices)
+    out = {}
+    for i, lat, rope, ql, qr in generate_sequences(lengths, q_len=q_len, n_heads=n_heads, seed=seed, device=device):
+        if i in want:
+            out[i] = {"latent": lat.cpu(), "rope": rope.cpu(), "q_lat": ql.cpu(), "q_rope": qr.cpu()}
+        if len(out) == len(want):
+            break
+    return out
+
+
+def make_shard_workload(
+    name: str,
+    lengths: list[int],
+    hot: list[int],
+    shard: list[int],
+    *,
+    q_len: int = 1,
+    n_heads: int = 16,
+    seed: int = 0,
+    device="cuda",
+    page_tokens: int = 512,
+    keep_host: set[int] | None = None,
+) -> Workload:
+    """The sequences `shard` (indices into `lengths`) of a seeded batch, with pools for them
+    only: every rank of a sequence-sharded job draws the whole batch from the same seed and
+    keeps its own sequences, so the shards together are exactly the one-GPU batch.
+    ``keep_host`` indices are batch indices; ``Workload.host`` is keyed by position in the shard."""
+    device = torch.device(device)
+    pos = {gi: k for k, gi in enumerate(shard)}
+    b = PoolBuilder([lengths[i] for i in shard], [hot[i] for i in shard], q_len=q_len, n_heads=n_heads,
+                    page_tokens=page_tokens, device=device)
+    keep_host = keep_host or set()
+    host: dict[int, dict[str, torch.Tensor]] = {}
+    pending: dict[int, tuple] = {}
+    for i, lat, rope, ql, qr in generate_sequences(lengths, q_len=q_len, n_heads=n_heads, seed=seed, device=device):
+        if i not in pos:
+            continue
+        pending[pos[i]] = (lat, rope, ql, qr)
         if i in keep_host:
-            host[i] = {"latent": lat.cpu(), "rope": rope.cpu(), "q_lat": ql.cpu(), "q_rope": qr.cpu()}
+            host[pos[i]] = {"latent": lat.cpu(), "rope": rope.cpu(), "q_lat": ql.cpu(), "q_rope": qr.cpu()}
+        while len(b.layouts) in pending:  # add in shard order
+            b.add(*pending.pop(len(b.layouts)))
     return b.finish(name, host)
 
 

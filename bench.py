@@ -1,19 +1,23 @@
 """Decode-attention benchmark (one JSON line on rank 0).
 
-Workload (per GPU): BASELINE config 3, ragged continuous-batching decode --
+Workload: BASELINE config 3, ragged continuous-batching decode -- one batch of
 64 sequences with seeded context lengths U[1024, 32768], the newest
 min(len, 2048) tokens hot BF16, the rest INT4 chunks of 512, 16 heads, latent
-512 + RoPE 64, q_len 1.  Sequences are sharded across GPUs: every rank owns its
-own 64-sequence batch (weak scaling, no collective in the timed step).
+512 + RoPE 64, q_len 1.  With N GPUs the batch is split longest-first by step
+bytes (asterq.sharding): every rank decodes its own sequences, no collective
+(strong scaling: the whole job is always the same 64 sequences).
 
-  value  device-timed whole-job seq-steps/s (CUDA events, max over ranks),
-         inputs resident in HBM (0.53 GB per GPU, larger than the 126 MB L2)
+  value  device-timed whole-job seq-steps/s: 64 sequences / the max over ranks
+         of the per-step decode time (CUDA events around each step's launches;
+         a 256 MB write flushes L2 between steps, outside the events)
   e2e    the same metric through the public API (asterq.decode.latent_decode)
          with the step's query/new-token inputs copied from pinned host memory
          and the context latents copied back, every step
-  roofline  achieved HBM GB/s of the decode kernel = algorithmic bytes per
+  roofline  achieved HBM GB/s of rank 0's decode kernel = algorithmic bytes per
          launch / its CUDA-event duration, against MEASURED_PEAKS.json
-  cpu_baseline  the CPU oracle port on the host cores (bounded sample)
+  cpu_baseline  the reference's own decode (LatentAttention._absorbed_decode of
+         the unmodified AsterLM package installed under baseline/_ref) on the
+         host cores, over 8 of the same 64 sequences, plus a one-thread figure
 
   python bench.py [--gpus N --steps K --warmup W] [--impl reference]
 """
@@ -41,7 +45,7 @@ METRIC = json.loads((ROOT / "BASELINE.json").read_text())["metric"] if (ROOT / "
     "decode-attn seq-steps/s per GPU and % of HBM peak, 1/2/4/8 B200 vs host CPU"
 UNIT = "seq-steps/s"
 SOFTMAX_SCALE = 1.0 / math.sqrt(512 + 64)
-WORKLOAD = ("C3 ragged continuous-batching decode: 64 seqs/GPU, ctx U[1024,32768] (seed 0), hot min(len,2048) "
+WORKLOAD = ("C3 ragged continuous-batching decode: one batch of 64 seqs, ctx U[1024,32768] (seed 0), hot min(len,2048) "
             "BF16 + INT4 chunks of 512, 16 heads, latent 512 + RoPE 64, q_len 1")
 
 
@@ -71,8 +75,9 @@ def profiled_traffic() -> float | None:
 class ClockSampler:
     """SM clocks and throttle reasons sampled during the timed region.
 
-    NVML is polled from a thread every ~2 ms (read-only queries), so even a
-    timed region of a few tens of milliseconds yields samples.  Falls back to
+    NVML is polled from a thread every ~0.5 ms (read-only queries) from the
+    warm-up through the end-to-end loop, so even a timed region of a few
+    milliseconds yields samples.  Falls back to
     ``nvidia-smi -lms 100`` when NVML cannot be opened.
     """
 
@@ -124,7 +129,7 @@ class ClockSampler:
                 self.samples.append((sm, mx, bits))
             except Exception:
                 break
-            time.sleep(0.002)
+            time.sleep(0.0005)
 
     def __enter__(self):
         try:
@@ -198,101 +203,195 @@ class ClockSampler:
         }
 
 
-def build_workload(device, rank: int, n_seqs: int = 64, keep_host=None):
-    from asterq.synth import c3_lengths, make_workload
-
-    lens = c3_lengths(0, n_seqs)
-    return make_workload("C3", lens, [min(n, 2048) for n in lens], q_len=1, seed=1000 + rank, device=device,
-                         keep_host=keep_host)
-
-
-def oracle_caches(host_seqs: dict, lengths, hot) -> list:
-    """The sampled sequences' caches in the oracle's form (built once, outside any timing)."""
-    from oracle import hq4_oracle as O
-
-    caches = []
-    for i, h in sorted(host_seqs.items()):
-        lat = h["latent"].float().numpy()
-        rope = h["rope"].float().numpy()
-        n = lengths[i]
-        caches.append((O.build_cache_split(lat[:n], rope[:n], hot[i], 512), h, lat[n:], rope[n:]))
-    return caches
+C3_SEQS = 64
+C3_DATA_SEED = 1000
+REF_SAMPLE = list(range(0, C3_SEQS, 8))  # the sequences the CPU baselines decode (every 8th)
+REF_DIR = ROOT / "baseline" / "_ref"
+L2_FLUSH_BYTES = 256 << 20
 
 
-def cpu_oracle_rate(caches: list, budget_s: float = 12.0):
-    """Oracle decode (numpy port of the reference path) on host cores over prebuilt caches; seq-steps/s."""
-    from oracle import hq4_oracle as O
+def c3_batch() -> tuple[list[int], list[int]]:
+    from asterq.synth import c3_lengths
 
-    done, t0 = 0, time.perf_counter()
-    tokens = 0
-    while True:
-        for cache, h, nl, nr in caches:
-            O.absorbed_decode(h["q_lat"].float().numpy(), h["q_rope"].float().numpy(), nl, nr, cache, SOFTMAX_SCALE)
-            done += 1
-            tokens += cache.length
-            if time.perf_counter() - t0 > budget_s:
-                break
-        if time.perf_counter() - t0 > budget_s:
-            break
-    dt = time.perf_counter() - t0
-    return done / dt, done, tokens, dt
+    lens = c3_lengths(0, C3_SEQS)
+    return lens, [min(n, 2048) for n in lens]
+
+
+def run_config(world: int) -> dict:
+    """The workload description both arms print (the same for --impl asterq and reference)."""
+    lens, hot = c3_batch()
+    return {
+        "workload": WORKLOAD,
+        "seqs": C3_SEQS,
+        "cached_tokens": int(sum(lens)),
+        "q_len": 1,
+        "n_heads": 16,
+        "data_seed": C3_DATA_SEED,
+        "parallelism": f"sequence sharding over {world} GPU(s): the one batch split longest-first by step bytes, "
+                       "no collective",
+        "l2": f"flushed between steps ({L2_FLUSH_BYTES >> 20} MB write, outside the per-step events)",
+    }
+
+
+# ---------------------------------------------------------------------------
+# the reference's own CPU path (baseline/_ref: the unmodified AsterLM package)
+# ---------------------------------------------------------------------------
+def load_reference():
+    """(modules, None) or (None, reason): LatentAttention, LatentLayerCache and quantize_tensor
+    imported from the reference package installed under baseline/_ref."""
+    if not (REF_DIR / "asterlm").is_dir():
+        return None, "the reference is not installed under baseline/_ref"
+    if str(REF_DIR) not in sys.path:
+        sys.path.insert(0, str(REF_DIR))
+    try:
+        from asterlm.cache import LatentLayerCache
+        from asterlm.layers.latent_attention import LatentAttention
+        from asterlm.quantization.kv import quantize_tensor
+    except Exception as exc:  # a broken install is reported, not hidden
+        return None, f"importing the reference failed: {exc!r}"
+    import types
+
+    return types.SimpleNamespace(LatentLayerCache=LatentLayerCache, LatentAttention=LatentAttention,
+                                 quantize_tensor=quantize_tensor), None
+
+
+def reference_cases(ref, host: dict, lengths: list[int], hot: list[int]) -> list:
+    """One (attention module, decode arguments) per sampled sequence, in the reference's production
+    dtype (bf16): the cache is the reference's own LatentLayerCache holding the C3 split (newest
+    min(len, 2048) tokens hot, older tokens in 512-token chunks encoded by the reference quantizer,
+    the newest chunk possibly partial), and the attention module is a duck-typed LatentAttention
+    with identity absorption (head_dim = latent_rank = 512), as the golden fixtures use."""
+    import types
+
+    import torch
+
+    def linear():
+        m = torch.nn.Linear(512, 16 * 512, bias=False)
+        m.weight.data = torch.eye(512).repeat(16, 1).to(torch.bfloat16)
+        return m
+
+    attn = types.SimpleNamespace(n_heads=16, head_dim=512, latent_rank=512, rope_dim=64, logit_softcap=None,
+                                 training=False, dropout_p=0.0, k_up=linear(), v_up=linear())
+    cases = []
+    for i, h in sorted(host.items()):
+        n, hn = lengths[i], hot[i]
+        lat, rope = h["latent"], h["rope"]
+        cache = ref.LatentLayerCache(cache_dtype="hadamard_int4", group_size=64, recent_tokens=hn, chunk_tokens=512)
+        cold = n - hn
+        for s0 in range(0, cold, 512):
+            e0 = min(cold, s0 + 512)
+            cache.cold_latent.append(ref.quantize_tensor(lat[None, s0:e0].contiguous(), "hadamard_int4", group_size=64))
+            cache.cold_rope.append(rope[None, s0:e0].contiguous())
+        cache.latent = lat[None, cold:n].contiguous()
+        cache.rope_key = rope[None, cold:n].contiguous()
+        args = (h["q_lat"][None], h["q_rope"][None], lat[None, n:], rope[None, n:], cache)
+        cases.append((attn, args, n))
+    return cases
+
+
+def reference_rate(ref, cases, threads: int, budget_s: float, min_rounds: int = 1):
+    """seq-steps/s of the reference decode (LatentAttention._absorbed_decode) on `threads` host
+    threads: whole rounds over the sampled sequences until `budget_s` is spent."""
+    import torch
+
+    old = torch.get_num_threads()
+    torch.set_num_threads(threads)
+    try:
+        done, t0 = 0, time.perf_counter()
+        rounds = 0
+        with torch.inference_mode():
+            while rounds < min_rounds or time.perf_counter() - t0 < budget_s:
+                for attn, args, _ in cases:
+                    ref.LatentAttention._absorbed_decode(attn, *args)
+                    done += 1
+                rounds += 1
+        dt = time.perf_counter() - t0
+    finally:
+        torch.set_num_threads(old)
+    return done / dt, done, dt
+
+
+def reference_host_sample(dev):
+    """CPU copies of the sampled C3 sequences, drawn exactly as the GPU arm draws its batch
+    (on the GPU's generator when there is one)."""
+    import torch
+
+    from asterq.synth import host_sequences
+
+    lens, _ = c3_batch()
+    gen_dev = dev if (dev is not None and torch.cuda.is_available()) else "cpu"
+    return host_sequences(lens, REF_SAMPLE, seed=C3_DATA_SEED, device=gen_dev), str(gen_dev)
+
+
+def cpu_baseline_block(ref, host, lengths, hot, budget_s: float, one_thread_s: float) -> dict:
+    cores = host_cores()
+    cases = reference_cases(ref, host, lengths, hot)
+    rate, done, dt = reference_rate(ref, cases, cores, budget_s)
+    rate1, done1, dt1 = reference_rate(ref, cases[:2], 1, one_thread_s)
+    toks = sum(n for _, _, n in cases)
+    return {
+        "value": rate, "unit": UNIT, "cores": cores, "kind": "reference",
+        "sample": (f"{len(cases)} of the 64 C3 sequences (every 8th, {toks} cached tokens), {done} decodes in "
+                   f"{dt:.1f} s by LatentAttention._absorbed_decode of the unmodified reference (baseline/_ref), "
+                   "bf16 cache built by its own quantizer"),
+        "one_thread": {"value": rate1, "unit": UNIT, "cores": 1,
+                       "sample": f"sequences {REF_SAMPLE[:2]}, {done1} decodes in {dt1:.1f} s"},
+    }
 
 
 def run_reference_arm(args) -> None:
-    """--impl reference: the CPU oracle port of the reference path, all host threads."""
-    import torch
-
+    """--impl reference: the reference's own CPU decode path (baseline/_ref) on the host cores."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from asterq.synth import c3_lengths
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
+    ref, why = load_reference()
+    if ref is None:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+        return
+    import torch
 
-    lens = c3_lengths(0, 64)
-    hot = [min(n, 2048) for n in lens]
-    # the sample: 8 sequences of the config-3 batch, generated on the CPU
-    pick = list(range(0, 64, 8))
-    host = {}
-    g = torch.Generator().manual_seed(7)
-    from asterq.synth import outlier_channels
-
-    oc = outlier_channels(7)
-    for i in pick:
-        n = lens[i]
-        lat = torch.randn(n + 1, 512, generator=g)
-        lat[:, oc] *= 20
-        host[i] = {"latent": lat.to(torch.bfloat16), "rope": torch.randn(n + 1, 64, generator=g).to(torch.bfloat16),
-                   "q_lat": torch.randn(1, 16, 512, generator=g).to(torch.bfloat16),
-                   "q_rope": torch.randn(1, 16, 64, generator=g).to(torch.bfloat16)}
+    dev = torch.device("cuda", 0) if torch.cuda.is_available() else None
+    host, gen_dev = reference_host_sample(dev)
+    lens, hot = c3_batch()
+    cases = reference_cases(ref, host, lens, hot)
     cores = host_cores()
-    caches = oracle_caches(host, lens, hot)
-    for _ in range(max(0, args.warmup)):
-        cpu_oracle_rate(caches, budget_s=0.5)
-    rates = []
+    torch.set_num_threads(cores)
+    with torch.inference_mode():
+        for _ in range(max(0, args.warmup)):
+            for attn, a, _ in cases:
+                ref.LatentAttention._absorbed_decode(attn, *a)
+    # one step = one decode of each sampled sequence (all host threads)
+    steps = max(1, args.steps)
     t0 = time.perf_counter()
-    # each step is a bounded sample; the whole timed run stays near one minute
-    step_budget = min(2.0, 60.0 / max(1, args.steps))
-    for _ in range(max(1, args.steps)):
-        r, _, _, _ = cpu_oracle_rate(caches, budget_s=step_budget)
-        rates.append(r)
+    with torch.inference_mode():
+        for _ in range(steps):
+            for attn, a, _ in cases:
+                ref.LatentAttention._absorbed_decode(attn, *a)
     elapsed = time.perf_counter() - t0
-    value = statistics.median(rates)
-    sample = f"{len(pick)} config-3 sequences (every 8th), each step = {step_budget:.2f} s of oracle decodes"
+    value = steps * len(cases) / elapsed
+    rate1, done1, dt1 = reference_rate(ref, cases[:2], 1, 4.0)
+    sample = (f"{len(cases)} of the 64 C3 sequences (every 8th, {sum(n for _, _, n in cases)} cached tokens, drawn on "
+              f"{gen_dev}); each step decodes each of them once with LatentAttention._absorbed_decode of the "
+              "unmodified reference (baseline/_ref), bf16 cache built by its own quantizer")
     line = {
         "impl": "reference",
         "metric": METRIC,
         "value": value,
         "unit": UNIT,
-        "n_gpus": args.gpus,
-        "steps": args.steps,
+        "n_gpus": world,
+        "steps": steps,
         "warmup": args.warmup,
-        "ms_per_step": elapsed / max(1, args.steps) * 1e3,
+        "ms_per_step": elapsed / steps * 1e3,
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": "bf16",
         "data": "synthetic",
-        "config": {"workload": WORKLOAD, "sample": sample},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "config": run_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference", "sample": sample,
+                         "one_thread": {"value": rate1, "unit": UNIT, "cores": 1,
+                                        "sample": f"sequences {REF_SAMPLE[:2]}, {done1} decodes in {dt1:.1f} s"}},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -326,6 +425,8 @@ def main() -> None:
     from asterq import _lib
     from asterq.decode import DeviceDecodePlan, latent_decode, make_params
     from asterq.plan import build_plan
+    from asterq.sharding import shard_sequences
+    from asterq.synth import make_shard_workload
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -338,14 +439,19 @@ def main() -> None:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     args.warmup = max(args.warmup, 3)
 
-    keep = set(range(0, 64, 16)) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
-    wl = build_workload(dev, rank, keep_host=keep)
+    # the one C3 batch, split over the ranks (every rank computes the same split)
+    lens, hot = c3_batch()
+    shard = shard_sequences(lens, hot, world)[rank]
+    keep = set(REF_SAMPLE) if (rank == 0 and world == 1 and not args.no_cpu_baseline) else None
+    wl = make_shard_workload("C3", lens, hot, shard, q_len=1, n_heads=16, seed=C3_DATA_SEED, device=dev,
+                             keep_host=keep)
     plan = build_plan(wl.layouts, wl.n_heads)
     dplan = DeviceDecodePlan(plan, dev)
     out = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
     lib = _lib.load()
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
 
     # decode-only and combine-only parameter blocks (same kernels as latent_decode)
     p_dec = make_params(wl.pools, dplan, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out,
@@ -371,41 +477,107 @@ def main() -> None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        step_device()
-    torch.cuda.synchronize()
-
-    # ---- device-timed steps ----
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local, dev) as clocks:
-        t_start = torch.cuda.Event(enable_timing=True)
-        t_end = torch.cuda.Event(enable_timing=True)
-        t_start.record(stream)
+        for _ in range(args.warmup):
+            flush_buf.zero_()
+            step_device()
+        torch.cuda.synchronize()
+
+        # ---- device-timed steps (events around each step's launches; the L2 flush between) ----
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+               torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        barrier()
+        torch.cuda.synchronize()
         for e0, e1, e2 in ev:
+            flush_buf.zero_()
             e0.record(stream)
             _lib.check(lib.asterq_latent_decode(ctypes.byref(p_dec), sh))
             e1.record(stream)
             if n_combine:  # blocks cut into more pieces than the decode kernel merges itself
                 _lib.check(lib.asterq_splitkv_combine(ws.data_ptr(), plan.n_slots, dplan.combine.data_ptr(),
                                                       n_combine, 512, out.data_ptr(), _lib.DTYPE_BF16, sh))
-                e2.record(stream)
-        t_end.record(stream)
+            e2.record(stream)
         torch.cuda.synchronize()
-    barrier()
-    total_ms = max_over_ranks(t_start.elapsed_time(t_end))
-    dec_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1, _ in ev)
-    comb_ms = statistics.mean(e1.elapsed_time(e2) for _, e1, e2 in ev) if n_combine else 0.0
-    ms_per_step = total_ms / args.steps
-    n_seqs = len(wl.lengths)
-    value = world * n_seqs / (ms_per_step / 1e3)
+        barrier()
+        dec_ms = statistics.mean(e0.elapsed_time(e1) for e0, e1, _ in ev)
+        step_ms_local = statistics.mean(e0.elapsed_time(e2) for e0, _, e2 in ev)
+        comb_ms = statistics.mean(e1.elapsed_time(e2) for _, e1, e2 in ev) if n_combine else 0.0
+        ms_per_step = max_over_ranks(step_ms_local)
+        value = C3_SEQS / (ms_per_step / 1e3)
 
-    # ---- end-to-end through the public API with host buffers ----
-    # A serving loop's shape: every step copies its inputs from pinned host memory and
-    # reads its result back; the copies run on a second stream, double-buffered, so
-    # step k + 1's inputs and step k - 1's result move while step k decodes.
+        # ---- end-to-end through the public API with host buffers ----
+        e2e = e2e_measure(wl, dplan, out, dev, stream, args, barrier, max_over_ranks)
+
+    peak, peak_kind = measured_peaks()
+    alg_bytes = wl.algorithmic_bytes()
+    achieved = alg_bytes / (dec_ms / 1e3) / 1e9
+    traffic = profiled_traffic() if world == 1 else None
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "int4 codes + bf16/fp16 tensor-core operands, fp32 accumulate",
+        "data": "synthetic",
+        "config": run_config(world),
+        "shard": {"rank0_seqs": len(shard), "rank0_cached_tokens": int(sum(wl.lengths)),
+                  "rank0_work_items": int(plan.items.shape[0])},
+        "roofline": {
+            "bound": "hbm",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "GB/s",
+            "frac": achieved / peak,
+            "peak_kind": peak_kind,
+            "traffic": traffic,
+            "kernel": "asterq::dec::decode_kernel (timed with its query-preparation launch), rank 0",
+            "algorithmic_bytes_per_launch": alg_bytes,
+            "kernel_ms": dec_ms,
+            "combine_ms": comb_ms,
+        },
+        "e2e": e2e,
+        # per step: query preparation + decode_kernel, then combine_kernel when items were split
+        "gpu_launches": args.steps * (3 if n_combine else 2),
+        "clocks": clocks.summary(),
+    }
+
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["extras"] = extras(dev, args)
+    if world > 1 and not args.no_extras:
+        ex = multi_gpu_extras(dev, rank, world, args, max_over_ranks, barrier)
+        if rank == 0:
+            line["extras"] = ex
+
+    if keep:
+        ref, why = load_reference()
+        if ref is not None:
+            line["cpu_baseline"] = cpu_baseline_block(ref, {g: wl.host[k] for k, g in enumerate(shard) if k in wl.host},
+                                                      lens, hot, budget_s=10.0, one_thread_s=4.0)
+        else:
+            line["cpu_baseline"] = {"value": None, "unit": UNIT, "cores": host_cores(), "kind": "reference",
+                                    "sample": f"not measured: {why}"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def e2e_measure(wl, dplan, out, dev, stream, args, barrier, max_over_ranks) -> dict:
+    """The same metric through the public API (asterq.decode.latent_decode) with host buffers:
+    every step copies its inputs from pinned host memory and reads its result back; the copies
+    run on a second stream, double-buffered, so step k + 1's inputs and step k - 1's result
+    move while step k decodes (a serving loop's shape)."""
+    import torch
+
+    from asterq.decode import latent_decode
+
     host_in = [t.cpu().pin_memory() for t in (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)]
     dev_in = [[torch.empty_like(t) for t in (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)] for _ in range(2)]
     dev_out = [torch.empty_like(out) for _ in range(2)]
@@ -423,7 +595,7 @@ def main() -> None:
                 d.copy_(h, non_blocking=True)
             in_ready[b].record(copy_stream)
 
-    def run_e2e(n_steps, start_ev=None, end_ev=None):
+    def run(n_steps, start_ev=None, end_ev=None):
         for b in range(2):
             dec_done[b].record(stream)
         if start_ev is not None:
@@ -442,81 +614,65 @@ def main() -> None:
         if end_ev is not None:
             end_ev.record(copy_stream)
 
-    run_e2e(max(args.warmup, 2))
+    run(max(args.warmup, 2))
     torch.cuda.synchronize()
     barrier()
     e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    run_e2e(args.steps, e_s, e_e)
+    run(args.steps, e_s, e_e)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e_s.elapsed_time(e_e)) / args.steps
-    e2e_value = world * n_seqs / (e2e_ms / 1e3)
+    return {"value": C3_SEQS / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": e2e_ms, "per_rank": "h2d/d2h bytes are rank 0's"}
 
-    peak, peak_kind = measured_peaks()
-    alg_bytes = wl.algorithmic_bytes()
-    achieved = alg_bytes / (dec_ms / 1e3) / 1e9
-    traffic = profiled_traffic()
-    line = {
-        "metric": METRIC,
-        "value": value,
-        "unit": UNIT,
-        "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms_per_step,
-        "higher_is_better": True,
-        "scaling": "weak",
-        "vs_baseline": None,
-        "dtype": "int4 codes + bf16/fp16 tensor-core operands, fp32 accumulate",
-        "data": "synthetic",
-        "config": {
-            "workload": WORKLOAD,
-            "seqs_per_gpu": n_seqs,
-            "cached_tokens_per_gpu": int(sum(wl.lengths)),
-            "q_len": 1,
-            "n_heads": wl.n_heads,
-            "parallelism": f"sequence sharding x{world} (independent batches, no collective)",
-            "l2": f"no flush: {alg_bytes / 1e9:.2f} GB read per step per GPU > 126 MB L2",
-            "work_items": int(plan.items.shape[0]),
-        },
-        "roofline": {
-            "bound": "hbm",
-            "achieved": achieved,
-            "peak": peak,
-            "unit": "GB/s",
-            "frac": achieved / peak,
-            "peak_kind": peak_kind,
-            "traffic": traffic,
-            "kernel": "asterq::dec::decode_kernel (timed with its query-preparation launch)",
-            "algorithmic_bytes_per_launch": alg_bytes,
-            "kernel_ms": dec_ms,
-            "combine_ms": comb_ms,
-        },
-        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                "ms_per_step": e2e_ms},
-        # per step: query preparation + decode_kernel, then combine_kernel when items were split
-        "gpu_launches": args.steps * (3 if n_combine else 2),
-        "clocks": clocks.summary(),
-    }
 
-    if rank == 0 and world == 1 and not args.no_extras:
-        line["extras"] = extras(dev, args)
-    if world > 1 and not args.no_extras:
-        cp = context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier)
-        if rank == 0:
-            line["extras"] = {"c4_context_parallel": cp}
+def multi_gpu_extras(dev, rank, world, args, max_over_ranks, barrier) -> dict:
+    """N > 1: weak scaling (every rank its own 64-sequence C3 batch), C5 sharded by sequence, and
+    C4 context-parallel over the ranks."""
+    import torch
 
-    if keep:
-        rate, done, toks, dt = cpu_oracle_rate(oracle_caches(wl.host, wl.lengths, wl.hot))
-        line["cpu_baseline"] = {
-            "value": rate, "unit": UNIT, "cores": host_cores(), "kind": "port",
-            "sample": f"{len(keep)} of the 64 sequences, {done} oracle decodes ({toks} cached tokens) in {dt:.1f} s",
-        }
-    if rank == 0:
-        print(json.dumps(line), flush=True)
-    if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
+    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.plan import build_plan
+    from asterq.sharding import shard_sequences
+    from asterq.synth import c5_lengths, make_shard_workload, make_workload
+
+    res = {}
+
+    def timed_decode(wl, iters):
+        plan = build_plan(wl.layouts, wl.n_heads)
+        dp = DeviceDecodePlan(plan, dev)
+        o = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
+        fn = lambda: latent_decode(wl.pools, dp, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope,  # noqa: E731
+                                   softmax_scale=SOFTMAX_SCALE, out=o)
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        barrier()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(iters):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return max_over_ranks(s.elapsed_time(e) / iters)
+
+    lens, hot = c3_batch()
+    wl = make_workload("C3 weak", lens, hot, q_len=1, seed=C3_DATA_SEED + rank, device=dev)
+    ms = timed_decode(wl, 20)
+    res["c3_weak_scaling"] = {"seqs_per_gpu": C3_SEQS, "ms": ms, "seq_steps_per_s": world * C3_SEQS / ms * 1e3,
+                              "scaling": "weak (every rank its own 64-sequence batch, seed 1000 + rank)"}
+    del wl
+    lens5 = c5_lengths(0, 256)
+    hot5 = [min(n, 2048) for n in lens5]
+    shard5 = shard_sequences(lens5, hot5, world, q_len=3)[rank]
+    wl = make_shard_workload("C5", lens5, hot5, shard5, q_len=3, n_heads=16, seed=0, device=dev)
+    ms = timed_decode(wl, 5)
+    res["c5_sharded"] = {"seqs": 256, "q_len": 3, "ms": ms, "seq_steps_per_s": 256 / ms * 1e3,
+                         "scaling": f"strong (256 sequences split over {world} GPUs)"}
+    del wl
+    torch.cuda.empty_cache()
+    res["c4_context_parallel"] = context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier)
+    return res
 
 
 def context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier) -> dict:

@@ -472,3 +472,17 @@ def rel_l2(a: np.ndarray, b: np.ndarray) -> float:
 
 def max_abs(a: np.ndarray, b: np.ndarray) -> float:
     return float(np.max(np.abs(np.asarray(a, np.float64) - np.asarray(b, np.float64)))) if np.size(a) else 0.0
+
+
+def decode_sequence(latent: np.ndarray, rope: np.ndarray, q_lat: np.ndarray, q_rope: np.ndarray, n: int, hot: int,
+                    softmax_scale: float, chunk: int = 512) -> np.ndarray:
+    """One sequence of a ragged batch: tokens [0, n) are the cache (the newest ``hot`` in the hot
+    window, older ones in ``chunk``-token cold chunks, the newest possibly partial), tokens
+    [n, n + q_len) the step's new tokens; returns the context latents [q_len, H, 512]
+    (latent_attention.py:177-231 for q_len 1, :116-175 otherwise).  A module-level function so
+    that a process pool can run sequences in parallel."""
+    latent = np.asarray(latent, dtype=np.float32)
+    rope = np.asarray(rope, dtype=np.float32)
+    cache = build_cache_split(latent[:n], rope[:n], hot, chunk)
+    return decode(np.asarray(q_lat, np.float32), np.asarray(q_rope, np.float32), latent[n:], rope[n:], cache,
+                  softmax_scale)

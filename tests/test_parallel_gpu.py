@@ -141,3 +141,68 @@ def test_context_parallel_step_replays_as_cuda_graph(cuda):
     ref = O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[ctx:], rope[ctx:], cache, SCALE)
     got = eager.cpu().numpy()
     assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2
+
+
+def _cp_gloo_rank(rank: int, world: int, port: int, result_q) -> None:
+    """One process of a context-parallel step: the product's partial records on the GPU, a real
+    all-gather over the process group (gloo, through host copies), the product's combine."""
+    import os
+    from datetime import timedelta
+
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    try:
+        from asterq.context_parallel import ContextParallelDecoder
+        from asterq.synth import PoolBuilder, c1_inputs
+
+        dev = torch.device("cuda:0")
+        ctx, hot = 20 * 512 + 300, 700
+        inp = c1_inputs(seed=60, ctx=ctx, q_len=1)  # CPU generator: the same tensors on every rank
+        b = PoolBuilder([ctx], [hot], q_len=1, n_heads=16, device=dev)
+        b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+        wl = b.finish("cp")
+        dec = ContextParallelDecoder(wl.pools, wl.layouts[0], 16, rank, world, dev)
+        rec = dec.partial(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE).cpu()
+        gathered = torch.empty(world * rec.numel(), dtype=torch.float32)
+        dist.all_gather_into_tensor(gathered, rec)
+        out = torch.empty(1, 16, 512, dtype=torch.float32, device=dev)
+        dec.finish(gathered.to(dev), out)
+        torch.cuda.synchronize()
+        result_q.put((rank, out.cpu().numpy()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_context_parallel_processes_exchange_records(cuda, world):
+    """`world` processes (one GPU, kernels that never wait on one another) each decode their chunk
+    range, exchange the merged records with a real collective and combine: every rank's output
+    matches the single-process oracle decode."""
+    import multiprocessing as mp
+    import socket
+
+    from asterq.synth import c1_inputs
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_cp_gloo_rank, args=(r, world, port, q)) for r in range(world)]
+    for pr in procs:
+        pr.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for pr in procs:
+        pr.join(timeout=120)
+    assert all(pr.exitcode == 0 for pr in procs)
+    c, hot = 20 * 512 + 300, 700
+    inp = c1_inputs(seed=60, ctx=c, q_len=1)
+    lat, rope = inp["latent"].float().numpy(), inp["rope"].float().numpy()
+    cache = O.build_cache_split(lat[:c], rope[:c], hot, 512)
+    ref = O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[c:], rope[c:], cache, SCALE)
+    for r in range(world):
+        got = results[r][0:1]
+        assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2, r
+        assert np.array_equal(results[r], results[0])
