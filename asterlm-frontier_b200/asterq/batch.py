@@ -313,6 +313,8 @@ class PagedLatentBatch:
         self.planner = DevicePlanner(self.tables, n_heads, P, max_q_len=q_len, n_workers=n_workers)
         self.append_status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.flushes = 0  # pages encoded into the cold pool so far
+        self.flush_launches = 0  # encode launches those flushes took (one per step that flushed)
+        self._provisional = False  # a verify() step awaits accept()
         self.tables.upload()
 
     # ------------------------------------------------------------------ sizes
@@ -477,19 +479,64 @@ class PagedLatentBatch:
         the step's queries over each cache plus the step's own tokens, which are then appended."""
         if out is None:
             out = torch.empty(q_lat.shape[0], self.n_heads, LATENT_DIM, dtype=torch.bfloat16, device=self.device)
+        if self._provisional:
+            raise RuntimeError("accept() the pending verification step first")
         self._check_step_inputs(q_lat, q_rope, new_latent, new_rope, out)
         self.enqueue_step(q_lat, q_rope, new_latent, new_rope, out, softmax_scale=softmax_scale,
                           logit_softcap=logit_softcap)
         self.advance()
         return out
 
+    def verify(self, q_lat, q_rope, new_latent, new_rope, out=None, *, softmax_scale: float | None = None,
+               logit_softcap: float | None = None) -> torch.Tensor:
+        """A cache-aware verification step for multi-token prediction: the ``q_len`` tokens of every
+        active slot (the last accepted token, then the drafts) attend to the cache and causally to
+        each other, as ``step`` does, and are appended provisionally.  ``accept`` must follow: it
+        keeps a prefix of them per slot and only then flushes, so the cache ends exactly as if
+        only the accepted tokens had been appended (cache.py:186-201).
+
+        The reference verifier re-runs the model over the whole prefix each round
+        (speculative.py:45-60); here the prefix is read from the cache once."""
+        if out is None:
+            out = torch.empty(q_lat.shape[0], self.n_heads, LATENT_DIM, dtype=torch.bfloat16, device=self.device)
+        if self._provisional:
+            raise RuntimeError("accept() the previous verification step first")
+        self._check_step_inputs(q_lat, q_rope, new_latent, new_rope, out)
+        self.enqueue_step(q_lat, q_rope, new_latent, new_rope, out, softmax_scale=softmax_scale,
+                          logit_softcap=logit_softcap)
+        h = self.tables.host
+        h["hot_tokens"][h["q_len"] > 0] += self.q_len
+        self._provisional = True
+        return out
+
+    def accept(self, keep) -> None:
+        """After ``verify``: keep the first ``keep[s]`` (1 .. q_len) of slot s's provisional tokens
+        and drop the rest from its hot window (entries of empty slots are ignored); then flush and
+        hand out pages as after a ``step``."""
+        if not self._provisional:
+            raise RuntimeError("accept() follows a verify() step")
+        h = self.tables.host
+        act = h["q_len"] > 0
+        keep = np.asarray(keep, dtype=np.int64).reshape(-1)
+        if keep.shape[0] != self.max_seqs:
+            raise ValueError(f"keep must have one entry per slot ({self.max_seqs})")
+        if ((keep[act] < 1) | (keep[act] > self.q_len)).any():
+            raise ValueError(f"keep must be in 1..{self.q_len} for every active slot")
+        h["hot_tokens"][act] -= (self.q_len - keep[act]).astype(np.int32)
+        self._provisional = False
+        self._settle(force_upload=True)
+
     def advance(self) -> None:
         """Host bookkeeping after a step's launches: advance the mirror's hot lengths, flush the
         sequences over the threshold and hand out pages the next step's tokens need."""
+        h = self.tables.host
+        h["hot_tokens"][h["q_len"] > 0] += self.q_len
+        self._settle()
+
+    def _settle(self, force_upload: bool = False) -> None:
         h, P = self.tables.host, self.page_tokens
         act = h["q_len"] > 0
-        h["hot_tokens"][act] += self.q_len
-        changed = False
+        changed = force_upload
         over = np.nonzero(h["hot_tokens"] > self.threshold)[0]
         if over.size:
             self._flush(over)
@@ -527,6 +574,7 @@ class PagedLatentBatch:
             h["hot_tokens"][s] -= P
         self._hot_free.release(src)
         self.flushes += len(seqs)
+        self.flush_launches += 1
 
     def capture(self, q_lat, q_rope, new_latent, new_rope, out, *, softmax_scale: float | None = None,
                 logit_softcap: float | None = None) -> "StepGraph":

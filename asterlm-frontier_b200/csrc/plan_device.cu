@@ -18,8 +18,9 @@
 // CTA that writes the last one), more go to the combine launch.
 //
 // One CTA of 1024 threads.  Every stage is a loop over an index space (sequences x pages,
-// units, boundaries, items) strided over the threads, with block-wide prefix sums between
-// stages over arrays in the caller's scratch buffer.
+// tiles, units, boundaries, items) strided over the threads, with block-wide prefix sums
+// between stages over arrays in the caller's scratch buffer (the segment offsets also in
+// shared memory while the tile table is written, up to 40K segments).
 #include "asterq_internal.h"
 
 namespace asterq {
@@ -90,30 +91,47 @@ inline int64_t scratch_bytes(long long n_segs, int n_seqs, int cap_tiles, int ca
   return 8 * words + 4LL * (3LL * n_workers + cap_items);
 }
 
-// Exclusive prefix sum of a[0 .. n) in place over the whole block; returns the total.
+// Exclusive prefix sum of a[0 .. n) in place over the whole block; returns the total.  Warp w
+// owns one contiguous chunk, read 32 consecutive elements at a time (coalesced): the chunk
+// sums are scanned by the first warp (two block barriers in all), then every warp scans its
+// chunk 32 elements at a time with shuffles, carrying the running sum.
+constexpr int kWarps = kThreads / 32;
+static_assert(kWarps == 32, "the chunk totals are scanned by one warp");
 __device__ long long block_scan(long long* a, long long n, long long* sm) {
-  const int tid = threadIdx.x;
-  const long long per = (n + kThreads - 1) / kThreads;
-  const long long lo = min(n, tid * per), hi = min(n, lo + per);
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const long long per_warp = ((n + kWarps - 1) / kWarps + 31) / 32 * 32;
+  const long long lo = min(n, wid * per_warp), hi = min(n, lo + per_warp);
   long long sum = 0;
-#pragma unroll 8
-  for (long long i = lo; i < hi; ++i) sum += a[i];
-  sm[tid] = sum;
+  for (long long i = lo + lane; i < hi; i += 32) sum += a[i];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+  if (lane == 0) sm[wid] = sum;
   __syncthreads();
-  for (int off = 1; off < kThreads; off <<= 1) {
-    const long long v = (tid >= off) ? sm[tid - off] : 0;
-    __syncthreads();
-    sm[tid] += v;
-    __syncthreads();
-  }
-  long long run = (tid > 0) ? sm[tid - 1] : 0;
-  const long long total = sm[kThreads - 1];
-  for (long long i = lo; i < hi; ++i) {
-    const long long v = a[i];
-    a[i] = run;
-    run += v;
+  if (wid == 0) {
+    long long x = sm[lane];
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    sm[lane] = x;  // inclusive chunk sums
   }
   __syncthreads();
+  long long run = (wid > 0) ? sm[wid - 1] : 0;
+  const long long total = sm[kWarps - 1];
+  for (long long base = lo; base < hi; base += 32) {
+    const long long i = base + lane;
+    const long long v = (i < hi) ? a[i] : 0;
+    long long x = v;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const long long y = __shfl_up_sync(0xffffffffu, x, off);
+      if (lane >= off) x += y;
+    }
+    if (i < hi) a[i] = run + x - v;
+    run += __shfl_sync(0xffffffffu, x, 31);
+  }
+  __syncthreads();  // every thread has read `total` before `sm` is reused
   return total;
 }
 
@@ -150,8 +168,14 @@ __device__ void fail_all(const asterq_plan_buffers& b, int n_workers) {
   for (int w = threadIdx.x; w <= n_workers; w += kThreads) b.workers[w] = 0;
 }
 
+// segment offsets staged in shared memory for the per-tile pass (int32), when they fit
+constexpr long long kSegSharedMax = 40 * 1024;
+
+__host__ __device__ inline bool segs_in_shared(long long n_segs) { return n_segs + 1 <= kSegSharedMax; }
+
 __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc d, const asterq_plan_buffers b) {
   __shared__ long long sm[kThreads];
+  extern __shared__ int seg_sh[];  // [n_segs + 1] when segs_in_shared(n_segs)
   const int tid = threadIdx.x;
   const int B = d.n_seqs, H = d.n_heads, W = d.n_workers, P = d.page_tokens, MC = d.max_cold_pages;
   const int seg_w = MC + 2;  // segments per sequence: MC cold pages, the hot window, the new tokens
@@ -160,24 +184,43 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc 
   const int hot_tiles_per_page = (P + kHotTile - 1) / kHotTile;
 
   auto q_len = [&](int q) { return min(d.q_len[q], kMaxQLen); };  // <= 0: an inactive sequence slot
-  auto hot_len = [&](int q) { return clampi(d.hot_tokens[q], 0, d.max_hot_pages * P); };
 
-  // 1. tiles per segment, 16-row units per sequence
-  for (long long g = tid; g < n_segs; g += kThreads) {
-    const int q = (int)(g / seg_w), k = (int)(g % seg_w);
-    long long n = 0;
-    if (q_len(q) > 0) {
-      if (k < MC) {
-        if (k < clampi(d.n_cold_pages[q], 0, MC))
-          n = (clampi(d.cold_page_tokens[(long long)q * MC + k], 0, P) + kColdTile - 1) / kColdTile;
-      } else if (k == MC) {
-        const int h = hot_len(q);
-        n = (long long)(h / P) * hot_tiles_per_page + ((h % P) + kHotTile - 1) / kHotTile;
-      } else {
-        n = (q_len(q) + kHotTile - 1) / kHotTile;
-      }
+  // 1. tiles per segment, 16-row units per sequence (four segments per thread and pass, their
+  //    loads in flight together)
+  // (32-bit indices throughout: segment and tile counts are bounded by the int32 capacities,
+  // and 64-bit division is a long software routine)
+  const int n_segs32 = (int)n_segs;
+  for (int g0 = tid; g0 < n_segs32; g0 += 4 * kThreads) {
+    int ql[4], nc[4], x[4], qq[4], kk[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int g = min(g0 + u * kThreads, n_segs32 - 1);
+      qq[u] = g / seg_w;
+      kk[u] = g - qq[u] * seg_w;
+      ql[u] = __ldg(d.q_len + qq[u]);
+      nc[u] = __ldg(d.n_cold_pages + qq[u]);
+      x[u] = (kk[u] < MC) ? __ldg(d.cold_page_tokens + (long long)qq[u] * MC + kk[u])
+                          : (kk[u] == MC ? __ldg(d.hot_tokens + qq[u]) : 0);
     }
-    s.seg[g] = n;
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int g = g0 + u * kThreads;
+      if (g >= n_segs32) break;
+      const int k = kk[u];
+      const int qlen = min(ql[u], kMaxQLen);
+      long long n = 0;
+      if (qlen > 0) {
+        if (k < MC) {
+          if (k < clampi(nc[u], 0, MC)) n = (clampi(x[u], 0, P) + kColdTile - 1) / kColdTile;
+        } else if (k == MC) {
+          const int h = clampi(x[u], 0, d.max_hot_pages * P);
+          n = (long long)(h / P) * hot_tiles_per_page + ((h % P) + kHotTile - 1) / kHotTile;
+        } else {
+          n = (qlen + kHotTile - 1) / kHotTile;
+        }
+      }
+      s.seg[g] = n;
+    }
   }
   for (int q = tid; q < B; q += kThreads)
     s.seq_units[q] = q_len(q) > 0 ? ((long long)q_len(q) * H + kRows - 1) / kRows : 0;
@@ -194,26 +237,82 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc 
   }
   __syncthreads();
 
-  // 2. the tile table and the tiles' estimated times
-  for (long long g = tid; g < n_segs; g += kThreads) {
-    const int q = (int)(g / seg_w), k = (int)(g % seg_w);
-    const long long t0 = s.seg[g], cnt = s.seg[g + 1] - t0;
-    for (long long i = 0; i < cnt; ++i) {
-      const long long t = t0 + i;
+  // 2. the tile table and the tiles' estimated times, one thread per tile (a segment can hold
+  //    a whole hot window of tiles, too many for one thread): tile t lies in the last segment
+  //    whose offset is <= t, found by binary search over the offsets (in shared memory when
+  //    they fit; empty segments share their successor's offset and never win the search)
+  const bool sh = segs_in_shared(n_segs);
+  if (sh)
+    for (long long g = tid; g <= n_segs; g += kThreads) seg_sh[g] = (int)s.seg[g];
+  __syncthreads();
+  // four tiles per thread and pass: their searches, then all their loads, then the stores, so
+  // the loads of the four are in flight together
+  constexpr int kU = 4;
+  const int n_tiles32 = (int)n_tiles;
+  for (int t0 = tid; t0 < n_tiles32; t0 += kU * kThreads) {
+    int g[kU], i[kU], kk[kU];
+    const int* src1[kU];
+    const int* src2[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int t = t0 + u * kThreads;
+      g[u] = 0;
+      if (t < n_tiles32) {
+        int lo = 0, hi = n_segs32 - 1;
+        if (sh) {
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (seg_sh[mid] <= t) lo = mid;
+            else hi = mid - 1;
+          }
+        } else {
+          while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (s.seg[mid] <= t) lo = mid;
+            else hi = mid - 1;
+          }
+        }
+        g[u] = lo;
+      }
+      i[u] = t - (sh ? seg_sh[g[u]] : (int)s.seg[g[u]]);
+      const int q = g[u] / seg_w, k = g[u] - q * seg_w;
+      kk[u] = k;
+      if (k < MC) {  // page id, tokens in the page
+        src1[u] = d.cold_pages + (long long)q * MC + k;
+        src2[u] = d.cold_page_tokens + (long long)q * MC + k;
+      } else if (k == MC) {  // page id, hot tokens
+        src1[u] = d.hot_pages + (long long)q * d.max_hot_pages + i[u] / hot_tiles_per_page;
+        src2[u] = d.hot_tokens + q;
+      } else {  // first row of the new tokens, their number
+        src1[u] = d.q_start + q;
+        src2[u] = d.q_len + q;
+      }
+    }
+    int v1[kU], v2[kU];
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const bool live = t0 + u * kThreads < n_tiles32;
+      v1[u] = live ? __ldg(src1[u]) : 0;
+      v2[u] = live ? __ldg(src2[u]) : 0;
+    }
+#pragma unroll
+    for (int u = 0; u < kU; ++u) {
+      const int t = t0 + u * kThreads;
+      if (t >= n_tiles32) break;
+      const int k = kk[u];
       int4 tile;
       if (k < MC) {
-        const long long row = (long long)q * MC + k;
-        const int tok = clampi(d.cold_page_tokens[row], 0, P), off = (int)i * kColdTile;
-        tile = make_int4(ASTERQ_TILE_COLD, d.cold_pages[row], off, min(kColdTile, tok - off));
+        const int tok = clampi(v2[u], 0, P), off = i[u] * kColdTile;
+        tile = make_int4(ASTERQ_TILE_COLD, v1[u], off, min(kColdTile, tok - off));
         s.tile_cost[t] = cold_cost(tile.w);
       } else if (k == MC) {
-        const int h = hot_len(q), page = (int)(i / hot_tiles_per_page), off = (int)(i % hot_tiles_per_page) * kHotTile;
-        tile = make_int4(ASTERQ_TILE_HOT, d.hot_pages[(long long)q * d.max_hot_pages + page], off,
-                         min(kHotTile, min(P, h - page * P) - off));
+        const int h = clampi(v2[u], 0, d.max_hot_pages * P), page = i[u] / hot_tiles_per_page;
+        const int off = (i[u] - page * hot_tiles_per_page) * kHotTile;
+        tile = make_int4(ASTERQ_TILE_HOT, v1[u], off, min(kHotTile, min(P, h - page * P) - off));
         s.tile_cost[t] = hot_cost(tile.w);
       } else {
-        const int off = (int)i * kHotTile;
-        tile = make_int4(ASTERQ_TILE_NEW, d.q_start[q], off, min(kHotTile, q_len(q) - off));
+        const int off = i[u] * kHotTile;
+        tile = make_int4(ASTERQ_TILE_NEW, v1[u], off, min(kHotTile, min(v2[u], kMaxQLen) - off));
         s.tile_cost[t] = hot_cost(tile.w);
       }
       *reinterpret_cast<int4*>(b.tiles + 4 * t) = tile;
@@ -322,7 +421,11 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc 
     *reinterpret_cast<int4*>(it) = make_int4((int)u, rb, a, e);
     *reinterpret_cast<int4*>(it + 4) = make_int4(slot, b.units[2 * u], b.units[2 * u + 1], q_len(q));
     const int t0 = (int)(s.unit_t[u] & 0xffffffffLL);
-    const long long start = (a == t0) ? uoff[u] : uoff[u] + kItemNs + pc[a] - pc[t0];
+    // A unit's first piece goes to the worker whose share holds its first min_gap of work: a
+    // boundary that falls within that much of the unit's start made no cut (the piece would
+    // be a sliver), so the piece runs on to the next cut, a whole share further on; placed by
+    // its start time it would land on the worker before and double that worker's load.
+    const long long start = (a == t0) ? uoff[u] + kItemNs + min_gap : uoff[u] + kItemNs + pc[a] - pc[t0];
     s.item_worker[idx] = (int)min((long long)W - 1, start / wd);
   };
   for (long long u = tid; u < n_units; u += kThreads) {
@@ -478,7 +581,18 @@ extern "C" int asterq_plan_batch(const asterq_batch_desc* d, const asterq_plan_b
   for (const void* ptr : aligned)
     if (reinterpret_cast<uintptr_t>(ptr) & 15)
       return set_error(ASTERQ_ERR_MISALIGNED, "plan_batch: tables and scratch must be 16-byte aligned");
-  plan::plan_kernel<<<1, plan::kThreads, 0, reinterpret_cast<cudaStream_t>(stream)>>>(*d, *b);
+  const long long n_segs = plan::n_segments(d->n_seqs, d->max_cold_pages);
+  const size_t smem = plan::segs_in_shared(n_segs) ? (size_t)(n_segs + 1) * sizeof(int) : 0;
+  static int configured_device = -1;  // the opt-in above 48 KB is per device
+  int dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess && dev != configured_device) {
+    cudaError_t e = cudaFuncSetAttribute(plan::plan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(plan::kSegSharedMax * sizeof(int)));
+    if (e != cudaSuccess)
+      return set_error(ASTERQ_ERR_CUDA, "plan_batch: shared memory opt-in: %s", cudaGetErrorString(e));
+    configured_device = dev;
+  }
+  plan::plan_kernel<<<1, plan::kThreads, smem, reinterpret_cast<cudaStream_t>(stream)>>>(*d, *b);
   return check_launch("plan_batch");
 }
 

@@ -324,3 +324,82 @@ def test_captured_step_replays_like_the_eager_step(cuda):
     assert graphed.flushes == eager.flushes > 0
     for name in ("hot_tokens", "n_cold", "hot_pages", "cold_pages"):
         assert torch.equal(graphed.tables.dev[name], eager.tables.dev[name]), name
+
+
+def test_mtp_verification_keeps_only_accepted_tokens(cuda):
+    """Cache-aware verification (q_len 3: the last accepted token and two drafts): every step's
+    three tokens attend to the cache and causally to each other (checked against the oracle over
+    the accepted history), then a random prefix of them is accepted.  Flushes follow the accepted
+    history only (the reference's rule, cache.py:167-177, replayed on it), and at the end the pages
+    hold exactly that history: hot tokens bit-exact, cold codes and scales the oracle's."""
+    from asterq.batch import PagedLatentBatch
+
+    q_len, P, recent = 3, 128, 64
+    threshold = recent + P
+    batch = PagedLatentBatch(16, max_seqs=4, q_len=q_len, page_tokens=P, recent_tokens=recent,
+                             max_cold_pages=24, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(17)
+    rng = np.random.default_rng(17)
+    hist = _History()
+    sim = {}  # the reference's (cold, hot) lengths, replayed on the accepted tokens
+    for n in (5, 150, 191, 900):
+        lat = torch.randn(n, 512, generator=g, device=cuda)
+        lat[:, :5] *= 20.0
+        lat, rope = lat.bfloat16(), torch.randn(n, 64, generator=g, device=cuda).bfloat16()
+        s = batch.add_sequence(lat, rope)
+        hist.start(s, lat, rope)
+        cold = 0
+        while n - cold > threshold:
+            cold += P
+        sim[s] = [cold, n - cold]
+    rows = 4 * q_len
+    checked = 0
+    for step in range(70):
+        q_lat = torch.randn(rows, 16, 512, generator=g, device=cuda).bfloat16()
+        q_rope = torch.randn(rows, 16, 64, generator=g, device=cuda).bfloat16()
+        new_lat = torch.randn(rows, 512, generator=g, device=cuda).bfloat16()
+        new_rope = torch.randn(rows, 64, generator=g, device=cuda).bfloat16()
+        before = {s: (batch.length(s), batch.hot_length(s)) for s in batch.active()}
+        for s, (n, hot) in before.items():
+            assert (n, hot) == (sum(sim[s]), sim[s][1]), f"step {step} slot {s}"
+        out = batch.verify(q_lat, q_rope, new_lat, new_rope, torch.empty(rows, 16, 512, device=cuda))
+        with pytest.raises(RuntimeError):
+            batch.step(q_lat, q_rope, new_lat, new_rope)
+        if step % 9 == 0 or step == 69:
+            got = out.cpu().numpy()
+            for s, (n, hot) in before.items():
+                lat, rope = hist.tokens(s)
+                r = slice(s * q_len, (s + 1) * q_len)
+                lat = np.concatenate([lat, new_lat[r].float().cpu().numpy()])
+                rope = np.concatenate([rope, new_rope[r].float().cpu().numpy()])
+                want = O.decode_sequence(lat, rope, q_lat[r].float().cpu().numpy(), q_rope[r].float().cpu().numpy(),
+                                         n, hot, SCALE, chunk=P)
+                _close(got[r], want, f"step {step} slot {s} (n {n}, hot {hot})")
+                checked += 1
+        keep = rng.integers(1, q_len + 1, size=4)
+        batch.accept(keep)
+        for s in before:
+            k = int(keep[s])
+            r = slice(s * q_len, s * q_len + k)
+            hist.extend(s, new_lat[r], new_rope[r])
+            sim[s][1] += k
+            if sim[s][1] > threshold:
+                sim[s][0] += P
+                sim[s][1] -= P
+    batch.raise_if_failed()
+    assert checked >= 30 and batch.flushes >= 4
+    h = batch.tables.host
+    for s in batch.active():
+        lat, rope = hist.tokens(s)
+        n_cold = int(h["n_cold"][s])
+        cold = int(h["cold_tokens"][s, :n_cold].sum())
+        assert [cold, int(h["hot_tokens"][s])] == sim[s] and cold + sim[s][1] == lat.shape[0]
+        assert batch.tables.dev["hot_tokens"][s].item() == sim[s][1]
+        hot_pages = [int(p) for p in h["hot_pages"][s] if p >= 0]
+        hot = torch.cat([batch.pools.hot_latent[p] for p in hot_pages])[: sim[s][1]].float().cpu().numpy()
+        np.testing.assert_array_equal(hot, lat[cold:])
+        if n_cold:
+            pages = [int(p) for p in h["cold_pages"][s, :n_cold]]
+            codes = torch.cat([batch.pools.cold_codes[p] for p in pages]).cpu().numpy()
+            q = O.quantize(lat[:cold], "hadamard_int4", 64)
+            np.testing.assert_array_equal(codes, q.data.reshape(cold, 256))
