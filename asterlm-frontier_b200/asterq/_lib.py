@@ -23,6 +23,16 @@ DTYPE_F32 = 0
 DTYPE_BF16 = 1
 DTYPE_F16 = 2
 
+
+def dtype_code(dtype) -> int:
+    """The C ABI's element-type code of a torch dtype (float32, bfloat16, float16)."""
+    import torch
+
+    codes = {torch.float32: DTYPE_F32, torch.bfloat16: DTYPE_BF16, torch.float16: DTYPE_F16}
+    if dtype not in codes:
+        raise TypeError(f"dtype {dtype}: the kernels read float32, bfloat16 or float16")
+    return codes[dtype]
+
 SCHEME_HADAMARD_INT4 = 0
 SCHEME_INT4 = 1
 SCHEME_INT8 = 2
@@ -31,6 +41,8 @@ TILE_COLD = 0
 TILE_HOT = 1
 TILE_NEW = 2
 TILE_HOLD = 3  # failure-detection test hook (see include/asterq.h)
+
+IPC_HANDLE_BYTES = 64
 
 # entry points declared in include/asterq.h
 EXPORTED_SYMBOLS = (
@@ -46,6 +58,13 @@ EXPORTED_SYMBOLS = (
     "asterq_splitkv_combine",
     "asterq_splitkv_merge",
     "asterq_splitkv_combine_ranks",
+    "asterq_mailbox_bytes",
+    "asterq_mailbox_create",
+    "asterq_mailbox_open",
+    "asterq_mailbox_close",
+    "asterq_mailbox_destroy",
+    "asterq_cp_merge_push",
+    "asterq_cp_combine_wait",
     "asterq_plan_scratch_bytes",
     "asterq_plan_batch",
     "asterq_batch_append",
@@ -189,6 +208,20 @@ def load() -> ctypes.CDLL:
     lib.asterq_splitkv_merge.argtypes = [vp, i32, vp, i32, i32, vp, vp]
     lib.asterq_splitkv_combine_ranks.restype = ctypes.c_int
     lib.asterq_splitkv_combine_ranks.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp]
+    lib.asterq_mailbox_bytes.restype = i64
+    lib.asterq_mailbox_bytes.argtypes = [i32, i32, i32]
+    lib.asterq_mailbox_create.restype = ctypes.c_int
+    lib.asterq_mailbox_create.argtypes = [i64, ctypes.POINTER(ctypes.c_void_p), vp]
+    lib.asterq_mailbox_open.restype = ctypes.c_int
+    lib.asterq_mailbox_open.argtypes = [vp, ctypes.POINTER(ctypes.c_void_p)]
+    lib.asterq_mailbox_close.restype = ctypes.c_int
+    lib.asterq_mailbox_close.argtypes = [vp]
+    lib.asterq_mailbox_destroy.restype = ctypes.c_int
+    lib.asterq_mailbox_destroy.argtypes = [vp]
+    lib.asterq_cp_merge_push.restype = ctypes.c_int
+    lib.asterq_cp_merge_push.argtypes = [vp, i32, vp, i32, i32, vp, i32, i32, vp]
+    lib.asterq_cp_combine_wait.restype = ctypes.c_int
+    lib.asterq_cp_combine_wait.argtypes = [vp, i32, i32, vp, i32, vp, i32, i64, vp, vp]
     lib.asterq_plan_scratch_bytes.restype = i64
     lib.asterq_plan_scratch_bytes.argtypes = [ctypes.POINTER(BatchDesc), i32, i32, i32]
     lib.asterq_plan_batch.restype = ctypes.c_int

@@ -19,6 +19,14 @@ and releases the hot page.  The decode kernel reads the pools through
 The hot window holds at most ``recent_tokens + chunk_tokens`` tokens, exactly as
 in the reference: after every append, whole chunks move from the front of the
 hot window to the cold pool while the hot length exceeds that threshold.
+
+The hot window keeps the caller's dtype (cache.py:193-200 stores the appended
+tensors as they come): a caller appending float32 (or float16) latents gets them
+back from ``latent`` / ``materialize_*`` unchanged, and flushed chunks are
+quantized from those values (cache.py:172, bit-exact codes and scales).  The
+decode kernel reads bf16 operands, so for such callers the hot pages also hold
+a bf16 copy that only the kernel reads (bf16 rounding of the hot keys and
+values, like the bf16 rounding of the query).
 """
 from __future__ import annotations
 
@@ -138,7 +146,7 @@ class LatentLayerCache:
         """Bytes the reference would account (cache.py:79-87): codes + scales + cold RoPE + hot tensors."""
         b, cold = self._batch, self.cold_length
         total = b * cold * (LATENT_DIM // 2 + (LATENT_DIM // GROUP_SIZE) * 2 + ROPE_DIM * 2)
-        total += b * self._hot_len * (LATENT_DIM + ROPE_DIM) * 2
+        total += b * self._hot_len * (LATENT_DIM + ROPE_DIM) * self._dtype.itemsize
         return int(total)
 
     # ------------------------------------------------------------------ pools
@@ -146,8 +154,12 @@ class LatentLayerCache:
         if self._hot is None:
             self._batch = batch
             self._dtype = dtype
-            self._hot = _Pool({"latent": ((LATENT_DIM,), torch.bfloat16), "rope": ((ROPE_DIM,), torch.bfloat16)},
-                              self.page_tokens, device)
+            fields = {"latent": ((LATENT_DIM,), torch.bfloat16), "rope": ((ROPE_DIM,), torch.bfloat16)}
+            if dtype != torch.bfloat16:
+                # the caller's own values (the reference keeps the appended dtype), beside the
+                # bf16 operands the decode kernel reads
+                fields.update(src_latent=((LATENT_DIM,), dtype), src_rope=((ROPE_DIM,), dtype))
+            self._hot = _Pool(fields, self.page_tokens, device)
             self._cold = _Pool({"codes": ((LATENT_DIM // 2,), torch.uint8),
                                 "scales": ((LATENT_DIM // GROUP_SIZE,), torch.float16),
                                 "rope": ((ROPE_DIM,), torch.bfloat16)}, self.page_tokens, device)
@@ -155,6 +167,13 @@ class LatentLayerCache:
             self._cold_pages = [[] for _ in range(batch)]
         elif batch != self._batch:
             raise ValueError(f"batch size changed from {self._batch} to {batch}")
+        elif dtype != self._dtype:
+            raise ValueError(f"latent dtype changed from {self._dtype} to {dtype} (the hot window keeps one dtype)")
+
+    @property
+    def _src(self) -> str:
+        """Prefix of the hot-pool fields holding the caller's values ("" when they are the bf16 operands)."""
+        return "" if self._dtype == torch.bfloat16 else "src_"
 
     def pools(self) -> LatentPools:
         """The five device pools in the layout the decode C ABI reads."""
@@ -211,8 +230,12 @@ class LatentLayerCache:
         pages = torch.tensor(self._hot_pages, dtype=torch.int64, device=latent.device)  # [B, n_pages]
         slot = pages[:, pos // P] * P + (pos % P)  # [B, T]
         flat = slot.reshape(-1)
-        self._hot["latent"].view(-1, LATENT_DIM).index_copy_(0, flat, latent.reshape(-1, LATENT_DIM).to(torch.bfloat16))
-        self._hot["rope"].view(-1, ROPE_DIM).index_copy_(0, flat, rope_key.reshape(-1, ROPE_DIM).to(torch.bfloat16))
+        lat, rope = latent.reshape(-1, LATENT_DIM), rope_key.reshape(-1, ROPE_DIM).to(latent.dtype)
+        self._hot["latent"].view(-1, LATENT_DIM).index_copy_(0, flat, lat.to(torch.bfloat16))
+        self._hot["rope"].view(-1, ROPE_DIM).index_copy_(0, flat, rope.to(torch.bfloat16))
+        if self._src:
+            self._hot["src_latent"].view(-1, LATENT_DIM).index_copy_(0, flat, lat.to(self._dtype))
+            self._hot["src_rope"].view(-1, ROPE_DIM).index_copy_(0, flat, rope.to(self._dtype))
         self._hot_len = end
 
     def _flush_cold_chunks(self) -> None:
@@ -229,15 +252,17 @@ class LatentLayerCache:
         src = torch.tensor([self._hot_pages[b][0] for b in range(bsz)], dtype=torch.int64, device=dev)
         dst_pages = self._cold.alloc(bsz)
         dst = torch.tensor(dst_pages, dtype=torch.int64, device=dev)
-        x = self._hot["latent"].index_select(0, src).reshape(bsz * P, LATENT_DIM)
+        # quantized from the caller's values (cache.py:172 encodes the hot tensor as stored)
+        x = self._hot[self._src + "latent"].index_select(0, src).reshape(bsz * P, LATENT_DIM)
         codes = torch.empty(bsz * P, LATENT_DIM // 2, dtype=torch.uint8, device=dev)
         scales = torch.empty(bsz * P, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=dev)
         lib = _lib.load()
-        _lib.check(lib.asterq_quantize(x.data_ptr(), _lib.DTYPE_BF16, bsz * P, LATENT_DIM, LATENT_DIM,
+        _lib.check(lib.asterq_quantize(x.data_ptr(), _lib.dtype_code(x.dtype), bsz * P, LATENT_DIM, LATENT_DIM,
                                        _SCHEME_IDS[self.cache_dtype], GROUP_SIZE, codes.data_ptr(), scales.data_ptr(),
                                        _lib.stream_handle(dev)))
         self._cold["codes"].index_copy_(0, dst, codes.view(bsz, P, -1))
         self._cold["scales"].index_copy_(0, dst, scales.view(bsz, P, -1))
+        # cold RoPE keys are bf16 whatever the caller's dtype (cache.py:162-164)
         self._cold["rope"].index_copy_(0, dst, self._hot["rope"].index_select(0, src))
         freed = []
         for b in range(bsz):
@@ -274,12 +299,12 @@ class LatentLayerCache:
     # ------------------------------------------------------------------ reads (API parity, not the decode path)
     @property
     def latent(self) -> torch.Tensor | None:
-        """Hot window [B, S_hot, 512] (a gathered copy of the hot pages)."""
-        return self._gather_hot("latent")
+        """Hot window [B, S_hot, 512] in the caller's dtype (a gathered copy of the hot pages)."""
+        return self._gather_hot(self._src + "latent")
 
     @property
     def rope_key(self) -> torch.Tensor | None:
-        return self._gather_hot("rope")
+        return self._gather_hot(self._src + "rope")
 
     def _gather_hot(self, name: str) -> torch.Tensor | None:
         if self._hot is None:

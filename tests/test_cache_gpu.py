@@ -176,3 +176,51 @@ def test_window_trim_keeps_sink_and_recent(cuda):
     assert cache.length == 1000
     cache.append(lat[:, 2000:2100], rope[:, 2000:2100], 1000, 4)
     assert cache.length <= 1000 + 256 and cache.hot_length <= 512
+
+
+def test_float32_caller_keeps_float32_and_codes_come_from_it(cuda):
+    """The reference keeps the appended dtype in the hot window (cache.py:193-200) and quantizes
+    flushed chunks from it (cache.py:172); cold RoPE keys become bf16 (cache.py:162-164).  A
+    float32 caller therefore gets float32 hot tokens back unchanged, codes and scales bit-exact
+    to quantizing the float32 values, and float32 hot bytes in ``num_bytes``.  The decode kernel
+    reads bf16 operands of the hot window, the new tokens and the query; its result is checked
+    against the oracle on exactly those operands."""
+    import dataclasses
+
+    from asterq.attention import latent_attention
+    from asterq.cache import LatentLayerCache
+
+    n = 2300
+    g = torch.Generator().manual_seed(13)
+    lat = torch.randn(n + 1, 512, generator=g)
+    lat[:, :5] *= 20.0
+    rope = torch.randn(n + 1, 64, generator=g)
+    q_lat, q_rope = torch.randn(1, 16, 512, generator=g), torch.randn(1, 16, 64, generator=g)
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=512, chunk_tokens=512)
+    cache.append(lat[None, :1000].to(cuda), rope[None, :1000].to(cuda), None, 0)
+    cache.append(lat[None, 1000:n].to(cuda), rope[None, 1000:n].to(cuda), None, 0)
+
+    lat_np, rope_np = lat.numpy(), rope.numpy()
+    ref = O.build_cache_from_tokens(lat_np[:n], O.round_bf16(rope_np[:n]), 512, 512)
+    assert cache.cold_chunks == len(ref.cold) > 0 and cache.length == n
+    for q, r, c in zip(cache.cold_latent, cache.cold_rope, ref.cold):
+        np.testing.assert_array_equal(q.data[0].cpu().numpy(), c.codes)
+        np.testing.assert_array_equal(q.scale[0, :, :, 0].cpu().numpy(), c.scales)
+        assert r.dtype == torch.bfloat16
+        np.testing.assert_array_equal(r[0].float().cpu().numpy(), c.rope)
+    cold = cache.cold_length
+    assert cache.latent.dtype == torch.float32 and cache.rope_key.dtype == torch.float32
+    np.testing.assert_array_equal(cache.latent[0].cpu().numpy(), lat_np[cold:n])
+    np.testing.assert_array_equal(cache.rope_key[0].cpu().numpy(), rope_np[cold:n])
+    assert cache.materialize_latent().dtype == torch.float32
+    assert cache.num_bytes == cold * 400 + (n - cold) * (512 + 64) * 4
+    with pytest.raises(ValueError, match="dtype"):
+        cache.append(lat[None, n:].to(cuda).bfloat16(), rope[None, n:].to(cuda).bfloat16(), None, 0)
+
+    out = latent_attention(q_lat[None].to(cuda), q_rope[None].to(cuda), lat[None, n:].to(cuda),
+                           rope[None, n:].to(cuda), cache, softmax_scale=SCALE)
+    bf = O.round_bf16
+    view = dataclasses.replace(ref, hot_latent=bf(ref.hot_latent), hot_rope=bf(ref.hot_rope))
+    want = O.decode(bf(q_lat.numpy()), bf(q_rope.numpy()), bf(lat_np[n:]), bf(rope_np[n:]), view, SCALE)
+    got = out[0].cpu().numpy()
+    assert O.rel_l2(got, want) <= 1e-3 and O.max_abs(got, want) <= 2e-2
