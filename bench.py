@@ -10,9 +10,11 @@ bytes (asterq.sharding): every rank decodes its own sequences, no collective
   value  device-timed whole-job seq-steps/s: 64 sequences / the max over ranks
          of the per-step decode time (CUDA events around each step's launches;
          a 256 MB write flushes L2 between steps, outside the events)
-  e2e    the same metric through the public API (asterq.decode.latent_decode)
-         with the step's query/new-token inputs copied from pinned host memory
-         and the context latents copied back, every step
+  e2e    the same metric through the serving API (asterq.batch.PagedLatentBatch):
+         every step copies its queries and new tokens from pinned host memory,
+         plans on the GPU, decodes, appends the new tokens (the cache grows one
+         token per sequence per step, flushing pages as they fill) and copies the
+         context latents back
   roofline  achieved HBM GB/s of rank 0's decode kernel = algorithmic bytes per
          launch / its CUDA-event duration, against MEASURED_PEAKS.json
   cpu_baseline  the reference's own decode (LatentAttention._absorbed_decode of
@@ -506,7 +508,7 @@ def main() -> None:
         value = C3_SEQS / (ms_per_step / 1e3)
 
         # ---- end-to-end through the public API with host buffers ----
-        e2e = e2e_measure(wl, dplan, out, dev, stream, args, barrier, max_over_ranks)
+        e2e = e2e_measure(wl, dev, stream, args, barrier, max_over_ranks)
 
     peak, peak_kind = measured_peaks()
     alg_bytes = wl.algorithmic_bytes()
@@ -543,7 +545,11 @@ def main() -> None:
         },
         "e2e": e2e,
         # per step: query preparation + decode_kernel, then combine_kernel when items were split
-        "gpu_launches": args.steps * (3 if n_combine else 2),
+        # device-timed steps: query preparation + decode_kernel (+ combine_kernel when blocks were cut
+        # into more pieces than the kernel merges); e2e steps: plan_batch, query preparation, decode,
+        # append (+ combine), and any flush's encode
+        "gpu_launches": args.steps * (3 if n_combine else 2) + args.steps * e2e["launches_per_step"]
+        + e2e["flush_launches_timed"],
         "clocks": clocks.summary(),
     }
 
@@ -569,28 +575,44 @@ def main() -> None:
         dist.destroy_process_group()
 
 
-def e2e_measure(wl, dplan, out, dev, stream, args, barrier, max_over_ranks) -> dict:
-    """The same metric through the public API (asterq.decode.latent_decode) with host buffers:
-    every step copies its inputs from pinned host memory and reads its result back; the copies
-    run on a second stream, double-buffered, so step k + 1's inputs and step k - 1's result
-    move while step k decodes (a serving loop's shape)."""
+def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
+    """The same metric end to end through the serving API (``asterq.batch.PagedLatentBatch``),
+    with the cache growing by one token per sequence every step, as in a decode loop
+    (generate_tokens, decode.py:113-129, with LatentLayerCache.append, cache.py:186-201):
+
+    each step copies its queries and new tokens from pinned host memory, plans the step on the
+    GPU from the device page tables (``asterq_plan_batch``), decodes, appends the new tokens to
+    the hot windows in place, flushes a sequence's oldest hot page into a cold page once its
+    window passes recent + page tokens (cache.py:167-177), and copies the context latents back
+    to pinned host memory.  The copies run on a second stream, double-buffered, so step k + 1's
+    inputs and step k - 1's result move while step k decodes."""
     import torch
 
-    from asterq.decode import latent_decode
+    from asterq.batch import PagedLatentBatch
 
-    host_in = [t.cpu().pin_memory() for t in (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)]
-    dev_in = [[torch.empty_like(t) for t in (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)] for _ in range(2)]
-    dev_out = [torch.empty_like(out) for _ in range(2)]
-    host_out = [torch.empty(out.shape, dtype=out.dtype).pin_memory() for _ in range(2)]
+    n, P = len(wl.lengths), wl.pools.page_tokens
+    warm = max(args.warmup, 2)
+    max_cold = max(len(lay.cold) for lay in wl.layouts) + (warm + args.steps) // P + 2
+    batch = PagedLatentBatch(wl.n_heads, max_seqs=n, q_len=1, page_tokens=P, recent_tokens=2048 - P,
+                             max_cold_pages=max_cold, device=dev)
+    for lay in wl.layouts:  # slot s = shard position s: the step's row s
+        batch.add_layout(wl.pools, lay.cold, lay.hot)
+    inputs = (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)
+    host_in = [t.cpu().pin_memory() for t in inputs]
+    dev_in = [[torch.empty_like(t) for t in inputs] for _ in range(2)]
+    out_shape = (wl.total_q, wl.n_heads, 512)
+    dev_out = [torch.empty(out_shape, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+    host_out = [torch.empty(out_shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in host_in)
     d2h = host_out[0].numel() * host_out[0].element_size()
     copy_stream = torch.cuda.Stream(device=dev)
     in_ready = [torch.cuda.Event() for _ in range(2)]
     dec_done = [torch.cuda.Event() for _ in range(2)]
+    host_s = []
 
     def copy_in(b):
         with torch.cuda.stream(copy_stream):
-            copy_stream.wait_event(dec_done[b])  # the decode that last read buffer b is done
+            copy_stream.wait_event(dec_done[b])  # the step that last read buffer b is done
             for d, h in zip(dev_in[b], host_in):
                 d.copy_(h, non_blocking=True)
             in_ready[b].record(copy_stream)
@@ -606,7 +628,9 @@ def e2e_measure(wl, dplan, out, dev, stream, args, barrier, max_over_ranks) -> d
             stream.wait_event(in_ready[b])
             if k + 1 < n_steps:
                 copy_in(1 - b)
-            latent_decode(wl.pools, dplan, *dev_in[b], softmax_scale=SOFTMAX_SCALE, out=dev_out[b])
+            t0 = time.perf_counter()
+            batch.step(*dev_in[b], dev_out[b], softmax_scale=SOFTMAX_SCALE)
+            host_s.append(time.perf_counter() - t0)
             dec_done[b].record(stream)
             with torch.cuda.stream(copy_stream):
                 copy_stream.wait_event(dec_done[b])
@@ -614,16 +638,30 @@ def e2e_measure(wl, dplan, out, dev, stream, args, barrier, max_over_ranks) -> d
         if end_ev is not None:
             end_ev.record(copy_stream)
 
-    run(max(args.warmup, 2))
+    run(warm)
     torch.cuda.synchronize()
+    batch.raise_if_failed()
     barrier()
+    host_s.clear()
+    flushes0, flush_launches0 = batch.flushes, batch.flush_launches
     e_s, e_e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     run(args.steps, e_s, e_e)
     torch.cuda.synchronize()
+    batch.raise_if_failed()
     barrier()
     e2e_ms = max_over_ranks(e_s.elapsed_time(e_e)) / args.steps
-    return {"value": C3_SEQS / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": e2e_ms, "per_rank": "h2d/d2h bytes are rank 0's"}
+    counts = batch.planner.host_counts()
+    host_ms = statistics.mean(host_s) * 1e3
+    res = {"value": C3_SEQS / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "ms_per_step": e2e_ms, "api": "asterq.batch.PagedLatentBatch.step",
+           "per_step": "H2D of queries and new tokens, plan on the GPU, decode, append (cache grows one token per "
+                       "sequence), flushes as they fall due, D2H of the context latents",
+           "host_ms_per_step": host_ms, "host_frac_of_step": host_ms / e2e_ms,
+           "flushes_timed": batch.flushes - flushes0, "flush_launches_timed": batch.flush_launches - flush_launches0,
+           "launches_per_step": 4 + (1 if counts["n_separate"] else 0),
+           "per_rank": "h2d/d2h bytes are rank 0's"}
+    del batch
+    return res
 
 
 def multi_gpu_extras(dev, rank, world, args, max_over_ranks, barrier) -> dict:
@@ -703,6 +741,14 @@ def context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier) -> d
         return max_over_ranks(s.elapsed_time(e) / iters)
 
     ms_eager = timed(step)
+    # the phases on their own (eager): decode + rank-local merge, the all-gather, the combine
+    import torch.distributed as dist
+
+    rec = dec.partial(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SOFTMAX_SCALE)
+    ms_partial = timed(lambda: dec.partial(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope,
+                                           softmax_scale=SOFTMAX_SCALE))
+    ms_gather = timed(lambda: dist.all_gather_into_tensor(dec.gathered, rec))
+    ms_finish = timed(lambda: dec.finish(dec.gathered, out))
     # the same step as one CUDA graph per rank (decode, merge, NCCL all-gather, combine)
     graph = dec.capture(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SOFTMAX_SCALE)
     ms = timed(graph.replay)
@@ -710,6 +756,8 @@ def context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier) -> d
     del graph  # released before the process group is destroyed
     alg = wl.algorithmic_bytes()
     return {"seqs": 1, "cached_tokens": int(wl.lengths[0]), "ranks": world, "ms": ms, "ms_eager": ms_eager,
+            "phases_ms_eager": {"decode_and_merge": ms_partial, "all_gather": ms_gather, "combine": ms_finish,
+                                "rank0_pieces": int(dec.plan.n_slots)},
             "seq_steps_per_s": 1e3 / ms, "GB/s_total": alg / (ms / 1e3) / 1e9,
             "launch": "CUDA graph replay per step (ms_eager: the same step launched from Python)",
             "collective": "one all_gather_into_tensor of 32,896 B per rank per step (NCCL)"}
