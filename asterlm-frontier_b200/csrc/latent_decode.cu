@@ -44,6 +44,7 @@
 // Every wait is bounded; a timeout sets a status flag instead of hanging.
 #include <atomic>
 #include <mutex>
+#include <string.h>
 #include <cuda.h>
 
 #include "common.cuh"
@@ -1346,6 +1347,133 @@ __global__ void __launch_bounds__(kCombThreads) merge_kernel(const float* __rest
 }
 
 // ---------------------------------------------------------------------------
+// Context-parallel record exchange by peer stores (no collective library)
+// ---------------------------------------------------------------------------
+// Every rank owns one mailbox in its own device memory, which the other ranks map through
+// CUDA IPC.  Layout: a 256-byte header (step counter, CTAs done, one flag per source rank),
+// then the records, [2 step parities][world source ranks][n_blocks merged records], each
+// rank's part laid out as merge_kernel writes it (o [n][16][512], m [n][16], l [n][16]).
+// A step is merge_push_kernel then combine_wait_kernel on each rank's stream:
+//  * merge_push merges the rank's split-KV pieces into one record per 16-row block and stores
+//    it into slot `rank` of every rank's mailbox (its own and, over NVLink, its peers'); the
+//    last of its CTAs then raises flag `rank` in every mailbox to the step number (a release
+//    store at system scope after system-scope fences of every CTA's stores);
+//  * combine_wait reads the step number, waits (bounded) until every rank's flag in its own
+//    mailbox has reached it, and combines the records of all ranks from its own memory.
+// Steps alternate between two record parities, so a rank that runs one step ahead writes the
+// other parity; it cannot run two steps ahead, because its own combine waits for every rank's
+// push of the step in between, which each rank issues only after its previous combine.
+constexpr int kMailHeaderBytes = 256;
+constexpr int kMailMaxWorld = 56;
+struct MailHeader {
+  unsigned counter;  // steps completed (written by the last CTA of merge_push)
+  unsigned done;     // CTAs of the current merge_push that finished their stores
+  unsigned pad[6];
+  unsigned flags[kMailMaxWorld];  // flag r: the last step whose records rank r has stored here
+};
+static_assert(sizeof(MailHeader) <= kMailHeaderBytes, "mailbox header");
+
+__host__ __device__ inline int64_t mail_rank_floats(int n_blocks, int latent_dim) {
+  return (int64_t)n_blocks * kRows * (latent_dim + 2);
+}
+
+ASTERQ_DEVICE unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+ASTERQ_DEVICE void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(kCombThreads) merge_push_kernel(const float* __restrict__ wo,
+                                                         const float* __restrict__ wm,
+                                                         const float* __restrict__ wl,
+                                                         const int32_t* __restrict__ jobs, int n_slots, int n_jobs,
+                                                         int latent_dim, void* const* __restrict__ mailboxes,
+                                                         int world, int rank) {
+  MailHeader* own = reinterpret_cast<MailHeader*>(mailboxes[rank]);
+  // every CTA reads the counter before the last CTA of this launch advances it
+  const unsigned step = *reinterpret_cast<volatile unsigned*>(&own->counter) + 1u;
+  const int64_t part = mail_rank_floats(n_jobs, latent_dim);
+  const int64_t rec_off = ((int64_t)(step & 1u) * world + rank) * part;  // floats past the header
+  float* mine = reinterpret_cast<float*>(reinterpret_cast<char*>(own) + kMailHeaderBytes) + rec_off;
+  combine_job<true>(wo, wm, wl, jobs, n_slots, n_jobs, latent_dim, mine, ASTERQ_DTYPE_F32,
+                    SlotLayout{(int64_t)kRows * latent_dim, kRows, 0, 0});
+  __syncthreads();  // this CTA's part of the record is in `mine`
+  // the same part, into every peer's mailbox: o rows (16 x 4 dims) and, for the first dim
+  // chunk, the rows' m and l
+  const int tid = threadIdx.x;
+  const int d = blockIdx.y * kCombDims;
+  int64_t off = -1;
+  if (tid < kRows && d < latent_dim) {
+    off = ((int64_t)blockIdx.x * kRows + tid) * latent_dim + d;
+  } else if (blockIdx.y == 0 && tid >= 32 && tid < 32 + 2 * kRows) {
+    const int k = tid - 32;  // m of row k, then l of row k - 16
+    off = (int64_t)n_jobs * kRows * latent_dim + (k >= kRows ? (int64_t)n_jobs * kRows : 0) +
+          (int64_t)blockIdx.x * kRows + (k & (kRows - 1));
+  }
+  if (off >= 0) {
+    const bool vec = tid < kRows;
+    const float4 v4 = vec ? *reinterpret_cast<const float4*>(mine + off) : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float v1 = vec ? 0.0f : mine[off];
+    for (int r = 0; r < world; ++r) {
+      if (r == rank) continue;
+      float* dst = reinterpret_cast<float*>(reinterpret_cast<char*>(mailboxes[r]) + kMailHeaderBytes) + rec_off + off;
+      if (vec)
+        *reinterpret_cast<float4*>(dst) = v4;
+      else
+        *dst = v1;
+    }
+  }
+  __threadfence_system();  // this CTA's stores (local and remote) before its arrival below
+  __syncthreads();
+  if (tid == 0) {
+    const unsigned total = gridDim.x * gridDim.y;
+    if (atomicAdd(&own->done, 1u) == total - 1u) {
+      __threadfence_system();  // every CTA's stores (observed through `done`) before the flags
+      own->done = 0u;
+      for (int r = 0; r < world; ++r) st_release_sys(&reinterpret_cast<MailHeader*>(mailboxes[r])->flags[rank], step);
+      own->counter = step;
+    }
+  }
+}
+
+__global__ void __launch_bounds__(kCombThreads) combine_wait_kernel(const void* __restrict__ mailbox, int world,
+                                                           int n_jobs, const int32_t* __restrict__ jobs,
+                                                           int latent_dim, void* __restrict__ out, int out_dtype,
+                                                           long long limit, int32_t* __restrict__ status) {
+  const MailHeader* h = reinterpret_cast<const MailHeader*>(mailbox);
+  // the step merge_push (earlier on this stream) has just completed
+  const unsigned step = *reinterpret_cast<const volatile unsigned*>(&h->counter);
+  __shared__ int ready;
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const long long t0 = clock64();
+    for (int r = 0; r < world && ok; ++r) {
+      while ((int)(ld_acquire_sys(&h->flags[r]) - step) < 0) {
+        if (clock64() - t0 > limit) {
+          ok = 0;
+          break;
+        }
+        __nanosleep(256);
+      }
+    }
+    ready = ok;
+    if (!ok && status != nullptr) atomicExch(status, 1);
+  }
+  __syncthreads();
+  if (!ready) return;  // a rank's records never arrived: the output is left unwritten
+  const int64_t part = mail_rank_floats(n_jobs, latent_dim);
+  const float* base = reinterpret_cast<const float*>(reinterpret_cast<const char*>(mailbox) + kMailHeaderBytes) +
+                      (int64_t)(step & 1u) * world * part;
+  const float* wm = base + (int64_t)n_jobs * kRows * latent_dim;
+  const float* wl = wm + (int64_t)n_jobs * kRows;
+  combine_job<false>(base, wm, wl, jobs, world, 0, latent_dim, out, out_dtype,
+                     SlotLayout{part, part, (int64_t)kRows * latent_dim, kRows});
+}
+
+// ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 int validate(const asterq_decode_params* p) {
@@ -1597,6 +1725,97 @@ extern "C" int asterq_splitkv_combine_ranks(const float* gathered, int32_t world
       gathered, wm, wl, jobs, world, latent_dim, out, out_dtype,
       dec::SlotLayout{part, part, (int64_t)dec::kRows * latent_dim, dec::kRows}, nullptr);
   return check_launch("splitkv_combine_ranks");
+}
+
+extern "C" int64_t asterq_mailbox_bytes(int32_t world, int32_t n_blocks, int32_t latent_dim) {
+  if (world < 1 || world > dec::kMailMaxWorld || n_blocks < 1 || latent_dim != dec::kL) return 0;
+  return dec::kMailHeaderBytes + 2LL * world * dec::mail_rank_floats(n_blocks, latent_dim) * 4;
+}
+
+extern "C" int asterq_mailbox_create(int64_t bytes, void** dev_ptr, void* ipc_handle) {
+  clear_error();
+  if (bytes <= dec::kMailHeaderBytes || !dev_ptr || !ipc_handle)
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "mailbox_create: bad arguments");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, (size_t)bytes);
+  if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "mailbox_create: cudaMalloc: %s", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, (size_t)bytes);  // counter, done count and flags start at 0
+  cudaIpcMemHandle_t h;
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, p);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return set_error(ASTERQ_ERR_CUDA, "mailbox_create: %s", cudaGetErrorString(e));
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == ASTERQ_IPC_HANDLE_BYTES, "IPC handle size");
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return ASTERQ_OK;
+}
+
+extern "C" int asterq_mailbox_open(const void* ipc_handle, void** peer_ptr) {
+  clear_error();
+  if (!ipc_handle || !peer_ptr) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "mailbox_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "mailbox_open: %s", cudaGetErrorString(e));
+  return ASTERQ_OK;
+}
+
+extern "C" int asterq_mailbox_close(void* peer_ptr) {
+  clear_error();
+  if (!peer_ptr) return ASTERQ_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(peer_ptr);
+  if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "mailbox_close: %s", cudaGetErrorString(e));
+  return ASTERQ_OK;
+}
+
+extern "C" int asterq_mailbox_destroy(void* dev_ptr) {
+  clear_error();
+  if (!dev_ptr) return ASTERQ_OK;
+  cudaError_t e = cudaFree(dev_ptr);
+  if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "mailbox_destroy: %s", cudaGetErrorString(e));
+  return ASTERQ_OK;
+}
+
+extern "C" int asterq_cp_merge_push(const float* partials, int32_t n_slots, const int32_t* jobs, int32_t n_blocks,
+                                    int32_t latent_dim, void* const* mailboxes, int32_t world, int32_t rank,
+                                    void* stream) {
+  clear_error();
+  if (latent_dim != dec::kL) return set_error(ASTERQ_ERR_UNSUPPORTED, "merge_push: latent_dim must be 512");
+  if (n_slots < 0 || n_blocks < 1 || world < 1 || world > dec::kMailMaxWorld || rank < 0 || rank >= world)
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "merge_push: bad sizes (world %d, rank %d, blocks %d)", world, rank,
+                     n_blocks);
+  if (!partials || !jobs || !mailboxes) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "merge_push: null pointer");
+  if ((reinterpret_cast<uintptr_t>(partials) | reinterpret_cast<uintptr_t>(jobs) |
+       reinterpret_cast<uintptr_t>(mailboxes)) & 15)
+    return set_error(ASTERQ_ERR_MISALIGNED, "merge_push: pointers must be 16-byte aligned");
+  const float* wm = partials + (int64_t)n_slots * dec::kRows * latent_dim;
+  const float* wl = wm + (int64_t)n_slots * dec::kRows;
+  dec::merge_push_kernel<<<dim3(n_blocks, dec::kL / dec::kCombDims), dec::kCombThreads, 0,
+                           reinterpret_cast<cudaStream_t>(stream)>>>(partials, wm, wl, jobs, n_slots, n_blocks,
+                                                                     latent_dim, mailboxes, world, rank);
+  return check_launch("cp_merge_push");
+}
+
+extern "C" int asterq_cp_combine_wait(const void* mailbox, int32_t world, int32_t n_blocks, const int32_t* jobs,
+                                      int32_t latent_dim, void* out, int32_t out_dtype, int64_t wait_limit_cycles,
+                                      int32_t* status, void* stream) {
+  clear_error();
+  if (latent_dim != dec::kL) return set_error(ASTERQ_ERR_UNSUPPORTED, "combine_wait: latent_dim must be 512");
+  if (world < 1 || world > dec::kMailMaxWorld || n_blocks < 1)
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "combine_wait: bad sizes");
+  if (!mailbox || !jobs || !out) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "combine_wait: null pointer");
+  if (out_dtype != ASTERQ_DTYPE_F32 && out_dtype != ASTERQ_DTYPE_BF16)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "combine_wait: out_dtype must be f32 or bf16");
+  if ((reinterpret_cast<uintptr_t>(mailbox) | reinterpret_cast<uintptr_t>(jobs) | reinterpret_cast<uintptr_t>(out)) & 15)
+    return set_error(ASTERQ_ERR_MISALIGNED, "combine_wait: pointers must be 16-byte aligned");
+  const long long limit = wait_limit_cycles > 0 ? wait_limit_cycles : kDefaultWaitLimit;
+  dec::combine_wait_kernel<<<dim3(n_blocks, dec::kL / dec::kCombDims), dec::kCombThreads, 0,
+                             reinterpret_cast<cudaStream_t>(stream)>>>(mailbox, world, n_blocks, jobs, latent_dim, out,
+                                                                       out_dtype, limit, status);
+  return check_launch("cp_combine_wait");
 }
 
 // ---------------------------------------------------------------------------

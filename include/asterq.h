@@ -13,6 +13,9 @@
  *                          iterating the cache like cache.py:139-159 iter_chunks
  *   asterq_splitkv_combine layers/latent_attention.py:212-220 (the online-softmax merge rule)
  *   asterq_splitkv_merge   the same rule, leaving merged (m, l, o) records for a later combine
+ *   asterq_cp_merge_push / asterq_cp_combine_wait  the same rule across ranks, records exchanged
+ *                          by peer stores into CUDA IPC mailboxes (no counterpart: the
+ *                          reference is single-device)
  *   asterq_splitkv_combine_ranks  the same rule over the merged records of all ranks, read where
  *                          a rank-major all-gather left them
  *
@@ -311,6 +314,42 @@ int asterq_splitkv_merge(const float* partials, int32_t n_slots, const int32_t* 
  */
 int asterq_splitkv_combine_ranks(const float* gathered, int32_t world, int32_t n_blocks, const int32_t* jobs,
                                  int32_t latent_dim, void* out, int32_t out_dtype, void* stream);
+
+/*
+ * Context-parallel record exchange by peer stores, in place of the all-gather above (the
+ * reference has no multi-GPU code; this replaces the collective that
+ * asterq_splitkv_merge + all_gather + asterq_splitkv_combine_ranks need, with the same
+ * merge rule, latent_attention.py:212-220, across ranks).
+ *
+ * Every rank creates one mailbox (device memory of asterq_mailbox_bytes bytes, zeroed) and
+ * gets a CUDA IPC handle for it; the ranks exchange handles on the host, and each maps its
+ * peers' mailboxes with asterq_mailbox_open.  A step on each rank, on one stream:
+ *   asterq_latent_decode  (split-KV partial records in the workspace, n_combine = 0)
+ *   asterq_cp_merge_push  merges them into one record per 16-row block (jobs as for
+ *                         asterq_splitkv_merge) and stores it into slot `rank` of every rank's
+ *                         mailbox (mailboxes: a device array of `world` pointers, this rank's
+ *                         own mailbox at index `rank`, the mapped peers' at theirs), then raises
+ *                         this rank's flag in every mailbox to the step number;
+ *   asterq_cp_combine_wait waits until every rank's flag in this rank's mailbox has reached the
+ *                         step (bounded by wait_limit_cycles SM cycles, 0: about 2 s; on timeout
+ *                         *status = 1 and `out` is left unwritten), then combines all ranks'
+ *                         records as asterq_splitkv_combine_ranks does (jobs likewise).
+ * Steps alternate between two record buffers; every rank must run the same steps.  No TMA or
+ * library kernel reads a peer's memory: records cross NVLink as plain stores.  Close the peer
+ * mappings and destroy the mailboxes only after every rank has finished its last step.
+ * world <= 56.
+ */
+#define ASTERQ_IPC_HANDLE_BYTES 64
+int64_t asterq_mailbox_bytes(int32_t world, int32_t n_blocks, int32_t latent_dim);
+int asterq_mailbox_create(int64_t bytes, void** dev_ptr, void* ipc_handle /* ASTERQ_IPC_HANDLE_BYTES out */);
+int asterq_mailbox_open(const void* ipc_handle, void** peer_ptr);
+int asterq_mailbox_close(void* peer_ptr);
+int asterq_mailbox_destroy(void* dev_ptr);
+int asterq_cp_merge_push(const float* partials, int32_t n_slots, const int32_t* jobs, int32_t n_blocks,
+                         int32_t latent_dim, void* const* mailboxes, int32_t world, int32_t rank, void* stream);
+int asterq_cp_combine_wait(const void* mailbox, int32_t world, int32_t n_blocks, const int32_t* jobs,
+                           int32_t latent_dim, void* out, int32_t out_dtype, int64_t wait_limit_cycles,
+                           int32_t* status, void* stream);
 
 #ifdef __cplusplus
 }
