@@ -67,8 +67,23 @@ class BatchTables:
             "q_len": np.zeros(n_seqs, np.int32),
             "q_start": np.zeros(n_seqs, np.int32),
         }
-        self.dev = {k: torch.from_numpy(v.copy()).to(self.device) for k, v in self.host.items()}
         self.generation = 0  # bumped whenever a device array is reallocated (bound pointers change)
+        self._build_device()
+        self.upload()
+
+    def _build_device(self) -> None:
+        """All arrays as views of one device buffer, so an upload is one copy, staged through two
+        pinned buffers used in turn (a staging buffer is refilled only after its last copy has run)."""
+        offs, total = {}, 0
+        for name, a in self.host.items():
+            offs[name] = total
+            total += (a.size + 3) // 4 * 4  # each array 16-byte aligned
+        self._offs, self._total = offs, total
+        self._flat = torch.zeros(total, dtype=torch.int32, device=self.device)
+        self.dev = {k: self._flat[o : o + self.host[k].size].view(self.host[k].shape) for k, o in offs.items()}
+        self._stage = [torch.zeros(total, dtype=torch.int32).pin_memory() for _ in range(2)]
+        self._stage_done: list = [None, None]
+        self._stage_next = 0
 
     @property
     def max_cold_pages(self) -> int:
@@ -81,18 +96,43 @@ class BatchTables:
     def grow(self, max_cold_pages: int | None = None, max_hot_pages: int | None = None) -> None:
         """Widen the page tables (reallocates the device arrays)."""
         h = self.host
+        grown = False
         for name, want, fill in (("cold_pages", max_cold_pages, 0), ("cold_tokens", max_cold_pages, 0),
                                  ("hot_pages", max_hot_pages, -1)):
             if want is not None and want > h[name].shape[1]:
                 wide = np.full((self.n_seqs, want), fill, np.int32)
                 wide[:, : h[name].shape[1]] = h[name]
                 h[name] = wide
-                self.dev[name] = torch.from_numpy(wide.copy()).to(self.device)
-                self.generation += 1
+                grown = True
+        if grown:
+            self._build_device()
+            self.upload()
+            self.generation += 1
+
+    def shadow(self) -> "BatchTables":
+        """A second set of device arrays over the same host mirror (``upload`` fills it): what a
+        planner reads while the primary arrays are being changed by the step in flight."""
+        t = BatchTables.__new__(BatchTables)
+        t.device, t.n_seqs, t.host = self.device, self.n_seqs, self.host
+        t.generation = 0
+        t._build_device()
+        return t
 
     def upload(self, names=None) -> None:
-        for name in names or self.host:
-            self.dev[name].copy_(_pinned(self.host[name]), non_blocking=True)
+        """Copy the whole mirror to the device on the current stream (one copy; `names` is accepted
+        for compatibility and ignored)."""
+        j = self._stage_next
+        self._stage_next ^= 1
+        if self._stage_done[j] is not None:
+            self._stage_done[j].synchronize()
+        st = self._stage[j].numpy()
+        for name, a in self.host.items():
+            o = self._offs[name]
+            st[o : o + a.size] = a.reshape(-1)
+        self._flat.copy_(self._stage[j], non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record(torch.cuda.current_stream(self.device))
+        self._stage_done[j] = ev
 
     def desc(self, n_heads: int, page_tokens: int, n_workers: int) -> _lib.BatchDesc:
         d = _lib.BatchDesc()
@@ -289,7 +329,7 @@ class PagedLatentBatch:
     def __init__(self, n_heads: int, *, max_seqs: int, q_len: int = 1, page_tokens: int = 512,
                  recent_tokens: int = 512, cache_dtype: str = "hadamard_int4", max_cold_pages: int = 64,
                  hot_pool_pages: int | None = None, cold_pool_pages: int | None = None,
-                 n_workers: int | None = None, device="cuda") -> None:
+                 n_workers: int | None = None, plan_ahead: bool = False, device="cuda") -> None:
         if cache_dtype not in COLD_SCHEMES:
             raise NotImplementedError(f"cache_dtype {cache_dtype!r}: the pools serve {tuple(COLD_SCHEMES)}")
         if not 0 < q_len <= page_tokens:
@@ -310,7 +350,21 @@ class PagedLatentBatch:
         self.pools = LatentPools.empty(cold_pool_pages, hot_pool_pages, P, self.device)
         self.pools.cold_scheme = cache_dtype
         self._hot_free, self._cold_free = _PagePool(hot_pool_pages), _PagePool(cold_pool_pages)
+        # plan_ahead: the next step's schedule is built on a side stream while this step decodes,
+        # on the one SM the decode leaves free (one worker fewer), into the other of two planners
+        # whose tables are copies of the host mirror taken after this step's bookkeeping
+        self.plan_ahead = bool(plan_ahead)
+        if self.plan_ahead and n_workers is None:
+            n_workers = torch.cuda.get_device_properties(self.device).multi_processor_count - 1
         self.planner = DevicePlanner(self.tables, n_heads, P, max_q_len=q_len, n_workers=n_workers)
+        self._ahead: list[DevicePlanner] = []
+        self._ahead_gen = -1
+        self._ahead_ready: int | None = None  # planner index holding the next step's schedule
+        self._ahead_cur = 0
+        if self.plan_ahead:
+            self._plan_stream = torch.cuda.Stream(self.device)
+            self._planned = [torch.cuda.Event(), torch.cuda.Event()]
+            self._decoded = [torch.cuda.Event(), torch.cuda.Event()]
         self.append_status = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.flushes = 0  # pages encoded into the cold pool so far
         self.flush_launches = 0  # encode launches those flushes took (one per step that flushed)
@@ -373,6 +427,7 @@ class PagedLatentBatch:
         h["hot_tokens"][slot] = hot
         h["q_len"][slot] = self.q_len
         self.tables.upload()
+        self._invalidate_plan()
         return slot
 
     def add_layout(self, pools: LatentPools, cold: list[tuple[int, int, int]], hot: list[tuple[int, int, int]]) -> int:
@@ -412,6 +467,7 @@ class PagedLatentBatch:
         h["hot_tokens"][slot] = hot_len
         h["q_len"][slot] = self.q_len
         self.tables.upload()
+        self._invalidate_plan()
         return slot
 
     def remove_sequence(self, slot: int) -> None:
@@ -423,6 +479,7 @@ class PagedLatentBatch:
         h["hot_pages"][slot, :] = -1
         h["q_len"][slot] = 0
         self.tables.upload()
+        self._invalidate_plan()
 
     # ------------------------------------------------------------------ pools
     def _write_rows(self, latent: torch.Tensor, rope: torch.Tensor, pages: list[int]) -> None:
@@ -448,15 +505,51 @@ class PagedLatentBatch:
         self.pools.cold_rope.index_copy_(0, di, rope.reshape(len(pages), P, ROPE_DIM))
 
     # ------------------------------------------------------------------ steps
+    def _ahead_planners(self) -> list[DevicePlanner]:
+        if self._ahead_gen != self.tables.generation:  # (re)bind to the tables as they are now
+            self._ahead = [DevicePlanner(self.tables.shadow(), self.n_heads, self.page_tokens, max_q_len=self.q_len,
+                                         n_workers=self.planner.n_workers) for _ in range(2)]
+            self._ahead_gen = self.tables.generation
+            self._ahead_ready = None
+        return self._ahead
+
+    def _plan_into(self, i: int) -> None:
+        """Side stream: copy the host mirror into planner i's tables and plan into its buffers, once
+        the decode that last read those buffers is done."""
+        pl = self._ahead_planners()[i]
+        side = self._plan_stream
+        side.wait_event(self._decoded[i])
+        with torch.cuda.stream(side):
+            pl.tables.upload()
+            pl.plan(side.cuda_stream)
+            self._planned[i].record(side)
+
+    def _invalidate_plan(self) -> None:
+        self._ahead_ready = None
+
     def enqueue_step(self, q_lat, q_rope, new_latent, new_rope, out, *, softmax_scale: float | None = None,
                      logit_softcap: float | None = None, wait_limit_cycles: int = 0) -> None:
-        """Enqueue plan + decode + append for every active slot (no host bookkeeping; see ``step``)."""
+        """Enqueue plan + decode + append for every active slot (no host bookkeeping; see ``step``).
+        With ``plan_ahead`` the schedule comes from the side stream (planned during the previous
+        step, or now if the batch changed since)."""
         if softmax_scale is None:
             softmax_scale = 1.0 / math.sqrt(LATENT_DIM + ROPE_DIM)
         stream = _lib.stream_handle(self.device)
-        self.planner.plan(stream)
-        self.planner.decode(self.pools, q_lat, q_rope, new_latent, new_rope, out, softmax_scale=softmax_scale,
-                            logit_softcap=logit_softcap, wait_limit_cycles=wait_limit_cycles, stream=stream)
+        if self.plan_ahead:
+            i = self._ahead_ready
+            if i is None:
+                i = self._ahead_cur
+                self._plan_into(i)
+            torch.cuda.current_stream(self.device).wait_event(self._planned[i])
+            planner = self._ahead_planners()[i]
+            planner.decode(self.pools, q_lat, q_rope, new_latent, new_rope, out, softmax_scale=softmax_scale,
+                           logit_softcap=logit_softcap, wait_limit_cycles=wait_limit_cycles, stream=stream)
+            self._decoded[i].record(torch.cuda.current_stream(self.device))
+            self._ahead_cur, self._ahead_ready = i, None
+        else:
+            self.planner.plan(stream)
+            self.planner.decode(self.pools, q_lat, q_rope, new_latent, new_rope, out, softmax_scale=softmax_scale,
+                                logit_softcap=logit_softcap, wait_limit_cycles=wait_limit_cycles, stream=stream)
         d = self.planner.desc
         _lib.check(_lib.load().asterq_batch_append(
             ctypes.byref(d), self.tables.dev["hot_tokens"].data_ptr(), new_latent.data_ptr(), new_rope.data_ptr(),
@@ -485,6 +578,10 @@ class PagedLatentBatch:
         self.enqueue_step(q_lat, q_rope, new_latent, new_rope, out, softmax_scale=softmax_scale,
                           logit_softcap=logit_softcap)
         self.advance()
+        if self.plan_ahead:  # the next step's schedule, built while this step decodes
+            nxt = self._ahead_cur ^ 1
+            self._plan_into(nxt)
+            self._ahead_ready = nxt
         return out
 
     def verify(self, q_lat, q_rope, new_latent, new_rope, out=None, *, softmax_scale: float | None = None,
@@ -507,6 +604,7 @@ class PagedLatentBatch:
         h = self.tables.host
         h["hot_tokens"][h["q_len"] > 0] += self.q_len
         self._provisional = True
+        self._invalidate_plan()
         return out
 
     def accept(self, keep) -> None:
@@ -525,6 +623,7 @@ class PagedLatentBatch:
         h["hot_tokens"][act] -= (self.q_len - keep[act]).astype(np.int32)
         self._provisional = False
         self._settle(force_upload=True)
+        self._invalidate_plan()
 
     def advance(self) -> None:
         """Host bookkeeping after a step's launches: advance the mirror's hot lengths, flush the
@@ -580,12 +679,21 @@ class PagedLatentBatch:
                 logit_softcap: float | None = None) -> "StepGraph":
         """Record plan + decode + append on these fixed buffers as a CUDA graph (refill the
         buffers in place between replays; ``StepGraph.replay`` also does the host bookkeeping)."""
+        if self.plan_ahead:
+            raise NotImplementedError("a captured step plans in-line: build the batch without plan_ahead")
         self._check_step_inputs(q_lat, q_rope, new_latent, new_rope, out)
         return StepGraph(self, (q_lat, q_rope, new_latent, new_rope, out), softmax_scale, logit_softcap)
+
+    @property
+    def last_planner(self) -> DevicePlanner:
+        """The planner whose schedule the latest step decoded."""
+        return self._ahead[self._ahead_cur] if (self.plan_ahead and self._ahead) else self.planner
 
     def raise_if_failed(self) -> None:
         """Synchronize; raise if the planner, a decode wait or an append failed."""
         self.planner.raise_if_failed()
+        for pl in self._ahead:
+            pl.raise_if_failed()
         if int(self.append_status.item()) != 0:
             self.append_status.zero_()
             raise RuntimeError("asterq batch_append: a sequence's hot page was missing")

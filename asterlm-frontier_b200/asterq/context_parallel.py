@@ -16,6 +16,13 @@ window and the step's new tokens, so it takes fewer chunks).  Each rank:
 
 ``capture`` records the four steps as one CUDA graph per rank.
 
+With a ``PeerExchange`` (``use_peer_exchange``), steps 2-4 become two kernels and no
+collective: ``asterq_cp_merge_push`` merges the rank's records and stores the merged record
+into every rank's mailbox (device memory mapped between the rank processes through CUDA IPC,
+written with plain stores over NVLink), then raises the rank's flag in each; and
+``asterq_cp_combine_wait`` waits (bounded) for every rank's flag and combines the records from
+local memory.
+
 The merge rule is the reference's online softmax (latent_attention.py:212-220)
 applied across ranks instead of across chunks.  No TMA or library kernel reads
 another GPU's memory: the records arrive by NCCL into local buffers.
@@ -68,6 +75,70 @@ def rank_layout(layout: SequenceLayout, rank: int, world: int) -> SequenceLayout
     return replace(layout, cold=list(layout.cold[a:b]), hot=list(layout.hot) if last else [], attend_new=last)
 
 
+class PeerExchange:
+    """Mailboxes for exchanging merged records between the ranks of one process group.
+
+    Every rank allocates one mailbox in its own device memory (``asterq_mailbox_create``),
+    the ranks swap CUDA IPC handles over the group (``all_gather_object``), and each maps its
+    peers' mailboxes.  ``close`` must run on every rank after all ranks have finished their
+    last step (a barrier first), or a peer could still be writing into a freed mailbox.
+    """
+
+    def __init__(self, n_blocks: int, rank: int, world: int, device, *, group=None,
+                 wait_limit_cycles: int = 0) -> None:
+        import torch.distributed as dist
+
+        lib = _lib.load()
+        self.rank, self.world, self.n_blocks = rank, world, n_blocks
+        self.device = torch.device(device)
+        self.group = group
+        self.wait_limit_cycles = int(wait_limit_cycles)
+        nbytes = lib.asterq_mailbox_bytes(world, n_blocks, LATENT_DIM)
+        if nbytes <= 0:
+            raise ValueError(f"no mailbox for world {world}, {n_blocks} blocks")
+        own = ctypes.c_void_p()
+        handle = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+        with torch.cuda.device(self.device):
+            _lib.check(lib.asterq_mailbox_create(nbytes, ctypes.byref(own), handle))
+        self.own = own.value
+        handles: list = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peers: list[int] = []
+        ptrs = []
+        with torch.cuda.device(self.device):
+            for r, h in enumerate(handles):
+                if r == rank:
+                    ptrs.append(self.own)
+                    continue
+                buf = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES).from_buffer_copy(h)
+                peer = ctypes.c_void_p()
+                _lib.check(lib.asterq_mailbox_open(buf, ctypes.byref(peer)))
+                self.peers.append(peer.value)
+                ptrs.append(peer.value)
+        self.table = torch.tensor(ptrs, dtype=torch.int64, device=self.device)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+
+    def raise_if_failed(self) -> None:
+        """Synchronize; raise if a combine gave up waiting for a rank's records."""
+        if int(self.status.item()) != 0:
+            self.status.zero_()
+            raise RuntimeError("asterq context parallel: a rank's records did not arrive in time")
+
+    def close(self) -> None:
+        import torch.distributed as dist
+
+        if self.own is None:
+            return
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # no rank writes into a mailbox any more
+        lib = _lib.load()
+        with torch.cuda.device(self.device):
+            for peer in self.peers:
+                _lib.check(lib.asterq_mailbox_close(peer))
+            _lib.check(lib.asterq_mailbox_destroy(self.own))
+        self.peers, self.own = [], None
+
+
 class ContextParallelDecoder:
     """One rank's share of a context-parallel decode step for one sequence (B = 1)."""
 
@@ -85,25 +156,56 @@ class ContextParallelDecoder:
         # job rb merges record rb of every rank (asterq_splitkv_combine_ranks)
         jobs = [(0, world, int(self.plan.combine[rb, 2]), int(self.plan.combine[rb, 3])) for rb in range(self.n_rb)]
         self.final_jobs = torch.tensor(jobs, dtype=torch.int32, device=self.device).reshape(-1, 4)
+        self.exchange: PeerExchange | None = None
         # the decode's own output rows stay unwritten (every item writes partial records)
         self._unused_out = torch.empty(layout.q_len, n_heads, LATENT_DIM, dtype=torch.float32, device=self.device)
 
     def partial(self, q_lat, q_rope, new_latent, new_rope, *, softmax_scale: float,
                 logit_softcap: float | None = None) -> torch.Tensor:
         """Steps 1-2: this rank's merged (m, l, o) records, [n_rb * 16 * 514] fp32."""
+        stream = self._decode_records(q_lat, q_rope, new_latent, new_rope, softmax_scale=softmax_scale,
+                                      logit_softcap=logit_softcap)
+        lib = _lib.load()
+        _lib.check(lib.asterq_splitkv_merge(self.dplan.workspace.data_ptr(), self.plan.n_slots,
+                                            self.dplan.combine.data_ptr(), self.n_rb, LATENT_DIM,
+                                            self.merged.data_ptr(), stream))
+        return self.merged
+
+    def _decode_records(self, q_lat, q_rope, new_latent, new_rope, *, softmax_scale: float,
+                        logit_softcap: float | None = None) -> int:
+        """Step 1: this rank's split-KV partial records into the workspace; returns the stream."""
         out = self._unused_out
         if out.shape[0] != q_lat.shape[0]:
             out = torch.empty(q_lat.shape[0], self.n_heads, LATENT_DIM, dtype=torch.float32, device=self.device)
         p = make_params(self.pools, self.dplan, q_lat, q_rope, new_latent, new_rope, out, n_heads=self.n_heads,
                         softmax_scale=softmax_scale, logit_softcap=logit_softcap)
-        p.n_combine = 0  # the records are merged below, not combined
-        lib = _lib.load()
+        p.n_combine = 0  # the records are merged later, not combined
         stream = _lib.stream_handle(self.device)
-        _lib.check(lib.asterq_latent_decode(ctypes.byref(p), stream))
-        _lib.check(lib.asterq_splitkv_merge(self.dplan.workspace.data_ptr(), self.plan.n_slots,
+        _lib.check(_lib.load().asterq_latent_decode(ctypes.byref(p), stream))
+        return stream
+
+    def use_peer_exchange(self, group=None, *, wait_limit_cycles: int = 0) -> "PeerExchange":
+        """Set up mailboxes with the other ranks of `group` (collective: every rank calls it);
+        ``step`` then exchanges records by peer stores instead of ``all_gather``."""
+        self.exchange = PeerExchange(self.n_rb, self.rank, self.world, self.device, group=group,
+                                     wait_limit_cycles=wait_limit_cycles)
+        return self.exchange
+
+    def step_peer(self, q_lat, q_rope, new_latent, new_rope, out, *, softmax_scale: float,
+                  logit_softcap: float | None = None) -> torch.Tensor:
+        """Steps 1-4 with the peer exchange: decode, merge + push to every rank, wait + combine."""
+        ex = self.exchange
+        stream = self._decode_records(q_lat, q_rope, new_latent, new_rope, softmax_scale=softmax_scale,
+                                      logit_softcap=logit_softcap)
+        lib = _lib.load()
+        _lib.check(lib.asterq_cp_merge_push(self.dplan.workspace.data_ptr(), self.plan.n_slots,
                                             self.dplan.combine.data_ptr(), self.n_rb, LATENT_DIM,
-                                            self.merged.data_ptr(), stream))
-        return self.merged
+                                            ex.table.data_ptr(), self.world, self.rank, stream))
+        dtype = _lib.DTYPE_F32 if out.dtype == torch.float32 else _lib.DTYPE_BF16
+        _lib.check(lib.asterq_cp_combine_wait(ex.own, self.world, self.n_rb, self.final_jobs.data_ptr(), LATENT_DIM,
+                                              out.data_ptr(), dtype, ex.wait_limit_cycles, ex.status.data_ptr(),
+                                              stream))
+        return out
 
     def finish(self, gathered: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """Step 4: combine the records of all ranks (rank-major as all_gather leaves them) into `out`.
@@ -138,4 +240,13 @@ class ContextParallelDecoder:
         """
         return capture_step(lambda: self.step(q_lat, q_rope, new_latent, new_rope, out, group=group,
                                               softmax_scale=softmax_scale, logit_softcap=logit_softcap),
+                            self.device)
+
+    def capture_peer(self, q_lat, q_rope, new_latent, new_rope, out, *, softmax_scale: float,
+                     logit_softcap: float | None = None) -> torch.cuda.CUDAGraph:
+        """``step_peer`` recorded as one CUDA graph (decode, merge-push, combine-wait); every rank
+        replays its graph once per step, in the same order.  The step number lives in the
+        mailbox, so replays need no host bookkeeping."""
+        return capture_step(lambda: self.step_peer(q_lat, q_rope, new_latent, new_rope, out,
+                                                   softmax_scale=softmax_scale, logit_softcap=logit_softcap),
                             self.device)

@@ -594,7 +594,7 @@ def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
     warm = max(args.warmup, 2)
     max_cold = max(len(lay.cold) for lay in wl.layouts) + (warm + args.steps) // P + 2
     batch = PagedLatentBatch(wl.n_heads, max_seqs=n, q_len=1, page_tokens=P, recent_tokens=2048 - P,
-                             max_cold_pages=max_cold, device=dev)
+                             max_cold_pages=max_cold, plan_ahead=True, device=dev)
     for lay in wl.layouts:  # slot s = shard position s: the step's row s
         batch.add_layout(wl.pools, lay.cold, lay.hot)
     inputs = (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)
@@ -650,12 +650,13 @@ def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
     batch.raise_if_failed()
     barrier()
     e2e_ms = max_over_ranks(e_s.elapsed_time(e_e)) / args.steps
-    counts = batch.planner.host_counts()
+    counts = batch.last_planner.host_counts()
     host_ms = statistics.mean(host_s) * 1e3
     res = {"value": C3_SEQS / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
            "ms_per_step": e2e_ms, "api": "asterq.batch.PagedLatentBatch.step",
            "per_step": "H2D of queries and new tokens, plan on the GPU, decode, append (cache grows one token per "
-                       "sequence), flushes as they fall due, D2H of the context latents",
+                       "sequence), flushes as they fall due, D2H of the context latents; each step's schedule is "
+                       "planned on a side stream while the step before it decodes (one SM left to the planner)",
            "host_ms_per_step": host_ms, "host_frac_of_step": host_ms / e2e_ms,
            "flushes_timed": batch.flushes - flushes0, "flush_launches_timed": batch.flush_launches - flush_launches0,
            "launches_per_step": 4 + (1 if counts["n_separate"] else 0),
@@ -754,13 +755,28 @@ def context_parallel_extra(dev, rank, world, args, max_over_ranks, barrier) -> d
     ms = timed(graph.replay)
     torch.cuda.synchronize()
     del graph  # released before the process group is destroyed
+    # the records exchanged by peer stores into CUDA IPC mailboxes (no collective in the step)
+    ex = dec.use_peer_exchange()
+    try:
+        ms_peer_eager = timed(lambda: dec.step_peer(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out,
+                                                    softmax_scale=SOFTMAX_SCALE))
+        graph = dec.capture_peer(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SOFTMAX_SCALE)
+        ms_peer = timed(graph.replay)
+        torch.cuda.synchronize()
+        del graph
+        ex.raise_if_failed()
+    finally:
+        ex.close()
     alg = wl.algorithmic_bytes()
     return {"seqs": 1, "cached_tokens": int(wl.lengths[0]), "ranks": world, "ms": ms, "ms_eager": ms_eager,
             "phases_ms_eager": {"decode_and_merge": ms_partial, "all_gather": ms_gather, "combine": ms_finish,
                                 "rank0_pieces": int(dec.plan.n_slots)},
             "seq_steps_per_s": 1e3 / ms, "GB/s_total": alg / (ms / 1e3) / 1e9,
             "launch": "CUDA graph replay per step (ms_eager: the same step launched from Python)",
-            "collective": "one all_gather_into_tensor of 32,896 B per rank per step (NCCL)"}
+            "collective": "one all_gather_into_tensor of 32,896 B per rank per step (NCCL)",
+            "peer_exchange": {"ms": ms_peer, "ms_eager": ms_peer_eager, "seq_steps_per_s": 1e3 / ms_peer,
+                              "exchange": "merged records stored into every rank's CUDA IPC mailbox over NVLink, "
+                                          "bounded wait on per-rank flags, combine from local memory"}}
 
 
 def timed_ms(fn, iters: int) -> float:

@@ -403,3 +403,46 @@ def test_mtp_verification_keeps_only_accepted_tokens(cuda):
             codes = torch.cat([batch.pools.cold_codes[p] for p in pages]).cpu().numpy()
             q = O.quantize(lat[:cold], "hadamard_int4", 64)
             np.testing.assert_array_equal(codes, q.data.reshape(cold, 256))
+
+
+def test_planning_ahead_gives_the_same_steps(cuda):
+    """With ``plan_ahead`` each step's schedule is built on a side stream while the step before it
+    decodes, from a copy of the page tables taken after that step's bookkeeping.  Against a batch
+    that plans in line with the same worker count (so the same schedule), every step's output is
+    bit-identical, through flushes, a sequence leaving and one joining (which replan in line)."""
+    from asterq.batch import PagedLatentBatch
+
+    sms = torch.cuda.get_device_properties(cuda).multi_processor_count
+    g0 = torch.Generator(device=cuda).manual_seed(33)
+    prompts = [(torch.randn(n, 512, generator=g0, device=cuda).bfloat16(),
+                torch.randn(n, 64, generator=g0, device=cuda).bfloat16()) for n in (60, 300, 1000, 2500)]
+
+    def make(ahead):
+        b = PagedLatentBatch(16, max_seqs=5, q_len=1, page_tokens=128, recent_tokens=64, max_cold_pages=40,
+                             n_workers=sms - 1, plan_ahead=ahead, device=cuda)
+        for lat, rope in prompts:
+            b.add_sequence(lat, rope)
+        return b
+
+    ahead, inline = make(True), make(False)
+    g = torch.Generator(device=cuda).manual_seed(34)
+    for step in range(150):  # every hot window passes recent + page tokens at least once
+        if step == 50:
+            for b in (ahead, inline):
+                b.remove_sequence(1)
+        if step == 90:
+            for b in (ahead, inline):
+                b.add_sequence(*prompts[2])
+        inputs = [torch.randn(5, 16, 512, generator=g, device=cuda).bfloat16(),
+                  torch.randn(5, 16, 64, generator=g, device=cuda).bfloat16(),
+                  torch.randn(5, 512, generator=g, device=cuda).bfloat16(),
+                  torch.randn(5, 64, generator=g, device=cuda).bfloat16()]
+        got = ahead.step(*inputs, torch.empty(5, 16, 512, device=cuda))
+        want = inline.step(*inputs, torch.empty(5, 16, 512, device=cuda))
+        for s in inline.active():
+            assert torch.equal(got[s], want[s]), f"step {step} slot {s}"
+    ahead.raise_if_failed()
+    inline.raise_if_failed()
+    assert ahead.flushes == inline.flushes > 0
+    for name in ("hot_tokens", "n_cold", "hot_pages", "cold_pages", "cold_tokens"):
+        assert torch.equal(ahead.tables.dev[name], inline.tables.dev[name]), name
