@@ -749,21 +749,27 @@ __global__ void __launch_bounds__(kThreads, 1)
               }
             }
           };
-          // S += scale_g x (256 hi + lo), the biased accumulators read as exact floats
+          // S += scale_g x (256 hi + lo + B), the biased accumulators read as exact floats
           // (packed f32x2 arithmetic: two accumulator elements per instruction; elements
-          // c = 0,1 belong to token row gid, c = 2,3 to row gid + 8)
+          // c = 0,1 belong to token row gid, c = 2,3 to row gid + 8).  The hi limb's bias B is
+          // subtracted exactly; the lo limb keeps its bias, so each token's S carries
+          // B x (sum of its group scales), subtracted once after the last group (|S| stays
+          // below ~2^27 x scale, so the extra rounding is ~2^-21 of the score).
+          float ssum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
           auto qk_finish = [&](int g, const int (&acc)[2][2][2][4]) {
             const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
 #pragma unroll
             for (int m = 0; m < 2; ++m) {
               const float s0 = __half2float(scl[8 * tok[m][0] + g]);
               const float s1 = __half2float(scl[8 * tok[m][1] + g]);
+              ssum[m][0] += s0;
+              ssum[m][1] += s1;
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                   const float2 fh = add2(make_float2(__int_as_float(acc[0][m][nt][2 * h]), __int_as_float(acc[0][m][nt][2 * h + 1])), bias2);
-                  const float2 fl = add2(make_float2(__int_as_float(acc[1][m][nt][2 * h]), __int_as_float(acc[1][m][nt][2 * h + 1])), bias2);
+                  const float2 fl = make_float2(__int_as_float(acc[1][m][nt][2 * h]), __int_as_float(acc[1][m][nt][2 * h + 1]));
                   const float sc = h ? s1 : s0;
                   const float2 r = fma2(fma2(fh, k256, fl), make_float2(sc, sc),
                                         make_float2(S[m][nt][2 * h], S[m][nt][2 * h + 1]));
@@ -783,6 +789,17 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (g + 2 < 8) qk_issue(g + 2, accA);
             qk_finish(g + 1, accB);
           }
+          // the lo limbs' bias: B x (sum of the token's group scales)
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const float corr = -kAccBiasF * ssum[m][h];
+                S[m][nt][2 * h] += corr;
+                S[m][nt][2 * h + 1] += corr;
+              }
         } else {
           // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
           // S[1] is a second partial accumulator (odd groups) folded in below
