@@ -329,7 +329,8 @@ class PagedLatentBatch:
     def __init__(self, n_heads: int, *, max_seqs: int, q_len: int = 1, page_tokens: int = 512,
                  recent_tokens: int = 512, cache_dtype: str = "hadamard_int4", max_cold_pages: int = 64,
                  hot_pool_pages: int | None = None, cold_pool_pages: int | None = None,
-                 n_workers: int | None = None, plan_ahead: bool = False, device="cuda") -> None:
+                 n_workers: int | None = None, plan_ahead: bool = False, window_size: int | None = None,
+                 sink_tokens: int = 0, device="cuda") -> None:
         if cache_dtype not in COLD_SCHEMES:
             raise NotImplementedError(f"cache_dtype {cache_dtype!r}: the pools serve {tuple(COLD_SCHEMES)}")
         if not 0 < q_len <= page_tokens:
@@ -338,6 +339,13 @@ class PagedLatentBatch:
         self.n_heads, self.q_len, self.page_tokens = n_heads, q_len, page_tokens
         self.recent_tokens, self.cache_dtype = recent_tokens, cache_dtype
         self.threshold = recent_tokens + page_tokens  # cache.py:170: flush while hot > recent + chunk
+        # sliding window with sink tokens (cache.py:203-221), trimmed by dropping whole cold pages
+        # (no re-quantization): once a sequence is longer than window (+ one page of slack when
+        # the window exceeds two pages), the cold pages between its sink and recent tokens go
+        if window_size is not None and window_size <= 0:
+            raise ValueError("window_size must be positive")
+        self.window_size, self.sink_tokens = window_size, int(sink_tokens)
+        self.pages_trimmed = 0
         P = page_tokens
         max_hot_pages = math.ceil((self.threshold + q_len) / P) + 1
         self.tables = BatchTables(max_seqs, max_cold_pages, max_hot_pages, self.device)
@@ -640,6 +648,8 @@ class PagedLatentBatch:
         if over.size:
             self._flush(over)
             changed = True
+        if self.window_size is not None and self._trim_windows():
+            changed = True
         need = (h["hot_tokens"] + self.q_len + P - 1) // P
         have = (h["hot_pages"] >= 0).sum(axis=1)
         short = np.nonzero(act & (need > have))[0]
@@ -649,6 +659,32 @@ class PagedLatentBatch:
             changed = True
         if changed:
             self.tables.upload()
+
+    def _trim_windows(self) -> bool:
+        """Drop the cold pages between each over-long sequence's sink and recent tokens."""
+        from .cache import trim_page_range
+
+        h, P, W = self.tables.host, self.page_tokens, self.window_size
+        slack = P if W > 2 * P else 0
+        trimmed = False
+        for s in np.nonzero(h["q_len"] > 0)[0]:
+            n = int(h["n_cold"][s])
+            if self.length(s) <= W + slack or n == 0:
+                continue
+            rng = trim_page_range(n, h["cold_tokens"][s, :n], int(h["hot_tokens"][s]), P, W, self.sink_tokens)
+            if rng is None:
+                continue
+            a, b = rng
+            self._cold_free.release(h["cold_pages"][s, a:b])
+            keep = n - (b - a)
+            for name in ("cold_pages", "cold_tokens"):
+                row = h[name][s]
+                row[a:keep] = row[b:n].copy()
+                row[keep:n] = 0
+            h["n_cold"][s] = keep
+            self.pages_trimmed += b - a
+            trimmed = True
+        return trimmed
 
     def _flush(self, seqs: np.ndarray) -> None:
         """cache.py:167-177 for the given slots: the oldest hot page (full) of each is encoded

@@ -80,6 +80,24 @@ class _Pool:
         return self.tensors[name]
 
 
+def trim_page_range(n_cold: int, cold_tokens, hot_tokens: int, page_tokens: int, window_size: int,
+                    sink_tokens: int) -> tuple[int, int] | None:
+    """The cold pages [a, b) a whole-page window trim drops, or None: pages [0, a) hold the first
+    min(sink, window) tokens (the sink), pages [b, n_cold) with the hot window hold at least the
+    last window - sink tokens (cache.py:210-219 keeps exactly these token ranges)."""
+    sink = min(sink_tokens, window_size)
+    recent = window_size - sink
+    a, held = 0, 0
+    while a < n_cold and held < sink:
+        held += int(cold_tokens[a])
+        a += 1
+    b, back = n_cold, hot_tokens
+    while b > a and back < recent:
+        b -= 1
+        back += int(cold_tokens[b])
+    return (a, b) if b > a else None
+
+
 @dataclass
 class LatentLayerCache:
     """Hot/cold latent cache for one global-attention layer (cache.py:52).
@@ -95,6 +113,11 @@ class LatentLayerCache:
     recent_tokens: int = 512
     chunk_tokens: int = 1024
     quantize_rope: bool = False
+    # window trimming (cache.py:203-221): "requantize" keeps exactly sink + recent tokens and
+    # re-encodes them, as the reference does (double quantization); "pages" drops whole cold
+    # pages between the sink and the recent tokens instead, with no re-quantization (up to a page
+    # more on each side is kept, and a window shorter than the hot window keeps the hot window)
+    trim_mode: str = "requantize"
     _batch: int = field(default=0, repr=False)
     _hot_len: int = field(default=0, repr=False)
     _hot_pages: list[list[int]] = field(default_factory=list, repr=False)
@@ -115,6 +138,8 @@ class LatentLayerCache:
             raise ValueError("chunk_tokens must be a positive multiple of 16 (one chunk per page)")
         if self.recent_tokens < 0:
             raise ValueError("recent_tokens must be non-negative")
+        if self.trim_mode not in ("requantize", "pages"):
+            raise ValueError("trim_mode must be 'requantize' or 'pages'")
 
     # ------------------------------------------------------------------ sizes
     @property
@@ -216,7 +241,24 @@ class LatentLayerCache:
         self._flush_cold_chunks()
         trim_slack = self.chunk_tokens if window_size is not None and window_size > 2 * self.chunk_tokens else 0
         if window_size is not None and self.length > window_size + trim_slack:
-            self._trim(window_size, sink_tokens, latent.dtype, latent.device)
+            if self.trim_mode == "pages":
+                self._trim_pages(window_size, sink_tokens)
+            else:
+                self._trim(window_size, sink_tokens, latent.dtype, latent.device)
+
+    def _trim_pages(self, window_size: int, sink_tokens: int) -> None:
+        """Keep the cold pages holding the first min(sink, window) tokens and the newest cold pages
+        that, with the hot window, hold the last window - sink tokens; release the pages between
+        (whole pages, codes untouched)."""
+        drop = trim_page_range(self.cold_chunks, [self.chunk_tokens] * self.cold_chunks, self._hot_len,
+                               self.chunk_tokens, window_size, sink_tokens)
+        if drop is None:
+            return
+        a, b = drop
+        for row in range(self._batch):
+            pages = self._cold_pages[row]
+            self._cold.release(pages[a:b])
+            self._cold_pages[row] = pages[:a] + pages[b:]
 
     def _write_hot(self, latent: torch.Tensor, rope_key: torch.Tensor) -> None:
         P, (bsz, t) = self.page_tokens, latent.shape[:2]

@@ -446,3 +446,83 @@ def test_planning_ahead_gives_the_same_steps(cuda):
     assert ahead.flushes == inline.flushes > 0
     for name in ("hot_tokens", "n_cold", "hot_pages", "cold_pages", "cold_tokens"):
         assert torch.equal(ahead.tables.dev[name], inline.tables.dev[name]), name
+
+
+def test_sliding_window_drops_whole_pages_and_decodes_the_kept_tokens(cuda):
+    """A batch with a window of 600 tokens and 10 sink tokens: once a sequence is longer than the
+    window plus a page of slack, the cold pages between its sink and its recent tokens are
+    released (no re-quantization).  Every kept cold page still holds the chunk of the history it
+    was flushed from, the kept chunks are the sink pages plus the newest ones, and each checked
+    step matches the oracle over exactly the kept tokens."""
+    from asterq.batch import PagedLatentBatch
+
+    P, recent, W, sink = 128, 64, 600, 10
+    batch = PagedLatentBatch(16, max_seqs=3, q_len=1, page_tokens=P, recent_tokens=recent, max_cold_pages=40,
+                             window_size=W, sink_tokens=sink, device=cuda)
+    g = torch.Generator(device=cuda).manual_seed(23)
+    hist = _History()
+    chunk_of = {}  # live cold page id -> index of the history chunk it holds
+    flushed = {}
+    for n in (100, 900, 2000):
+        lat = torch.randn(n, 512, generator=g, device=cuda)
+        lat[:, :5] *= 20.0
+        lat, rope = lat.bfloat16(), torch.randn(n, 64, generator=g, device=cuda).bfloat16()
+        s = batch.add_sequence(lat, rope)
+        hist.start(s, lat, rope)
+        h = batch.tables.host
+        flushed[s] = int(h["n_cold"][s])
+        for j in range(flushed[s]):
+            chunk_of[int(h["cold_pages"][s, j])] = j
+
+    def kept_tokens(s):
+        h = batch.tables.host
+        lat, rope = hist.tokens(s)
+        chunks = [chunk_of[int(p)] for p in h["cold_pages"][s, : h["n_cold"][s]]]
+        hot = int(h["hot_tokens"][s])
+        sel = np.concatenate([np.arange(c * P, (c + 1) * P) for c in chunks] + [np.arange(lat.shape[0] - hot, lat.shape[0])])
+        return lat[sel], rope[sel], chunks, hot
+
+    checked = 0
+    for step in range(160):
+        q_lat = torch.randn(3, 16, 512, generator=g, device=cuda).bfloat16()
+        q_rope = torch.randn(3, 16, 64, generator=g, device=cuda).bfloat16()
+        new_lat = torch.randn(3, 512, generator=g, device=cuda).bfloat16()
+        new_rope = torch.randn(3, 64, generator=g, device=cuda).bfloat16()
+        before = {s: kept_tokens(s) for s in batch.active()}
+        out = batch.step(q_lat, q_rope, new_lat, new_rope, torch.empty(3, 16, 512, device=cuda))
+        if step % 31 == 0 or step == 159:
+            got = out.cpu().numpy()
+            for s, (klat, krope, _, hot) in before.items():
+                lat = np.concatenate([klat, new_lat[s : s + 1].float().cpu().numpy()])
+                rope = np.concatenate([krope, new_rope[s : s + 1].float().cpu().numpy()])
+                want = O.decode_sequence(lat, rope, q_lat[s : s + 1].float().cpu().numpy(),
+                                         q_rope[s : s + 1].float().cpu().numpy(), klat.shape[0], hot, SCALE, chunk=P)
+                _close(got[s : s + 1], want, f"step {step} slot {s}")
+                checked += 1
+        for s in before:
+            hist.extend(s, new_lat[s : s + 1], new_rope[s : s + 1])
+        h = batch.tables.host
+        live_all = {int(p) for s in before for p in h["cold_pages"][s, : h["n_cold"][s]]}
+        for p in [p for p in chunk_of if p not in live_all]:  # released by a trim (ids are reused later)
+            del chunk_of[p]
+        for s in before:  # a page flushed this step holds the next chunk of the history
+            n_cold = int(h["n_cold"][s])
+            for p in [int(p) for p in h["cold_pages"][s, :n_cold]]:
+                if p not in chunk_of:
+                    chunk_of[p] = flushed[s]
+                    flushed[s] += 1
+    batch.raise_if_failed()
+    assert checked >= 15 and batch.pages_trimmed > 0
+    for s in batch.active():
+        _, _, chunks, hot = kept_tokens(s)
+        n_sink = -(-min(sink, W) // P)
+        assert chunks[:n_sink] == list(range(n_sink)), chunks
+        rest = chunks[n_sink:]
+        assert rest == list(range(flushed[s] - len(rest), flushed[s])), chunks  # the newest chunks
+        assert batch.length(s) <= W + P + 2 * P
+        # the kept pages hold their chunks' codes (flushed once, never re-quantized)
+        lat, _ = hist.tokens(s)
+        pages = [int(p) for p in batch.tables.host["cold_pages"][s, : len(chunks)]]
+        for p, c in zip(pages, chunks):
+            q = O.quantize(lat[c * P : (c + 1) * P], "hadamard_int4", 64)
+            np.testing.assert_array_equal(batch.pools.cold_codes[p].cpu().numpy(), q.data.reshape(P, 256))

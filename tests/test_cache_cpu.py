@@ -47,3 +47,23 @@ def test_aster_cache_builds_layers_from_its_settings():
     assert cache.num_bytes == 0
     cache.reset()
     assert not cache.latent
+
+
+def test_trim_page_range_keeps_sink_and_recent_pages():
+    """Whole-page window trim: pages holding the first min(sink, window) tokens and the newest
+    pages that, with the hot window, hold window - sink tokens survive; the rest go."""
+    from asterq.cache import trim_page_range
+
+    P = 256
+    # 10 full cold pages + 440 hot tokens, window 1500 with 4 sink tokens: page 0 holds the sink,
+    # the hot window plus the 5 newest pages hold >= 1496 tokens, pages 1-4 are dropped
+    assert trim_page_range(10, [P] * 10, 440, P, 1500, 4) == (1, 5)
+    # no sink: only the recent side is kept
+    assert trim_page_range(10, [P] * 10, 440, P, 1500, 0) == (0, 5)
+    # a sink longer than the window is clipped to the window (recent = 0)
+    assert trim_page_range(10, [P] * 10, 440, P, 700, 5000) == (3, 10)
+    # nothing between sink and recent pages: no trim
+    assert trim_page_range(3, [P] * 3, 440, P, 1500, 4) is None
+    # partial cold pages count their own tokens
+    assert trim_page_range(5, [100, 256, 256, 256, 30], 10, P, 300, 150) == (2, 3)
+    assert trim_page_range(4, [100, 256, 256, 30], 10, P, 300, 150) is None

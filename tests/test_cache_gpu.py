@@ -224,3 +224,36 @@ def test_float32_caller_keeps_float32_and_codes_come_from_it(cuda):
     want = O.decode(bf(q_lat.numpy()), bf(q_rope.numpy()), bf(lat_np[n:]), bf(rope_np[n:]), view, SCALE)
     got = out[0].cpu().numpy()
     assert O.rel_l2(got, want) <= 1e-3 and O.max_abs(got, want) <= 2e-2
+
+
+def test_window_trim_by_pages_keeps_codes_and_matches_the_oracle(cuda):
+    """trim_mode="pages": the cold pages between the sink and the recent tokens are released
+    whole; the kept pages' codes are the ones written at flush time (no re-quantization), and
+    decoding over the trimmed cache equals the oracle over exactly the kept tokens."""
+    from asterq.attention import latent_attention
+    from asterq.cache import LatentLayerCache
+
+    P, n = 256, 3000
+    inp = _inputs(14, n)
+    lat, rope = inp["latent"][:n], inp["rope"][:n]
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=256, chunk_tokens=P, trim_mode="pages")
+    cache.append(lat[None].to(cuda), rope[None].to(cuda), 1500, 4)
+    # 10 cold pages + 440 hot; page 0 holds the sink, pages 5-9 and the hot window the recent tokens
+    assert cache.cold_chunks == 6 and cache.hot_length == 440 and cache.length == 6 * P + 440
+    full = O.build_cache_from_tokens(_bf16_np(lat), _bf16_np(rope), 256, P)
+    kept = [full.cold[0]] + full.cold[5:]
+    for q, c in zip(cache.cold_latent, kept):
+        np.testing.assert_array_equal(q.data[0].cpu().numpy(), c.codes)
+        np.testing.assert_array_equal(q.scale[0, :, :, 0].cpu().numpy(), c.scales)
+    import dataclasses
+
+    view = dataclasses.replace(full, cold=kept)
+    out = latent_attention(inp["q_lat"][None].to(cuda), inp["q_rope"][None].to(cuda), inp["latent"][None, n:].to(cuda),
+                           inp["rope"][None, n:].to(cuda), cache, softmax_scale=SCALE)
+    want = O.decode(_bf16_np(inp["q_lat"]), _bf16_np(inp["q_rope"]), _bf16_np(inp["latent"][n:]),
+                    _bf16_np(inp["rope"][n:]), view, SCALE)
+    got = out[0].cpu().numpy()
+    assert O.rel_l2(got, want) <= 1e-3 and O.max_abs(got, want) <= 2e-2
+    # a second append re-checks the window: nothing left between sink and recent pages
+    cache.append(lat[None, :8].to(cuda), rope[None, :8].to(cuda), 1500, 4)
+    assert cache.cold_chunks == 6
