@@ -60,26 +60,33 @@ def latent_attention(
     if not 0 < t <= MAX_Q_LEN:
         raise ValueError(f"the decode kernels take 1..{MAX_Q_LEN} new tokens per step (got {t})")
     dev = q_latent.device
+    bf = torch.bfloat16
+    args = (q_latent.reshape(bsz * t, n_heads, LATENT_DIM).to(bf).contiguous(),
+            q_rope.reshape(bsz * t, n_heads, ROPE_DIM).to(bf).contiguous(),
+            latent.reshape(bsz * t, LATENT_DIM).to(bf).contiguous(),
+            k_rope.reshape(bsz * t, ROPE_DIM).to(bf).contiguous())
+    kernel_dtype = torch.float32 if out_dtype in (None, torch.float32) else torch.bfloat16
     if cache is not None and cache.length:
         if cache.batch_size != bsz:
             raise ValueError(f"cache holds {cache.batch_size} rows, the step has {bsz}")
         pools = cache.pools()
+        if not plan_kw:
+            # the step planned on the GPU from the cache's device page tables (kept across calls)
+            planner = cache.device_planner(n_heads, t)
+            planner.plan()
+            out = torch.empty(bsz * t, n_heads, LATENT_DIM, dtype=kernel_dtype, device=dev)
+            planner.decode(pools, *args, out, softmax_scale=softmax_scale, logit_softcap=logit_softcap)
+            out = out.view(bsz, t, n_heads, LATENT_DIM)
+            return out if out_dtype is None else out.to(out_dtype)
         layouts = cache.decode_layouts(t)
     else:
         pools = _empty_pools(dev)
         layouts = [SequenceLayout(q_start=b * t, q_len=t) for b in range(bsz)]
+    # host-built schedule: an empty cache, or explicit planner options (plan_kw)
     plan = build_plan(layouts, n_heads, **plan_kw)
     dplan = DeviceDecodePlan(plan, dev)
-    bf = torch.bfloat16
-    out = latent_decode(
-        pools, dplan,
-        q_latent.reshape(bsz * t, n_heads, LATENT_DIM).to(bf).contiguous(),
-        q_rope.reshape(bsz * t, n_heads, ROPE_DIM).to(bf).contiguous(),
-        latent.reshape(bsz * t, LATENT_DIM).to(bf).contiguous(),
-        k_rope.reshape(bsz * t, ROPE_DIM).to(bf).contiguous(),
-        softmax_scale=softmax_scale, logit_softcap=logit_softcap,
-        out_dtype=torch.float32 if out_dtype in (None, torch.float32) else torch.bfloat16,
-    )
+    out = latent_decode(pools, dplan, *args, softmax_scale=softmax_scale, logit_softcap=logit_softcap,
+                        out_dtype=kernel_dtype)
     out = out.view(bsz, t, n_heads, LATENT_DIM)
     return out if out_dtype is None else out.to(out_dtype)
 

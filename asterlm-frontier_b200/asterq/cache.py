@@ -13,8 +13,12 @@ different: every batch row's tokens live in fixed-size pages of two pools
 so that appending writes the new token in place (no re-concatenation of the
 hot window, cache.py:195-200) and a flush (cache.py:167-177) encodes the oldest
 full hot page of every row straight into a cold page with the write-path kernel
-and releases the hot page.  The decode kernel reads the pools through
-``decode_layouts``; nothing is materialized on the decode path.
+and releases the hot page.  The page lists are mirrored in device page tables
+(``device_tables``), rebuilt only when pages change: bf16 appends run the in-place
+append kernel on them, and ``asterq.attention.latent_attention`` plans each step on
+the GPU from them (``device_planner``), so a decode step needs no host schedule, no
+host index tensors and no per-call allocation.  Nothing is materialized on the
+decode path.
 
 The hot window holds at most ``recent_tokens + chunk_tokens`` tokens, exactly as
 in the reference: after every append, whole chunks move from the front of the
@@ -125,6 +129,10 @@ class LatentLayerCache:
     _hot: _Pool | None = field(default=None, repr=False)
     _cold: _Pool | None = field(default=None, repr=False)
     _dtype: torch.dtype = field(default=torch.bfloat16, repr=False)
+    # device page tables mirroring the page lists (asterq.batch.BatchTables), rebuilt only when
+    # pages change, with the GPU planner bound to them: appends and attention need no host
+    # plan, host index tensors or per-call allocations
+    _dev: Any = field(default=None, repr=False)
 
     def __post_init__(self) -> None:
         if self.cache_dtype not in _KERNEL_SCHEMES:
@@ -255,10 +263,70 @@ class LatentLayerCache:
         if drop is None:
             return
         a, b = drop
+        self._mark_dirty()
         for row in range(self._batch):
             pages = self._cold_pages[row]
             self._cold.release(pages[a:b])
             self._cold_pages[row] = pages[:a] + pages[b:]
+
+    # ------------------------------------------------------------------ device tables
+    def _mark_dirty(self) -> None:
+        if self._dev is not None:
+            self._dev.dirty = True
+
+    def device_tables(self, q_len: int):
+        """The page tables on the GPU (``asterq.batch.BatchTables``), every row with ``q_len`` new
+        tokens at rows ``b * q_len``; rebuilt from the page lists and uploaded (one copy) only when
+        pages changed or ``q_len`` did since the last call."""
+        import types
+
+        import numpy as np
+
+        from .batch import BatchTables
+
+        P, B = self.page_tokens, self._batch
+        n_cold = self.cold_chunks
+        n_hot = max((len(pg) for pg in self._hot_pages), default=0)
+        st = self._dev
+        if st is None or st.tables.max_cold_pages < max(1, n_cold) or st.tables.max_hot_pages < max(1, n_hot):
+            tables = BatchTables(B, max(16, 2 * n_cold), max(4, 2 * n_hot), self._hot.device)
+            st = self._dev = types.SimpleNamespace(tables=tables, dirty=True, q_len=None, planner=None,
+                                                   status=torch.zeros(1, dtype=torch.int32, device=self._hot.device))
+        if st.dirty or st.q_len != q_len:
+            h = st.tables.host
+            h["cold_pages"][:] = 0
+            h["cold_tokens"][:] = 0
+            h["hot_pages"][:] = -1
+            h["n_cold"][:] = n_cold
+            for b in range(B):
+                h["cold_pages"][b, :n_cold] = self._cold_pages[b]
+                h["cold_tokens"][b, :n_cold] = P
+                h["hot_pages"][b, : len(self._hot_pages[b])] = self._hot_pages[b]
+            h["hot_tokens"][:] = self._hot_len
+            h["q_len"][:] = q_len
+            h["q_start"][:] = np.arange(B, dtype=np.int32) * q_len
+            st.tables.upload()
+            st.dirty, st.q_len = False, q_len
+        return st.tables
+
+    def device_planner(self, n_heads: int, q_len: int):
+        """A GPU planner (``asterq.batch.DevicePlanner``) bound to ``device_tables(q_len)``, kept
+        across calls (re-created only when the tables are re-created or a step has more rows)."""
+        from .batch import DevicePlanner
+
+        tables = self.device_tables(q_len)
+        st = self._dev
+        pl = st.planner
+        if pl is None or pl.tables is not tables or pl.n_heads != n_heads or pl.max_q_len < q_len:
+            max_q = max(q_len, pl.max_q_len if (pl is not None and pl.tables is tables) else 1)
+            st.planner = pl = DevicePlanner(tables, n_heads, self.page_tokens, max_q_len=max_q)
+        return pl
+
+    def raise_if_failed(self) -> None:
+        """Synchronize; raise if an in-place append found a hot page missing."""
+        if self._dev is not None and int(self._dev.status.item()) != 0:
+            self._dev.status.zero_()
+            raise RuntimeError("asterq cache: an append found a hot page missing")
 
     def _write_hot(self, latent: torch.Tensor, rope_key: torch.Tensor) -> None:
         P, (bsz, t) = self.page_tokens, latent.shape[:2]
@@ -268,6 +336,23 @@ class LatentLayerCache:
             missing = need - len(self._hot_pages[b])
             if missing > 0:
                 self._hot_pages[b].extend(self._hot.alloc(missing))
+                self._mark_dirty()
+        if not self._src and latent.dtype == torch.bfloat16 and rope_key.dtype == torch.bfloat16 and t <= 2048:
+            # in place on the device page tables (asterq_batch_append): no host index tensors
+            import ctypes
+
+            tables = self.device_tables(t)
+            lat = latent.reshape(bsz * t, LATENT_DIM).contiguous()
+            rope = rope_key.reshape(bsz * t, ROPE_DIM).contiguous()
+            d = tables.desc(1, P, 1)
+            _lib.check(_lib.load().asterq_batch_append(
+                ctypes.byref(d), tables.dev["hot_tokens"].data_ptr(), lat.data_ptr(), rope.data_ptr(), bsz * t,
+                self._hot["latent"].data_ptr(), self._hot["rope"].data_ptr(), int(self._hot["latent"].shape[0]),
+                self._dev.status.data_ptr(), _lib.stream_handle(latent.device)))
+            tables.host["hot_tokens"][:] = end  # the kernel advanced the device copy
+            self._hot_len = end
+            return
+        self._mark_dirty()
         pos = torch.arange(self._hot_len, end, device=latent.device)
         pages = torch.tensor(self._hot_pages, dtype=torch.int64, device=latent.device)  # [B, n_pages]
         slot = pages[:, pos // P] * P + (pos % P)  # [B, T]
@@ -291,9 +376,11 @@ class LatentLayerCache:
     def _flush_one(self) -> None:
         P, bsz = self.page_tokens, self._batch
         dev = self._hot.device
-        src = torch.tensor([self._hot_pages[b][0] for b in range(bsz)], dtype=torch.int64, device=dev)
+        self._mark_dirty()
+        src = torch.tensor([self._hot_pages[b][0] for b in range(bsz)], dtype=torch.int64).pin_memory().to(
+            dev, non_blocking=True)
         dst_pages = self._cold.alloc(bsz)
-        dst = torch.tensor(dst_pages, dtype=torch.int64, device=dev)
+        dst = torch.tensor(dst_pages, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         # quantized from the caller's values (cache.py:172 encodes the hot tensor as stored)
         x = self._hot[self._src + "latent"].index_select(0, src).reshape(bsz * P, LATENT_DIM)
         codes = torch.empty(bsz * P, LATENT_DIM // 2, dtype=torch.uint8, device=dev)
@@ -331,6 +418,7 @@ class LatentLayerCache:
         self._flush_cold_chunks()
 
     def _release_all(self) -> None:
+        self._mark_dirty()
         for b in range(self._batch):
             self._hot.release(self._hot_pages[b])
             self._cold.release(self._cold_pages[b])

@@ -257,3 +257,43 @@ def test_window_trim_by_pages_keeps_codes_and_matches_the_oracle(cuda):
     # a second append re-checks the window: nothing left between sink and recent pages
     cache.append(lat[None, :8].to(cuda), rope[None, :8].to(cuda), 1500, 4)
     assert cache.cold_chunks == 6
+
+
+def test_decode_loop_through_the_drop_in_cache_plans_on_the_gpu(cuda, monkeypatch):
+    """The reference-interface loop (latent_attention over the cache, then cache.append of the
+    step's token, as latent_attention.py:233-253 and cache.py:186-201 do it) with flushes along
+    the way: no host-built schedule (the host planner is made to fail), the new tokens land in
+    the hot pages through the in-place append kernel, and the outputs follow the oracle."""
+    import asterq.attention as attn_mod
+    from asterq.cache import LatentLayerCache
+
+    def no_host_plan(*a, **k):
+        raise AssertionError("the host planner ran")
+
+    n, B = 700, 2
+    g = torch.Generator().manual_seed(15)
+    lat = torch.randn(B, n + 80, 512, generator=g)
+    lat[..., :5] *= 20.0
+    lat = lat.to(torch.bfloat16)
+    rope = torch.randn(B, n + 80, 64, generator=g).to(torch.bfloat16)
+    cache = LatentLayerCache("hadamard_int4", 64, recent_tokens=128, chunk_tokens=128)
+    cache.append(lat[:, :n].to(cuda), rope[:, :n].to(cuda), None, 0)
+    monkeypatch.setattr(attn_mod, "build_plan", no_host_plan)
+    for step in range(80):
+        k = n + step
+        q = torch.randn(B, 1, 16, 512, generator=g).to(torch.bfloat16)
+        qr = torch.randn(B, 1, 16, 64, generator=g).to(torch.bfloat16)
+        out = attn_mod.latent_attention(q.to(cuda), qr.to(cuda), lat[:, k : k + 1].to(cuda), rope[:, k : k + 1].to(cuda),
+                                        cache, softmax_scale=SCALE)
+        if step % 19 == 0 or step == 79:
+            got = out.cpu().numpy()
+            for b in range(B):
+                lb, rb = _bf16_np(lat[b, : k + 1]), _bf16_np(rope[b, : k + 1])
+                want = O.decode(_bf16_np(q[b]), _bf16_np(qr[b]), lb[k:], rb[k:],
+                                O.build_cache_from_tokens(lb[:k], rb[:k], 128, 128), SCALE)
+                assert O.rel_l2(got[b], want) <= 1e-3 and O.max_abs(got[b], want) <= 2e-2, (step, b)
+        cache.append(lat[:, k : k + 1].to(cuda), rope[:, k : k + 1].to(cuda), None, 0)
+    cache.raise_if_failed()
+    assert cache.length == n + 80 and cache.cold_chunks == len(O.build_cache_from_tokens(
+        _bf16_np(lat[0, : n + 80]), _bf16_np(rope[0, : n + 80]), 128, 128).cold)
+    np.testing.assert_array_equal(_bf16_np(cache.latent[1]), _bf16_np(lat[1, cache.cold_length : n + 80]))
