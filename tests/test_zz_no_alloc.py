@@ -6,7 +6,8 @@ same context latents as the ordinary entry point (same tolerance as the other
 decode tests: rel-L2 <= 1e-3 and max-abs <= 2e-2; the schedule and kernels are
 the same, so the results are expected to be identical) on consecutive calls,
 including a call whose schedule differs from the one before it (the shared
-array still holds the previous call's records).
+array still holds the previous call's records); the second call is also checked
+against the CPU oracle directly.
 
 Kept in a file of its own that pytest collects last, so that it runs both after
 every other test and alone in a fresh process.
@@ -33,7 +34,18 @@ MAX_SLOTS = 256  # size of the library's built-in partial-record array
 def _workload(seed, lengths, device):
     from asterq.synth import make_workload
 
-    return make_workload("no-alloc", lengths, [min(n, 700) for n in lengths], q_len=1, seed=seed, device=device)
+    return make_workload("no-alloc", lengths, [min(n, 700) for n in lengths], q_len=1, seed=seed, device=device,
+                         keep_host=set(range(len(lengths))))
+
+
+def _oracle(wl):
+    """The oracle's context latents for every sequence of the workload, [total_q, H, 512]."""
+    rows = []
+    for i, (n, hot) in enumerate(zip(wl.lengths, wl.hot)):
+        h = wl.host[i]
+        rows.append(O.decode_sequence(h["latent"].float().numpy(), h["rope"].float().numpy(),
+                                      h["q_lat"].float().numpy(), h["q_rope"].float().numpy(), n, hot, SCALE))
+    return np.concatenate(rows)
 
 
 def _params(wl, plan_kw, out_dtype):
@@ -86,6 +98,8 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls(cuda):
             assert 0 < n_slots <= MAX_SLOTS, n_slots
         fused_calls += n_fused > 0
         _assert_same(got, ref, f"call {i} ({wl.lengths}, {dt})")
+        if i == 1:  # a second call in a row: also against the oracle directly
+            _assert_same(got, _oracle(wl), f"call {i} against the oracle")
     # the in-kernel merge (whose per-block counters sit in the built-in array, zeroed every call)
     # ran on consecutive calls
     assert fused_calls >= 2
