@@ -206,3 +206,51 @@ def test_context_parallel_processes_exchange_records(cuda, world):
         got = results[r][0:1]
         assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2, r
         assert np.array_equal(results[r], results[0])
+
+
+def test_peer_exchange_wait_times_out_without_a_fault(cuda):
+    """Failure detection for the peer exchange, without a fault: one process, a mailbox sized for
+    two ranks whose second rank never stores its records (a flag that nothing sets).  The
+    combine's wait runs into a short cycle limit, sets the status word, leaves the output
+    unwritten and returns; the context stays usable."""
+    import ctypes
+
+    from asterq import _lib
+    from asterq.context_parallel import ContextParallelDecoder
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    ctx, hot = 6 * 512 + 100, 300
+    inp = c1_inputs(seed=61, ctx=ctx)
+    b = PoolBuilder([ctx], [hot], q_len=1, n_heads=16, device=cuda)
+    b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    wl = b.finish("cp")
+    dec = ContextParallelDecoder(wl.pools, wl.layouts[0], 16, 0, 2, cuda)  # rank 0 of 2
+    lib = _lib.load()
+    nbytes = lib.asterq_mailbox_bytes(2, dec.n_rb, 512)
+    own = ctypes.c_void_p()
+    handle = (ctypes.c_ubyte * _lib.IPC_HANDLE_BYTES)()
+    _lib.check(lib.asterq_mailbox_create(nbytes, ctypes.byref(own), handle))
+    try:
+        table = torch.tensor([own.value, own.value], dtype=torch.int64, device=cuda)  # rank 1's slot: never written
+        status = torch.zeros(1, dtype=torch.int32, device=cuda)
+        out = torch.full((1, 16, 512), float("nan"), dtype=torch.float32, device=cuda)
+        stream = dec._decode_records(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE)
+        _lib.check(lib.asterq_cp_merge_push(dec.dplan.workspace.data_ptr(), dec.plan.n_slots, dec.dplan.combine.data_ptr(),
+                                            dec.n_rb, 512, table.data_ptr(), 2, 0, stream))
+        _lib.check(lib.asterq_cp_combine_wait(own.value, 2, dec.n_rb, dec.final_jobs.data_ptr(), 512, out.data_ptr(),
+                                              _lib.DTYPE_F32, 2_000_000, status.data_ptr(), stream))
+        torch.cuda.synchronize()
+        assert int(status.item()) == 1
+        assert torch.isnan(out).all()  # nothing was combined
+        # the context still works: an ordinary decode afterwards matches the oracle
+        from asterq.decode import DeviceDecodePlan, latent_decode
+        from asterq.plan import build_plan
+
+        got = latent_decode(wl.pools, DeviceDecodePlan(build_plan(wl.layouts, 16), cuda), wl.q_lat, wl.q_rope,
+                            wl.new_latent, wl.new_rope, softmax_scale=SCALE, out_dtype=torch.float32).cpu().numpy()
+        lat, rope = inp["latent"].float().numpy(), inp["rope"].float().numpy()
+        cache = O.build_cache_split(lat[:ctx], rope[:ctx], hot, 512)
+        ref = O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[ctx:], rope[ctx:], cache, SCALE)
+        assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2
+    finally:
+        _lib.check(lib.asterq_mailbox_destroy(own.value))
