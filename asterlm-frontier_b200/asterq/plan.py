@@ -37,13 +37,15 @@ _COLD_TOKEN_BYTES = 256 + 16 + 128
 _HOT_TOKEN_BYTES = 1024 + 128
 _ITEM_OVERHEAD_BYTES = 48 * 1024  # query load + rotation + output/partial write
 
-# time model of the persistent schedule (ns, one B200 SM; least-squares fit to the item
-# timelines of the C3 and C5 batches): a full cold tile 3.1 us, a full hot tile 2.1 us, an
-# item's fixed cost (query copy, first tile in flight, rotation back and output or partial
-# write, barrier reset) 5 us
-_COLD_TILE_NS = (1200, 1890)  # fixed + per full tile
-_HOT_TILE_NS = (800, 1285)
-_ITEM_NS = 5000
+# time model of the persistent schedule (ns, one B200 SM; least-squares fit to the measured end
+# times of every worker of the C3 batch and of one C5 shard under five schedules, rms 4 us):
+# a full cold tile 2.75 us, a full hot tile 1.66 us, an item's fixed cost (query copy, barrier
+# reset, output write) 1.8 us, and 5.7 us more for a piece of a cut block (its partial record
+# written and, for one piece per block, the merge of the block's records)
+_COLD_TILE_NS = (1000, 1750)  # fixed + per full tile
+_HOT_TILE_NS = (560, 1100)
+_ITEM_NS = 1800
+_PIECE_NS = 5700
 _MIN_PIECE_NS = 4 * sum(_COLD_TILE_NS)  # a worker does not start a piece of a block below this
 # a block cut into at most this many pieces is merged by the decode kernel itself (the CTA
 # that writes the last piece reads them all back from L2); more pieces go to the combine launch
@@ -212,11 +214,13 @@ def _greedy_cut(units, P, T: int, limit: int, min_piece: int = _MIN_PIECE_NS):
         a = t0
         while a < t1:
             rest = P[t1] - P[a]
-            room = T - load - _ITEM_NS
+            fixed = _ITEM_NS + (_PIECE_NS if a > t0 else 0)  # the tail of a cut block is a piece too
+            room = T - load - fixed
             if rest <= room or (rest < 2 * min_piece and load == 0):
                 pieces.append((ui, a, t1, w))  # the rest fits, or cannot be cut and the worker is empty
-                load += _ITEM_NS + rest
+                load += fixed + rest
                 break
+            room = T - load - _ITEM_NS - _PIECE_NS  # this item becomes a piece of a cut block
             if rest < 2 * min_piece or room < min_piece:
                 if load > 0:
                     if not next_worker():
@@ -228,7 +232,7 @@ def _greedy_cut(units, P, T: int, limit: int, min_piece: int = _MIN_PIECE_NS):
                 b = bisect.bisect_right(P, P[t1] - min_piece, a + 1, t1 + 1) - 1
             b = min(max(b, a + 1), t1)
             pieces.append((ui, a, b, w))
-            load += _ITEM_NS + P[b] - P[a]
+            load += _ITEM_NS + _PIECE_NS + P[b] - P[a]
             a = b
             if a < t1 and not next_worker():
                 return None
@@ -240,7 +244,7 @@ def _balanced_cut(units, P, n_workers: int):
     total = int(sum(P[t1] - P[t0] for _, t0, t1 in units)) + _ITEM_NS * len(units)
     longest_tile = int(np.diff(np.asarray(P)).max()) if len(P) > 1 else 0
     lo = max(total // n_workers, _ITEM_NS + longest_tile) - 1
-    hi = total + _ITEM_NS * (n_workers + len(units)) + int(P[-1])
+    hi = total + (_ITEM_NS + _PIECE_NS) * (n_workers + len(units)) + int(P[-1])
     # a small batch (little work per SM) cuts its blocks finer, down to one full cold tile of
     # work per piece (one 8k-token sequence: 31.8 -> 28.0 us a step)
     min_piece = max(sum(_COLD_TILE_NS), min(_MIN_PIECE_NS, total // n_workers))
