@@ -421,12 +421,19 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc 
     *reinterpret_cast<int4*>(it) = make_int4((int)u, rb, a, e);
     *reinterpret_cast<int4*>(it + 4) = make_int4(slot, b.units[2 * u], b.units[2 * u + 1], q_len(q));
     const int t0 = (int)(s.unit_t[u] & 0xffffffffLL);
-    // A unit's first piece goes to the worker whose share holds its first min_gap of work: a
-    // boundary that falls within that much of the unit's start made no cut (the piece would
-    // be a sliver), so the piece runs on to the next cut, a whole share further on; placed by
-    // its start time it would land on the worker before and double that worker's load.
-    const long long start = (a == t0) ? uoff[u] + kItemNs + min_gap : uoff[u] + kItemNs + pc[a] - pc[t0];
-    s.item_worker[idx] = (int)min((long long)W - 1, start / wd);
+    // A later piece starts at its cut, a worker boundary.  A unit's first piece goes to the
+    // worker whose share holds the middle of its time span: when the boundary just after the
+    // unit's start made no cut (the piece would have been a sliver), the piece runs on to the
+    // next cut, a whole share further on, and belongs to the later worker; when that boundary
+    // did cut a short first piece, the piece lies before it and belongs to the earlier one.
+    long long at;
+    if (a == t0) {
+      const long long end = (e < (int)(s.unit_t[u] >> 32)) ? uoff[u] + kItemNs + pc[e] - pc[t0] : uoff[u + 1];
+      at = (uoff[u] + end) / 2;
+    } else {
+      at = uoff[u] + kItemNs + pc[a] - pc[t0];
+    }
+    s.item_worker[idx] = (int)min((long long)W - 1, at / wd);
   };
   for (long long u = tid; u < n_units; u += kThreads) {
     int kb, ke;
