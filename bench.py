@@ -593,8 +593,13 @@ def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
     n, P = len(wl.lengths), wl.pools.page_tokens
     warm = max(args.warmup, 2)
     max_cold = max(len(lay.cold) for lay in wl.layouts) + (warm + args.steps) // P + 2
+    # A large per-GPU batch plans each step on a side stream while the one before decodes (the
+    # planner would otherwise add its time to the step); a small one replays the whole step
+    # (plan, decode, append) as a CUDA graph, since there the host's per-step Python would
+    # outlast the step's GPU time.
+    use_graph = n <= 32
     batch = PagedLatentBatch(wl.n_heads, max_seqs=n, q_len=1, page_tokens=P, recent_tokens=2048 - P,
-                             max_cold_pages=max_cold, plan_ahead=True, device=dev)
+                             max_cold_pages=max_cold, plan_ahead=not use_graph, device=dev)
     for lay in wl.layouts:  # slot s = shard position s: the step's row s
         batch.add_layout(wl.pools, lay.cold, lay.hot)
     inputs = (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)
@@ -609,6 +614,14 @@ def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
     in_ready = [torch.cuda.Event() for _ in range(2)]
     dec_done = [torch.cuda.Event() for _ in range(2)]
     host_s = []
+    if use_graph:
+        graphs = [batch.capture(*dev_in[b], dev_out[b], softmax_scale=SOFTMAX_SCALE) for b in range(2)]
+
+        def one_step(b):
+            graphs[b].replay()
+    else:
+        def one_step(b):
+            batch.step(*dev_in[b], dev_out[b], softmax_scale=SOFTMAX_SCALE)
 
     def copy_in(b):
         with torch.cuda.stream(copy_stream):
@@ -629,7 +642,7 @@ def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
             if k + 1 < n_steps:
                 copy_in(1 - b)
             t0 = time.perf_counter()
-            batch.step(*dev_in[b], dev_out[b], softmax_scale=SOFTMAX_SCALE)
+            one_step(b)
             host_s.append(time.perf_counter() - t0)
             dec_done[b].record(stream)
             with torch.cuda.stream(copy_stream):
@@ -652,15 +665,20 @@ def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
     e2e_ms = max_over_ranks(e_s.elapsed_time(e_e)) / args.steps
     counts = batch.last_planner.host_counts()
     host_ms = statistics.mean(host_s) * 1e3
+    how = ("the step (plan, decode, append) replayed as one CUDA graph (PagedLatentBatch.capture), host bookkeeping "
+           "between replays" if use_graph else
+           "each step's schedule planned on a side stream while the step before it decodes (one SM left to the planner)")
     res = {"value": C3_SEQS / (e2e_ms / 1e3), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-           "ms_per_step": e2e_ms, "api": "asterq.batch.PagedLatentBatch.step",
+           "ms_per_step": e2e_ms,
+           "api": "asterq.batch.PagedLatentBatch." + ("capture + StepGraph.replay" if use_graph else "step"),
            "per_step": "H2D of queries and new tokens, plan on the GPU, decode, append (cache grows one token per "
-                       "sequence), flushes as they fall due, D2H of the context latents; each step's schedule is "
-                       "planned on a side stream while the step before it decodes (one SM left to the planner)",
+                       "sequence), flushes as they fall due, D2H of the context latents; " + how,
            "host_ms_per_step": host_ms, "host_frac_of_step": host_ms / e2e_ms,
            "flushes_timed": batch.flushes - flushes0, "flush_launches_timed": batch.flush_launches - flush_launches0,
            "launches_per_step": 4 + (1 if counts["n_separate"] else 0),
            "per_rank": "h2d/d2h bytes are rank 0's"}
+    if use_graph:
+        del graphs
     del batch
     return res
 
