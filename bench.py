@@ -878,8 +878,54 @@ def extras(dev, args) -> dict:
     del wl
     wl = c5_workload(dev)
     decode_rate(wl, "c5_mtp_verification_1gpu", 10)
+    res["c5_mtp_verify_loop"] = mtp_verify_loop(wl, dev, iters=10)
     del wl
     torch.cuda.empty_cache()
+    return res
+
+
+def mtp_verify_loop(wl, dev, iters: int) -> dict:
+    """C5 as a multi-token-prediction serving loop: the 256 sequences in a PagedLatentBatch with
+    q_len 3 (the last accepted token and two drafts), each step ``verify`` (the three tokens
+    attend to the cache and causally to each other, and are appended provisionally) then
+    ``accept`` with a seeded random number of kept tokens per sequence (1-3), flushes after
+    acceptance.  The inputs are already on the device; the host's accept bookkeeping and the
+    device-side planning are inside the timed region."""
+    import numpy as np
+    import torch
+
+    from asterq.batch import PagedLatentBatch
+
+    n, P = len(wl.lengths), wl.pools.page_tokens
+    max_cold = max(len(lay.cold) for lay in wl.layouts) + 4
+    batch = PagedLatentBatch(wl.n_heads, max_seqs=n, q_len=wl.q_len, page_tokens=P, recent_tokens=2048 - P,
+                             max_cold_pages=max_cold, device=dev)
+    for lay in wl.layouts:
+        batch.add_layout(wl.pools, lay.cold, lay.hot)
+    out = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
+    rng = np.random.default_rng(5)
+    keeps = [rng.integers(1, wl.q_len + 1, size=n) for _ in range(iters + 3)]
+
+    def step(k):
+        batch.verify(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, out, softmax_scale=SOFTMAX_SCALE)
+        batch.accept(keeps[k])
+
+    for k in range(3):
+        step(k)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for k in range(iters):
+        step(3 + k)
+    e.record()
+    torch.cuda.synchronize()
+    batch.raise_if_failed()
+    ms = s.elapsed_time(e) / iters
+    accepted = float(np.mean([kp.mean() for kp in keeps[3:]]))
+    res = {"seqs": n, "q_len": wl.q_len, "ms": ms, "seq_steps_per_s": n / ms * 1e3,
+           "tokens_per_s": n * accepted / ms * 1e3, "mean_tokens_kept": accepted,
+           "api": "asterq.batch.PagedLatentBatch.verify + accept"}
+    del batch
     return res
 
 
