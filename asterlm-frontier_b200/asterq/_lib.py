@@ -36,6 +36,8 @@ def dtype_code(dtype) -> int:
 SCHEME_HADAMARD_INT4 = 0
 SCHEME_INT4 = 1
 SCHEME_INT8 = 2
+ROPE_BF16 = 0  # cold RoPE keys stored as bf16
+ROPE_QUANTIZED = 1  # cold RoPE keys stored as INT4 codes of the cold scheme + one fp16 scale a token
 
 TILE_COLD = 0
 TILE_HOT = 1
@@ -115,6 +117,8 @@ class DecodeParams(ctypes.Structure):
         ("unit_jobs", ctypes.c_void_p),
         ("wait_limit_cycles", ctypes.c_int64),
         ("plan_counts", ctypes.c_void_p),
+        ("rope_scheme", ctypes.c_int32),
+        ("cold_rope_scales", ctypes.c_void_p),
     ]
 
 

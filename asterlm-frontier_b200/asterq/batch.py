@@ -31,7 +31,8 @@ import numpy as np
 import torch
 
 from . import _lib
-from .decode import COLD_SCHEMES, GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools
+from .decode import COLD_SCHEMES, GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools, set_cold_pools
+from .plan import QPREP_BYTES
 
 COLD_TILE = 128
 HOT_TILE = 32
@@ -259,15 +260,10 @@ class DevicePlanner:
         p.softmax_scale = float(softmax_scale)
         p.logit_softcap = float(logit_softcap) if logit_softcap else 0.0
         p.wait_limit_cycles = int(wait_limit_cycles)
-        p.n_cold_pages, p.n_hot_pages = int(pools.cold_codes.shape[0]), int(pools.hot_latent.shape[0])
-        p.cold_codes = pools.cold_codes.data_ptr() if pools.cold_codes.numel() else None
-        p.cold_scales = pools.cold_scales.data_ptr() if pools.cold_scales.numel() else None
-        p.cold_rope = pools.cold_rope.data_ptr() if pools.cold_rope.numel() else None
+        set_cold_pools(p, pools)
+        p.n_hot_pages = int(pools.hot_latent.shape[0])
         p.hot_latent = pools.hot_latent.data_ptr() if pools.hot_latent.numel() else None
         p.hot_rope = pools.hot_rope.data_ptr() if pools.hot_rope.numel() else None
-        if pools.cold_scheme not in COLD_SCHEMES:
-            raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
-        p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]
         p.total_q = int(q_lat.shape[0])
         p.q_lat, p.q_rope = q_lat.data_ptr(), q_rope.data_ptr()
         p.new_latent, p.new_rope, p.out = new_latent.data_ptr(), new_rope.data_ptr(), out.data_ptr()
@@ -295,7 +291,7 @@ class DevicePlanner:
             raise RuntimeError("asterq decode: a pipeline wait timed out on the device (output not valid)")
 
 
-_QPREP_BYTES = 35328  # prepared query operands of one 16-row block
+_QPREP_BYTES = QPREP_BYTES  # prepared query operands of one 16-row block
 
 
 class _PagePool:

@@ -108,8 +108,10 @@ class LatentLayerCache:
 
     Same constructor fields and defaults as the reference.  The decode kernels
     serve ``cache_dtype`` "hadamard_int4" and "int4" (cold chunks) and "bfloat16" (never
-    flushes, cache.py:169); ``group_size`` must be 64 and ``quantize_rope``
-    False for the kernel path, as in every BASELINE configuration.
+    flushes, cache.py:169); ``group_size`` must be 64.  With ``quantize_rope`` the cold
+    chunks' RoPE keys are quantized with the cold scheme as well (cache.py:160-164: one
+    group of 64, 32 code bytes and one fp16 scale per token), and the kernel scores those
+    codes directly.
     """
 
     cache_dtype: str = "bfloat16"
@@ -140,8 +142,6 @@ class LatentLayerCache:
                 f"cache_dtype {self.cache_dtype!r}: the asterq pools serve 'hadamard_int4', 'int4' and 'bfloat16'")
         if self.cache_dtype in _SCHEME_IDS and self.group_size != GROUP_SIZE:
             raise NotImplementedError(f"group_size {self.group_size}: the decode kernels use groups of {GROUP_SIZE}")
-        if self.quantize_rope:
-            raise NotImplementedError("quantize_rope=True: the decode kernels read bf16 RoPE keys")
         if self.chunk_tokens <= 0 or self.chunk_tokens % 16:
             raise ValueError("chunk_tokens must be a positive multiple of 16 (one chunk per page)")
         if self.recent_tokens < 0:
@@ -178,7 +178,8 @@ class LatentLayerCache:
     def num_bytes(self) -> int:
         """Bytes the reference would account (cache.py:79-87): codes + scales + cold RoPE + hot tensors."""
         b, cold = self._batch, self.cold_length
-        total = b * cold * (LATENT_DIM // 2 + (LATENT_DIM // GROUP_SIZE) * 2 + ROPE_DIM * 2)
+        rope = (ROPE_DIM // 2 + 2) if self._rope_quantized else ROPE_DIM * 2  # codes + scale, or bf16
+        total = b * cold * (LATENT_DIM // 2 + (LATENT_DIM // GROUP_SIZE) * 2 + rope)
         total += b * self._hot_len * (LATENT_DIM + ROPE_DIM) * self._dtype.itemsize
         return int(total)
 
@@ -193,15 +194,23 @@ class LatentLayerCache:
                 # bf16 operands the decode kernel reads
                 fields.update(src_latent=((LATENT_DIM,), dtype), src_rope=((ROPE_DIM,), dtype))
             self._hot = _Pool(fields, self.page_tokens, device)
-            self._cold = _Pool({"codes": ((LATENT_DIM // 2,), torch.uint8),
-                                "scales": ((LATENT_DIM // GROUP_SIZE,), torch.float16),
-                                "rope": ((ROPE_DIM,), torch.bfloat16)}, self.page_tokens, device)
+            cold = {"codes": ((LATENT_DIM // 2,), torch.uint8), "scales": ((LATENT_DIM // GROUP_SIZE,), torch.float16)}
+            if self._rope_quantized:
+                cold.update(rope=((ROPE_DIM // 2,), torch.uint8), rope_scales=((), torch.float16))
+            else:
+                cold.update(rope=((ROPE_DIM,), torch.bfloat16))
+            self._cold = _Pool(cold, self.page_tokens, device)
             self._hot_pages = [[] for _ in range(batch)]
             self._cold_pages = [[] for _ in range(batch)]
         elif batch != self._batch:
             raise ValueError(f"batch size changed from {self._batch} to {batch}")
         elif dtype != self._dtype:
             raise ValueError(f"latent dtype changed from {self._dtype} to {dtype} (the hot window keeps one dtype)")
+
+    @property
+    def _rope_quantized(self) -> bool:
+        """Cold RoPE keys stored as codes (cache.py:163: only the integer schemes with quantize_rope)."""
+        return self.quantize_rope and self.cache_dtype in _SCHEME_IDS
 
     @property
     def _src(self) -> str:
@@ -214,7 +223,8 @@ class LatentLayerCache:
             raise RuntimeError("empty cache")
         return LatentPools(cold_codes=self._cold["codes"], cold_scales=self._cold["scales"],
                            cold_rope=self._cold["rope"], hot_latent=self._hot["latent"], hot_rope=self._hot["rope"],
-                           cold_scheme=self.cache_dtype if self.cache_dtype in _SCHEME_IDS else "hadamard_int4")
+                           cold_scheme=self.cache_dtype if self.cache_dtype in _SCHEME_IDS else "hadamard_int4",
+                           cold_rope_scales=self._cold["rope_scales"] if self._rope_quantized else None)
 
     def decode_layouts(self, q_len: int) -> list[SequenceLayout]:
         """One SequenceLayout per batch row; row b's new tokens are rows b*q_len.. of the step's arrays."""
@@ -391,8 +401,19 @@ class LatentLayerCache:
                                        _lib.stream_handle(dev)))
         self._cold["codes"].index_copy_(0, dst, codes.view(bsz, P, -1))
         self._cold["scales"].index_copy_(0, dst, scales.view(bsz, P, -1))
-        # cold RoPE keys are bf16 whatever the caller's dtype (cache.py:162-164)
-        self._cold["rope"].index_copy_(0, dst, self._hot["rope"].index_select(0, src))
+        if self._rope_quantized:
+            # quantize_rope (cache.py:163): the RoPE keys as stored, cold scheme, one group of 64
+            r = self._hot[self._src + "rope"].index_select(0, src).reshape(bsz * P, ROPE_DIM)
+            rcodes = torch.empty(bsz * P, ROPE_DIM // 2, dtype=torch.uint8, device=dev)
+            rscales = torch.empty(bsz * P, 1, dtype=torch.float16, device=dev)
+            _lib.check(lib.asterq_quantize(r.data_ptr(), _lib.dtype_code(r.dtype), bsz * P, ROPE_DIM, ROPE_DIM,
+                                           _SCHEME_IDS[self.cache_dtype], GROUP_SIZE, rcodes.data_ptr(),
+                                           rscales.data_ptr(), _lib.stream_handle(dev)))
+            self._cold["rope"].index_copy_(0, dst, rcodes.view(bsz, P, -1))
+            self._cold["rope_scales"].index_copy_(0, dst, rscales.view(bsz, P))
+        else:
+            # cold RoPE keys are bf16 whatever the caller's dtype (cache.py:162-164)
+            self._cold["rope"].index_copy_(0, dst, self._hot["rope"].index_select(0, src))
         freed = []
         for b in range(bsz):
             self._cold_pages[b].append(dst_pages[b])
@@ -458,14 +479,32 @@ class LatentLayerCache:
         return out
 
     @property
-    def cold_rope(self) -> list[torch.Tensor]:
-        return [torch.stack([self._cold["rope"][self._cold_pages[b][c]] for b in range(self._batch)])
-                for c in range(self.cold_chunks)]
+    def cold_rope(self) -> list[torch.Tensor] | list[QuantizedTensor]:
+        """Cold RoPE pieces: bf16 [B, chunk, 64], or with quantize_rope one QuantizedTensor per
+        chunk (data [B, chunk, 32], scale [B, chunk, 1, 1]), as the reference stores them."""
+        if not self._rope_quantized:
+            return [torch.stack([self._cold["rope"][self._cold_pages[b][c]] for b in range(self._batch)])
+                    for c in range(self.cold_chunks)]
+        out = []
+        for c in range(self.cold_chunks):
+            pages = [self._cold_pages[b][c] for b in range(self._batch)]
+            data = torch.stack([self._cold["rope"][pg] for pg in pages])
+            scale = torch.stack([self._cold["rope_scales"][pg] for pg in pages]).reshape(self._batch, -1, 1, 1)
+            out.append(QuantizedTensor(data=data, scale=scale, original_shape=(self._batch, self.chunk_tokens, ROPE_DIM),
+                                       padded_dim=ROPE_DIM, group_size=GROUP_SIZE, scheme=self.cache_dtype,
+                                       source_dtype=self._dtype))
+        return out
+
+    @staticmethod
+    def _rope_piece(piece, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+        if isinstance(piece, QuantizedTensor):
+            return dequantize_tensor(piece, dtype=dtype).to(device)
+        return piece.to(device=device, dtype=dtype)
 
     def iter_chunks(self, *, dtype: torch.dtype, device: torch.device):
         """cache.py:139-159: dequantized (latent, rope) per cold chunk, then the hot window."""
         for q, rope in zip(self.cold_latent, self.cold_rope, strict=True):
-            yield dequantize_tensor(q, dtype=dtype).to(device), rope.to(device=device, dtype=dtype)
+            yield dequantize_tensor(q, dtype=dtype).to(device), self._rope_piece(rope, dtype, device)
         if self._hot_len:
             yield self.latent.to(device=device, dtype=dtype), self.rope_key.to(device=device, dtype=dtype)
 
@@ -486,7 +525,7 @@ class LatentLayerCache:
             return None
         dtype = self._dtype if dtype is None else dtype
         device = self._hot.device if device is None else device
-        parts = [r.to(device=device, dtype=dtype) for r in self.cold_rope]
+        parts = [self._rope_piece(r, dtype, device) for r in self.cold_rope]
         if self._hot_len:
             parts.append(self.rope_key.to(device=device, dtype=dtype))
         return torch.cat(parts, dim=1)

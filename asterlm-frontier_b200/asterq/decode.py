@@ -28,28 +28,68 @@ class LatentPools:
 
     cold_codes: torch.Tensor  # uint8 [Pc, page, 256]
     cold_scales: torch.Tensor  # fp16 [Pc, page, 8]
-    cold_rope: torch.Tensor  # bf16 [Pc, page, 64]
+    cold_rope: torch.Tensor  # bf16 [Pc, page, 64], or uint8 [Pc, page, 32] INT4 codes (quantized RoPE keys)
     hot_latent: torch.Tensor  # bf16 [Ph, page, 512]
     hot_rope: torch.Tensor  # bf16 [Ph, page, 64]
     cold_scheme: str = "hadamard_int4"  # or "int4": plain groupwise codes, same layout
+    # fp16 [Pc, page]: one scale per token of quantized cold RoPE keys (quantize_rope=True,
+    # cache.py:160-164), whose codes (cold scheme, one group of 64) are in cold_rope
+    cold_rope_scales: torch.Tensor | None = None
 
     @property
     def page_tokens(self) -> int:
         return int(self.cold_codes.shape[1] if self.cold_codes.numel() else self.hot_latent.shape[1])
 
+    @property
+    def rope_quantized(self) -> bool:
+        return self.cold_rope.dtype == torch.uint8
+
     @staticmethod
-    def empty(n_cold_pages: int, n_hot_pages: int, page_tokens: int, device) -> "LatentPools":
+    def empty(n_cold_pages: int, n_hot_pages: int, page_tokens: int, device, *,
+              quantize_rope: bool = False) -> "LatentPools":
+        if quantize_rope:
+            cold_rope = torch.empty(n_cold_pages, page_tokens, ROPE_DIM // 2, dtype=torch.uint8, device=device)
+            rope_scales = torch.empty(n_cold_pages, page_tokens, dtype=torch.float16, device=device)
+        else:
+            cold_rope = torch.empty(n_cold_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device)
+            rope_scales = None
         return LatentPools(
             cold_codes=torch.empty(n_cold_pages, page_tokens, LATENT_DIM // 2, dtype=torch.uint8, device=device),
             cold_scales=torch.empty(n_cold_pages, page_tokens, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=device),
-            cold_rope=torch.empty(n_cold_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device),
+            cold_rope=cold_rope,
             hot_latent=torch.empty(n_hot_pages, page_tokens, LATENT_DIM, dtype=torch.bfloat16, device=device),
             hot_rope=torch.empty(n_hot_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device),
+            cold_rope_scales=rope_scales,
         )
 
     @property
     def num_bytes(self) -> int:
-        return sum(t.numel() * t.element_size() for t in (self.cold_codes, self.cold_scales, self.cold_rope, self.hot_latent, self.hot_rope))
+        parts = [self.cold_codes, self.cold_scales, self.cold_rope, self.hot_latent, self.hot_rope]
+        if self.cold_rope_scales is not None:
+            parts.append(self.cold_rope_scales)
+        return sum(t.numel() * t.element_size() for t in parts)
+
+
+def set_cold_pools(p: _lib.DecodeParams, pools: LatentPools) -> None:
+    """The cold-pool fields of ``asterq_decode_params``: codes, scales, RoPE keys (bf16, or
+    quantized codes with their scales) and the cold scheme."""
+    p.n_cold_pages = int(pools.cold_codes.shape[0])
+    p.cold_codes = pools.cold_codes.data_ptr() if pools.cold_codes.numel() else None
+    p.cold_scales = pools.cold_scales.data_ptr() if pools.cold_scales.numel() else None
+    p.cold_rope = pools.cold_rope.data_ptr() if pools.cold_rope.numel() else None
+    if pools.rope_quantized:
+        if pools.cold_rope_scales is None:
+            raise ValueError("quantized cold RoPE keys (uint8 cold_rope) need cold_rope_scales")
+        if pools.cold_rope.shape[-1] != ROPE_DIM // 2 or pools.cold_rope_scales.dtype != torch.float16:
+            raise ValueError("quantized cold RoPE keys: cold_rope [Pc, page, 32] uint8, cold_rope_scales fp16 [Pc, page]")
+        p.rope_scheme = _lib.ROPE_QUANTIZED
+        p.cold_rope_scales = pools.cold_rope_scales.data_ptr() if pools.cold_rope_scales.numel() else None
+    else:
+        p.rope_scheme = _lib.ROPE_BF16
+        p.cold_rope_scales = None
+    if pools.cold_scheme not in COLD_SCHEMES:
+        raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
+    p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]
 
 
 class DeviceDecodePlan:
@@ -109,7 +149,7 @@ def make_params(
     p.out_dtype = _lib.DTYPE_F32 if out.dtype == torch.float32 else _lib.DTYPE_BF16
     p.softmax_scale = float(softmax_scale)
     p.logit_softcap = float(logit_softcap) if logit_softcap else 0.0
-    p.n_cold_pages = int(pools.cold_codes.shape[0])
+    set_cold_pools(p, pools)
     p.n_hot_pages = int(pools.hot_latent.shape[0])
     p.total_q = int(q_lat.shape[0])
     p.n_tiles = int(plan.tiles.shape[0])
@@ -121,9 +161,6 @@ def make_params(
     p.q_rope = q_rope.data_ptr()
     p.new_latent = new_latent.data_ptr()
     p.new_rope = new_rope.data_ptr()
-    p.cold_codes = pools.cold_codes.data_ptr() if pools.cold_codes.numel() else None
-    p.cold_scales = pools.cold_scales.data_ptr() if pools.cold_scales.numel() else None
-    p.cold_rope = pools.cold_rope.data_ptr() if pools.cold_rope.numel() else None
     p.hot_latent = pools.hot_latent.data_ptr() if pools.hot_latent.numel() else None
     p.hot_rope = pools.hot_rope.data_ptr() if pools.hot_rope.numel() else None
     p.tiles = dplan.tiles.data_ptr()
@@ -141,9 +178,6 @@ def make_params(
         p.unit_jobs = dplan.unit_jobs.data_ptr()
     p.device_status = dplan.status.data_ptr()
     p.wait_limit_cycles = int(wait_limit_cycles)
-    if pools.cold_scheme not in COLD_SCHEMES:
-        raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
-    p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]
     return p
 
 

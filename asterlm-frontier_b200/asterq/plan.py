@@ -81,7 +81,8 @@ class SequenceLayout:
         return self.cold_tokens * _COLD_TOKEN_BYTES + (self.hot_tokens + self.q_len * self.attend_new) * _HOT_TOKEN_BYTES
 
 
-QPREP_BYTES = 35328  # prepared query operands of one 16-row block (int8 limbs, bf16 fragments, scalars)
+QPREP_BYTES = 37376  # prepared query operands of one 16-row block (int8 limbs, bf16 fragments, scalars,
+                     # int8 limbs of the RoPE query for quantized cold RoPE keys)
 
 
 @dataclass

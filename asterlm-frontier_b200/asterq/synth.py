@@ -67,7 +67,8 @@ class Workload:
         cold = sum(n - h for n, h in zip(self.lengths, self.hot))
         hot = sum(self.hot) + self.total_q
         per_q = self.n_heads * (LATENT_DIM + ROPE_DIM) * 2 + self.n_heads * LATENT_DIM * 2
-        return cold * (256 + 16 + 128) + hot * (1024 + 128) + self.total_q * per_q
+        rope = (ROPE_DIM // 2 + 2) if self.pools.rope_quantized else ROPE_DIM * 2  # codes + scale, or bf16
+        return cold * (256 + 16 + rope) + hot * (1024 + 128) + self.total_q * per_q
 
     def flops(self) -> int:
         """Useful multiply-adds x 2 (QK over 576 dims + PV over 512) for all rows."""
@@ -96,7 +97,8 @@ class PoolBuilder:
     chunks (the newest possibly partial) and encoded with the write-path kernel.
     """
 
-    def __init__(self, lengths, hot, *, q_len, n_heads, page_tokens=512, device="cuda", scheme="hadamard_int4"):
+    def __init__(self, lengths, hot, *, q_len, n_heads, page_tokens=512, device="cuda", scheme="hadamard_int4",
+                 quantize_rope=False):
         from . import _lib
 
         self._lib = _lib
@@ -106,7 +108,8 @@ class PoolBuilder:
         self.lengths, self.hot = list(lengths), list(hot)
         n_cold_pages = sum(math.ceil(max(0, n - h) / page_tokens) for n, h in zip(lengths, hot))
         n_hot_pages = sum(math.ceil(h / page_tokens) for h in hot)
-        self.pools = LatentPools.empty(n_cold_pages, n_hot_pages, page_tokens, self.device)
+        # quantize_rope: cold RoPE keys encoded like the latent (cold scheme, one group of 64)
+        self.pools = LatentPools.empty(n_cold_pages, n_hot_pages, page_tokens, self.device, quantize_rope=quantize_rope)
         self.pools.cold_scheme = scheme
         self._scheme_id = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4}[scheme]
         total_q = len(self.lengths) * q_len
@@ -142,7 +145,16 @@ class PoolBuilder:
                     self._lib.stream_handle(self.device),
                 )
             )
-            pools.cold_rope.view(-1, ROPE_DIM)[r0 : r0 + cold].copy_(rope[:cold])
+            if pools.rope_quantized:
+                self._lib.check(
+                    self.lib.asterq_quantize(
+                        rope.data_ptr(), self._lib.DTYPE_BF16, cold, ROPE_DIM, ROPE_DIM, self._scheme_id, GROUP_SIZE,
+                        pools.cold_rope.view(-1, ROPE_DIM // 2)[r0].data_ptr(),
+                        pools.cold_rope_scales.view(-1)[r0:].data_ptr(), self._lib.stream_handle(self.device),
+                    )
+                )
+            else:
+                pools.cold_rope.view(-1, ROPE_DIM)[r0 : r0 + cold].copy_(rope[:cold])
             for s in range(0, cold, P):
                 lay.cold.append((self._cold_page, 0, min(P, cold - s)))
                 self._cold_page += 1
@@ -178,6 +190,7 @@ def make_workload(
     device="cuda",
     page_tokens: int = 512,
     keep_host: set[int] | None = None,
+    quantize_rope: bool = False,
 ) -> Workload:
     """Generate every sequence on the device and build its pools.
 
@@ -185,7 +198,8 @@ def make_workload(
     """
     device = torch.device(device)
     keep_host = keep_host or set()
-    b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=n_heads, page_tokens=page_tokens, device=device)
+    b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=n_heads, page_tokens=page_tokens, device=device,
+                    quantize_rope=quantize_rope)
     host: dict[int, dict[str, torch.Tensor]] = {}
     for i, lat, rope, ql, qr in generate_sequences(lengths, q_len=q_len, n_heads=n_heads, seed=seed, device=device):
         b.add(lat, rope, ql, qr)
@@ -259,10 +273,10 @@ def make_shard_workload(
     return b.finish(name, host)
 
 
-def c3_workload(device="cuda", seed: int = 0, n_seqs: int = 64, keep_host=None) -> Workload:
+def c3_workload(device="cuda", seed: int = 0, n_seqs: int = 64, keep_host=None, quantize_rope: bool = False) -> Workload:
     lens = c3_lengths(seed, n_seqs)
     return make_workload("C3 ragged decode", lens, [min(n, 2048) for n in lens], q_len=1, seed=seed, device=device,
-                         keep_host=keep_host)
+                         keep_host=keep_host, quantize_rope=quantize_rope)
 
 
 def c5_workload(device="cuda", seed: int = 0, n_seqs: int = 256, keep_host=None) -> Workload:

@@ -75,7 +75,10 @@ static_assert(32 * (kScoreWarps * kScoreRegs + kValueWarps * kValueRegs) <= kThr
 // one pipeline stage (offsets in bytes, swizzled regions 1024-aligned)
 constexpr int kCodesLo = 0;        // cold: [128][128 B] codes of dims 0..255, SW128
 constexpr int kCodesHi = 16384;    // cold: [128][128 B] codes of dims 256..511, SW128
-constexpr int kCRope = 32768;      // cold: [128][128 B] RoPE keys, SW128
+constexpr int kCRope = 32768;      // cold: [128][128 B] RoPE keys, SW128; quantized RoPE (ASTERQ_ROPE_QUANTIZED):
+                                   // [128][32 B] codes, plain
+constexpr int kCRopeScale = kCRope + 4096;  // quantized RoPE: fp16 scales of the tile's tokens from the
+                                            // 8-token boundary at or below its first token
 constexpr int kScales = 49152;     // cold: [128][16 B] fp16 scales, plain
 constexpr int kHotBlock = 4096;    // hot: latent scale-group g at g*4096: [32][128 B], SW128
 constexpr int kHRope = 32768;      // hot: [32][128 B] RoPE keys, SW128
@@ -83,6 +86,8 @@ constexpr int kStageBytes = 51200;
 
 constexpr int kOffQi = kStages * kStageBytes;  // cold query int8 limb fragments [16 k-steps][2][32] uint4
                                                // (32 KB region: the [16][512] fp32 scratch after the tiles)
+constexpr int kOffQri = kOffQi + 16384;         // quantized RoPE: query int8 limb fragments [2][2][32] uint4
+                                                // (in the scratch half that the tile loop leaves unused)
 constexpr int kOffQh = kOffQi + 32768;          // hot query B fragments  [8][4][2][32] uint2
 constexpr int kOffQr = kOffQh + 16384;          // rope query B fragments [4][2][32] uint2
 constexpr int kPStride = kColdTile + 4;         // p tile row stride (floats)
@@ -100,7 +105,8 @@ constexpr int kMQscale = 32;   // [16]
 constexpr int kMQinv = 48;     // [16]  (score multiplier 2^-e * softmax_scale)
 constexpr int kMQint = 64;     // [16]  fixed-point query scale (32511 / max |rotated row|)
 constexpr int kMQinvI = 80;    // [16]  cold integer-score multiplier softmax_scale / (16 * kMQint)
-constexpr int kMRopeR = 96;    // [16]  RoPE score -> integer-score units (kMQinv / kMQinvI)
+constexpr int kMRopeR = 96;    // [16]  RoPE score -> integer-score units (kMQinv / kMQinvI); with quantized
+                               //       RoPE keys: kMQint / (the RoPE query's own fixed-point scale)
 constexpr int kQScalars = 80;  // kMQscale .. kMRopeR: the per-row scalars of a prepared query block
 constexpr int kMWmax = 112;    // [2 teams][2][4][16] tile maxima (a team's tiles alternate buffers);
                                // after the tile loop [16] = final running max
@@ -110,7 +116,8 @@ constexpr int kMComb = 528;    // fused combine: [2][16] per-row max and 1 / sum
 
 // workspace: n_slots partial records, then n_units prepared query blocks
 constexpr int kRecordBytes = kRows * (kL + 2) * 4;                    // 32,896
-constexpr int kQPrepBytes = 16384 + 16384 + 2048 + 512;               // 35,328: qi | qh | qr | scalars
+constexpr int kQPrepRopeInt = 16384 + 16384 + 2048 + 512;             // quantized RoPE limb fragments
+constexpr int kQPrepBytes = kQPrepRopeInt + 2048;                     // 37,376: qi | qh | qr | scalars | qri
 // then one int32 per unit: partial records written so far (fused combine jobs)
 __host__ __device__ inline int64_t counters_offset(int n_slots, int n_units) {
   return (int64_t)n_slots * kRecordBytes + (int64_t)n_units * kQPrepBytes;
@@ -268,7 +275,7 @@ ASTERQ_DEVICE int qk_token(int warp, int m, int r) {
 // ---------------------------------------------------------------------------
 constexpr int kPrepThreads = 512;
 constexpr int kPrepRowsPerWarp = kRows / (kPrepThreads / 32);  // one query row per warp
-constexpr int kPrepSmem = 16 * kL * 4 + 16 * kL * 2 + 16 * kRope * 2 + 4 * kQScalars;
+constexpr int kPrepSmem = 16 * kL * 4 + 16 * kL * 2 + 16 * kRope * 2 + 4 * kQScalars + 4 * (16 * kRope + 16);
 
 __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_constant__ asterq_decode_params p) {
   extern __shared__ __align__(16) uint8_t prep_smem[];
@@ -276,6 +283,8 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   uint16_t* qraw = reinterpret_cast<uint16_t*>(prep_smem + 16 * kL * 4);           // [16][512] bf16
   uint16_t* rraw = reinterpret_cast<uint16_t*>(prep_smem + 16 * kL * 6);           // [16][64] bf16
   float* sc = reinterpret_cast<float*>(prep_smem + 16 * kL * 6 + 16 * kRope * 2);  // kQScalars, from kMQscale
+  float* rscr = sc + kQScalars;  // quantized RoPE: [16][64] fp32 rotated RoPE query, then [16] fixed-point scales
+  const bool rope_q = p.rope_scheme == ASTERQ_ROPE_QUANTIZED;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int unit = blockIdx.x;
   // the decode grid may launch now; it waits for this grid's results before reading them
@@ -332,6 +341,38 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
       sc[kMQinvI - kMQscale + r] = p.softmax_scale / (16.0f * qs);
       sc[kMRopeR - kMQscale + r] = ldexpf(1.0f, -e) * (16.0f * qs);
     }
+    if (rope_q) {
+      // Quantized cold RoPE keys are scored like a ninth scale group: the RoPE query in the
+      // codes' basis (normalized 64-point Hadamard for hadamard_int4: butterflies (a + b, a - b)
+      // at distances 1, 2, .., 32, then / 8), with its own fixed-point scale; lane l holds
+      // dims 2l and 2l + 1.
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(rraw + r * kRope + 2 * lane);
+      float x0 = bf16lo_to_f32(w), x1 = bf16hi_to_f32(w);
+      if (p.cold_scheme == ASTERQ_SCHEME_HADAMARD_INT4) {
+        const float a = x0, b = x1;
+        x0 = a + b;
+        x1 = a - b;
+#pragma unroll
+        for (int d = 1; d < 32; d <<= 1) {
+          const float o0 = __shfl_xor_sync(0xffffffffu, x0, d), o1 = __shfl_xor_sync(0xffffffffu, x1, d);
+          const bool upper = (lane & d) != 0;
+          x0 = upper ? o0 - x0 : x0 + o0;
+          x1 = upper ? o1 - x1 : x1 + o1;
+        }
+        x0 *= 0.125f;
+        x1 *= 0.125f;
+      }
+      rscr[r * kRope + 2 * lane] = x0;
+      rscr[r * kRope + 2 * lane + 1] = x1;
+      float rmx = fmaxf(fabsf(x0), fabsf(x1));
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) rmx = fmaxf(rmx, __shfl_xor_sync(0xffffffffu, rmx, off));
+      if (lane == 0) {
+        const float qr_s = (rmx > 0.0f) ? 32511.0f / rmx : 1.0f;
+        rscr[16 * kRope + r] = qr_s;
+        sc[kMRopeR - kMQscale + r] = sc[kMQint - kMQscale + r] / qr_s;
+      }
+    }
   }
   __syncthreads();
   // cold QK B fragments: k-step ks = 2 * group + j; lane (gid, tq) holds query row 8nt + gid at
@@ -380,8 +421,33 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   }
   float* scalars = reinterpret_cast<float*>(dst + 34816);
   for (int e = tid; e < kQScalars; e += kPrepThreads) scalars[e] = sc[e];
+  if (rope_q) {
+    // quantized RoPE limb fragments: k-step j, lane (gid, tq) holds query row 8nt + gid at the
+    // dims of code word W = 2tq + j of the 32-byte RoPE code row (same expansion as the latent)
+    uint4* qri = reinterpret_cast<uint4*>(dst + kQPrepRopeInt);
+    for (int e = tid; e < 2 * 2 * 32; e += kPrepThreads) {
+      const int ln = e & 31, nt = (e >> 5) & 1, j = e >> 6;
+      const int row = 8 * nt + (ln >> 2), W = 2 * (ln & 3) + j;
+      const float qs = rscr[16 * kRope + row];
+      uint32_t hb[2] = {0u, 0u}, lb[2] = {0u, 0u};
+#pragma unroll
+      for (int half = 0; half < 2; ++half)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int qv = min(max(__float2int_rn(rscr[row * kRope + 8 * W + 2 * i + half] * qs), -32511), 32511);
+          const int q1 = (qv + 128) >> 8;
+          const int q2 = qv - 256 * q1;
+          hb[half] |= (uint32_t)(q1 & 0xff) << (8 * i);
+          lb[half] |= (uint32_t)(q2 & 0xff) << (8 * i);
+        }
+      qri[e] = make_uint4(hb[0], hb[1], lb[0], lb[1]);
+    }
+  }
 }
 
+// kRopeQ: cold RoPE keys quantized (ASTERQ_ROPE_QUANTIZED); a separate instantiation, so that the
+// bf16-RoPE kernel's code and register allocation do not carry the quantized path
+template <bool kRopeQ>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
   extern __shared__ uint8_t smem_raw[];
@@ -463,9 +529,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (t.kind == ASTERQ_TILE_COLD) {
       const int y = t.page * p.page_tokens + t.off;
-      mbar_expect_tx(full, 3 * 16384 + 16 * t.n);
-      tma_3d(st + kCodesLo, &maps.codes, y, full);  // both halves: kCodesHi = kCodesLo + 128 rows x 128 B
-      tma_2d(st + kCRope, &maps.crope, 0, y, full);
+      if constexpr (kRopeQ) {
+        // RoPE codes (32 B a token) and scales (2 B a token, copied from the 8-token boundary
+        // at or below y to the one at or above y + n: both within the page, whose first token
+        // index is a multiple of 16)
+        const int y8 = y & ~7, n8 = ((y + t.n + 7) & ~7) - y8;
+        mbar_expect_tx(full, 2 * 16384 + 16 * t.n + 32 * t.n + 2 * n8);
+        tma_3d(st + kCodesLo, &maps.codes, y, full);
+        bulk_1d(st + kCRope, reinterpret_cast<const uint8_t*>(p.cold_rope) + (int64_t)y * 32, 32 * t.n, full);
+        bulk_1d(st + kCRopeScale, reinterpret_cast<const uint8_t*>(p.cold_rope_scales) + (int64_t)y8 * 2, 2 * n8, full);
+      } else {
+        mbar_expect_tx(full, 3 * 16384 + 16 * t.n);
+        tma_3d(st + kCodesLo, &maps.codes, y, full);  // both halves: kCodesHi = kCodesLo + 128 rows x 128 B
+        tma_2d(st + kCRope, &maps.crope, 0, y, full);
+      }
       bulk_1d(st + kScales, reinterpret_cast<const uint8_t*>(p.cold_scales) + (int64_t)y * 16, 16 * t.n, full);
     } else {
       const bool hot = t.kind == ASTERQ_TILE_HOT;
@@ -487,11 +564,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint8_t* src = reinterpret_cast<const uint8_t*>(p.workspace) + (int64_t)p.n_slots * kRecordBytes +
                          (int64_t)max(itm[0], 0) * kQPrepBytes;
     const uint32_t qb = bar(kBarQ);
-    mbar_expect_tx(qb, kQPrepCopyBytes);
+    constexpr bool rope_q = kRopeQ;
+    mbar_expect_tx(qb, kQPrepCopyBytes + (rope_q ? 2048u : 0u));
     bulk_1d(sbase + kOffQi, src, 16384, qb);
     bulk_1d(sbase + kOffQh, src + 16384, 16384, qb);
     bulk_1d(sbase + kOffQr, src + 32768, 2048, qb);
     bulk_1d(sbase + kOffMisc + 4 * kMQscale, src + 34816, 4 * kQScalars, qb);
+    if (rope_q) bulk_1d(sbase + kOffQri, src + kQPrepRopeInt, 2048, qb);
     if (!tiles_issued)
       for (int j = 0; j < min(n_t, kStages); ++j) issue(j);
   };
@@ -695,40 +774,49 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(tw, m, gid + 8 * h);
           const __half* scl = reinterpret_cast<const __half*>(st + kScales);
-          // RoPE channel first (bf16, exact products), moved into the integer-score units
+          if constexpr (kRopeQ) {
+            // quantized RoPE keys: scored as a ninth scale group in the group loop below
+          } else {
+            // RoPE channel first (bf16, exact products), moved into the integer-score units
 #pragma unroll
-          for (int m = 0; m < 2; ++m) {
-            const int row = qk_token(tw, m, (lane & 7) + 8 * ((lane >> 3) & 1));
+            for (int m = 0; m < 2; ++m) {
+              const int row = qk_token(tw, m, (lane & 7) + 8 * ((lane >> 3) & 1));
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              uint32_t a[4];
-              ldmatrix_x4(a, sst + kCRope + swz(row, 2 * ks + (lane >> 4)));
+              for (int ks = 0; ks < 4; ++ks) {
+                uint32_t a[4];
+                ldmatrix_x4(a, sst + kCRope + swz(row, 2 * ks + (lane >> 4)));
 #pragma unroll
-              for (int nt = 0; nt < 2; ++nt) {
-                const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
-                mma_bf16(S[m][nt], a, bq.x, bq.y);
+                for (int nt = 0; nt < 2; ++nt) {
+                  const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
+                  mma_bf16(S[m][nt], a, bq.x, bq.y);
+                }
               }
             }
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
           }
-#pragma unroll
-          for (int m = 0; m < 2; ++m)
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-              for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
           const uint4* qi = reinterpret_cast<const uint4*>(smem + kOffQi);
           // Group g's integer dot products (two int8 limbs of the query, both k-steps):
           // loads, code expansion and 16 MMAs into acc.
           auto qk_issue = [&](int g, int (&acc)[2][2][2][4]) {
-            // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens
+            // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens;
+            // group 8 (quantized RoPE keys): words 2tq and 2tq + 1 of the token's 32-byte RoPE code
+            // row, whose query limbs follow those of group 7 (k-steps 16 and 17)
             const int region = (g < 4) ? kCodesLo : kCodesHi;
             const int chunk = 2 * (g & 3) + (tq >> 1);
             uint2 v[2][2];
 #pragma unroll
             for (int m = 0; m < 2; ++m)
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
-                v[m][h] = *reinterpret_cast<const uint2*>(st + region + swz(tok[m][h], chunk) + 8 * (tq & 1));
+              for (int h = 0; h < 2; ++h) {
+                const int off = (kRopeQ && g == 8) ? kCRope + 32 * tok[m][h] + 8 * tq
+                                                   : region + swz(tok[m][h], chunk) + 8 * (tq & 1);
+                v[m][h] = *reinterpret_cast<const uint2*>(st + off);
+              }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
               const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
@@ -781,7 +869,35 @@ __global__ void __launch_bounds__(kThreads, 1)
           // two groups in flight: group g + 1's MMAs run on the tensor pipe while
           // group g's accumulators are scaled into S
           int accA[2][2][2][4], accB[2][2][2][4];
-          qk_issue(0, accA);
+          if constexpr (kRopeQ) {
+            // group 8, the quantized RoPE keys, first: its MMAs overlap group 0's, then
+            // S = (256 hi + lo) x token scale x (latent / RoPE fixed-point scales), both limbs'
+            // biases subtracted exactly (packed f32x2: elements 2h, 2h + 1 are token tok[m][h]
+            // against rows 8nt + 2tq + {0, 1})
+            qk_issue(8, accB);
+            qk_issue(0, accA);
+            // (the scales were copied from the 8-token boundary below the tile's first token
+            // page * page_tokens + off; page_tokens is a multiple of 16, so that is off & 7 tokens back)
+            const __half* rsc = reinterpret_cast<const __half*>(st + kCRopeScale) + (t.off & 7);
+            const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+              for (int h = 0; h < 2; ++h) {
+                const float rs = __half2float(rsc[tok[m][h]]);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                  const float2 fh = add2(make_float2(__int_as_float(accB[0][m][nt][2 * h]), __int_as_float(accB[0][m][nt][2 * h + 1])), bias2);
+                  const float2 fl = add2(make_float2(__int_as_float(accB[1][m][nt][2 * h]), __int_as_float(accB[1][m][nt][2 * h + 1])), bias2);
+                  const float2 w = mul2(make_float2(rs, rs), make_float2(rratio[nt][0], rratio[nt][1]));
+                  const float2 r = mul2(fma2(fh, k256, fl), w);
+                  S[m][nt][2 * h] = r.x;
+                  S[m][nt][2 * h + 1] = r.y;
+                }
+              }
+          } else {
+            qk_issue(0, accA);
+          }
 #pragma unroll 1
           for (int g = 0; g < 8; g += 2) {
             qk_issue(g + 1, accB);
@@ -1510,15 +1626,19 @@ int validate(const asterq_decode_params* p) {
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: negative table size");
   if (p->n_items > 0 && (!p->items || !p->tiles || !p->q_lat || !p->q_rope || !p->out))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null pointer");
+  if (p->rope_scheme != ASTERQ_ROPE_BF16 && p->rope_scheme != ASTERQ_ROPE_QUANTIZED)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: rope scheme %d unsupported (bf16 or quantized)", p->rope_scheme);
   if (p->n_cold_pages > 0 && (!p->cold_codes || !p->cold_scales || !p->cold_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null cold pool");
+  if (p->n_cold_pages > 0 && p->rope_scheme == ASTERQ_ROPE_QUANTIZED && !p->cold_rope_scales)
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: quantized RoPE keys need cold_rope_scales");
   if (p->n_hot_pages > 0 && (!p->hot_latent || !p->hot_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null hot pool");
   if (p->n_items > 0 && p->total_q > 0 && (!p->new_latent || !p->new_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null new-token arrays");
   const void* aligned[] = {p->q_lat, p->q_rope, p->new_latent, p->new_rope, p->cold_codes, p->cold_scales,
                            p->cold_rope, p->hot_latent, p->hot_rope, p->tiles, p->items, p->combine, p->out,
-                           p->workspace};
+                           p->workspace, p->cold_rope_scales};
   for (const void* ptr : aligned)
     if (reinterpret_cast<uintptr_t>(ptr) & 15)
       return set_error(ASTERQ_ERR_MISALIGNED, "decode: pointers must be 16-byte aligned");
@@ -1618,18 +1738,23 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     static unsigned long long configured = 0;  // one bit per device ordinal
     if (dev >= 64 || !(configured & (1ull << dev))) {
       cudaError_t e =
-          cudaFuncSetAttribute(dec::decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
+          cudaFuncSetAttribute(dec::decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
+      if (e == cudaSuccess)
+        e = cudaFuncSetAttribute(dec::decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(dec::qprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kPrepSmem);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
       // the score/value register split (setmaxnreg) assumes exactly kLaunchRegs per thread at launch:
       // refuse to launch a build that allocates fewer (an increase could then never be granted)
-      cudaFuncAttributes fa;
-      e = cudaFuncGetAttributes(&fa, dec::decode_kernel);
-      if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
-      if (fa.numRegs != dec::kLaunchRegs)
-        return set_error(ASTERQ_ERR_CUDA, "latent_decode: kernel built with %d registers per thread, the register split needs %d",
-                         fa.numRegs, dec::kLaunchRegs);
+      for (const void* fn : {reinterpret_cast<const void*>(dec::decode_kernel<false>),
+                             reinterpret_cast<const void*>(dec::decode_kernel<true>)}) {
+        cudaFuncAttributes fa;
+        e = cudaFuncGetAttributes(&fa, fn);
+        if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
+        if (fa.numRegs != dec::kLaunchRegs)
+          return set_error(ASTERQ_ERR_CUDA, "latent_decode: kernel built with %d registers per thread, the register split needs %d",
+                           fa.numRegs, dec::kLaunchRegs);
+      }
       if (dev < 64) configured |= (1ull << dev);
     }
     dec::TensorMaps maps;
@@ -1638,7 +1763,9 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     const void* dummy = p->q_lat;
     const int64_t cold_rows = p->n_cold_pages * p->page_tokens, hot_rows = p->n_hot_pages * p->page_tokens;
     if ((st = dec::make_map(&maps.codes, p->cold_codes, cold_rows, 256, dec::kColdTile, dummy, 1024, 2)) ||
-        (st = dec::make_map(&maps.crope, p->cold_rope, cold_rows, 128, dec::kColdTile, dummy, 1024)) ||
+        // (quantized RoPE codes come in by plain bulk copies: no tensor map over their pool)
+        (st = dec::make_map(&maps.crope, p->rope_scheme == ASTERQ_ROPE_BF16 ? p->cold_rope : nullptr, cold_rows,
+                            128, dec::kColdTile, dummy, 1024)) ||
         (st = dec::make_map(&maps.hlat, p->hot_latent, hot_rows, 1024, dec::kHotTile, dummy, 1024, 8)) ||
         (st = dec::make_map(&maps.hrope, p->hot_rope, hot_rows, 128, dec::kHotTile, dummy, 1024)) ||
         (st = dec::make_map(&maps.nlat, p->new_latent, p->total_q, 1024, dec::kHotTile, dummy, 1024, 8)) ||
@@ -1663,7 +1790,9 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      cudaError_t e = cudaLaunchKernelEx(&cfg, dec::decode_kernel, kp, maps);
+      cudaError_t e = (kp.rope_scheme == ASTERQ_ROPE_QUANTIZED)
+                          ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<true>, kp, maps)
+                          : cudaLaunchKernelEx(&cfg, dec::decode_kernel<false>, kp, maps);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: launch failed: %s", cudaGetErrorString(e));
     }
     st = check_launch("latent_decode");

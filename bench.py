@@ -847,7 +847,7 @@ def extras(dev, args) -> dict:
 
     from asterq.decode import DeviceDecodePlan, capture_step, latent_decode
     from asterq.plan import build_plan
-    from asterq.synth import c1_inputs, c4_workload, c5_workload, PoolBuilder
+    from asterq.synth import c1_inputs, c3_workload, c4_workload, c5_workload, PoolBuilder
 
     peak, _ = measured_peaks()
     res = {}
@@ -873,6 +873,10 @@ def extras(dev, args) -> dict:
     b1 = PoolBuilder([8192], [1024], q_len=1, n_heads=16, device=dev)
     b1.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
     decode_rate(b1.finish("C1"), "c1_single_sequence", 50)
+    # C3 with quantize_rope=True: cold RoPE keys as INT4 codes (306 instead of 400 bytes a cold token)
+    wl = c3_workload(dev, seed=1000, quantize_rope=True)
+    decode_rate(wl, "c3_quantize_rope_1gpu", 20)
+    del wl
     wl = c4_workload(dev)
     decode_rate(wl, "c4_long_context_1gpu", 30)
     del wl

@@ -53,6 +53,12 @@ extern "C" {
 #define ASTERQ_SCHEME_INT4 1
 #define ASTERQ_SCHEME_INT8 2
 
+/* cold RoPE keys (cache.py:160-164: quantized only with quantize_rope=True) */
+#define ASTERQ_ROPE_BF16 0      /* cold_rope: bf16 [tokens][rope_dim] */
+#define ASTERQ_ROPE_QUANTIZED 1 /* cold_rope: [tokens][rope_dim/2] u8 codes of the cold scheme, one scale
+                                   group of rope_dim (Hadamard-rotated for hadamard_int4);
+                                   cold_rope_scales: fp16 [tokens] */
+
 /* tile kinds in the decode schedule */
 #define ASTERQ_TILE_COLD 0 /* tokens of a cold page: INT4 codes + fp16 scales + bf16 RoPE key */
 #define ASTERQ_TILE_HOT 1  /* tokens of a hot page: bf16 latent + bf16 RoPE key */
@@ -102,7 +108,9 @@ int asterq_codec_status(int32_t* timeouts);
  * Layout in device memory (all row-major, token-major):
  *   cold_codes  uint8 [n_cold_pages, page_tokens, latent_dim/2]   rotated INT4 codes (kv.py:41-48 packing)
  *   cold_scales fp16  [n_cold_pages, page_tokens, latent_dim/64]
- *   cold_rope   bf16  [n_cold_pages, page_tokens, rope_dim]
+ *   cold_rope   bf16  [n_cold_pages, page_tokens, rope_dim]        (rope_scheme ASTERQ_ROPE_BF16), or
+ *               uint8 [n_cold_pages, page_tokens, rope_dim/2]      (ASTERQ_ROPE_QUANTIZED: INT4 codes)
+ *   cold_rope_scales fp16 [n_cold_pages, page_tokens]              (ASTERQ_ROPE_QUANTIZED only)
  *   hot_latent  bf16  [n_hot_pages, page_tokens, latent_dim]
  *   hot_rope    bf16  [n_hot_pages, page_tokens, rope_dim]
  *   q_lat       bf16  [total_q, n_heads, latent_dim]   absorbed query q_content @ W_k
@@ -180,6 +188,12 @@ typedef struct asterq_decode_params {
                                  query blocks beyond counts[1] are not prepared, jobs [0, counts[6])
                                  run in the combine launch (n_combine is its grid), the others in
                                  the decode kernel.  NULL: the sizes above are exact. */
+  int32_t rope_scheme;        /* ASTERQ_ROPE_BF16 (0) or ASTERQ_ROPE_QUANTIZED: the cold RoPE keys are
+                                 INT4 codes of the cold scheme with one fp16 scale per token
+                                 (LatentLayerCache quantize_rope=True, cache.py:160-164 -> kv.py:76-118);
+                                 the kernel scores them on the int8 tensor path like a ninth latent
+                                 group.  Hot and new tokens keep bf16 RoPE keys. */
+  const void* cold_rope_scales; /* fp16 [n_cold_pages * page_tokens], 16-byte aligned (quantized RoPE) */
 } asterq_decode_params;
 
 /*

@@ -195,7 +195,12 @@ def dequantize(q: Quantized) -> np.ndarray:
 
 @dataclass
 class ColdChunk:
-    """One cold chunk: packed codes [n, D/2] u8, scales [n, D/G] f16, RoPE [n, R] f32."""
+    """One cold chunk: packed codes [n, D/2] u8, scales [n, D/G] f16, RoPE [n, R] f32.
+
+    With ``quantize_rope`` (cache.py:160-164) the RoPE keys are stored like the latent
+    (``rope_codes`` [n, R/2] u8, ``rope_scales`` [n] f16, one group of R = 64) and ``rope``
+    holds their dequantized values (kv.py:121-134), which is what ``iter_chunks`` yields.
+    """
 
     codes: np.ndarray
     scales: np.ndarray
@@ -203,6 +208,8 @@ class ColdChunk:
     latent_dim: int
     group_size: int = 64
     scheme: str = "hadamard_int4"
+    rope_codes: np.ndarray | None = None
+    rope_scales: np.ndarray | None = None
 
     @property
     def length(self) -> int:
@@ -394,6 +401,21 @@ def merge_partials(parts: list[tuple[np.ndarray, np.ndarray, np.ndarray]]) -> np
     return (o / np.maximum(l, np.float32(1e-20))[..., None]).astype(np.float32)
 
 
+def cold_chunk(latent: np.ndarray, rope: np.ndarray, group_size: int = 64, scheme: str = "hadamard_int4",
+               quantize_rope: bool = False) -> ColdChunk:
+    """``LatentLayerCache._encode`` of one chunk (cache.py:160-164): the latent always, the RoPE
+    keys only with ``quantize_rope`` (else kept as they are)."""
+    q = quantize(latent, scheme, group_size)
+    chunk = ColdChunk(codes=q.data, scales=q.scale.reshape(latent.shape[0], -1), rope=rope.copy(),
+                      latent_dim=latent.shape[-1], group_size=group_size, scheme=scheme)
+    if quantize_rope:
+        qr = quantize(rope, scheme, group_size)
+        chunk.rope_codes = qr.data
+        chunk.rope_scales = qr.scale.reshape(rope.shape[0])
+        chunk.rope = dequantize(qr)
+    return chunk
+
+
 def build_cache_from_tokens(
     latent: np.ndarray,
     rope: np.ndarray,
@@ -401,6 +423,7 @@ def build_cache_from_tokens(
     chunk_tokens: int,
     group_size: int = 64,
     scheme: str = "hadamard_int4",
+    quantize_rope: bool = False,
 ) -> LatentCacheView:
     """Replay ``LatentLayerCache.append`` + ``_flush_cold_chunks`` (cache.py:167-201).
 
@@ -415,18 +438,8 @@ def build_cache_from_tokens(
     cold: list[ColdChunk] = []
     start = 0
     while latent.shape[0] - start > threshold:
-        piece = latent[start : start + chunk_tokens]
-        q = quantize(piece, scheme, group_size)
-        cold.append(
-            ColdChunk(
-                codes=q.data,
-                scales=q.scale.reshape(piece.shape[0], -1),
-                rope=rope[start : start + chunk_tokens].copy(),
-                latent_dim=latent.shape[-1],
-                group_size=group_size,
-                scheme=scheme,
-            )
-        )
+        cold.append(cold_chunk(latent[start : start + chunk_tokens], rope[start : start + chunk_tokens], group_size,
+                               scheme, quantize_rope))
         start += chunk_tokens
     return LatentCacheView(cold=cold, hot_latent=latent[start:].copy(), hot_rope=rope[start:].copy())
 
@@ -438,6 +451,7 @@ def build_cache_split(
     chunk_tokens: int,
     group_size: int = 64,
     scheme: str = "hadamard_int4",
+    quantize_rope: bool = False,
 ) -> LatentCacheView:
     """Cold/hot split used by the ragged workloads: the newest ``hot_tokens``
     stay hot, the rest is cut oldest-first into ``chunk_tokens`` chunks whose
@@ -450,17 +464,7 @@ def build_cache_split(
     cold = []
     for start in range(0, n_cold, chunk_tokens):
         end = min(start + chunk_tokens, n_cold)
-        q = quantize(latent[start:end], scheme, group_size)
-        cold.append(
-            ColdChunk(
-                codes=q.data,
-                scales=q.scale.reshape(end - start, -1),
-                rope=rope[start:end].copy(),
-                latent_dim=latent.shape[-1],
-                group_size=group_size,
-                scheme=scheme,
-            )
-        )
+        cold.append(cold_chunk(latent[start:end], rope[start:end], group_size, scheme, quantize_rope))
     return LatentCacheView(cold=cold, hot_latent=latent[n_cold:].copy(), hot_rope=rope[n_cold:].copy())
 
 

@@ -69,16 +69,17 @@ def fake_attention(dtype: torch.dtype, n_heads: int = H):
     )
 
 
-def reference_cache(lat, rope, recent, chunk, group=64):
-    cache = LatentLayerCache(cache_dtype="hadamard_int4", group_size=group, recent_tokens=recent, chunk_tokens=chunk)
+def reference_cache(lat, rope, recent, chunk, group=64, scheme="hadamard_int4", quantize_rope=False):
+    cache = LatentLayerCache(cache_dtype=scheme, group_size=group, recent_tokens=recent, chunk_tokens=chunk,
+                             quantize_rope=quantize_rope)
     cache.append(lat.unsqueeze(0), rope.unsqueeze(0), window_size=None, sink_tokens=0)
     return cache
 
 
-def decode_case(seed, ctx, q_len, recent, chunk):
+def decode_case(seed, ctx, q_len, recent, chunk, scheme="hadamard_int4", quantize_rope=False):
     inp = c1_inputs(seed=seed, ctx=ctx, q_len=q_len)
     lat, rope, q, qr = inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"]
-    cache = reference_cache(lat[:ctx], rope[:ctx], recent, chunk)
+    cache = reference_cache(lat[:ctx], rope[:ctx], recent, chunk, scheme=scheme, quantize_rope=quantize_rope)
     outs = {}
     for name, dtype in (("fp32", torch.float32), ("bf16", torch.bfloat16)):
         f = fake_attention(dtype)
@@ -98,6 +99,8 @@ def decode_case(seed, ctx, q_len, recent, chunk):
         "out_bf16": outs["bf16"],
         "codes_sha256": sha(*[c.data for c in cache.cold_latent]),
         "scales_sha256": sha(*[c.scale for c in cache.cold_latent]),
+        **({"rope_codes_sha256": sha(*[c.data for c in cache.cold_rope]),
+            "rope_scales_sha256": sha(*[c.scale for c in cache.cold_rope])} if quantize_rope else {}),
     }
 
 
@@ -139,6 +142,15 @@ def main() -> None:
     q4 = quantize_tensor(tie, "int4", group_size=16)
     fixtures["tie_int4_codes"] = q4.data.numpy()
     fixtures["tie_int4_scales"] = q4.scale.numpy()
+    # RoPE keys as the cache quantizes them with quantize_rope=True (cache.py:160-164): [tokens, 64],
+    # one group of 64, for both INT4 schemes
+    g = torch.Generator().manual_seed(9)
+    xr = (torch.randn(96, R, generator=g) * torch.linspace(0.1, 6.0, R)).to(torch.bfloat16)
+    fixtures["rope_x_bits"] = bf16_bits(xr)
+    for scheme in ("hadamard_int4", "int4"):
+        qr = quantize_tensor(xr, scheme, group_size=64)
+        fixtures[f"rope_{scheme}_codes"] = qr.data.numpy()
+        fixtures[f"rope_{scheme}_scales"] = qr.scale.numpy().reshape(xr.shape[0])
     np.savez_compressed(HERE / "encode_golden.npz", **fixtures)
 
     # ---- decode -----------------------------------------------------------------
@@ -151,6 +163,9 @@ def main() -> None:
         "hotonly": dict(seed=4, ctx=700, q_len=1, recent=512, chunk=512),
         # q_len = 3 causal verification over a populated cache (config 5 shape)
         "t3": dict(seed=5, ctx=4096, q_len=3, recent=512, chunk=512),
+        # quantize_rope=True: the cold chunks' RoPE keys quantized too (cache.py:160-164)
+        "qrope": dict(seed=6, ctx=2200, q_len=1, recent=512, chunk=512, quantize_rope=True),
+        "qr4": dict(seed=8, ctx=2700, q_len=1, recent=512, chunk=512, scheme="int4", quantize_rope=True),
     }
     dec: dict[str, np.ndarray] = {}
     for name, kw in cases.items():

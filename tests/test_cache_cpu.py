@@ -12,10 +12,19 @@ def test_unsupported_configurations_raise():
         LatentLayerCache("int8")
     with pytest.raises(NotImplementedError):
         LatentLayerCache("hadamard_int4", group_size=32)
-    with pytest.raises(NotImplementedError):
-        LatentLayerCache("hadamard_int4", quantize_rope=True)
     with pytest.raises(ValueError):
         LatentLayerCache("hadamard_int4", chunk_tokens=100)
+
+
+def test_quantize_rope_is_accepted_for_every_kernel_scheme():
+    """quantize_rope=True (cache.py:64, :160-164) is served: the integer schemes store codes, bfloat16
+    never flushes, so its RoPE keys stay bf16 as in the reference."""
+    from asterq.cache import LatentLayerCache
+
+    for scheme in ("hadamard_int4", "int4", "bfloat16"):
+        c = LatentLayerCache(scheme, quantize_rope=True, chunk_tokens=512)
+        assert c.quantize_rope and c._rope_quantized == (scheme != "bfloat16")
+        assert c.num_bytes == 0
 
 
 def test_empty_cache_reports_nothing():

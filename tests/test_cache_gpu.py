@@ -126,6 +126,50 @@ def test_latent_attention_over_the_cache(cuda, q_len, scheme):
     assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2
 
 
+@pytest.mark.parametrize("scheme,dtype", [("hadamard_int4", torch.bfloat16), ("int4", torch.bfloat16),
+                                          ("hadamard_int4", torch.float32)])
+def test_quantize_rope_cache_matches_reference(cuda, scheme, dtype):
+    """quantize_rope=True (cache.py:64, :160-164): each flushed chunk's RoPE keys are quantized from
+    the values as stored (the caller's dtype) with the cold scheme, one group of 64 -- codes and
+    scales bit-exact to quantize_tensor, the reference's byte accounting (32 code bytes and one fp16
+    scale a token), dequantized views bit-exact -- and attention reads the codes directly (q_len 1
+    and 3, within the decode tolerance)."""
+    from asterq.attention import latent_attention
+    from asterq.cache import LatentLayerCache
+    from asterq.kv import QuantizedTensor
+
+    n = 3300
+    inp = _inputs(41, n, 3)
+    lat, rope = inp["latent"].to(dtype), inp["rope"].to(dtype)
+    cache = LatentLayerCache(scheme, 64, recent_tokens=512, chunk_tokens=512, quantize_rope=True)
+    cache.append(lat[None, :1200].to(cuda), rope[None, :1200].to(cuda), None, 0)
+    cache.append(lat[None, 1200:n].to(cuda), rope[None, 1200:n].to(cuda), None, 0)
+    lat_np, rope_np = lat.float().numpy(), rope.float().numpy()
+    ref = O.build_cache_from_tokens(lat_np[:n], rope_np[:n], 512, 512, scheme=scheme, quantize_rope=True)
+    assert cache.cold_chunks == len(ref.cold) > 0 and cache.length == n
+    for q, r, c in zip(cache.cold_latent, cache.cold_rope, ref.cold):
+        np.testing.assert_array_equal(q.data[0].cpu().numpy(), c.codes)
+        assert isinstance(r, QuantizedTensor) and r.scheme == scheme and r.original_shape == (1, 512, 64)
+        np.testing.assert_array_equal(r.data[0].cpu().numpy(), c.rope_codes)
+        np.testing.assert_array_equal(r.scale[0, :, 0, 0].cpu().numpy(), c.rope_scales)
+    cold = cache.cold_length
+    assert cache.num_bytes == cold * (256 + 16 + 32 + 2) + (n - cold) * (512 + 64) * dtype.itemsize
+    got_rope = cache.materialize_rope(dtype=torch.float32)[0].cpu().numpy()
+    np.testing.assert_array_equal(got_rope, ref.materialize()[1])
+
+    bf = O.round_bf16
+    view = ref if dtype == torch.bfloat16 else O.LatentCacheView(
+        cold=ref.cold, hot_latent=bf(ref.hot_latent), hot_rope=bf(ref.hot_rope))
+    for q_len in (1, 3):
+        out = latent_attention(inp["q_lat"][None, :q_len].to(cuda), inp["q_rope"][None, :q_len].to(cuda),
+                               lat[None, n:n + q_len].to(cuda), rope[None, n:n + q_len].to(cuda), cache,
+                               softmax_scale=SCALE)
+        want = O.decode(_bf16_np(inp["q_lat"][:q_len]), _bf16_np(inp["q_rope"][:q_len]), bf(lat_np[n:n + q_len]),
+                        bf(rope_np[n:n + q_len]), view, SCALE)
+        got = out[0].cpu().numpy()
+        assert O.rel_l2(got, want) <= 1e-3 and O.max_abs(got, want) <= 2e-2, q_len
+
+
 def test_empty_cache_prefill_is_causal(cuda):
     from asterq.attention import latent_attention
 

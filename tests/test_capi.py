@@ -4,6 +4,7 @@ from __future__ import annotations
 
 import ctypes
 import re
+import shutil
 import subprocess
 from pathlib import Path
 
@@ -42,14 +43,44 @@ def test_version_and_error_string():
 def test_struct_layout_matches_header():
     # sizes of the C struct: 6 int32 + 2 float + 3 int64 + 4 int32 + 14 pointers + int64 + 2 pointers + 2 int32
     # + the workers pointer + 2 int32 + the unit_jobs pointer + the int64 wait limit + the plan_counts pointer
-    size = 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8 + 8 + 8 + 2 * 4 + 8 + 2 * 4 + 8 + 8 + 8
+    # + the RoPE scheme int32 (+ padding) and the cold_rope_scales pointer
+    size = 6 * 4 + 2 * 4 + 3 * 8 + 4 * 4 + 14 * 8 + 8 + 8 + 8 + 2 * 4 + 8 + 2 * 4 + 8 + 8 + 8 + 8 + 8
     assert ctypes.sizeof(_lib.DecodeParams) == size
-    assert _lib.DecodeParams.workers.offset == size - 40
-    assert _lib.DecodeParams.wait_limit_cycles.offset == size - 16
-    assert _lib.DecodeParams.plan_counts.offset == size - 8
+    assert _lib.DecodeParams.workers.offset == size - 56
+    assert _lib.DecodeParams.wait_limit_cycles.offset == size - 32
+    assert _lib.DecodeParams.plan_counts.offset == size - 24
+    assert _lib.DecodeParams.rope_scheme.offset == size - 16
+    assert _lib.DecodeParams.cold_rope_scales.offset == size - 8
     # asterq_batch_desc: 6 int32 + 7 pointers; asterq_plan_buffers: 3 int32 (+ padding) + 8 pointers
     assert ctypes.sizeof(_lib.BatchDesc) == 6 * 4 + 7 * 8
     assert ctypes.sizeof(_lib.PlanBuffers) == 16 + 8 * 8 and _lib.PlanBuffers.tiles.offset == 16
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs a C compiler")
+def test_ctypes_mirrors_match_the_c_compiler(tmp_path):
+    """Every field offset and struct size of the ctypes mirrors equals what a C compiler lays out
+    from include/asterq.h."""
+    structs = {"asterq_decode_params": _lib.DecodeParams, "asterq_batch_desc": _lib.BatchDesc,
+               "asterq_plan_buffers": _lib.PlanBuffers}
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "asterq.h"', "int main(void) {"]
+    for cname, cls in structs.items():
+        lines.append(f'  printf("{cname} sizeof %zu\\n", sizeof({cname}));')
+        for fname, _ in cls._fields_:
+            lines.append(f'  printf("{cname} {fname} %zu\\n", offsetof({cname}, {fname}));')
+    lines += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    include = Path(__file__).resolve().parent.parent / "include"
+    subprocess.run(["gcc", "-std=c11", "-I", str(include), str(src), "-o", str(exe)], check=True)
+    got = {}
+    for line in subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.splitlines():
+        cname, fname, value = line.split()
+        got[(cname, fname)] = int(value)
+    for cname, cls in structs.items():
+        assert got[(cname, "sizeof")] == ctypes.sizeof(cls), cname
+        for fname, _ in cls._fields_:
+            assert got[(cname, fname)] == getattr(cls, fname).offset, (cname, fname)
 
 
 def test_quantize_rejects_bad_sizes_without_touching_the_gpu():
@@ -123,7 +154,7 @@ def test_decode_noop_and_workspace_query():
     assert lib.asterq_decode_workspace_bytes(ctypes.byref(p)) == 3 * 16 * 514 * 4
     # + the prepared query blocks and one counter per unit (fused combine), rounded to 16 bytes
     p.n_units = 5
-    assert lib.asterq_decode_workspace_bytes(ctypes.byref(p)) == 3 * 16 * 514 * 4 + 5 * 35328 + 32
+    assert lib.asterq_decode_workspace_bytes(ctypes.byref(p)) == 3 * 16 * 514 * 4 + 5 * 37376 + 32
 
 
 def test_plan_workspace_matches_the_library():

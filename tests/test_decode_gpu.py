@@ -58,30 +58,35 @@ def run_decode(wl, *, out_dtype=torch.float32, softcap=None, **plan_kw):
     return out, plan
 
 
-def single_sequence_workload(inp, ctx, hot, q_len, device, scheme="hadamard_int4"):
+def single_sequence_workload(inp, ctx, hot, q_len, device, scheme="hadamard_int4", quantize_rope=False):
     from asterq.synth import PoolBuilder
 
-    b = PoolBuilder([ctx], [hot], q_len=q_len, n_heads=inp["q_lat"].shape[1], device=device, scheme=scheme)
+    b = PoolBuilder([ctx], [hot], q_len=q_len, n_heads=inp["q_lat"].shape[1], device=device, scheme=scheme,
+                    quantize_rope=quantize_rope)
     b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
     return b.finish("single")
 
 
-def oracle_for(inp, ctx, hot, q_len, softcap=None, chunk=512, scheme="hadamard_int4"):
+def oracle_for(inp, ctx, hot, q_len, softcap=None, chunk=512, scheme="hadamard_int4", quantize_rope=False):
     lat = inp["latent"].float().numpy()
     rope = inp["rope"].float().numpy()
-    cache = O.build_cache_split(lat[:ctx], rope[:ctx], hot, chunk, scheme=scheme)
+    cache = O.build_cache_split(lat[:ctx], rope[:ctx], hot, chunk, scheme=scheme, quantize_rope=quantize_rope)
     return O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[ctx:], rope[ctx:], cache,
                     SCALE, softcap)
 
 
-@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3"])
+@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4"])
 def test_decode_matches_reference_golden(cuda, golden_decode, case):
+    """The reference's own outputs; "qrope" / "qr4": quantize_rope=True caches (cold RoPE keys as
+    hadamard_int4 / int4 codes, cache.py:160-164)."""
     from asterq.synth import c1_inputs
 
     g = {k[len(case) + 1:]: v for k, v in golden_decode.items() if k.startswith(case + "_")}
     ctx, q_len = int(g["ctx"]), int(g["q_len"])
     inp = c1_inputs(seed=int(g["seed"]), ctx=ctx, q_len=q_len)
-    wl = single_sequence_workload(inp, ctx, int(g["hot_tokens"]), q_len, cuda)
+    scheme = str(g["scheme"]) if "scheme" in g else "hadamard_int4"
+    quantize_rope = bool(g["quantize_rope"]) if "quantize_rope" in g else False
+    wl = single_sequence_workload(inp, ctx, int(g["hot_tokens"]), q_len, cuda, scheme, quantize_rope)
     ref = g["out_fp32"]
     out32, _ = run_decode(wl, out_dtype=torch.float32)
     assert_close(out32.cpu().numpy(), ref, f"{case} fp32")
@@ -160,6 +165,50 @@ def test_plain_int4_cold_scheme(cuda, q_len):
     assert plan.n_slots > 2
     assert_close(one.cpu().numpy(), ref, f"int4 q_len {q_len}")
     assert_close(many.cpu().numpy(), ref, f"int4 q_len {q_len} split")
+
+
+@pytest.mark.parametrize("scheme,q_len", [("hadamard_int4", 1), ("hadamard_int4", 3), ("int4", 1), ("int4", 2)])
+def test_quantized_rope_ragged_batch(cuda, scheme, q_len):
+    """Cold RoPE keys stored as INT4 codes + one scale per token (quantize_rope=True): ragged
+    lengths with partial cold pages (tiles of 1..128 tokens), hot windows and a cold-only sequence."""
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    lengths, hot = [1300, 700, 2600, 129, 1031], [300, 0, 1000, 1, 7]
+    b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=16, device=cuda, scheme=scheme, quantize_rope=True)
+    refs = []
+    for i, (n, h) in enumerate(zip(lengths, hot)):
+        inp = c1_inputs(seed=60 + i, ctx=n, q_len=q_len)
+        b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+        refs.append(oracle_for(inp, n, h, q_len, scheme=scheme, quantize_rope=True))
+    wl = b.finish("quantized rope")
+    out, _ = run_decode(wl)
+    out = out.cpu().numpy()
+    for i, ref in enumerate(refs):
+        assert_close(out[i * q_len:(i + 1) * q_len], ref, f"sequence {i}")
+    split, plan = run_decode(wl, n_sms=16, ctas_per_sm=2, waves=4)
+    assert plan.n_slots > 0
+    assert O.rel_l2(split.cpu().numpy(), out) < 1e-4
+
+
+def test_quantized_rope_cold_tiles_at_any_offset(cuda):
+    """Cold tiles that start and end off the 8-token grid of the RoPE scale copies: the layout
+    takes tokens 5..511 of the first cold page, all of the second and 100 tokens from offset 3
+    of the third."""
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    n, h, q_len = 1500, 300, 2
+    inp = c1_inputs(seed=71, ctx=n, q_len=q_len)
+    b = PoolBuilder([n], [h], q_len=q_len, n_heads=16, device=cuda, quantize_rope=True)
+    b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    wl = b.finish("offsets")
+    (p0, _, _), (p1, _, _), (p2, _, _) = wl.layouts[0].cold
+    wl.layouts[0].cold = [(p0, 5, 507), (p1, 0, 512), (p2, 3, 100)]
+    out, _ = run_decode(wl)
+    lat, rope = inp["latent"].float().numpy(), inp["rope"].float().numpy()
+    keep = np.r_[5:512, 512:1024, 1027:1127, n - h:n]
+    cache = O.build_cache_split(lat[keep], rope[keep], h, 512, quantize_rope=True)
+    ref = O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[n:], rope[n:], cache, SCALE)
+    assert_close(out.cpu().numpy(), ref, "offsets")
 
 
 def test_n_heads_not_multiple_of_16(cuda):

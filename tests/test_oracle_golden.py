@@ -68,7 +68,17 @@ def test_fwht_is_self_inverse():
     np.testing.assert_allclose(O.normalized_fwht(O.normalized_fwht(x)), x, atol=1e-5)
 
 
-@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3"])
+@pytest.mark.parametrize("scheme", ["hadamard_int4", "int4"])
+def test_oracle_rope_quantization_matches_reference(golden_encode, scheme):
+    """quantize_rope=True encodes [tokens, 64] RoPE keys as one group of 64 (cache.py:160-164)."""
+    x = O.bf16_to_f32(golden_encode["rope_x_bits"])
+    q = O.quantize(x, scheme, 64)
+    np.testing.assert_array_equal(q.data, golden_encode[f"rope_{scheme}_codes"])
+    np.testing.assert_array_equal(q.scale.reshape(-1).view(np.uint16),
+                                  golden_encode[f"rope_{scheme}_scales"].view(np.uint16))
+
+
+@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4"])
 def test_oracle_decode_matches_reference(golden_decode, case):
     g = {k[len(case) + 1:]: v for k, v in golden_decode.items() if k.startswith(case + "_")}
     ctx, q_len = int(g["ctx"]), int(g["q_len"])
@@ -76,8 +86,13 @@ def test_oracle_decode_matches_reference(golden_decode, case):
     assert _sha(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"]) == str(g["input_sha256"])
     lat = inp["latent"].float().numpy()
     rope = inp["rope"].float().numpy()
-    cache = O.build_cache_from_tokens(lat[:ctx], rope[:ctx], int(g["recent"]), int(g["chunk"]))
+    scheme = str(g["scheme"]) if "scheme" in g else "hadamard_int4"
+    quantize_rope = bool(g["quantize_rope"]) if "quantize_rope" in g else False
+    cache = O.build_cache_from_tokens(lat[:ctx], rope[:ctx], int(g["recent"]), int(g["chunk"]), scheme=scheme,
+                                      quantize_rope=quantize_rope)
     assert len(cache.cold) == int(g["cold_chunks"])
+    if quantize_rope:
+        assert _sha(*[torch.from_numpy(c.rope_codes) for c in cache.cold]) == str(g["rope_codes_sha256"])
     assert cache.hot_latent.shape[0] == int(g["hot_tokens"])
     out = O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[ctx:], rope[ctx:], cache, SCALE)
     ref = g["out_fp32"]
