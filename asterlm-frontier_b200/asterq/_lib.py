@@ -139,6 +139,7 @@ class BatchDesc(ctypes.Structure):
         ("hot_pages", ctypes.c_void_p),
         ("q_len", ctypes.c_void_p),
         ("q_start", ctypes.c_void_p),
+        ("cold_tile_tokens", ctypes.c_int32),
     ]
 
 

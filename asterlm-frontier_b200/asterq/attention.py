@@ -24,7 +24,7 @@ import math
 import torch
 
 from .cache import LatentLayerCache
-from .decode import LATENT_DIM, ROPE_DIM, DeviceDecodePlan, LatentPools, latent_decode
+from .decode import COLD_TILE_TOKENS, LATENT_DIM, ROPE_DIM, DeviceDecodePlan, LatentPools, latent_decode
 from .plan import MAX_Q_LEN, SequenceLayout, build_plan
 
 
@@ -83,6 +83,7 @@ def latent_attention(
         pools = _empty_pools(dev)
         layouts = [SequenceLayout(q_start=b * t, q_len=t) for b in range(bsz)]
     # host-built schedule: an empty cache, or explicit planner options (plan_kw)
+    plan_kw.setdefault("cold_tile", COLD_TILE_TOKENS.get(pools.cold_scheme, 128))
     plan = build_plan(layouts, n_heads, **plan_kw)
     dplan = DeviceDecodePlan(plan, dev)
     out = latent_decode(pools, dplan, *args, softmax_scale=softmax_scale, logit_softcap=logit_softcap,

@@ -179,13 +179,15 @@ class DevicePlanner:
     """
 
     def __init__(self, tables: BatchTables, n_heads: int, page_tokens: int, *, max_q_len: int = 1,
-                 n_workers: int | None = None) -> None:
+                 n_workers: int | None = None, cold_tile: int = COLD_TILE) -> None:
         if not 0 < max_q_len <= MAX_Q_LEN:
             raise ValueError(f"max_q_len must be in 1..{MAX_Q_LEN}")
         if page_tokens <= 0 or page_tokens % 16:
             raise ValueError("page_tokens must be a positive multiple of 16")
         self.tables = tables
-        self.n_heads, self.page_tokens, self.max_q_len = n_heads, page_tokens, max_q_len
+        if cold_tile not in (64, COLD_TILE):
+            raise ValueError("cold_tile must be 64 (int8 codes) or 128")
+        self.n_heads, self.page_tokens, self.max_q_len, self.cold_tile = n_heads, page_tokens, max_q_len, cold_tile
         dev = tables.device
         if n_workers is None:
             n_workers = torch.cuda.get_device_properties(dev).multi_processor_count
@@ -196,7 +198,7 @@ class DevicePlanner:
     def _alloc(self) -> None:
         t, P, S = self.tables, self.page_tokens, self.tables.n_seqs
         dev = t.device
-        per_seq = (t.max_cold_pages * math.ceil(P / COLD_TILE) + t.max_hot_pages * math.ceil(P / HOT_TILE)
+        per_seq = (t.max_cold_pages * math.ceil(P / self.cold_tile) + t.max_hot_pages * math.ceil(P / HOT_TILE)
                    + math.ceil(self.max_q_len / HOT_TILE))
         self.cap_tiles = max(1, S * per_seq)
         self.cap_units = max(1, S * math.ceil(self.max_q_len * self.n_heads / ROWS_PER_BLOCK))
@@ -210,6 +212,7 @@ class DevicePlanner:
         self.workers = torch.zeros(self.n_workers + 1, dtype=i32, device=dev)
         self.counts = torch.zeros(8, dtype=i32, device=dev)
         self.desc = t.desc(self.n_heads, self.page_tokens, self.n_workers)
+        self.desc.cold_tile_tokens = self.cold_tile
         nbytes = _lib.load().asterq_plan_scratch_bytes(ctypes.byref(self.desc), self.cap_tiles, self.cap_units,
                                                        self.cap_items)
         if nbytes <= 0:
@@ -327,8 +330,8 @@ class PagedLatentBatch:
                  hot_pool_pages: int | None = None, cold_pool_pages: int | None = None,
                  n_workers: int | None = None, plan_ahead: bool = False, window_size: int | None = None,
                  sink_tokens: int = 0, device="cuda") -> None:
-        if cache_dtype not in COLD_SCHEMES:
-            raise NotImplementedError(f"cache_dtype {cache_dtype!r}: the pools serve {tuple(COLD_SCHEMES)}")
+        if cache_dtype not in ("hadamard_int4", "int4"):
+            raise NotImplementedError(f"cache_dtype {cache_dtype!r}: the serving batch pools hadamard_int4 and int4")
         if not 0 < q_len <= page_tokens:
             raise ValueError("q_len must be in 1..page_tokens")
         self.device = torch.device(device)

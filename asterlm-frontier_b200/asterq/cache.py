@@ -40,12 +40,12 @@ from typing import Any
 import torch
 
 from . import _lib
-from .decode import GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools
+from .decode import COLD_TILE_TOKENS, GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools
 from .kv import QuantizedTensor, dequantize_tensor
 from .plan import SequenceLayout
 
-_KERNEL_SCHEMES = ("hadamard_int4", "int4", "bfloat16")
-_SCHEME_IDS = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4}
+_KERNEL_SCHEMES = ("hadamard_int4", "int4", "int8", "bfloat16")
+_SCHEME_IDS = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4, "int8": _lib.SCHEME_INT8}
 
 
 class _Pool:
@@ -107,11 +107,11 @@ class LatentLayerCache:
     """Hot/cold latent cache for one global-attention layer (cache.py:52).
 
     Same constructor fields and defaults as the reference.  The decode kernels
-    serve ``cache_dtype`` "hadamard_int4" and "int4" (cold chunks) and "bfloat16" (never
-    flushes, cache.py:169); ``group_size`` must be 64.  With ``quantize_rope`` the cold
-    chunks' RoPE keys are quantized with the cold scheme as well (cache.py:160-164: one
-    group of 64, 32 code bytes and one fp16 scale per token), and the kernel scores those
-    codes directly.
+    serve ``cache_dtype`` "hadamard_int4", "int4" and "int8" (cold chunks; int8 codes are one
+    signed byte a dim, 512 bytes a token) and "bfloat16" (never flushes, cache.py:169);
+    ``group_size`` must be 64.  With ``quantize_rope`` (INT4 schemes) the cold chunks' RoPE
+    keys are quantized with the cold scheme as well (cache.py:160-164: one group of 64, 32
+    code bytes and one fp16 scale per token), and the kernel scores those codes directly.
     """
 
     cache_dtype: str = "bfloat16"
@@ -140,6 +140,9 @@ class LatentLayerCache:
         if self.cache_dtype not in _KERNEL_SCHEMES:
             raise NotImplementedError(
                 f"cache_dtype {self.cache_dtype!r}: the asterq pools serve 'hadamard_int4', 'int4' and 'bfloat16'")
+        if self.cache_dtype == "int8" and self.quantize_rope:
+            raise NotImplementedError("quantize_rope=True with int8 chunks: the decode kernel reads quantized RoPE "
+                                      "keys with the INT4 schemes only")
         if self.cache_dtype in _SCHEME_IDS and self.group_size != GROUP_SIZE:
             raise NotImplementedError(f"group_size {self.group_size}: the decode kernels use groups of {GROUP_SIZE}")
         if self.chunk_tokens <= 0 or self.chunk_tokens % 16:
@@ -179,7 +182,7 @@ class LatentLayerCache:
         """Bytes the reference would account (cache.py:79-87): codes + scales + cold RoPE + hot tensors."""
         b, cold = self._batch, self.cold_length
         rope = (ROPE_DIM // 2 + 2) if self._rope_quantized else ROPE_DIM * 2  # codes + scale, or bf16
-        total = b * cold * (LATENT_DIM // 2 + (LATENT_DIM // GROUP_SIZE) * 2 + rope)
+        total = b * cold * (self._code_bytes + (LATENT_DIM // GROUP_SIZE) * 2 + rope)
         total += b * self._hot_len * (LATENT_DIM + ROPE_DIM) * self._dtype.itemsize
         return int(total)
 
@@ -194,7 +197,8 @@ class LatentLayerCache:
                 # bf16 operands the decode kernel reads
                 fields.update(src_latent=((LATENT_DIM,), dtype), src_rope=((ROPE_DIM,), dtype))
             self._hot = _Pool(fields, self.page_tokens, device)
-            cold = {"codes": ((LATENT_DIM // 2,), torch.uint8), "scales": ((LATENT_DIM // GROUP_SIZE,), torch.float16)}
+            code_dtype = torch.int8 if self.cache_dtype == "int8" else torch.uint8
+            cold = {"codes": ((self._code_bytes,), code_dtype), "scales": ((LATENT_DIM // GROUP_SIZE,), torch.float16)}
             if self._rope_quantized:
                 cold.update(rope=((ROPE_DIM // 2,), torch.uint8), rope_scales=((), torch.float16))
             else:
@@ -206,6 +210,11 @@ class LatentLayerCache:
             raise ValueError(f"batch size changed from {self._batch} to {batch}")
         elif dtype != self._dtype:
             raise ValueError(f"latent dtype changed from {self._dtype} to {dtype} (the hot window keeps one dtype)")
+
+    @property
+    def _code_bytes(self) -> int:
+        """Code bytes of a cold token: one a dim for int8, two dims a byte for the INT4 schemes."""
+        return LATENT_DIM if self.cache_dtype == "int8" else LATENT_DIM // 2
 
     @property
     def _rope_quantized(self) -> bool:
@@ -329,7 +338,8 @@ class LatentLayerCache:
         pl = st.planner
         if pl is None or pl.tables is not tables or pl.n_heads != n_heads or pl.max_q_len < q_len:
             max_q = max(q_len, pl.max_q_len if (pl is not None and pl.tables is tables) else 1)
-            st.planner = pl = DevicePlanner(tables, n_heads, self.page_tokens, max_q_len=max_q)
+            st.planner = pl = DevicePlanner(tables, n_heads, self.page_tokens, max_q_len=max_q,
+                                            cold_tile=COLD_TILE_TOKENS.get(self.cache_dtype, 128))
         return pl
 
     def raise_if_failed(self) -> None:
@@ -393,7 +403,7 @@ class LatentLayerCache:
         dst = torch.tensor(dst_pages, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         # quantized from the caller's values (cache.py:172 encodes the hot tensor as stored)
         x = self._hot[self._src + "latent"].index_select(0, src).reshape(bsz * P, LATENT_DIM)
-        codes = torch.empty(bsz * P, LATENT_DIM // 2, dtype=torch.uint8, device=dev)
+        codes = torch.empty(bsz * P, self._code_bytes, dtype=self._cold["codes"].dtype, device=dev)
         scales = torch.empty(bsz * P, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=dev)
         lib = _lib.load()
         _lib.check(lib.asterq_quantize(x.data_ptr(), _lib.dtype_code(x.dtype), bsz * P, LATENT_DIM, LATENT_DIM,

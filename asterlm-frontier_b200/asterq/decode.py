@@ -19,14 +19,16 @@ from .plan import DecodePlan
 LATENT_DIM = 512
 ROPE_DIM = 64
 GROUP_SIZE = 64
-COLD_SCHEMES = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4}
+COLD_SCHEMES = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4, "int8": _lib.SCHEME_INT8}
+# tokens of a cold tile per scheme (the host and device planners cut pages into such tiles)
+COLD_TILE_TOKENS = {"hadamard_int4": 128, "int4": 128, "int8": 64}
 
 
 @dataclass
 class LatentPools:
     """Device pools (layout documented in include/asterq.h)."""
 
-    cold_codes: torch.Tensor  # uint8 [Pc, page, 256]
+    cold_codes: torch.Tensor  # uint8 [Pc, page, 256] INT4 codes, or int8 [Pc, page, 512] (scheme "int8")
     cold_scales: torch.Tensor  # fp16 [Pc, page, 8]
     cold_rope: torch.Tensor  # bf16 [Pc, page, 64], or uint8 [Pc, page, 32] INT4 codes (quantized RoPE keys)
     hot_latent: torch.Tensor  # bf16 [Ph, page, 512]
@@ -46,7 +48,13 @@ class LatentPools:
 
     @staticmethod
     def empty(n_cold_pages: int, n_hot_pages: int, page_tokens: int, device, *,
-              quantize_rope: bool = False) -> "LatentPools":
+              quantize_rope: bool = False, cold_scheme: str = "hadamard_int4") -> "LatentPools":
+        if cold_scheme not in COLD_SCHEMES:
+            raise NotImplementedError(f"cold scheme {cold_scheme!r}: the decode kernels read {tuple(COLD_SCHEMES)}")
+        if cold_scheme == "int8":
+            codes = torch.empty(n_cold_pages, page_tokens, LATENT_DIM, dtype=torch.int8, device=device)
+        else:
+            codes = torch.empty(n_cold_pages, page_tokens, LATENT_DIM // 2, dtype=torch.uint8, device=device)
         if quantize_rope:
             cold_rope = torch.empty(n_cold_pages, page_tokens, ROPE_DIM // 2, dtype=torch.uint8, device=device)
             rope_scales = torch.empty(n_cold_pages, page_tokens, dtype=torch.float16, device=device)
@@ -54,12 +62,13 @@ class LatentPools:
             cold_rope = torch.empty(n_cold_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device)
             rope_scales = None
         return LatentPools(
-            cold_codes=torch.empty(n_cold_pages, page_tokens, LATENT_DIM // 2, dtype=torch.uint8, device=device),
+            cold_codes=codes,
             cold_scales=torch.empty(n_cold_pages, page_tokens, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=device),
             cold_rope=cold_rope,
             hot_latent=torch.empty(n_hot_pages, page_tokens, LATENT_DIM, dtype=torch.bfloat16, device=device),
             hot_rope=torch.empty(n_hot_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device),
             cold_rope_scales=rope_scales,
+            cold_scheme=cold_scheme,
         )
 
     @property
@@ -89,6 +98,9 @@ def set_cold_pools(p: _lib.DecodeParams, pools: LatentPools) -> None:
         p.cold_rope_scales = None
     if pools.cold_scheme not in COLD_SCHEMES:
         raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
+    width = LATENT_DIM if pools.cold_scheme == "int8" else LATENT_DIM // 2
+    if pools.cold_codes.numel() and (pools.cold_codes.shape[-1] != width or pools.cold_codes.element_size() != 1):
+        raise ValueError(f"cold_codes of scheme {pools.cold_scheme!r} must be one-byte [Pc, page, {width}]")
     p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]
 
 
@@ -140,6 +152,10 @@ def make_params(
     wait_limit_cycles: int = 0,
 ) -> _lib.DecodeParams:
     plan = dplan.plan
+    want = COLD_TILE_TOKENS.get(pools.cold_scheme, 128)
+    if pools.cold_codes.numel() and plan.cold_tile != want:
+        raise ValueError(f"the plan cuts cold tiles of {plan.cold_tile} tokens; scheme {pools.cold_scheme!r} "
+                         f"needs {want} (build_plan(..., cold_tile={want}))")
     p = _lib.DecodeParams()
     p.n_heads = n_heads
     p.latent_dim = LATENT_DIM

@@ -28,6 +28,7 @@ import numpy as np
 from . import _lib
 
 COLD_TILE = 128
+COLD_TILE_INT8 = 64  # int8 codes: a 64-token cold tile holds the code bytes of a 128-token INT4 tile
 HOT_TILE = 32
 ROWS_PER_BLOCK = 16
 MAX_Q_LEN = 2048  # new tokens per sequence and step (the reference prefills in chunks of 2048)
@@ -99,6 +100,7 @@ class DecodePlan:
     # the decode kernel itself (unit_jobs[u] = the unit's job, or -1)
     n_separate_combine: int | None = None
     unit_jobs: np.ndarray | None = None
+    cold_tile: int = COLD_TILE  # tokens of a cold tile (COLD_TILE_INT8 for int8 codes)
 
     @property
     def n_workers(self) -> int:
@@ -118,11 +120,11 @@ class DecodePlan:
         return self.n_slots * ROWS_PER_BLOCK * (512 + 2) * 4 + self.n_units * QPREP_BYTES + counters
 
 
-def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
+def _tiles_of(seq: SequenceLayout, cold_tile: int = COLD_TILE) -> list[tuple[int, int, int, int]]:
     out = []
     for page, off, n in seq.cold:
-        for s in range(0, n, COLD_TILE):
-            out.append((_lib.TILE_COLD, page, off + s, min(COLD_TILE, n - s)))
+        for s in range(0, n, cold_tile):
+            out.append((_lib.TILE_COLD, page, off + s, min(cold_tile, n - s)))
     for page, off, n in seq.hot:
         for s in range(0, n, HOT_TILE):
             out.append((_lib.TILE_HOT, page, off + s, min(HOT_TILE, n - s)))
@@ -132,7 +134,7 @@ def _tiles_of(seq: SequenceLayout) -> list[tuple[int, int, int, int]]:
     return out
 
 
-def _tile_table(seqs: list[SequenceLayout]) -> tuple[np.ndarray, np.ndarray]:
+def _tile_table(seqs: list[SequenceLayout], cold_tile: int = COLD_TILE) -> tuple[np.ndarray, np.ndarray]:
     """All sequences' tiles at once (numpy, no per-tile Python): [n_tiles, 4] int32 in the
     order of _tiles_of per sequence, and [n_seqs + 1] offsets of each sequence's tiles."""
     rows, seg_kind, seg_len, per_seq = [], [], [], []
@@ -155,7 +157,7 @@ def _tile_table(seqs: list[SequenceLayout]) -> tuple[np.ndarray, np.ndarray]:
     if bad.any():
         i = int(np.argmax(bad))
         raise ValueError(f"bad chunk (page={int(Pg[i])}, offset={int(Of[i])}, n={int(N[i])})")
-    T = np.where(K == cold_k, COLD_TILE, HOT_TILE)
+    T = np.where(K == cold_k, cold_tile, HOT_TILE)
     cnt = (N + T - 1) // T
     rep = np.repeat(np.arange(K.shape[0]), cnt)
     first = np.cumsum(cnt) - cnt
@@ -167,12 +169,14 @@ def _tile_table(seqs: list[SequenceLayout]) -> tuple[np.ndarray, np.ndarray]:
     return tiles.reshape(-1, 4), tile_off
 
 
-def _tile_costs(tiles: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
-    """Per-tile bytes (cost model of the one-CTA-per-item schedule) and estimated ns."""
+def _tile_costs(tiles: np.ndarray, cold_tile: int = COLD_TILE) -> tuple[np.ndarray, np.ndarray]:
+    """Per-tile bytes (cost model of the one-CTA-per-item schedule) and estimated ns.  A full
+    cold tile has the same estimated time for either tile size (the same code bytes and MMAs)."""
     cold = tiles[:, 0] == _lib.TILE_COLD
     n = tiles[:, 3].astype(np.int64)
-    nbytes = n * np.where(cold, _COLD_TOKEN_BYTES, _HOT_TOKEN_BYTES)
-    ns = np.where(cold, _COLD_TILE_NS[0] + (_COLD_TILE_NS[1] * n) // COLD_TILE,
+    n_cold = n * (COLD_TILE // cold_tile)  # in INT4-tile token units
+    nbytes = np.where(cold, n_cold * _COLD_TOKEN_BYTES, n * _HOT_TOKEN_BYTES)
+    ns = np.where(cold, _COLD_TILE_NS[0] + (_COLD_TILE_NS[1] * n) // cold_tile,
                   _HOT_TILE_NS[0] + (_HOT_TILE_NS[1] * n) // HOT_TILE)
     return nbytes.astype(np.int64), ns.astype(np.int64)
 
@@ -270,6 +274,7 @@ def build_plan(
     max_items_per_seq: int | None = None,
     force_partial: bool = False,
     persistent: bool = True,
+    cold_tile: int = COLD_TILE,
 ) -> DecodePlan:
     """Cut the batch into balanced work items.
 
@@ -281,7 +286,11 @@ def build_plan(
     ``force_partial``: every (sequence, row block) writes partial records and gets
     a combine job, even when one item covers it (context-parallel decode merges
     these records across ranks).
+    ``cold_tile``: tokens of a cold tile, ``COLD_TILE`` for the INT4 schemes and
+    ``COLD_TILE_INT8`` for int8 codes (the decode call checks it against the scheme).
     """
+    if cold_tile not in (COLD_TILE, COLD_TILE_INT8):
+        raise ValueError(f"cold_tile must be {COLD_TILE} or {COLD_TILE_INT8}")
     if n_heads <= 0:
         raise ValueError("n_heads must be positive")
     total_q = 0
@@ -289,9 +298,9 @@ def build_plan(
         if not (0 < seq.q_len <= MAX_Q_LEN):
             raise ValueError(f"q_len must be in 1..{MAX_Q_LEN} (got {seq.q_len})")
         total_q = max(total_q, seq.q_start + seq.q_len)
-    tile_arr, tile_off = _tile_table(seqs)
+    tile_arr, tile_off = _tile_table(seqs, cold_tile)
     seq_tile_ranges = [(int(a), int(b)) for a, b in zip(tile_off[:-1], tile_off[1:])]
-    costs, tile_ns = _tile_costs(tile_arr)
+    costs, tile_ns = _tile_costs(tile_arr, cold_tile)
     prefix = np.concatenate(([0], np.cumsum(costs)))
 
     # work units: (seq, row_block)
@@ -351,7 +360,8 @@ def build_plan(
         workers = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
         comb_arr = np.asarray(combine, dtype=np.int32).reshape(-1, 4)
         return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, workers,
-                          n_separate_combine=len(separate), unit_jobs=unit_jobs if fused else None)
+                          n_separate_combine=len(separate), unit_jobs=unit_jobs if fused else None,
+                          cold_tile=cold_tile)
 
     slots_target = max(1, int(n_sms * ctas_per_sm * waves))
     item_cost = max(total_cost / slots_target, 4 * COLD_TILE * _COLD_TOKEN_BYTES)
@@ -385,7 +395,7 @@ def build_plan(
     item_arr = np.asarray([it[:8] for it in items], dtype=np.int32).reshape(-1, 8)
     comb_arr = np.asarray(combine, dtype=np.int32).reshape(-1, 4)
     if not persistent or not items:
-        return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr)
+        return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, cold_tile=cold_tile)
     # deal the items (longest first) to the least loaded of the workers
     P = np.concatenate(([0], np.cumsum(tile_ns)))
     heap = [(0, w) for w in range(min(n_workers, len(items)))]
@@ -398,4 +408,4 @@ def build_plan(
     item_arr = item_arr[order]
     counts = np.bincount(np.asarray(owner), minlength=len(heap))
     workers = np.concatenate(([0], np.cumsum(counts))).astype(np.int32)
-    return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, workers)
+    return DecodePlan(tile_arr, item_arr, comb_arr, n_slots, total_q, n_heads, unit_arr, workers, cold_tile=cold_tile)

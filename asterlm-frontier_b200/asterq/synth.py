@@ -68,7 +68,8 @@ class Workload:
         hot = sum(self.hot) + self.total_q
         per_q = self.n_heads * (LATENT_DIM + ROPE_DIM) * 2 + self.n_heads * LATENT_DIM * 2
         rope = (ROPE_DIM // 2 + 2) if self.pools.rope_quantized else ROPE_DIM * 2  # codes + scale, or bf16
-        return cold * (256 + 16 + rope) + hot * (1024 + 128) + self.total_q * per_q
+        codes = int(self.pools.cold_codes.shape[-1])  # 256 (INT4) or 512 (int8)
+        return cold * (codes + 16 + rope) + hot * (1024 + 128) + self.total_q * per_q
 
     def flops(self) -> int:
         """Useful multiply-adds x 2 (QK over 576 dims + PV over 512) for all rows."""
@@ -109,9 +110,10 @@ class PoolBuilder:
         n_cold_pages = sum(math.ceil(max(0, n - h) / page_tokens) for n, h in zip(lengths, hot))
         n_hot_pages = sum(math.ceil(h / page_tokens) for h in hot)
         # quantize_rope: cold RoPE keys encoded like the latent (cold scheme, one group of 64)
-        self.pools = LatentPools.empty(n_cold_pages, n_hot_pages, page_tokens, self.device, quantize_rope=quantize_rope)
-        self.pools.cold_scheme = scheme
-        self._scheme_id = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4}[scheme]
+        self.pools = LatentPools.empty(n_cold_pages, n_hot_pages, page_tokens, self.device, quantize_rope=quantize_rope,
+                                       cold_scheme=scheme)
+        self._scheme_id = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4,
+                           "int8": _lib.SCHEME_INT8}[scheme]
         total_q = len(self.lengths) * q_len
         dev = self.device
         self.q_lat = torch.zeros(total_q, n_heads, LATENT_DIM, dtype=torch.bfloat16, device=dev)
@@ -136,7 +138,7 @@ class PoolBuilder:
         lay = SequenceLayout(q_start=i * q_len, q_len=q_len)
         if cold:
             r0 = self._cold_page * P
-            codes = pools.cold_codes.view(-1, LATENT_DIM // 2)
+            codes = pools.cold_codes.view(-1, pools.cold_codes.shape[-1])
             scales = pools.cold_scales.view(-1, LATENT_DIM // GROUP_SIZE)
             self._lib.check(
                 self.lib.asterq_quantize(
@@ -191,6 +193,7 @@ def make_workload(
     page_tokens: int = 512,
     keep_host: set[int] | None = None,
     quantize_rope: bool = False,
+    scheme: str = "hadamard_int4",
 ) -> Workload:
     """Generate every sequence on the device and build its pools.
 
@@ -199,7 +202,7 @@ def make_workload(
     device = torch.device(device)
     keep_host = keep_host or set()
     b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=n_heads, page_tokens=page_tokens, device=device,
-                    quantize_rope=quantize_rope)
+                    quantize_rope=quantize_rope, scheme=scheme)
     host: dict[int, dict[str, torch.Tensor]] = {}
     for i, lat, rope, ql, qr in generate_sequences(lengths, q_len=q_len, n_heads=n_heads, seed=seed, device=device):
         b.add(lat, rope, ql, qr)
@@ -273,10 +276,11 @@ def make_shard_workload(
     return b.finish(name, host)
 
 
-def c3_workload(device="cuda", seed: int = 0, n_seqs: int = 64, keep_host=None, quantize_rope: bool = False) -> Workload:
+def c3_workload(device="cuda", seed: int = 0, n_seqs: int = 64, keep_host=None, quantize_rope: bool = False,
+                scheme: str = "hadamard_int4") -> Workload:
     lens = c3_lengths(seed, n_seqs)
     return make_workload("C3 ragged decode", lens, [min(n, 2048) for n in lens], q_len=1, seed=seed, device=device,
-                         keep_host=keep_host, quantize_rope=quantize_rope)
+                         keep_host=keep_host, quantize_rope=quantize_rope, scheme=scheme)
 
 
 def c5_workload(device="cuda", seed: int = 0, n_seqs: int = 256, keep_host=None) -> Workload:

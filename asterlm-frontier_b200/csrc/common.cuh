@@ -117,6 +117,16 @@ ASTERQ_DEVICE uint32_t nib_hi_f16x2(uint32_t x) {
   return hfma2_u32(and_or(x, 0x00F000F0u, kF16Magic), kF16Sixteenth, kF16Minus72);
 }
 
+// Signed bytes with the same trick: a byte v with its sign bit flipped is u = v + 128 in
+// [0, 255], and 0x6400 | u is 1024 + u, so (x & 0x00FF00FF) ^ 0x64806480 (one LOP3) holds
+// 1152 + v in each half and subtracting 1152 leaves v exactly.
+constexpr uint32_t kF16Bias1152 = 0x64806480u;  // (1152, 1152), also the XOR pattern
+ASTERQ_DEVICE uint32_t s8_bytes02_f16x2(uint32_t x) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0x6A;" : "=r"(d) : "r"(x), "r"(0x00FF00FFu), "r"(kF16Bias1152));  // (a & b) ^ c
+  return hsub2_u32(d, kF16Bias1152);
+}
+
 // ---------------------------------------------------------------------------
 // Warp-level tensor-core MMA (m16n8k16, fp32 accumulate)
 // ---------------------------------------------------------------------------

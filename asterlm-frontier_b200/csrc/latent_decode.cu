@@ -57,6 +57,8 @@ constexpr int kL = 512;
 constexpr int kRope = 64;
 constexpr int kRows = 16;
 constexpr int kColdTile = 128;
+constexpr int kColdTile8 = 64;     // int8 codes: tokens of a cold tile
+constexpr int kCodeBlock8 = 8192;  // int8 codes: dims 128b..128b+127 of the tile's 64 tokens at b * 8192, SW128
 constexpr int kHotTile = 32;
 constexpr int kStages = 3;
 constexpr int kTeamWarps = 4;                  // score warps of one team (one tile at a time)
@@ -193,8 +195,8 @@ ASTERQ_DEVICE Tile check_tile(const asterq_decode_params& p, int4 t) {
   // a malformed entry reads nothing instead of faulting
   bool ok = tile.n > 0 && tile.off >= 0;
   if (tile.kind == ASTERQ_TILE_COLD) {
-    ok = ok && tile.page >= 0 && tile.page < p.n_cold_pages && tile.n <= kColdTile &&
-         tile.off + tile.n <= p.page_tokens;
+    ok = ok && tile.page >= 0 && tile.page < p.n_cold_pages &&
+         tile.n <= (p.cold_scheme == ASTERQ_SCHEME_INT8 ? kColdTile8 : kColdTile) && tile.off + tile.n <= p.page_tokens;
   } else if (tile.kind == ASTERQ_TILE_HOT) {
     ok = ok && tile.page >= 0 && tile.page < p.n_hot_pages && tile.n <= kHotTile && tile.off + tile.n <= p.page_tokens;
   } else if (tile.kind == ASTERQ_TILE_NEW) {
@@ -285,6 +287,7 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   float* sc = reinterpret_cast<float*>(prep_smem + 16 * kL * 6 + 16 * kRope * 2);  // kQScalars, from kMQscale
   float* rscr = sc + kQScalars;  // quantized RoPE: [16][64] fp32 rotated RoPE query, then [16] fixed-point scales
   const bool rope_q = p.rope_scheme == ASTERQ_ROPE_QUANTIZED;
+  const bool b8 = p.cold_scheme == ASTERQ_SCHEME_INT8;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int unit = blockIdx.x;
   // the decode grid may launch now; it waits for this grid's results before reading them
@@ -335,11 +338,13 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
         e = min(max(14 - ex, -100), 100);
       }
       const float qs = (mx > 0.0f) ? 32511.0f / mx : 1.0f;
+      // INT4 codes enter the int8 MMAs as 16 x code (the nibble in the high half of the byte)
+      const float cm = b8 ? 1.0f : 16.0f;
       sc[r] = ldexpf(1.0f, e);
       sc[kMQinv - kMQscale + r] = ldexpf(1.0f, -e) * p.softmax_scale;
       sc[kMQint - kMQscale + r] = qs;
-      sc[kMQinvI - kMQscale + r] = p.softmax_scale / (16.0f * qs);
-      sc[kMRopeR - kMQscale + r] = ldexpf(1.0f, -e) * (16.0f * qs);
+      sc[kMQinvI - kMQscale + r] = p.softmax_scale / (cm * qs);
+      sc[kMRopeR - kMQscale + r] = ldexpf(1.0f, -e) * (cm * qs);
     }
     if (rope_q) {
       // Quantized cold RoPE keys are scored like a ninth scale group: the RoPE query in the
@@ -376,19 +381,22 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   }
   __syncthreads();
   // cold QK B fragments: k-step ks = 2 * group + j; lane (gid, tq) holds query row 8nt + gid at
-  // k = 4tq + i (b0) and 16 + 4tq + i (b1), which the code expansion maps to dims 8W + 2i and
-  // 8W + 2i + 1 of code word W = 8 * group + 2tq + j.  Two int8 limbs: q = 256 hi + lo.
+  // k = 4tq + i (b0) and 16 + 4tq + i (b1), which the INT4 code expansion maps to dims 8W + 2i
+  // and 8W + 2i + 1 of code word W = 8 * group + 2tq + j, and int8 codes to dims
+  // 64 * group + 16tq + 8j + i and + 4 + i.  Two int8 limbs: q = 256 hi + lo.
   uint4* qi = reinterpret_cast<uint4*>(dst);
   for (int e = tid; e < 16 * 2 * 32; e += kPrepThreads) {
     const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
     const int row = 8 * nt + (ln >> 2), W = 8 * (ks >> 1) + 2 * (ln & 3) + (ks & 1);
+    const int d8 = 64 * (ks >> 1) + 16 * (ln & 3) + 8 * (ks & 1);
     const float qs = sc[kMQint - kMQscale + row];
     uint32_t hb[2] = {0u, 0u}, lb[2] = {0u, 0u};
 #pragma unroll
     for (int half = 0; half < 2; ++half)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int qv = min(max(__float2int_rn(scratch[row * kL + 8 * W + 2 * i + half] * qs), -32511), 32511);
+        const int dim = b8 ? d8 + 4 * half + i : 8 * W + 2 * i + half;
+        const int qv = min(max(__float2int_rn(scratch[row * kL + dim] * qs), -32511), 32511);
         const int q1 = (qv + 128) >> 8;  // floor((q + 128) / 256): q1 in [-127, 127], q - 256 q1 in [-128, 127]
         const int q2 = qv - 256 * q1;
         hb[half] |= (uint32_t)(q1 & 0xff) << (8 * i);
@@ -445,11 +453,20 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   }
 }
 
-// kRopeQ: cold RoPE keys quantized (ASTERQ_ROPE_QUANTIZED); a separate instantiation, so that the
-// bf16-RoPE kernel's code and register allocation do not carry the quantized path
-template <bool kRopeQ>
+// Kernel instantiations (each mode's code and register allocation carry only its own path):
+//  kModeInt4: INT4 codes (hadamard_int4 or int4) with bf16 RoPE keys;
+//  kModeInt4RopeQ: INT4 codes with quantized RoPE keys (ASTERQ_ROPE_QUANTIZED);
+//  kModeInt8: int8 codes (kv.py scheme "int8": one signed byte a dim, fp16 scale per group of 64),
+//    bf16 RoPE keys, in 64-token cold tiles (512 code bytes a token: a tile holds as many code
+//    bytes as a 128-token INT4 tile, so every warp's share of a stage is unchanged).
+constexpr int kModeInt4 = 0, kModeInt4RopeQ = 1, kModeInt8 = 2;
+template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
+  constexpr bool kRopeQ = kMode == kModeInt4RopeQ;
+  constexpr bool kB8 = kMode == kModeInt8;
+  constexpr int kCT = kB8 ? kColdTile8 : kColdTile;  // tokens of a cold tile
+  constexpr int kCM = kCT / 64;                      // 16-token m-tiles of a cold tile per score warp
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base, derived by indexing the __shared__ array so that the
   // compiler keeps every access through `smem` in the shared state space
@@ -538,6 +555,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_3d(st + kCodesLo, &maps.codes, y, full);
         bulk_1d(st + kCRope, reinterpret_cast<const uint8_t*>(p.cold_rope) + (int64_t)y * 32, 32 * t.n, full);
         bulk_1d(st + kCRopeScale, reinterpret_cast<const uint8_t*>(p.cold_rope_scales) + (int64_t)y8 * 2, 2 * n8, full);
+      } else if constexpr (kB8) {
+        mbar_expect_tx(full, 4 * kCodeBlock8 + kColdTile8 * 128 + 16 * t.n);
+        tma_3d(st + kCodesLo, &maps.codes, y, full);  // four blocks of [64 rows][128 B]
+        tma_2d(st + kCRope, &maps.crope, 0, y, full);
       } else {
         mbar_expect_tx(full, 3 * 16384 + 16 * t.n);
         tma_3d(st + kCodesLo, &maps.codes, y, full);  // both halves: kCodesHi = kCodesLo + 128 rows x 128 B
@@ -715,6 +736,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kScoreRegs));
     // team `team` takes tiles team, team + 2, ...; tw is the warp's index in its team
     const int team = warp / kTeamWarps, tw = warp % kTeamWarps;
+    // cold tile token of accumulator row r (0..15) of this warp's m-tile m: INT4 tiles give each
+    // warp 32 tokens in a code-word-derived order, int8 tiles 16 tokens in order
+    auto ctok = [&](int m, int r) { return kB8 ? 16 * tw + r : qk_token(tw, m, r); };
 #pragma unroll 1
     for (int it = it_begin; it < it_end; ++it) {
       begin_item(it);
@@ -772,15 +796,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int m = 0; m < 2; ++m)
 #pragma unroll
-            for (int h = 0; h < 2; ++h) tok[m][h] = qk_token(tw, m, gid + 8 * h);
+            for (int h = 0; h < 2; ++h) tok[m][h] = ctok(m, gid + 8 * h);
           const __half* scl = reinterpret_cast<const __half*>(st + kScales);
           if constexpr (kRopeQ) {
             // quantized RoPE keys: scored as a ninth scale group in the group loop below
           } else {
             // RoPE channel first (bf16, exact products), moved into the integer-score units
 #pragma unroll
-            for (int m = 0; m < 2; ++m) {
-              const int row = qk_token(tw, m, (lane & 7) + 8 * ((lane >> 3) & 1));
+            for (int m = 0; m < kCM; ++m) {
+              const int row = ctok(m, (lane & 7) + 8 * ((lane >> 3) & 1));
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks) {
                 uint32_t a[4];
@@ -803,6 +827,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Group g's integer dot products (two int8 limbs of the query, both k-steps):
           // loads, code expansion and 16 MMAs into acc.
           auto qk_issue = [&](int g, int (&acc)[2][2][2][4]) {
+            if constexpr (kB8) {
+              // int8 codes: lane tq's 16 bytes of group g (dims 64g + 16tq .. + 15) of each of its
+              // two tokens; k-step j takes dims 16tq + 8j + {0..3} (b0) and + {4..7} (b1), the
+              // order the query limbs were laid out in
+              uint4 v[2];
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                v[h] = *reinterpret_cast<const uint4*>(st + (g >> 1) * kCodeBlock8 + swz(tok[0][h], 4 * (g & 1) + tq));
+#pragma unroll
+              for (int j = 0; j < 2; ++j) {
+                const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
+                const uint32_t a[4] = {j ? v[0].z : v[0].x, j ? v[1].z : v[1].x, j ? v[0].w : v[0].y, j ? v[1].w : v[1].y};
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                  if (j == 0) {
+                    mma_s8_from(acc[0][0][nt], a, bq[nt].x, bq[nt].y, kAccBias);
+                    mma_s8_from(acc[1][0][nt], a, bq[nt].z, bq[nt].w, kAccBias);
+                  } else {
+                    mma_s8(acc[0][0][nt], a, bq[nt].x, bq[nt].y);
+                    mma_s8(acc[1][0][nt], a, bq[nt].z, bq[nt].w);
+                  }
+                }
+              }
+              return;
+            }
             // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens;
             // group 8 (quantized RoPE keys): words 2tq and 2tq + 1 of the token's 32-byte RoPE code
             // row, whose query limbs follow those of group 7 (k-steps 16 and 17)
@@ -847,7 +896,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           auto qk_finish = [&](int g, const int (&acc)[2][2][2][4]) {
             const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
 #pragma unroll
-            for (int m = 0; m < 2; ++m) {
+            for (int m = 0; m < kCM; ++m) {
               const float s0 = __half2float(scl[8 * tok[m][0] + g]);
               const float s1 = __half2float(scl[8 * tok[m][1] + g]);
               ssum[m][0] += s0;
@@ -907,7 +956,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           // the lo limbs' bias: B x (sum of the token's group scales)
 #pragma unroll
-          for (int m = 0; m < 2; ++m)
+          for (int m = 0; m < kCM; ++m)
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
@@ -962,17 +1011,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (cold) {
           const uint16_t* scl = reinterpret_cast<const uint16_t*>(st + kScales);
 #pragma unroll
-          for (int m = 0; m < 2; ++m)
+          for (int m = 0; m < kCM; ++m)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int tk = qk_token(tw, m, gid + 8 * h);
+              const int tk = ctok(m, gid + 8 * h);
               kept_scl[m][h] = (tk < t.n) ? *reinterpret_cast<const uint32_t*>(scl + 8 * tk + 2 * tq) : 0u;
             }
         }
         mbar_arrive(bar(kBarEmpty + s));
 
         // ---- finalize scores, mask, tile max ----
-        const int n_m = cold ? 2 : 1;
+        const int n_m = cold ? kCM : 1;  // m-tiles of this tile's scores
         float tmax[2][2];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
@@ -986,7 +1035,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 4; ++c) {
               const int h = c >> 1, cc = c & 1;
               const int r = 8 * nt + 2 * tq + cc;
-              const int tk = cold ? qk_token(tw, m, gid + 8 * h) : 8 * tw + gid;
+              const int tk = cold ? ctok(m, gid + 8 * h) : 8 * tw + gid;
               bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
               if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
               float sv = S[m][nt][c] * (cold ? qinvi[nt][cc] : qinv[nt][cc]);
@@ -1052,10 +1101,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* Pc = smem + kOffP + b * kPBytes;
           uint16_t* sT = reinterpret_cast<uint16_t*>(smem + kOffST + b * 2048);
 #pragma unroll
-          for (int m = 0; m < 2; ++m)
+          for (int m = 0; m < kCM; ++m)
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-              const int tk = qk_token(tw, m, gid + 8 * h);
+              const int tk = ctok(m, gid + 8 * h);
 #pragma unroll
               for (int nt = 0; nt < 2; ++nt) {
                 const float p0 = ex2_ftz((S[m][nt][2 * h] - msub[nt][0]) * kLog2e);
@@ -1153,7 +1202,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int c = 0; c < 4; ++c) {
-              const int dim = (order == 0) ? 64 * g + 2 * (4 * gid + mi) + (c >> 1) : 64 * g + 16 * mi + gid + 8 * (c >> 1);
+              // order 0, INT4: rows gid / gid + 8 of m-tile mi are dims 2(4gid + mi) / + 1 of the group;
+              // int8: dims 8gid + mi / 8gid + 4 + mi
+              const int dim = (order == 0) ? (kB8 ? 64 * g + 8 * gid + 4 * (c >> 1) + mi : 64 * g + 2 * (4 * gid + mi) + (c >> 1))
+                                           : 64 * g + 16 * mi + gid + 8 * (c >> 1);
               scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + dim] = o[mi][nt][c];
             }
       };
@@ -1179,7 +1231,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         // of all 128 tokens; hot: its bf16 A fragments of all 32 tokens), so the stage is
         // released, and refilled with tile i + 3, before this tile's p is even ready.
         uint32_t xs[8][4];
-        if (cold) {
+        if (cold && kB8) {
+          // int8: 8 bytes (dims 64g + 8gid .. + 7) of each of the lane's four tokens per k-step:
+          // token j of k-step kt -> xs[2kt + (j >> 1)][2(j & 1) .. + 1]
+#pragma unroll
+          for (int kt = 0; kt < kColdTile8 / 16; ++kt) {
+            const int t0 = 16 * kt + 2 * tq;
+            const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint2 w = *reinterpret_cast<const uint2*>(st + (g >> 1) * kCodeBlock8 +
+                                                               swz(tk[j], 4 * (g & 1) + (gid >> 1)) + 8 * (gid & 1));
+              xs[2 * kt + (j >> 1)][2 * (j & 1)] = w.x;
+              xs[2 * kt + (j >> 1)][2 * (j & 1) + 1] = w.y;
+            }
+          }
+        } else if (cold) {
 #pragma unroll
           for (int kt = 0; kt < kColdTile / 16; ++kt) {
             const int t0 = 16 * kt + 2 * tq;
@@ -1257,7 +1324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint16_t* sT = reinterpret_cast<const uint16_t*>(smem + kOffST + b * 2048) + g * kColdTile;
           const int lt = (lane & 7) + 8 * ((lane >> 3) & 1), lhalf = lane >> 4;
 #pragma unroll
-          for (int kt = 0; kt < kColdTile / 16; ++kt) {
+          for (int kt = 0; kt < kCT / 16; ++kt) {
             // tokens 16kt + {2tq, 2tq+1, 2tq+8, 2tq+9} are this lane's k indices
             const int t0 = 16 * kt + 2 * tq;
             // p B fragments (fp16) of rows 0-7 / 8-15, times the tokens' group-g code scales
@@ -1273,20 +1340,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             pb[0][1] = hmul2_u32(pr[1], s89);
             pb[1][0] = hmul2_u32(pr[2], s01);
             pb[1][1] = hmul2_u32(pr[3], s89);
+            if constexpr (kB8) {
 #pragma unroll
-            for (int mi = 0; mi < 4; ++mi) {
-              // rows gid / gid+8 of m-tile mi are dims 2(4gid+mi) / 2(4gid+mi)+1 of group g
-              const uint32_t sel =
-                  (uint32_t)mi | ((uint32_t)mi << 4) | ((uint32_t)(4 + mi) << 8) | ((uint32_t)(4 + mi) << 12);
-              const uint32_t z01 = prmt(xs[kt][0], xs[kt][1], sel);
-              const uint32_t z23 = prmt(xs[kt][2], xs[kt][3], sel);
-              uint32_t a[4];
-              a[0] = nib_lo_f16x2(z01);
-              a[1] = nib_hi_f16x2(z01);
-              a[2] = nib_lo_f16x2(z23);
-              a[3] = nib_hi_f16x2(z23);
+              for (int mi = 0; mi < 4; ++mi) {
+                // rows gid / gid+8 of m-tile mi are dims 8gid + mi / 8gid + 4 + mi of group g: byte mi
+                // of word 0 / word 1 of each token; a pair = the same byte of tokens (t0, t0 + 1)
+                // in a[0], a[1] and (t0 + 8, t0 + 9) in a[2], a[3]
+                const uint32_t sel = (uint32_t)mi | ((uint32_t)(4 + mi) << 8);
+                const uint32_t* x01 = xs[2 * kt];
+                const uint32_t* x89 = xs[2 * kt + 1];
+                uint32_t a[4];
+                a[0] = s8_bytes02_f16x2(prmt(x01[0], x01[2], sel));
+                a[1] = s8_bytes02_f16x2(prmt(x01[1], x01[3], sel));
+                a[2] = s8_bytes02_f16x2(prmt(x89[0], x89[2], sel));
+                a[3] = s8_bytes02_f16x2(prmt(x89[1], x89[3], sel));
 #pragma unroll
-              for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt][0], pb[nt][1]);
+                for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt][0], pb[nt][1]);
+              }
+            } else {
+#pragma unroll
+              for (int mi = 0; mi < 4; ++mi) {
+                // rows gid / gid+8 of m-tile mi are dims 2(4gid+mi) / 2(4gid+mi)+1 of group g
+                const uint32_t sel =
+                    (uint32_t)mi | ((uint32_t)mi << 4) | ((uint32_t)(4 + mi) << 8) | ((uint32_t)(4 + mi) << 12);
+                const uint32_t z01 = prmt(xs[kt][0], xs[kt][1], sel);
+                const uint32_t z23 = prmt(xs[kt][2], xs[kt][3], sel);
+                uint32_t a[4];
+                a[0] = nib_lo_f16x2(z01);
+                a[1] = nib_hi_f16x2(z01);
+                a[2] = nib_lo_f16x2(z23);
+                a[3] = nib_hi_f16x2(z23);
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt][0], pb[nt][1]);
+              }
             }
           }
         } else {
@@ -1620,14 +1706,18 @@ int validate(const asterq_decode_params* p) {
                      p->page_tokens);
   if (p->out_dtype != ASTERQ_DTYPE_F32 && p->out_dtype != ASTERQ_DTYPE_BF16)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: out_dtype must be f32 or bf16");
-  if (p->cold_scheme != ASTERQ_SCHEME_HADAMARD_INT4 && p->cold_scheme != ASTERQ_SCHEME_INT4)
-    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: cold scheme %d unsupported (hadamard_int4 or int4)", p->cold_scheme);
+  if (p->cold_scheme != ASTERQ_SCHEME_HADAMARD_INT4 && p->cold_scheme != ASTERQ_SCHEME_INT4 &&
+      p->cold_scheme != ASTERQ_SCHEME_INT8)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: cold scheme %d unsupported (hadamard_int4, int4 or int8)",
+                     p->cold_scheme);
   if (p->n_items < 0 || p->n_tiles < 0 || p->n_combine < 0 || p->n_slots < 0)
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: negative table size");
   if (p->n_items > 0 && (!p->items || !p->tiles || !p->q_lat || !p->q_rope || !p->out))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null pointer");
   if (p->rope_scheme != ASTERQ_ROPE_BF16 && p->rope_scheme != ASTERQ_ROPE_QUANTIZED)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: rope scheme %d unsupported (bf16 or quantized)", p->rope_scheme);
+  if (p->rope_scheme == ASTERQ_ROPE_QUANTIZED && p->cold_scheme == ASTERQ_SCHEME_INT8)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: quantized RoPE keys are read with the INT4 schemes only");
   if (p->n_cold_pages > 0 && (!p->cold_codes || !p->cold_scales || !p->cold_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null cold pool");
   if (p->n_cold_pages > 0 && p->rope_scheme == ASTERQ_ROPE_QUANTIZED && !p->cold_rope_scales)
@@ -1737,17 +1827,18 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     cudaGetDevice(&dev);
     static unsigned long long configured = 0;  // one bit per device ordinal
     if (dev >= 64 || !(configured & (1ull << dev))) {
-      cudaError_t e =
-          cudaFuncSetAttribute(dec::decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
-      if (e == cudaSuccess)
-        e = cudaFuncSetAttribute(dec::decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
+      const void* kernels[] = {reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt4>),
+                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt4RopeQ>),
+                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt8>)};
+      cudaError_t e = cudaSuccess;
+      for (const void* fn : kernels)
+        if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
       if (e == cudaSuccess)
         e = cudaFuncSetAttribute(dec::qprep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kPrepSmem);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
       // the score/value register split (setmaxnreg) assumes exactly kLaunchRegs per thread at launch:
       // refuse to launch a build that allocates fewer (an increase could then never be granted)
-      for (const void* fn : {reinterpret_cast<const void*>(dec::decode_kernel<false>),
-                             reinterpret_cast<const void*>(dec::decode_kernel<true>)}) {
+      for (const void* fn : kernels) {
         cudaFuncAttributes fa;
         e = cudaFuncGetAttributes(&fa, fn);
         if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: %s", cudaGetErrorString(e));
@@ -1762,10 +1853,13 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     // base for the map of an empty pool
     const void* dummy = p->q_lat;
     const int64_t cold_rows = p->n_cold_pages * p->page_tokens, hot_rows = p->n_hot_pages * p->page_tokens;
-    if ((st = dec::make_map(&maps.codes, p->cold_codes, cold_rows, 256, dec::kColdTile, dummy, 1024, 2)) ||
+    const bool b8 = p->cold_scheme == ASTERQ_SCHEME_INT8;
+    const int ct = b8 ? dec::kColdTile8 : dec::kColdTile;
+    if ((st = b8 ? dec::make_map(&maps.codes, p->cold_codes, cold_rows, 512, ct, dummy, 1024, 4)
+                 : dec::make_map(&maps.codes, p->cold_codes, cold_rows, 256, ct, dummy, 1024, 2)) ||
         // (quantized RoPE codes come in by plain bulk copies: no tensor map over their pool)
         (st = dec::make_map(&maps.crope, p->rope_scheme == ASTERQ_ROPE_BF16 ? p->cold_rope : nullptr, cold_rows,
-                            128, dec::kColdTile, dummy, 1024)) ||
+                            128, ct, dummy, 1024)) ||
         (st = dec::make_map(&maps.hlat, p->hot_latent, hot_rows, 1024, dec::kHotTile, dummy, 1024, 8)) ||
         (st = dec::make_map(&maps.hrope, p->hot_rope, hot_rows, 128, dec::kHotTile, dummy, 1024)) ||
         (st = dec::make_map(&maps.nlat, p->new_latent, p->total_q, 1024, dec::kHotTile, dummy, 1024, 8)) ||
@@ -1790,9 +1884,10 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      cudaError_t e = (kp.rope_scheme == ASTERQ_ROPE_QUANTIZED)
-                          ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<true>, kp, maps)
-                          : cudaLaunchKernelEx(&cfg, dec::decode_kernel<false>, kp, maps);
+      cudaError_t e = (kp.cold_scheme == ASTERQ_SCHEME_INT8) ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt8>, kp, maps)
+                      : (kp.rope_scheme == ASTERQ_ROPE_QUANTIZED)
+                          ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4RopeQ>, kp, maps)
+                          : cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4>, kp, maps);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: launch failed: %s", cudaGetErrorString(e));
     }
     st = check_launch("latent_decode");

@@ -156,7 +156,12 @@ __device__ int lower_tile(const long long* pc, int lo, int hi, long long y) {
   return lo;
 }
 
-__device__ __forceinline__ long long cold_cost(int n) { return kColdFixed + (kColdFull * n) / kColdTile; }
+// a full cold tile costs the same whatever its token count: a 64-token int8 tile holds as many
+// code bytes and MMAs as a 128-token INT4 tile
+__device__ __forceinline__ long long cold_cost(int n, int ct) { return kColdFixed + (kColdFull * n) / ct; }
+__host__ __device__ inline int cold_tile_of(const asterq_batch_desc& d) {
+  return d.cold_tile_tokens == 64 ? 64 : kColdTile;
+}
 __device__ __forceinline__ long long hot_cost(int n) { return kHotFixed + (kHotFull * n) / kHotTile; }
 __device__ __forceinline__ int clampi(int v, int lo, int hi) { return min(max(v, lo), hi); }
 
@@ -182,6 +187,7 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc 
   const long long n_segs = n_segments(B, MC);
   const Scratch s = scratch_of(b.scratch, n_segs, B, b.cap_tiles, b.cap_units, W);
   const int hot_tiles_per_page = (P + kHotTile - 1) / kHotTile;
+  const int CT = cold_tile_of(d);  // tokens of a cold tile
 
   auto q_len = [&](int q) { return min(d.q_len[q], kMaxQLen); };  // <= 0: an inactive sequence slot
 
@@ -211,7 +217,7 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc 
       long long n = 0;
       if (qlen > 0) {
         if (k < MC) {
-          if (k < clampi(nc[u], 0, MC)) n = (clampi(x[u], 0, P) + kColdTile - 1) / kColdTile;
+          if (k < clampi(nc[u], 0, MC)) n = (clampi(x[u], 0, P) + CT - 1) / CT;
         } else if (k == MC) {
           const int h = clampi(x[u], 0, d.max_hot_pages * P);
           n = (long long)(h / P) * hot_tiles_per_page + ((h % P) + kHotTile - 1) / kHotTile;
@@ -302,9 +308,9 @@ __global__ void __launch_bounds__(kThreads) plan_kernel(const asterq_batch_desc 
       const int k = kk[u];
       int4 tile;
       if (k < MC) {
-        const int tok = clampi(v2[u], 0, P), off = i[u] * kColdTile;
-        tile = make_int4(ASTERQ_TILE_COLD, v1[u], off, min(kColdTile, tok - off));
-        s.tile_cost[t] = cold_cost(tile.w);
+        const int tok = clampi(v2[u], 0, P), off = i[u] * CT;
+        tile = make_int4(ASTERQ_TILE_COLD, v1[u], off, min(CT, tok - off));
+        s.tile_cost[t] = cold_cost(tile.w, CT);
       } else if (k == MC) {
         const int h = clampi(v2[u], 0, d.max_hot_pages * P), page = i[u] / hot_tiles_per_page;
         const int off = (i[u] - page * hot_tiles_per_page) * kHotTile;
@@ -558,6 +564,9 @@ int check_desc(const asterq_batch_desc* d, const char* who) {
   if (d->page_tokens <= 0 || d->page_tokens % 16)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "%s: page_tokens %d must be a positive multiple of 16", who,
                      d->page_tokens);
+  if (d->cold_tile_tokens != 0 && d->cold_tile_tokens != 64 && d->cold_tile_tokens != 128)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "%s: cold_tile_tokens %d must be 0, 64 or 128", who,
+                     d->cold_tile_tokens);
   if (d->n_seqs > 0 && (!d->n_cold_pages || !d->cold_page_tokens || !d->hot_tokens || !d->q_len || !d->q_start ||
                         (d->max_cold_pages > 0 && !d->cold_pages) || (d->max_hot_pages > 0 && !d->hot_pages)))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "%s: null sequence table", who);

@@ -845,7 +845,7 @@ def extras(dev, args) -> dict:
     """Secondary single-GPU measurements: the write path (config 2) and configs 1, 4, 5."""
     import torch
 
-    from asterq.decode import DeviceDecodePlan, capture_step, latent_decode
+    from asterq.decode import COLD_TILE_TOKENS, DeviceDecodePlan, capture_step, latent_decode
     from asterq.plan import build_plan
     from asterq.synth import c1_inputs, c3_workload, c4_workload, c5_workload, PoolBuilder
 
@@ -855,7 +855,7 @@ def extras(dev, args) -> dict:
     res["c2_write_path"] = write_path_rate(dev, peak)
 
     def decode_rate(wl, name, iters):
-        plan = build_plan(wl.layouts, wl.n_heads)
+        plan = build_plan(wl.layouts, wl.n_heads, cold_tile=COLD_TILE_TOKENS[wl.pools.cold_scheme])
         dp = DeviceDecodePlan(plan, dev)
         out = torch.empty(wl.total_q, wl.n_heads, 512, dtype=torch.bfloat16, device=dev)
         fn = lambda: latent_decode(wl.pools, dp, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope,  # noqa: E731
@@ -876,6 +876,10 @@ def extras(dev, args) -> dict:
     # C3 with quantize_rope=True: cold RoPE keys as INT4 codes (306 instead of 400 bytes a cold token)
     wl = c3_workload(dev, seed=1000, quantize_rope=True)
     decode_rate(wl, "c3_quantize_rope_1gpu", 20)
+    del wl
+    # C3 with cache_dtype="int8": 512 code bytes a cold token (656 B with scales and RoPE key)
+    wl = c3_workload(dev, seed=1000, scheme="int8")
+    decode_rate(wl, "c3_int8_1gpu", 20)
     del wl
     wl = c4_workload(dev)
     decode_rate(wl, "c4_long_context_1gpu", 30)

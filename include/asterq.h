@@ -60,7 +60,7 @@ extern "C" {
                                    cold_rope_scales: fp16 [tokens] */
 
 /* tile kinds in the decode schedule */
-#define ASTERQ_TILE_COLD 0 /* tokens of a cold page: INT4 codes + fp16 scales + bf16 RoPE key */
+#define ASTERQ_TILE_COLD 0 /* tokens of a cold page: INT4 (or int8) codes + fp16 scales + RoPE key */
 #define ASTERQ_TILE_HOT 1  /* tokens of a hot page: bf16 latent + bf16 RoPE key */
 #define ASTERQ_TILE_NEW 2  /* the step's own new tokens (causal among themselves) */
 #define ASTERQ_TILE_HOLD 3 /* failure-detection test hook: nothing is loaded for this tile and its
@@ -122,7 +122,8 @@ int asterq_codec_status(int32_t* timeouts);
  *
  * Schedule (built by the host, see the Python package's plan builder):
  *   tiles [n_tiles][4] int32 = {kind, page (ASTERQ_TILE_NEW: first new-token row), token offset, n_tokens}
- *          cold tiles hold <= 128 tokens, hot/new tiles <= 32 tokens; a tile never crosses a page.
+ *          cold tiles hold <= 128 tokens (<= 64 with int8 codes), hot/new tiles <= 32 tokens; a tile
+          never crosses a page.
  *   units [n_units][2] int32 = {out_row0, n_rows}: one per 16-row query block; its query operands
  *          (rotated, fixed-point, fragment-ordered) are prepared once per call into the workspace.
  *   items [n_items][8] int32 = {unit, row_block, tile_begin, tile_end, slot, out_row0, n_rows, q_len}
@@ -131,9 +132,11 @@ int asterq_codec_status(int32_t* timeouts);
  *          slot < 0: the item covers the whole sequence and writes `out` directly;
  *          slot >= 0: it writes an (m, l, o) partial to the workspace.
  *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
- * Cold schemes: hadamard_int4 and int4 (params.cold_scheme).
+ * Cold schemes: hadamard_int4 and int4 (params.cold_scheme), and int8 (codes uint8/int8
+ *   [n_cold_pages, page_tokens, latent_dim]: one signed byte a dim, kv.py scheme "int8",
+ *   scales as above, not rotated; bf16 RoPE keys only).
  * Geometry supported: latent_dim 512, rope_dim 64, scale groups of 64, page_tokens
- * a multiple of 128, q_len <= 2048.  cold tiles hold <= 128 tokens, hot/new tiles <= 32.
+ * a multiple of 128, q_len <= 2048.  cold tiles hold <= 128 tokens (int8: <= 64), hot/new tiles <= 32.
  */
 typedef struct asterq_decode_params {
   int32_t n_heads;
@@ -207,7 +210,7 @@ typedef struct asterq_decode_params {
  * cold_page_tokens[s][j] tokens from offset 0; a hot window of hot_tokens[s] tokens in pages
  * hot_pages[s][0 ..] (every page full except the last); q_len[s] new tokens at rows
  * q_start[s] .. of the step's arrays (q_len[s] <= 0: an empty slot, planned as nothing).
- * Tiles of a sequence: cold (<= 128 tokens, never across a page), hot (<= 32), new (<= 32);
+ * Tiles of a sequence: cold (<= cold_tile_tokens, never across a page), hot (<= 32), new (<= 32);
  * every 16-row query block is a unit; the units' tile ranges are cut into one contiguous share
  * per worker of equal estimated time.
  */
@@ -225,6 +228,8 @@ typedef struct asterq_batch_desc {
   const int32_t* hot_pages;         /* [n_seqs][max_hot_pages] */
   const int32_t* q_len;             /* [n_seqs], <= 2048 */
   const int32_t* q_start;           /* [n_seqs] */
+  int32_t cold_tile_tokens;         /* tokens of a cold tile: 128 (0 means 128) for the INT4 schemes,
+                                       64 for int8 codes (the decode kernel's cold tile of that scheme) */
 } asterq_batch_desc;
 
 /* Device tables asterq_plan_batch writes, sized by capacities chosen by the caller. */

@@ -166,6 +166,9 @@ def main() -> None:
         # quantize_rope=True: the cold chunks' RoPE keys quantized too (cache.py:160-164)
         "qrope": dict(seed=6, ctx=2200, q_len=1, recent=512, chunk=512, quantize_rope=True),
         "qr4": dict(seed=8, ctx=2700, q_len=1, recent=512, chunk=512, scheme="int4", quantize_rope=True),
+        # int8 cold chunks (kv.py scheme "int8": one signed byte a dim, no rotation)
+        "q8": dict(seed=10, ctx=2400, q_len=1, recent=512, chunk=512, scheme="int8"),
+        "q8t3": dict(seed=11, ctx=1900, q_len=3, recent=512, chunk=512, scheme="int8"),
     }
     dec: dict[str, np.ndarray] = {}
     for name, kw in cases.items():

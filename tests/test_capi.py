@@ -51,8 +51,9 @@ def test_struct_layout_matches_header():
     assert _lib.DecodeParams.plan_counts.offset == size - 24
     assert _lib.DecodeParams.rope_scheme.offset == size - 16
     assert _lib.DecodeParams.cold_rope_scales.offset == size - 8
-    # asterq_batch_desc: 6 int32 + 7 pointers; asterq_plan_buffers: 3 int32 (+ padding) + 8 pointers
-    assert ctypes.sizeof(_lib.BatchDesc) == 6 * 4 + 7 * 8
+    # asterq_batch_desc: 6 int32 + 7 pointers + the cold tile int32 (+ padding); asterq_plan_buffers:
+    # 3 int32 (+ padding) + 8 pointers
+    assert ctypes.sizeof(_lib.BatchDesc) == 6 * 4 + 7 * 8 + 8
     assert ctypes.sizeof(_lib.PlanBuffers) == 16 + 8 * 8 and _lib.PlanBuffers.tiles.offset == 16
 
 

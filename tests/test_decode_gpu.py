@@ -47,9 +47,10 @@ def assert_close_bf16(out_bf16: np.ndarray, ref_fp32: np.ndarray, what: str) -> 
 
 
 def run_decode(wl, *, out_dtype=torch.float32, softcap=None, **plan_kw):
-    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.decode import COLD_TILE_TOKENS, DeviceDecodePlan, latent_decode
     from asterq.plan import build_plan
 
+    plan_kw.setdefault("cold_tile", COLD_TILE_TOKENS[wl.pools.cold_scheme])
     plan = build_plan(wl.layouts, wl.n_heads, **plan_kw)
     dplan = DeviceDecodePlan(plan, wl.q_lat.device)
     out = latent_decode(wl.pools, dplan, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE,
@@ -75,7 +76,7 @@ def oracle_for(inp, ctx, hot, q_len, softcap=None, chunk=512, scheme="hadamard_i
                     SCALE, softcap)
 
 
-@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4"])
+@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4", "q8", "q8t3"])
 def test_decode_matches_reference_golden(cuda, golden_decode, case):
     """The reference's own outputs; "qrope" / "qr4": quantize_rope=True caches (cold RoPE keys as
     hadamard_int4 / int4 codes, cache.py:160-164)."""
@@ -188,6 +189,45 @@ def test_quantized_rope_ragged_batch(cuda, scheme, q_len):
     split, plan = run_decode(wl, n_sms=16, ctas_per_sm=2, waves=4)
     assert plan.n_slots > 0
     assert O.rel_l2(split.cpu().numpy(), out) < 1e-4
+
+
+@pytest.mark.parametrize("q_len", [1, 3])
+def test_int8_cold_scheme_ragged_batch(cuda, q_len):
+    """int8 cold chunks (kv.py scheme "int8": one signed byte a dim, fp16 scale per group of 64, no
+    rotation) in 64-token tiles: ragged lengths with partial pages and tiles of 1..64 tokens, hot
+    windows, a cold-only sequence; one item per block and a split schedule agree."""
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    lengths, hot = [1300, 700, 2600, 65, 1031], [300, 0, 1000, 1, 7]
+    b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=16, device=cuda, scheme="int8")
+    refs = []
+    for i, (n, h) in enumerate(zip(lengths, hot)):
+        inp = c1_inputs(seed=80 + i, ctx=n, q_len=q_len)
+        b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+        refs.append(oracle_for(inp, n, h, q_len, scheme="int8"))
+    wl = b.finish("int8")
+    out, plan = run_decode(wl)
+    assert plan.cold_tile == 64 and int(plan.tiles[plan.tiles[:, 0] == 0][:, 3].max()) == 64
+    out = out.cpu().numpy()
+    for i, ref in enumerate(refs):
+        assert_close(out[i * q_len:(i + 1) * q_len], ref, f"sequence {i}")
+    split, plan = run_decode(wl, n_sms=16, ctas_per_sm=2, waves=4)
+    assert plan.n_slots > 0
+    assert O.rel_l2(split.cpu().numpy(), out) < 1e-4
+
+
+def test_int8_plan_with_int4_tiles_is_rejected(cuda):
+    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.plan import build_plan
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    inp = c1_inputs(seed=90, ctx=900, q_len=1)
+    b = PoolBuilder([900], [100], q_len=1, n_heads=16, device=cuda, scheme="int8")
+    b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    wl = b.finish("int8")
+    dplan = DeviceDecodePlan(build_plan(wl.layouts, 16), cuda)
+    with pytest.raises(ValueError, match="cold tiles"):
+        latent_decode(wl.pools, dplan, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE)
 
 
 def test_quantized_rope_cold_tiles_at_any_offset(cuda):
