@@ -36,6 +36,7 @@ def dtype_code(dtype) -> int:
 SCHEME_HADAMARD_INT4 = 0
 SCHEME_INT4 = 1
 SCHEME_INT8 = 2
+SCHEME_FLOAT8 = 3
 ROPE_BF16 = 0  # cold RoPE keys stored as bf16
 ROPE_QUANTIZED = 1  # cold RoPE keys stored as INT4 codes of the cold scheme + one fp16 scale a token
 

@@ -44,8 +44,12 @@ from .decode import COLD_TILE_TOKENS, GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPo
 from .kv import QuantizedTensor, dequantize_tensor
 from .plan import SequenceLayout
 
-_KERNEL_SCHEMES = ("hadamard_int4", "int4", "int8", "bfloat16")
-_SCHEME_IDS = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4, "int8": _lib.SCHEME_INT8}
+_KERNEL_SCHEMES = ("hadamard_int4", "int4", "int8", "float8", "bfloat16")
+_SCHEME_IDS = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4, "int8": _lib.SCHEME_INT8,
+               "float8": _lib.SCHEME_FLOAT8}
+# code storage of the one-byte schemes (else packed INT4 bytes, uint8); float8 pages hold the raw
+# e4m3 bytes (torch has no float8 page copies) and are viewed as float8_e4m3fn when handed out
+_CODE_DTYPES = {"int8": torch.int8, "float8": torch.uint8}
 
 
 class _Pool:
@@ -140,10 +144,10 @@ class LatentLayerCache:
         if self.cache_dtype not in _KERNEL_SCHEMES:
             raise NotImplementedError(
                 f"cache_dtype {self.cache_dtype!r}: the asterq pools serve 'hadamard_int4', 'int4' and 'bfloat16'")
-        if self.cache_dtype == "int8" and self.quantize_rope:
-            raise NotImplementedError("quantize_rope=True with int8 chunks: the decode kernel reads quantized RoPE "
-                                      "keys with the INT4 schemes only")
-        if self.cache_dtype in _SCHEME_IDS and self.group_size != GROUP_SIZE:
+        if self.cache_dtype in ("int8", "float8") and self.quantize_rope:
+            raise NotImplementedError(f"quantize_rope=True with {self.cache_dtype} chunks: the decode kernel reads "
+                                      "quantized RoPE keys with the INT4 schemes only")
+        if self.cache_dtype in _SCHEME_IDS and self.cache_dtype != "float8" and self.group_size != GROUP_SIZE:
             raise NotImplementedError(f"group_size {self.group_size}: the decode kernels use groups of {GROUP_SIZE}")
         if self.chunk_tokens <= 0 or self.chunk_tokens % 16:
             raise ValueError("chunk_tokens must be a positive multiple of 16 (one chunk per page)")
@@ -182,7 +186,7 @@ class LatentLayerCache:
         """Bytes the reference would account (cache.py:79-87): codes + scales + cold RoPE + hot tensors."""
         b, cold = self._batch, self.cold_length
         rope = (ROPE_DIM // 2 + 2) if self._rope_quantized else ROPE_DIM * 2  # codes + scale, or bf16
-        total = b * cold * (self._code_bytes + (LATENT_DIM // GROUP_SIZE) * 2 + rope)
+        total = b * cold * (self._code_bytes + self._n_scales * 2 + rope)
         total += b * self._hot_len * (LATENT_DIM + ROPE_DIM) * self._dtype.itemsize
         return int(total)
 
@@ -197,8 +201,8 @@ class LatentLayerCache:
                 # bf16 operands the decode kernel reads
                 fields.update(src_latent=((LATENT_DIM,), dtype), src_rope=((ROPE_DIM,), dtype))
             self._hot = _Pool(fields, self.page_tokens, device)
-            code_dtype = torch.int8 if self.cache_dtype == "int8" else torch.uint8
-            cold = {"codes": ((self._code_bytes,), code_dtype), "scales": ((LATENT_DIM // GROUP_SIZE,), torch.float16)}
+            code_dtype = _CODE_DTYPES.get(self.cache_dtype, torch.uint8)
+            cold = {"codes": ((self._code_bytes,), code_dtype), "scales": ((self._n_scales,), torch.float16)}
             if self._rope_quantized:
                 cold.update(rope=((ROPE_DIM // 2,), torch.uint8), rope_scales=((), torch.float16))
             else:
@@ -214,7 +218,12 @@ class LatentLayerCache:
     @property
     def _code_bytes(self) -> int:
         """Code bytes of a cold token: one a dim for int8, two dims a byte for the INT4 schemes."""
-        return LATENT_DIM if self.cache_dtype == "int8" else LATENT_DIM // 2
+        return LATENT_DIM if self.cache_dtype in _CODE_DTYPES else LATENT_DIM // 2
+
+    @property
+    def _n_scales(self) -> int:
+        """fp16 scales of a cold token: one per group of 64, none for float8 (kv.py:85-89)."""
+        return 0 if self.cache_dtype == "float8" else LATENT_DIM // GROUP_SIZE
 
     @property
     def _rope_quantized(self) -> bool:
@@ -404,13 +413,14 @@ class LatentLayerCache:
         # quantized from the caller's values (cache.py:172 encodes the hot tensor as stored)
         x = self._hot[self._src + "latent"].index_select(0, src).reshape(bsz * P, LATENT_DIM)
         codes = torch.empty(bsz * P, self._code_bytes, dtype=self._cold["codes"].dtype, device=dev)
-        scales = torch.empty(bsz * P, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=dev)
+        scales = torch.empty(bsz * P, max(self._n_scales, 1), dtype=torch.float16, device=dev)
         lib = _lib.load()
         _lib.check(lib.asterq_quantize(x.data_ptr(), _lib.dtype_code(x.dtype), bsz * P, LATENT_DIM, LATENT_DIM,
                                        _SCHEME_IDS[self.cache_dtype], GROUP_SIZE, codes.data_ptr(), scales.data_ptr(),
                                        _lib.stream_handle(dev)))
         self._cold["codes"].index_copy_(0, dst, codes.view(bsz, P, -1))
-        self._cold["scales"].index_copy_(0, dst, scales.view(bsz, P, -1))
+        if self._n_scales:
+            self._cold["scales"].index_copy_(0, dst, scales.view(bsz, P, -1))
         if self._rope_quantized:
             # quantize_rope (cache.py:163): the RoPE keys as stored, cold scheme, one group of 64
             r = self._hot[self._src + "rope"].index_select(0, src).reshape(bsz * P, ROPE_DIM)
@@ -477,12 +487,15 @@ class LatentLayerCache:
 
     @property
     def cold_latent(self) -> list[QuantizedTensor]:
-        """One reference-format QuantizedTensor per cold chunk (kv.py:58-73): data [B, chunk, 256], scale [B, chunk, 8, 1]."""
+        """One reference-format QuantizedTensor per cold chunk (kv.py:58-73): data [B, chunk, 256] (INT4) or
+        [B, chunk, 512] (int8, float8), scale [B, chunk, 8, 1] (None for float8)."""
         out = []
         for c in range(self.cold_chunks):
             pages = [self._cold_pages[b][c] for b in range(self._batch)]
             data = torch.stack([self._cold["codes"][pg] for pg in pages])
-            scale = torch.stack([self._cold["scales"][pg] for pg in pages]).unsqueeze(-1)
+            if self.cache_dtype == "float8":
+                data = data.view(torch.float8_e4m3fn)
+            scale = torch.stack([self._cold["scales"][pg] for pg in pages]).unsqueeze(-1) if self._n_scales else None
             out.append(QuantizedTensor(data=data, scale=scale, original_shape=(self._batch, self.chunk_tokens, LATENT_DIM),
                                        padded_dim=LATENT_DIM, group_size=GROUP_SIZE, scheme=self.cache_dtype,
                                        source_dtype=self._dtype))

@@ -19,17 +19,20 @@ from .plan import DecodePlan
 LATENT_DIM = 512
 ROPE_DIM = 64
 GROUP_SIZE = 64
-COLD_SCHEMES = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4, "int8": _lib.SCHEME_INT8}
+COLD_SCHEMES = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4, "int8": _lib.SCHEME_INT8,
+                "float8": _lib.SCHEME_FLOAT8}
 # tokens of a cold tile per scheme (the host and device planners cut pages into such tiles)
-COLD_TILE_TOKENS = {"hadamard_int4": 128, "int4": 128, "int8": 64}
+COLD_TILE_TOKENS = {"hadamard_int4": 128, "int4": 128, "int8": 64, "float8": 64}
+# one code byte a dim (512 a token) for these schemes, two dims a byte for the INT4 ones
+BYTE_SCHEMES = ("int8", "float8")
 
 
 @dataclass
 class LatentPools:
     """Device pools (layout documented in include/asterq.h)."""
 
-    cold_codes: torch.Tensor  # uint8 [Pc, page, 256] INT4 codes, or int8 [Pc, page, 512] (scheme "int8")
-    cold_scales: torch.Tensor  # fp16 [Pc, page, 8]
+    cold_codes: torch.Tensor  # uint8 [Pc, page, 256] INT4 codes, or [Pc, page, 512] int8 codes / e4m3 bytes
+    cold_scales: torch.Tensor  # fp16 [Pc, page, 8] (float8: [Pc, page, 0], no scales)
     cold_rope: torch.Tensor  # bf16 [Pc, page, 64], or uint8 [Pc, page, 32] INT4 codes (quantized RoPE keys)
     hot_latent: torch.Tensor  # bf16 [Ph, page, 512]
     hot_rope: torch.Tensor  # bf16 [Ph, page, 64]
@@ -51,8 +54,12 @@ class LatentPools:
               quantize_rope: bool = False, cold_scheme: str = "hadamard_int4") -> "LatentPools":
         if cold_scheme not in COLD_SCHEMES:
             raise NotImplementedError(f"cold scheme {cold_scheme!r}: the decode kernels read {tuple(COLD_SCHEMES)}")
+        n_scales = LATENT_DIM // GROUP_SIZE
         if cold_scheme == "int8":
             codes = torch.empty(n_cold_pages, page_tokens, LATENT_DIM, dtype=torch.int8, device=device)
+        elif cold_scheme == "float8":
+            codes = torch.empty(n_cold_pages, page_tokens, LATENT_DIM, dtype=torch.uint8, device=device)  # e4m3 bytes
+            n_scales = 0
         else:
             codes = torch.empty(n_cold_pages, page_tokens, LATENT_DIM // 2, dtype=torch.uint8, device=device)
         if quantize_rope:
@@ -63,7 +70,7 @@ class LatentPools:
             rope_scales = None
         return LatentPools(
             cold_codes=codes,
-            cold_scales=torch.empty(n_cold_pages, page_tokens, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=device),
+            cold_scales=torch.empty(n_cold_pages, page_tokens, n_scales, dtype=torch.float16, device=device),
             cold_rope=cold_rope,
             hot_latent=torch.empty(n_hot_pages, page_tokens, LATENT_DIM, dtype=torch.bfloat16, device=device),
             hot_rope=torch.empty(n_hot_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device),
@@ -98,7 +105,7 @@ def set_cold_pools(p: _lib.DecodeParams, pools: LatentPools) -> None:
         p.cold_rope_scales = None
     if pools.cold_scheme not in COLD_SCHEMES:
         raise NotImplementedError(f"cold scheme {pools.cold_scheme!r}: the decode kernels read {COLD_SCHEMES}")
-    width = LATENT_DIM if pools.cold_scheme == "int8" else LATENT_DIM // 2
+    width = LATENT_DIM if pools.cold_scheme in BYTE_SCHEMES else LATENT_DIM // 2
     if pools.cold_codes.numel() and (pools.cold_codes.shape[-1] != width or pools.cold_codes.element_size() != 1):
         raise ValueError(f"cold_codes of scheme {pools.cold_scheme!r} must be one-byte [Pc, page, {width}]")
     p.cold_scheme = COLD_SCHEMES[pools.cold_scheme]

@@ -68,8 +68,9 @@ class Workload:
         hot = sum(self.hot) + self.total_q
         per_q = self.n_heads * (LATENT_DIM + ROPE_DIM) * 2 + self.n_heads * LATENT_DIM * 2
         rope = (ROPE_DIM // 2 + 2) if self.pools.rope_quantized else ROPE_DIM * 2  # codes + scale, or bf16
-        codes = int(self.pools.cold_codes.shape[-1])  # 256 (INT4) or 512 (int8)
-        return cold * (codes + 16 + rope) + hot * (1024 + 128) + self.total_q * per_q
+        codes = int(self.pools.cold_codes.shape[-1])  # 256 (INT4) or 512 (int8, float8)
+        scales = 2 * int(self.pools.cold_scales.shape[-1])  # 16, or 0 for float8
+        return cold * (codes + scales + rope) + hot * (1024 + 128) + self.total_q * per_q
 
     def flops(self) -> int:
         """Useful multiply-adds x 2 (QK over 576 dims + PV over 512) for all rows."""
@@ -113,7 +114,7 @@ class PoolBuilder:
         self.pools = LatentPools.empty(n_cold_pages, n_hot_pages, page_tokens, self.device, quantize_rope=quantize_rope,
                                        cold_scheme=scheme)
         self._scheme_id = {"hadamard_int4": _lib.SCHEME_HADAMARD_INT4, "int4": _lib.SCHEME_INT4,
-                           "int8": _lib.SCHEME_INT8}[scheme]
+                           "int8": _lib.SCHEME_INT8, "float8": _lib.SCHEME_FLOAT8}[scheme]
         total_q = len(self.lengths) * q_len
         dev = self.device
         self.q_lat = torch.zeros(total_q, n_heads, LATENT_DIM, dtype=torch.bfloat16, device=dev)
@@ -139,11 +140,12 @@ class PoolBuilder:
         if cold:
             r0 = self._cold_page * P
             codes = pools.cold_codes.view(-1, pools.cold_codes.shape[-1])
-            scales = pools.cold_scales.view(-1, LATENT_DIM // GROUP_SIZE)
+            n_scales = int(pools.cold_scales.shape[-1])  # 0 for float8 (no scales)
+            scales_ptr = pools.cold_scales.view(-1, n_scales)[r0].data_ptr() if n_scales else None
             self._lib.check(
                 self.lib.asterq_quantize(
                     lat.data_ptr(), self._lib.DTYPE_BF16, cold, LATENT_DIM, LATENT_DIM,
-                    self._scheme_id, GROUP_SIZE, codes[r0].data_ptr(), scales[r0].data_ptr(),
+                    self._scheme_id, GROUP_SIZE, codes[r0].data_ptr(), scales_ptr,
                     self._lib.stream_handle(self.device),
                 )
             )

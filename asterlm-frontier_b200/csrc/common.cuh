@@ -117,6 +117,25 @@ ASTERQ_DEVICE uint32_t nib_hi_f16x2(uint32_t x) {
   return hfma2_u32(and_or(x, 0x00F000F0u, kF16Magic), kF16Sixteenth, kF16Minus72);
 }
 
+// float -> float8 e4m3 byte as torch's x.to(torch.float8_e4m3fn) writes it: the hardware
+// conversion (round to nearest even, subnormals kept; it saturates 448 < |x| <= 464 to 448,
+// where rounding to nearest even lands anyway), with NaN, infinities and |x| > 464 mapped to
+// NaN carrying the sign of x
+ASTERQ_DEVICE uint32_t f32_to_e4m3(float x) {
+  unsigned short d;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %1;" : "=h"(d) : "f"(x));
+  uint32_t code = d & 0xFFu;
+  if (!(fabsf(x) <= 464.0f)) code = (__float_as_uint(x) >> 31) ? 0xFFu : 0x7Fu;
+  return code;
+}
+// two e4m3 bytes (bits 0-7 and 8-15 of x) -> fp16x2, the low byte in the low half (exact:
+// every e4m3 value is an fp16 value)
+ASTERQ_DEVICE uint32_t e4m3x2_to_f16x2(uint32_t x) {
+  uint32_t d;
+  asm("{\n .reg .b16 t;\n cvt.u16.u32 t, %1;\n cvt.rn.f16x2.e4m3x2 %0, t;\n}" : "=r"(d) : "r"(x));
+  return d;
+}
+
 // Signed bytes with the same trick: a byte v with its sign bit flipped is u = v + 128 in
 // [0, 255], and 0x6400 | u is 1024 + u, so (x & 0x00FF00FF) ^ 0x64806480 (one LOP3) holds
 // 1152 + v in each half and subtracting 1152 leaves v exactly.

@@ -895,6 +895,37 @@ int pow2_at_least(int v) {
   return p;
 }
 
+// float8 (kv.py:85-89): x.to(torch.float8_e4m3fn), one byte a value, no scales.  One block
+// per row at a time (rows grid-strided), threads over the row's values.
+__global__ void __launch_bounds__(256) f8_encode_kernel(const void* __restrict__ x, int x_dtype, int64_t n_tokens,
+                                                        int dim, int64_t stride, uint8_t* __restrict__ codes) {
+  for (int64_t t = blockIdx.x; t < n_tokens; t += gridDim.x)
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+      const int64_t i = t * stride + d;
+      float v;
+      if (x_dtype == ASTERQ_DTYPE_F32) v = reinterpret_cast<const float*>(x)[i];
+      else if (x_dtype == ASTERQ_DTYPE_BF16) v = __bfloat162float(reinterpret_cast<const __nv_bfloat16*>(x)[i]);
+      else v = __half2float(reinterpret_cast<const __half*>(x)[i]);
+      codes[t * dim + d] = (uint8_t)f32_to_e4m3(v);
+    }
+}
+
+// the e4m3 values widened to out_dtype (exact in fp32, bf16 and fp16)
+__global__ void __launch_bounds__(256) f8_decode_kernel(const uint8_t* __restrict__ codes, int64_t n_tokens, int dim,
+                                                        void* __restrict__ out, int out_dtype, int64_t out_stride) {
+  for (int64_t t = blockIdx.x; t < n_tokens; t += gridDim.x)
+    for (int d = threadIdx.x; d < dim; d += blockDim.x) {
+      const uint32_t c = codes[t * dim + d];
+      const float v = __half2float(__ushort_as_half((unsigned short)(e4m3x2_to_f16x2(c | (c << 8)) & 0xFFFFu)));
+      const int64_t i = t * out_stride + d;
+      if (out_dtype == ASTERQ_DTYPE_F32) reinterpret_cast<float*>(out)[i] = v;
+      else if (out_dtype == ASTERQ_DTYPE_BF16) reinterpret_cast<__nv_bfloat16*>(out)[i] = __float2bfloat16_rn(v);
+      else reinterpret_cast<__half*>(out)[i] = __float2half_rn(v);
+    }
+}
+
+int f8_grid(int64_t n_tokens) { return (int)(n_tokens < 148 * 16 ? n_tokens : 148 * 16); }
+
 }  // namespace
 
 }  // namespace asterq
@@ -910,8 +941,16 @@ extern "C" int asterq_quantize(const void* x, int x_dtype, int64_t n_tokens, int
   if (x_row_stride < dim) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "quantize: row stride %lld < dim %d",
                                            (long long)x_row_stride, dim);
   if (n_tokens == 0) return ASTERQ_OK;
-  if (!x || !codes || !scales) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "quantize: null pointer");
+  if (!x || !codes || (!scales && scheme != ASTERQ_SCHEME_FLOAT8))
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "quantize: null pointer");
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (scheme == ASTERQ_SCHEME_FLOAT8) {
+    if (x_dtype != ASTERQ_DTYPE_F32 && x_dtype != ASTERQ_DTYPE_BF16 && x_dtype != ASTERQ_DTYPE_F16)
+      return set_error(ASTERQ_ERR_UNSUPPORTED, "quantize: float8 from dtype %d unsupported", x_dtype);
+    f8_encode_kernel<<<f8_grid(n_tokens), 256, 0, st>>>(x, x_dtype, n_tokens, dim, x_row_stride,
+                                                        reinterpret_cast<uint8_t*>(codes));
+    return check_launch("encode (float8)");
+  }
   if (scheme == ASTERQ_SCHEME_HADAMARD_INT4) {
     const int padded = pow2_at_least(dim);
     if (padded % group_size) return set_error(ASTERQ_ERR_UNSUPPORTED, "quantize: group %d does not divide %d", group_size, padded);
@@ -953,10 +992,16 @@ extern "C" int asterq_dequantize(const void* codes, const void* scales, int64_t 
   if (n_tokens < 0 || dim <= 0 || group_size <= 0 || out_row_stride < dim)
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "dequantize: bad sizes");
   if (n_tokens == 0) return ASTERQ_OK;
-  if (!codes || !scales || !out) return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "dequantize: null pointer");
+  if (!codes || (!scales && scheme != ASTERQ_SCHEME_FLOAT8) || !out)
+    return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "dequantize: null pointer");
   if (out_dtype != ASTERQ_DTYPE_F32 && out_dtype != ASTERQ_DTYPE_BF16 && out_dtype != ASTERQ_DTYPE_F16)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "dequantize: unsupported output dtype %d", out_dtype);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (scheme == ASTERQ_SCHEME_FLOAT8) {
+    f8_decode_kernel<<<f8_grid(n_tokens), 256, 0, st>>>(reinterpret_cast<const uint8_t*>(codes), n_tokens, dim, out,
+                                                        out_dtype, out_row_stride);
+    return check_launch("decode (float8)");
+  }
   if (scheme == ASTERQ_SCHEME_HADAMARD_INT4) {
     const int padded = pow2_at_least(dim);
     if (padded % group_size) return set_error(ASTERQ_ERR_UNSUPPORTED, "dequantize: group %d does not divide %d", group_size, padded);

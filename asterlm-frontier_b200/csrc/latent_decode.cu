@@ -196,7 +196,7 @@ ASTERQ_DEVICE Tile check_tile(const asterq_decode_params& p, int4 t) {
   bool ok = tile.n > 0 && tile.off >= 0;
   if (tile.kind == ASTERQ_TILE_COLD) {
     ok = ok && tile.page >= 0 && tile.page < p.n_cold_pages &&
-         tile.n <= (p.cold_scheme == ASTERQ_SCHEME_INT8 ? kColdTile8 : kColdTile) && tile.off + tile.n <= p.page_tokens;
+         tile.n <= (p.cold_scheme >= ASTERQ_SCHEME_INT8 ? kColdTile8 : kColdTile) && tile.off + tile.n <= p.page_tokens;
   } else if (tile.kind == ASTERQ_TILE_HOT) {
     ok = ok && tile.page >= 0 && tile.page < p.n_hot_pages && tile.n <= kHotTile && tile.off + tile.n <= p.page_tokens;
   } else if (tile.kind == ASTERQ_TILE_NEW) {
@@ -385,7 +385,22 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   // and 8W + 2i + 1 of code word W = 8 * group + 2tq + j, and int8 codes to dims
   // 64 * group + 16tq + 8j + i and + 4 + i.  Two int8 limbs: q = 256 hi + lo.
   uint4* qi = reinterpret_cast<uint4*>(dst);
-  for (int e = tid; e < 16 * 2 * 32; e += kPrepThreads) {
+  if (p.cold_scheme == ASTERQ_SCHEME_FLOAT8) {
+    // float8 codes are scored with fp16 MMAs: the same region holds the query in fp16 (times 2^e,
+    // exact for a bf16 query), [group g][k-step ks][nt][lane] uint2, lane (gid, tq) holding row
+    // 8nt + gid at dims 64g + 16tq + 4ks + {0, 1} (b0) and + {2, 3} (b1)
+    uint2* qf = reinterpret_cast<uint2*>(dst);
+    for (int e = tid; e < 8 * 4 * 2 * 32; e += kPrepThreads) {
+      const int ln = e & 31, nt = (e >> 5) & 1, ks = (e >> 6) & 3, g = e >> 8;
+      const int row = 8 * nt + (ln >> 2);
+      const int d0 = 64 * g + 16 * (ln & 3) + 4 * ks;
+      const float s2 = sc[row];
+      const float2 f0 = unpack_bf162(*reinterpret_cast<const uint32_t*>(qraw + row * kL + d0));
+      const float2 f1 = unpack_bf162(*reinterpret_cast<const uint32_t*>(qraw + row * kL + d0 + 2));
+      qf[e] = make_uint2(pack_half2(f0.x * s2, f0.y * s2), pack_half2(f1.x * s2, f1.y * s2));
+    }
+  }
+  for (int e = tid; e < 16 * 2 * 32 && p.cold_scheme != ASTERQ_SCHEME_FLOAT8; e += kPrepThreads) {
     const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
     const int row = 8 * nt + (ln >> 2), W = 8 * (ks >> 1) + 2 * (ln & 3) + (ks & 1);
     const int d8 = 64 * (ks >> 1) + 16 * (ln & 3) + 8 * (ks & 1);
@@ -459,13 +474,17 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
 //  kModeInt8: int8 codes (kv.py scheme "int8": one signed byte a dim, fp16 scale per group of 64),
 //    bf16 RoPE keys, in 64-token cold tiles (512 code bytes a token: a tile holds as many code
 //    bytes as a 128-token INT4 tile, so every warp's share of a stage is unchanged).
-constexpr int kModeInt4 = 0, kModeInt4RopeQ = 1, kModeInt8 = 2;
+//  kModeF8: float8 e4m3 codes (kv.py scheme "float8": one byte a dim, no scales), bf16 RoPE keys,
+//    64-token cold tiles like int8.
+constexpr int kModeInt4 = 0, kModeInt4RopeQ = 1, kModeInt8 = 2, kModeF8 = 3;
 template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
   constexpr bool kRopeQ = kMode == kModeInt4RopeQ;
   constexpr bool kB8 = kMode == kModeInt8;
-  constexpr int kCT = kB8 ? kColdTile8 : kColdTile;  // tokens of a cold tile
+  constexpr bool kF8 = kMode == kModeF8;
+  constexpr bool kBytes = kB8 || kF8;                   // one code byte a dim, 64-token cold tiles
+  constexpr int kCT = kBytes ? kColdTile8 : kColdTile;  // tokens of a cold tile
   constexpr int kCM = kCT / 64;                      // 16-token m-tiles of a cold tile per score warp
   extern __shared__ uint8_t smem_raw[];
   // 1024-byte aligned base, derived by indexing the __shared__ array so that the
@@ -555,8 +574,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_3d(st + kCodesLo, &maps.codes, y, full);
         bulk_1d(st + kCRope, reinterpret_cast<const uint8_t*>(p.cold_rope) + (int64_t)y * 32, 32 * t.n, full);
         bulk_1d(st + kCRopeScale, reinterpret_cast<const uint8_t*>(p.cold_rope_scales) + (int64_t)y8 * 2, 2 * n8, full);
-      } else if constexpr (kB8) {
-        mbar_expect_tx(full, 4 * kCodeBlock8 + kColdTile8 * 128 + 16 * t.n);
+      } else if constexpr (kBytes) {
+        mbar_expect_tx(full, 4 * kCodeBlock8 + kColdTile8 * 128 + (kF8 ? 0 : 16 * t.n));
         tma_3d(st + kCodesLo, &maps.codes, y, full);  // four blocks of [64 rows][128 B]
         tma_2d(st + kCRope, &maps.crope, 0, y, full);
       } else {
@@ -564,7 +583,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_3d(st + kCodesLo, &maps.codes, y, full);  // both halves: kCodesHi = kCodesLo + 128 rows x 128 B
         tma_2d(st + kCRope, &maps.crope, 0, y, full);
       }
-      bulk_1d(st + kScales, reinterpret_cast<const uint8_t*>(p.cold_scales) + (int64_t)y * 16, 16 * t.n, full);
+      if constexpr (!kF8)
+        bulk_1d(st + kScales, reinterpret_cast<const uint8_t*>(p.cold_scales) + (int64_t)y * 16, 16 * t.n, full);
     } else {
       const bool hot = t.kind == ASTERQ_TILE_HOT;
       const int y = hot ? t.page * p.page_tokens + t.off : t.page + t.off;
@@ -738,7 +758,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int team = warp / kTeamWarps, tw = warp % kTeamWarps;
     // cold tile token of accumulator row r (0..15) of this warp's m-tile m: INT4 tiles give each
     // warp 32 tokens in a code-word-derived order, int8 tiles 16 tokens in order
-    auto ctok = [&](int m, int r) { return kB8 ? 16 * tw + r : qk_token(tw, m, r); };
+    auto ctok = [&](int m, int r) { return kBytes ? 16 * tw + r : qk_token(tw, m, r); };
 #pragma unroll 1
     for (int it = it_begin; it < it_end; ++it) {
       begin_item(it);
@@ -816,155 +836,184 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
               }
             }
+            if constexpr (!kF8) {  // float8 scores stay in the hot tiles' units (qinv)
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
+              for (int m = 0; m < 2; ++m)
 #pragma unroll
-              for (int nt = 0; nt < 2; ++nt)
+                for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-                for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
+                  for (int c = 0; c < 4; ++c) S[m][nt][c] *= rratio[nt][c & 1];
+            }
           }
-          const uint4* qi = reinterpret_cast<const uint4*>(smem + kOffQi);
-          // Group g's integer dot products (two int8 limbs of the query, both k-steps):
-          // loads, code expansion and 16 MMAs into acc.
-          auto qk_issue = [&](int g, int (&acc)[2][2][2][4]) {
-            if constexpr (kB8) {
-              // int8 codes: lane tq's 16 bytes of group g (dims 64g + 16tq .. + 15) of each of its
-              // two tokens; k-step j takes dims 16tq + 8j + {0..3} (b0) and + {4..7} (b1), the
-              // order the query limbs were laid out in
+          if constexpr (kF8) {
+            // float8 codes: fp16 MMAs (m16n8k16) of the exact fp16 values of the e4m3 bytes against
+            // the query in fp16 (the bf16 query times 2^e, exact); no scales.  Lane tq's 16 bytes of
+            // group g (dims 64g + 16tq .. + 15) of its two tokens; k-step ks takes dims
+            // 16tq + 4ks + {0, 1} (a0 / b0) and + {2, 3} (a2 / b1)
+            const uint2* qf = reinterpret_cast<const uint2*>(smem + kOffQi);
+#pragma unroll 2
+            for (int g = 0; g < 8; ++g) {
               uint4 v[2];
 #pragma unroll
               for (int h = 0; h < 2; ++h)
                 v[h] = *reinterpret_cast<const uint4*>(st + (g >> 1) * kCodeBlock8 + swz(tok[0][h], 4 * (g & 1) + tq));
 #pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t w0 = ks == 0 ? v[0].x : ks == 1 ? v[0].y : ks == 2 ? v[0].z : v[0].w;
+                const uint32_t w1 = ks == 0 ? v[1].x : ks == 1 ? v[1].y : ks == 2 ? v[1].z : v[1].w;
+                const uint32_t a[4] = {e4m3x2_to_f16x2(w0), e4m3x2_to_f16x2(w1), e4m3x2_to_f16x2(w0 >> 16),
+                                       e4m3x2_to_f16x2(w1 >> 16)};
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                  const uint2 bq = qf[((g * 4 + ks) * 2 + nt) * 32 + lane];
+                  mma_f16(S[0][nt], a, bq.x, bq.y);
+                }
+              }
+            }
+          } else {
+            const uint4* qi = reinterpret_cast<const uint4*>(smem + kOffQi);
+            // Group g's integer dot products (two int8 limbs of the query, both k-steps):
+            // loads, code expansion and 16 MMAs into acc.
+            auto qk_issue = [&](int g, int (&acc)[2][2][2][4]) {
+              if constexpr (kB8) {
+                // int8 codes: lane tq's 16 bytes of group g (dims 64g + 16tq .. + 15) of each of its
+                // two tokens; k-step j takes dims 16tq + 8j + {0..3} (b0) and + {4..7} (b1), the
+                // order the query limbs were laid out in
+                uint4 v[2];
+  #pragma unroll
+                for (int h = 0; h < 2; ++h)
+                  v[h] = *reinterpret_cast<const uint4*>(st + (g >> 1) * kCodeBlock8 + swz(tok[0][h], 4 * (g & 1) + tq));
+  #pragma unroll
+                for (int j = 0; j < 2; ++j) {
+                  const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
+                  const uint32_t a[4] = {j ? v[0].z : v[0].x, j ? v[1].z : v[1].x, j ? v[0].w : v[0].y, j ? v[1].w : v[1].y};
+  #pragma unroll
+                  for (int nt = 0; nt < 2; ++nt) {
+                    if (j == 0) {
+                      mma_s8_from(acc[0][0][nt], a, bq[nt].x, bq[nt].y, kAccBias);
+                      mma_s8_from(acc[1][0][nt], a, bq[nt].z, bq[nt].w, kAccBias);
+                    } else {
+                      mma_s8(acc[0][0][nt], a, bq[nt].x, bq[nt].y);
+                      mma_s8(acc[1][0][nt], a, bq[nt].z, bq[nt].w);
+                    }
+                  }
+                }
+                return;
+              }
+              // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens;
+              // group 8 (quantized RoPE keys): words 2tq and 2tq + 1 of the token's 32-byte RoPE code
+              // row, whose query limbs follow those of group 7 (k-steps 16 and 17)
+              const int region = (g < 4) ? kCodesLo : kCodesHi;
+              const int chunk = 2 * (g & 3) + (tq >> 1);
+              uint2 v[2][2];
+  #pragma unroll
+              for (int m = 0; m < 2; ++m)
+  #pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const int off = (kRopeQ && g == 8) ? kCRope + 32 * tok[m][h] + 8 * tq
+                                                     : region + swz(tok[m][h], chunk) + 8 * (tq & 1);
+                  v[m][h] = *reinterpret_cast<const uint2*>(st + off);
+                }
+  #pragma unroll
               for (int j = 0; j < 2; ++j) {
                 const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
-                const uint32_t a[4] = {j ? v[0].z : v[0].x, j ? v[1].z : v[1].x, j ? v[0].w : v[0].y, j ? v[1].w : v[1].y};
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                  if (j == 0) {
-                    mma_s8_from(acc[0][0][nt], a, bq[nt].x, bq[nt].y, kAccBias);
-                    mma_s8_from(acc[1][0][nt], a, bq[nt].z, bq[nt].w, kAccBias);
-                  } else {
-                    mma_s8(acc[0][0][nt], a, bq[nt].x, bq[nt].y);
-                    mma_s8(acc[1][0][nt], a, bq[nt].z, bq[nt].w);
+  #pragma unroll
+                for (int m = 0; m < 2; ++m) {
+                  const uint32_t x0 = j ? v[m][0].y : v[m][0].x, x1 = j ? v[m][1].y : v[m][1].x;
+                  const uint32_t a[4] = {s8_lo_nibbles(x0), s8_lo_nibbles(x1), s8_hi_nibbles(x0), s8_hi_nibbles(x1)};
+  #pragma unroll
+                  for (int nt = 0; nt < 2; ++nt) {
+                    if (j == 0) {
+                      mma_s8_from(acc[0][m][nt], a, bq[nt].x, bq[nt].y, kAccBias);
+                      mma_s8_from(acc[1][m][nt], a, bq[nt].z, bq[nt].w, kAccBias);
+                    } else {
+                      mma_s8(acc[0][m][nt], a, bq[nt].x, bq[nt].y);
+                      mma_s8(acc[1][m][nt], a, bq[nt].z, bq[nt].w);
+                    }
                   }
                 }
               }
-              return;
-            }
-            // code words 8g + 2tq (k-step 2g) and 8g + 2tq + 1 (k-step 2g + 1) of the four tokens;
-            // group 8 (quantized RoPE keys): words 2tq and 2tq + 1 of the token's 32-byte RoPE code
-            // row, whose query limbs follow those of group 7 (k-steps 16 and 17)
-            const int region = (g < 4) ? kCodesLo : kCodesHi;
-            const int chunk = 2 * (g & 3) + (tq >> 1);
-            uint2 v[2][2];
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const int off = (kRopeQ && g == 8) ? kCRope + 32 * tok[m][h] + 8 * tq
-                                                   : region + swz(tok[m][h], chunk) + 8 * (tq & 1);
-                v[m][h] = *reinterpret_cast<const uint2*>(st + off);
-              }
-#pragma unroll
-            for (int j = 0; j < 2; ++j) {
-              const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
-#pragma unroll
-              for (int m = 0; m < 2; ++m) {
-                const uint32_t x0 = j ? v[m][0].y : v[m][0].x, x1 = j ? v[m][1].y : v[m][1].x;
-                const uint32_t a[4] = {s8_lo_nibbles(x0), s8_lo_nibbles(x1), s8_hi_nibbles(x0), s8_hi_nibbles(x1)};
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                  if (j == 0) {
-                    mma_s8_from(acc[0][m][nt], a, bq[nt].x, bq[nt].y, kAccBias);
-                    mma_s8_from(acc[1][m][nt], a, bq[nt].z, bq[nt].w, kAccBias);
-                  } else {
-                    mma_s8(acc[0][m][nt], a, bq[nt].x, bq[nt].y);
-                    mma_s8(acc[1][m][nt], a, bq[nt].z, bq[nt].w);
+            };
+            // S += scale_g x (256 hi + lo + B), the biased accumulators read as exact floats
+            // (packed f32x2 arithmetic: two accumulator elements per instruction; elements
+            // c = 0,1 belong to token row gid, c = 2,3 to row gid + 8).  The hi limb's bias B is
+            // subtracted exactly; the lo limb keeps its bias, so each token's S carries
+            // B x (sum of its group scales), subtracted once after the last group (|S| stays
+            // below ~2^27 x scale, so the extra rounding is ~2^-21 of the score).
+            float ssum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
+            auto qk_finish = [&](int g, const int (&acc)[2][2][2][4]) {
+              const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
+  #pragma unroll
+              for (int m = 0; m < kCM; ++m) {
+                const float s0 = __half2float(scl[8 * tok[m][0] + g]);
+                const float s1 = __half2float(scl[8 * tok[m][1] + g]);
+                ssum[m][0] += s0;
+                ssum[m][1] += s1;
+  #pragma unroll
+                for (int nt = 0; nt < 2; ++nt)
+  #pragma unroll
+                  for (int h = 0; h < 2; ++h) {
+                    const float2 fh = add2(make_float2(__int_as_float(acc[0][m][nt][2 * h]), __int_as_float(acc[0][m][nt][2 * h + 1])), bias2);
+                    const float2 fl = make_float2(__int_as_float(acc[1][m][nt][2 * h]), __int_as_float(acc[1][m][nt][2 * h + 1]));
+                    const float sc = h ? s1 : s0;
+                    const float2 r = fma2(fma2(fh, k256, fl), make_float2(sc, sc),
+                                          make_float2(S[m][nt][2 * h], S[m][nt][2 * h + 1]));
+                    S[m][nt][2 * h] = r.x;
+                    S[m][nt][2 * h + 1] = r.y;
                   }
-                }
               }
-            }
-          };
-          // S += scale_g x (256 hi + lo + B), the biased accumulators read as exact floats
-          // (packed f32x2 arithmetic: two accumulator elements per instruction; elements
-          // c = 0,1 belong to token row gid, c = 2,3 to row gid + 8).  The hi limb's bias B is
-          // subtracted exactly; the lo limb keeps its bias, so each token's S carries
-          // B x (sum of its group scales), subtracted once after the last group (|S| stays
-          // below ~2^27 x scale, so the extra rounding is ~2^-21 of the score).
-          float ssum[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
-          auto qk_finish = [&](int g, const int (&acc)[2][2][2][4]) {
-            const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
-#pragma unroll
-            for (int m = 0; m < kCM; ++m) {
-              const float s0 = __half2float(scl[8 * tok[m][0] + g]);
-              const float s1 = __half2float(scl[8 * tok[m][1] + g]);
-              ssum[m][0] += s0;
-              ssum[m][1] += s1;
-#pragma unroll
-              for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
+            };
+            // two groups in flight: group g + 1's MMAs run on the tensor pipe while
+            // group g's accumulators are scaled into S
+            int accA[2][2][2][4], accB[2][2][2][4];
+            if constexpr (kRopeQ) {
+              // group 8, the quantized RoPE keys, first: its MMAs overlap group 0's, then
+              // S = (256 hi + lo) x token scale x (latent / RoPE fixed-point scales), both limbs'
+              // biases subtracted exactly (packed f32x2: elements 2h, 2h + 1 are token tok[m][h]
+              // against rows 8nt + 2tq + {0, 1})
+              qk_issue(8, accB);
+              qk_issue(0, accA);
+              // (the scales were copied from the 8-token boundary below the tile's first token
+              // page * page_tokens + off; page_tokens is a multiple of 16, so that is off & 7 tokens back)
+              const __half* rsc = reinterpret_cast<const __half*>(st + kCRopeScale) + (t.off & 7);
+              const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
+  #pragma unroll
+              for (int m = 0; m < 2; ++m)
+  #pragma unroll
                 for (int h = 0; h < 2; ++h) {
-                  const float2 fh = add2(make_float2(__int_as_float(acc[0][m][nt][2 * h]), __int_as_float(acc[0][m][nt][2 * h + 1])), bias2);
-                  const float2 fl = make_float2(__int_as_float(acc[1][m][nt][2 * h]), __int_as_float(acc[1][m][nt][2 * h + 1]));
-                  const float sc = h ? s1 : s0;
-                  const float2 r = fma2(fma2(fh, k256, fl), make_float2(sc, sc),
-                                        make_float2(S[m][nt][2 * h], S[m][nt][2 * h + 1]));
-                  S[m][nt][2 * h] = r.x;
-                  S[m][nt][2 * h + 1] = r.y;
+                  const float rs = __half2float(rsc[tok[m][h]]);
+  #pragma unroll
+                  for (int nt = 0; nt < 2; ++nt) {
+                    const float2 fh = add2(make_float2(__int_as_float(accB[0][m][nt][2 * h]), __int_as_float(accB[0][m][nt][2 * h + 1])), bias2);
+                    const float2 fl = add2(make_float2(__int_as_float(accB[1][m][nt][2 * h]), __int_as_float(accB[1][m][nt][2 * h + 1])), bias2);
+                    const float2 w = mul2(make_float2(rs, rs), make_float2(rratio[nt][0], rratio[nt][1]));
+                    const float2 r = mul2(fma2(fh, k256, fl), w);
+                    S[m][nt][2 * h] = r.x;
+                    S[m][nt][2 * h + 1] = r.y;
+                  }
                 }
+            } else {
+              qk_issue(0, accA);
             }
-          };
-          // two groups in flight: group g + 1's MMAs run on the tensor pipe while
-          // group g's accumulators are scaled into S
-          int accA[2][2][2][4], accB[2][2][2][4];
-          if constexpr (kRopeQ) {
-            // group 8, the quantized RoPE keys, first: its MMAs overlap group 0's, then
-            // S = (256 hi + lo) x token scale x (latent / RoPE fixed-point scales), both limbs'
-            // biases subtracted exactly (packed f32x2: elements 2h, 2h + 1 are token tok[m][h]
-            // against rows 8nt + 2tq + {0, 1})
-            qk_issue(8, accB);
-            qk_issue(0, accA);
-            // (the scales were copied from the 8-token boundary below the tile's first token
-            // page * page_tokens + off; page_tokens is a multiple of 16, so that is off & 7 tokens back)
-            const __half* rsc = reinterpret_cast<const __half*>(st + kCRopeScale) + (t.off & 7);
-            const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float rs = __half2float(rsc[tok[m][h]]);
-#pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                  const float2 fh = add2(make_float2(__int_as_float(accB[0][m][nt][2 * h]), __int_as_float(accB[0][m][nt][2 * h + 1])), bias2);
-                  const float2 fl = add2(make_float2(__int_as_float(accB[1][m][nt][2 * h]), __int_as_float(accB[1][m][nt][2 * h + 1])), bias2);
-                  const float2 w = mul2(make_float2(rs, rs), make_float2(rratio[nt][0], rratio[nt][1]));
-                  const float2 r = mul2(fma2(fh, k256, fl), w);
-                  S[m][nt][2 * h] = r.x;
-                  S[m][nt][2 * h + 1] = r.y;
+  #pragma unroll 1
+            for (int g = 0; g < 8; g += 2) {
+              qk_issue(g + 1, accB);
+              qk_finish(g, accA);
+              if (g + 2 < 8) qk_issue(g + 2, accA);
+              qk_finish(g + 1, accB);
+            }
+            // the lo limbs' bias: B x (sum of the token's group scales)
+  #pragma unroll
+            for (int m = 0; m < kCM; ++m)
+  #pragma unroll
+              for (int nt = 0; nt < 2; ++nt)
+  #pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                  const float corr = -kAccBiasF * ssum[m][h];
+                  S[m][nt][2 * h] += corr;
+                  S[m][nt][2 * h + 1] += corr;
                 }
-              }
-          } else {
-            qk_issue(0, accA);
           }
-#pragma unroll 1
-          for (int g = 0; g < 8; g += 2) {
-            qk_issue(g + 1, accB);
-            qk_finish(g, accA);
-            if (g + 2 < 8) qk_issue(g + 2, accA);
-            qk_finish(g + 1, accB);
-          }
-          // the lo limbs' bias: B x (sum of the token's group scales)
-#pragma unroll
-          for (int m = 0; m < kCM; ++m)
-#pragma unroll
-            for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-              for (int h = 0; h < 2; ++h) {
-                const float corr = -kAccBiasF * ssum[m][h];
-                S[m][nt][2 * h] += corr;
-                S[m][nt][2 * h + 1] += corr;
-              }
         } else {
           // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
           // S[1] is a second partial accumulator (odd groups) folded in below
@@ -1008,7 +1057,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // 2tq, 2tq + 1 of this lane's four tokens) move to registers, and the stage is
         // released to the producer before the softmax.
         uint32_t kept_scl[2][2] = {{0u, 0u}, {0u, 0u}};
-        if (cold) {
+        if (cold && !kF8) {  // (float8 chunks have no scales)
           const uint16_t* scl = reinterpret_cast<const uint16_t*>(st + kScales);
 #pragma unroll
           for (int m = 0; m < kCM; ++m)
@@ -1038,7 +1087,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const int tk = cold ? ctok(m, gid + 8 * h) : 8 * tw + gid;
               bool valid = (m < n_m) && (cold || h == 0) && tk < t.n;
               if (t.kind == ASTERQ_TILE_NEW) valid = valid && (t.off + tk) <= (rb * kRows + r) / H;
-              float sv = S[m][nt][c] * (cold ? qinvi[nt][cc] : qinv[nt][cc]);
+              float sv = S[m][nt][c] * ((cold && !kF8) ? qinvi[nt][cc] : qinv[nt][cc]);
               if (p.logit_softcap > 0.0f) sv = p.logit_softcap * tanhf(sv / p.logit_softcap);
               sv = valid ? sv : -INFINITY;
               S[m][nt][c] = sv;
@@ -1204,7 +1253,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int c = 0; c < 4; ++c) {
               // order 0, INT4: rows gid / gid + 8 of m-tile mi are dims 2(4gid + mi) / + 1 of the group;
               // int8: dims 8gid + mi / 8gid + 4 + mi
-              const int dim = (order == 0) ? (kB8 ? 64 * g + 8 * gid + 4 * (c >> 1) + mi : 64 * g + 2 * (4 * gid + mi) + (c >> 1))
+              const int dim = (order == 0) ? (kBytes ? 64 * g + 8 * gid + 4 * (c >> 1) + mi : 64 * g + 2 * (4 * gid + mi) + (c >> 1))
                                            : 64 * g + 16 * mi + gid + 8 * (c >> 1);
               scratch_o[(8 * nt + 2 * tq + (c & 1)) * kL + dim] = o[mi][nt][c];
             }
@@ -1231,7 +1280,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // of all 128 tokens; hot: its bf16 A fragments of all 32 tokens), so the stage is
         // released, and refilled with tile i + 3, before this tile's p is even ready.
         uint32_t xs[8][4];
-        if (cold && kB8) {
+        if (cold && kBytes) {
           // int8: 8 bytes (dims 64g + 8gid .. + 7) of each of the lane's four tokens per k-step:
           // token j of k-step kt -> xs[2kt + (j >> 1)][2(j & 1) .. + 1]
 #pragma unroll
@@ -1240,8 +1289,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int tk[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
-              const uint2 w = *reinterpret_cast<const uint2*>(st + (g >> 1) * kCodeBlock8 +
-                                                               swz(tk[j], 4 * (g & 1) + (gid >> 1)) + 8 * (gid & 1));
+              uint2 w = *reinterpret_cast<const uint2*>(st + (g >> 1) * kCodeBlock8 +
+                                                         swz(tk[j], 4 * (g & 1) + (gid >> 1)) + 8 * (gid & 1));
+              // rows past the tile's tokens hold whatever follows in the pool: any int8 byte is a
+              // finite value that p = 0 cancels, but an e4m3 byte may be NaN (0 x NaN poisons the sum)
+              if (kF8 && tk[j] >= t.n) w = make_uint2(0u, 0u);
               xs[2 * kt + (j >> 1)][2 * (j & 1)] = w.x;
               xs[2 * kt + (j >> 1)][2 * (j & 1) + 1] = w.y;
             }
@@ -1336,11 +1388,34 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t s01 = *reinterpret_cast<const uint32_t*>(sT + t0);
             const uint32_t s89 = *reinterpret_cast<const uint32_t*>(sT + t0 + 8);
             uint32_t pb[2][2];
-            pb[0][0] = hmul2_u32(pr[0], s01);
-            pb[0][1] = hmul2_u32(pr[1], s89);
-            pb[1][0] = hmul2_u32(pr[2], s01);
-            pb[1][1] = hmul2_u32(pr[3], s89);
-            if constexpr (kB8) {
+            if constexpr (kF8) {  // float8 chunks have no scales
+              pb[0][0] = pr[0];
+              pb[0][1] = pr[1];
+              pb[1][0] = pr[2];
+              pb[1][1] = pr[3];
+            } else {
+              pb[0][0] = hmul2_u32(pr[0], s01);
+              pb[0][1] = hmul2_u32(pr[1], s89);
+              pb[1][0] = hmul2_u32(pr[2], s01);
+              pb[1][1] = hmul2_u32(pr[3], s89);
+            }
+            if constexpr (kF8) {
+#pragma unroll
+              for (int mi = 0; mi < 4; ++mi) {
+                // as for int8 below, with the byte pair (token t0, t0 + 1) in bits 0-15 converted
+                // from e4m3 to fp16 (the low byte to the low half)
+                const uint32_t sel = (uint32_t)mi | ((uint32_t)(4 + mi) << 4);
+                const uint32_t* x01 = xs[2 * kt];
+                const uint32_t* x89 = xs[2 * kt + 1];
+                uint32_t a[4];
+                a[0] = e4m3x2_to_f16x2(prmt(x01[0], x01[2], sel));
+                a[1] = e4m3x2_to_f16x2(prmt(x01[1], x01[3], sel));
+                a[2] = e4m3x2_to_f16x2(prmt(x89[0], x89[2], sel));
+                a[3] = e4m3x2_to_f16x2(prmt(x89[1], x89[3], sel));
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) mma_f16(o[mi][nt], a, pb[nt][0], pb[nt][1]);
+              }
+            } else if constexpr (kB8) {
 #pragma unroll
               for (int mi = 0; mi < 4; ++mi) {
                 // rows gid / gid+8 of m-tile mi are dims 8gid + mi / 8gid + 4 + mi of group g: byte mi
@@ -1707,8 +1782,8 @@ int validate(const asterq_decode_params* p) {
   if (p->out_dtype != ASTERQ_DTYPE_F32 && p->out_dtype != ASTERQ_DTYPE_BF16)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: out_dtype must be f32 or bf16");
   if (p->cold_scheme != ASTERQ_SCHEME_HADAMARD_INT4 && p->cold_scheme != ASTERQ_SCHEME_INT4 &&
-      p->cold_scheme != ASTERQ_SCHEME_INT8)
-    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: cold scheme %d unsupported (hadamard_int4, int4 or int8)",
+      p->cold_scheme != ASTERQ_SCHEME_INT8 && p->cold_scheme != ASTERQ_SCHEME_FLOAT8)
+    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: cold scheme %d unsupported (hadamard_int4, int4, int8 or float8)",
                      p->cold_scheme);
   if (p->n_items < 0 || p->n_tiles < 0 || p->n_combine < 0 || p->n_slots < 0)
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: negative table size");
@@ -1716,9 +1791,9 @@ int validate(const asterq_decode_params* p) {
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null pointer");
   if (p->rope_scheme != ASTERQ_ROPE_BF16 && p->rope_scheme != ASTERQ_ROPE_QUANTIZED)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: rope scheme %d unsupported (bf16 or quantized)", p->rope_scheme);
-  if (p->rope_scheme == ASTERQ_ROPE_QUANTIZED && p->cold_scheme == ASTERQ_SCHEME_INT8)
+  if (p->rope_scheme == ASTERQ_ROPE_QUANTIZED && p->cold_scheme >= ASTERQ_SCHEME_INT8)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: quantized RoPE keys are read with the INT4 schemes only");
-  if (p->n_cold_pages > 0 && (!p->cold_codes || !p->cold_scales || !p->cold_rope))
+  if (p->n_cold_pages > 0 && (!p->cold_codes || (!p->cold_scales && p->cold_scheme != ASTERQ_SCHEME_FLOAT8) || !p->cold_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null cold pool");
   if (p->n_cold_pages > 0 && p->rope_scheme == ASTERQ_ROPE_QUANTIZED && !p->cold_rope_scales)
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: quantized RoPE keys need cold_rope_scales");
@@ -1829,7 +1904,8 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     if (dev >= 64 || !(configured & (1ull << dev))) {
       const void* kernels[] = {reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt4>),
                                reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt4RopeQ>),
-                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt8>)};
+                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt8>),
+                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeF8>)};
       cudaError_t e = cudaSuccess;
       for (const void* fn : kernels)
         if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
@@ -1853,7 +1929,7 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
     // base for the map of an empty pool
     const void* dummy = p->q_lat;
     const int64_t cold_rows = p->n_cold_pages * p->page_tokens, hot_rows = p->n_hot_pages * p->page_tokens;
-    const bool b8 = p->cold_scheme == ASTERQ_SCHEME_INT8;
+    const bool b8 = p->cold_scheme == ASTERQ_SCHEME_INT8 || p->cold_scheme == ASTERQ_SCHEME_FLOAT8;  // byte codes
     const int ct = b8 ? dec::kColdTile8 : dec::kColdTile;
     if ((st = b8 ? dec::make_map(&maps.codes, p->cold_codes, cold_rows, 512, ct, dummy, 1024, 4)
                  : dec::make_map(&maps.codes, p->cold_codes, cold_rows, 256, ct, dummy, 1024, 2)) ||
@@ -1884,7 +1960,8 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      cudaError_t e = (kp.cold_scheme == ASTERQ_SCHEME_INT8) ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt8>, kp, maps)
+      cudaError_t e = (kp.cold_scheme == ASTERQ_SCHEME_FLOAT8) ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeF8>, kp, maps)
+                      : (kp.cold_scheme == ASTERQ_SCHEME_INT8) ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt8>, kp, maps)
                       : (kp.rope_scheme == ASTERQ_ROPE_QUANTIZED)
                           ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4RopeQ>, kp, maps)
                           : cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4>, kp, maps);

@@ -881,6 +881,10 @@ def extras(dev, args) -> dict:
     wl = c3_workload(dev, seed=1000, scheme="int8")
     decode_rate(wl, "c3_int8_1gpu", 20)
     del wl
+    # C3 with cache_dtype="float8": 512 e4m3 bytes a cold token, no scales (640 B with the RoPE key)
+    wl = c3_workload(dev, seed=1000, scheme="float8")
+    decode_rate(wl, "c3_float8_1gpu", 20)
+    del wl
     wl = c4_workload(dev)
     decode_rate(wl, "c4_long_context_1gpu", 30)
     del wl

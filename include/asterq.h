@@ -52,6 +52,7 @@ extern "C" {
 #define ASTERQ_SCHEME_HADAMARD_INT4 0
 #define ASTERQ_SCHEME_INT4 1
 #define ASTERQ_SCHEME_INT8 2
+#define ASTERQ_SCHEME_FLOAT8 3 /* kv.py:85-89 "float8": x.to(float8_e4m3fn), one byte a value, no scales */
 
 /* cold RoPE keys (cache.py:160-164: quantized only with quantize_rope=True) */
 #define ASTERQ_ROPE_BF16 0      /* cold_rope: bf16 [tokens][rope_dim] */
@@ -79,6 +80,10 @@ const char* asterq_last_error(void);
  * where P = next power of two >= dim for hadamard_int4 and
  * ceil(dim/group_size)*group_size otherwise.  x_dtype: ASTERQ_DTYPE_*.
  * x_row_stride is in elements.  P <= 512, group_size in {16, 32, 64}.
+ * ASTERQ_SCHEME_FLOAT8: codes [n_tokens, dim] float8 e4m3 bytes as torch's
+ * x.to(torch.float8_e4m3fn) writes them (round to nearest even, subnormals kept,
+ * NaN, infinities and |x| > 464 become NaN with the sign of x); no scales (`scales`
+ * and `group_size` are not used).
  */
 int asterq_quantize(const void* x, int x_dtype, int64_t n_tokens, int dim, int64_t x_row_stride, int scheme,
                     int group_size, void* codes, void* scales, void* stream);
@@ -86,7 +91,8 @@ int asterq_quantize(const void* x, int x_dtype, int64_t n_tokens, int dim, int64
 /*
  * Inverse of asterq_quantize (dequantize_tensor, quantization/kv.py:121-134):
  * codes * float(scale), inverse normalized FWHT for hadamard_int4, cropped to
- * `dim`, rounded to out_dtype.  Bit-identical to the reference.
+ * `dim`, rounded to out_dtype.  Bit-identical to the reference.  ASTERQ_SCHEME_FLOAT8:
+ * the e4m3 values widened to out_dtype (exact); `scales` is not used.
  */
 int asterq_dequantize(const void* codes, const void* scales, int64_t n_tokens, int dim, int scheme, int group_size,
                       void* out, int out_dtype, int64_t out_row_stride, void* stream);

@@ -135,8 +135,27 @@ class Quantized:
         return int(total)
 
 
+def float8_bytes(x: np.ndarray) -> np.ndarray:
+    """kv.py:85-89: ``x.to(torch.float8_e4m3fn)`` as raw bytes.  The reference's float8 scheme
+    is torch's own cast (round to nearest even, NaN for |x| > 464 and non-finite values), so
+    the oracle calls the same cast on the CPU rather than restating it."""
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(np.asarray(x, dtype=np.float32)))
+    return t.to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+
+
+def float8_values(codes: np.ndarray) -> np.ndarray:
+    """The float32 values of e4m3 bytes (exact)."""
+    import torch
+
+    t = torch.from_numpy(np.ascontiguousarray(codes, dtype=np.uint8))
+    return t.view(torch.float8_e4m3fn).float().numpy()
+
+
 def quantize(x: np.ndarray, scheme: str = "hadamard_int4", group_size: int = 64) -> Quantized:
-    """Groupwise absmax quantizer (kv.py:76-118) for int8 / int4 / hadamard_int4.
+    """Groupwise absmax quantizer (kv.py:76-118) for int8 / int4 / hadamard_int4, and the
+    scale-free float8 cast (kv.py:85-89).
 
     ``x`` holds the source values already widened to float32 (the reference's
     ``x.float()``, kv.py:96).  The scale is ``amax(|g|).clamp_min(1e-8) / qmax``
@@ -144,6 +163,10 @@ def quantize(x: np.ndarray, scheme: str = "hadamard_int4", group_size: int = 64)
     round-half-to-even, clamped (kv.py:107); the stored scale is the float32
     scale rounded to float16 (kv.py:112).
     """
+    if scheme == "float8":
+        x = np.asarray(x, dtype=np.float32)
+        return Quantized(data=float8_bytes(x), scale=None, original_shape=tuple(x.shape), padded_dim=x.shape[-1],
+                         group_size=group_size, scheme=scheme)
     if scheme not in {"int8", "int4", "hadamard_int4"}:
         raise ValueError(f"unsupported quantization scheme: {scheme}")
     if group_size <= 0:
@@ -176,6 +199,8 @@ def quantize(x: np.ndarray, scheme: str = "hadamard_int4", group_size: int = 64)
 
 def dequantize(q: Quantized) -> np.ndarray:
     """kv.py:121-134, returning float32 (the oracle never narrows)."""
+    if q.scheme == "float8":
+        return float8_values(q.data).reshape(q.original_shape).astype(np.float32)
     if q.scale is None:
         raise RuntimeError("integer quantized tensor is missing scales")
     width = q.scale.shape[-2] * q.group_size
@@ -220,7 +245,7 @@ class ColdChunk:
         padded = next_power_of_two(self.latent_dim) if self.scheme == "hadamard_int4" else self.latent_dim
         q = Quantized(
             data=self.codes,
-            scale=self.scales.reshape(self.length, -1, 1),
+            scale=None if self.scales is None else self.scales.reshape(self.length, -1, 1),
             original_shape=(self.length, self.latent_dim),
             padded_dim=padded,
             group_size=self.group_size,
@@ -406,7 +431,8 @@ def cold_chunk(latent: np.ndarray, rope: np.ndarray, group_size: int = 64, schem
     """``LatentLayerCache._encode`` of one chunk (cache.py:160-164): the latent always, the RoPE
     keys only with ``quantize_rope`` (else kept as they are)."""
     q = quantize(latent, scheme, group_size)
-    chunk = ColdChunk(codes=q.data, scales=q.scale.reshape(latent.shape[0], -1), rope=rope.copy(),
+    scales = None if q.scale is None else q.scale.reshape(latent.shape[0], -1)
+    chunk = ColdChunk(codes=q.data, scales=scales, rope=rope.copy(),
                       latent_dim=latent.shape[-1], group_size=group_size, scheme=scheme)
     if quantize_rope:
         qr = quantize(rope, scheme, group_size)

@@ -98,7 +98,7 @@ def decode_case(seed, ctx, q_len, recent, chunk, scheme="hadamard_int4", quantiz
         "out_fp32": outs["fp32"],
         "out_bf16": outs["bf16"],
         "codes_sha256": sha(*[c.data for c in cache.cold_latent]),
-        "scales_sha256": sha(*[c.scale for c in cache.cold_latent]),
+        "scales_sha256": sha(*[c.scale for c in cache.cold_latent if c.scale is not None]),
         **({"rope_codes_sha256": sha(*[c.data for c in cache.cold_rope]),
             "rope_scales_sha256": sha(*[c.scale for c in cache.cold_rope])} if quantize_rope else {}),
     }
@@ -151,6 +151,19 @@ def main() -> None:
         qr = quantize_tensor(xr, scheme, group_size=64)
         fixtures[f"rope_{scheme}_codes"] = qr.data.numpy()
         fixtures[f"rope_{scheme}_scales"] = qr.scale.numpy().reshape(xr.shape[0])
+    # float8 (kv.py:85-89: x.to(torch.float8_e4m3fn), no scales) from bf16 and from float32:
+    # normal values, subnormals and their rounding ties, the top of the range (448 < |x| <= 464
+    # rounds to 448, beyond it NaN), infinities, NaN and signed zeros
+    g = torch.Generator().manual_seed(12)
+    xf = torch.randn(64, 512, generator=g) * torch.logspace(-3, 2.5, 512)
+    edge = torch.tensor([0.0, -0.0, 2.0 ** -10, -(2.0 ** -10), 3 * 2.0 ** -11, 2.0 ** -9, 1e-30, 447.0, 448.0,
+                         456.0, 460.0, 464.0, 464.5, 470.0, 1e4, -1e4, float("inf"), float("-inf"), float("nan"),
+                         1.0625, 1.1875, -1.0625, 0.01, -0.01, 240.0, 248.0, 232.0, 3.0e-3, -7.8e-3, 1.5, 2.5, 3.5])
+    xf[0, : edge.numel()] = edge
+    fixtures["f8_x_bits"] = bf16_bits(xf.to(torch.bfloat16))
+    fixtures["f8_codes_bf16"] = quantize_tensor(xf.to(torch.bfloat16), "float8").data.view(torch.uint8).numpy()
+    fixtures["f8_x_f32"] = xf.numpy()
+    fixtures["f8_codes_f32"] = quantize_tensor(xf, "float8").data.view(torch.uint8).numpy()
     np.savez_compressed(HERE / "encode_golden.npz", **fixtures)
 
     # ---- decode -----------------------------------------------------------------
@@ -169,6 +182,9 @@ def main() -> None:
         # int8 cold chunks (kv.py scheme "int8": one signed byte a dim, no rotation)
         "q8": dict(seed=10, ctx=2400, q_len=1, recent=512, chunk=512, scheme="int8"),
         "q8t3": dict(seed=11, ctx=1900, q_len=3, recent=512, chunk=512, scheme="int8"),
+        # float8 cold chunks (kv.py:85-89: e4m3 values, no scales)
+        "f8": dict(seed=13, ctx=2300, q_len=1, recent=512, chunk=512, scheme="float8"),
+        "f8t3": dict(seed=14, ctx=1800, q_len=3, recent=512, chunk=512, scheme="float8"),
     }
     dec: dict[str, np.ndarray] = {}
     for name, kw in cases.items():

@@ -9,9 +9,11 @@ def test_unsupported_configurations_raise():
     from asterq.cache import LatentLayerCache
 
     with pytest.raises(NotImplementedError):
-        LatentLayerCache("float8")
+        LatentLayerCache("int2")
     with pytest.raises(NotImplementedError):
         LatentLayerCache("int8", quantize_rope=True)
+    with pytest.raises(NotImplementedError):
+        LatentLayerCache("float8", quantize_rope=True)
     with pytest.raises(NotImplementedError):
         LatentLayerCache("hadamard_int4", group_size=32)
     with pytest.raises(ValueError):

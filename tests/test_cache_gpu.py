@@ -86,7 +86,7 @@ def test_batch_rows_are_independent(cuda):
         assert torch.equal(both.latent[row], one.latent[0])
 
 
-@pytest.mark.parametrize("scheme", ["hadamard_int4", "int4", "int8"])
+@pytest.mark.parametrize("scheme", ["hadamard_int4", "int4", "int8", "float8"])
 def test_materialize_and_iter_chunks_match_oracle(cuda, scheme):
     from asterq.cache import LatentLayerCache
 
@@ -106,7 +106,7 @@ def test_materialize_and_iter_chunks_match_oracle(cuda, scheme):
 
 
 @pytest.mark.parametrize("q_len,scheme", [(1, "hadamard_int4"), (3, "hadamard_int4"), (1, "int4"), (3, "int4"),
-                                          (1, "int8"), (3, "int8")])
+                                          (1, "int8"), (3, "int8"), (1, "float8"), (3, "float8")])
 def test_latent_attention_over_the_cache(cuda, q_len, scheme):
     """Every cold scheme the kernels read: hadamard_int4 (scores in the rotated basis), plain
     int4 (kv.py scheme "int4", no rotation) and int8 (one signed byte a dim, 64-token tiles);
@@ -172,26 +172,31 @@ def test_quantize_rope_cache_matches_reference(cuda, scheme, dtype):
         assert O.rel_l2(got, want) <= 1e-3 and O.max_abs(got, want) <= 2e-2, q_len
 
 
-def test_int8_cache_codes_bytes_and_decode_loop(cuda):
-    """cache_dtype="int8" (kv.py:76-118 with qmax 127): flushed chunks hold the reference's int8
-    codes and scales bit for bit, ``num_bytes`` counts 512 code bytes a cold token, and a decode
-    loop of appends and attention (device planner, 64-token cold tiles) matches the oracle."""
+@pytest.mark.parametrize("scheme", ["int8", "float8"])
+def test_byte_cache_codes_bytes_and_decode_loop(cuda, scheme):
+    """cache_dtype="int8" (kv.py:76-118 with qmax 127) and "float8" (kv.py:85-89, no scales):
+    flushed chunks hold the reference's codes (and scales) bit for bit, ``num_bytes`` counts 512
+    code bytes a cold token, and a decode loop of appends and attention (device planner, 64-token
+    cold tiles) matches the oracle."""
     from asterq.attention import latent_attention
     from asterq.cache import LatentLayerCache
 
     n, steps = 2000, 40
     inp = _inputs(43, n + steps, 1)
     lat, rope = inp["latent"], inp["rope"]
-    cache = LatentLayerCache("int8", 64, recent_tokens=256, chunk_tokens=512)
+    cache = LatentLayerCache(scheme, 64, recent_tokens=256, chunk_tokens=512)
     cache.append(lat[None, :n].to(cuda), rope[None, :n].to(cuda), None, 0)
-    ref = O.build_cache_from_tokens(_bf16_np(lat[:n]), _bf16_np(rope[:n]), 256, 512, scheme="int8")
+    ref = O.build_cache_from_tokens(_bf16_np(lat[:n]), _bf16_np(rope[:n]), 256, 512, scheme=scheme)
     assert cache.cold_chunks == len(ref.cold) > 0
     for q, c in zip(cache.cold_latent, ref.cold):
-        assert q.data.dtype == torch.int8 and q.scheme == "int8"
-        np.testing.assert_array_equal(q.data[0].cpu().numpy(), c.codes)
-        np.testing.assert_array_equal(q.scale[0, :, :, 0].cpu().numpy(), c.scales)
+        assert q.scheme == scheme and q.data.dtype == (torch.int8 if scheme == "int8" else torch.float8_e4m3fn)
+        np.testing.assert_array_equal(q.data[0].view(torch.uint8).cpu().numpy(), c.codes.view(np.uint8))
+        if scheme == "int8":
+            np.testing.assert_array_equal(q.scale[0, :, :, 0].cpu().numpy(), c.scales)
+        else:
+            assert q.scale is None
     cold = cache.cold_length
-    assert cache.num_bytes == cold * (512 + 16 + 128) + (n - cold) * 1152
+    assert cache.num_bytes == cold * (512 + (16 if scheme == "int8" else 0) + 128) + (n - cold) * 1152
     q = inp["q_lat"][:1]
     qr = inp["q_rope"][:1]
     lat_np, rope_np = _bf16_np(lat), _bf16_np(rope)
@@ -199,7 +204,7 @@ def test_int8_cache_codes_bytes_and_decode_loop(cuda):
         out = latent_attention(q[None].to(cuda), qr[None].to(cuda), lat[None, t:t + 1].to(cuda),
                                rope[None, t:t + 1].to(cuda), cache, softmax_scale=SCALE)
         if t in (n, n + steps - 1):
-            view = O.build_cache_from_tokens(lat_np[:t], rope_np[:t], 256, 512, scheme="int8")
+            view = O.build_cache_from_tokens(lat_np[:t], rope_np[:t], 256, 512, scheme=scheme)
             want = O.decode(_bf16_np(q), _bf16_np(qr), lat_np[t:t + 1], rope_np[t:t + 1], view, SCALE)
             got = out[0].cpu().numpy()
             assert O.rel_l2(got, want) <= 1e-3 and O.max_abs(got, want) <= 2e-2, t

@@ -196,6 +196,32 @@ def test_encode_c2_full_size_properties(cuda):
     assert float(err) < 0.2
 
 
+@pytest.mark.parametrize("src", ["bf16", "f32"])
+def test_float8_write_path_matches_reference_fixture(cuda, golden_encode, src):
+    """asterq_quantize with ASTERQ_SCHEME_FLOAT8 writes the bytes of the reference's
+    x.to(torch.float8_e4m3fn) (kv.py:85-89) for bf16 and float32 rows, edge values included
+    (subnormal ties, 448 < |x| <= 464, beyond 464, infinities, NaN, signed zeros), and
+    asterq_dequantize widens them back exactly."""
+    from asterq import _lib
+
+    lib = _lib.load()
+    if src == "bf16":
+        x = _bf16_from_bits(golden_encode["f8_x_bits"], cuda)
+        want = golden_encode["f8_codes_bf16"]
+    else:
+        x = torch.from_numpy(golden_encode["f8_x_f32"]).to(cuda)
+        want = golden_encode["f8_codes_f32"]
+    n, dim = x.shape
+    codes = torch.empty(n, dim, dtype=torch.uint8, device=cuda)
+    _lib.check(lib.asterq_quantize(x.data_ptr(), _lib.dtype_code(x.dtype), n, dim, dim, _lib.SCHEME_FLOAT8, 64,
+                                   codes.data_ptr(), None, _lib.stream_handle(x.device)))
+    np.testing.assert_array_equal(codes.cpu().numpy(), want)
+    back = torch.empty(n, dim, dtype=torch.float32, device=cuda)
+    _lib.check(lib.asterq_dequantize(codes.data_ptr(), None, n, dim, _lib.SCHEME_FLOAT8, 64, back.data_ptr(),
+                                     _lib.DTYPE_F32, dim, _lib.stream_handle(x.device)))
+    np.testing.assert_array_equal(back.cpu().numpy(), O.float8_values(want))
+
+
 @pytest.mark.parametrize("out_dtype", [torch.float32, torch.bfloat16, torch.float16])
 def test_dequantize_bit_exact(cuda, golden_encode, out_dtype):
     from asterq.kv import QuantizedTensor, dequantize_tensor

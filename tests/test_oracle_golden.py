@@ -68,6 +68,13 @@ def test_fwht_is_self_inverse():
     np.testing.assert_allclose(O.normalized_fwht(O.normalized_fwht(x)), x, atol=1e-5)
 
 
+def test_oracle_float8_matches_reference(golden_encode):
+    """float8 (kv.py:85-89) from bf16 and float32 inputs, edge values included."""
+    x16 = O.bf16_to_f32(golden_encode["f8_x_bits"])
+    np.testing.assert_array_equal(O.quantize(x16, "float8").data, golden_encode["f8_codes_bf16"])
+    np.testing.assert_array_equal(O.quantize(golden_encode["f8_x_f32"], "float8").data, golden_encode["f8_codes_f32"])
+
+
 @pytest.mark.parametrize("scheme", ["hadamard_int4", "int4"])
 def test_oracle_rope_quantization_matches_reference(golden_encode, scheme):
     """quantize_rope=True encodes [tokens, 64] RoPE keys as one group of 64 (cache.py:160-164)."""
@@ -78,7 +85,7 @@ def test_oracle_rope_quantization_matches_reference(golden_encode, scheme):
                                   golden_encode[f"rope_{scheme}_scales"].view(np.uint16))
 
 
-@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4", "q8", "q8t3"])
+@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4", "q8", "q8t3", "f8", "f8t3"])
 def test_oracle_decode_matches_reference(golden_decode, case):
     g = {k[len(case) + 1:]: v for k, v in golden_decode.items() if k.startswith(case + "_")}
     ctx, q_len = int(g["ctx"]), int(g["q_len"])
