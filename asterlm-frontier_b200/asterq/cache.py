@@ -144,9 +144,6 @@ class LatentLayerCache:
         if self.cache_dtype not in _KERNEL_SCHEMES:
             raise NotImplementedError(
                 f"cache_dtype {self.cache_dtype!r}: the asterq pools serve 'hadamard_int4', 'int4' and 'bfloat16'")
-        if self.cache_dtype in ("int8", "float8") and self.quantize_rope:
-            raise NotImplementedError(f"quantize_rope=True with {self.cache_dtype} chunks: the decode kernel reads "
-                                      "quantized RoPE keys with the INT4 schemes only")
         if self.cache_dtype in _SCHEME_IDS and self.cache_dtype != "float8" and self.group_size != GROUP_SIZE:
             raise NotImplementedError(f"group_size {self.group_size}: the decode kernels use groups of {GROUP_SIZE}")
         if self.chunk_tokens <= 0 or self.chunk_tokens % 16:
@@ -185,7 +182,8 @@ class LatentLayerCache:
     def num_bytes(self) -> int:
         """Bytes the reference would account (cache.py:79-87): codes + scales + cold RoPE + hot tensors."""
         b, cold = self._batch, self.cold_length
-        rope = (ROPE_DIM // 2 + 2) if self._rope_quantized else ROPE_DIM * 2  # codes + scale, or bf16
+        # RoPE: codes + scale (none for float8), or bf16
+        rope = (self._rope_code_bytes + (self.cache_dtype != "float8") * 2) if self._rope_quantized else ROPE_DIM * 2
         total = b * cold * (self._code_bytes + self._n_scales * 2 + rope)
         total += b * self._hot_len * (LATENT_DIM + ROPE_DIM) * self._dtype.itemsize
         return int(total)
@@ -204,7 +202,10 @@ class LatentLayerCache:
             code_dtype = _CODE_DTYPES.get(self.cache_dtype, torch.uint8)
             cold = {"codes": ((self._code_bytes,), code_dtype), "scales": ((self._n_scales,), torch.float16)}
             if self._rope_quantized:
-                cold.update(rope=((ROPE_DIM // 2,), torch.uint8), rope_scales=((), torch.float16))
+                # RoPE codes of the cold scheme (float8: raw e4m3 bytes) and, but for float8, their scales
+                cold.update(rope=((self._rope_code_bytes,), _CODE_DTYPES.get(self.cache_dtype, torch.uint8)))
+                if self.cache_dtype != "float8":
+                    cold.update(rope_scales=((), torch.float16))
             else:
                 cold.update(rope=((ROPE_DIM,), torch.bfloat16))
             self._cold = _Pool(cold, self.page_tokens, device)
@@ -219,6 +220,10 @@ class LatentLayerCache:
     def _code_bytes(self) -> int:
         """Code bytes of a cold token: one a dim for int8, two dims a byte for the INT4 schemes."""
         return LATENT_DIM if self.cache_dtype in _CODE_DTYPES else LATENT_DIM // 2
+
+    @property
+    def _rope_code_bytes(self) -> int:
+        return ROPE_DIM if self.cache_dtype in _CODE_DTYPES else ROPE_DIM // 2
 
     @property
     def _n_scales(self) -> int:
@@ -242,7 +247,8 @@ class LatentLayerCache:
         return LatentPools(cold_codes=self._cold["codes"], cold_scales=self._cold["scales"],
                            cold_rope=self._cold["rope"], hot_latent=self._hot["latent"], hot_rope=self._hot["rope"],
                            cold_scheme=self.cache_dtype if self.cache_dtype in _SCHEME_IDS else "hadamard_int4",
-                           cold_rope_scales=self._cold["rope_scales"] if self._rope_quantized else None)
+                           cold_rope_scales=(self._cold["rope_scales"] if self._rope_quantized and
+                                             self.cache_dtype != "float8" else None))
 
     def decode_layouts(self, q_len: int) -> list[SequenceLayout]:
         """One SequenceLayout per batch row; row b's new tokens are rows b*q_len.. of the step's arrays."""
@@ -424,13 +430,14 @@ class LatentLayerCache:
         if self._rope_quantized:
             # quantize_rope (cache.py:163): the RoPE keys as stored, cold scheme, one group of 64
             r = self._hot[self._src + "rope"].index_select(0, src).reshape(bsz * P, ROPE_DIM)
-            rcodes = torch.empty(bsz * P, ROPE_DIM // 2, dtype=torch.uint8, device=dev)
+            rcodes = torch.empty(bsz * P, self._rope_code_bytes, dtype=self._cold["rope"].dtype, device=dev)
             rscales = torch.empty(bsz * P, 1, dtype=torch.float16, device=dev)
             _lib.check(lib.asterq_quantize(r.data_ptr(), _lib.dtype_code(r.dtype), bsz * P, ROPE_DIM, ROPE_DIM,
                                            _SCHEME_IDS[self.cache_dtype], GROUP_SIZE, rcodes.data_ptr(),
                                            rscales.data_ptr(), _lib.stream_handle(dev)))
             self._cold["rope"].index_copy_(0, dst, rcodes.view(bsz, P, -1))
-            self._cold["rope_scales"].index_copy_(0, dst, rscales.view(bsz, P))
+            if self.cache_dtype != "float8":
+                self._cold["rope_scales"].index_copy_(0, dst, rscales.view(bsz, P))
         else:
             # cold RoPE keys are bf16 whatever the caller's dtype (cache.py:162-164)
             self._cold["rope"].index_copy_(0, dst, self._hot["rope"].index_select(0, src))
@@ -504,7 +511,8 @@ class LatentLayerCache:
     @property
     def cold_rope(self) -> list[torch.Tensor] | list[QuantizedTensor]:
         """Cold RoPE pieces: bf16 [B, chunk, 64], or with quantize_rope one QuantizedTensor per
-        chunk (data [B, chunk, 32], scale [B, chunk, 1, 1]), as the reference stores them."""
+        chunk (data [B, chunk, 32] INT4 / [B, chunk, 64] int8 or float8, scale [B, chunk, 1, 1] or
+        None for float8), as the reference stores them."""
         if not self._rope_quantized:
             return [torch.stack([self._cold["rope"][self._cold_pages[b][c]] for b in range(self._batch)])
                     for c in range(self.cold_chunks)]
@@ -512,7 +520,10 @@ class LatentLayerCache:
         for c in range(self.cold_chunks):
             pages = [self._cold_pages[b][c] for b in range(self._batch)]
             data = torch.stack([self._cold["rope"][pg] for pg in pages])
-            scale = torch.stack([self._cold["rope_scales"][pg] for pg in pages]).reshape(self._batch, -1, 1, 1)
+            if self.cache_dtype == "float8":
+                data, scale = data.view(torch.float8_e4m3fn), None
+            else:
+                scale = torch.stack([self._cold["rope_scales"][pg] for pg in pages]).reshape(self._batch, -1, 1, 1)
             out.append(QuantizedTensor(data=data, scale=scale, original_shape=(self._batch, self.chunk_tokens, ROPE_DIM),
                                        padded_dim=ROPE_DIM, group_size=GROUP_SIZE, scheme=self.cache_dtype,
                                        source_dtype=self._dtype))

@@ -47,7 +47,7 @@ class LatentPools:
 
     @property
     def rope_quantized(self) -> bool:
-        return self.cold_rope.dtype == torch.uint8
+        return self.cold_rope.element_size() == 1
 
     @staticmethod
     def empty(n_cold_pages: int, n_hot_pages: int, page_tokens: int, device, *,
@@ -63,8 +63,13 @@ class LatentPools:
         else:
             codes = torch.empty(n_cold_pages, page_tokens, LATENT_DIM // 2, dtype=torch.uint8, device=device)
         if quantize_rope:
-            cold_rope = torch.empty(n_cold_pages, page_tokens, ROPE_DIM // 2, dtype=torch.uint8, device=device)
-            rope_scales = torch.empty(n_cold_pages, page_tokens, dtype=torch.float16, device=device)
+            # RoPE codes of the cold scheme: 32 bytes a token (INT4) or 64 (int8, float8); one fp16
+            # scale a token but for float8
+            width = ROPE_DIM if cold_scheme in BYTE_SCHEMES else ROPE_DIM // 2
+            rdt = torch.int8 if cold_scheme == "int8" else torch.uint8
+            cold_rope = torch.empty(n_cold_pages, page_tokens, width, dtype=rdt, device=device)
+            rope_scales = (None if cold_scheme == "float8"
+                           else torch.empty(n_cold_pages, page_tokens, dtype=torch.float16, device=device))
         else:
             cold_rope = torch.empty(n_cold_pages, page_tokens, ROPE_DIM, dtype=torch.bfloat16, device=device)
             rope_scales = None
@@ -94,12 +99,16 @@ def set_cold_pools(p: _lib.DecodeParams, pools: LatentPools) -> None:
     p.cold_scales = pools.cold_scales.data_ptr() if pools.cold_scales.numel() else None
     p.cold_rope = pools.cold_rope.data_ptr() if pools.cold_rope.numel() else None
     if pools.rope_quantized:
-        if pools.cold_rope_scales is None:
-            raise ValueError("quantized cold RoPE keys (uint8 cold_rope) need cold_rope_scales")
-        if pools.cold_rope.shape[-1] != ROPE_DIM // 2 or pools.cold_rope_scales.dtype != torch.float16:
-            raise ValueError("quantized cold RoPE keys: cold_rope [Pc, page, 32] uint8, cold_rope_scales fp16 [Pc, page]")
+        width = ROPE_DIM if pools.cold_scheme in BYTE_SCHEMES else ROPE_DIM // 2
+        if pools.cold_rope.shape[-1] != width:
+            raise ValueError(f"quantized cold RoPE keys of scheme {pools.cold_scheme!r}: cold_rope [Pc, page, {width}]")
+        if pools.cold_scheme == "float8":
+            p.cold_rope_scales = None
+        else:
+            if pools.cold_rope_scales is None or pools.cold_rope_scales.dtype != torch.float16:
+                raise ValueError("quantized cold RoPE keys need cold_rope_scales fp16 [Pc, page]")
+            p.cold_rope_scales = pools.cold_rope_scales.data_ptr() if pools.cold_rope_scales.numel() else None
         p.rope_scheme = _lib.ROPE_QUANTIZED
-        p.cold_rope_scales = pools.cold_rope_scales.data_ptr() if pools.cold_rope_scales.numel() else None
     else:
         p.rope_scheme = _lib.ROPE_BF16
         p.cold_rope_scales = None

@@ -153,8 +153,9 @@ class PoolBuilder:
                 self._lib.check(
                     self.lib.asterq_quantize(
                         rope.data_ptr(), self._lib.DTYPE_BF16, cold, ROPE_DIM, ROPE_DIM, self._scheme_id, GROUP_SIZE,
-                        pools.cold_rope.view(-1, ROPE_DIM // 2)[r0].data_ptr(),
-                        pools.cold_rope_scales.view(-1)[r0:].data_ptr(), self._lib.stream_handle(self.device),
+                        pools.cold_rope.view(-1, pools.cold_rope.shape[-1])[r0].data_ptr(),
+                        None if pools.cold_rope_scales is None else pools.cold_rope_scales.view(-1)[r0:].data_ptr(),
+                        self._lib.stream_handle(self.device),
                     )
                 )
             else:

@@ -373,9 +373,18 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) rmx = fmaxf(rmx, __shfl_xor_sync(0xffffffffu, rmx, off));
       if (lane == 0) {
-        const float qr_s = (rmx > 0.0f) ? 32511.0f / rmx : 1.0f;
-        rscr[16 * kRope + r] = qr_s;
-        sc[kMRopeR - kMQscale + r] = sc[kMQint - kMQscale + r] / qr_s;
+        if (p.cold_scheme == ASTERQ_SCHEME_FLOAT8) {
+          // float8: the RoPE query in fp16 times its own power of two (largest value below 2^14)
+          int ex = 0;
+          if (rmx > 0.0f) frexpf(rmx, &ex);
+          const float s2r = ldexpf(1.0f, rmx > 0.0f ? min(max(14 - ex, -100), 100) : 0);
+          rscr[16 * kRope + r] = s2r;
+          sc[kMRopeR - kMQscale + r] = sc[r] / s2r;
+        } else {
+          const float qr_s = (rmx > 0.0f) ? 32511.0f / rmx : 1.0f;
+          rscr[16 * kRope + r] = qr_s;
+          sc[kMRopeR - kMQscale + r] = sc[kMQint - kMQscale + r] / qr_s;
+        }
       }
     }
   }
@@ -444,9 +453,21 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
   }
   float* scalars = reinterpret_cast<float*>(dst + 34816);
   for (int e = tid; e < kQScalars; e += kPrepThreads) scalars[e] = sc[e];
-  if (rope_q) {
+  if (rope_q && p.cold_scheme == ASTERQ_SCHEME_FLOAT8) {
+    // float8 RoPE codes: fp16 fragments [k-step ks][nt][lane] uint2, lane (gid, tq) holding row
+    // 8nt + gid at RoPE dims 16tq + 4ks + {0, 1} (b0) and + {2, 3} (b1), times its power of two
+    uint2* qfr = reinterpret_cast<uint2*>(dst + kQPrepRopeInt);
+    for (int e = tid; e < 4 * 2 * 32; e += kPrepThreads) {
+      const int ln = e & 31, nt = (e >> 5) & 1, ks = e >> 6;
+      const int row = 8 * nt + (ln >> 2), d0 = 16 * (ln & 3) + 4 * ks;
+      const float s2r = rscr[16 * kRope + row];
+      const float* x = rscr + row * kRope + d0;
+      qfr[e] = make_uint2(pack_half2(x[0] * s2r, x[1] * s2r), pack_half2(x[2] * s2r, x[3] * s2r));
+    }
+  } else if (rope_q) {
     // quantized RoPE limb fragments: k-step j, lane (gid, tq) holds query row 8nt + gid at the
-    // dims of code word W = 2tq + j of the 32-byte RoPE code row (same expansion as the latent)
+    // dims of code word W = 2tq + j of the 32-byte INT4 RoPE code row (same expansion as the
+    // latent), or for int8 RoPE codes at dims 16tq + 8j + i and + 4 + i
     uint4* qri = reinterpret_cast<uint4*>(dst + kQPrepRopeInt);
     for (int e = tid; e < 2 * 2 * 32; e += kPrepThreads) {
       const int ln = e & 31, nt = (e >> 5) & 1, j = e >> 6;
@@ -457,7 +478,8 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
       for (int half = 0; half < 2; ++half)
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          const int qv = min(max(__float2int_rn(rscr[row * kRope + 8 * W + 2 * i + half] * qs), -32511), 32511);
+          const int rd = b8 ? 16 * (ln & 3) + 8 * j + 4 * half + i : 8 * W + 2 * i + half;
+          const int qv = min(max(__float2int_rn(rscr[row * kRope + rd] * qs), -32511), 32511);
           const int q1 = (qv + 128) >> 8;
           const int q2 = qv - 256 * q1;
           hb[half] |= (uint32_t)(q1 & 0xff) << (8 * i);
@@ -476,13 +498,15 @@ __global__ void __launch_bounds__(kPrepThreads) qprep_kernel(const __grid_consta
 //    bytes as a 128-token INT4 tile, so every warp's share of a stage is unchanged).
 //  kModeF8: float8 e4m3 codes (kv.py scheme "float8": one byte a dim, no scales), bf16 RoPE keys,
 //    64-token cold tiles like int8.
-constexpr int kModeInt4 = 0, kModeInt4RopeQ = 1, kModeInt8 = 2, kModeF8 = 3;
+//  kModeInt8RopeQ / kModeF8RopeQ: the same with quantized RoPE keys (64 bytes a token: int8 codes
+//    with one fp16 scale, or e4m3 bytes).
+constexpr int kModeInt4 = 0, kModeInt4RopeQ = 1, kModeInt8 = 2, kModeF8 = 3, kModeInt8RopeQ = 4, kModeF8RopeQ = 5;
 template <int kMode>
 __global__ void __launch_bounds__(kThreads, 1)
     decode_kernel(const __grid_constant__ asterq_decode_params p, const __grid_constant__ TensorMaps maps) {
-  constexpr bool kRopeQ = kMode == kModeInt4RopeQ;
-  constexpr bool kB8 = kMode == kModeInt8;
-  constexpr bool kF8 = kMode == kModeF8;
+  constexpr bool kRopeQ = kMode == kModeInt4RopeQ || kMode == kModeInt8RopeQ || kMode == kModeF8RopeQ;
+  constexpr bool kB8 = kMode == kModeInt8 || kMode == kModeInt8RopeQ;
+  constexpr bool kF8 = kMode == kModeF8 || kMode == kModeF8RopeQ;
   constexpr bool kBytes = kB8 || kF8;                   // one code byte a dim, 64-token cold tiles
   constexpr int kCT = kBytes ? kColdTile8 : kColdTile;  // tokens of a cold tile
   constexpr int kCM = kCT / 64;                      // 16-token m-tiles of a cold tile per score warp
@@ -566,14 +590,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (t.kind == ASTERQ_TILE_COLD) {
       const int y = t.page * p.page_tokens + t.off;
       if constexpr (kRopeQ) {
-        // RoPE codes (32 B a token) and scales (2 B a token, copied from the 8-token boundary
-        // at or below y to the one at or above y + n: both within the page, whose first token
-        // index is a multiple of 16)
+        // RoPE codes (32 B a token for INT4, 64 B for int8 / float8) and, but for float8, their
+        // scales (2 B a token, copied from the 8-token boundary at or below y to the one at or
+        // above y + n: both within the page, whose first token index is a multiple of 16)
+        constexpr int kRB = kBytes ? 64 : 32;
         const int y8 = y & ~7, n8 = ((y + t.n + 7) & ~7) - y8;
-        mbar_expect_tx(full, 2 * 16384 + 16 * t.n + 32 * t.n + 2 * n8);
+        mbar_expect_tx(full, (kBytes ? 4 * kCodeBlock8 : 2 * 16384) + (kF8 ? 0 : 16 * t.n + 2 * n8) + kRB * t.n);
         tma_3d(st + kCodesLo, &maps.codes, y, full);
-        bulk_1d(st + kCRope, reinterpret_cast<const uint8_t*>(p.cold_rope) + (int64_t)y * 32, 32 * t.n, full);
-        bulk_1d(st + kCRopeScale, reinterpret_cast<const uint8_t*>(p.cold_rope_scales) + (int64_t)y8 * 2, 2 * n8, full);
+        bulk_1d(st + kCRope, reinterpret_cast<const uint8_t*>(p.cold_rope) + (int64_t)y * kRB, kRB * t.n, full);
+        if constexpr (!kF8)
+          bulk_1d(st + kCRopeScale, reinterpret_cast<const uint8_t*>(p.cold_rope_scales) + (int64_t)y8 * 2, 2 * n8, full);
       } else if constexpr (kBytes) {
         mbar_expect_tx(full, 4 * kCodeBlock8 + kColdTile8 * 128 + (kF8 ? 0 : 16 * t.n));
         tma_3d(st + kCodesLo, &maps.codes, y, full);  // four blocks of [64 rows][128 B]
@@ -851,6 +877,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             // group g (dims 64g + 16tq .. + 15) of its two tokens; k-step ks takes dims
             // 16tq + 4ks + {0, 1} (a0 / b0) and + {2, 3} (a2 / b1)
             const uint2* qf = reinterpret_cast<const uint2*>(smem + kOffQi);
+            if constexpr (kRopeQ) {
+              // quantized RoPE keys (e4m3 bytes, 64 a token) first, against the RoPE query in fp16
+              // with its own power-of-two scale, then brought to the latent query's scale
+              const uint2* qfr = reinterpret_cast<const uint2*>(smem + kOffQri);
+              const uint4 r0 = *reinterpret_cast<const uint4*>(st + kCRope + 64 * tok[0][0] + 16 * tq);
+              const uint4 r1 = *reinterpret_cast<const uint4*>(st + kCRope + 64 * tok[0][1] + 16 * tq);
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                const uint32_t w0 = ks == 0 ? r0.x : ks == 1 ? r0.y : ks == 2 ? r0.z : r0.w;
+                const uint32_t w1 = ks == 0 ? r1.x : ks == 1 ? r1.y : ks == 2 ? r1.z : r1.w;
+                const uint32_t a[4] = {e4m3x2_to_f16x2(w0), e4m3x2_to_f16x2(w1), e4m3x2_to_f16x2(w0 >> 16),
+                                       e4m3x2_to_f16x2(w1 >> 16)};
+#pragma unroll
+                for (int nt = 0; nt < 2; ++nt) {
+                  const uint2 bq = qfr[(ks * 2 + nt) * 32 + lane];
+                  mma_f16(S[0][nt], a, bq.x, bq.y);
+                }
+              }
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                for (int c = 0; c < 4; ++c) S[0][nt][c] *= rratio[nt][c & 1];
+            }
 #pragma unroll 2
             for (int g = 0; g < 8; ++g) {
               uint4 v[2];
@@ -881,8 +930,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // order the query limbs were laid out in
                 uint4 v[2];
   #pragma unroll
-                for (int h = 0; h < 2; ++h)
-                  v[h] = *reinterpret_cast<const uint4*>(st + (g >> 1) * kCodeBlock8 + swz(tok[0][h], 4 * (g & 1) + tq));
+                for (int h = 0; h < 2; ++h)  // group 8: the token's 64-byte RoPE code row (quantized RoPE keys)
+                  v[h] = *reinterpret_cast<const uint4*>(st + ((kRopeQ && g == 8) ? kCRope + 64 * tok[0][h] + 16 * tq
+                                                                                  : (g >> 1) * kCodeBlock8 + swz(tok[0][h], 4 * (g & 1) + tq)));
   #pragma unroll
                 for (int j = 0; j < 2; ++j) {
                   const uint4 bq[2] = {qi[((2 * g + j) * 2) * 32 + lane], qi[((2 * g + j) * 2 + 1) * 32 + lane]};
@@ -978,7 +1028,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               const __half* rsc = reinterpret_cast<const __half*>(st + kCRopeScale) + (t.off & 7);
               const float2 bias2 = make_float2(-kAccBiasF, -kAccBiasF), k256 = make_float2(256.0f, 256.0f);
   #pragma unroll
-              for (int m = 0; m < 2; ++m)
+              for (int m = 0; m < kCM; ++m)
   #pragma unroll
                 for (int h = 0; h < 2; ++h) {
                   const float rs = __half2float(rsc[tok[m][h]]);
@@ -1791,11 +1841,10 @@ int validate(const asterq_decode_params* p) {
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null pointer");
   if (p->rope_scheme != ASTERQ_ROPE_BF16 && p->rope_scheme != ASTERQ_ROPE_QUANTIZED)
     return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: rope scheme %d unsupported (bf16 or quantized)", p->rope_scheme);
-  if (p->rope_scheme == ASTERQ_ROPE_QUANTIZED && p->cold_scheme >= ASTERQ_SCHEME_INT8)
-    return set_error(ASTERQ_ERR_UNSUPPORTED, "decode: quantized RoPE keys are read with the INT4 schemes only");
   if (p->n_cold_pages > 0 && (!p->cold_codes || (!p->cold_scales && p->cold_scheme != ASTERQ_SCHEME_FLOAT8) || !p->cold_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null cold pool");
-  if (p->n_cold_pages > 0 && p->rope_scheme == ASTERQ_ROPE_QUANTIZED && !p->cold_rope_scales)
+  if (p->n_cold_pages > 0 && p->rope_scheme == ASTERQ_ROPE_QUANTIZED && p->cold_scheme != ASTERQ_SCHEME_FLOAT8 &&
+      !p->cold_rope_scales)
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: quantized RoPE keys need cold_rope_scales");
   if (p->n_hot_pages > 0 && (!p->hot_latent || !p->hot_rope))
     return set_error(ASTERQ_ERR_INVALID_ARGUMENT, "decode: null hot pool");
@@ -1905,7 +1954,9 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
       const void* kernels[] = {reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt4>),
                                reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt4RopeQ>),
                                reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt8>),
-                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeF8>)};
+                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeF8>),
+                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeInt8RopeQ>),
+                               reinterpret_cast<const void*>(dec::decode_kernel<dec::kModeF8RopeQ>)};
       cudaError_t e = cudaSuccess;
       for (const void* fn : kernels)
         if (e == cudaSuccess) e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, dec::kSmemBytes);
@@ -1960,11 +2011,17 @@ extern "C" int asterq_latent_decode(const asterq_decode_params* p, void* stream)
       attr[0].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      cudaError_t e = (kp.cold_scheme == ASTERQ_SCHEME_FLOAT8) ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeF8>, kp, maps)
-                      : (kp.cold_scheme == ASTERQ_SCHEME_INT8) ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt8>, kp, maps)
-                      : (kp.rope_scheme == ASTERQ_ROPE_QUANTIZED)
-                          ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4RopeQ>, kp, maps)
-                          : cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4>, kp, maps);
+      const bool rq = kp.rope_scheme == ASTERQ_ROPE_QUANTIZED;
+      cudaError_t e;
+      if (kp.cold_scheme == ASTERQ_SCHEME_FLOAT8)
+        e = rq ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeF8RopeQ>, kp, maps)
+               : cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeF8>, kp, maps);
+      else if (kp.cold_scheme == ASTERQ_SCHEME_INT8)
+        e = rq ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt8RopeQ>, kp, maps)
+               : cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt8>, kp, maps);
+      else
+        e = rq ? cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4RopeQ>, kp, maps)
+               : cudaLaunchKernelEx(&cfg, dec::decode_kernel<dec::kModeInt4>, kp, maps);
       if (e != cudaSuccess) return set_error(ASTERQ_ERR_CUDA, "latent_decode: launch failed: %s", cudaGetErrorString(e));
     }
     st = check_launch("latent_decode");

@@ -56,9 +56,10 @@ extern "C" {
 
 /* cold RoPE keys (cache.py:160-164: quantized only with quantize_rope=True) */
 #define ASTERQ_ROPE_BF16 0      /* cold_rope: bf16 [tokens][rope_dim] */
-#define ASTERQ_ROPE_QUANTIZED 1 /* cold_rope: [tokens][rope_dim/2] u8 codes of the cold scheme, one scale
-                                   group of rope_dim (Hadamard-rotated for hadamard_int4);
-                                   cold_rope_scales: fp16 [tokens] */
+#define ASTERQ_ROPE_QUANTIZED 1 /* cold_rope: codes of the cold scheme, one scale group of rope_dim:
+                                   [tokens][rope_dim/2] INT4 (Hadamard-rotated for hadamard_int4) or
+                                   [tokens][rope_dim] int8 / float8 bytes; cold_rope_scales: fp16
+                                   [tokens] (none for float8) */
 
 /* tile kinds in the decode schedule */
 #define ASTERQ_TILE_COLD 0 /* tokens of a cold page: INT4 (or int8) codes + fp16 scales + RoPE key */
@@ -115,7 +116,8 @@ int asterq_codec_status(int32_t* timeouts);
  *   cold_codes  uint8 [n_cold_pages, page_tokens, latent_dim/2]   rotated INT4 codes (kv.py:41-48 packing)
  *   cold_scales fp16  [n_cold_pages, page_tokens, latent_dim/64]
  *   cold_rope   bf16  [n_cold_pages, page_tokens, rope_dim]        (rope_scheme ASTERQ_ROPE_BF16), or
- *               uint8 [n_cold_pages, page_tokens, rope_dim/2]      (ASTERQ_ROPE_QUANTIZED: INT4 codes)
+ *               uint8 [n_cold_pages, page_tokens, rope_dim/2]      (ASTERQ_ROPE_QUANTIZED: INT4 codes; int8 and
+ *                                                                   float8: [.., rope_dim] bytes)
  *   cold_rope_scales fp16 [n_cold_pages, page_tokens]              (ASTERQ_ROPE_QUANTIZED only)
  *   hot_latent  bf16  [n_hot_pages, page_tokens, latent_dim]
  *   hot_rope    bf16  [n_hot_pages, page_tokens, rope_dim]
@@ -140,7 +142,8 @@ int asterq_codec_status(int32_t* timeouts);
  *   combine [n_combine][4] int32 = {slot_begin, slot_end, out_row0, n_rows}: merges partials into `out`.
  * Cold schemes: hadamard_int4 and int4 (params.cold_scheme), and int8 (codes uint8/int8
  *   [n_cold_pages, page_tokens, latent_dim]: one signed byte a dim, kv.py scheme "int8",
- *   scales as above, not rotated; bf16 RoPE keys only).
+ *   scales as above, not rotated), and float8 (e4m3 bytes [.., latent_dim], no scales: cold_scales
+ *   may be NULL).
  * Geometry supported: latent_dim 512, rope_dim 64, scale groups of 64, page_tokens
  * a multiple of 128, q_len <= 2048.  cold tiles hold <= 128 tokens (int8: <= 64), hot/new tiles <= 32.
  */
@@ -202,7 +205,8 @@ typedef struct asterq_decode_params {
                                  (LatentLayerCache quantize_rope=True, cache.py:160-164 -> kv.py:76-118);
                                  the kernel scores them on the int8 tensor path like a ninth latent
                                  group.  Hot and new tokens keep bf16 RoPE keys. */
-  const void* cold_rope_scales; /* fp16 [n_cold_pages * page_tokens], 16-byte aligned (quantized RoPE) */
+  const void* cold_rope_scales; /* fp16 [n_cold_pages * page_tokens], 16-byte aligned (quantized RoPE keys
+                                   of the INT4 schemes and int8; NULL for float8) */
 } asterq_decode_params;
 
 /*

@@ -223,7 +223,8 @@ class ColdChunk:
     """One cold chunk: packed codes [n, D/2] u8, scales [n, D/G] f16, RoPE [n, R] f32.
 
     With ``quantize_rope`` (cache.py:160-164) the RoPE keys are stored like the latent
-    (``rope_codes`` [n, R/2] u8, ``rope_scales`` [n] f16, one group of R = 64) and ``rope``
+    (``rope_codes`` [n, R/2] u8 for INT4, [n, R] for int8 / float8; ``rope_scales`` [n] f16, one
+    group of R = 64, none for float8) and ``rope``
     holds their dequantized values (kv.py:121-134), which is what ``iter_chunks`` yields.
     """
 
@@ -437,7 +438,7 @@ def cold_chunk(latent: np.ndarray, rope: np.ndarray, group_size: int = 64, schem
     if quantize_rope:
         qr = quantize(rope, scheme, group_size)
         chunk.rope_codes = qr.data
-        chunk.rope_scales = qr.scale.reshape(rope.shape[0])
+        chunk.rope_scales = None if qr.scale is None else qr.scale.reshape(rope.shape[0])
         chunk.rope = dequantize(qr)
     return chunk
 

@@ -100,7 +100,8 @@ def decode_case(seed, ctx, q_len, recent, chunk, scheme="hadamard_int4", quantiz
         "codes_sha256": sha(*[c.data for c in cache.cold_latent]),
         "scales_sha256": sha(*[c.scale for c in cache.cold_latent if c.scale is not None]),
         **({"rope_codes_sha256": sha(*[c.data for c in cache.cold_rope]),
-            "rope_scales_sha256": sha(*[c.scale for c in cache.cold_rope])} if quantize_rope else {}),
+            "rope_scales_sha256": sha(*[c.scale for c in cache.cold_rope if c.scale is not None])}
+           if quantize_rope else {}),
     }
 
 
@@ -185,6 +186,9 @@ def main() -> None:
         # float8 cold chunks (kv.py:85-89: e4m3 values, no scales)
         "f8": dict(seed=13, ctx=2300, q_len=1, recent=512, chunk=512, scheme="float8"),
         "f8t3": dict(seed=14, ctx=1800, q_len=3, recent=512, chunk=512, scheme="float8"),
+        # quantize_rope=True with the one-byte schemes (RoPE keys as int8 codes / e4m3 bytes)
+        "q8r": dict(seed=15, ctx=2100, q_len=1, recent=512, chunk=512, scheme="int8", quantize_rope=True),
+        "f8r": dict(seed=16, ctx=2500, q_len=1, recent=512, chunk=512, scheme="float8", quantize_rope=True),
     }
     dec: dict[str, np.ndarray] = {}
     for name, kw in cases.items():

@@ -11,10 +11,6 @@ def test_unsupported_configurations_raise():
     with pytest.raises(NotImplementedError):
         LatentLayerCache("int2")
     with pytest.raises(NotImplementedError):
-        LatentLayerCache("int8", quantize_rope=True)
-    with pytest.raises(NotImplementedError):
-        LatentLayerCache("float8", quantize_rope=True)
-    with pytest.raises(NotImplementedError):
         LatentLayerCache("hadamard_int4", group_size=32)
     with pytest.raises(ValueError):
         LatentLayerCache("hadamard_int4", chunk_tokens=100)
@@ -25,7 +21,7 @@ def test_quantize_rope_is_accepted_for_every_kernel_scheme():
     never flushes, so its RoPE keys stay bf16 as in the reference."""
     from asterq.cache import LatentLayerCache
 
-    for scheme in ("hadamard_int4", "int4", "bfloat16"):
+    for scheme in ("hadamard_int4", "int4", "int8", "float8", "bfloat16"):
         c = LatentLayerCache(scheme, quantize_rope=True, chunk_tokens=512)
         assert c.quantize_rope and c._rope_quantized == (scheme != "bfloat16")
         assert c.num_bytes == 0

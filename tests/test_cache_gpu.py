@@ -129,13 +129,15 @@ def test_latent_attention_over_the_cache(cuda, q_len, scheme):
 
 
 @pytest.mark.parametrize("scheme,dtype", [("hadamard_int4", torch.bfloat16), ("int4", torch.bfloat16),
-                                          ("hadamard_int4", torch.float32)])
+                                          ("hadamard_int4", torch.float32), ("int8", torch.bfloat16),
+                                          ("float8", torch.bfloat16), ("int8", torch.float32)])
 def test_quantize_rope_cache_matches_reference(cuda, scheme, dtype):
     """quantize_rope=True (cache.py:64, :160-164): each flushed chunk's RoPE keys are quantized from
     the values as stored (the caller's dtype) with the cold scheme, one group of 64 -- codes and
     scales bit-exact to quantize_tensor, the reference's byte accounting (32 code bytes and one fp16
-    scale a token), dequantized views bit-exact -- and attention reads the codes directly (q_len 1
-    and 3, within the decode tolerance)."""
+    scale a token for INT4, 64 bytes and a scale for int8, 64 e4m3 bytes for float8), dequantized
+    views bit-exact -- and attention reads the codes directly (q_len 1 and 3, within the decode
+    tolerance)."""
     from asterq.attention import latent_attention
     from asterq.cache import LatentLayerCache
     from asterq.kv import QuantizedTensor
@@ -150,12 +152,17 @@ def test_quantize_rope_cache_matches_reference(cuda, scheme, dtype):
     ref = O.build_cache_from_tokens(lat_np[:n], rope_np[:n], 512, 512, scheme=scheme, quantize_rope=True)
     assert cache.cold_chunks == len(ref.cold) > 0 and cache.length == n
     for q, r, c in zip(cache.cold_latent, cache.cold_rope, ref.cold):
-        np.testing.assert_array_equal(q.data[0].cpu().numpy(), c.codes)
+        np.testing.assert_array_equal(q.data[0].view(torch.uint8).cpu().numpy(), c.codes.view(np.uint8))
         assert isinstance(r, QuantizedTensor) and r.scheme == scheme and r.original_shape == (1, 512, 64)
-        np.testing.assert_array_equal(r.data[0].cpu().numpy(), c.rope_codes)
-        np.testing.assert_array_equal(r.scale[0, :, 0, 0].cpu().numpy(), c.rope_scales)
+        np.testing.assert_array_equal(r.data[0].view(torch.uint8).cpu().numpy(), c.rope_codes.view(np.uint8))
+        if scheme == "float8":
+            assert r.scale is None and c.rope_scales is None
+        else:
+            np.testing.assert_array_equal(r.scale[0, :, 0, 0].cpu().numpy(), c.rope_scales)
     cold = cache.cold_length
-    assert cache.num_bytes == cold * (256 + 16 + 32 + 2) + (n - cold) * (512 + 64) * dtype.itemsize
+    per_cold = {"hadamard_int4": 256 + 16 + 32 + 2, "int4": 256 + 16 + 32 + 2, "int8": 512 + 16 + 64 + 2,
+                "float8": 512 + 64}[scheme]
+    assert cache.num_bytes == cold * per_cold + (n - cold) * (512 + 64) * dtype.itemsize
     got_rope = cache.materialize_rope(dtype=torch.float32)[0].cpu().numpy()
     np.testing.assert_array_equal(got_rope, ref.materialize()[1])
 

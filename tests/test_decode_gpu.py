@@ -76,7 +76,7 @@ def oracle_for(inp, ctx, hot, q_len, softcap=None, chunk=512, scheme="hadamard_i
                     SCALE, softcap)
 
 
-@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4", "q8", "q8t3", "f8", "f8t3"])
+@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4", "q8", "q8t3", "f8", "f8t3", "q8r", "f8r"])
 def test_decode_matches_reference_golden(cuda, golden_decode, case):
     """The reference's own outputs; "qrope" / "qr4": quantize_rope=True caches (cold RoPE keys as
     hadamard_int4 / int4 codes, cache.py:160-164)."""
@@ -191,21 +191,22 @@ def test_quantized_rope_ragged_batch(cuda, scheme, q_len):
     assert O.rel_l2(split.cpu().numpy(), out) < 1e-4
 
 
-@pytest.mark.parametrize("scheme,q_len", [("int8", 1), ("int8", 3), ("float8", 1), ("float8", 3)])
-def test_byte_cold_schemes_ragged_batch(cuda, scheme, q_len):
+@pytest.mark.parametrize("scheme,q_len,qrope", [("int8", 1, False), ("int8", 3, False), ("float8", 1, False),
+                                                ("float8", 3, False), ("int8", 1, True), ("float8", 2, True)])
+def test_byte_cold_schemes_ragged_batch(cuda, scheme, q_len, qrope):
     """int8 cold chunks (kv.py scheme "int8": one signed byte a dim, fp16 scale per group of 64, no
     rotation) and float8 chunks (e4m3 bytes, no scales) in 64-token tiles: ragged lengths with
     partial pages and tiles of 1..64 tokens, hot windows, a cold-only sequence; one item per
-    block and a split schedule agree."""
+    block and a split schedule agree.  ``qrope``: the RoPE keys quantized too (quantize_rope=True)."""
     from asterq.synth import PoolBuilder, c1_inputs
 
     lengths, hot = [1300, 700, 2600, 65, 1031], [300, 0, 1000, 1, 7]
-    b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=16, device=cuda, scheme=scheme)
+    b = PoolBuilder(lengths, hot, q_len=q_len, n_heads=16, device=cuda, scheme=scheme, quantize_rope=qrope)
     refs = []
     for i, (n, h) in enumerate(zip(lengths, hot)):
         inp = c1_inputs(seed=80 + i, ctx=n, q_len=q_len)
         b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
-        refs.append(oracle_for(inp, n, h, q_len, scheme=scheme))
+        refs.append(oracle_for(inp, n, h, q_len, scheme=scheme, quantize_rope=qrope))
     wl = b.finish(scheme)
     out, plan = run_decode(wl)
     assert plan.cold_tile == 64 and int(plan.tiles[plan.tiles[:, 0] == 0][:, 3].max()) == 64

@@ -85,7 +85,7 @@ def test_oracle_rope_quantization_matches_reference(golden_encode, scheme):
                                   golden_encode[f"rope_{scheme}_scales"].view(np.uint16))
 
 
-@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4", "q8", "q8t3", "f8", "f8t3"])
+@pytest.mark.parametrize("case", ["c1", "small", "hotonly", "t3", "qrope", "qr4", "q8", "q8t3", "f8", "f8t3", "q8r", "f8r"])
 def test_oracle_decode_matches_reference(golden_decode, case):
     g = {k[len(case) + 1:]: v for k, v in golden_decode.items() if k.startswith(case + "_")}
     ctx, q_len = int(g["ctx"]), int(g["q_len"])
