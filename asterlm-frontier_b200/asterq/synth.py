@@ -256,6 +256,8 @@ def make_shard_workload(
     device="cuda",
     page_tokens: int = 512,
     keep_host: set[int] | None = None,
+    scheme: str = "hadamard_int4",
+    quantize_rope: bool = False,
 ) -> Workload:
     """The sequences `shard` (indices into `lengths`) of a seeded batch, with pools for them
     only: every rank of a sequence-sharded job draws the whole batch from the same seed and
@@ -264,7 +266,7 @@ def make_shard_workload(
     device = torch.device(device)
     pos = {gi: k for k, gi in enumerate(shard)}
     b = PoolBuilder([lengths[i] for i in shard], [hot[i] for i in shard], q_len=q_len, n_heads=n_heads,
-                    page_tokens=page_tokens, device=device)
+                    page_tokens=page_tokens, device=device, scheme=scheme, quantize_rope=quantize_rope)
     keep_host = keep_host or set()
     host: dict[int, dict[str, torch.Tensor]] = {}
     pending: dict[int, tuple] = {}

@@ -869,6 +869,19 @@ def extras(dev, args) -> dict:
                      "GB/s": b / ms / 1e6, "frac_hbm": b / ms / 1e6 / peak, "TFLOP/s": wl.flops() / ms / 1e9,
                      "ms_graph": ms_graph, "seq_steps_per_s_graph": len(wl.lengths) / ms_graph * 1e3}
 
+    # chunked prefill (decode.py:105-108, prefill_chunk_size 2048): 2048 new tokens attending to an
+    # 8k-token cache and causally to each other, through the decode kernel (one 16-row block per
+    # new token); FLOPs counted over each token's visible keys
+    T, ctx = 2048, 8192
+    inp = c1_inputs(seed=0, ctx=ctx, q_len=T)
+    bp = PoolBuilder([ctx], [1024], q_len=T, n_heads=16, device=dev)
+    bp.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    decode_rate(bp.finish("prefill"), "prefill_2048_over_8k", 5)
+    pf = res["prefill_2048_over_8k"]
+    pf_flops = 2 * 16 * (512 + 64 + 512) * sum(ctx + t + 1 for t in range(T))
+    pf.update({"TFLOP/s": pf_flops / pf["ms"] / 1e9, "tokens_per_s": T / pf["ms"] * 1e3,
+               "note": "TFLOP/s over the causally visible keys; seq_steps_per_s counts chunks"})
+    del bp, inp
     inp = c1_inputs(seed=0)
     b1 = PoolBuilder([8192], [1024], q_len=1, n_heads=16, device=dev)
     b1.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])

@@ -12,7 +12,8 @@ result is meant to be bit-exact:
 * ``normalized_fwht``      quantization/kv.py:13-32
 * ``pack_int4``            quantization/kv.py:41-48
 * ``unpack_int4``          quantization/kv.py:51-55
-* ``quantize``             quantization/kv.py:76-118
+* ``quantize``             quantization/kv.py:76-118 (the float8 scheme, kv.py:85-89, is torch's
+                           own cast, which ``float8_bytes`` calls rather than restates)
 * ``dequantize``           quantization/kv.py:121-134
 * ``absorbed_decode``      layers/latent_attention.py:177-231 (q_len == 1)
 * ``causal_attention``     layers/latent_attention.py:116-175 (q_len >= 1)
@@ -506,7 +507,8 @@ def max_abs(a: np.ndarray, b: np.ndarray) -> float:
 
 
 def decode_sequence(latent: np.ndarray, rope: np.ndarray, q_lat: np.ndarray, q_rope: np.ndarray, n: int, hot: int,
-                    softmax_scale: float, chunk: int = 512) -> np.ndarray:
+                    softmax_scale: float, chunk: int = 512, scheme: str = "hadamard_int4",
+                    quantize_rope: bool = False) -> np.ndarray:
     """One sequence of a ragged batch: tokens [0, n) are the cache (the newest ``hot`` in the hot
     window, older ones in ``chunk``-token cold chunks, the newest possibly partial), tokens
     [n, n + q_len) the step's new tokens; returns the context latents [q_len, H, 512]
@@ -514,6 +516,6 @@ def decode_sequence(latent: np.ndarray, rope: np.ndarray, q_lat: np.ndarray, q_r
     that a process pool can run sequences in parallel."""
     latent = np.asarray(latent, dtype=np.float32)
     rope = np.asarray(rope, dtype=np.float32)
-    cache = build_cache_split(latent[:n], rope[:n], hot, chunk)
+    cache = build_cache_split(latent[:n], rope[:n], hot, chunk, scheme=scheme, quantize_rope=quantize_rope)
     return decode(np.asarray(q_lat, np.float32), np.asarray(q_rope, np.float32), latent[n:], rope[n:], cache,
                   softmax_scale)

@@ -46,10 +46,11 @@ def assert_close_bf16(out_bf16: np.ndarray, ref_fp32: np.ndarray, what: str) -> 
     assert rel <= REL_L2 and worst <= 0.0, f"{what}: rel-L2 {rel:.3e}, worst excess over bound {worst:.3e}"
 
 
-def oracle_batch(host: dict, lengths, hot) -> dict:
+def oracle_batch(host: dict, lengths, hot, scheme: str = "hadamard_int4", quantize_rope: bool = False) -> dict:
     """Oracle outputs of the sequences in ``host`` (position -> CPU bf16 tensors), in parallel."""
     jobs = {k: (h["latent"].float().numpy(), h["rope"].float().numpy(), h["q_lat"].float().numpy(),
-                h["q_rope"].float().numpy(), lengths[k], hot[k], SCALE) for k, h in host.items()}
+                h["q_rope"].float().numpy(), lengths[k], hot[k], SCALE, 512, scheme, quantize_rope)
+            for k, h in host.items()}
     workers = max(1, min(16, (os.cpu_count() or 2) // 2, len(jobs)))
     with ProcessPoolExecutor(max_workers=workers, mp_context=mp.get_context("spawn")) as ex:
         futs = {k: ex.submit(O.decode_sequence, *args) for k, args in jobs.items()}
@@ -57,10 +58,11 @@ def oracle_batch(host: dict, lengths, hot) -> dict:
 
 
 def run_decode(wl, out_dtype):
-    from asterq.decode import DeviceDecodePlan, latent_decode
+    from asterq.decode import COLD_TILE_TOKENS, DeviceDecodePlan, latent_decode
     from asterq.plan import build_plan
 
-    dplan = DeviceDecodePlan(build_plan(wl.layouts, wl.n_heads), wl.q_lat.device)
+    plan = build_plan(wl.layouts, wl.n_heads, cold_tile=COLD_TILE_TOKENS[wl.pools.cold_scheme])
+    dplan = DeviceDecodePlan(plan, wl.q_lat.device)
     out = latent_decode(wl.pools, dplan, wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE,
                         out_dtype=out_dtype)
     torch.cuda.synchronize()
@@ -100,6 +102,25 @@ def test_c3_every_sequence_of_the_benched_batch(cuda):
     for i in range(64):
         assert_close(out32[i:i + 1], refs[i], f"C3 seq {i} (len {lens[i]}) fp32")
         assert_close_bf16(out16[i:i + 1], refs[i], f"C3 seq {i} bf16")
+
+
+@pytest.mark.parametrize("scheme,qrope", [("int8", False), ("float8", False), ("hadamard_int4", True),
+                                          ("int8", True)])
+def test_c3_batch_other_cache_schemes(cuda, scheme, qrope):
+    """The benched C3 batch (64 sequences, 948k cached tokens) stored with the other cache schemes
+    the reference offers (int8, float8, quantized RoPE keys); every 4th sequence checked against
+    the oracle (16 sequences from 1k to 32k tokens), fp32 output."""
+    from asterq.synth import c3_lengths, make_shard_workload
+
+    lens = c3_lengths(0, 64)
+    hot = [min(n, 2048) for n in lens]
+    keep = set(range(0, 64, 4))
+    wl = make_shard_workload("C3", lens, hot, list(range(64)), q_len=1, seed=1000, device=cuda, keep_host=keep,
+                             scheme=scheme, quantize_rope=qrope)
+    out32 = run_decode(wl, torch.float32).cpu().numpy()
+    refs = oracle_batch(wl.host, wl.lengths, wl.hot, scheme, qrope)
+    for i in sorted(keep):
+        assert_close(out32[i:i + 1], refs[i], f"C3 {scheme} qrope={qrope} seq {i} (len {lens[i]})")
 
 
 def test_c4_full_length_one_gpu_and_context_parallel(cuda):
