@@ -84,7 +84,10 @@ constexpr int kCRopeScale = kCRope + 4096;  // quantized RoPE: fp16 scales of th
 constexpr int kScales = 49152;     // cold: [128][16 B] fp16 scales, plain
 constexpr int kHotBlock = 4096;    // hot: latent scale-group g at g*4096: [32][128 B], SW128
 constexpr int kHRope = 32768;      // hot: [32][128 B] RoPE keys, SW128
+constexpr int kHotPartial = 36864; // hot, byte-code modes: the score team's partial scores
+constexpr int kPartStride = 20;    //   [4 warps][32 tokens][kPartStride floats] (padded row stride)
 constexpr int kStageBytes = 51200;
+static_assert(kHotPartial + 4 * 32 * kPartStride * 4 <= kStageBytes, "hot partial scores fit the stage's tail");
 
 constexpr int kOffQi = kStages * kStageBytes;  // cold query int8 limb fragments [16 k-steps][2][32] uint4
                                                // (32 KB region: the [16][512] fp32 scratch after the tiles)
@@ -1065,40 +1068,113 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
           }
         } else {
-          // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
-          // S[1] is a second partial accumulator (odd groups) folded in below
-          const int row = 8 * tw + (lane & 7);
-#pragma unroll 1
-          for (int g = 0; g < 8; g += 2) {
+          if constexpr (kBytes) {
+            // hot / new tile (32 tokens), byte-code modes: warp tw scores all 32 tokens (two full
+            // m-tiles) over scale groups 2tw and 2tw + 1 and RoPE k-step tw; the four partial scores
+            // meet in the stage's tail (a hot tile's bf16 data ends at kHotPartial) and warp tw sums
+            // the rows of its own 8 tokens 8tw + gid, the layout the softmax below reads.  (The
+            // INT4 modes keep the form below, which measured faster there.)
+            float part[2][2][2][4];  // [group of the pair][m-tile][nt][c]
 #pragma unroll
-            for (int ks = 0; ks < 4; ++ks) {
-              uint32_t a[2][4];
-              ldmatrix_x4(a[0], sst + g * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
-              ldmatrix_x4(a[1], sst + (g + 1) * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+            for (int h2 = 0; h2 < 2; ++h2)
 #pragma unroll
-              for (int h2 = 0; h2 < 2; ++h2)
+              for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-                for (int nt = 0; nt < 2; ++nt) {
-                  const uint2 bq = qh[(((g + h2) * 4 + ks) * 2 + nt) * 32 + lane];
-                  mma_bf16(S[h2][nt], a[h2], bq.x, bq.y);
+                for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+                  for (int c = 0; c < 4; ++c) part[h2][mt][nt][c] = 0.0f;
+            const int lrow = (lane & 7) + 8 * ((lane >> 3) & 1);
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+              for (int h2 = 0; h2 < 2; ++h2) {
+                const int g = 2 * tw + h2;
+#pragma unroll
+                for (int mt = 0; mt < 2; ++mt) {
+                  uint32_t a[4];
+                  ldmatrix_x4(a, sst + g * kHotBlock + swz(16 * mt + lrow, 2 * ks + (lane >> 4)));
+#pragma unroll
+                  for (int nt = 0; nt < 2; ++nt) {
+                    const uint2 bq = qh[((g * 4 + ks) * 2 + nt) * 32 + lane];
+                    mma_bf16(part[h2][mt][nt], a, bq.x, bq.y);
+                  }
                 }
+              }
+#pragma unroll
+            for (int mt = 0; mt < 2; ++mt) {
+              uint32_t a[4];
+              ldmatrix_x4(a, sst + kHRope + swz(16 * mt + lrow, 2 * tw + (lane >> 4)));
+#pragma unroll
+              for (int nt = 0; nt < 2; ++nt) {
+                const uint2 bq = qr[(tw * 2 + nt) * 32 + lane];
+                mma_bf16(part[1][mt][nt], a, bq.x, bq.y);
+              }
             }
-          }
+            // partial scores [warp][token][row] (row stride kPartStride floats) in the stage's tail
+            float* xbuf = reinterpret_cast<float*>(smem + s * kStageBytes + kHotPartial);
 #pragma unroll
-          for (int nt = 0; nt < 2; ++nt)
+            for (int mt = 0; mt < 2; ++mt)
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-              S[0][nt][c] += S[1][nt][c];
-              S[1][nt][c] = 0.0f;
-            }
+              for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-          for (int ks = 0; ks < 4; ++ks) {
-            uint32_t a[4];
-            ldmatrix_x4(a, sst + kHRope + swz(row, 2 * ks + (lane >> 4)));
+                for (int h = 0; h < 2; ++h) {
+                  const int token = 16 * mt + gid + 8 * h;
+                  *reinterpret_cast<float2*>(xbuf + (tw * kHotTile + token) * kPartStride + 8 * nt + 2 * tq) =
+                      make_float2(part[0][mt][nt][2 * h] + part[1][mt][nt][2 * h],
+                                  part[0][mt][nt][2 * h + 1] + part[1][mt][nt][2 * h + 1]);
+                }
+            named_sync(1 + team, 32 * kTeamWarps);
 #pragma unroll
             for (int nt = 0; nt < 2; ++nt) {
-              const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
-              mma_bf16(S[0][nt], a, bq.x, bq.y);
+              float2 sum = make_float2(0.0f, 0.0f);
+#pragma unroll
+              for (int w = 0; w < kTeamWarps; ++w) {
+                const float2 v =
+                    *reinterpret_cast<const float2*>(xbuf + (w * kHotTile + 8 * tw + gid) * kPartStride + 8 * nt + 2 * tq);
+                sum.x += v.x;
+                sum.y += v.y;
+              }
+              S[0][nt][0] = sum.x;
+              S[0][nt][1] = sum.y;
+            }
+            // these generic-proxy writes precede the next TMA write of this stage (after its release)
+            fence_async_shared();
+          } else {
+            // hot / new tile: this warp's 8 tokens fill m-tile rows 0-7 (rows 8-15 repeat them);
+            // S[1] is a second partial accumulator (odd groups) folded in below
+            const int row = 8 * tw + (lane & 7);
+  #pragma unroll 1
+            for (int g = 0; g < 8; g += 2) {
+  #pragma unroll
+              for (int ks = 0; ks < 4; ++ks) {
+                uint32_t a[2][4];
+                ldmatrix_x4(a[0], sst + g * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+                ldmatrix_x4(a[1], sst + (g + 1) * kHotBlock + swz(row, 2 * ks + (lane >> 4)));
+  #pragma unroll
+                for (int h2 = 0; h2 < 2; ++h2)
+  #pragma unroll
+                  for (int nt = 0; nt < 2; ++nt) {
+                    const uint2 bq = qh[(((g + h2) * 4 + ks) * 2 + nt) * 32 + lane];
+                    mma_bf16(S[h2][nt], a[h2], bq.x, bq.y);
+                  }
+              }
+            }
+  #pragma unroll
+            for (int nt = 0; nt < 2; ++nt)
+  #pragma unroll
+              for (int c = 0; c < 4; ++c) {
+                S[0][nt][c] += S[1][nt][c];
+                S[1][nt][c] = 0.0f;
+              }
+  #pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              uint32_t a[4];
+              ldmatrix_x4(a, sst + kHRope + swz(row, 2 * ks + (lane >> 4)));
+  #pragma unroll
+              for (int nt = 0; nt < 2; ++nt) {
+                const uint2 bq = qr[(ks * 2 + nt) * 32 + lane];
+                mma_bf16(S[0][nt], a, bq.x, bq.y);
+              }
             }
           }
         }
