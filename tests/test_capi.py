@@ -204,6 +204,10 @@ def test_plan_and_append_reject_bad_arguments_without_touching_the_gpu():
     assert lib.asterq_plan_batch(ctypes.byref(d), ctypes.byref(b), None) == _lib.ASTERQ_ERR_INVALID_ARGUMENT
     assert lib.asterq_plan_scratch_bytes(ctypes.byref(d), 4, 4, 4) == 0
     d.n_workers = 148
+    d.cold_tile_tokens = 32  # cold tiles of 0 (= 128), 64 or 128 tokens only
+    assert lib.asterq_plan_batch(ctypes.byref(d), ctypes.byref(b), None) == _lib.ASTERQ_ERR_UNSUPPORTED
+    assert b"cold_tile_tokens" in lib.asterq_last_error()
+    d.cold_tile_tokens = 0
     # scratch: tile costs, segment and per-unit prefix arrays (int64), per-boundary and per-item int32
     n_segs = 2 * (4 + 2)
     want = 8 * (10 + 1 + n_segs + 1 + 2 + 1 + 6 * (3 + 1) + 148 + 1) + 4 * (3 * 148 + 5)

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 
 from asterq import _lib
-from asterq.plan import COLD_TILE, HOT_TILE, SequenceLayout, build_plan
+from asterq.plan import COLD_TILE, COLD_TILE_INT8, HOT_TILE, SequenceLayout, build_plan
 
 
 def _layout(cold, hot, q_start=0, q_len=1):
@@ -215,10 +215,28 @@ def test_vectorized_tile_table_matches_the_per_sequence_walk():
         hot = [(int(rng.integers(0, 99)), int(rng.integers(0, 64)), int(rng.integers(1, 600))) for _ in range(rng.integers(0, 4))]
         seqs.append(SequenceLayout(cold=cold, hot=hot, q_start=3 * i, q_len=int(rng.integers(1, 70)),
                                    attend_new=bool(rng.integers(0, 4))))
-    tiles, off = _tile_table(seqs)
-    want = []
-    for k, seq in enumerate(seqs):
-        mine = _tiles_of(seq)
-        assert off[k + 1] - off[k] == len(mine)
-        want.extend(mine)
-    assert np.array_equal(tiles, np.asarray(want, dtype=np.int32).reshape(-1, 4))
+    for cold_tile in (COLD_TILE, COLD_TILE_INT8):
+        tiles, off = _tile_table(seqs, cold_tile)
+        want = []
+        for k, seq in enumerate(seqs):
+            mine = _tiles_of(seq, cold_tile)
+            assert off[k + 1] - off[k] == len(mine)
+            want.extend(mine)
+        assert np.array_equal(tiles, np.asarray(want, dtype=np.int32).reshape(-1, 4))
+
+
+def test_one_byte_schemes_plan_64_token_cold_tiles():
+    """cold_tile=64 (int8 / float8 codes): every cold tile at most 64 tokens, each token once, and the
+    same estimated time per full tile as a 128-token INT4 tile (an equal split of the work)."""
+    seqs = [SequenceLayout(cold=[(0, 0, 512), (1, 0, 300)], hot=[(0, 0, 100)], q_start=0, q_len=1),
+            SequenceLayout(cold=[(2, 0, 512)] * 6, hot=[(1, 0, 2048)], q_start=1, q_len=1)]
+    p128 = build_plan(seqs, 16, n_sms=16)
+    p64 = build_plan(seqs, 16, n_sms=16, cold_tile=COLD_TILE_INT8)
+    assert p128.cold_tile == COLD_TILE and p64.cold_tile == COLD_TILE_INT8
+    cold64 = p64.tiles[p64.tiles[:, 0] == _lib.TILE_COLD]
+    cold128 = p128.tiles[p128.tiles[:, 0] == _lib.TILE_COLD]
+    assert cold64[:, 3].max() == 64 and cold64[:, 3].sum() == cold128[:, 3].sum() == 512 + 300 + 6 * 512
+    pages = [512, 300] + [512] * 6
+    assert len(cold64) == sum(-(-n // 64) for n in pages) and len(cold128) == sum(-(-n // 128) for n in pages)
+    with pytest.raises(ValueError, match="cold_tile"):
+        build_plan(seqs, 16, cold_tile=32)
