@@ -31,7 +31,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from .decode import COLD_SCHEMES, GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools, set_cold_pools
+from .decode import COLD_SCHEMES, COLD_TILE_TOKENS, GROUP_SIZE, LATENT_DIM, ROPE_DIM, LatentPools, set_cold_pools
 from .plan import QPREP_BYTES
 
 COLD_TILE = 128
@@ -322,7 +322,8 @@ class PagedLatentBatch:
     ``s * q_len`` .. of the step's arrays ([max_seqs * q_len, H, 512] etc.; rows of empty
     slots are ignored).  Pools have fixed capacities (``hot_pool_pages``, ``cold_pool_pages``
     pages of ``page_tokens`` tokens), so the step's pointers never change and a captured step
-    stays valid.  ``cache_dtype`` "hadamard_int4" or "int4" (cold pages) as in the reference.
+    stays valid.  ``cache_dtype`` "hadamard_int4", "int4", "int8" or "float8" (cold pages) as in the
+    reference (bf16 cold RoPE keys).
     """
 
     def __init__(self, n_heads: int, *, max_seqs: int, q_len: int = 1, page_tokens: int = 512,
@@ -330,8 +331,8 @@ class PagedLatentBatch:
                  hot_pool_pages: int | None = None, cold_pool_pages: int | None = None,
                  n_workers: int | None = None, plan_ahead: bool = False, window_size: int | None = None,
                  sink_tokens: int = 0, device="cuda") -> None:
-        if cache_dtype not in ("hadamard_int4", "int4"):
-            raise NotImplementedError(f"cache_dtype {cache_dtype!r}: the serving batch pools hadamard_int4 and int4")
+        if cache_dtype not in COLD_SCHEMES:
+            raise NotImplementedError(f"cache_dtype {cache_dtype!r}: the serving batch pools {tuple(COLD_SCHEMES)}")
         if not 0 < q_len <= page_tokens:
             raise ValueError("q_len must be in 1..page_tokens")
         self.device = torch.device(device)
@@ -354,8 +355,8 @@ class PagedLatentBatch:
             hot_pool_pages = max_seqs * max_hot_pages
         if cold_pool_pages is None:
             cold_pool_pages = max_seqs * max_cold_pages
-        self.pools = LatentPools.empty(cold_pool_pages, hot_pool_pages, P, self.device)
-        self.pools.cold_scheme = cache_dtype
+        self.pools = LatentPools.empty(cold_pool_pages, hot_pool_pages, P, self.device, cold_scheme=cache_dtype)
+        self.cold_tile = COLD_TILE_TOKENS[cache_dtype]
         self._hot_free, self._cold_free = _PagePool(hot_pool_pages), _PagePool(cold_pool_pages)
         # plan_ahead: the next step's schedule is built on a side stream while this step decodes,
         # on the one SM the decode leaves free (one worker fewer), into the other of two planners
@@ -363,7 +364,8 @@ class PagedLatentBatch:
         self.plan_ahead = bool(plan_ahead)
         if self.plan_ahead and n_workers is None:
             n_workers = torch.cuda.get_device_properties(self.device).multi_processor_count - 1
-        self.planner = DevicePlanner(self.tables, n_heads, P, max_q_len=q_len, n_workers=n_workers)
+        self.planner = DevicePlanner(self.tables, n_heads, P, max_q_len=q_len, n_workers=n_workers,
+                                     cold_tile=self.cold_tile)
         self._ahead: list[DevicePlanner] = []
         self._ahead_gen = -1
         self._ahead_ready: int | None = None  # planner index holding the next step's schedule
@@ -501,21 +503,24 @@ class PagedLatentBatch:
         """Encode len(pages) full chunks of bf16 tokens into the given cold pages."""
         P, n = self.page_tokens, latent.shape[0]
         lib = _lib.load()
-        codes = torch.empty(n, LATENT_DIM // 2, dtype=torch.uint8, device=self.device)
-        scales = torch.empty(n, LATENT_DIM // GROUP_SIZE, dtype=torch.float16, device=self.device)
+        codes = torch.empty(n, self.pools.cold_codes.shape[-1], dtype=self.pools.cold_codes.dtype, device=self.device)
+        n_scales = int(self.pools.cold_scales.shape[-1])  # 0 for float8
+        scales = torch.empty(n, max(n_scales, 1), dtype=torch.float16, device=self.device)
         _lib.check(lib.asterq_quantize(latent.data_ptr(), _lib.DTYPE_BF16, n, LATENT_DIM, LATENT_DIM,
                                        COLD_SCHEMES[self.cache_dtype], GROUP_SIZE, codes.data_ptr(),
                                        scales.data_ptr(), _lib.stream_handle(self.device)))
         di = _pinned(np.asarray(pages, np.int64)).to(self.device, non_blocking=True)
         self.pools.cold_codes.index_copy_(0, di, codes.view(len(pages), P, -1))
-        self.pools.cold_scales.index_copy_(0, di, scales.view(len(pages), P, -1))
+        if n_scales:
+            self.pools.cold_scales.index_copy_(0, di, scales.view(len(pages), P, -1))
         self.pools.cold_rope.index_copy_(0, di, rope.reshape(len(pages), P, ROPE_DIM))
 
     # ------------------------------------------------------------------ steps
     def _ahead_planners(self) -> list[DevicePlanner]:
         if self._ahead_gen != self.tables.generation:  # (re)bind to the tables as they are now
             self._ahead = [DevicePlanner(self.tables.shadow(), self.n_heads, self.page_tokens, max_q_len=self.q_len,
-                                         n_workers=self.planner.n_workers) for _ in range(2)]
+                                         n_workers=self.planner.n_workers, cold_tile=self.cold_tile)
+                           for _ in range(2)]
             self._ahead_gen = self.tables.generation
             self._ahead_ready = None
         return self._ahead

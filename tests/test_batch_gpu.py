@@ -223,13 +223,15 @@ class _History:
         return torch.cat(self.lat[slot]).float().numpy(), torch.cat(self.rope[slot]).float().numpy()
 
 
-@pytest.mark.parametrize("q_len", [1, 3])
-def test_decode_loop_with_flushes_and_turnover_matches_the_oracle(cuda, q_len):
+@pytest.mark.parametrize("q_len,scheme", [(1, "hadamard_int4"), (3, "hadamard_int4"), (1, "int8"), (3, "float8")])
+def test_decode_loop_with_flushes_and_turnover_matches_the_oracle(cuda, q_len, scheme):
+    """The serving loop with flushes and a sequence replaced mid-run, for INT4 pages and for the
+    one-byte schemes (int8, float8: 64-token cold tiles planned on the GPU)."""
     from asterq.batch import PagedLatentBatch
 
     P, recent = 128, 64  # a page is flushed whenever a hot window passes 192 tokens
     batch = PagedLatentBatch(16, max_seqs=5, q_len=q_len, page_tokens=P, recent_tokens=recent,
-                             max_cold_pages=40, device=cuda)
+                             max_cold_pages=40, cache_dtype=scheme, device=cuda)
     g = torch.Generator(device=cuda).manual_seed(11 + q_len)
     hist = _History()
 
@@ -266,7 +268,7 @@ def test_decode_loop_with_flushes_and_turnover_matches_the_oracle(cuda, q_len):
                 lat = np.concatenate([lat, new_lat[r].float().cpu().numpy()])
                 rope = np.concatenate([rope, new_rope[r].float().cpu().numpy()])
                 want = O.decode_sequence(lat, rope, q_lat[r].float().cpu().numpy(), q_rope[r].float().cpu().numpy(),
-                                         n, hot, SCALE, chunk=P)
+                                         n, hot, SCALE, chunk=P, scheme=scheme)
                 _close(got[r], want, f"step {step} slot {s} (n {n}, hot {hot})")
                 checked += 1
         for s in before:
@@ -288,10 +290,11 @@ def test_decode_loop_with_flushes_and_turnover_matches_the_oracle(cuda, q_len):
         if n_cold:
             pages = [int(p) for p in h["cold_pages"][s, :n_cold]]
             codes = torch.cat([batch.pools.cold_codes[p] for p in pages]).cpu().numpy()
-            scales = torch.cat([batch.pools.cold_scales[p] for p in pages]).cpu().numpy()
-            q = O.quantize(lat[:cold], "hadamard_int4", 64)
-            np.testing.assert_array_equal(codes, q.data.reshape(cold, 256))
-            np.testing.assert_array_equal(scales.view(np.uint16), q.scale.reshape(cold, 8).view(np.uint16))
+            q = O.quantize(lat[:cold], scheme, 64)
+            np.testing.assert_array_equal(codes.view(np.uint8), q.data.reshape(cold, -1).view(np.uint8))
+            if q.scale is not None:
+                scales = torch.cat([batch.pools.cold_scales[p] for p in pages]).cpu().numpy()
+                np.testing.assert_array_equal(scales.view(np.uint16), q.scale.reshape(cold, 8).view(np.uint16))
 
 
 def test_captured_step_replays_like_the_eager_step(cuda):
