@@ -323,14 +323,15 @@ class PagedLatentBatch:
     slots are ignored).  Pools have fixed capacities (``hot_pool_pages``, ``cold_pool_pages``
     pages of ``page_tokens`` tokens), so the step's pointers never change and a captured step
     stays valid.  ``cache_dtype`` "hadamard_int4", "int4", "int8" or "float8" (cold pages) as in the
-    reference (bf16 cold RoPE keys).
+    reference; ``quantize_rope`` stores the cold RoPE keys as codes of the same scheme
+    (cache.py:160-164), else they stay bf16.
     """
 
     def __init__(self, n_heads: int, *, max_seqs: int, q_len: int = 1, page_tokens: int = 512,
                  recent_tokens: int = 512, cache_dtype: str = "hadamard_int4", max_cold_pages: int = 64,
                  hot_pool_pages: int | None = None, cold_pool_pages: int | None = None,
                  n_workers: int | None = None, plan_ahead: bool = False, window_size: int | None = None,
-                 sink_tokens: int = 0, device="cuda") -> None:
+                 sink_tokens: int = 0, quantize_rope: bool = False, device="cuda") -> None:
         if cache_dtype not in COLD_SCHEMES:
             raise NotImplementedError(f"cache_dtype {cache_dtype!r}: the serving batch pools {tuple(COLD_SCHEMES)}")
         if not 0 < q_len <= page_tokens:
@@ -355,7 +356,8 @@ class PagedLatentBatch:
             hot_pool_pages = max_seqs * max_hot_pages
         if cold_pool_pages is None:
             cold_pool_pages = max_seqs * max_cold_pages
-        self.pools = LatentPools.empty(cold_pool_pages, hot_pool_pages, P, self.device, cold_scheme=cache_dtype)
+        self.pools = LatentPools.empty(cold_pool_pages, hot_pool_pages, P, self.device, cold_scheme=cache_dtype,
+                                       quantize_rope=quantize_rope)
         self.cold_tile = COLD_TILE_TOKENS[cache_dtype]
         self._hot_free, self._cold_free = _PagePool(hot_pool_pages), _PagePool(cold_pool_pages)
         # plan_ahead: the next step's schedule is built on a side stream while this step decodes,
@@ -460,7 +462,10 @@ class PagedLatentBatch:
             dst = self._cold_free.alloc(len(cold))
             src = torch.tensor([pg for pg, _, _ in cold], dtype=torch.int64, device=dev)
             di = torch.tensor(dst, dtype=torch.int64, device=dev)
-            for name in ("cold_codes", "cold_scales", "cold_rope"):
+            names = ["cold_codes", "cold_scales", "cold_rope"]
+            if self.pools.cold_rope_scales is not None:
+                names.append("cold_rope_scales")
+            for name in names:  # (the source pools must use the batch's scheme and RoPE form)
                 getattr(self.pools, name).index_copy_(0, di, getattr(pools, name).index_select(0, src))
             h["cold_pages"][slot, : len(cold)] = dst
             h["cold_tokens"][slot, : len(cold)] = [n for _, _, n in cold]
@@ -513,7 +518,19 @@ class PagedLatentBatch:
         self.pools.cold_codes.index_copy_(0, di, codes.view(len(pages), P, -1))
         if n_scales:
             self.pools.cold_scales.index_copy_(0, di, scales.view(len(pages), P, -1))
-        self.pools.cold_rope.index_copy_(0, di, rope.reshape(len(pages), P, ROPE_DIM))
+        if self.pools.rope_quantized:
+            # quantize_rope (cache.py:163): RoPE keys as codes of the cold scheme, one group of 64
+            rcodes = torch.empty(n, self.pools.cold_rope.shape[-1], dtype=self.pools.cold_rope.dtype, device=self.device)
+            rscales = torch.empty(n, 1, dtype=torch.float16, device=self.device)
+            rope = rope.reshape(n, ROPE_DIM).to(torch.bfloat16).contiguous()
+            _lib.check(lib.asterq_quantize(rope.data_ptr(), _lib.DTYPE_BF16, n, ROPE_DIM, ROPE_DIM,
+                                           COLD_SCHEMES[self.cache_dtype], GROUP_SIZE, rcodes.data_ptr(),
+                                           rscales.data_ptr(), _lib.stream_handle(self.device)))
+            self.pools.cold_rope.index_copy_(0, di, rcodes.view(len(pages), P, -1))
+            if self.pools.cold_rope_scales is not None:
+                self.pools.cold_rope_scales.index_copy_(0, di, rscales.view(len(pages), P))
+        else:
+            self.pools.cold_rope.index_copy_(0, di, rope.reshape(len(pages), P, ROPE_DIM))
 
     # ------------------------------------------------------------------ steps
     def _ahead_planners(self) -> list[DevicePlanner]:

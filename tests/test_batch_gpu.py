@@ -223,15 +223,18 @@ class _History:
         return torch.cat(self.lat[slot]).float().numpy(), torch.cat(self.rope[slot]).float().numpy()
 
 
-@pytest.mark.parametrize("q_len,scheme", [(1, "hadamard_int4"), (3, "hadamard_int4"), (1, "int8"), (3, "float8")])
-def test_decode_loop_with_flushes_and_turnover_matches_the_oracle(cuda, q_len, scheme):
+@pytest.mark.parametrize("q_len,scheme,qrope", [(1, "hadamard_int4", False), (3, "hadamard_int4", False),
+                                                (1, "int8", False), (3, "float8", False), (1, "hadamard_int4", True),
+                                                (1, "int8", True), (1, "float8", True)])
+def test_decode_loop_with_flushes_and_turnover_matches_the_oracle(cuda, q_len, scheme, qrope):
     """The serving loop with flushes and a sequence replaced mid-run, for INT4 pages and for the
-    one-byte schemes (int8, float8: 64-token cold tiles planned on the GPU)."""
+    one-byte schemes (int8, float8: 64-token cold tiles planned on the GPU), with bf16 or
+    quantized cold RoPE keys."""
     from asterq.batch import PagedLatentBatch
 
     P, recent = 128, 64  # a page is flushed whenever a hot window passes 192 tokens
     batch = PagedLatentBatch(16, max_seqs=5, q_len=q_len, page_tokens=P, recent_tokens=recent,
-                             max_cold_pages=40, cache_dtype=scheme, device=cuda)
+                             max_cold_pages=40, cache_dtype=scheme, quantize_rope=qrope, device=cuda)
     g = torch.Generator(device=cuda).manual_seed(11 + q_len)
     hist = _History()
 
@@ -268,7 +271,7 @@ def test_decode_loop_with_flushes_and_turnover_matches_the_oracle(cuda, q_len, s
                 lat = np.concatenate([lat, new_lat[r].float().cpu().numpy()])
                 rope = np.concatenate([rope, new_rope[r].float().cpu().numpy()])
                 want = O.decode_sequence(lat, rope, q_lat[r].float().cpu().numpy(), q_rope[r].float().cpu().numpy(),
-                                         n, hot, SCALE, chunk=P, scheme=scheme)
+                                         n, hot, SCALE, chunk=P, scheme=scheme, quantize_rope=qrope)
                 _close(got[r], want, f"step {step} slot {s} (n {n}, hot {hot})")
                 checked += 1
         for s in before:
