@@ -35,7 +35,7 @@ from dataclasses import replace
 import torch
 
 from . import _lib
-from .decode import LATENT_DIM, DeviceDecodePlan, LatentPools, capture_step, make_params
+from .decode import COLD_TILE_TOKENS, LATENT_DIM, DeviceDecodePlan, LatentPools, capture_step, make_params
 from .plan import ROWS_PER_BLOCK, SequenceLayout, build_plan
 from .sharding import COLD_TOKEN_BYTES, HOT_TOKEN_BYTES
 
@@ -147,6 +147,7 @@ class ContextParallelDecoder:
         self.pools, self.rank, self.world, self.n_heads = pools, rank, world, n_heads
         self.device = torch.device(device)
         self.local = rank_layout(replace(layout, q_start=0), rank, world)
+        plan_kw.setdefault("cold_tile", COLD_TILE_TOKENS.get(pools.cold_scheme, 128))
         self.plan = build_plan([self.local], n_heads, force_partial=True, **plan_kw)
         self.dplan = DeviceDecodePlan(self.plan, self.device)
         self.n_rb = int(self.plan.combine.shape[0])

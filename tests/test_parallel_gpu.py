@@ -51,6 +51,30 @@ def test_emulated_ranks_match_oracle(cuda, world, q_len, n_chunks):
     assert torch.equal(out, out2)
 
 
+@pytest.mark.parametrize("scheme,qrope", [("int8", False), ("float8", True), ("int4", True)])
+def test_emulated_ranks_other_cache_schemes(cuda, scheme, qrope):
+    """Context-parallel decode of a sequence stored with the other cache schemes: each rank's plan
+    cuts its cold pages into the scheme's tiles (64 tokens for int8 / float8)."""
+    from asterq.context_parallel import ContextParallelDecoder
+    from asterq.synth import PoolBuilder, c1_inputs
+
+    world, ctx, hot = 3, 9 * 512 + 200, 600
+    inp = c1_inputs(seed=77, ctx=ctx, q_len=1)
+    b = PoolBuilder([ctx], [hot], q_len=1, n_heads=16, device=cuda, scheme=scheme, quantize_rope=qrope)
+    b.add(inp["latent"], inp["rope"], inp["q_lat"], inp["q_rope"])
+    wl = b.finish("cp")
+    decs = [ContextParallelDecoder(wl.pools, wl.layouts[0], 16, r, world, cuda) for r in range(world)]
+    recs = [d.partial(wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope, softmax_scale=SCALE).clone() for d in decs]
+    out = torch.empty(1, 16, 512, dtype=torch.float32, device=cuda)
+    decs[1].finish(torch.cat(recs), out)
+    torch.cuda.synchronize()
+    lat, rope = inp["latent"].float().numpy(), inp["rope"].float().numpy()
+    cache = O.build_cache_split(lat[:ctx], rope[:ctx], hot, 512, scheme=scheme, quantize_rope=qrope)
+    ref = O.decode(inp["q_lat"].float().numpy(), inp["q_rope"].float().numpy(), lat[ctx:], rope[ctx:], cache, SCALE)
+    got = out.cpu().numpy()
+    assert O.rel_l2(got, ref) <= 1e-3 and O.max_abs(got, ref) <= 2e-2
+
+
 def test_merge_then_combine_equals_direct_combine(cuda):
     from asterq import _lib
     from asterq.decode import DeviceDecodePlan, latent_decode
