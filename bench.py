@@ -599,7 +599,8 @@ def e2e_measure(wl, dev, stream, args, barrier, max_over_ranks) -> dict:
     # outlast the step's GPU time.
     use_graph = n <= 32
     batch = PagedLatentBatch(wl.n_heads, max_seqs=n, q_len=1, page_tokens=P, recent_tokens=2048 - P,
-                             max_cold_pages=max_cold, plan_ahead=not use_graph, device=dev)
+                             max_cold_pages=max_cold, plan_ahead=not use_graph, cache_dtype=wl.pools.cold_scheme,
+                             quantize_rope=wl.pools.rope_quantized, device=dev)
     for lay in wl.layouts:  # slot s = shard position s: the step's row s
         batch.add_layout(wl.pools, lay.cold, lay.hot)
     inputs = (wl.q_lat, wl.q_rope, wl.new_latent, wl.new_rope)
@@ -893,6 +894,11 @@ def extras(dev, args) -> dict:
     # C3 with cache_dtype="int8": 512 code bytes a cold token (656 B with scales and RoPE key)
     wl = c3_workload(dev, seed=1000, scheme="int8")
     decode_rate(wl, "c3_int8_1gpu", 20)
+    # the same batch end to end through the serving loop (int8 flushes, 64-token tiles planned on
+    # the GPU)
+    e2e_args = argparse.Namespace(warmup=3, steps=20)
+    res["c3_int8_1gpu"]["e2e"] = e2e_measure(wl, dev, torch.cuda.current_stream(dev), e2e_args, lambda: None,
+                                             lambda x: x)
     del wl
     # C3 with cache_dtype="float8": 512 e4m3 bytes a cold token, no scales (640 B with the RoPE key)
     wl = c3_workload(dev, seed=1000, scheme="float8")
