@@ -71,6 +71,12 @@ constexpr int kThreads = 32 * (kScoreWarps + kValueWarps);
 constexpr int kScoreRegs = 160;
 constexpr int kValueRegs = 96;
 constexpr int kLaunchRegs = 128;
+// the one-byte-code modes: one m-tile per score warp needs fewer score registers, and their value
+// warps' code bytes need more (at 96 they spill)
+constexpr int kScoreRegsB = 152;
+constexpr int kValueRegsB = 104;
+static_assert(32 * (kScoreWarps * kScoreRegsB + kValueWarps * kValueRegsB) <= kThreads * kLaunchRegs,
+              "setmaxnreg split of the byte-code modes exceeds the launch's register allocation");
 static_assert(32 * (kScoreWarps * kScoreRegs + kValueWarps * kValueRegs) <= kThreads * kLaunchRegs,
               "setmaxnreg split exceeds the launch's register allocation");
 
@@ -782,7 +788,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =====================================================================
     // score warps
     // =====================================================================
-    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kScoreRegs));
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kBytes ? kScoreRegsB : kScoreRegs));
     // team `team` takes tiles team, team + 2, ...; tw is the warp's index in its team
     const int team = warp / kTeamWarps, tw = warp % kTeamWarps;
     // cold tile token of accumulator row r (0..15) of this warp's m-tile m: INT4 tiles give each
@@ -1343,7 +1349,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // =====================================================================
     // value warps: scale group g = warp - 8, latent dims [64g, 64g + 64)
     // =====================================================================
-    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kValueRegs));
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kBytes ? kValueRegsB : kValueRegs));
     const int g = warp - kScoreWarps;
     const bool rotated = p.cold_scheme == ASTERQ_SCHEME_HADAMARD_INT4;  // else plain int4: no rotation back
 #pragma unroll 1
