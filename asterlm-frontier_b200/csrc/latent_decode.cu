@@ -73,8 +73,8 @@ constexpr int kValueRegs = 96;
 constexpr int kLaunchRegs = 128;
 // the one-byte-code modes: one m-tile per score warp needs fewer score registers, and their value
 // warps' code bytes need more (at 96 they spill)
-constexpr int kScoreRegsB = 152;
-constexpr int kValueRegsB = 104;
+constexpr int kScoreRegsB = 144;
+constexpr int kValueRegsB = 112;
 static_assert(32 * (kScoreWarps * kScoreRegsB + kValueWarps * kValueRegsB) <= kThreads * kLaunchRegs,
               "setmaxnreg split of the byte-code modes exceeds the launch's register allocation");
 static_assert(32 * (kScoreWarps * kScoreRegs + kValueWarps * kValueRegs) <= kThreads * kLaunchRegs,
